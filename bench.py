@@ -1,0 +1,354 @@
+#!/usr/bin/env python
+"""Needle 3 batched agent decode on B200.
+
+Each GPU holds the 121M CQ-W4 model and 1024 independent sequences (weak
+scaling: sequences are partitioned across GPUs, no collective on the data
+path). Every sequence gets a 118-token random prompt (prefilled outside the
+timed region) and then 45 greedy decode steps, each under its own seeded
+random vocabulary mask that allows 5-50% of the ids. A bench "step" is one
+decode step of all sequences: masked argmax of the last logits, then the
+forward of the chosen ids through all 20 layers and the lm_head.
+
+`value` times K steps with masks and ids resident in HBM (CUDA events on the
+engine's stream, max over ranks); `e2e` times K steps through the C ABI with
+host buffers: each step copies the masks in from pinned host memory and the
+chosen ids back. `--impl reference` times the CPU restatement of the
+reference engine on the host's cores (the reference itself is Rust and cannot
+be built in this image).
+"""
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "needle-rs_b200"))
+
+import numpy as np  # noqa: E402
+
+PROMPT, STEPS_CFG = 118, 45
+METRIC = "batched agent decode tok/s (1024 seqs/GPU, 118-token prompt, masked greedy)"
+CACHE = os.environ.get("NEEDLE_BENCH_CACHE", "/tmp/needle_b200_bench_cache")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=40)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--seqs", type=int, default=1024, help="sequences per GPU")
+    ap.add_argument("--roofline-site", default="auto")
+    ap.add_argument("--cpu-baseline", type=int, default=1, help="time the oracle on rank 0 (N=1 only)")
+    return ap.parse_args()
+
+
+def archive_bytes():
+    import needle_b200 as nb
+
+    path = os.path.join(CACHE, "needle3-seed0.cact")
+    if not os.path.exists(path):
+        os.makedirs(CACHE, exist_ok=True)
+        data = nb.synth_cact(seed=0)
+        tmp = f"{path}.{os.getpid()}.tmp"
+        with open(tmp, "wb") as f:
+            f.write(data)
+        os.replace(tmp, path)
+    with open(path, "rb") as f:
+        return f.read()
+
+
+def make_inputs(rank, S, steps, vocab):
+    """Prompts [S, 118] and masks [steps, S, vocab/8] (bit set = allowed)."""
+    rng = np.random.default_rng(1000 + rank)
+    prompts = rng.integers(0, vocab, (S, PROMPT)).astype(np.int32)
+    frac = rng.uniform(0.05, 0.5, (steps, S, 1))
+    masks = np.empty((steps, S, (vocab + 7) // 8), np.uint8)
+    for k in range(steps):
+        allow = rng.random((S, vocab), np.float32) < frac[k]
+        allow[np.arange(S), rng.integers(0, vocab, S)] = True
+        masks[k] = np.packbits(allow, axis=1, bitorder="little")
+    return prompts, masks
+
+
+class Clocks:
+    """nvidia-smi samples of the SM clock and throttle reasons while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def site_algorithmic(site, S, n_keys):
+    """Algorithmic work of one launch of a site at a decode step (T = 1, S
+    rows): (amount, unit, bound). Bytes count every input once and every
+    output once; int8 ops count a multiply-add as two."""
+    act = S * (768 + 6 * 4)
+    gemm = {"qkvg": 1568, "out": 768, "lm_head": 16384, "engram_kv": 1536}
+    if site in gemm:
+        n = gemm[site]
+        return n * 396 + act + S * n * 4, "bytes", "hbm"
+    if site == "attention":
+        # per row: 12 q heads read the 2 kv heads' keys/values of n positions
+        kv = S * 2 * n_keys * (48 + 4 + 64 + 4)
+        return kv + S * (576 + 768 + 768) * 4, "bytes", "hbm"
+    if site == "post":
+        return S * (768 * 5 + 3072 * 2 + 24) * 4, "bytes", "hbm"
+    if site == "mhc":
+        return S * (3072 + 768 + 24) * 4 + 24 * 3072, "bytes", "hbm"
+    if site == "conv":
+        return S * (1568 + 576) * 4 + S * 2 * (48 + 64 + 8), "bytes", "hbm"
+    if site == "norm":
+        return S * (768 * 2 + 768 + 6 * 4) * 4, "bytes", "hbm"
+    raise KeyError(site)
+
+
+def run_reference(args, rank, world):
+    """The reference arm: the CPU restatement of needle-rs's engine on every
+    host thread, the same metric on a bounded sample of sequences."""
+    if rank != 0:
+        return
+    import needle_b200 as nb  # for the archive writer only
+    from oracle import oracle as orc
+
+    threads = os.cpu_count() or 1
+    data = archive_bytes()
+    model = orc.Model(data)
+    S = threads
+    prompts, masks = make_inputs(0, S, args.warmup + args.steps, model.out_rows)
+    b = orc.Batch(model, S, threads)
+    b.prefill(prompts)
+    for k in range(args.warmup):
+        b.step(masks[k])
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        b.step(masks[args.warmup + k])
+    dt = time.perf_counter() - t0
+    value = S * args.steps / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "i8/f32", "data": "synthetic",
+        "config": {"workload": "agent_decode", "seqs": S, "prompt": PROMPT, "decode_steps": args.warmup + args.steps,
+                   "parallelism": "host threads", "model": "needle3-121M random-init CQ-W4 seed 0"},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": f"{S} sequences (one per host thread), {args.steps} timed masked greedy steps after "
+                                   f"a 118-token prefill and {args.warmup} warm-up steps"},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_sample(data):
+    from oracle import oracle as orc
+
+    threads = os.cpu_count() or 1
+    model = orc.Model(data)
+    S, steps = threads, 20
+    prompts, masks = make_inputs(0, S, steps, model.out_rows)
+    b = orc.Batch(model, S, threads)
+    b.prefill(prompts)
+    t0 = time.perf_counter()
+    for k in range(steps):
+        b.step(masks[k])
+    dt = time.perf_counter() - t0
+    return {"value": S * steps / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{S} sequences (one per host thread), {steps} masked greedy decode steps after a 118-token "
+                      f"prefill (decode timed only)"}
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch
+
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    import needle_b200 as nb
+
+    S, W, K = args.seqs, args.warmup, args.steps
+    total_steps = W + K
+    data = archive_bytes()
+    model = nb.Model(data, device=local)
+    V = model.out_rows
+    prompts, masks = make_inputs(rank, S, total_steps, V)
+    sites = ["qkvg", "out", "lm_head", "engram_kv", "attention", "post", "mhc", "conv", "norm"]
+    cap = PROMPT + total_steps + len(sites) + 2
+
+    # --- device-resident run (value)
+    bA = model.batch(S, cap)
+    bA.forward(prompts, nb.OUT_LAST_LOGITS, out=np.zeros((S, 1, V), np.float32))
+    d_masks = torch.from_numpy(masks).to(f"cuda:{local}")
+    d_next = torch.zeros(S, dtype=torch.int32, device=f"cuda:{local}")
+    stream = torch.cuda.ExternalStream(bA.stream, device=f"cuda:{local}")
+
+    # --- host-buffer run (e2e), plus an untimed per-site kernel sweep first
+    bB = model.batch(S, cap)
+    bB.forward(prompts, nb.OUT_LAST_LOGITS, out=np.zeros((S, 1, V), np.float32))
+    sweep = {}
+    for k, site in enumerate(sites):
+        bB.time_site(site)
+        bB.step(masks[k % total_steps])
+        ms, n = bB.site_time()
+        sweep[site] = {"ms_per_step": ms, "launches": n}
+    bB.time_site("none")
+    site = args.roofline_site
+    if site == "auto":
+        site = max(sweep, key=lambda s: sweep[s]["ms_per_step"])
+
+    def barrier():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if not dist:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    with Clocks(local) as clocks:
+        for k in range(W):
+            bA.step(d_masks[k], d_next)
+        barrier()
+        bA.time_site(site)
+        l0 = nb.launch_count()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for k in range(K):
+            bA.step(d_masks[W + k], d_next)
+        ev1.record(stream)
+        launches = nb.launch_count() - l0
+        barrier()
+        t_value = ev0.elapsed_time(ev1) / 1e3
+        site_ms, site_n = bA.site_time()
+        bA.time_site("none")
+        # e2e: host masks in pinned memory, ids back to the host, every step
+        h_masks = torch.from_numpy(masks).pin_memory().numpy()
+        h_next = torch.zeros(S, dtype=torch.int32).pin_memory().numpy()
+        streamB = torch.cuda.ExternalStream(bB.stream, device=f"cuda:{local}")
+        for k in range(W):
+            bB.step(h_masks[k], h_next)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(streamB)
+        for k in range(K):
+            bB.step(h_masks[W + k], h_next)
+        e1.record(streamB)
+        barrier()
+        t_e2e = e0.elapsed_time(e1) / 1e3
+    t_value = max_over_ranks(t_value)
+    t_e2e = max_over_ranks(t_e2e)
+    clk = clocks.summary()
+
+    if rank == 0:
+        hbm, bf16, kind = peaks()
+        n_keys = PROMPT + W + K // 2 + len(sites)
+        amount, unit, bound = site_algorithmic(site, S, n_keys)
+        avg_s = site_ms / 1e3 / max(site_n, 1)
+        achieved = amount / avg_s / 1e9
+        roofline = {"bound": bound, "kernel_site": site, "achieved": achieved, "peak": hbm,
+                    "unit": "GB/s", "frac": achieved / hbm, "peak_kind": kind,
+                    "algorithmic_bytes_per_launch": amount, "avg_launch_us": avg_s * 1e6, "launches": site_n,
+                    "traffic": None}
+        cpu = None
+        if args.cpu_baseline and world == 1:
+            cpu = cpu_baseline_sample(data)
+        line = {
+            "metric": METRIC, "value": S * K * world / t_value, "unit": "tok/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": t_value / K * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "i8/f32", "data": "synthetic",
+            "config": {"workload": "agent_decode", "seqs_per_gpu": S, "prompt": PROMPT, "decode_steps": W + K,
+                       "mask_allow": "uniform 5-50% of 16384 ids per (seq, step)",
+                       "l2": "inputs larger than L2: ~0.8 GB of int8 KV per GPU read every step; the 31 MB of "
+                             "weights stay L2-resident as in serving",
+                       "parallelism": f"sequences sharded, {world} GPU(s), no collective",
+                       "model": "needle3-121M random-init CQ-W4 seed 0"},
+            "e2e": {"value": S * K * world / t_e2e, "unit": "tok/s", "h2d_bytes_per_step": int(masks[0].nbytes),
+                    "d2h_bytes_per_step": S * 4},
+            "gpu_launches": int(launches),
+            "roofline": roofline,
+            "sites_ms_per_step": {k: round(v["ms_per_step"], 4) for k, v in sweep.items()},
+            "cpu_baseline": cpu,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    del bA, bB
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,142 @@
+/*
+ * needle_engine.h — the model-level C ABI under needle.h: the contract the
+ * reference's engine crate gives its agent, CLI and benches (Model, Session,
+ * head logits), made batched so one call advances many independent
+ * sequences on one GPU. Plain pointers and sizes only.
+ *
+ * Each entry names the reference interface it replaces (file:line in
+ * needle-rs). A batch holds S sequences that are fed in lockstep: every call
+ * gives each sequence the same number of new tokens, so they share positions.
+ * A batch is driven by one host thread at a time.
+ *
+ * Pointers: with ND_DEVICE in `flags` the id/mask/output pointers are device
+ * pointers on the model's GPU and the call is asynchronous on the batch's
+ * stream; otherwise they are host pointers, copied in and out inside the
+ * call, which returns when the results are in host memory.
+ */
+#ifndef NEEDLE_ENGINE_H
+#define NEEDLE_ENGINE_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct nd_model nd_model;
+typedef struct nd_batch nd_batch;
+
+enum { ND_DEVICE = 1 };
+
+/* crates/needle-engine/src/model.rs:150-160 (`Outputs`). */
+enum {
+    ND_OUT_NONE = 0,        /* Outputs::None */
+    ND_OUT_LAST_LOGITS = 1, /* Outputs::LastLogits: [S][out_rows] */
+    ND_OUT_LAST_HIDDEN = 2, /* Outputs::LastHidden: [S][d_model] */
+    ND_OUT_ALL_LOGITS = 3,  /* Outputs::AllLogits: [S][t][out_rows] */
+    ND_OUT_HIDDEN = 4       /* Outputs::Hidden: [S][t][d_model] */
+};
+
+/* crates/needle-engine/src/loader.rs:40-59 with weights.rs:314-497
+ * (Weights::from_archive_mode, fast) and model.rs:248-253 (Model::quantized):
+ * parse the archive, upload its packed matrices and small weights to GPU
+ * `device`, build the int8 gate projection and RoPE tables. The archive
+ * bytes are only read during the call. 0 on success, -1 on error. */
+int nd_model_load(const unsigned char* cact, unsigned long long n, int device, nd_model** out);
+void nd_model_free(nd_model* m);
+
+/* crates/needle-core/src/cact.rs:173-202 (Header::to_config): dims[0..9] =
+ * vocab, out_rows, d_model, num_layers, num_heads, num_kv_heads,
+ * qk_head_dim, v_head_dim, max_seq_len. */
+int nd_model_dims(const nd_model* m, int* dims);
+
+/* model.rs:264-274 (Model::session), for `num_seqs` sequences of up to
+ * `max_len` positions each. */
+int nd_batch_new(nd_model* m, int num_seqs, int max_len, nd_batch** out);
+void nd_batch_free(nd_batch* b);
+
+/* model.rs:72-74 (Session::len): positions every sequence has been fed. */
+int nd_batch_len(const nd_batch* b);
+
+/* model.rs:304-306 (Model::forward) through infer.rs:1105-1131
+ * (forward_native): feed ids[S][t] to every sequence in the engine's chunks
+ * of at most 32, writing `outputs` to out (may be NULL for ND_OUT_NONE).
+ * Returns the rows written per sequence, -1 on error. */
+int nd_batch_forward(nd_batch* b, const int* ids, int t, int outputs, float* out, int flags);
+
+/* The greedy decode loop of crates/needle-cli/src/main.rs:577-581 and
+ * generate.rs:110-125, with the agent's ban (agent.rs:1114-1127): for each
+ * sequence take the first index of the maximum of its last logits after the
+ * ids its mask disallows read -1e30 (allow_bits [S][ceil(out_rows/8)], bit
+ * set = allowed, LSB first; NULL allows all), write it to next_ids[S], and
+ * feed it as one decode step. Needs a preceding forward with logits. */
+int nd_batch_step(nd_batch* b, const unsigned char* allow_bits, int* next_ids, int flags);
+
+/* infer.rs:1016 (NatState::last_hidden): each sequence's final normed hidden
+ * state of the last position a forward returned outputs for, [S][d_model]. */
+int nd_batch_last_hidden(nd_batch* b, float* out, int flags);
+
+/* infer.rs:1135-1141 (Model::head_logits): logits of h[rows][d_model] with
+ * the decode kernel, out[rows][out_rows]. */
+int nd_head_logits(nd_batch* b, const float* h, int rows, float* out, int flags);
+
+/* infer.rs:1145-1166 (Model::head_logits_sparse): one row h[d_model]; the
+ * ids are scored with the single-row kernel, every other entry is NEG
+ * (0xf149f2ca). out[out_rows]. Host pointers. */
+int nd_head_logits_sparse(nd_batch* b, const float* h, const int* ids, int n, float* out);
+
+/* The CUDA stream a batch's work runs on (a cudaStream_t); no counterpart
+ * in the reference, which runs on the CPU. */
+void* nd_batch_stream(nd_batch* b);
+
+/* crates/needle-core/src/quant.rs:233-256 (cq_pack, bits 4, group 128):
+ * w[rows][d] to codes[rows][ceil(d/128)*64] and f16 norms[rows][ceil(d/128)]. */
+int nd_cq_pack(const float* w, int rows, int d, unsigned char* codes, unsigned short* norms);
+
+/* crates/needle-core/src/cact.rs:399-475 (pack) over random-init Needle 3
+ * weights: every tensor ~N(0, std^2), seeded; CQ-4 matrices, f16 small
+ * weights, MT19937 Hadamard permutations. Shape knobs let tests shrink the
+ * model (num_layers, vocab, engram_slots, sliding_window; engram_sites is
+ * a bit mask of layers, global_mask likewise). With out == NULL returns the
+ * byte size in *len; else writes up to cap bytes. */
+int nd_synth_cact(int num_layers, int vocab, int engram_slots, int sliding_window, unsigned long long global_mask,
+                  unsigned long long engram_sites, unsigned long long seed, float std, unsigned char* out,
+                  unsigned long long cap, unsigned long long* len);
+
+/* Kernel launches this process has issued (all batches, all devices); no
+ * counterpart in the reference. */
+long long nd_launch_count(void);
+
+/* Launch sites whose kernels can be timed with CUDA events on the batch's
+ * stream (no counterpart in the reference): nd_batch_time_site(b, site)
+ * starts recording every launch of that site (clearing earlier records;
+ * ND_SITE_NONE stops), nd_batch_site_time() waits for the stream and
+ * returns the summed kernel time and the number of launches. */
+enum {
+    ND_SITE_NONE = 0,
+    ND_SITE_QKVG = 1,      /* q|k|v|gate projection */
+    ND_SITE_OUT = 2,       /* attention out projection */
+    ND_SITE_LM_HEAD = 3,   /* tied lm_head logits */
+    ND_SITE_ENGRAM_KV = 4, /* engram key|value projection */
+    ND_SITE_ATTENTION = 5, /* int8 KV attention + gate */
+    ND_SITE_POST = 6,      /* post block: norms, Hadamard MLP, Sinkhorn, mHC write */
+    ND_SITE_MHC = 7,       /* mHC read */
+    ND_SITE_CONV = 8,      /* conv taps, head norm, RoPE, int8 KV write */
+    ND_SITE_NORM = 9       /* engram gate, input norm, A8 */
+};
+int nd_batch_time_site(nd_batch* b, int site);
+int nd_batch_site_time(nd_batch* b, double* total_ms, int* launches);
+
+/* The last failure on this thread (empty if none). */
+const char* nd_last_error(void);
+
+/* Test support: copy an internal per-row buffer of the last forward
+ * ("xs", "u", "p", "x1", "proj", "qbuf", "att", "o", "h", "logits", or the
+ * same names snapped after layer `layer` when nd_batch_debug_layer(b, layer)
+ * was set, prefixed "snap."). Returns the float count, -1 if unknown. */
+int nd_batch_debug(nd_batch* b, const char* name, float* out, long long cap);
+int nd_batch_debug_layer(nd_batch* b, int layer);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NEEDLE_ENGINE_H */

@@ -1,0 +1,899 @@
+// The Needle 3 engine on one GPU: archive upload, batched sequence state and
+// the forward sequencing of the reference's native path, behind the C ABI of
+// include/needle_engine.h and include/needle.h.
+
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "cact.h"
+#include "kernels.h"
+#include "needle.h"
+#include "needle_engine.h"
+
+namespace nd {
+
+static thread_local std::string g_err;
+
+#define CK(x)                                                                                                          \
+    do {                                                                                                               \
+        cudaError_t e_ = (x);                                                                                          \
+        if (e_ != cudaSuccess) throw std::runtime_error(std::string("CUDA error: ") + cudaGetErrorString(e_) + " (" #x ")"); \
+    } while (0)
+
+struct Config {
+    int vocab, out_vocab, d, nh, nkv, L, qk, vd, max_seq, hada_n, lanes, sw;
+    uint64_t global_mask;
+    int taps, eslots, esub, ntables, etaps, edil, eseed;
+    std::vector<int> orders, sites;
+    float theta;
+    int out_rows() const { return out_vocab > 0 ? out_vocab : vocab; }
+    int window(int l) const { return (sw > 0 && !((global_mask >> l) & 1)) ? sw : 0; }
+};
+
+struct Model {
+    int device = 0;
+    Config c;
+    std::vector<void*> allocs;
+    DevMat embedding;
+    std::vector<LayerW> layers;
+    std::vector<DevMat> etables, ekv;
+    std::vector<const float*> etaps;
+    std::vector<int> site_of_layer;
+    const int32_t *perm1 = nullptr, *perm2 = nullptr;
+    const float* final_norm = nullptr;
+    const float *rope_cos = nullptr, *rope_sin = nullptr, *sd = nullptr, *cd = nullptr;
+    std::vector<float> h_sd, h_cd;
+
+    template <class T>
+    T* upload(const T* h, size_t n) {
+        void* p = nullptr;
+        CK(cudaMalloc(&p, n * sizeof(T) + 16));
+        allocs.push_back(p);
+        CK(cudaMemcpy(p, h, n * sizeof(T), cudaMemcpyHostToDevice));
+        return (T*)p;
+    }
+    ~Model() {
+        cudaSetDevice(device);
+        for (void* p : allocs) cudaFree(p);
+    }
+};
+
+// cact.rs:173-202
+static Config config_of(const CactArchive& a) {
+    Config c;
+    const uint32_t* h = a.h;
+    c.vocab = h[5]; c.out_vocab = h[6]; c.d = h[7]; c.nh = h[8]; c.nkv = h[9]; c.L = h[10];
+    c.qk = h[11]; c.vd = h[12]; c.max_seq = h[13]; c.hada_n = h[14]; c.lanes = h[15]; c.sw = h[16];
+    c.global_mask = (uint64_t)h[17] | ((uint64_t)h[18] << 32);
+    c.taps = h[19]; c.eslots = h[20]; c.esub = h[21]; c.ntables = h[22]; c.etaps = h[23]; c.edil = h[24]; c.eseed = h[25];
+    for (uint32_t i = 0; i < h[26]; i++) c.orders.push_back(h[27 + i]);
+    for (uint32_t i = 0; i < h[31]; i++) c.sites.push_back(h[32 + i]);
+    std::memcpy(&c.theta, &h[48], 4);
+    return c;
+}
+
+struct Cursor {
+    const CactArchive& a;
+    size_t i = 0;
+    const CactRecord& next(int dtype) {
+        if (i >= a.recs.size()) throw std::runtime_error("archive ends before the model does");
+        const CactRecord& r = a.recs[i++];
+        if (r.dtype != dtype) throw std::runtime_error("archive tensor " + std::to_string(i - 1) + " has the wrong dtype");
+        return r;
+    }
+};
+
+static std::vector<float> small_f32(const CactArchive& a, Cursor& cur, size_t expect) {
+    size_t idx = cur.i;
+    const CactRecord& r = cur.a.recs.at(idx);
+    std::vector<float> v;
+    if (r.dtype == CACT_F16) {
+        cur.i++;
+        v.resize(r.nbytes / 2);
+        for (size_t k = 0; k < v.size(); k++) {
+            uint16_t h;
+            std::memcpy(&h, a.bytes(idx) + 2 * k, 2);
+            v[k] = f16_to_f32(h);
+        }
+    } else if (r.dtype == CACT_F32) {
+        cur.i++;
+        v.resize(r.nbytes / 4);
+        std::memcpy(v.data(), a.bytes(idx), r.nbytes);
+    } else {
+        throw std::runtime_error("archive tensor " + std::to_string(idx) + " is not a small f16/f32 weight");
+    }
+    if (expect && v.size() < expect) throw std::runtime_error("archive tensor " + std::to_string(idx) + " is too small");
+    return v;
+}
+
+struct HostMat {
+    std::vector<uint8_t> codes;
+    std::vector<uint16_t> norms;
+    int out = 0, in_dim = 0, groups = 0;
+};
+
+// qlinear.rs:220-236 (4-bit records, group 128)
+static HostMat host_mat(const CactArchive& a, Cursor& cur, int in_dim) {
+    const CactRecord& r = cur.next(CACT_CQ);
+    if (r.group != 128) throw std::runtime_error("CQ group size " + std::to_string(r.group) + " is not supported");
+    if (r.bits != 4) throw std::runtime_error("only 4-bit CQ records are supported by this engine");
+    if (r.shape.size() != 2 || (int)r.shape[1] != in_dim) throw std::runtime_error("CQ matrix has the wrong input width");
+    HostMat m;
+    m.out = (int)r.shape[0];
+    m.in_dim = in_dim;
+    m.groups = (in_dim + 127) / 128;
+    size_t nc = (size_t)m.out * m.groups * 64, nn = (size_t)m.out * m.groups;
+    if (r.nbytes < nc + nn * 2) throw std::runtime_error("CQ record is truncated");
+    const uint8_t* b = a.bytes(cur.i - 1);
+    m.codes.assign(b, b + nc);
+    m.norms.resize(nn);
+    std::memcpy(m.norms.data(), b + nc, nn * 2);
+    return m;
+}
+
+static void append(HostMat& dst, const HostMat& src) {
+    if (dst.out == 0) { dst = src; return; }
+    dst.out += src.out;
+    dst.codes.insert(dst.codes.end(), src.codes.begin(), src.codes.end());
+    dst.norms.insert(dst.norms.end(), src.norms.begin(), src.norms.end());
+}
+
+static DevMat to_dev(Model& m, const HostMat& h) {
+    DevMat d;
+    d.codes = m.upload(h.codes.data(), h.codes.size());
+    d.norms = m.upload(h.norms.data(), h.norms.size());
+    d.out = h.out;
+    d.in_dim = h.in_dim;
+    d.groups = h.groups;
+    return d;
+}
+
+// weights.rs:314-497 (record walk, fast mode), infer.rs:938-962 (Tables).
+static Model* load_model(const uint8_t* bytes, size_t n, int device) {
+    CactArchive a;
+    cact_parse(bytes, n, a);
+    std::unique_ptr<Model> mp(new Model());
+    Model& m = *mp;
+    m.device = device;
+    CK(cudaSetDevice(device));
+    Config& c = m.c;
+    c = config_of(a);
+    if (c.lanes != 4 || c.hada_n != 1024 || c.taps != 3 || c.qk != 48 || c.vd != 64 || c.d != 768 || c.nh != 12 ||
+        c.nkv != 2 || c.etaps != 4 || c.edil != 3 || c.esub != 128 || c.ntables != 6 || c.orders.size() != 2 ||
+        c.orders[0] != 2 || c.orders[1] != 3 || c.eseed != 0)
+        throw std::runtime_error("the native path covers the shipped Needle 3 geometry only");
+    if (c.L < 1 || c.L > 64 || c.vocab < 1 || c.out_rows() > c.vocab || c.max_seq < 1)
+        throw std::runtime_error("corrupt .cact header");
+    Cursor cur{a};
+    const int d = c.d;
+    HostMat emb = host_mat(a, cur, d);
+    if (emb.out != c.vocab) throw std::runtime_error("embedding shape does not match the header");
+    m.embedding = to_dev(m, emb);
+    m.layers.resize(c.L);
+    std::vector<HostMat> qkvg(c.L);
+    for (int l = 0; l < c.L; l++) {
+        LayerW& w = m.layers[l];
+        std::memset(&w, 0, sizeof w);
+        w.norm_in = m.upload(small_f32(a, cur, d).data(), d);
+        HostMat q = host_mat(a, cur, d), k = host_mat(a, cur, d), v = host_mat(a, cur, d);
+        auto qt = small_f32(a, cur, 3 * 576), kt = small_f32(a, cur, 3 * 96), vt = small_f32(a, cur, 3 * 128);
+        w.q_taps = m.upload(qt.data(), qt.size());
+        w.k_taps = m.upload(kt.data(), kt.size());
+        w.v_taps = m.upload(vt.data(), vt.size());
+        w.q_norm = m.upload(small_f32(a, cur, 48).data(), 48);
+        w.k_norm = m.upload(small_f32(a, cur, 48).data(), 48);
+        HostMat g = host_mat(a, cur, d), o = host_mat(a, cur, 768);
+        if (q.out != 576 || k.out != 96 || v.out != 128 || g.out != 768 || o.out != d)
+            throw std::runtime_error("attention projection shapes do not match the header");
+        HostMat f;
+        append(f, q); append(f, k); append(f, v); append(f, g);
+        w.qkvg = to_dev(m, f);
+        w.out = to_dev(m, o);
+        w.post_norm = m.upload(small_f32(a, cur, d).data(), d);
+        w.attn_gate = small_f32(a, cur, 1)[0];
+        w.pre_hada = m.upload(small_f32(a, cur, d).data(), d);
+        auto d1 = small_f32(a, cur, d), d2 = small_f32(a, cur, 1024), b2 = small_f32(a, cur, 1024),
+             d3 = small_f32(a, cur, 1024), d4 = small_f32(a, cur, d);
+        w.d1 = m.upload(d1.data(), d1.size());
+        w.d2 = m.upload(d2.data(), d2.size());
+        w.b2 = m.upload(b2.data(), b2.size());
+        w.d3 = m.upload(d3.data(), d3.size());
+        w.d4 = m.upload(d4.data(), d4.size());
+        for (int k6 = 0; k6 < 6; k6++) w.kron[k6] = m.upload(small_f32(a, cur, 1024).data(), 1024);
+        w.cond_v = m.upload(small_f32(a, cur, (size_t)d * 8).data(), (size_t)d * 8);
+        w.cond_u = m.upload(small_f32(a, cur, 8 * 1024).data(), 8 * 1024);
+    }
+    const int nl = c.lanes, nc = nl * d;
+    auto a_pre = small_f32(a, cur, c.L), a_post = small_f32(a, cur, c.L), a_res = small_f32(a, cur, c.L);
+    auto b_pre = small_f32(a, cur, c.L * nl), b_post = small_f32(a, cur, c.L * nl), b_res = small_f32(a, cur, c.L * nl * nl);
+    HostMat phi[3] = {host_mat(a, cur, nc), host_mat(a, cur, nc), host_mat(a, cur, nc)};
+    if (phi[0].out != c.L * nl || phi[1].out != c.L * nl || phi[2].out != c.L * nl * nl)
+        throw std::runtime_error("mHC projection shapes do not match the header");
+    std::vector<float> row(nc);
+    for (int l = 0; l < c.L; l++) {
+        LayerW& w = m.layers[l];
+        w.a_pre = a_pre[l]; w.a_post = a_post[l]; w.a_res = a_res[l];
+        for (int j = 0; j < 4; j++) { w.b_pre[j] = b_pre[l * 4 + j]; w.b_post[j] = b_post[l * 4 + j]; }
+        for (int j = 0; j < 16; j++) w.b_res[j] = b_res[l * 16 + j];
+        // weights.rs:380-391 + 493 (pre | post | res rows dequantized),
+        // infer.rs:852-866 (each row requantized to int8 with its scale)
+        std::vector<int8_t> q(24 * (size_t)nc);
+        std::vector<float> s(24);
+        int k = 0;
+        const int base[3] = {l * 4, l * 4, l * 16}, cnt[3] = {4, 4, 16};
+        for (int part = 0; part < 3; part++)
+            for (int rr = 0; rr < cnt[part]; rr++, k++) {
+                cq_row(phi[part].codes.data(), phi[part].norms.data(), phi[part].groups, nc, base[part] + rr, row.data());
+                s[k] = quant_i8(row.data(), nc, q.data() + (size_t)k * nc);
+            }
+        w.phi_q = m.upload(q.data(), q.size());
+        w.phi_s = m.upload(s.data(), s.size());
+    }
+    auto p1 = small_f32(a, cur, 1024), p2 = small_f32(a, cur, 1024);
+    if ((int)p1.size() != c.hada_n || (int)p2.size() != c.hada_n) throw std::runtime_error("Hadamard permutations do not match hada_n");
+    std::vector<int32_t> ip1(1024), ip2(1024);
+    for (int j = 0; j < 1024; j++) {
+        ip1[j] = (int32_t)p1[j];
+        ip2[j] = (int32_t)p2[j];
+        if (ip1[j] < 0 || ip1[j] >= 1024 || ip2[j] < 0 || ip2[j] >= 1024) throw std::runtime_error("corrupt Hadamard permutation");
+    }
+    m.perm1 = m.upload(ip1.data(), 1024);
+    m.perm2 = m.upload(ip2.data(), 1024);
+    for (size_t s = 0; s < c.sites.size(); s++) {
+        HostMat t = host_mat(a, cur, 128);
+        if (t.out != c.ntables * c.eslots) throw std::runtime_error("engram table shape does not match the header");
+        HostMat k = host_mat(a, cur, d), v = host_mat(a, cur, d);
+        HostMat kv;
+        append(kv, k);
+        append(kv, v);
+        m.etables.push_back(to_dev(m, t));
+        m.ekv.push_back(to_dev(m, kv));
+        auto taps = small_f32(a, cur, 4 * (size_t)d);
+        m.etaps.push_back(m.upload(taps.data(), taps.size()));
+    }
+    m.final_norm = m.upload(small_f32(a, cur, d).data(), d);
+    m.site_of_layer.assign(c.L, -1);
+    for (size_t s = 0; s < c.sites.size(); s++) {
+        if (c.sites[s] < 0 || c.sites[s] >= c.L) throw std::runtime_error("engram site outside the stack");
+        m.site_of_layer[c.sites[s]] = (int)s;
+    }
+    // infer.rs:938-946 with the reference's non-Apple libm stand-ins
+    // (infer.rs:83-102): f32 results of f64 pow / sincos, rounded once.
+    const int half = c.qk / 2;
+    float coef = -2.0f / (float)c.qk;
+    std::vector<float> freq(half);
+    m.h_sd.resize(half);
+    m.h_cd.resize(half);
+    for (int f = 0; f < half; f++) {
+        freq[f] = (float)std::pow((double)c.theta, (double)((float)f * coef));
+        double sv, cv;
+        sincos((double)freq[f], &sv, &cv);
+        m.h_sd[f] = (float)sv;
+        m.h_cd[f] = (float)cv;
+    }
+    std::vector<float> tc((size_t)c.max_seq * half), ts((size_t)c.max_seq * half);
+    for (int p = 0; p < c.max_seq; p++)
+        for (int f = 0; f < half; f++) {
+            double sv, cv;
+            sincos((double)(freq[f] * (float)p), &sv, &cv);
+            tc[(size_t)p * half + f] = (float)cv;
+            ts[(size_t)p * half + f] = (float)sv;
+        }
+    m.rope_cos = m.upload(tc.data(), tc.size());
+    m.rope_sin = m.upload(ts.data(), ts.size());
+    m.sd = m.upload(m.h_sd.data(), half);
+    m.cd = m.upload(m.h_cd.data(), half);
+    // qlinear.rs:211-216, 244-265: the shared 4-bit codebook and its int8 form
+    std::vector<float> cb = cq_codebook(4, 128);
+    int8_t vals[16];
+    float cbs = 0.f;
+    {
+        float mx = 0.f;
+        for (float v : cb) mx = std::fmax(mx, std::fabs(v));
+        uint32_t k127u = 0x3c010204u;
+        float k127;
+        std::memcpy(&k127, &k127u, 4);
+        cbs = mx > 0.f ? mx * k127 : 1.0f;
+        float inv = 1.0f / cbs;
+        for (int i = 0; i < 16; i++) vals[i] = (int8_t)std::min(std::max(std::round(cb[i] * inv), -128.f), 127.f);
+    }
+    set_constants(vals, cb.data(), cbs, (float)(1.0 / std::sqrt(128.0)));
+    CK(cudaGetLastError());
+    CK(cudaDeviceSynchronize());
+    return mp.release();
+}
+
+// ----------------------------------------------------------------- batch
+
+struct Batch {
+    Model* m = nullptr;
+    int S = 0, cap = 0, Mmax = 0;
+    cudaStream_t st = nullptr;
+    int len = 0;          // positions fed to every sequence
+    int hist_base = 0;    // first position whose pre-tap row the conv may read
+    bool rope_valid = false;
+    bool have_logits = false;
+    int logits_rows = 0;
+    int debug_layer = -1;
+    Caches c{};
+    std::vector<void*> allocs;
+    float *xs, *u, *p, *x1, *proj, *qbuf, *att, *o, *e, *ekv, *evals, *cosr, *sinr, *rope_state, *h, *logits = nullptr;
+    int8_t* act;
+    float* sx;
+    int32_t *ids, *next;
+    uint8_t* masks;
+    size_t logits_cap = 0;
+    std::map<std::string, std::pair<float*, size_t>> snaps;
+    int last_rows = 0, last_T = 0;
+    int time_site = 0;                 // launch site timed with events (ND_SITE_*)
+    std::vector<cudaEvent_t> evs;
+    size_t ev_used = 0;
+
+    template <class T>
+    T* alloc(size_t n) {
+        void* p = nullptr;
+        CK(cudaMalloc(&p, n * sizeof(T) + 64));
+        allocs.push_back(p);
+        CK(cudaMemsetAsync(p, 0, n * sizeof(T) + 64, st));
+        return (T*)p;
+    }
+    ~Batch() {
+        cudaSetDevice(m->device);
+        if (st) cudaStreamSynchronize(st);
+        for (void* p : allocs) cudaFree(p);
+        if (logits) cudaFree(logits);
+        for (auto& kv : snaps) cudaFree(kv.second.first);
+        for (auto e : evs) cudaEventDestroy(e);
+        if (st) cudaStreamDestroy(st);
+    }
+};
+
+static Batch* batch_new(Model* m, int S, int max_len) {
+    const Config& c = m->c;
+    if (S < 1) throw std::runtime_error("a batch needs at least one sequence");
+    if (max_len < 1 || max_len > c.max_seq) throw std::runtime_error("max_len must be in [1, max_seq_len]");
+    CK(cudaSetDevice(m->device));
+    std::unique_ptr<Batch> bp(new Batch());
+    Batch& b = *bp;
+    b.m = m;
+    b.S = S;
+    b.cap = max_len;
+    b.Mmax = S * 32;
+    CK(cudaStreamCreateWithFlags(&b.st, cudaStreamNonBlocking));
+    const int L = c.L, nsites = (int)c.sites.size();
+    const size_t M = b.Mmax;
+    b.c.S = S;
+    b.c.L = L;
+    b.c.cap = max_len;
+    b.c.k8 = b.alloc<int8_t>((size_t)S * L * 2 * max_len * 48);
+    b.c.ks = b.alloc<float>((size_t)S * L * 2 * max_len);
+    b.c.v8 = b.alloc<int8_t>((size_t)S * L * 2 * max_len * 64);
+    b.c.vs = b.alloc<float>((size_t)S * L * 2 * max_len);
+    b.c.hist = b.alloc<float>((size_t)S * L * HIST_RING * 800);
+    b.c.ev8 = b.alloc<int8_t>((size_t)S * std::max(nsites, 1) * ENG_RING * 768);
+    b.c.evs = b.alloc<float>((size_t)S * std::max(nsites, 1) * ENG_RING * 24);
+    b.c.tokens = b.alloc<int32_t>((size_t)S * max_len);
+    b.xs = b.alloc<float>(M * 3072);
+    b.u = b.alloc<float>(M * 768);
+    b.p = b.alloc<float>(M * 24);
+    b.x1 = b.alloc<float>(M * 768);
+    b.proj = b.alloc<float>(M * 1568);
+    b.qbuf = b.alloc<float>(M * 576);
+    b.att = b.alloc<float>(M * 768);
+    b.o = b.alloc<float>(M * 768);
+    b.e = b.alloc<float>(M * 768);
+    b.ekv = b.alloc<float>((size_t)std::max(nsites, 1) * M * 1536);
+    b.evals = b.alloc<float>((size_t)std::max(nsites, 1) * M * 768);
+    b.cosr = b.alloc<float>(32 * 24);
+    b.sinr = b.alloc<float>(32 * 24);
+    b.rope_state = b.alloc<float>(48);
+    b.h = b.alloc<float>(M * 768);
+    b.act = b.alloc<int8_t>(M * 768);
+    b.sx = b.alloc<float>(M * 8);
+    b.ids = b.alloc<int32_t>(M);
+    b.next = b.alloc<int32_t>(S);
+    b.masks = b.alloc<uint8_t>((size_t)S * ((c.out_rows() + 7) / 8));
+    CK(cudaStreamSynchronize(b.st));
+    return bp.release();
+}
+
+static void ensure_logits(Batch& b, size_t rows) {
+    size_t need = rows * (size_t)b.m->c.out_rows();
+    if (need <= b.logits_cap) return;
+    if (b.logits) CK(cudaFree(b.logits));
+    b.logits = nullptr;
+    CK(cudaMalloc(&b.logits, need * sizeof(float)));
+    b.logits_cap = need;
+}
+
+// An event on the batch's stream around each launch of the timed site.
+static void tick(Batch& b, int site) {
+    if (b.time_site != site) return;
+    if (b.ev_used == b.evs.size()) {
+        cudaEvent_t e;
+        CK(cudaEventCreate(&e));
+        b.evs.push_back(e);
+    }
+    CK(cudaEventRecord(b.evs[b.ev_used++], b.st));
+}
+
+static void snap(Batch& b, const char* name, const float* src, size_t n) {
+    auto it = b.snaps.find(name);
+    if (it == b.snaps.end() || it->second.second < n) {
+        if (it != b.snaps.end()) cudaFree(it->second.first);
+        float* p = nullptr;
+        CK(cudaMalloc(&p, n * sizeof(float)));
+        b.snaps[name] = {p, n};
+    }
+    b.snaps[name].second = n;
+    CK(cudaMemcpyAsync(b.snaps[name].first, src, n * sizeof(float), cudaMemcpyDeviceToDevice, b.st));
+}
+
+// infer.rs:1168-1240 (chunk_native) for every sequence's chunk of T tokens
+// at positions len .. len + T - 1; ids are device int32 [S][T].
+static int chunk(Batch& b, const int32_t* ids, int T, int outputs) {
+    Model& m = *b.m;
+    const Config& c = m.c;
+    const int S = b.S, M = S * T, p0 = b.len, nsites = (int)c.sites.size();
+    cudaStream_t st = b.st;
+    if (p0 + T > b.cap) throw std::runtime_error("sequence exceeds the batch's max_len");
+    launch_write_tokens(ids, S, T, p0, b.c, st);
+    // infer.rs:1720: the recurrence serves one token right after the newest
+    launch_rope_rows(m.rope_cos, m.rope_sin, m.sd, m.cd, p0, T, (T == 1 && b.rope_valid) ? 1 : 0, b.rope_state, b.cosr,
+                     b.sinr, st);
+    launch_embed(m.embedding, ids, M, b.xs, st);
+    // infer.rs:1244-1328
+    for (int s = 0; s < nsites; s++) {
+        float* kv = b.ekv + (size_t)s * b.Mmax * 1536;
+        launch_engram_gather(m.etables[s], b.c, S, T, p0, c.eslots, b.e, st);
+        launch_prep_act(b.e, 768, 768, M, b.act, b.sx, st);
+        tick(b, ND_SITE_ENGRAM_KV);
+        launch_cq_gemm(m.ekv[s], b.act, b.sx, M, T, kv, 1536, 0, st);
+        tick(b, ND_SITE_ENGRAM_KV);
+        launch_engram_vhist(kv, b.c, s, nsites, S, T, p0, st);
+        launch_engram_conv(m.etaps[s], b.c, s, nsites, S, T, p0, b.evals + (size_t)s * b.Mmax * 768, st);
+    }
+    for (int l = 0; l < c.L; l++) {
+        const LayerW& w = m.layers[l];
+        const int lane = l % 4, site = m.site_of_layer[l];
+        tick(b, ND_SITE_MHC);
+        launch_mhc_read(w, lane, b.xs, M, b.u, b.p, st);
+        tick(b, ND_SITE_MHC);
+        tick(b, ND_SITE_NORM);
+        launch_input_norm(w, b.u, site >= 0 ? b.ekv + (size_t)site * b.Mmax * 1536 : nullptr,
+                          site >= 0 ? b.evals + (size_t)site * b.Mmax * 768 : nullptr, M, b.x1, b.act, b.sx, st);
+        tick(b, ND_SITE_NORM);
+        tick(b, ND_SITE_QKVG);
+        launch_cq_gemm(w.qkvg, b.act, b.sx, M, T, b.proj, 1568, 0, st);
+        tick(b, ND_SITE_QKVG);
+        tick(b, ND_SITE_CONV);
+        launch_conv_rope_kv(w, l, b.proj, b.c, S, T, p0, b.hist_base, b.cosr, b.sinr, b.qbuf, st);
+        tick(b, ND_SITE_CONV);
+        launch_hist_update(b.proj, b.c, l, S, T, p0, st);
+        tick(b, ND_SITE_ATTENTION);
+        launch_attention(b.qbuf, b.proj, b.c, l, S, T, p0, c.window(l), b.att, st);
+        tick(b, ND_SITE_ATTENTION);
+        launch_prep_act(b.att, 768, 768, M, b.act, b.sx, st);
+        tick(b, ND_SITE_OUT);
+        launch_cq_gemm(w.out, b.act, b.sx, M, T, b.o, 768, 0, st);
+        tick(b, ND_SITE_OUT);
+        if (l == b.debug_layer) {
+            snap(b, "snap.u", b.u, (size_t)M * 768);
+            snap(b, "snap.p", b.p, (size_t)M * 24);
+            snap(b, "snap.x1", b.x1, (size_t)M * 768);
+            snap(b, "snap.proj", b.proj, (size_t)M * 1568);
+            snap(b, "snap.qbuf", b.qbuf, (size_t)M * 576);
+            snap(b, "snap.att", b.att, (size_t)M * 768);
+            snap(b, "snap.o", b.o, (size_t)M * 768);
+        }
+        tick(b, ND_SITE_POST);
+        launch_post_block(w, lane, b.o, b.x1, b.u, b.p, m.perm1, m.perm2, M, b.xs, st);
+        tick(b, ND_SITE_POST);
+        if (l == b.debug_layer) snap(b, "snap.xs", b.xs, (size_t)M * 3072);
+    }
+    b.len += T;
+    b.rope_valid = true;
+    b.last_T = T;
+    CK(cudaGetLastError());
+    if (outputs == ND_OUT_NONE) return 0;
+    const bool all = outputs == ND_OUT_ALL_LOGITS || outputs == ND_OUT_HIDDEN;
+    const int rows = all ? M : S;
+    launch_final_hidden(b.xs, m.final_norm, S, T, all ? 1 : 0, b.h, st);
+    b.last_rows = rows;
+    if (outputs == ND_OUT_LAST_LOGITS || outputs == ND_OUT_ALL_LOGITS) {
+        ensure_logits(b, rows);
+        launch_prep_act(b.h, 768, 768, rows, b.act, b.sx, st);
+        // infer.rs:1135-1141: QAct of one row each, so the decode combine
+        tick(b, ND_SITE_LM_HEAD);
+        launch_cq_gemm(m.embedding, b.act, b.sx, rows, 1, b.logits, c.out_rows(), 0, st);
+        tick(b, ND_SITE_LM_HEAD);
+        b.have_logits = true;
+        b.logits_rows = rows;
+    }
+    CK(cudaGetLastError());
+    return all ? T : 1;
+}
+
+// infer.rs:1105-1131: chunks of at most 32 from the feed start; a Last*
+// request is served by the last chunk only.
+static int forward(Batch& b, const int32_t* dev_ids, int t, int outputs) {
+    if (t < 1) throw std::runtime_error("forward needs at least one token");
+    if (outputs < 0 || outputs > 4) throw std::runtime_error("unknown outputs value");
+    if ((outputs == ND_OUT_ALL_LOGITS || outputs == ND_OUT_HIDDEN) && t > 32)
+        throw std::runtime_error("per-token outputs are served for feeds of at most 32 tokens");
+    if (b.len + t > b.cap) throw std::runtime_error("sequence exceeds the batch's max_len");
+    int rows = 0;
+    for (int c0 = 0; c0 < t; c0 += 32) {
+        int len = std::min(32, t - c0);
+        bool last = c0 + len >= t;
+        int want = outputs;
+        if ((outputs == ND_OUT_LAST_LOGITS || outputs == ND_OUT_LAST_HIDDEN) && !last) want = ND_OUT_NONE;
+        const int32_t* src = dev_ids;
+        if (t > 32) {
+            // gather this chunk's columns [S][len] from ids [S][t]
+            CK(cudaMemcpy2DAsync(b.ids, len * sizeof(int32_t), dev_ids + c0, t * sizeof(int32_t), len * sizeof(int32_t), b.S,
+                                 cudaMemcpyDeviceToDevice, b.st));
+            src = b.ids;
+        }
+        rows = chunk(b, src, len, want);
+    }
+    return rows;
+}
+
+// ----------------------------------------------------------- the C ABI
+
+static int fail(const std::exception& e) {
+    g_err = e.what();
+    return -1;
+}
+
+}  // namespace nd
+
+using namespace nd;
+
+struct nd_model {
+    std::unique_ptr<Model> m;
+};
+struct nd_batch {
+    std::unique_ptr<Batch> b;
+    std::vector<int32_t> host_ids;
+};
+
+extern "C" {
+
+const char* nd_last_error(void) { return g_err.c_str(); }
+
+int nd_model_load(const unsigned char* cact, unsigned long long n, int device, nd_model** out) {
+    try {
+        if (!cact || !out) throw std::runtime_error("nd_model_load: null argument");
+        nd_model* h = new nd_model();
+        h->m.reset(load_model(cact, (size_t)n, device));
+        *out = h;
+        return 0;
+    } catch (std::exception& e) {
+        return fail(e);
+    }
+}
+
+void nd_model_free(nd_model* m) { delete m; }
+
+int nd_model_dims(const nd_model* mh, int* dims) {
+    if (!mh || !dims) return -1;
+    const Config& c = mh->m->c;
+    int v[9] = {c.vocab, c.out_rows(), c.d, c.L, c.nh, c.nkv, c.qk, c.vd, c.max_seq};
+    std::memcpy(dims, v, sizeof v);
+    return 0;
+}
+
+int nd_batch_new(nd_model* mh, int num_seqs, int max_len, nd_batch** out) {
+    try {
+        if (!mh || !out) throw std::runtime_error("nd_batch_new: null argument");
+        nd_batch* h = new nd_batch();
+        h->b.reset(batch_new(mh->m.get(), num_seqs, max_len));
+        *out = h;
+        return 0;
+    } catch (std::exception& e) {
+        return fail(e);
+    }
+}
+
+void nd_batch_free(nd_batch* b) { delete b; }
+
+int nd_batch_len(const nd_batch* b) { return b ? b->b->len : -1; }
+
+void* nd_batch_stream(nd_batch* b) { return b ? (void*)b->b->st : nullptr; }
+
+int nd_batch_forward(nd_batch* bh, const int* ids, int t, int outputs, float* out, int flags) {
+    try {
+        if (!bh || !ids) throw std::runtime_error("nd_batch_forward: null argument");
+        Batch& b = *bh->b;
+        CK(cudaSetDevice(b.m->device));
+        const bool dev = flags & ND_DEVICE;
+        const int32_t* dids = (const int32_t*)ids;
+        int32_t* staging = nullptr;
+        if (!dev) {
+            CK(cudaMallocAsync((void**)&staging, (size_t)b.S * t * sizeof(int32_t), b.st));
+            CK(cudaMemcpyAsync(staging, ids, (size_t)b.S * t * sizeof(int32_t), cudaMemcpyHostToDevice, b.st));
+            dids = staging;
+        }
+        int rows = forward(b, dids, t, outputs);
+        if (staging) CK(cudaFreeAsync(staging, b.st));
+        if (out && outputs != ND_OUT_NONE) {
+            const Config& c = b.m->c;
+            size_t width = (outputs == ND_OUT_LAST_HIDDEN || outputs == ND_OUT_HIDDEN) ? c.d : c.out_rows();
+            const float* src = width == (size_t)c.d ? b.h : b.logits;
+            size_t n = (size_t)b.last_rows * width;
+            CK(cudaMemcpyAsync(out, src, n * sizeof(float), dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, b.st));
+        }
+        if (!dev) CK(cudaStreamSynchronize(b.st));
+        return rows;
+    } catch (std::exception& e) {
+        return fail(e);
+    }
+}
+
+int nd_batch_step(nd_batch* bh, const unsigned char* allow_bits, int* next_ids, int flags) {
+    try {
+        if (!bh) throw std::runtime_error("nd_batch_step: null argument");
+        Batch& b = *bh->b;
+        CK(cudaSetDevice(b.m->device));
+        if (!b.have_logits || b.logits_rows != b.S) throw std::runtime_error("nd_batch_step needs the last logits of every sequence");
+        const bool dev = flags & ND_DEVICE;
+        const Config& c = b.m->c;
+        const size_t mb = (size_t)(c.out_rows() + 7) / 8;
+        const uint8_t* allow = allow_bits;
+        if (allow_bits && !dev) {
+            CK(cudaMemcpyAsync(b.masks, allow_bits, (size_t)b.S * mb, cudaMemcpyHostToDevice, b.st));
+            allow = b.masks;
+        }
+        launch_masked_argmax(b.logits, b.S, c.out_rows(), allow, b.next, b.st);
+        if (next_ids)
+            CK(cudaMemcpyAsync(next_ids, b.next, (size_t)b.S * sizeof(int32_t),
+                               dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, b.st));
+        forward(b, b.next, 1, ND_OUT_LAST_LOGITS);
+        if (!dev) CK(cudaStreamSynchronize(b.st));
+        return 0;
+    } catch (std::exception& e) {
+        return fail(e);
+    }
+}
+
+int nd_batch_last_hidden(nd_batch* bh, float* out, int flags) {
+    try {
+        Batch& b = *bh->b;
+        CK(cudaSetDevice(b.m->device));
+        if (b.last_rows < 1) throw std::runtime_error("no forward has returned outputs yet");
+        // the last row of each sequence's outputs
+        const int per = b.last_rows / b.S;
+        CK(cudaMemcpy2DAsync(out, 768 * sizeof(float), b.h + (size_t)(per - 1) * 768, (size_t)per * 768 * sizeof(float),
+                             768 * sizeof(float), b.S, (flags & ND_DEVICE) ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
+                             b.st));
+        if (!(flags & ND_DEVICE)) CK(cudaStreamSynchronize(b.st));
+        return 0;
+    } catch (std::exception& e) {
+        return fail(e);
+    }
+}
+
+int nd_head_logits(nd_batch* bh, const float* h, int rows, float* out, int flags) {
+    try {
+        Batch& b = *bh->b;
+        Model& m = *b.m;
+        CK(cudaSetDevice(m.device));
+        if (rows < 1 || rows > b.Mmax) throw std::runtime_error("nd_head_logits: rows out of range");
+        const bool dev = flags & ND_DEVICE;
+        CK(cudaMemcpyAsync(b.e, h, (size_t)rows * 768 * sizeof(float), dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                           b.st));
+        ensure_logits(b, rows);
+        launch_prep_act(b.e, 768, 768, rows, b.act, b.sx, b.st);
+        launch_cq_gemm(m.embedding, b.act, b.sx, rows, 1, b.logits, m.c.out_rows(), 0, b.st);
+        b.have_logits = false;
+        CK(cudaMemcpyAsync(out, b.logits, (size_t)rows * m.c.out_rows() * sizeof(float),
+                           dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, b.st));
+        if (!dev) CK(cudaStreamSynchronize(b.st));
+        return 0;
+    } catch (std::exception& e) {
+        return fail(e);
+    }
+}
+
+int nd_head_logits_sparse(nd_batch* bh, const float* h, const int* ids, int n, float* out) {
+    try {
+        Batch& b = *bh->b;
+        Model& m = *b.m;
+        const int V = m.c.out_rows();
+        for (int k = 0; k < n; k++)
+            if (ids[k] < 0 || ids[k] >= V) throw std::runtime_error("nd_head_logits_sparse: id out of range");
+        // the single-row kernel is the prefill combine's block form
+        // (qlinear.rs:454-456): each id scored as a lone block token, i.e.
+        // a T = 4 feed of which it is row 0.
+        CK(cudaSetDevice(m.device));
+        std::vector<float> h4(4 * 768, 0.f);
+        std::memcpy(h4.data(), h, 768 * sizeof(float));
+        CK(cudaMemcpyAsync(b.e, h4.data(), 4 * 768 * sizeof(float), cudaMemcpyHostToDevice, b.st));
+        ensure_logits(b, 4);
+        launch_prep_act(b.e, 768, 768, 4, b.act, b.sx, b.st);
+        launch_cq_gemm(m.embedding, b.act, b.sx, 4, 4, b.logits, V, 0, b.st);
+        b.have_logits = false;
+        std::vector<float> full(V);
+        CK(cudaMemcpyAsync(full.data(), b.logits, V * sizeof(float), cudaMemcpyDeviceToHost, b.st));
+        CK(cudaStreamSynchronize(b.st));
+        uint32_t negu = 0xf149f2cau;
+        float neg;
+        std::memcpy(&neg, &negu, 4);
+        for (int k = 0; k < V; k++) out[k] = neg;
+        for (int k = 0; k < n; k++) out[ids[k]] = full[ids[k]];
+        return 0;
+    } catch (std::exception& e) {
+        return fail(e);
+    }
+}
+
+int nd_cq_pack(const float* w, int rows, int d, unsigned char* codes, unsigned short* norms) {
+    try {
+        cq_pack4(w, rows, d, codes, norms);
+        return 0;
+    } catch (std::exception& e) {
+        return fail(e);
+    }
+}
+
+int nd_synth_cact(int num_layers, int vocab, int engram_slots, int sliding_window, unsigned long long global_mask,
+                  unsigned long long engram_sites, unsigned long long seed, float std, unsigned char* out,
+                  unsigned long long cap, unsigned long long* len) {
+    try {
+        SynthSpec sp;
+        sp.num_layers = num_layers;
+        sp.vocab = vocab;
+        sp.engram_slots = engram_slots;
+        sp.sliding_window = sliding_window;
+        sp.global_mask = global_mask;
+        sp.engram_sites.clear();
+        for (int l = 0; l < 64; l++)
+            if ((engram_sites >> l) & 1) sp.engram_sites.push_back(l);
+        sp.seed = seed;
+        sp.std = std;
+        std::vector<uint8_t> buf = synth_cact(sp);
+        if (len) *len = buf.size();
+        if (out) {
+            if (cap < buf.size()) throw std::runtime_error("nd_synth_cact: buffer too small");
+            std::memcpy(out, buf.data(), buf.size());
+        }
+        return 0;
+    } catch (std::exception& e) {
+        return fail(e);
+    }
+}
+
+long long nd_launch_count(void) { return launch_count(); }
+
+int nd_batch_time_site(nd_batch* bh, int site) {
+    if (!bh) return -1;
+    Batch& b = *bh->b;
+    b.time_site = site;
+    b.ev_used = 0;
+    return 0;
+}
+
+int nd_batch_site_time(nd_batch* bh, double* total_ms, int* launches) {
+    try {
+        Batch& b = *bh->b;
+        CK(cudaSetDevice(b.m->device));
+        CK(cudaStreamSynchronize(b.st));
+        double tot = 0;
+        for (size_t k = 0; k + 1 < b.ev_used; k += 2) {
+            float ms = 0;
+            CK(cudaEventElapsedTime(&ms, b.evs[k], b.evs[k + 1]));
+            tot += ms;
+        }
+        if (total_ms) *total_ms = tot;
+        if (launches) *launches = (int)(b.ev_used / 2);
+        return 0;
+    } catch (std::exception& e) {
+        return fail(e);
+    }
+}
+
+int nd_batch_debug_layer(nd_batch* bh, int layer) {
+    if (!bh) return -1;
+    bh->b->debug_layer = layer;
+    return 0;
+}
+
+int nd_batch_debug(nd_batch* bh, const char* name, float* out, long long cap) {
+    try {
+        Batch& b = *bh->b;
+        CK(cudaSetDevice(b.m->device));
+        CK(cudaStreamSynchronize(b.st));
+        const int M = b.S * b.last_T;
+        std::string nm(name);
+        const float* src = nullptr;
+        size_t n = 0;
+        if (nm.rfind("snap.", 0) == 0) {
+            auto it = b.snaps.find(nm);
+            if (it == b.snaps.end()) return -1;
+            src = it->second.first;
+            n = it->second.second;
+        } else if (nm == "xs") { src = b.xs; n = (size_t)M * 3072; }
+        else if (nm == "u") { src = b.u; n = (size_t)M * 768; }
+        else if (nm == "p") { src = b.p; n = (size_t)M * 24; }
+        else if (nm == "x1") { src = b.x1; n = (size_t)M * 768; }
+        else if (nm == "proj") { src = b.proj; n = (size_t)M * 1568; }
+        else if (nm == "qbuf") { src = b.qbuf; n = (size_t)M * 576; }
+        else if (nm == "att") { src = b.att; n = (size_t)M * 768; }
+        else if (nm == "o") { src = b.o; n = (size_t)M * 768; }
+        else if (nm == "h") { src = b.h; n = (size_t)b.last_rows * 768; }
+        else if (nm == "logits") { src = b.logits; n = b.logits ? (size_t)b.logits_rows * b.m->c.out_rows() : 0; }
+        else if (nm.rfind("ekv", 0) == 0) { src = b.ekv + (size_t)std::stoi(nm.substr(3)) * b.Mmax * 1536; n = (size_t)M * 1536; }
+        else if (nm.rfind("evals", 0) == 0) { src = b.evals + (size_t)std::stoi(nm.substr(5)) * b.Mmax * 768; n = (size_t)M * 768; }
+        else return -1;
+        if (!src) return -1;
+        if (out) CK(cudaMemcpy(out, src, std::min<size_t>(n, (size_t)cap) * sizeof(float), cudaMemcpyDeviceToHost));
+        return (int)n;
+    } catch (std::exception& e) {
+        return fail(e);
+    }
+}
+
+// ------------------------------------------------------------- needle.h
+
+static std::mutex g_engine_mu;
+static std::unique_ptr<nd_model> g_model;
+static std::string g_needle_err;
+
+static int needle_fail(const std::string& msg, int code) {
+    g_needle_err = msg;
+    return code;
+}
+
+int needle_load(const unsigned char* cact, unsigned long long n) {
+    std::lock_guard<std::mutex> lk(g_engine_mu);
+    if (!cact) return needle_fail("needle_load: null archive", -1);
+    int device = 0;
+    if (const char* d = getenv("NEEDLE_DEVICE")) device = atoi(d);
+    nd_model* m = nullptr;
+    if (nd_model_load(cact, n, device, &m) != 0) return needle_fail(g_err, -1);
+    g_model.reset(m);
+    return 0;
+}
+
+static const char* AGENT_MISSING =
+    "the agent layer (tokenizer, chat template, tool-call grammar) is not part of this GPU engine; drive the model "
+    "through needle_engine.h";
+
+int needle_init(const char*, const char*, const char*) {
+    std::lock_guard<std::mutex> lk(g_engine_mu);
+    if (!g_model) return needle_fail("no model loaded: call needle_load first", -1);
+    return needle_fail(AGENT_MISSING, -1);
+}
+
+int needle_complete(const char*, int, char* out, int out_capacity) {
+    std::lock_guard<std::mutex> lk(g_engine_mu);
+    std::string msg = "no toolset bound: call needle_init first";
+    g_needle_err = msg;
+    if (out && out_capacity > (int)msg.size()) {
+        std::memcpy(out, msg.c_str(), msg.size() + 1);
+    }
+    return -1;
+}
+
+int needle_embed(const char*, float* out, int) {
+    std::lock_guard<std::mutex> lk(g_engine_mu);
+    if (!g_model) return needle_fail("no model loaded", -1);
+    // lib.rs:152: confidence_queries * d_model when the archive has no
+    // embedding head (probe heads are not loaded by this engine).
+    if (!out) return 4 * g_model->m->c.d;
+    return needle_fail("no toolset bound: call needle_init first", -1);
+}
+
+void needle_reset(void) {}
+
+const char* needle_last_error(void) { return g_needle_err.c_str(); }
+
+}  // extern "C"

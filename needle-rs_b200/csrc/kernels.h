@@ -1,0 +1,84 @@
+// Kernel launchers of the Needle 3 packed forward pass on sm_100a.
+//
+// Row index m of a step is (sequence s, token i) = (m / T, m % T): every
+// sequence of a batch feeds the same T tokens at the same positions
+// p0 .. p0 + T - 1. Caches are per sequence and per layer.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace nd {
+
+// A CQ-4 matrix as the archive stores it: codes [out][groups][64] (two codes
+// per byte, low nibble first), f16 group norms [out][groups].
+struct DevMat {
+    const uint8_t* codes = nullptr;
+    const uint16_t* norms = nullptr;
+    int out = 0, in_dim = 0, groups = 0;
+};
+
+// One layer's weights on the device (small weights widened to f32, which
+// is exact for the archive's f16 values).
+struct LayerW {
+    const float *norm_in, *q_taps, *k_taps, *v_taps, *q_norm, *k_norm, *post_norm, *pre_hada;
+    const float *d1, *d2, *b2, *d3, *d4, *kron[6], *cond_v, *cond_u;
+    const int8_t* phi_q;  // [24][3072]
+    const float* phi_s;   // [24]
+    float attn_gate, a_pre, a_post, a_res;
+    float b_pre[4], b_post[4], b_res[16];
+    DevMat qkvg, out;
+};
+
+// Per-sequence caches of one batch.
+struct Caches {
+    int S, L, cap;        // sequences, layers, KV slots per sequence
+    int8_t* k8;           // [S][L][2][cap][48]
+    float* ks;            // [S][L][2][cap]
+    int8_t* v8;           // [S][L][2][cap][64]
+    float* vs;            // [S][L][2][cap]
+    float* hist;          // [S][L][HIST_RING][800] pre-tap q|k|v rows by position
+    int8_t* ev8;          // [S][sites][ENG_RING][768] engram value history
+    float* evs;           // [S][sites][ENG_RING][24]
+    int32_t* tokens;      // [S][cap]
+};
+
+// Pre-tap rows kept per (sequence, layer): the conv reads two back, and a
+// chunk's rows are written only after every row has read its taps.
+constexpr int HIST_RING = 2;
+// Engram value history kept per (sequence, site), by position: a chunk's 32
+// rows are all written before the dilated conv reads 3 taps of dilation 3
+// back, so the ring must hold 32 + 9 positions.
+constexpr int ENG_RING = 64;
+
+// Kernels this process has launched through the launchers below.
+long long launch_count();
+
+void set_constants(const int8_t vals[16], const float fvals[16], float cbs, float hs128);
+
+void launch_write_tokens(const int32_t* ids, int S, int T, int p0, Caches c, cudaStream_t st);
+void launch_embed(DevMat emb, const int32_t* ids, int M, float* xs, cudaStream_t st);
+void launch_prep_act(const float* x, int ldx, int K, int M, int8_t* act, float* sx, cudaStream_t st);
+// y[m][col0 + n] for n < W.out. T sets the combine per row: T == 1 the
+// decode kernel, else the prefill kernel with the block/remainder rule over
+// each sequence's T rows.
+void launch_cq_gemm(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y, int ldy, int col0, cudaStream_t st);
+void launch_engram_gather(DevMat tables, Caches c, int S, int T, int p0, int slots, float* e, cudaStream_t st);
+void launch_engram_vhist(const float* kv, Caches c, int site, int nsites, int S, int T, int p0, cudaStream_t st);
+void launch_engram_conv(const float* taps, Caches c, int site, int nsites, int S, int T, int p0, float* v, cudaStream_t st);
+void launch_mhc_read(LayerW w, int lane, const float* xs, int M, float* u, float* p, cudaStream_t st);
+void launch_input_norm(LayerW w, const float* u, const float* ekv, const float* evals, int M, float* x1, int8_t* act,
+                       float* sx, cudaStream_t st);
+void launch_conv_rope_kv(LayerW w, int l, const float* proj, Caches c, int S, int T, int p0, int hist_base, const float* cosr,
+                         const float* sinr, float* qbuf, cudaStream_t st);
+void launch_hist_update(const float* proj, Caches c, int l, int S, int T, int p0, cudaStream_t st);
+void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int S, int T, int p0, int window, float* att,
+                      cudaStream_t st);
+void launch_post_block(LayerW w, int lane, const float* o, const float* x1, const float* u, const float* p,
+                       const int32_t* perm1, const int32_t* perm2, int M, float* xs, cudaStream_t st);
+void launch_final_hidden(const float* xs, const float* final_norm, int S, int T, int all_rows, float* h, cudaStream_t st);
+void launch_rope_rows(const float* table_cos, const float* table_sin, const float* sd, const float* cd, int p0, int T,
+                      int recur, float* state, float* cosr, float* sinr, cudaStream_t st);
+void launch_masked_argmax(const float* logits, int S, int V, const uint8_t* allow, int32_t* next, cudaStream_t st);
+
+}  // namespace nd

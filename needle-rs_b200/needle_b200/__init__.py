@@ -1,0 +1,249 @@
+"""Python view of libneedle3.so, the B200 engine for Needle 3.
+
+Mirrors the reference engine's model-level interface
+(crates/needle-engine/src/model.rs: ``Model::{forward, prefill, session,
+head_logits, head_logits_sparse}``, ``Session``) over the C ABI declared in
+include/needle_engine.h, batched: a ``Batch`` is S sessions fed in lockstep.
+There is no CPU fallback; importing fails if the CUDA library is missing.
+"""
+
+import ctypes as C
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libneedle3.so")
+
+OUT_NONE, OUT_LAST_LOGITS, OUT_LAST_HIDDEN, OUT_ALL_LOGITS, OUT_HIDDEN = 0, 1, 2, 3, 4
+SITES = dict(none=0, qkvg=1, out=2, lm_head=3, engram_kv=4, attention=5, post=6, mhc=7, conv=8, norm=9)
+ND_DEVICE = 1
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with __graft_entry__.build()")
+        L = C.CDLL(LIB_PATH)
+        P, I, U64 = C.c_void_p, C.c_int, C.c_uint64
+        sig = {
+            "nd_last_error": (C.c_char_p, []),
+            "nd_model_load": (I, [P, U64, I, C.POINTER(P)]),
+            "nd_model_free": (None, [P]),
+            "nd_model_dims": (I, [P, P]),
+            "nd_batch_new": (I, [P, I, I, C.POINTER(P)]),
+            "nd_batch_free": (None, [P]),
+            "nd_batch_len": (I, [P]),
+            "nd_batch_forward": (I, [P, P, I, I, P, I]),
+            "nd_batch_step": (I, [P, P, P, I]),
+            "nd_batch_last_hidden": (I, [P, P, I]),
+            "nd_head_logits": (I, [P, P, I, P, I]),
+            "nd_head_logits_sparse": (I, [P, P, P, I, P]),
+            "nd_batch_stream": (P, [P]),
+            "nd_cq_pack": (I, [P, I, I, P, P]),
+            "nd_synth_cact": (I, [I, I, I, I, U64, U64, U64, C.c_float, P, U64, C.POINTER(U64)]),
+            "nd_batch_debug": (I, [P, C.c_char_p, P, C.c_longlong]),
+            "nd_batch_debug_layer": (I, [P, I]),
+            "nd_launch_count": (C.c_longlong, []),
+            "nd_batch_time_site": (I, [P, I]),
+            "nd_batch_site_time": (I, [P, C.POINTER(C.c_double), C.POINTER(I)]),
+            "needle_load": (I, [P, U64]),
+            "needle_init": (I, [C.c_char_p, C.c_char_p, C.c_char_p]),
+            "needle_complete": (I, [C.c_char_p, I, P, I]),
+            "needle_embed": (I, [C.c_char_p, P, I]),
+            "needle_reset": (None, []),
+            "needle_last_error": (C.c_char_p, []),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _err():
+    return RuntimeError(lib().nd_last_error().decode(errors="replace"))
+
+
+def _p(a):
+    if a is None:
+        return None
+    if isinstance(a, int):
+        return C.c_void_p(a)
+    if hasattr(a, "data_ptr"):  # a torch tensor on the device
+        return C.c_void_p(a.data_ptr())
+    return a.ctypes.data_as(C.c_void_p)
+
+
+NEEDLE3_DEFAULTS = dict(num_layers=20, vocab=16384, engram_slots=18432, sliding_window=1024,
+                        global_layers=(4, 9, 14, 19), engram_sites=(3, 7, 11, 15, 19))
+
+
+def launch_count() -> int:
+    """Kernel launches this process has issued through the engine."""
+    return lib().nd_launch_count()
+
+
+def synth_cact(seed=0, std=0.02, **shape) -> bytes:
+    """A random-init Needle 3 archive (every tensor ~N(0, std^2)), CQ-4
+    matrices packed by the reference's quantizer, in the reference's record
+    order (crates/needle-core/src/cact.rs:279-475)."""
+    g = dict(NEEDLE3_DEFAULTS)
+    g.update(shape)
+    gm = sum(1 << l for l in g["global_layers"])
+    es = sum(1 << l for l in g["engram_sites"])
+    n = C.c_uint64(0)
+    args = (g["num_layers"], g["vocab"], g["engram_slots"], g["sliding_window"], gm, es, seed, std)
+    if lib().nd_synth_cact(*args, None, 0, C.byref(n)) != 0:
+        raise _err()
+    buf = np.zeros(n.value, np.uint8)
+    if lib().nd_synth_cact(*args, _p(buf), n.value, C.byref(n)) != 0:
+        raise _err()
+    return buf.tobytes()
+
+
+def cq_pack(w):
+    """crates/needle-core/src/quant.rs:233-256 (4-bit, group 128)."""
+    w = np.ascontiguousarray(w, np.float32)
+    rows, d = w.shape
+    g = (d + 127) // 128
+    codes = np.zeros((rows, g * 64), np.uint8)
+    norms = np.zeros((rows, g), np.uint16)
+    if lib().nd_cq_pack(_p(w), rows, d, _p(codes), _p(norms)) != 0:
+        raise _err()
+    return codes, norms
+
+
+class Model:
+    """A packed model resident on one GPU (`Model::quantized`)."""
+
+    def __init__(self, archive: bytes, device: int = 0):
+        buf = np.frombuffer(archive, np.uint8)
+        h = C.c_void_p()
+        if lib().nd_model_load(_p(buf), len(buf), device, C.byref(h)) != 0:
+            raise _err()
+        self._h = h
+        self.device = device
+        dims = np.zeros(9, np.int32)
+        lib().nd_model_dims(self._h, _p(dims))
+        (self.vocab, self.out_rows, self.d_model, self.num_layers, self.num_heads, self.num_kv_heads,
+         self.qk_head_dim, self.v_head_dim, self.max_seq_len) = (int(v) for v in dims)
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().nd_model_free(self._h)
+            self._h = None
+
+    def batch(self, num_seqs: int, max_len: int) -> "Batch":
+        return Batch(self, num_seqs, max_len)
+
+    def session(self, max_len: int = None) -> "Batch":
+        """One sequence (`Model::session`)."""
+        return Batch(self, 1, max_len or self.max_seq_len)
+
+
+class Batch:
+    """S sessions fed in lockstep on the model's GPU."""
+
+    def __init__(self, model: Model, num_seqs: int, max_len: int):
+        h = C.c_void_p()
+        if lib().nd_batch_new(model._h, num_seqs, max_len, C.byref(h)) != 0:
+            raise _err()
+        self._h = h
+        self.model = model
+        self.num_seqs = num_seqs
+        self.max_len = max_len
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().nd_batch_free(self._h)
+            self._h = None
+
+    def __len__(self):
+        return lib().nd_batch_len(self._h)
+
+    @property
+    def stream(self) -> int:
+        return lib().nd_batch_stream(self._h) or 0
+
+    def forward(self, ids, outputs=OUT_LAST_LOGITS, out=None):
+        """`Model::forward` for every sequence: ids [S, t] (host array, or a
+        device tensor with ``out`` also on the device)."""
+        m = self.model
+        dev = hasattr(ids, "data_ptr")
+        if dev:
+            S, t = ids.shape
+        else:
+            ids = np.ascontiguousarray(ids, np.int32).reshape(self.num_seqs, -1)
+            S, t = ids.shape
+        rows = {OUT_NONE: 0, OUT_LAST_LOGITS: 1, OUT_LAST_HIDDEN: 1, OUT_ALL_LOGITS: t, OUT_HIDDEN: t}[outputs]
+        width = m.d_model if outputs in (OUT_LAST_HIDDEN, OUT_HIDDEN) else m.out_rows
+        if out is None and not dev and rows:
+            out = np.zeros((S, rows, width), np.float32)
+        rc = lib().nd_batch_forward(self._h, _p(ids), t, outputs, _p(out), ND_DEVICE if dev else 0)
+        if rc < 0:
+            raise _err()
+        return out
+
+    prefill = forward  # `Model::prefill` equals `forward` without an attention span
+
+    def step(self, allow_bits=None, next_ids=None):
+        """One greedy decode step: argmax of the last logits under the masks,
+        fed back; returns the chosen ids [S]."""
+        dev = next_ids is not None and hasattr(next_ids, "data_ptr")
+        if next_ids is None:
+            next_ids = np.zeros(self.num_seqs, np.int32)
+        if allow_bits is not None and not dev:
+            allow_bits = np.ascontiguousarray(allow_bits, np.uint8)
+        if lib().nd_batch_step(self._h, _p(allow_bits), _p(next_ids), ND_DEVICE if dev else 0) != 0:
+            raise _err()
+        return next_ids
+
+    def last_hidden(self):
+        out = np.zeros((self.num_seqs, self.model.d_model), np.float32)
+        if lib().nd_batch_last_hidden(self._h, _p(out), 0) != 0:
+            raise _err()
+        return out
+
+    def head_logits(self, h):
+        h = np.ascontiguousarray(h, np.float32).reshape(-1, self.model.d_model)
+        out = np.zeros((h.shape[0], self.model.out_rows), np.float32)
+        if lib().nd_head_logits(self._h, _p(h), h.shape[0], _p(out), 0) != 0:
+            raise _err()
+        return out
+
+    def head_logits_sparse(self, h, ids):
+        h = np.ascontiguousarray(h, np.float32)
+        ids = np.ascontiguousarray(ids, np.int32)
+        out = np.zeros(self.model.out_rows, np.float32)
+        if lib().nd_head_logits_sparse(self._h, _p(h), _p(ids), len(ids), _p(out)) != 0:
+            raise _err()
+        return out
+
+    def time_site(self, site):
+        """Record CUDA events around every launch of a site (see SITES)."""
+        if lib().nd_batch_time_site(self._h, SITES[site] if isinstance(site, str) else site) != 0:
+            raise _err()
+
+    def site_time(self):
+        """(summed kernel milliseconds, launches) of the timed site."""
+        ms = C.c_double(0)
+        n = C.c_int(0)
+        if lib().nd_batch_site_time(self._h, C.byref(ms), C.byref(n)) != 0:
+            raise _err()
+        return ms.value, n.value
+
+    def debug(self, name):
+        n = lib().nd_batch_debug(self._h, name.encode(), None, 0)
+        if n < 0:
+            raise KeyError(name)
+        out = np.zeros(n, np.float32)
+        lib().nd_batch_debug(self._h, name.encode(), _p(out), n)
+        return out
+
+    def debug_layer(self, layer):
+        lib().nd_batch_debug_layer(self._h, layer)

@@ -1,0 +1,31 @@
+"""Build recipe for the CPU oracle (test infrastructure only).
+
+Compiles ``needle_oracle.cpp`` — the scalar C++ restatement of needle-rs's
+packed CPU path — into ``oracle/liboracle.so``. Float contraction is off so
+every fused multiply-add is the explicit ``fmaf`` the reference's ``mul_add``
+calls for; ``-mfma`` only lets those calls compile to the hardware instruction.
+"""
+
+import os
+import platform
+import subprocess
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+SRC = os.path.join(HERE, "needle_oracle.cpp")
+LIB = os.path.join(HERE, "liboracle.so")
+
+
+def build(force: bool = False) -> str:
+    if not force and os.path.exists(LIB) and os.path.getmtime(LIB) >= os.path.getmtime(SRC):
+        return LIB
+    flags = ["-O2", "-std=c++17", "-fPIC", "-shared", "-pthread", "-ffp-contract=off", "-fno-fast-math"]
+    if platform.machine() in ("x86_64", "AMD64"):
+        flags += ["-mfma", "-mavx2"]
+    tmp = LIB + ".tmp"
+    subprocess.check_call(["g++", *flags, SRC, "-o", tmp])
+    os.replace(tmp, LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(force=True))

@@ -1,0 +1,1716 @@
+// TEST INFRASTRUCTURE ONLY — never linked into or called by the product path.
+//
+// A scalar C++ restatement of ddrscott/needle-rs's packed CPU inference path
+// (the native-exact `needle-engine` forward pass on a `.cact` archive), used
+// by tests/ as the parity checker for the CUDA engine and by bench.py as the
+// timed CPU baseline ("port"). The reference is Rust and cannot be built in
+// this image (no cargo/rustc), so this file restates its arithmetic from the
+// source. Every function names the reference file:line it follows; paths are
+// relative to the needle-rs repository root. The spec is the portable scalar
+// branch of each reference function (the `#[cfg(not(aarch64|wasm32))]` arms
+// and the `*_ref` functions the SIMD kernels are tested bit-equal against).
+//
+// Float discipline: compiled with -ffp-contract=off; every `mul_add` of the
+// reference is an explicit fmaf here, every other op is a single IEEE op in
+// the reference's order. Integer sums are exact and computed in any order.
+// libm stand-ins follow the reference's non-Apple `sys` module
+// (crates/needle-engine/src/infer.rs:83-102): f32 exp/pow/sincos are f64 libm
+// rounded once; this file uses glibc's f64 functions where the reference links
+// the `libm` crate 0.2.16 (parity of those last bits is not pinned).
+
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <cstdio>
+#include <string>
+#include <vector>
+#include <map>
+#include <thread>
+#include <atomic>
+#include <algorithm>
+#include <functional>
+#include <stdexcept>
+
+namespace orc {
+
+// ---------------------------------------------------------------- numerics
+
+static inline uint32_t fbits(float f) { uint32_t u; std::memcpy(&u, &f, 4); return u; }
+static inline float bitsf(uint32_t u) { float f; std::memcpy(&f, &u, 4); return f; }
+
+// `half` 2.7.1 f16 <-> f32, round to nearest even (Cargo.lock pins half 2.7.1).
+float f16_to_f32(uint16_t h) {
+    uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    uint32_t e = (h >> 10) & 0x1f, m = h & 0x3ff;
+    if (e == 0) {
+        float v = (float)m * 5.9604644775390625e-8f;  // m * 2^-24, exact
+        return bitsf(fbits(v) | sign);
+    }
+    if (e == 31) return bitsf(sign | 0x7f800000u | (m << 13));
+    return bitsf(sign | ((e + 112) << 23) | (m << 13));
+}
+
+uint16_t f32_to_f16(float f) {
+    uint32_t x = fbits(f);
+    uint16_t sign = (uint16_t)((x >> 16) & 0x8000u);
+    uint32_t ax = x & 0x7fffffffu;
+    if (ax >= 0x7f800000u) return sign | (ax > 0x7f800000u ? 0x7e00 : 0x7c00);
+    if (ax >= 0x477ff000u) return sign | 0x7c00;
+    if (ax < 0x38800000u) {
+        float s = bitsf(ax) * 16777216.0f;  // exact power-of-two scaling
+        return sign | (uint16_t)std::nearbyint(s);
+    }
+    uint32_t h = (((ax >> 23) - 112) << 10) | ((ax & 0x7fffff) >> 13);
+    uint32_t rem = ax & 0x1fff;
+    if (rem > 0x1000 || (rem == 0x1000 && (h & 1))) h++;
+    return sign | (uint16_t)h;
+}
+
+// crates/needle-engine/src/infer.rs:83-102 (non-Apple `sys`).
+static inline float lexpf(float x) { return (float)std::exp((double)x); }
+static inline double lexp(double x) { return std::exp(x); }
+static inline float lpowf(float x, float y) { return (float)std::pow((double)x, (double)y); }
+static inline void lsincosf(float x, float* s, float* c) {
+    double sd, cd;
+    sincos((double)x, &sd, &cd);
+    *s = (float)sd;
+    *c = (float)cd;
+}
+
+// crates/needle-engine/src/qlinear.rs:40
+static const float K127 = bitsf(0x3c010204u);
+// crates/needle-engine/src/infer.rs:30-36
+static const float INV_SQRT_QK = bitsf(0x3e13cd3au);
+static const float Q21 = bitsf(0x49fffff8u);
+static const float C21 = bitsf(0x35000004u);
+static const float NEG = bitsf(0xf149f2cau);
+static const int NATIVE_TEAM = 4;  // infer.rs:38
+static const int ROLLBACK = 32;    // model.rs:184
+static const int GROUP = 128;      // qlinear.rs:37
+
+// Rust f32::max / f32::min (IEEE maxNum: a NaN operand loses).
+static inline float rmax(float a, float b) { return std::fmax(a, b); }
+static inline float rmin(float a, float b) { return std::fmin(a, b); }
+// Rust f32::round: half away from zero.
+static inline float rround(float x) { return std::round(x); }
+
+// crates/needle-engine/src/infer.rs:353-366
+float nexp(float x) {
+    x = rmin(rmax(x, bitsf(0xc2b0c0a5u)), bitsf(0x42b0c0a5u));
+    float k = std::nearbyint(x * bitsf(0x3fb8aa3bu));  // round_ties_even
+    float r = std::fmaf(k, bitsf(0xbf318000u), x);
+    r = std::fmaf(k, bitsf(0x395e8083u), r);
+    float p = std::fmaf(bitsf(0x39506967u), r, bitsf(0x3ab743ceu));
+    p = std::fmaf(r, p, bitsf(0x3c088908u));
+    p = std::fmaf(r, p, bitsf(0x3d2aa9c1u));
+    p = std::fmaf(r, p, bitsf(0x3e2aaaaau));
+    p = std::fmaf(r, p, 0.5f);
+    float y = std::fmaf(r * r, p, r);
+    float s = bitsf((uint32_t)(((int32_t)k << 23) + 0x3f800000));
+    return std::fmaf(s, y, s);
+}
+
+// crates/needle-engine/src/infer.rs:372-417 (scalar arm 405-416)
+float dot16(const float* x, const float* y, int n) {
+    float a[4][4] = {{0}};
+    for (int c = 0; c < n / 16; c++)
+        for (int j = 0; j < 4; j++)
+            for (int l = 0; l < 4; l++) {
+                int i = c * 16 + j * 4 + l;
+                a[j][l] = std::fmaf(x[i], y[i], a[j][l]);
+            }
+    float t[4];
+    for (int l = 0; l < 4; l++) t[l] = ((a[2][l] + a[3][l]) + a[1][l]) + a[0][l];
+    return (t[0] + t[1]) + (t[2] + t[3]);
+}
+
+// infer.rs:421-423
+static inline float rinv(float ss, int n) { return 1.0f / std::sqrt(ss / (float)n + 1e-6f); }
+
+// infer.rs:426-443 (scalar arm); s given as f32 (f16-exact archive values)
+void zcn(const float* x, const float* s, float* out, int n) {
+    float r = rinv(dot16(x, x, n), n);
+    for (int i = 0; i < n; i++) {
+        float t = x[i] * r;
+        out[i] = std::fmaf(t, s[i], t);
+    }
+}
+
+// qlinear.rs:77-88, 113-140 (scalar arms): absmax int8, round half away, saturate.
+float quant_i8(const float* x, int n, int8_t* q) {
+    float m = 0.f;
+    for (int i = 0; i < n; i++) m = rmax(m, std::fabs(x[i]));
+    float s = m > 0.f ? m * K127 : 1.0f;
+    float inv = 1.0f / s;
+    for (int i = 0; i < n; i++) {
+        float v = rround(x[i] * inv);
+        v = std::min(std::max(v, -128.f), 127.f);
+        q[i] = (int8_t)v;
+    }
+    return s;
+}
+
+// ------------------------------------------------------------ quant.rs
+
+// crates/needle-core/src/quant.rs:19-47 — the reference's Lloyd-Max
+// centroids as exact f64 bit patterns (a data table that must match).
+static const uint64_t LM2[4] = {0xbff81b52e4028034ull, 0xbfdce467275b97c2ull, 0x3fdcfd177c54d348ull, 0x3ff828af1c856640ull};
+static const uint64_t LM3[8] = {0xc00121468f3c6b81ull, 0xbff556e7125deacaull, 0xbfe7f2e0f9d592abull, 0xbfce6e4509e1aa2cull,
+                                0x3fd000bb25e4dfa5ull, 0x3fe82dc469b936a5ull, 0x3ff568607ac227c5ull, 0x40012e5beccc8fdaull};
+static const uint64_t LM4[16] = {0xc005ae0f408928fbull, 0xc0005b0b8a516d54ull, 0xbff9841ff0758fc8ull, 0xbff3bbbebadac679ull,
+                                 0xbfed82c6dd21f59eull, 0xbfe47717151708b5ull, 0xbfd7d9b9e4b565faull, 0xbfbd4ca474b8559bull,
+                                 0x3fc2683e9154fce2ull, 0x3fd9daf49368793aull, 0x3fe586b43e57d29dull, 0x3feec3d50cbc3b33ull,
+                                 0x3ff4688db93b85f1ull, 0x3ffa3164906b428full, 0x4000ace7bbde2442ull, 0x4005ed98d06f2a4aull};
+
+static double d_of(uint64_t b) { double d; std::memcpy(&d, &b, 8); return d; }
+
+// quant.rs:50-68
+std::vector<float> codebook(int bits, int group) {
+    std::vector<double> c;
+    if (bits == 2) for (auto b : LM2) c.push_back(d_of(b));
+    else if (bits == 3) for (auto b : LM3) c.push_back(d_of(b));
+    else if (bits == 4) for (auto b : LM4) c.push_back(d_of(b));
+    else if (bits == 5) c = {-1.2240064, 0.0, 1.2240064};
+    else throw std::runtime_error("no CQ codebook");
+    double s = std::sqrt((double)group);
+    std::vector<float> out;
+    for (double v : c) out.push_back((float)(v / s));
+    return out;
+}
+
+// quant.rs:71-73
+static inline float hadamard_scale(int n) { return (float)(1.0 / std::sqrt((double)n)); }
+
+// quant.rs:91-105
+void fwht(float* x, int n) {
+    for (int h = 1; h < n; h *= 2)
+        for (int i = 0; i < n; i += 2 * h)
+            for (int j = i; j < i + h; j++) {
+                float a = x[j], b = x[j + h];
+                x[j] = a + b;
+                x[j + h] = a - b;
+            }
+}
+
+// quant.rs:109-115
+void rotate(float* x, int n) {
+    fwht(x, n);
+    float s = hadamard_scale(n);
+    for (int i = 0; i < n; i++) x[i] *= s;
+}
+
+// quant.rs:119-124
+int nearest(float x, const float* cb, int n) {
+    int pos = 0;
+    while (pos < n && cb[pos] < x) pos++;
+    pos = std::min(std::max(pos, 1), n - 1);
+    float l = cb[pos - 1], r = cb[pos];
+    return std::fabs(x - l) <= std::fabs(x - r) ? pos - 1 : pos;
+}
+
+// quant.rs:127-135
+static float quantize_group(float* g, const float* cb, int ncb, uint8_t* idx) {
+    rotate(g, GROUP);
+    float ss = 0.f;
+    for (int i = 0; i < GROUP; i++) ss = ss + g[i] * g[i];
+    float norm = std::sqrt(ss);
+    float denom = rmax(norm, 1e-12f);
+    for (int i = 0; i < GROUP; i++) idx[i] = (uint8_t)nearest(g[i] / denom, cb, ncb);
+    return norm;
+}
+
+// quant.rs:185-198 (4-bit: byte j = idx[2j] | idx[2j+1] << 4)
+static void pack_lsb4(const uint8_t* idx, int n, uint8_t* out) {
+    for (int j = 0; j < n / 2; j++) out[j] = (uint8_t)(idx[2 * j] | (idx[2 * j + 1] << 4));
+}
+
+// quant.rs:233-256 (bits = 4)
+void cq_pack(const float* w, int rows, int d, uint8_t* packed, uint16_t* norms) {
+    std::vector<float> cb = codebook(4, GROUP);
+    int in_pad = (d + GROUP - 1) / GROUP * GROUP, groups = in_pad / GROUP;
+    int per_row = in_pad / 2;
+    std::vector<uint8_t> idx(in_pad);
+    float g[GROUP];
+    for (int r = 0; r < rows; r++) {
+        const float* src = w + (size_t)r * d;
+        for (int gi = 0; gi < groups; gi++) {
+            int start = gi * GROUP, take = std::min(GROUP, std::max(0, d - start));
+            for (int i = 0; i < GROUP; i++) g[i] = i < take ? src[start + i] : 0.f;
+            float norm = quantize_group(g, cb.data(), (int)cb.size(), idx.data() + start);
+            norms[(size_t)r * groups + gi] = f32_to_f16(norm);
+        }
+        pack_lsb4(idx.data(), in_pad, packed + (size_t)r * per_row);
+    }
+}
+
+// --------------------------------------------------------------- rng.rs
+
+// crates/needle-core/src/rng.rs:4-74
+struct Mt19937 {
+    uint32_t mt[624];
+    int idx;
+    explicit Mt19937(uint32_t seed) {
+        mt[0] = seed;
+        for (int i = 1; i < 624; i++) mt[i] = 1812433253u * (mt[i - 1] ^ (mt[i - 1] >> 30)) + (uint32_t)i;
+        idx = 624;
+    }
+    void twist() {
+        for (int i = 0; i < 624; i++) {
+            uint32_t y = (mt[i] & 0x80000000u) | (mt[(i + 1) % 624] & 0x7fffffffu);
+            uint32_t v = mt[(i + 397) % 624] ^ (y >> 1);
+            if (y & 1) v ^= 0x9908b0dfu;
+            mt[i] = v;
+        }
+        idx = 0;
+    }
+    uint32_t next() {
+        if (idx >= 624) twist();
+        uint32_t y = mt[idx++];
+        y ^= y >> 11;
+        y ^= (y << 7) & 0x9d2c5680u;
+        y ^= (y << 15) & 0xefc60000u;
+        return y ^ (y >> 18);
+    }
+    uint32_t interval(uint32_t max) {
+        if (max == 0) return 0;
+        uint32_t mask = max;
+        mask |= mask >> 1; mask |= mask >> 2; mask |= mask >> 4; mask |= mask >> 8; mask |= mask >> 16;
+        for (;;) {
+            uint32_t v = next() & mask;
+            if (v <= max) return v;
+        }
+    }
+    std::vector<int64_t> permutation(int n) {
+        std::vector<int64_t> a(n);
+        for (int i = 0; i < n; i++) a[i] = i;
+        for (int i = n - 1; i >= 1; i--) std::swap(a[i], a[interval((uint32_t)i)]);
+        return a;
+    }
+};
+
+// ------------------------------------------------------------ cact.rs
+
+// crates/needle-core/src/cact.rs:18-22, 47-244
+static const uint32_t TAG = 0x05E12A84u;
+static const uint32_t TAG_V2 = 0x05E12A83u;
+static const int HEADER_BYTES = 49 * 4;
+static const int REC_SIZE = 44;
+enum Dtype { F16 = 1, F32 = 2, CQ = 3, RAW = 4 };
+
+struct Record {
+    int dtype;
+    std::vector<int64_t> shape;
+    uint64_t offset, nbytes;
+    uint32_t group, bits;
+};
+
+struct Header {
+    uint32_t u[49];
+    uint32_t num_tensors() const { return u[1]; }
+};
+
+struct Archive {
+    const uint8_t* data;
+    size_t len;
+    uint32_t h[49];
+    std::vector<float> cb;
+    std::vector<Record> recs;
+    const uint8_t* bytes(size_t i) const { return data + recs[i].offset; }
+};
+
+static uint32_t rd32(const uint8_t* p) { uint32_t v; std::memcpy(&v, p, 4); return v; }
+static uint64_t rd64(const uint8_t* p) { uint64_t v; std::memcpy(&v, p, 8); return v; }
+
+// cact.rs:122-165 (Header::parse), 230-243 (Record::parse), 580-601 (Archive::parse)
+void parse_archive(const uint8_t* data, size_t len, Archive& a) {
+    if (len < (size_t)HEADER_BYTES) throw std::runtime_error("not a complete .cact archive");
+    uint32_t tag = rd32(data);
+    if (tag != TAG) {
+        if (tag == TAG_V2) throw std::runtime_error("this is a Needle 2 archive; Needle 3 is required");
+        throw std::runtime_error("unknown .cact format tag");
+    }
+    for (int i = 0; i < 49; i++) a.h[i] = rd32(data + 4 * i);
+    if (a.h[26] > 4 || a.h[31] > 16) throw std::runtime_error("corrupt .cact header");
+    a.data = data;
+    a.len = len;
+    size_t off = HEADER_BYTES;
+    size_t cbn = a.h[2];
+    if (off + cbn * 4 > len) throw std::runtime_error("truncated codebook");
+    a.cb.resize(cbn);
+    for (size_t i = 0; i < cbn; i++) a.cb[i] = bitsf(rd32(data + off + 4 * i));
+    off += cbn * 4;
+    a.recs.clear();
+    for (uint32_t i = 0; i < a.h[1]; i++) {
+        if (off + REC_SIZE > len) throw std::runtime_error("truncated directory");
+        const uint8_t* b = data + off;
+        Record r;
+        int nd = b[1];
+        if (nd > 4) throw std::runtime_error("corrupt .cact record");
+        r.dtype = b[0];
+        if (r.dtype < 1 || r.dtype > 4) throw std::runtime_error("unknown .cact tensor dtype");
+        for (int k = 0; k < nd; k++) r.shape.push_back(rd32(b + 4 + 4 * k));
+        r.offset = rd64(b + 20);
+        r.nbytes = rd64(b + 28);
+        r.group = rd32(b + 36);
+        r.bits = rd32(b + 40);
+        if (r.offset + r.nbytes > len) throw std::runtime_error("tensor past the end of the archive");
+        a.recs.push_back(r);
+        off += REC_SIZE;
+    }
+}
+
+// ---------------------------------------------------------- qlinear.rs
+
+// qlinear.rs:43-61, 211-265: a CQ-4 matrix, codes kept as stored.
+struct QMat {
+    int out = 0, in_dim = 0, groups = 0;
+    std::vector<uint8_t> codes;  // [out][groups][64]
+    std::vector<uint16_t> norms; // [out][groups] f16 bits
+    std::vector<int8_t> w8;      // codes expanded through `vals`, natural order
+    int8_t vals[16];
+    float cbs;
+    float fvals[16];
+};
+
+// qlinear.rs:211-216
+static void int8_codebook(const std::vector<float>& cb, int8_t* out, float* scale) {
+    float m = 0.f;
+    for (float v : cb) m = rmax(m, std::fabs(v));
+    float s = m > 0.f ? m * K127 : 1.0f;
+    float inv = 1.0f / s;
+    for (size_t i = 0; i < cb.size(); i++) {
+        float v = std::min(std::max(rround(cb[i] * inv), -128.f), 127.f);
+        out[i] = (int8_t)v;
+    }
+    *scale = s;
+}
+
+// qlinear.rs:220-236, 244-265 (4-bit records only)
+static void qmat_from_cq(const Archive& a, size_t i, QMat& q) {
+    const Record& r = a.recs[i];
+    if (r.dtype != CQ) throw std::runtime_error("tensor is not CQ");
+    if (r.group != (uint32_t)GROUP) throw std::runtime_error("CQ group size is not supported");
+    if (r.bits != 4) throw std::runtime_error("only 4-bit CQ records are supported");
+    q.out = (int)r.shape[0];
+    q.in_dim = (int)r.shape[1];
+    q.groups = (q.in_dim + GROUP - 1) / GROUP;
+    size_t ncode = (size_t)q.out * q.groups * 64;
+    const uint8_t* blob = a.bytes(i);
+    q.codes.assign(blob, blob + ncode);
+    q.norms.resize((size_t)q.out * q.groups);
+    std::memcpy(q.norms.data(), blob + ncode, q.norms.size() * 2);
+    std::vector<float> cb = codebook(4, GROUP);
+    int8_t cb8[16];
+    int8_codebook(cb, cb8, &q.cbs);
+    for (int c = 0; c < 16; c++) {
+        q.vals[c] = cb8[c];
+        q.fvals[c] = cb[c];
+    }
+    q.w8.resize(ncode * 2);
+    for (size_t k = 0; k < ncode; k++) {
+        q.w8[2 * k] = q.vals[q.codes[k] & 15];
+        q.w8[2 * k + 1] = q.vals[q.codes[k] >> 4];
+    }
+}
+
+static void qmat_concat(QMat& dst, const QMat& src) {
+    if (dst.out == 0) { dst = src; return; }
+    dst.out += src.out;
+    dst.codes.insert(dst.codes.end(), src.codes.begin(), src.codes.end());
+    dst.norms.insert(dst.norms.end(), src.norms.begin(), src.norms.end());
+    dst.w8.insert(dst.w8.end(), src.w8.begin(), src.w8.end());
+}
+
+// qlinear.rs:309-323
+static void qmat_row(const QMat& q, int r, float* out) {
+    std::vector<float> buf((size_t)q.groups * GROUP);
+    for (int g = 0; g < q.groups; g++) {
+        float norm = f16_to_f32(q.norms[(size_t)r * q.groups + g]);
+        float* dst = buf.data() + g * GROUP;
+        const uint8_t* c = q.codes.data() + ((size_t)r * q.groups + g) * 64;
+        for (int p = 0; p < GROUP; p++) {
+            int code = (p & 1) ? (c[p >> 1] >> 4) : (c[p >> 1] & 15);
+            dst[p] = q.fvals[code] * norm;
+        }
+        rotate(dst, GROUP);
+    }
+    std::memcpy(out, buf.data(), sizeof(float) * q.in_dim);
+}
+
+// qlinear.rs:65-72: activations, stored here in natural order (the
+// reference's de-interleaved layout only permutes exact integer sums).
+struct QAct {
+    int rows = 0, groups = 0;
+    std::vector<int8_t> xq;  // [rows][groups*128], natural order
+    std::vector<float> sx;   // [rows][groups]
+};
+
+// qlinear.rs:152-164
+float prep_group(const float* x, int n, int g, int8_t* q) {
+    float buf[GROUP];
+    int start = g * GROUP, take = std::min(GROUP, n - start);
+    for (int i = 0; i < GROUP; i++) buf[i] = i < take ? x[start + i] : 0.f;
+    rotate(buf, GROUP);
+    return quant_i8(buf, GROUP, q);
+}
+
+// qlinear.rs:191-207
+static QAct qact_new(const float* x, int rows, int in_dim) {
+    QAct a;
+    a.rows = rows;
+    a.groups = (in_dim + GROUP - 1) / GROUP;
+    a.xq.assign((size_t)rows * a.groups * GROUP, 0);
+    a.sx.assign((size_t)rows * a.groups, 0.f);
+    for (int r = 0; r < rows; r++)
+        for (int g = 0; g < a.groups; g++)
+            a.sx[(size_t)r * a.groups + g] =
+                prep_group(x + (size_t)r * in_dim, in_dim, g, a.xq.data() + ((size_t)r * a.groups + g) * GROUP);
+    return a;
+}
+
+// qlinear.rs:327-337: the 4 decode lanes of one group; lane = (p % 32) / 8.
+static inline void lane_sums(const QMat& q, int r, int g, const QAct& a, int t, int32_t s[4]) {
+    const int8_t* w = q.w8.data() + ((size_t)r * q.groups + g) * GROUP;
+    const int8_t* x = a.xq.data() + ((size_t)t * a.groups + g) * GROUP;
+    for (int l = 0; l < 4; l++) {
+        int32_t acc = 0;
+        for (int blk = 0; blk < 4; blk++) {
+            const int8_t* wp = w + blk * 32 + l * 8;
+            const int8_t* xp = x + blk * 32 + l * 8;
+            for (int b = 0; b < 8; b++) acc += (int32_t)wp[b] * (int32_t)xp[b];
+        }
+        s[l] = acc;
+    }
+}
+
+// qlinear.rs:340-350
+float decode_row_ref(const QMat& q, int r, const QAct& a) {
+    float lanes[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int g = 0; g < q.groups; g++) {
+        int32_t s[4];
+        lane_sums(q, r, g, a, 0, s);
+        float sc = (a.sx[g] * q.cbs) * f16_to_f32(q.norms[(size_t)r * q.groups + g]);
+        for (int l = 0; l < 4; l++) lanes[l] = std::fmaf((float)s[l], sc, lanes[l]);
+    }
+    return (lanes[0] + lanes[1]) + (lanes[2] + lanes[3]);
+}
+
+// qlinear.rs:353-363
+float prefill_row_ref(const QMat& q, int r, const QAct& a, int t, bool block) {
+    float acc = 0.f;
+    for (int g = 0; g < q.groups; g++) {
+        int32_t s[4];
+        lane_sums(q, r, g, a, t, s);
+        int32_t tot = s[0] + s[1] + s[2] + s[3];
+        float sx = a.sx[(size_t)t * a.groups + g];
+        float norm = f16_to_f32(q.norms[(size_t)r * q.groups + g]);
+        float sc = block ? (norm * q.cbs) * sx : norm * (q.cbs * sx);
+        acc = std::fmaf((float)tot, sc, acc);
+    }
+    return acc;
+}
+
+// qlinear.rs:366-419, 460-487: decode kernel for one token, prefill kernel
+// (block tokens t < T/4*4, remainder tokens after) for more.
+static void qmat_matmul(const QMat& q, const QAct& a, float* y, int ldy, int col0) {
+    if (a.rows == 1) {
+        for (int r = 0; r < q.out; r++) y[col0 + r] = decode_row_ref(q, r, a);
+    } else {
+        int blocked = a.rows / 4 * 4;
+        for (int t = 0; t < a.rows; t++)
+            for (int r = 0; r < q.out; r++) y[(size_t)t * ldy + col0 + r] = prefill_row_ref(q, r, a, t, t < blocked);
+    }
+}
+
+// qlinear.rs:454-456
+float single_row(const QMat& q, int r, const QAct& a) { return prefill_row_ref(q, r, a, 0, true); }
+
+// ----------------------------------------------------------- the model
+
+struct Config {
+    int vocab, out_vocab, d, nh, nkv, L, qk, vd, max_seq, hada_n, lanes, sw;
+    uint64_t global_mask;
+    int taps, eslots, esub, ntables, etaps, edil, eseed;
+    std::vector<int> orders, sites;
+    float theta;
+    int kv_window, kv_bits;
+    int out_rows() const { return out_vocab > 0 ? out_vocab : vocab; }
+    int window(int l) const { return (sw > 0 && !((global_mask >> l) & 1)) ? sw : 0; }
+    int eheads() const { return orders.empty() ? 0 : ntables / (int)orders.size(); }
+};
+
+struct Layer {
+    std::vector<float> norm_in, q_taps, k_taps, v_taps, q_norm, k_norm, post_norm, pre_hada;
+    float attn_gate;
+    std::vector<float> d1, d2, b2, d3, d4, kron[6], cond_v, cond_u;
+    float a_pre, a_post, a_res;
+    std::vector<float> b_pre, b_post, b_res;
+    QMat qkvg, out;
+    // infer.rs:852-866: the mHC gate projection, rows requantized to int8.
+    int phi_rows, phi_width;
+    std::vector<int8_t> phi_q;
+    std::vector<float> phi_s;
+};
+
+struct Engram {
+    QMat tables, kv;
+    std::vector<float> taps;
+};
+
+struct Model {
+    Config c;
+    std::vector<uint8_t> bytes;
+    QMat embedding;
+    std::vector<Layer> layers;
+    std::vector<Engram> engrams;
+    std::vector<int> site_of_layer;
+    std::vector<int64_t> perm1, perm2;
+    std::vector<float> final_norm;
+    std::vector<float> freq, sd, cd;  // infer.rs:938-962
+};
+
+static std::vector<float> f16_tensor(const Archive& a, size_t i) {
+    const Record& r = a.recs[i];
+    if (r.dtype == F16) {
+        std::vector<float> v(r.nbytes / 2);
+        for (size_t k = 0; k < v.size(); k++) {
+            uint16_t h;
+            std::memcpy(&h, a.bytes(i) + 2 * k, 2);
+            v[k] = f16_to_f32(h);
+        }
+        return v;
+    }
+    if (r.dtype == F32) {
+        std::vector<float> v(r.nbytes / 4);
+        std::memcpy(v.data(), a.bytes(i), r.nbytes);
+        return v;
+    }
+    throw std::runtime_error("expected an f16/f32 tensor");
+}
+
+// crates/needle-core/src/cact.rs:173-202 (Header::to_config) and
+// crates/needle-engine/src/weights.rs:314-497 (record walk, fast mode),
+// infer.rs:938-962 (Tables::new).
+static void load_model(Model& m) {
+    Archive a;
+    parse_archive(m.bytes.data(), m.bytes.size(), a);
+    Config& c = m.c;
+    const uint32_t* h = a.h;
+    c.vocab = h[5]; c.out_vocab = h[6]; c.d = h[7]; c.nh = h[8]; c.nkv = h[9]; c.L = h[10];
+    c.qk = h[11]; c.vd = h[12]; c.max_seq = h[13]; c.hada_n = h[14]; c.lanes = h[15]; c.sw = h[16];
+    c.global_mask = (uint64_t)h[17] | ((uint64_t)h[18] << 32);
+    c.taps = h[19]; c.eslots = h[20]; c.esub = h[21]; c.ntables = h[22]; c.etaps = h[23]; c.edil = h[24];
+    c.eseed = h[25];
+    for (uint32_t i = 0; i < h[26]; i++) c.orders.push_back(h[27 + i]);
+    for (uint32_t i = 0; i < h[31]; i++) c.sites.push_back(h[32 + i]);
+    c.theta = bitsf(h[48]);
+    c.kv_window = h[3];
+    c.kv_bits = h[4];
+    if (c.lanes != 4 || c.hada_n != 1024 || c.taps != 3 || c.qk != 48 || c.vd != 64 || c.etaps != 4)
+        throw std::runtime_error("the native path covers the shipped geometry only");
+    size_t i = 0;
+    qmat_from_cq(a, i++, m.embedding);
+    m.layers.resize(c.L);
+    for (int l = 0; l < c.L; l++) {
+        Layer& L = m.layers[l];
+        L.norm_in = f16_tensor(a, i++);
+        QMat q, k, v, g, o;
+        qmat_from_cq(a, i++, q);
+        qmat_from_cq(a, i++, k);
+        qmat_from_cq(a, i++, v);
+        L.q_taps = f16_tensor(a, i++);
+        L.k_taps = f16_tensor(a, i++);
+        L.v_taps = f16_tensor(a, i++);
+        L.q_norm = f16_tensor(a, i++);
+        L.k_norm = f16_tensor(a, i++);
+        qmat_from_cq(a, i++, g);
+        qmat_from_cq(a, i++, o);
+        qmat_concat(L.qkvg, q);
+        qmat_concat(L.qkvg, k);
+        qmat_concat(L.qkvg, v);
+        qmat_concat(L.qkvg, g);
+        L.out = o;
+        L.post_norm = f16_tensor(a, i++);
+        L.attn_gate = f16_tensor(a, i++)[0];
+        L.pre_hada = f16_tensor(a, i++);
+        L.d1 = f16_tensor(a, i++);
+        L.d2 = f16_tensor(a, i++);
+        L.b2 = f16_tensor(a, i++);
+        L.d3 = f16_tensor(a, i++);
+        L.d4 = f16_tensor(a, i++);
+        for (int k6 = 0; k6 < 6; k6++) L.kron[k6] = f16_tensor(a, i++);
+        L.cond_v = f16_tensor(a, i++);
+        L.cond_u = f16_tensor(a, i++);
+    }
+    int n = c.lanes;
+    std::vector<float> a_pre = f16_tensor(a, i++), a_post = f16_tensor(a, i++), a_res = f16_tensor(a, i++);
+    std::vector<float> b_pre = f16_tensor(a, i++), b_post = f16_tensor(a, i++), b_res = f16_tensor(a, i++);
+    QMat phi[3];
+    for (int k = 0; k < 3; k++) qmat_from_cq(a, i++, phi[k]);
+    for (int l = 0; l < c.L; l++) {
+        Layer& L = m.layers[l];
+        L.a_pre = a_pre[l]; L.a_post = a_post[l]; L.a_res = a_res[l];
+        L.b_pre.assign(b_pre.begin() + l * n, b_pre.begin() + (l + 1) * n);
+        L.b_post.assign(b_post.begin() + l * n, b_post.begin() + (l + 1) * n);
+        L.b_res.assign(b_res.begin() + l * n * n, b_res.begin() + (l + 1) * n * n);
+        // weights.rs:380-391, 493: pre|post|res rows, dequantized; infer.rs:852-866 requant.
+        int nc = n * c.d;
+        L.phi_rows = 2 * n + n * n;
+        L.phi_width = nc;
+        L.phi_q.assign((size_t)L.phi_rows * nc, 0);
+        L.phi_s.assign(L.phi_rows, 0.f);
+        std::vector<float> row(nc);
+        int k = 0;
+        const int base[3] = {l * n, l * n, l * n * n};
+        const int cnt[3] = {n, n, n * n};
+        for (int part = 0; part < 3; part++)
+            for (int rr = 0; rr < cnt[part]; rr++, k++) {
+                qmat_row(phi[part], base[part] + rr, row.data());
+                L.phi_s[k] = quant_i8(row.data(), nc, L.phi_q.data() + (size_t)k * nc);
+            }
+    }
+    std::vector<float> p1 = f16_tensor(a, i++), p2 = f16_tensor(a, i++);
+    for (float v : p1) m.perm1.push_back((int64_t)v);
+    for (float v : p2) m.perm2.push_back((int64_t)v);
+    m.engrams.resize(c.sites.size());
+    for (size_t s = 0; s < c.sites.size(); s++) {
+        QMat kk, vv;
+        qmat_from_cq(a, i++, m.engrams[s].tables);
+        qmat_from_cq(a, i++, kk);
+        qmat_from_cq(a, i++, vv);
+        qmat_concat(m.engrams[s].kv, kk);
+        qmat_concat(m.engrams[s].kv, vv);
+        m.engrams[s].taps = f16_tensor(a, i++);
+    }
+    m.final_norm = f16_tensor(a, i++);
+    if ((int)m.perm1.size() != c.hada_n || (int)m.perm2.size() != c.hada_n)
+        throw std::runtime_error("Hadamard permutations do not match hada_n");
+    m.site_of_layer.assign(c.L, -1);
+    for (size_t s = 0; s < c.sites.size(); s++) m.site_of_layer[c.sites[s]] = (int)s;
+    float coef = -2.0f / (float)c.qk;
+    for (int k = 0; k < c.qk / 2; k++) {
+        float f = lpowf(c.theta, (float)k * coef);
+        float s, co;
+        lsincosf(f, &s, &co);
+        m.freq.push_back(f);
+        m.sd.push_back(s);
+        m.cd.push_back(co);
+    }
+}
+
+// ------------------------------------------------------------- session
+
+struct LayerState {
+    std::vector<int8_t> k8;  // [slot][kvh][qk]
+    std::vector<float> ks;   // [slot][kvh]
+    std::vector<int8_t> v8;  // [slot][kvh][vd] (the reference keeps it transposed)
+    std::vector<float> vs;   // [slot][kvh]
+    std::vector<float> hist; // pre-tap q|k|v rows, newest last
+};
+
+struct RopeRow { int64_t pos; std::vector<float> c, s; };
+
+struct Session {
+    std::vector<uint32_t> tokens;
+    std::vector<LayerState> layers;
+    std::vector<std::vector<int8_t>> ev8;
+    std::vector<std::vector<float>> evs;
+    std::vector<RopeRow> rope;
+    std::vector<float> last_hidden;
+    std::vector<int64_t> slot_pos;
+    bool has_attend = false;
+    int64_t sink = 0, ring = 0;
+};
+
+static Session* session_new(const Model& m) {
+    Session* s = new Session();
+    s->layers.resize(m.c.L);
+    s->ev8.resize(m.c.sites.size());
+    s->evs.resize(m.c.sites.size());
+    return s;
+}
+
+// infer.rs:1749-1754
+static inline int64_t slot_of(int64_t p, const Session& s) {
+    if (s.has_attend && p >= s.sink) return (p - s.sink) % s.ring + s.sink;
+    return p;
+}
+
+// infer.rs:1768-1776
+static void mark_slots(Session& s, int64_t p0, int64_t end) {
+    for (int64_t p = p0; p < end; p++) {
+        int64_t sl = slot_of(p, s);
+        if ((int64_t)s.slot_pos.size() <= sl) s.slot_pos.resize(sl + 1, -1);
+        s.slot_pos[sl] = p;
+    }
+}
+
+struct Range { int64_t a, b; };
+
+// infer.rs:1781-1825
+static std::vector<Range> key_ranges(int64_t pos, int64_t chunk_end, int window, const Session& s) {
+    int64_t lo = window > 0 ? std::max<int64_t>(0, pos + 1 - window) : 0;
+    std::vector<Range> coarse;
+    if (!s.has_attend) {
+        coarse.push_back({lo, pos + 1});
+    } else {
+        int64_t a_end = std::max(lo, std::min(s.sink, pos + 1));
+        int64_t b0 = std::min(std::max(std::max<int64_t>(0, chunk_end - s.ring), s.sink), pos + 1);
+        coarse.push_back({lo, a_end});
+        coarse.push_back({b0, pos + 1});
+    }
+    std::vector<Range> out;
+    auto push = [&](int64_t a, int64_t b) {
+        if (b <= a) return;
+        if (out.size() >= 16) throw std::runtime_error("too many key runs");
+        out.push_back({a, b});
+    };
+    for (auto r : coarse) {
+        if (!s.has_attend) { push(r.a, r.b); continue; }
+        int64_t start = -1;
+        for (int64_t p = r.a; p < r.b; p++) {
+            int64_t sl = slot_of(p, s);
+            bool ok = sl < (int64_t)s.slot_pos.size() && s.slot_pos[sl] == p;
+            if (ok && start < 0) start = p;
+            else if (!ok && start >= 0) { push(start, p); start = -1; }
+        }
+        if (start >= 0) push(start, r.b);
+    }
+    return out;
+}
+
+// infer.rs:2093-2101
+void key_chunks(int64_t n, bool nested, int nkv, int64_t* count, int64_t* chunk) {
+    int64_t k = nested ? 1 : std::max(1, 2 * NATIVE_TEAM / nkv);
+    int64_t c = (n + 255) / 256;
+    if (k * 64 <= n && c < k) c = k;
+    int64_t cm = std::max<int64_t>(c, 1);
+    int64_t ch = ((n + cm - 1) / cm + 15) / 16 * 16;
+    *chunk = ch;
+    *count = ch > 0 ? (n + ch - 1) / ch : 0;
+}
+
+// infer.rs:2222-2318 (scalar arm)
+float chunk_exp(float* s, int l, float m) {
+    int i = 0;
+    float a[4] = {0, 0, 0, 0}, b[4] = {0, 0, 0, 0};
+    while (i + 8 <= l) {
+        for (int k = 0; k < 4; k++) { float e = nexp(s[i + k] - m); s[i + k] = e; a[k] += e; }
+        for (int k = 0; k < 4; k++) { float e = nexp(s[i + 4 + k] - m); s[i + 4 + k] = e; b[k] += e; }
+        i += 8;
+    }
+    while (i + 4 <= l) {
+        for (int k = 0; k < 4; k++) { float e = nexp(s[i + k] - m); s[i + k] = e; a[k] += e; }
+        i += 4;
+    }
+    float t[4];
+    for (int k = 0; k < 4; k++) t[k] = a[k] + b[k];
+    float sum = (t[0] + t[1]) + (t[2] + t[3]);
+    if (l - i >= 2) {
+        float e0 = lexpf(s[i] - m), e1 = lexpf(s[i + 1] - m);
+        s[i] = e0;
+        s[i + 1] = e1;
+        sum = (e0 + sum) + e1;
+        i += 2;
+    }
+    if (l - i == 1) {
+        float e = lexpf(s[i] - m);
+        s[i] = e;
+        sum += e;
+    }
+    return sum;
+}
+
+// infer.rs:2171-2217 (scalar tail, which the SIMD arms match)
+static void digits21(const float* w, int n, float qw, int8_t* hi, int8_t* mid, int8_t* lo) {
+    for (int i = 0; i < n; i++) {
+        int32_t wq = (int32_t)rround(w[i] * qw);
+        hi[i] = (int8_t)(wq >> 14);
+        mid[i] = (int8_t)((wq >> 7) & 127);
+        lo[i] = (int8_t)(wq & 127);
+    }
+}
+
+struct KVView {
+    const int8_t* k8; const float* ks; const int8_t* v8; const float* vs;
+    int nkv, qk, vd;
+};
+
+// infer.rs:1871-2004 (attend_head_ref), with the merge of 2143-2166.
+void attend_head_ref(const KVView& kv, const float* qh, int kvh, const std::vector<int64_t>& slots, bool nested, float* out) {
+    const int qk = kv.qk, vd = kv.vd, nkv = kv.nkv;
+    int8_t q8[64];
+    float qs = quant_i8(qh, qk, q8) * INV_SQRT_QK;
+    int64_t n = (int64_t)slots.size();
+    int64_t count, chunk;
+    key_chunks(n, nested, nkv, &count, &chunk);
+    std::vector<float> s(chunk), scale(chunk);
+    std::vector<int32_t> dots(chunk);
+    std::vector<int8_t> hi(chunk), mid(chunk), lo(chunk);
+    struct Part { float m, sum; float o[64]; };
+    std::vector<Part> parts;
+    for (int64_t c0 = 0; c0 < n; c0 += chunk) {
+        int len = (int)std::min(chunk, n - c0);
+        const int64_t* sl = slots.data() + c0;
+        int blocked = len / 4 * 4;
+        for (int i = 0; i < len; i++) {
+            const int8_t* kr = kv.k8 + (sl[i] * nkv + kvh) * qk;
+            int32_t acc = 0;
+            for (int e = 0; e < qk; e++) acc += (int32_t)q8[e] * (int32_t)kr[e];
+            dots[i] = acc;
+            scale[i] = kv.ks[sl[i] * nkv + kvh];
+        }
+        for (int i = 0; i < blocked; i++) s[i] = (scale[i] * (float)dots[i]) * qs;
+        for (int i = blocked; i < len; i++) s[i] = (scale[i] * qs) * (float)dots[i];
+        float m = -INFINITY;
+        for (int i = 0; i < len; i++) m = rmax(m, s[i]);
+        float sum = chunk_exp(s.data(), len, m);
+        float wmax = 0.f;
+        for (int i = 0; i < len; i++) {
+            s[i] *= kv.vs[sl[i] * nkv + kvh];
+            wmax = rmax(wmax, s[i]);
+        }
+        float qw = Q21 / wmax;
+        digits21(s.data(), len, qw, hi.data(), mid.data(), lo.data());
+        float cw = wmax * C21;
+        Part p;
+        p.m = m;
+        p.sum = sum;
+        for (int dm = 0; dm < vd; dm++) {
+            int32_t sh = 0, sm = 0, sl2 = 0;
+            for (int i = 0; i < len; i++) {
+                int32_t v = kv.v8[(sl[i] * nkv + kvh) * vd + dm];
+                sh += hi[i] * v;
+                sm += mid[i] * v;
+                sl2 += lo[i] * v;
+            }
+            p.o[dm] = std::fmaf(16384.f, (float)sh, std::fmaf(128.f, (float)sm, (float)sl2)) * cw;
+        }
+        parts.push_back(p);
+    }
+    if (parts.size() == 1) {
+        float inv = 1.0f / parts[0].sum;
+        for (int dm = 0; dm < vd; dm++) out[dm] = parts[0].o[dm] * inv;
+        return;
+    }
+    float big = -1e30f;
+    for (auto& p : parts) big = rmax(big, p.m);
+    float acc[64] = {0};
+    float total = 0.f;
+    for (auto& p : parts) {
+        float w = lexpf(p.m - big);
+        for (int dm = 0; dm < vd; dm++) acc[dm] = std::fmaf(p.o[dm], w, acc[dm]);
+        total = std::fmaf(w, p.sum, total);
+    }
+    float inv = 1.0f / total;
+    for (int dm = 0; dm < vd; dm++) out[dm] = acc[dm] * inv;
+}
+
+// infer.rs:1716-1744
+static void rope_rows(const Model& m, Session& st, int64_t p0, int t, std::vector<float>& cos, std::vector<float>& sin) {
+    int half = (int)m.freq.size();
+    cos.assign((size_t)t * half, 0.f);
+    sin.assign((size_t)t * half, 0.f);
+    const RopeRow* prev = nullptr;
+    if (!st.rope.empty() && t == 1 && st.rope.back().pos + 1 == p0) prev = &st.rope.back();
+    if (prev) {
+        for (int f = 0; f < half; f++) {
+            cos[f] = std::fmaf(-m.sd[f], prev->s[f], m.cd[f] * prev->c[f]);
+            sin[f] = std::fmaf(m.sd[f], prev->c[f], m.cd[f] * prev->s[f]);
+        }
+    } else {
+        for (int i = 0; i < t; i++)
+            for (int f = 0; f < half; f++) {
+                float sv, cv;
+                lsincosf(m.freq[f] * (float)(p0 + i), &sv, &cv);
+                cos[(size_t)i * half + f] = cv;
+                sin[(size_t)i * half + f] = sv;
+            }
+    }
+    std::vector<RopeRow> kept;
+    for (auto& r : st.rope)
+        if (r.pos < p0) kept.push_back(r);
+    st.rope.swap(kept);
+    for (int i = 0; i < t; i++)
+        st.rope.push_back({p0 + i, std::vector<float>(cos.begin() + i * half, cos.begin() + (i + 1) * half),
+                           std::vector<float>(sin.begin() + i * half, sin.begin() + (i + 1) * half)});
+    size_t keep = ROLLBACK + 1;
+    if (st.rope.size() > 2 * keep) st.rope.erase(st.rope.begin(), st.rope.end() - keep);
+}
+
+// infer.rs:1640-1694 (scalar arm)
+static void cond_weights(const float* h2, int d, const float* cond_v, float w[8]) {
+    float acc[4][8] = {{0}};
+    for (int j = 0; j < d; j++)
+        for (int k = 0; k < 8; k++) acc[j % 4][k] = std::fmaf(h2[j], cond_v[j * 8 + k], acc[j % 4][k]);
+    float lg[8], e[8];
+    for (int k = 0; k < 8; k++) lg[k] = ((acc[2][k] + acc[3][k]) + acc[1][k]) + acc[0][k];
+    float m = -INFINITY;
+    for (int k = 0; k < 8; k++) m = rmax(m, lg[k]);
+    for (int k = 0; k < 8; k++) e[k] = lexpf(lg[k] - m);
+    float sum = e[7] + ((e[6] + (e[5] + e[4])) + ((e[3] + e[2]) + (e[1] + e[0])));
+    float inv = 1.0f / sum;
+    for (int k = 0; k < 8; k++) w[k] = e[k] * inv;
+}
+
+// infer.rs:2322-2330, 2343-2460 (scalar arm 2442-2459): T = (A^T Z) B.
+static void kron_native(const float* z, const float* a, const float* b, float* t) {
+    float mt[1024];
+    for (int r = 0; r < 32; r++)
+        for (int c = 0; c < 32; c++) {
+            float o = 0.f;
+            for (int j = 0; j < 32; j++) o = std::fmaf(a[j * 32 + r], z[j * 32 + c], o);
+            mt[c * 32 + r] = o;
+        }
+    for (int r = 0; r < 32; r++)
+        for (int c = 0; c < 32; c++) {
+            float o = 0.f;
+            for (int j = 0; j < 32; j++) o = std::fmaf(mt[j * 32 + r], b[j * 32 + c], o);
+            t[r * 32 + c] = o;
+        }
+}
+
+// infer.rs:1610-1634 with axpy16 (494-528), perm_fma (689-713), silu (2463-2496)
+static void mlp_native(const Model& m, const Layer& L, const float* h2, float* out) {
+    const int d = m.c.d;
+    float w[8];
+    cond_weights(h2, d, L.cond_v.data(), w);
+    float z[1024] = {0}, t[1024], cond[1024];
+    for (int j = 0; j < d; j++) z[j] = h2[j] * L.d1[j];
+    kron_native(z, L.kron[0].data(), L.kron[1].data(), t);
+    for (int j = 0; j < 1024; j++) cond[j] = 1.0f;
+    for (int k = 0; k < 8; k++)
+        for (int j = 0; j < 1024; j++) cond[j] = std::fmaf(L.cond_u[k * 1024 + j], w[k], cond[j]);
+    for (int j = 0; j < 1024; j++) z[j] = std::fmaf(t[m.perm1[j]], cond[j] * L.d2[j], L.b2[j]);
+    for (int j = 0; j < 1024; j++) z[j] /= nexp(-z[j]) + 1.0f;
+    kron_native(z, L.kron[2].data(), L.kron[3].data(), t);
+    for (int j = 0; j < 1024; j++) z[j] = t[m.perm2[j]] * L.d3[j];
+    kron_native(z, L.kron[4].data(), L.kron[5].data(), t);
+    for (int j = 0; j < d; j++) out[j] = t[j] * L.d4[j];
+}
+
+// infer.rs:2501-2525
+static void sinkhorn64(const float z[16], float out[16]) {
+    double e[16];
+    for (int r = 0; r < 4; r++) {
+        double m = (double)rmax(rmax(z[r * 4], z[r * 4 + 1]), rmax(z[r * 4 + 2], z[r * 4 + 3]));
+        for (int c = 0; c < 4; c++) e[r * 4 + c] = lexp((double)z[r * 4 + c] - m);
+    }
+    for (int it = 0; it < 20; it++) {
+        for (int r = 0; r < 4; r++) {
+            double inv = 1.0 / ((e[r * 4] + e[r * 4 + 1]) + (e[r * 4 + 2] + e[r * 4 + 3]));
+            for (int c = 0; c < 4; c++) e[r * 4 + c] *= inv;
+        }
+        for (int c = 0; c < 4; c++) {
+            double inv = 1.0 / ((e[c] + e[4 + c]) + (e[8 + c] + e[12 + c]));
+            for (int r = 0; r < 4; r++) e[r * 4 + c] *= inv;
+        }
+    }
+    for (int k = 0; k < 16; k++) out[k] = (float)e[k];
+}
+
+// infer.rs:1707-1711
+static void lane_mean(const float* x, int d, float* out) {
+    for (int ch = 0; ch < d; ch++) out[ch] = (((x[ch] + x[d + ch]) + x[2 * d + ch]) + x[3 * d + ch]) * 0.25f;
+}
+
+// Named intermediate buffers recorded during a forward, for localising a
+// GPU divergence (tests only).
+struct Trace {
+    bool on = false;
+    std::map<std::string, std::vector<float>> buf;
+    void put(const std::string& k, const float* p, size_t n) {
+        if (on) buf[k].assign(p, p + n);
+    }
+};
+static thread_local Trace g_trace;
+
+// infer.rs:1244-1328
+static void engram_native(const Model& m, Session& st, int64_t p0, int t, std::vector<std::vector<float>>& keys,
+                          std::vector<std::vector<float>>& vals) {
+    const Config& c = m.c;
+    const int d = c.d, heads = c.eheads(), sub = c.esub;
+    const int stride = c.eseed > 0 ? c.eseed : heads;
+    const uint32_t SEED = 0x9E3779B9u, PRIME = 0x01000193u;  // config.rs:11-12
+    keys.assign(c.sites.size(), {});
+    vals.assign(c.sites.size(), {});
+    for (size_t site = 0; site < c.sites.size(); site++) {
+        std::vector<float> e((size_t)t * d, 0.f);
+        for (int i = 0; i < t; i++) {
+            int64_t pos = p0 + i;
+            for (size_t oi = 0; oi < c.orders.size(); oi++) {
+                int order = c.orders[oi];
+                for (int h = 0; h < heads; h++) {
+                    if (pos + 1 < order) continue;
+                    uint32_t acc = SEED * (uint32_t)(oi * stride + h + 1);
+                    for (int j = 0; j < order; j++) {
+                        uint32_t tok = pos >= j ? st.tokens[pos - j] : 0;
+                        acc = (acc ^ tok) * PRIME;
+                    }
+                    acc ^= acc >> 15;
+                    int tbl = (int)oi * heads + h;
+                    int row = tbl * c.eslots + (int)(acc % (uint32_t)c.eslots);
+                    qmat_row(m.engrams[site].tables, row, e.data() + (size_t)i * d + tbl * sub);
+                }
+            }
+        }
+        const QMat& kvm = m.engrams[site].kv;
+        QAct act = qact_new(e.data(), t, d);
+        std::vector<float> kv((size_t)t * 2 * d);
+        qmat_matmul(kvm, act, kv.data(), 2 * d, 0);
+        auto& v8 = st.ev8[site];
+        auto& vs = st.evs[site];
+        v8.resize((size_t)(p0 + t) * d, 0);
+        vs.resize((size_t)(p0 + t) * d / 32, 0.f);
+        for (int i = 0; i < t; i++) {
+            int64_t pos = p0 + i;
+            for (int g = 0; g < d / 32; g++)
+                vs[pos * d / 32 + g] = quant_i8(kv.data() + (size_t)i * 2 * d + d + g * 32, 32, v8.data() + pos * d + g * 32);
+        }
+        const std::vector<float>& taps = m.engrams[site].taps;
+        std::vector<float> v((size_t)t * d, 0.f), k((size_t)t * d);
+        for (int i = 0; i < t; i++) std::memcpy(&k[(size_t)i * d], &kv[(size_t)i * 2 * d], sizeof(float) * d);
+        for (int i = 0; i < t; i++) {
+            int64_t pos = p0 + i;
+            float* dst = v.data() + (size_t)i * d;
+            for (int j = 0; j < c.etaps; j++) {
+                int64_t p = pos - (int64_t)j * c.edil;
+                if (p < 0) break;
+                const int8_t* q8 = v8.data() + p * d;
+                const float* qs = vs.data() + p * d / 32;
+                for (int ch = 0; ch < d; ch++) {
+                    float deq = qs[ch / 32] * (float)q8[ch];
+                    dst[ch] = std::fmaf(taps[(size_t)j * d + ch], deq, dst[ch]);
+                }
+            }
+        }
+        keys[site] = std::move(k);
+        vals[site] = std::move(v);
+        if (g_trace.on) {
+            g_trace.put("engram_e" + std::to_string(site), e.data(), e.size());
+            g_trace.put("engram_kv" + std::to_string(site), kv.data(), kv.size());
+            g_trace.put("engram_v" + std::to_string(site), vals[site].data(), vals[site].size());
+        }
+    }
+}
+
+// infer.rs:1331-1606
+static void layer_native(const Model& m, int l, Session& st, int64_t p0, std::vector<float>& xs, int t,
+                         const std::vector<float>& cos, const std::vector<float>& sin,
+                         const std::vector<std::vector<float>>& ekeys, const std::vector<std::vector<float>>& evals) {
+    const Config& c = m.c;
+    const Layer& L = m.layers[l];
+    const int n = c.lanes, d = c.d, nc = n * d, lane = l % n;
+    const int qk = c.qk, vd = c.vd, nh = c.nh, nkv = c.nkv;
+    const int qd = nh * qk, kd = nkv * qk, vdim = nkv * vd, width = qd + kd + vdim;
+    const int half = qk / 2, ncols = L.phi_rows;
+    const int pout = L.qkvg.out;
+    std::string tag = "L" + std::to_string(l) + ".";
+
+    // (a) mHC read
+    std::vector<float> u((size_t)t * d), p((size_t)t * ncols);
+    {
+        std::vector<float> nx(nc);
+        std::vector<int8_t> q8(nc);
+        for (int i = 0; i < t; i++) {
+            const float* x = xs.data() + (size_t)i * nc;
+            float r = rinv(dot16(x, x, nc), nc);
+            for (int k = 0; k < nc; k++) nx[k] = x[k] * r;
+            float sx = quant_i8(nx.data(), nc, q8.data());
+            float* pr = p.data() + (size_t)i * ncols;
+            for (int k = 0; k < ncols; k++) {
+                const int8_t* w = L.phi_q.data() + (size_t)k * nc;
+                int32_t acc = 0;
+                for (int e = 0; e < nc; e++) acc += (int32_t)w[e] * (int32_t)q8[e];
+                pr[k] = (sx * L.phi_s[k]) * (float)acc;
+            }
+            float hp[4];
+            for (int j = 0; j < 4; j++) {
+                float off = j == lane ? 4.0f : -4.0f;
+                float z = ((pr[j] * L.a_pre) + off) + L.b_pre[j];
+                hp[j] = 1.0f / (lexpf(-z) + 1.0f);
+            }
+            float* ur = u.data() + (size_t)i * d;
+            for (int k = 0; k < d; k++) ur[k] = x[k] * hp[0];
+            for (int b = 1; b < 4; b++)
+                for (int k = 0; k < d; k++) ur[k] = std::fmaf(x[b * d + k], hp[b], ur[k]);
+        }
+    }
+    g_trace.put(tag + "u", u.data(), u.size());
+    g_trace.put(tag + "p", p.data(), p.size());
+
+    // (b) engram gate, (c) input norm, (d) A8 + qkvg
+    std::vector<float> x1 = u, h((size_t)t * d);
+    int site = m.site_of_layer[l];
+    for (int i = 0; i < t; i++) {
+        float* xr = x1.data() + (size_t)i * d;
+        if (site >= 0) {
+            const float* kr = ekeys[site].data() + (size_t)i * d;
+            float rx = rinv(dot16(xr, xr, d), d), rk = rinv(dot16(kr, kr, d), d);
+            std::vector<float> a(d), b(d);
+            for (int k = 0; k < d; k++) { a[k] = xr[k] * rx; b[k] = kr[k] * rk; }
+            float alpha = 1.0f / (lexpf((-dot16(a.data(), b.data(), d)) / std::sqrt((float)d)) + 1.0f);
+            const float* vr = evals[site].data() + (size_t)i * d;
+            for (int k = 0; k < d; k++) xr[k] = std::fmaf(vr[k], alpha, xr[k]);
+        }
+        zcn(xr, L.norm_in.data(), h.data() + (size_t)i * d, d);
+    }
+    g_trace.put(tag + "x1", x1.data(), x1.size());
+    g_trace.put(tag + "h", h.data(), h.size());
+    std::vector<float> proj((size_t)t * pout);
+    {
+        QAct act = qact_new(h.data(), t, d);
+        qmat_matmul(L.qkvg, act, proj.data(), pout, 0);
+    }
+    g_trace.put(tag + "proj", proj.data(), proj.size());
+
+    // (e) conv taps, (f) head norm + RoPE, (g) int8 KV
+    LayerState& ls = st.layers[l];
+    int64_t hrows = (int64_t)ls.hist.size() / width;
+    std::vector<float> qkv((size_t)t * width);
+    for (int i = 0; i < t; i++) {
+        auto prev = [&](int j) -> const float* {
+            if (j <= i) return proj.data() + (size_t)(i - j) * pout;
+            if (hrows + i >= j) return ls.hist.data() + (size_t)(hrows + i - j) * width;
+            return nullptr;
+        };
+        float* out = qkv.data() + (size_t)i * width;
+        const struct { int start, cw; const std::vector<float>* w; } parts[3] = {
+            {0, qd, &L.q_taps}, {qd, kd, &L.k_taps}, {qd + kd, vdim, &L.v_taps}};
+        for (auto& pt : parts) {
+            float* o = out + pt.start;
+            const float* cur = prev(0) + pt.start;
+            const float* w = pt.w->data();
+            for (int k = 0; k < pt.cw; k++) o[k] = w[k] * cur[k];
+            for (int j = 1; j < c.taps; j++) {
+                const float* wj = w + (size_t)j * pt.cw;
+                const float* r = prev(j);
+                if (r) {
+                    for (int k = 0; k < pt.cw; k++) o[k] = std::fmaf(wj[k], r[pt.start + k], o[k]);
+                } else {
+                    for (int k = 0; k < pt.cw; k++) o[k] = std::fmaf(wj[k], 0.0f, o[k]);
+                }
+            }
+        }
+        const float* cs = cos.data() + (size_t)i * half;
+        const float* sn = sin.data() + (size_t)i * half;
+        for (int hh = 0; hh < nh + nkv; hh++) {
+            int off = hh < nh ? hh * qk : qd + (hh - nh) * qk;
+            const float* scale = hh < nh ? L.q_norm.data() : L.k_norm.data();
+            float* x = out + off;
+            float r = rinv(dot16(x, x, qk), qk);
+            for (int k = 0; k < qk; k++) {
+                float tt = x[k] * r;
+                x[k] = std::fmaf(tt, scale[k], tt);
+            }
+            for (int f = 0; f < half; f++) {
+                float a = x[f], b = x[f + half];
+                x[f] = std::fmaf(-sn[f], b, cs[f] * a);
+                x[f + half] = std::fmaf(sn[f], a, cs[f] * b);
+            }
+        }
+    }
+    g_trace.put(tag + "qkv", qkv.data(), qkv.size());
+    for (int i = 0; i < t; i++) ls.hist.insert(ls.hist.end(), proj.begin() + (size_t)i * pout, proj.begin() + (size_t)i * pout + width);
+    {
+        int64_t keep = c.taps - 1 + ROLLBACK;
+        int64_t rows = (int64_t)ls.hist.size() / width;
+        if (rows > 2 * keep) ls.hist.erase(ls.hist.begin(), ls.hist.begin() + (rows - keep) * width);
+    }
+    int64_t end = p0 + t;
+    {
+        int64_t need = slot_of(end - 1, st) + 1;
+        if ((int64_t)ls.ks.size() < need * nkv) {
+            ls.k8.resize(need * nkv * qk, 0);
+            ls.ks.resize(need * nkv, 0.f);
+            ls.v8.resize(need * nkv * vd, 0);
+            ls.vs.resize(need * nkv, 0.f);
+        }
+        for (int i = 0; i < t; i++) {
+            int64_t slot = slot_of(p0 + i, st);
+            const float* row = qkv.data() + (size_t)i * width;
+            for (int kvh = 0; kvh < nkv; kvh++) {
+                ls.ks[slot * nkv + kvh] = quant_i8(row + qd + kvh * qk, qk, ls.k8.data() + (slot * nkv + kvh) * qk);
+                ls.vs[slot * nkv + kvh] = quant_i8(row + qd + kd + kvh * vd, vd, ls.v8.data() + (slot * nkv + kvh) * vd);
+            }
+        }
+    }
+
+    // (h) attention, (i) the gate
+    std::vector<float> att((size_t)t * nh * vd);
+    {
+        KVView kv{ls.k8.data(), ls.ks.data(), ls.v8.data(), ls.vs.data(), nkv, qk, vd};
+        int group = nh / nkv;
+        bool nested = t > 1;
+        int window = c.window(l);
+        for (int i = 0; i < t; i++) {
+            int64_t pos = p0 + i;
+            std::vector<Range> keys = key_ranges(pos, end, window, st);
+            std::vector<int64_t> slots;
+            for (auto& r : keys)
+                for (int64_t q = r.a; q < r.b; q++) slots.push_back(slot_of(q, st));
+            for (int hh = 0; hh < nh; hh++)
+                attend_head_ref(kv, qkv.data() + (size_t)i * width + hh * qk, hh / group, slots, nested,
+                                att.data() + ((size_t)i * nh + hh) * vd);
+        }
+    }
+    g_trace.put(tag + "attn", att.data(), att.size());
+    for (int i = 0; i < t; i++)
+        for (int k = 0; k < nh * vd; k++) {
+            float g = proj[(size_t)i * pout + width + k];
+            att[(size_t)i * nh * vd + k] /= nexp(-g) + 1.0f;
+        }
+    g_trace.put(tag + "att", att.data(), att.size());
+
+    // (j) A8 + out projection
+    std::vector<float> o((size_t)t * d);
+    {
+        QAct act = qact_new(att.data(), t, nh * vd);
+        qmat_matmul(L.out, act, o.data(), d, 0);
+    }
+    g_trace.put(tag + "o", o.data(), o.size());
+
+    // (k) post block
+    float ga = 1.0f / (lexpf(-L.attn_gate) + 1.0f);
+    std::vector<float> mlpv((size_t)t * d);
+    for (int i = 0; i < t; i++) {
+        std::vector<float> on(d), x2(d), h2(d), mlp(d);
+        zcn(o.data() + (size_t)i * d, L.post_norm.data(), on.data(), d);
+        for (int k = 0; k < d; k++) x2[k] = std::fmaf(on[k], ga, x1[(size_t)i * d + k]);
+        zcn(x2.data(), L.pre_hada.data(), h2.data(), d);
+        mlp_native(m, L, h2.data(), mlp.data());
+        std::memcpy(&mlpv[(size_t)i * d], mlp.data(), sizeof(float) * d);
+        const float* pr = p.data() + (size_t)i * ncols;
+        float hpost[4];
+        for (int j = 0; j < 4; j++) {
+            float off = j == lane ? 0.0f : -4.0f;
+            float z = ((pr[n + j] * L.a_post) + off) + L.b_post[j];
+            hpost[j] = 2.0f / (lexpf(-z) + 1.0f);
+        }
+        float zres[16], hres[16];
+        for (int k = 0; k < 16; k++) zres[k] = std::fmaf(pr[2 * n + k], L.a_res, L.b_res[k]);
+        sinkhorn64(zres, hres);
+        float* x = xs.data() + (size_t)i * nc;
+        std::vector<float> old(x, x + nc);
+        const float* ur = u.data() + (size_t)i * d;
+        for (int ch = 0; ch < d; ch++) {
+            float y = (x2[ch] + mlp[ch]) - ur[ch];
+            for (int a = 0; a < n; a++) {
+                float v = y * hpost[a];
+                for (int b = 0; b < n; b++) v = std::fmaf(old[b * d + ch], hres[a * n + b], v);
+                x[a * d + ch] = v;
+            }
+        }
+    }
+    g_trace.put(tag + "mlp", mlpv.data(), mlpv.size());
+    g_trace.put(tag + "xs", xs.data(), xs.size());
+}
+
+enum Outputs { OUT_NONE = 0, OUT_LAST_LOGITS = 1, OUT_LAST_HIDDEN = 2, OUT_ALL_LOGITS = 3, OUT_HIDDEN = 4 };
+
+// infer.rs:1135-1141
+static void head_logits(const Model& m, const float* h, float* out) {
+    QAct act = qact_new(h, 1, m.c.d);
+    for (int r = 0; r < m.c.out_rows(); r++) out[r] = decode_row_ref(m.embedding, r, act);
+}
+
+// infer.rs:1145-1166
+static void head_logits_sparse(const Model& m, const float* h, const uint32_t* ids, int n, float* out) {
+    QAct act = qact_new(h, 1, m.c.d);
+    for (int r = 0; r < m.c.out_rows(); r++) out[r] = NEG;
+    for (int k = 0; k < n; k++) out[ids[k]] = single_row(m.embedding, (int)ids[k], act);
+}
+
+// infer.rs:1168-1240 (chunk_native; step_native computes the same for t = 1,
+// crates/needle-engine/src/infer/step.rs:1-11). Returns rows written to out.
+static int chunk_native(const Model& m, Session& s, const uint32_t* toks, int t, int outputs, float* out) {
+    const Config& c = m.c;
+    const int n = c.lanes, d = c.d, nc = n * d;
+    int64_t p0 = (int64_t)s.tokens.size();
+    if (p0 + t > c.max_seq) throw std::runtime_error("sequence exceeds max_seq_len");
+    s.tokens.insert(s.tokens.end(), toks, toks + t);
+    mark_slots(s, p0, p0 + t);
+    float scale = std::sqrt((float)d);
+    std::vector<float> xs((size_t)t * nc), row(d);
+    for (int i = 0; i < t; i++) {
+        qmat_row(m.embedding, (int)toks[i], row.data());
+        for (int lane = 0; lane < n; lane++)
+            for (int k = 0; k < d; k++) xs[(size_t)i * nc + lane * d + k] = row[k] * scale;
+    }
+    g_trace.put("embed", xs.data(), xs.size());
+    std::vector<std::vector<float>> ekeys, evals;
+    engram_native(m, s, p0, t, ekeys, evals);
+    std::vector<float> cos, sin;
+    rope_rows(m, s, p0, t, cos, sin);
+    g_trace.put("cos", cos.data(), cos.size());
+    g_trace.put("sin", sin.data(), sin.size());
+    for (int l = 0; l < c.L; l++) layer_native(m, l, s, p0, xs, t, cos, sin, ekeys, evals);
+    std::vector<int> rows;
+    if (outputs == OUT_LAST_LOGITS || outputs == OUT_LAST_HIDDEN) rows.push_back(t - 1);
+    else if (outputs == OUT_ALL_LOGITS || outputs == OUT_HIDDEN)
+        for (int i = 0; i < t; i++) rows.push_back(i);
+    std::vector<float> h(rows.size() * (size_t)d), mean(d);
+    for (size_t r = 0; r < rows.size(); r++) {
+        lane_mean(xs.data() + (size_t)rows[r] * nc, d, mean.data());
+        zcn(mean.data(), m.final_norm.data(), h.data() + r * d, d);
+    }
+    if (!rows.empty()) s.last_hidden.assign(h.end() - d, h.end());
+    g_trace.put("hidden", h.data(), h.size());
+    if (outputs == OUT_NONE) return 0;
+    if (outputs == OUT_LAST_HIDDEN || outputs == OUT_HIDDEN) {
+        if (out) std::memcpy(out, h.data(), sizeof(float) * h.size());
+        return (int)rows.size();
+    }
+    for (size_t r = 0; r < rows.size(); r++)
+        if (out) head_logits(m, h.data() + r * d, out + r * (size_t)c.out_rows());
+    return (int)rows.size();
+}
+
+// infer.rs:1105-1131: chunks of at most 32 from the feed start; the last
+// chunk alone gets the outputs of a Last* request.
+static int forward_native(const Model& m, Session& s, const uint32_t* ids, int n, int outputs, float* out) {
+    int rows = 0;
+    size_t per = (outputs == OUT_LAST_HIDDEN || outputs == OUT_HIDDEN) ? m.c.d : m.c.out_rows();
+    for (int c0 = 0; c0 < n; c0 += 32) {
+        int len = std::min(32, n - c0);
+        bool last = c0 + len >= n;
+        int want = outputs;
+        if ((outputs == OUT_LAST_LOGITS || outputs == OUT_LAST_HIDDEN) && !last) want = OUT_NONE;
+        rows += chunk_native(m, s, ids + c0, len, want, out ? out + rows * per : nullptr);
+    }
+    return rows;
+}
+
+// crates/needle-engine/src/agent.rs:1114-1127: banned ids read -1e30, then the
+// first index of the maximum.
+static uint32_t masked_argmax(const float* x, int n, const uint8_t* allow_bits) {
+    float m = -INFINITY;
+    for (int i = 0; i < n; i++) {
+        float v = (!allow_bits || ((allow_bits[i >> 3] >> (i & 7)) & 1)) ? x[i] : -1e30f;
+        m = rmax(m, v);
+    }
+    for (int i = 0; i < n; i++) {
+        float v = (!allow_bits || ((allow_bits[i >> 3] >> (i & 7)) & 1)) ? x[i] : -1e30f;
+        if (v == m) return (uint32_t)i;
+    }
+    return 0;
+}
+
+}  // namespace orc
+
+// ================================================================ C ABI
+
+using namespace orc;
+
+static thread_local std::string g_err;
+
+extern "C" {
+
+const char* orc_last_error() { return g_err.c_str(); }
+
+uint16_t orc_f32_to_f16(float f) { return f32_to_f16(f); }
+float orc_f16_to_f32(uint16_t h) { return f16_to_f32(h); }
+float orc_nexp(float x) { return nexp(x); }
+float orc_dot16(const float* x, const float* y, int n) { return dot16(x, y, n); }
+float orc_quant_i8(const float* x, int n, int8_t* q) { return quant_i8(x, n, q); }
+void orc_rotate(float* x, int n) { rotate(x, n); }
+int orc_nearest(float x, const float* cb, int n) { return nearest(x, cb, n); }
+int orc_codebook(int bits, int group, float* out) {
+    auto v = codebook(bits, group);
+    if (out) std::memcpy(out, v.data(), v.size() * 4);
+    return (int)v.size();
+}
+void orc_mt_permutation(uint32_t seed, int n, int64_t* out) {
+    Mt19937 mt(seed);
+    auto p = mt.permutation(n);
+    std::memcpy(out, p.data(), sizeof(int64_t) * n);
+}
+// rng.rs:77-88
+void orc_hada_perms(int n, int split, int64_t* p1, int64_t* p2) {
+    const uint32_t seeds[2] = {11, 13};
+    int64_t* outs[2] = {p1, p2};
+    for (int k = 0; k < 2; k++) {
+        std::vector<int64_t> p;
+        if (split) {
+            int h = n / 2;
+            p = Mt19937(seeds[k]).permutation(h);
+            auto q = Mt19937(seeds[k] + 977).permutation(h);
+            for (auto v : q) p.push_back(h + v);
+        } else {
+            p = Mt19937(seeds[k]).permutation(n);
+        }
+        std::memcpy(outs[k], p.data(), sizeof(int64_t) * n);
+    }
+}
+void orc_cq_pack(const float* w, int rows, int d, uint8_t* packed, uint16_t* norms) { cq_pack(w, rows, d, packed, norms); }
+float orc_prep_group(const float* x, int n, int g, int8_t* q) { return prep_group(x, n, g, q); }
+float orc_chunk_exp(float* s, int l, float m) { return chunk_exp(s, l, m); }
+void orc_key_chunks(int64_t n, int nested, int nkv, int64_t* count, int64_t* chunk) { key_chunks(n, nested != 0, nkv, count, chunk); }
+
+// A raw CQ-4 matrix (codes as stored, f16 norm bits) times activations x
+// [T, in_dim]: the decode kernel when T == 1, else the prefill kernel with
+// the block/remainder rule (qlinear.rs:366-419). mode 2 = the single-row
+// kernel per token (qlinear.rs:454-456).
+int orc_cq_matmul(const uint8_t* codes, const uint16_t* norms, int out, int in_dim, const float* x, int T, int mode, float* y) {
+    try {
+        QMat q;
+        q.out = out;
+        q.in_dim = in_dim;
+        q.groups = (in_dim + GROUP - 1) / GROUP;
+        size_t ncode = (size_t)out * q.groups * 64;
+        q.codes.assign(codes, codes + ncode);
+        q.norms.assign(norms, norms + (size_t)out * q.groups);
+        std::vector<float> cb = codebook(4, GROUP);
+        int8_t cb8[16];
+        int8_codebook(cb, cb8, &q.cbs);
+        for (int c = 0; c < 16; c++) { q.vals[c] = cb8[c]; q.fvals[c] = cb[c]; }
+        q.w8.resize(ncode * 2);
+        for (size_t k = 0; k < ncode; k++) {
+            q.w8[2 * k] = q.vals[q.codes[k] & 15];
+            q.w8[2 * k + 1] = q.vals[q.codes[k] >> 4];
+        }
+        if (mode == 2) {
+            for (int t = 0; t < T; t++) {
+                QAct a = qact_new(x + (size_t)t * in_dim, 1, in_dim);
+                for (int r = 0; r < out; r++) y[(size_t)t * out + r] = single_row(q, r, a);
+            }
+            return 0;
+        }
+        QAct a = qact_new(x, T, in_dim);
+        qmat_matmul(q, a, y, out, 0);
+        return 0;
+    } catch (std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+
+// QMat::row of a raw CQ-4 matrix (qlinear.rs:309-323).
+void orc_cq_row(const uint8_t* codes, const uint16_t* norms, int rows, int in_dim, int r, float* out) {
+    QMat q;
+    q.out = rows;
+    q.in_dim = in_dim;
+    q.groups = (in_dim + GROUP - 1) / GROUP;
+    q.codes.assign(codes + (size_t)r * q.groups * 64, codes + (size_t)(r + 1) * q.groups * 64);
+    q.norms.assign(norms + (size_t)r * q.groups, norms + (size_t)(r + 1) * q.groups);
+    std::vector<float> cb = codebook(4, GROUP);
+    for (int c = 0; c < 16; c++) q.fvals[c] = cb[c];
+    qmat_row(q, 0, out);
+}
+
+// attend_head_ref over caller-provided caches ([slot][kvh][qk] keys,
+// [slot][kvh][vd] values) and a slot list.
+void orc_attend_head(const int8_t* k8, const float* ks, const int8_t* v8, const float* vs, int nkv, int qk, int vd,
+                     const float* qh, int kvh, const int64_t* slots, int n, int nested, float* out) {
+    KVView kv{k8, ks, v8, vs, nkv, qk, vd};
+    std::vector<int64_t> sl(slots, slots + n);
+    attend_head_ref(kv, qh, kvh, sl, nested != 0, out);
+}
+
+// ---- model level
+
+void* orc_model_load(const uint8_t* bytes, uint64_t n) {
+    try {
+        Model* m = new Model();
+        m->bytes.assign(bytes, bytes + n);
+        load_model(*m);
+        m->bytes.clear();
+        m->bytes.shrink_to_fit();
+        return m;
+    } catch (std::exception& e) {
+        g_err = e.what();
+        return nullptr;
+    }
+}
+void orc_model_free(void* m) { delete (Model*)m; }
+int orc_model_dims(void* mp, int* out) {
+    Model* m = (Model*)mp;
+    out[0] = m->c.vocab; out[1] = m->c.out_rows(); out[2] = m->c.d; out[3] = m->c.L;
+    out[4] = m->c.nh; out[5] = m->c.nkv; out[6] = m->c.qk; out[7] = m->c.vd; out[8] = m->c.max_seq;
+    return 0;
+}
+void* orc_session_new(void* m) { return session_new(*(Model*)m); }
+void orc_session_free(void* s) { delete (Session*)s; }
+void* orc_session_clone(void* s) { return new Session(*(Session*)s); }
+int orc_session_len(void* s) { return (int)((Session*)s)->tokens.size(); }
+void orc_session_set_attend(void* s, int64_t sink, int64_t ring) {
+    Session* ss = (Session*)s;
+    ss->has_attend = ring > 0;
+    ss->sink = sink;
+    ss->ring = ring;
+}
+
+int orc_forward(void* m, void* s, const uint32_t* ids, int n, int outputs, float* out) {
+    try {
+        return forward_native(*(Model*)m, *(Session*)s, ids, n, outputs, out);
+    } catch (std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+
+void orc_head_logits(void* m, const float* h, float* out) { head_logits(*(Model*)m, h, out); }
+void orc_head_logits_sparse(void* m, const float* h, const uint32_t* ids, int n, float* out) {
+    head_logits_sparse(*(Model*)m, h, ids, n, out);
+}
+int orc_last_hidden(void* s, float* out) {
+    Session* ss = (Session*)s;
+    if (out) std::memcpy(out, ss->last_hidden.data(), ss->last_hidden.size() * 4);
+    return (int)ss->last_hidden.size();
+}
+uint32_t orc_masked_argmax(const float* x, int n, const uint8_t* allow_bits) { return masked_argmax(x, n, allow_bits); }
+
+void orc_trace(int on) {
+    g_trace.on = on != 0;
+    if (!on) g_trace.buf.clear();
+}
+int orc_trace_get(const char* name, float* out, int cap) {
+    auto it = g_trace.buf.find(name);
+    if (it == g_trace.buf.end()) return -1;
+    int n = (int)it->second.size();
+    if (out) std::memcpy(out, it->second.data(), sizeof(float) * std::min(n, cap));
+    return n;
+}
+
+// Greedy decode as `needle bench --decode <steps>` drives the engine
+// (crates/needle-cli/src/main.rs:566-587): prefill in chunks of 32 with
+// LastLogits, then per step `next = argmax(logits)` and one decode forward of
+// `next`. masks (optional, `steps` rows of ceil(vocab/8) bytes, bit set =
+// allowed) apply the agent's ban (-1e30) before each argmax.
+int orc_generate(void* mp, const uint32_t* prompt, int n, int steps, const uint8_t* masks, uint32_t* out_ids,
+                 float* first_logits) {
+    try {
+        Model& m = *(Model*)mp;
+        Session* s = session_new(m);
+        std::vector<float> logits(m.c.out_rows());
+        forward_native(m, *s, prompt, n, OUT_LAST_LOGITS, logits.data());
+        if (first_logits) std::memcpy(first_logits, logits.data(), logits.size() * 4);
+        size_t mb = (m.c.out_rows() + 7) / 8;
+        for (int k = 0; k < steps; k++) {
+            uint32_t next = masked_argmax(logits.data(), m.c.out_rows(), masks ? masks + k * mb : nullptr);
+            out_ids[k] = next;
+            forward_native(m, *s, &next, 1, OUT_LAST_LOGITS, logits.data());
+        }
+        delete s;
+        return 0;
+    } catch (std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+
+// Many independent sequences on `threads` host threads (one sequence per
+// thread at a time, dynamically assigned): the CPU baseline for the batched
+// configs. prompts [S][n], masks [S][steps][mb] or null, out_ids [S][steps].
+int orc_generate_batch(void* mp, int S, const uint32_t* prompts, int n, int steps, const uint8_t* masks, uint32_t* out_ids,
+                       int threads) {
+    Model& m = *(Model*)mp;
+    size_t mb = (m.c.out_rows() + 7) / 8;
+    std::atomic<int> next(0), bad(0);
+    auto work = [&]() {
+        for (;;) {
+            int s = next.fetch_add(1);
+            if (s >= S) return;
+            if (orc_generate(mp, prompts + (size_t)s * n, n, steps, masks ? masks + (size_t)s * steps * mb : nullptr,
+                             out_ids + (size_t)s * steps, nullptr) != 0)
+                bad++;
+        }
+    };
+    std::vector<std::thread> th;
+    for (int k = 0; k < std::max(1, threads); k++) th.emplace_back(work);
+    for (auto& t : th) t.join();
+    return bad.load() ? -1 : 0;
+}
+
+// S sessions stepped together on host threads, for the timed CPU baseline of
+// the batched decode config: prefill once, then each call is one greedy
+// decode step of every session (masked argmax of its last logits, fed back).
+struct OrcBatch {
+    Model* m;
+    std::vector<Session*> ss;
+    std::vector<std::vector<float>> logits;
+};
+
+static void run_parallel(int S, int threads, const std::function<void(int)>& f) {
+    std::atomic<int> next(0);
+    auto work = [&]() {
+        for (;;) {
+            int s = next.fetch_add(1);
+            if (s >= S) return;
+            f(s);
+        }
+    };
+    std::vector<std::thread> th;
+    for (int k = 0; k < std::max(1, threads); k++) th.emplace_back(work);
+    for (auto& t : th) t.join();
+}
+
+void* orc_batch_new(void* mp, int S) {
+    OrcBatch* b = new OrcBatch();
+    b->m = (Model*)mp;
+    for (int s = 0; s < S; s++) b->ss.push_back(session_new(*b->m));
+    b->logits.assign(S, std::vector<float>(b->m->c.out_rows()));
+    return b;
+}
+
+void orc_batch_free(void* bp) {
+    OrcBatch* b = (OrcBatch*)bp;
+    for (auto s : b->ss) delete s;
+    delete b;
+}
+
+int orc_batch_prefill(void* bp, const uint32_t* prompts, int n, int threads) {
+    OrcBatch* b = (OrcBatch*)bp;
+    std::atomic<int> bad(0);
+    run_parallel((int)b->ss.size(), threads, [&](int s) {
+        try {
+            forward_native(*b->m, *b->ss[s], prompts + (size_t)s * n, n, OUT_LAST_LOGITS, b->logits[s].data());
+        } catch (...) {
+            bad++;
+        }
+    });
+    return bad.load() ? -1 : 0;
+}
+
+int orc_batch_step(void* bp, const uint8_t* masks, uint32_t* next_ids, int threads) {
+    OrcBatch* b = (OrcBatch*)bp;
+    const int V = b->m->c.out_rows();
+    const size_t mb = (V + 7) / 8;
+    std::atomic<int> bad(0);
+    run_parallel((int)b->ss.size(), threads, [&](int s) {
+        try {
+            uint32_t nx = masked_argmax(b->logits[s].data(), V, masks ? masks + s * mb : nullptr);
+            if (next_ids) next_ids[s] = nx;
+            forward_native(*b->m, *b->ss[s], &nx, 1, OUT_LAST_LOGITS, b->logits[s].data());
+        } catch (...) {
+            bad++;
+        }
+    });
+    return bad.load() ? -1 : 0;
+}
+
+// Prefill-only throughput sample: S sequences of n tokens each, last-position
+// logits per sequence into out [S][out_rows].
+int orc_prefill_batch(void* mp, int S, const uint32_t* prompts, int n, float* out, int threads) {
+    Model& m = *(Model*)mp;
+    std::atomic<int> next(0), bad(0);
+    auto work = [&]() {
+        for (;;) {
+            int s = next.fetch_add(1);
+            if (s >= S) return;
+            Session* ss = session_new(m);
+            try {
+                forward_native(m, *ss, prompts + (size_t)s * n, n, OUT_LAST_LOGITS, out ? out + (size_t)s * m.c.out_rows() : nullptr);
+            } catch (...) {
+                bad++;
+            }
+            delete ss;
+        }
+    };
+    std::vector<std::thread> th;
+    for (int k = 0; k < std::max(1, threads); k++) th.emplace_back(work);
+    for (auto& t : th) t.join();
+    return bad.load() ? -1 : 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,353 @@
+"""ctypes view of the CPU oracle (test infrastructure only).
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg use
+this module, as the checker and the timed CPU baseline. The product path never
+imports it.
+"""
+
+import ctypes as C
+import os
+
+import numpy as np
+
+from . import build as _build
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        path = _build.build()
+        L = C.CDLL(path)
+        P, I, U32, I64, F = C.c_void_p, C.c_int, C.c_uint32, C.c_int64, C.c_float
+        sig = {
+            "orc_last_error": (C.c_char_p, []),
+            "orc_f32_to_f16": (C.c_uint16, [F]),
+            "orc_f16_to_f32": (F, [C.c_uint16]),
+            "orc_nexp": (F, [F]),
+            "orc_dot16": (F, [P, P, I]),
+            "orc_quant_i8": (F, [P, I, P]),
+            "orc_rotate": (None, [P, I]),
+            "orc_nearest": (I, [F, P, I]),
+            "orc_codebook": (I, [I, I, P]),
+            "orc_mt_permutation": (None, [U32, I, P]),
+            "orc_hada_perms": (None, [I, I, P, P]),
+            "orc_cq_pack": (None, [P, I, I, P, P]),
+            "orc_prep_group": (F, [P, I, I, P]),
+            "orc_chunk_exp": (F, [P, I, F]),
+            "orc_key_chunks": (None, [I64, I, I, P, P]),
+            "orc_cq_matmul": (I, [P, P, I, I, P, I, I, P]),
+            "orc_cq_row": (None, [P, P, I, I, I, P]),
+            "orc_attend_head": (None, [P, P, P, P, I, I, I, P, I, P, I, I, P]),
+            "orc_model_load": (P, [P, C.c_uint64]),
+            "orc_model_free": (None, [P]),
+            "orc_model_dims": (I, [P, P]),
+            "orc_session_new": (P, [P]),
+            "orc_session_free": (None, [P]),
+            "orc_session_clone": (P, [P]),
+            "orc_session_len": (I, [P]),
+            "orc_session_set_attend": (None, [P, I64, I64]),
+            "orc_forward": (I, [P, P, P, I, I, P]),
+            "orc_head_logits": (None, [P, P, P]),
+            "orc_head_logits_sparse": (None, [P, P, P, I, P]),
+            "orc_last_hidden": (I, [P, P]),
+            "orc_masked_argmax": (U32, [P, I, P]),
+            "orc_trace": (None, [I]),
+            "orc_trace_get": (I, [C.c_char_p, P, I]),
+            "orc_generate": (I, [P, P, I, I, P, P, P]),
+            "orc_generate_batch": (I, [P, I, P, I, I, P, P, I]),
+            "orc_prefill_batch": (I, [P, I, P, I, P, I]),
+            "orc_batch_new": (P, [P, I]),
+            "orc_batch_free": (None, [P]),
+            "orc_batch_prefill": (I, [P, P, I, I]),
+            "orc_batch_step": (I, [P, P, P, I]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _p(a):
+    return a.ctypes.data_as(C.c_void_p) if a is not None else None
+
+
+def f32_to_f16_bits(x: float) -> int:
+    return lib().orc_f32_to_f16(float(x))
+
+
+def nexp(x: float) -> float:
+    return lib().orc_nexp(float(x))
+
+
+def dot16(x, y) -> float:
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.ascontiguousarray(y, np.float32)
+    return lib().orc_dot16(_p(x), _p(y), len(x))
+
+
+def quant_i8(x):
+    x = np.ascontiguousarray(x, np.float32)
+    q = np.zeros(len(x), np.int8)
+    s = lib().orc_quant_i8(_p(x), len(x), _p(q))
+    return q, s
+
+
+def rotate(x):
+    y = np.array(x, np.float32, copy=True)
+    lib().orc_rotate(_p(y), len(y))
+    return y
+
+
+def nearest(x: float, cb) -> int:
+    cb = np.ascontiguousarray(cb, np.float32)
+    return lib().orc_nearest(float(x), _p(cb), len(cb))
+
+
+def codebook(bits: int, group: int = 128):
+    n = lib().orc_codebook(bits, group, None)
+    out = np.zeros(n, np.float32)
+    lib().orc_codebook(bits, group, _p(out))
+    return out
+
+
+def mt_permutation(seed: int, n: int):
+    out = np.zeros(n, np.int64)
+    lib().orc_mt_permutation(seed, n, _p(out))
+    return out
+
+
+def hada_perms(n: int, split: bool = False):
+    a = np.zeros(n, np.int64)
+    b = np.zeros(n, np.int64)
+    lib().orc_hada_perms(n, int(split), _p(a), _p(b))
+    return a, b
+
+
+def cq_pack(w):
+    w = np.ascontiguousarray(w, np.float32)
+    rows, d = w.shape
+    g = (d + 127) // 128
+    packed = np.zeros((rows, g * 64), np.uint8)
+    norms = np.zeros((rows, g), np.uint16)
+    lib().orc_cq_pack(_p(w), rows, d, _p(packed), _p(norms))
+    return packed, norms
+
+
+def prep_group(x, g):
+    x = np.ascontiguousarray(x, np.float32)
+    q = np.zeros(128, np.int8)
+    s = lib().orc_prep_group(_p(x), len(x), g, _p(q))
+    return q, s
+
+
+def chunk_exp(s, m):
+    s = np.array(s, np.float32, copy=True)
+    tot = lib().orc_chunk_exp(_p(s), len(s), float(m))
+    return s, tot
+
+
+def key_chunks(n, nested, nkv):
+    c = np.zeros(1, np.int64)
+    k = np.zeros(1, np.int64)
+    lib().orc_key_chunks(int(n), int(nested), int(nkv), _p(c), _p(k))
+    return int(c[0]), int(k[0])
+
+
+def cq_matmul(codes, norms, in_dim, x, mode=0):
+    """y = x @ W^T with the reference's kernels: decode (T == 1), prefill
+    (block/remainder rule) otherwise; mode 2 = single-row kernel per token."""
+    codes = np.ascontiguousarray(codes, np.uint8)
+    norms = np.ascontiguousarray(norms, np.uint16)
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, in_dim)
+    out = norms.shape[0]
+    y = np.zeros((x.shape[0], out), np.float32)
+    rc = lib().orc_cq_matmul(_p(codes), _p(norms), out, in_dim, _p(x), x.shape[0], mode, _p(y))
+    if rc != 0:
+        raise RuntimeError(lib().orc_last_error().decode())
+    return y
+
+
+def cq_row(codes, norms, in_dim, r):
+    codes = np.ascontiguousarray(codes, np.uint8)
+    norms = np.ascontiguousarray(norms, np.uint16)
+    out = np.zeros(in_dim, np.float32)
+    lib().orc_cq_row(_p(codes), _p(norms), norms.shape[0], in_dim, r, _p(out))
+    return out
+
+
+def attend_head(k8, ks, v8, vs, q, kvh, slots, nested):
+    """attend_head_ref over caches k8 [slot][nkv][qk], v8 [slot][nkv][vd]."""
+    nkv, qk = k8.shape[1], k8.shape[2]
+    vd = v8.shape[2]
+    slots = np.ascontiguousarray(slots, np.int64)
+    out = np.zeros(vd, np.float32)
+    q = np.ascontiguousarray(q, np.float32)
+    lib().orc_attend_head(_p(np.ascontiguousarray(k8)), _p(np.ascontiguousarray(ks, np.float32)),
+                          _p(np.ascontiguousarray(v8)), _p(np.ascontiguousarray(vs, np.float32)),
+                          nkv, qk, vd, _p(q), kvh, _p(slots), len(slots), int(nested), _p(out))
+    return out
+
+
+def masked_argmax(x, allow_bits=None):
+    x = np.ascontiguousarray(x, np.float32)
+    return lib().orc_masked_argmax(_p(x), len(x), _p(allow_bits) if allow_bits is not None else None)
+
+
+OUT_NONE, OUT_LAST_LOGITS, OUT_LAST_HIDDEN, OUT_ALL_LOGITS, OUT_HIDDEN = 0, 1, 2, 3, 4
+
+
+class Model:
+    """The packed model as the reference's native path runs it."""
+
+    def __init__(self, archive: bytes):
+        buf = np.frombuffer(archive, np.uint8)
+        self._h = lib().orc_model_load(_p(buf), len(buf))
+        if not self._h:
+            raise RuntimeError(lib().orc_last_error().decode())
+        dims = np.zeros(9, np.int32)
+        lib().orc_model_dims(self._h, _p(dims))
+        (self.vocab, self.out_rows, self.d_model, self.num_layers, self.num_heads, self.num_kv_heads,
+         self.qk_head_dim, self.v_head_dim, self.max_seq_len) = (int(v) for v in dims)
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().orc_model_free(self._h)
+            self._h = None
+
+    def session(self):
+        return Session(self)
+
+    def head_logits(self, h):
+        h = np.ascontiguousarray(h, np.float32)
+        out = np.zeros(self.out_rows, np.float32)
+        lib().orc_head_logits(self._h, _p(h), _p(out))
+        return out
+
+    def head_logits_sparse(self, h, ids):
+        h = np.ascontiguousarray(h, np.float32)
+        ids = np.ascontiguousarray(ids, np.uint32)
+        out = np.zeros(self.out_rows, np.float32)
+        lib().orc_head_logits_sparse(self._h, _p(h), _p(ids), len(ids), _p(out))
+        return out
+
+    def generate(self, prompt, steps, masks=None, want_logits=False):
+        prompt = np.ascontiguousarray(prompt, np.uint32)
+        out = np.zeros(steps, np.uint32)
+        first = np.zeros(self.out_rows, np.float32) if want_logits else None
+        rc = lib().orc_generate(self._h, _p(prompt), len(prompt), steps,
+                                _p(np.ascontiguousarray(masks, np.uint8)) if masks is not None else None,
+                                _p(out), _p(first) if first is not None else None)
+        if rc != 0:
+            raise RuntimeError(lib().orc_last_error().decode())
+        return (out, first) if want_logits else out
+
+    def generate_batch(self, prompts, steps, masks=None, threads=None):
+        prompts = np.ascontiguousarray(prompts, np.uint32)
+        S, n = prompts.shape
+        out = np.zeros((S, steps), np.uint32)
+        threads = threads or os.cpu_count() or 1
+        rc = lib().orc_generate_batch(self._h, S, _p(prompts), n, steps,
+                                      _p(np.ascontiguousarray(masks, np.uint8)) if masks is not None else None,
+                                      _p(out), threads)
+        if rc != 0:
+            raise RuntimeError("oracle batch generation failed")
+        return out
+
+    def prefill_batch(self, prompts, threads=None, want_logits=True):
+        prompts = np.ascontiguousarray(prompts, np.uint32)
+        S, n = prompts.shape
+        out = np.zeros((S, self.out_rows), np.float32) if want_logits else None
+        threads = threads or os.cpu_count() or 1
+        rc = lib().orc_prefill_batch(self._h, S, _p(prompts), n, _p(out) if out is not None else None, threads)
+        if rc != 0:
+            raise RuntimeError("oracle batch prefill failed")
+        return out
+
+
+class Batch:
+    """S oracle sessions stepped together on host threads (the CPU baseline
+    of the batched decode config)."""
+
+    def __init__(self, model: Model, num_seqs: int, threads=None):
+        self.model = model
+        self.num_seqs = num_seqs
+        self.threads = threads or os.cpu_count() or 1
+        self._h = lib().orc_batch_new(model._h, num_seqs)
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().orc_batch_free(self._h)
+            self._h = None
+
+    def prefill(self, prompts):
+        prompts = np.ascontiguousarray(prompts, np.uint32)
+        if lib().orc_batch_prefill(self._h, _p(prompts), prompts.shape[1], self.threads) != 0:
+            raise RuntimeError("oracle batch prefill failed")
+
+    def step(self, masks=None):
+        out = np.zeros(self.num_seqs, np.uint32)
+        m = _p(np.ascontiguousarray(masks, np.uint8)) if masks is not None else None
+        if lib().orc_batch_step(self._h, m, _p(out), self.threads) != 0:
+            raise RuntimeError("oracle batch step failed")
+        return out
+
+
+class Session:
+    def __init__(self, model: Model, handle=None):
+        self.model = model
+        self._h = handle or lib().orc_session_new(model._h)
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().orc_session_free(self._h)
+            self._h = None
+
+    def clone(self):
+        return Session(self.model, lib().orc_session_clone(self._h))
+
+    def __len__(self):
+        return lib().orc_session_len(self._h)
+
+    def set_attend(self, sink, ring):
+        lib().orc_session_set_attend(self._h, sink, ring)
+
+    def forward(self, ids, outputs=OUT_LAST_LOGITS):
+        ids = np.ascontiguousarray(ids, np.uint32)
+        n = len(ids)
+        m = self.model
+        rows = {OUT_NONE: 0, OUT_LAST_LOGITS: 1, OUT_LAST_HIDDEN: 1, OUT_ALL_LOGITS: n, OUT_HIDDEN: n}[outputs]
+        width = m.d_model if outputs in (OUT_LAST_HIDDEN, OUT_HIDDEN) else m.out_rows
+        out = np.zeros((rows, width), np.float32)
+        rc = lib().orc_forward(m._h, self._h, _p(ids), n, outputs, _p(out))
+        if rc < 0:
+            raise RuntimeError(lib().orc_last_error().decode())
+        return out
+
+    def last_hidden(self):
+        out = np.zeros(self.model.d_model, np.float32)
+        lib().orc_last_hidden(self._h, _p(out))
+        return out
+
+
+class trace:
+    """Record the oracle's named intermediates (per layer ``L{l}.{name}``)."""
+
+    def __enter__(self):
+        lib().orc_trace(1)
+        return self
+
+    def __exit__(self, *a):
+        lib().orc_trace(0)
+
+    @staticmethod
+    def get(name):
+        n = lib().orc_trace_get(name.encode(), None, 0)
+        if n < 0:
+            raise KeyError(name)
+        out = np.zeros(n, np.float32)
+        lib().orc_trace_get(name.encode(), _p(out), n)
+        return out

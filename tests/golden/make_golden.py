@@ -1,0 +1,75 @@
+"""Writes the committed fixtures under tests/golden/.
+
+reference_kat.json: known answers transcribed from the reference's own unit
+tests (file:line in needle-rs given per entry).
+
+small_model_streams.json: the oracle's greedy token streams and a digest of
+its first logits on the small synthetic archive the tests build
+(tests/conftest.py SMALL), so a later change to the oracle, the archive
+writer or the engine shows up against a fixed record.
+
+Run: python tests/golden/make_golden.py
+"""
+
+import hashlib
+import json
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "needle-rs_b200"))
+sys.path.insert(0, os.path.dirname(HERE))
+
+import numpy as np  # noqa: E402
+
+REFERENCE_KAT = {
+    "mt19937_permutation": {
+        "source": "crates/needle-core/src/rng.rs:94-98",
+        "seed": 11, "n": 16, "expect": [8, 3, 6, 10, 15, 4, 5, 14, 2, 13, 12, 7, 1, 11, 0, 9],
+    },
+    "hada_blocks": {"source": "crates/needle-core/src/config.rs:495-499", "n": 1024, "expect": [32, 32]},
+    "nearest_ties_low": {
+        "source": "crates/needle-core/src/quant.rs:314-321",
+        "codebook": [-1.0, 0.0, 1.0],
+        "cases": [[0.5, 1], [-0.5, 0], [5.0, 2], [-5.0, 0]],
+    },
+    "nexp_tolerance": {"source": "crates/needle-engine/src/infer.rs:3078-3084", "rel": 2e-7, "x": "i * 0.37, i in -200..200"},
+    "kernels_match_reference": {
+        "source": "crates/needle-engine/src/qlinear.rs:976-1006",
+        "out": 37, "in": 384, "tolerance": "0.02 * (1 + |want|)", "prefill_rows": [2, 3, 5, 9, 13, 17],
+    },
+    "kv_window_default": {"source": "crates/needle-core/src/config.rs:448-482", "expect": 3456},
+}
+
+
+def streams():
+    from conftest import SMALL, _cached_archive
+    from oracle import oracle as orc
+
+    data = _cached_archive("small", **SMALL)
+    m = orc.Model(data)
+    out = {"archive_sha256": hashlib.sha256(data).hexdigest(), "shape": {k: list(v) if isinstance(v, tuple) else v
+                                                                        for k, v in SMALL.items()}, "cases": []}
+    rng = np.random.default_rng(2024)
+    for n in (5, 33, 70):
+        prompt = rng.integers(0, m.vocab, n).astype(np.uint32)
+        toks, logits = m.generate(prompt, 12, want_logits=True)
+        out["cases"].append({
+            "prompt": [int(v) for v in prompt],
+            "tokens": [int(v) for v in toks],
+            "first_logits_sha256": hashlib.sha256(logits.view(np.uint32).tobytes()).hexdigest(),
+        })
+    return out
+
+
+def main():
+    with open(os.path.join(HERE, "reference_kat.json"), "w") as f:
+        json.dump(REFERENCE_KAT, f, indent=1)
+    with open(os.path.join(HERE, "small_model_streams.json"), "w") as f:
+        json.dump(streams(), f, indent=1)
+
+
+if __name__ == "__main__":
+    main()

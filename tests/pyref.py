@@ -1,0 +1,225 @@
+"""A second, pure-Python restatement of a few reference functions, used only
+on small inputs to pin the C++ oracle: every f32 op is one numpy float32 op,
+and fused multiply-adds are rounded once from the exact rational value.
+
+Citations are needle-rs paths (crates/needle-engine/src/...).
+"""
+
+from fractions import Fraction
+
+import numpy as np
+
+f32 = np.float32
+
+
+def round_f32(x: Fraction) -> np.float32:
+    """The float32 nearest to the exact rational x, ties to even."""
+    if x == 0:
+        return f32(0.0)
+    d = f32(float(x))  # within one float32 ulp of the answer
+    best = None
+    for c in (np.nextafter(d, f32(-np.inf)), d, np.nextafter(d, f32(np.inf))):
+        if not np.isfinite(c):
+            continue
+        err = abs(Fraction(float(c)) - x)
+        if best is None or err < best[0] or (err == best[0] and (int(c.view(np.uint32)) & 1) == 0):
+            best = (err, c)
+    return f32(best[1])
+
+
+def fma32(a, b, c) -> np.float32:
+    return round_f32(Fraction(float(a)) * Fraction(float(b)) + Fraction(float(c)))
+
+
+def dot16(x, y):
+    """infer.rs:405-416 (scalar arm)."""
+    a = [[f32(0)] * 4 for _ in range(4)]
+    for c in range(len(x) // 16):
+        for j in range(4):
+            for l in range(4):
+                i = c * 16 + j * 4 + l
+                a[j][l] = fma32(x[i], y[i], a[j][l])
+    t = [((a[2][l] + a[3][l]) + a[1][l]) + a[0][l] for l in range(4)]
+    return (t[0] + t[1]) + (t[2] + t[3])
+
+
+def bits(u):
+    return np.array([u], np.uint32).view(np.float32)[0]
+
+
+def nexp(x):
+    """infer.rs:353-366."""
+    x = f32(min(max(f32(x), bits(0xC2B0C0A5)), bits(0x42B0C0A5)))
+    k = f32(np.rint(x * bits(0x3FB8AA3B)))
+    r = fma32(k, bits(0xBF318000), x)
+    r = fma32(k, bits(0x395E8083), r)
+    p = fma32(bits(0x39506967), r, bits(0x3AB743CE))
+    p = fma32(r, p, bits(0x3C088908))
+    p = fma32(r, p, bits(0x3D2AA9C1))
+    p = fma32(r, p, bits(0x3E2AAAAA))
+    p = fma32(r, p, f32(0.5))
+    y = fma32(r * r, p, r)
+    s = np.array([((int(k) << 23) + 0x3F800000) & 0xFFFFFFFF], np.uint32).view(np.float32)[0]
+    return fma32(s, y, s)
+
+
+K127 = bits(0x3C010204)
+
+
+def quant_i8(x):
+    """qlinear.rs:77-88, 137-139."""
+    x = np.asarray(x, np.float32)
+    m = f32(0)
+    for v in x:
+        m = max(m, abs(v))
+    s = m * K127 if m > 0 else f32(1.0)
+    inv = f32(1.0) / s
+    q = []
+    for v in x:
+        t = float(v * inv)
+        r = np.floor(abs(t) + 0.5) * np.sign(t)  # half away from zero
+        q.append(int(min(max(r, -128), 127)))
+    return np.array(q, np.int8), f32(s)
+
+
+def fwht(x):
+    x = list(np.asarray(x, np.float32))
+    n = len(x)
+    h = 1
+    while h < n:
+        for i in range(0, n, 2 * h):
+            for j in range(i, i + h):
+                a, b = x[j], x[j + h]
+                x[j], x[j + h] = a + b, a - b
+        h *= 2
+    return x
+
+
+def rotate(x):
+    s = f32(1.0 / np.sqrt(len(x)))
+    return np.array([v * s for v in fwht(x)], np.float32)
+
+
+def prep_group(x, g):
+    """qlinear.rs:152-164, natural order."""
+    buf = np.zeros(128, np.float32)
+    seg = np.asarray(x[g * 128:(g + 1) * 128], np.float32)
+    buf[:len(seg)] = seg
+    return quant_i8(rotate(buf))
+
+
+def int8_codebook(cb):
+    """qlinear.rs:211-216."""
+    m = f32(0)
+    for v in cb:
+        m = max(m, abs(f32(v)))
+    s = m * K127 if m > 0 else f32(1.0)
+    inv = f32(1.0) / s
+    out = []
+    for v in cb:
+        t = float(f32(v) * inv)
+        out.append(int(min(max(np.floor(abs(t) + 0.5) * np.sign(t), -128), 127)))
+    return out, f32(s)
+
+
+def unpack4(codes_row):
+    c = np.asarray(codes_row, np.uint8)
+    out = np.empty(len(c) * 2, np.int64)
+    out[0::2] = c & 15
+    out[1::2] = c >> 4
+    return out
+
+
+def decode_row(codes_row, norms_row, x, cb):
+    """qlinear.rs:327-350: prep every group, lane sums by (p % 32) / 8, the
+    four-lane fma combine."""
+    vals, cbs = int8_codebook(cb)
+    codes = unpack4(codes_row)
+    groups = len(norms_row)
+    lanes = [f32(0)] * 4
+    for g in range(groups):
+        q, sx = prep_group(x, g)
+        s = [0, 0, 0, 0]
+        for p in range(128):
+            s[(p % 32) // 8] += vals[codes[g * 128 + p]] * int(q[p])
+        norm = np.array([norms_row[g]], np.uint16).view(np.float16)[0].astype(np.float32)
+        sc = (sx * cbs) * norm
+        for l in range(4):
+            lanes[l] = fma32(f32(s[l]), sc, lanes[l])
+    return (lanes[0] + lanes[1]) + (lanes[2] + lanes[3])
+
+
+def prefill_row(codes_row, norms_row, x, cb, block):
+    """qlinear.rs:353-363."""
+    vals, cbs = int8_codebook(cb)
+    codes = unpack4(codes_row)
+    acc = f32(0)
+    for g in range(len(norms_row)):
+        q, sx = prep_group(x, g)
+        s = sum(vals[codes[g * 128 + p]] * int(q[p]) for p in range(128))
+        norm = np.array([norms_row[g]], np.uint16).view(np.float16)[0].astype(np.float32)
+        sc = (norm * cbs) * sx if block else norm * (cbs * sx)
+        acc = fma32(f32(s), sc, acc)
+    return acc
+
+
+def lexpf(x):
+    return f32(np.exp(np.float64(f32(x))))
+
+
+def chunk_exp(s, m):
+    """infer.rs:2279-2317 (scalar arm)."""
+    s = list(np.asarray(s, np.float32))
+    l, i = len(s), 0
+    a = [f32(0)] * 4
+    b = [f32(0)] * 4
+    while i + 8 <= l:
+        for k in range(4):
+            e = nexp(s[i + k] - f32(m)); s[i + k] = e; a[k] = a[k] + e
+        for k in range(4):
+            e = nexp(s[i + 4 + k] - f32(m)); s[i + 4 + k] = e; b[k] = b[k] + e
+        i += 8
+    while i + 4 <= l:
+        for k in range(4):
+            e = nexp(s[i + k] - f32(m)); s[i + k] = e; a[k] = a[k] + e
+        i += 4
+    t = [a[k] + b[k] for k in range(4)]
+    total = (t[0] + t[1]) + (t[2] + t[3])
+    if l - i >= 2:
+        e0, e1 = lexpf(s[i] - f32(m)), lexpf(s[i + 1] - f32(m))
+        s[i], s[i + 1] = e0, e1
+        total = (e0 + total) + e1
+        i += 2
+    if l - i == 1:
+        e = lexpf(s[i] - f32(m)); s[i] = e; total = total + e
+    return np.array(s, np.float32), total
+
+
+def key_chunks(n, nested, nkv):
+    """infer.rs:2093-2101."""
+    k = 1 if nested else max(1, 2 * 4 // nkv)
+    c = -(-n // 256)
+    if k * 64 <= n and c < k:
+        c = k
+    chunk = -(-(-(-n // max(c, 1))) // 16) * 16
+    return (-(-n // chunk) if chunk else 0), chunk
+
+
+def sinkhorn64(z):
+    """infer.rs:2501-2525."""
+    z = np.asarray(z, np.float32)
+    e = [0.0] * 16
+    for r in range(4):
+        m = float(max(max(z[r * 4], z[r * 4 + 1]), max(z[r * 4 + 2], z[r * 4 + 3])))
+        for c in range(4):
+            e[r * 4 + c] = float(np.exp(np.float64(z[r * 4 + c]) - m))
+    for _ in range(20):
+        for r in range(4):
+            inv = 1.0 / ((e[r * 4] + e[r * 4 + 1]) + (e[r * 4 + 2] + e[r * 4 + 3]))
+            for c in range(4):
+                e[r * 4 + c] *= inv
+        for c in range(4):
+            inv = 1.0 / ((e[c] + e[4 + c]) + (e[8 + c] + e[12 + c]))
+            for r in range(4):
+                e[r * 4 + c] *= inv
+    return np.array(e, np.float32)
