@@ -45,6 +45,7 @@ def parse():
     ap.add_argument("--seqs", type=int, default=1024, help="sequences per GPU")
     ap.add_argument("--roofline-site", default="auto")
     ap.add_argument("--cpu-baseline", type=int, default=1, help="time the oracle on rank 0 (N=1 only)")
+    ap.add_argument("--secondary", type=int, default=1, help="also time batch-1 decode and 256x700 prefill (N=1)")
     return ap.parse_args()
 
 
@@ -215,6 +216,53 @@ def cpu_baseline_sample(data):
                       f"prefill (decode timed only)"}
 
 
+def secondary(model, local):
+    """The other BASELINE.json throughput configs on this GPU, reported beside
+    the headline: batch-1 decode (configs[0]: 118-token prompt, 45 greedy
+    steps, as `needle bench --decode 45` drives the engine) and batched
+    prefill (configs[3]: 256 sequences x 700 tokens, logits of the last
+    position). CUDA events on the engine's stream."""
+    import torch
+
+    import needle_b200 as nb
+
+    out = {}
+    rng = np.random.default_rng(77)
+    dev = f"cuda:{local}"
+    # batch 1, host buffers, one call per step like the reference's bench loop
+    b = model.batch(1, PROMPT + STEPS_CFG + 1)
+    st = torch.cuda.ExternalStream(b.stream, device=dev)
+    prompt = rng.integers(0, model.vocab, (1, PROMPT)).astype(np.int32)
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    e[0].record(st)
+    b.forward(prompt)
+    e[1].record(st)
+    nxt = np.zeros(1, np.int32)
+    for _ in range(STEPS_CFG):
+        b.step(None, nxt)
+    e[2].record(st)
+    torch.cuda.synchronize()
+    out["decode_b1"] = {"prefill_tok_s": PROMPT / (e[0].elapsed_time(e[1]) / 1e3),
+                        "decode_tok_s": STEPS_CFG / (e[1].elapsed_time(e[2]) / 1e3),
+                        "decode_ms_per_token": e[1].elapsed_time(e[2]) / STEPS_CFG}
+    del b
+    # 256 x 700 prefill, ids resident in HBM
+    S, n = 256, 700
+    b = model.batch(S, n + 1)
+    st = torch.cuda.ExternalStream(b.stream, device=dev)
+    ids = torch.from_numpy(rng.integers(0, model.vocab, (S, n)).astype(np.int32)).to(dev)
+    logits = torch.empty((S, 1, model.out_rows), dtype=torch.float32, device=dev)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    b.forward(ids, nb.OUT_LAST_LOGITS, out=logits)
+    e1.record(st)
+    torch.cuda.synchronize()
+    out["prefill_256x700"] = {"tok_s": S * n / (e0.elapsed_time(e1) / 1e3), "ms": e0.elapsed_time(e1)}
+    del b
+    return out
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -311,6 +359,7 @@ def main():
     t_value = max_over_ranks(t_value)
     t_e2e = max_over_ranks(t_e2e)
     clk = clocks.summary()
+    extra = secondary(model, local) if (args.secondary and world == 1) else None
 
     if rank == 0:
         hbm, bf16, kind = peaks()
@@ -342,6 +391,7 @@ def main():
             "sites_ms_per_step": {k: round(v["ms_per_step"], 4) for k, v in sweep.items()},
             "cpu_baseline": cpu,
             "clocks": clk,
+            "secondary": extra,
         }
         print(json.dumps(line), flush=True)
     del bA, bB

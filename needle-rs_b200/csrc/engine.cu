@@ -144,13 +144,49 @@ static void append(HostMat& dst, const HostMat& src) {
     dst.norms.insert(dst.norms.end(), src.norms.begin(), src.norms.end());
 }
 
-static DevMat to_dev(Model& m, const HostMat& h) {
+// qlinear.rs:211-216, 244-265: the shared 4-bit codebook's int8 form.
+static void int8_codebook(int8_t vals[16], float* cbs_out, std::vector<float>* fvals) {
+    std::vector<float> cb = cq_codebook(4, 128);
+    float mx = 0.f;
+    for (float v : cb) mx = std::fmax(mx, std::fabs(v));
+    uint32_t k127u = 0x3c010204u;
+    float k127;
+    std::memcpy(&k127, &k127u, 4);
+    float cbs = mx > 0.f ? mx * k127 : 1.0f;
+    float inv = 1.0f / cbs;
+    for (int i = 0; i < 16; i++) vals[i] = (int8_t)std::min(std::max(std::round(cb[i] * inv), -128.f), 127.f);
+    *cbs_out = cbs;
+    if (fvals) *fvals = cb;
+}
+
+// A matrix on the device: the archive's codes and norms, plus (for the
+// projections that run as tensor-core GEMMs) the codes expanded through the
+// int8 codebook into lane-major groups (see DevMat::w8).
+static DevMat to_dev(Model& m, const HostMat& h, bool expand) {
     DevMat d;
     d.codes = m.upload(h.codes.data(), h.codes.size());
     d.norms = m.upload(h.norms.data(), h.norms.size());
     d.out = h.out;
     d.in_dim = h.in_dim;
     d.groups = h.groups;
+    if (expand) {
+        int8_t vals[16];
+        float cbs;
+        int8_codebook(vals, &cbs, nullptr);
+        const int K = h.groups * 128;
+        std::vector<int8_t> w((size_t)h.out * K);
+        for (size_t r = 0; r < (size_t)h.out; r++)
+            for (int g = 0; g < h.groups; g++) {
+                const uint8_t* c = h.codes.data() + (r * h.groups + g) * 64;
+                int8_t* dst = w.data() + r * K + g * 128;
+                for (int p = 0; p < 128; p++) {
+                    int code = (p & 1) ? (c[p >> 1] >> 4) : (c[p >> 1] & 15);
+                    int a = p >> 5, l = (p & 31) >> 3, b = p & 7;
+                    dst[l * 32 + a * 8 + b] = vals[code];
+                }
+            }
+        d.w8 = m.upload(w.data(), w.size());
+    }
     return d;
 }
 
@@ -174,7 +210,7 @@ static Model* load_model(const uint8_t* bytes, size_t n, int device) {
     const int d = c.d;
     HostMat emb = host_mat(a, cur, d);
     if (emb.out != c.vocab) throw std::runtime_error("embedding shape does not match the header");
-    m.embedding = to_dev(m, emb);
+    m.embedding = to_dev(m, emb, true);
     m.layers.resize(c.L);
     std::vector<HostMat> qkvg(c.L);
     for (int l = 0; l < c.L; l++) {
@@ -193,8 +229,8 @@ static Model* load_model(const uint8_t* bytes, size_t n, int device) {
             throw std::runtime_error("attention projection shapes do not match the header");
         HostMat f;
         append(f, q); append(f, k); append(f, v); append(f, g);
-        w.qkvg = to_dev(m, f);
-        w.out = to_dev(m, o);
+        w.qkvg = to_dev(m, f, true);
+        w.out = to_dev(m, o, true);
         w.post_norm = m.upload(small_f32(a, cur, d).data(), d);
         w.attn_gate = small_f32(a, cur, 1)[0];
         w.pre_hada = m.upload(small_f32(a, cur, d).data(), d);
@@ -252,8 +288,8 @@ static Model* load_model(const uint8_t* bytes, size_t n, int device) {
         HostMat kv;
         append(kv, k);
         append(kv, v);
-        m.etables.push_back(to_dev(m, t));
-        m.ekv.push_back(to_dev(m, kv));
+        m.etables.push_back(to_dev(m, t, false));
+        m.ekv.push_back(to_dev(m, kv, true));
         auto taps = small_f32(a, cur, 4 * (size_t)d);
         m.etaps.push_back(m.upload(taps.data(), taps.size()));
     }
@@ -289,20 +325,10 @@ static Model* load_model(const uint8_t* bytes, size_t n, int device) {
     m.rope_sin = m.upload(ts.data(), ts.size());
     m.sd = m.upload(m.h_sd.data(), half);
     m.cd = m.upload(m.h_cd.data(), half);
-    // qlinear.rs:211-216, 244-265: the shared 4-bit codebook and its int8 form
-    std::vector<float> cb = cq_codebook(4, 128);
     int8_t vals[16];
     float cbs = 0.f;
-    {
-        float mx = 0.f;
-        for (float v : cb) mx = std::fmax(mx, std::fabs(v));
-        uint32_t k127u = 0x3c010204u;
-        float k127;
-        std::memcpy(&k127, &k127u, 4);
-        cbs = mx > 0.f ? mx * k127 : 1.0f;
-        float inv = 1.0f / cbs;
-        for (int i = 0; i < 16; i++) vals[i] = (int8_t)std::min(std::max(std::round(cb[i] * inv), -128.f), 127.f);
-    }
+    std::vector<float> cb;
+    int8_codebook(vals, &cbs, &cb);
     set_constants(vals, cb.data(), cbs, (float)(1.0 / std::sqrt(128.0)));
     CK(cudaGetLastError());
     CK(cudaDeviceSynchronize());
@@ -493,7 +519,7 @@ static int chunk(Batch& b, const int32_t* ids, int T, int outputs) {
             snap(b, "snap.o", b.o, (size_t)M * 768);
         }
         tick(b, ND_SITE_POST);
-        launch_post_block(w, lane, b.o, b.x1, b.u, b.p, m.perm1, m.perm2, M, b.xs, st);
+        launch_post_block(w, b.o, b.x1, b.u, b.p, m.perm1, m.perm2, M, b.xs, st);
         tick(b, ND_SITE_POST);
         if (l == b.debug_layer) snap(b, "snap.xs", b.xs, (size_t)M * 3072);
     }

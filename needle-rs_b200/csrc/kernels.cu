@@ -85,7 +85,11 @@ void launch_embed(DevMat emb, const int32_t* ids, int M, float* xs, cudaStream_t
 // ------------------------------------------------------------ A8 prep
 
 // prep_group (qlinear.rs:152-164): zero-pad, rotate, int8 with one scale per
-// (row, group). Stored in natural order.
+// (row, group). Stored lane-major: input p = 32a + 8l + b of a group sits at
+// l*32 + a*8 + b, so the decode kernel's lane l (qlinear.rs:333) is the
+// contiguous 32-byte slice l*32 .. l*32+31 (lane i holds p = 4i .. 4i+3).
+__device__ __forceinline__ int lane_major_pos(int i) { return ((i & 7) >> 1) * 32 + (i >> 3) * 8 + (i & 1) * 4; }
+
 __device__ __forceinline__ void prep_group_warp(float v[4], int lane, int8_t* q, float* sx) {
     fwht128_warp(v, lane);
     float a = 0.f;
@@ -102,7 +106,7 @@ __device__ __forceinline__ void prep_group_warp(float v[4], int lane, int8_t* q,
     o.y = q8_round(v[1], inv);
     o.z = q8_round(v[2], inv);
     o.w = q8_round(v[3], inv);
-    *(char4*)(q + 4 * lane) = o;
+    *(char4*)(q + lane_major_pos(lane)) = o;
     if (lane == 0) *sx = s;
 }
 
@@ -191,11 +195,12 @@ __global__ void __launch_bounds__(256) cq_gemm_kernel(DevMat W, const int8_t* ac
         for (int blk = 0; blk < 4; blk++)
 #pragma unroll
             for (int l = 0; l < 4; l++) {
-                int off = g * 128 + blk * 32 + l * 8;
+                int off = g * 128 + blk * 32 + l * 8;     // weights: natural order
+                int offa = g * 128 + l * 32 + blk * 8;    // activations: lane-major
                 int w0 = *(const int*)(wr + off), w1 = *(const int*)(wr + off + 4);
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
-                    const int8_t* ar = as + (mq * 4 + i) * GEMM_LD + off;
+                    const int8_t* ar = as + (mq * 4 + i) * GEMM_LD + offa;
                     s[i][l] = __dp4a(w0, *(const int*)ar, s[i][l]);
                     s[i][l] = __dp4a(w1, *(const int*)(ar + 4), s[i][l]);
                 }
@@ -231,12 +236,207 @@ __global__ void __launch_bounds__(256) cq_gemm_kernel(DevMat W, const int8_t* ac
 
 static const size_t GEMM_SMEM = (GEMM_TN + GEMM_TM) * GEMM_LD + (GEMM_TM + GEMM_TN) * 6 * 4;
 
+// ---------------------------------------------- CQ matmul on tensor cores
+//
+// The same two combines with the integer sums from mma.sync m16n8k32 s8:
+// with both operands lane-major, the K-slice [g*128 + l*32, +32) is decode
+// lane l of group g, so one MMA gives exactly one lane sum (decode) and four
+// chained MMAs one group sum (prefill). Each accumulator starts at the bit
+// pattern of 1.5 * 2^23: every sum here is below 2^22 in magnitude, so the
+// result reinterpreted as a float minus 1.5 * 2^23 is the sum, exactly, in
+// one FP32 subtract. CTA tile 64 rows x 64 outputs, K = 768 resident in
+// shared memory, loaded one 128-wide group at a time with cp.async so the
+// first groups compute while the rest arrive.
+constexpr int MMA_BM = 64, MMA_BN = 64, MMA_K = 768, MMA_LD = MMA_K + 16;
+constexpr int MMA_MAGIC = 0x4B400000;
+constexpr size_t MMA_SMEM = (size_t)(MMA_BM + MMA_BN) * MMA_LD + (size_t)(2 * MMA_BM + 2 * MMA_BN) * 6 * 4;
+
+__device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2], const int (&c)[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};\n"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(c[3]));
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+    uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+    int n = valid ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(n));
+}
+
+__device__ __forceinline__ float magic_to_float(int v) { return __fsub_rn(__int_as_float(v), 12582912.0f); }
+
+template <bool DECODE>
+__global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y,
+                                                        int ldy, int col0) {
+    extern __shared__ __align__(16) int8_t smem[];
+    int8_t* ws = smem;                                  // [BN][LD]
+    int8_t* as = smem + MMA_BN * MMA_LD;                // [BM][LD]
+    float* s_sx = (float*)(as + MMA_BM * MMA_LD);       // [BM][6] sx
+    float* s_sxc = s_sx + MMA_BM * 6;                   // [BM][6] sx * cbs
+    float* s_nrm = s_sxc + MMA_BM * 6;                  // [BN][6] norm
+    float* s_nc = s_nrm + MMA_BN * 6;                   // [BN][6] norm * cbs
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n0 = blockIdx.x * MMA_BN, m0 = blockIdx.y * MMA_BM;
+    // cp.async: group g of every row of both tiles (8 x 16 B per row)
+    for (int g = 0; g < 6; g++) {
+        for (int idx = tid; idx < (MMA_BN + MMA_BM) * 8; idx += 256) {
+            int r = idx >> 3, c = idx & 7;
+            if (r < MMA_BN) {
+                int n = n0 + r;
+                bool ok = n < W.out;
+                cp_async16(ws + r * MMA_LD + g * 128 + c * 16, W.w8 + (size_t)(ok ? n : 0) * MMA_K + g * 128 + c * 16, ok);
+            } else {
+                int mr = r - MMA_BN, m = m0 + mr;
+                bool ok = m < M;
+                cp_async16(as + mr * MMA_LD + g * 128 + c * 16, act + (size_t)(ok ? m : 0) * MMA_K + g * 128 + c * 16, ok);
+            }
+        }
+        asm volatile("cp.async.commit_group;\n" ::);
+    }
+    const float cbs = c_cbs;
+    for (int idx = tid; idx < MMA_BM * 6; idx += 256) {
+        int m = m0 + idx / 6;
+        float v = m < M ? sx[(size_t)m * 6 + idx % 6] : 0.f;
+        s_sx[idx] = v;
+        s_sxc[idx] = __fmul_rn(v, cbs);
+    }
+    for (int idx = tid; idx < MMA_BN * 6; idx += 256) {
+        int n = n0 + idx / 6;
+        float v = n < W.out ? h2f(W.norms[(size_t)n * 6 + idx % 6]) : 0.f;
+        s_nrm[idx] = v;
+        s_nc[idx] = __fmul_rn(v, cbs);
+    }
+    const int wm = (warp & 3) * 16, wn = (warp >> 2) * 32;
+    const int gid = lane >> 2, tig = lane & 3;
+    const int r0 = wm + gid, r1 = r0 + 8;  // this thread's two rows in the tile
+    // per-row combine of the prefill kernel: block rows t < T/4*4
+    bool blk0 = true, blk1 = true;
+    if (!DECODE) {
+        blk0 = ((m0 + r0) % T) < T / 4 * 4;
+        blk1 = ((m0 + r1) % T) < T / 4 * 4;
+    }
+    float acc[4][4][4];  // [n-tile][element][lane] (prefill uses lane 0)
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+#pragma unroll
+            for (int l = 0; l < 4; l++) acc[j][e][l] = 0.f;
+    const int magic[4] = {MMA_MAGIC, MMA_MAGIC, MMA_MAGIC, MMA_MAGIC};
+#pragma unroll 1
+    for (int g = 0; g < 6; g++) {
+        switch (g) {  // wait for group g's bytes (5 - g groups may stay in flight)
+            case 0: asm volatile("cp.async.wait_group 5;\n" ::); break;
+            case 1: asm volatile("cp.async.wait_group 4;\n" ::); break;
+            case 2: asm volatile("cp.async.wait_group 3;\n" ::); break;
+            case 3: asm volatile("cp.async.wait_group 2;\n" ::); break;
+            case 4: asm volatile("cp.async.wait_group 1;\n" ::); break;
+            default: asm volatile("cp.async.wait_group 0;\n" ::); break;
+        }
+        __syncthreads();
+        // scales of this group for this thread's rows and columns
+        float rs0, rs1, cs[4][2];
+        if (DECODE) {
+            rs0 = s_sxc[r0 * 6 + g];
+            rs1 = s_sxc[r1 * 6 + g];
+        } else {
+            rs0 = blk0 ? s_sx[r0 * 6 + g] : s_sxc[r0 * 6 + g];
+            rs1 = blk1 ? s_sx[r1 * 6 + g] : s_sxc[r1 * 6 + g];
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                int cn = wn + j * 8 + tig * 2 + h;
+                cs[j][h] = s_nrm[cn * 6 + g];
+            }
+        int dsum[4][4];
+#pragma unroll
+        for (int l = 0; l < 4; l++) {
+            const int kb = g * 128 + l * 32 + tig * 4;
+            uint32_t a[4];
+            a[0] = *(const uint32_t*)(as + r0 * MMA_LD + kb);
+            a[1] = *(const uint32_t*)(as + r1 * MMA_LD + kb);
+            a[2] = *(const uint32_t*)(as + r0 * MMA_LD + kb + 16);
+            a[3] = *(const uint32_t*)(as + r1 * MMA_LD + kb + 16);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int nr = wn + j * 8 + gid;
+                uint32_t b[2];
+                b[0] = *(const uint32_t*)(ws + nr * MMA_LD + kb);
+                b[1] = *(const uint32_t*)(ws + nr * MMA_LD + kb + 16);
+                int d[4];
+                if (DECODE) {
+                    mma_s8(d, a, b, magic);
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        // (sx * cbs) * norm, then the lane's fma
+                        float sc = __fmul_rn(e < 2 ? rs0 : rs1, cs[j][e & 1]);
+                        acc[j][e][l] = __fmaf_rn(magic_to_float(d[e]), sc, acc[j][e][l]);
+                    }
+                } else {
+                    if (l == 0) {
+                        mma_s8(d, a, b, magic);
+                    } else {
+                        int c[4] = {dsum[j][0], dsum[j][1], dsum[j][2], dsum[j][3]};
+                        mma_s8(d, a, b, c);
+                    }
+#pragma unroll
+                    for (int e = 0; e < 4; e++) dsum[j][e] = d[e];
+                }
+            }
+        }
+        if (!DECODE) {
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const bool blk = e < 2 ? blk0 : blk1;
+                    const int cn = wn + j * 8 + tig * 2 + (e & 1);
+                    // block rows: (norm * cbs) * sx; remainder rows: norm * (cbs * sx)
+                    float sc = blk ? __fmul_rn(s_nc[cn * 6 + g], e < 2 ? rs0 : rs1)
+                                   : __fmul_rn(cs[j][e & 1], e < 2 ? rs0 : rs1);
+                    acc[j][e][0] = __fmaf_rn(magic_to_float(dsum[j][e]), sc, acc[j][e][0]);
+                }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int m = m0 + (e < 2 ? r0 : r1), n = n0 + wn + j * 8 + tig * 2 + (e & 1);
+            if (m >= M || n >= W.out) continue;
+            float v = DECODE ? __fadd_rn(__fadd_rn(acc[j][e][0], acc[j][e][1]), __fadd_rn(acc[j][e][2], acc[j][e][3]))
+                             : acc[j][e][0];
+            y[(size_t)m * ldy + col0 + n] = v;
+        }
+}
+
 void launch_cq_gemm(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y, int ldy, int col0, cudaStream_t st) {
     COUNT_LAUNCH();
+    if (W.w8 && W.groups == 6 && M >= 32) {
+        dim3 grid(cdiv(W.out, MMA_BN), cdiv(M, MMA_BM));
+        if (T == 1)
+            cq_mma_kernel<true><<<grid, 256, MMA_SMEM, st>>>(W, act, sx, M, T, y, ldy, col0);
+        else
+            cq_mma_kernel<false><<<grid, 256, MMA_SMEM, st>>>(W, act, sx, M, T, y, ldy, col0);
+        return;
+    }
     cq_gemm_kernel<<<dim3(cdiv(W.out, GEMM_TN), cdiv(M, GEMM_TM)), 256, GEMM_SMEM, st>>>(W, act, sx, M, T, y, ldy, col0);
 }
 
+template <bool DECODE>
+__global__ void cq_mma_kernel(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y, int ldy, int col0);
+
+struct AttSmem;
+extern const size_t ATT_SMEM;
+__global__ void attention_kernel(const float* qbuf, const float* proj, Caches c, int l, int T, int p0, int window, float* att);
+
 static cudaError_t init_attrs() {
+    cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_SMEM);
+    cudaFuncSetAttribute(cq_mma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
+    cudaFuncSetAttribute(cq_mma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
     return cudaFuncSetAttribute(cq_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM);
 }
 
@@ -362,7 +562,32 @@ __global__ void __launch_bounds__(256) mhc_read_kernel(LayerW w, int lane_own, c
         float z = __fadd_rn(__fadd_rn(__fmul_rn(pr[tid], w.a_pre), off), w.b_pre[tid]);
         hp[tid] = __fdiv_rn(1.0f, __fadd_rn(lexpf(-z), 1.0f));
     }
-    if (tid < 24) p[(size_t)m * 24 + tid] = pr[tid];
+    if (warp == 1) {
+        // The post block's gates, ready before it runs (infer.rs:1580-1586):
+        // lanes 0-15 hold the 4x4 Sinkhorn (sinkhorn64, 2501-2525) one element
+        // each; the pairwise row and column sums are xor-shuffles, which add
+        // (e0 + e1) + (e2 + e3) as the reference does. Lanes 16-19: hpost.
+        const int r = (ln & 15) >> 2;
+        float zr = ln < 16 ? __fmaf_rn(pr[8 + ln], w.a_res, w.b_res[ln]) : 0.f;
+        float zm = fmaxf(fmaxf(__shfl_sync(0xffffffffu, zr, (ln & 16) + r * 4), __shfl_sync(0xffffffffu, zr, (ln & 16) + r * 4 + 1)),
+                         fmaxf(__shfl_sync(0xffffffffu, zr, (ln & 16) + r * 4 + 2), __shfl_sync(0xffffffffu, zr, (ln & 16) + r * 4 + 3)));
+        double e = exp(__dsub_rn((double)zr, (double)zm));
+        for (int it = 0; it < 20; it++) {
+            double s2 = __dadd_rn(e, __shfl_xor_sync(0xffffffffu, e, 1));
+            double s4 = __dadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, 2));
+            e = __dmul_rn(e, __ddiv_rn(1.0, s4));
+            double c2 = __dadd_rn(e, __shfl_xor_sync(0xffffffffu, e, 4));
+            double c4 = __dadd_rn(c2, __shfl_xor_sync(0xffffffffu, c2, 8));
+            e = __dmul_rn(e, __ddiv_rn(1.0, c4));
+        }
+        if (ln < 16) p[(size_t)m * 24 + 4 + ln] = (float)e;
+        if (ln >= 16 && ln < 20) {
+            const int j = ln - 16;
+            float off = j == lane_own ? 0.0f : -4.0f;
+            float z = __fadd_rn(__fadd_rn(__fmul_rn(pr[4 + j], w.a_post), off), w.b_post[j]);
+            p[(size_t)m * 24 + j] = __fdiv_rn(2.0f, __fadd_rn(lexpf(-z), 1.0f));
+        }
+    }
     __syncthreads();
     for (int ch = tid; ch < 768; ch += 256) {
         float o = __fmul_rn(x[ch], hp[0]);
@@ -582,230 +807,286 @@ __device__ __forceinline__ void key_chunks_dev(int n, bool nested, int* count, i
     *count = ch > 0 ? (n + ch - 1) / ch : 0;
 }
 
-__global__ void __launch_bounds__(128) attention_kernel(const float* qbuf, const float* proj, Caches c, int l, int T, int p0,
+// One CTA per (row, kv head) serves the kv head's 6 query heads, so each
+// key and value row of the chunk is read from HBM once: keys to shared
+// memory as stored, values transposed [dim][key] so four keys' bytes of one
+// value dimension form one word for the digit dot products.
+constexpr int ATT_HEADS = 6, ATT_VT_LD = ATT_MAXCHUNK + 4;
+struct AttSmem {
+    int8_t k[ATT_MAXCHUNK][48];
+    int8_t vt[64][ATT_VT_LD];
+    float ks[ATT_MAXCHUNK], vs[ATT_MAXCHUNK];
+    float s[ATT_HEADS][ATT_MAXCHUNK];
+    int8_t dh[ATT_HEADS][ATT_MAXCHUNK], dmid[ATT_HEADS][ATT_MAXCHUNK], dl[ATT_HEADS][ATT_MAXCHUNK];
+    float po[ATT_HEADS][ATT_MAXPARTS][64];
+    float pm[ATT_HEADS][ATT_MAXPARTS], psum[ATT_HEADS][ATT_MAXPARTS];
+    int8_t q8[ATT_HEADS][48];
+    float qs[ATT_HEADS], mx[ATT_HEADS], wmax[ATT_HEADS];
+    float chains[ATT_HEADS][8];
+};
+
+__global__ void __launch_bounds__(256) attention_kernel(const float* qbuf, const float* proj, Caches c, int l, int T, int p0,
                                                         int window, float* att) {
-    __shared__ __align__(16) int8_t q8[48];
-    __shared__ float sbuf[ATT_MAXCHUNK];
-    __shared__ int8_t dh[ATT_MAXCHUNK], dm_[ATT_MAXCHUNK], dl[ATT_MAXCHUNK];
-    __shared__ float red[4];
-    __shared__ float pm[ATT_MAXPARTS], psum[ATT_MAXPARTS];
-    __shared__ float po[ATT_MAXPARTS][64];
-    __shared__ int pv[3][2][64];
-    __shared__ float qs_s, m_s, sum_s, wmax_s;
-    const int m = blockIdx.x, hh = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int s = m / T, i = m % T, pos = p0 + i, kvh = hh / 6;
+    extern __shared__ __align__(16) int8_t att_raw[];
+    AttSmem& sm = *reinterpret_cast<AttSmem*>(att_raw);
+    const int m = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int s = m / T, i = m % T, pos = p0 + i;
     const bool nested = T > 1;
     const int lo = window > 0 ? max(0, pos + 1 - window) : 0;
     const int n = pos + 1 - lo;
-    if (warp == 0) {
-        float x0 = qbuf[(size_t)m * 576 + hh * 48 + lane];
-        float x1 = lane < 16 ? qbuf[(size_t)m * 576 + hh * 48 + 32 + lane] : 0.f;
+    if (warp < ATT_HEADS) {
+        // quant_i8 of the head's query, scale folded with 1/sqrt(48) (infer.rs:1885)
+        const float* q = qbuf + (size_t)m * 576 + (kvh * ATT_HEADS + warp) * 48;
+        float x0 = q[lane], x1 = lane < 16 ? q[32 + lane] : 0.f;
         float a = warp_max(fmaxf(fabsf(x0), fabsf(x1)));
         float sc = a > 0.f ? __fmul_rn(a, ND_K127) : 1.0f;
         float inv = __fdiv_rn(1.0f, sc);
-        q8[lane] = q8_round(x0, inv);
-        if (lane < 16) q8[32 + lane] = q8_round(x1, inv);
-        if (lane == 0) qs_s = __fmul_rn(sc, ND_INV_SQRT_QK);
+        sm.q8[warp][lane] = q8_round(x0, inv);
+        if (lane < 16) sm.q8[warp][32 + lane] = q8_round(x1, inv);
+        if (lane == 0) sm.qs[warp] = __fmul_rn(sc, ND_INV_SQRT_QK);
     }
-    __syncthreads();
-    const float qs = qs_s;
     int count, chunk;
     key_chunks_dev(n, nested, &count, &chunk);
     const size_t kvrow = (((size_t)s * c.L + l) * 2 + kvh) * c.cap;
     const int8_t* k8 = c.k8 + kvrow * 48;
-    const float* ks = c.ks + kvrow;
     const int8_t* v8 = c.v8 + kvrow * 64;
-    const float* vs = c.vs + kvrow;
-    int qw4[12];
-#pragma unroll
-    for (int e = 0; e < 12; e++) qw4[e] = ((const int*)q8)[e];
     for (int ci = 0; ci < count; ci++) {
-        const int c0 = ci * chunk, len = min(chunk, n - c0), blocked = len / 4 * 4;
-        // scores
-        float mx = -INFINITY;
-        for (int k = tid; k < len; k += 128) {
-            int slot = lo + c0 + k;
-            const int* kr = (const int*)(k8 + (size_t)slot * 48);
+        const int c0 = ci * chunk, len = min(chunk, n - c0), blocked = len / 4 * 4, len4 = (len + 3) / 4 * 4;
+        const int base = lo + c0;
+        __syncthreads();  // the previous chunk's readers are done
+        for (int idx = tid; idx < len * 3; idx += 256) {
+            int k = idx / 3, part = idx % 3;
+            *(int4*)(&sm.k[k][part * 16]) = *(const int4*)(k8 + (size_t)(base + k) * 48 + part * 16);
+        }
+        for (int idx = tid; idx < len * 4; idx += 256) {
+            int k = idx >> 2, part = idx & 3;
+            int4 v = *(const int4*)(v8 + (size_t)(base + k) * 64 + part * 16);
+            const int8_t* b = (const int8_t*)&v;
+#pragma unroll
+            for (int e = 0; e < 16; e++) sm.vt[part * 16 + e][k] = b[e];
+        }
+        for (int k = tid; k < len; k += 256) {
+            sm.ks[k] = c.ks[kvrow + base + k];
+            sm.vs[k] = c.vs[kvrow + base + k];
+        }
+        __syncthreads();
+        // scores: (ks * dot) * qs in whole 4-blocks, (ks * qs) * dot after
+        for (int idx = tid; idx < ATT_HEADS * len; idx += 256) {
+            int h = idx / len, k = idx % len;
+            const int* kr = (const int*)sm.k[k];
+            const int* qr = (const int*)sm.q8[h];
             int dot = 0;
 #pragma unroll
-            for (int e = 0; e < 12; e++) dot = __dp4a(qw4[e], kr[e], dot);
-            float ksv = ks[slot];
-            float sv = k < blocked ? __fmul_rn(__fmul_rn(ksv, (float)dot), qs) : __fmul_rn(__fmul_rn(ksv, qs), (float)dot);
-            sbuf[k] = sv;
-            mx = fmaxf(mx, sv);
-        }
-        mx = warp_max(mx);
-        if (lane == 0) red[warp] = mx;
-        __syncthreads();
-        if (tid == 0) m_s = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-        __syncthreads();
-        const float mv = m_s;
-        // numerators: the inline exp on whole 4-blocks, libm exp after
-        const int n4 = len / 4 * 4;
-        for (int k = tid; k < len; k += 128) {
-            float dlt = __fsub_rn(sbuf[k], mv);
-            sbuf[k] = k < n4 ? nexp(dlt) : lexpf(dlt);
+            for (int e = 0; e < 12; e++) dot = __dp4a(qr[e], kr[e], dot);
+            float qs = sm.qs[h], ksv = sm.ks[k];
+            sm.s[h][k] = k < blocked ? __fmul_rn(__fmul_rn(ksv, (float)dot), qs) : __fmul_rn(__fmul_rn(ksv, qs), (float)dot);
         }
         __syncthreads();
-        if (tid == 0) {
-            // chunk_exp's sum: a[k] over 8-blocks (first halves) and the
-            // trailing 4-block, b[k] over the 8-blocks' second halves.
-            const int n8 = len / 8 * 8;
-            float av[4] = {0.f, 0.f, 0.f, 0.f}, bv[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int q = 0; q < n8; q += 8)
-                for (int k = 0; k < 4; k++) {
-                    av[k] = __fadd_rn(av[k], sbuf[q + k]);
-                    bv[k] = __fadd_rn(bv[k], sbuf[q + 4 + k]);
-                }
-            if (n4 > n8)
-                for (int k = 0; k < 4; k++) av[k] = __fadd_rn(av[k], sbuf[n8 + k]);
+        if (warp < ATT_HEADS) {
+            float mx = -INFINITY;
+            for (int k = lane; k < len; k += 32) mx = fmaxf(mx, sm.s[warp][k]);
+            mx = warp_max(mx);
+            if (lane == 0) sm.mx[warp] = mx;
+        }
+        __syncthreads();
+        // numerators: the inline exp on whole 4-blocks, libm exp for the rest
+        for (int idx = tid; idx < ATT_HEADS * len; idx += 256) {
+            int h = idx / len, k = idx % len;
+            float dlt = __fsub_rn(sm.s[h][k], sm.mx[h]);
+            sm.s[h][k] = k < blocked ? nexp(dlt) : lexpf(dlt);
+        }
+        __syncthreads();
+        // chunk_exp's sum order: chain j < 4 adds the first halves of the
+        // 8-blocks and the trailing 4-block, chain j >= 4 the second halves
+        if (tid < ATT_HEADS * 8) {
+            const int h = tid >> 3, j = tid & 7, n8 = len / 8 * 8;
+            float a = 0.f;
+            for (int q = 0; q < n8; q += 8) a = __fadd_rn(a, sm.s[h][q + j]);
+            if (j < 4 && blocked > n8) a = __fadd_rn(a, sm.s[h][n8 + j]);
+            sm.chains[h][j] = a;
+        }
+        __syncthreads();
+        if (tid < ATT_HEADS) {
+            const int h = tid;
             float t[4];
-            for (int k = 0; k < 4; k++) t[k] = __fadd_rn(av[k], bv[k]);
+            for (int k = 0; k < 4; k++) t[k] = __fadd_rn(sm.chains[h][k], sm.chains[h][4 + k]);
             float sum = __fadd_rn(__fadd_rn(t[0], t[1]), __fadd_rn(t[2], t[3]));
-            int ii = n4;
+            int ii = blocked;
             if (len - ii >= 2) {
-                sum = __fadd_rn(__fadd_rn(sbuf[ii], sum), sbuf[ii + 1]);
+                sum = __fadd_rn(__fadd_rn(sm.s[h][ii], sum), sm.s[h][ii + 1]);
                 ii += 2;
             }
-            if (len - ii == 1) sum = __fadd_rn(sum, sbuf[ii]);
-            sum_s = sum;
+            if (len - ii == 1) sum = __fadd_rn(sum, sm.s[h][ii]);
+            sm.psum[h][ci] = sum;
+            sm.pm[h][ci] = sm.mx[h];
         }
         __syncthreads();
-        // weights times the value scales, their max
-        float wm = 0.f;
-        for (int k = tid; k < len; k += 128) {
-            float wv = __fmul_rn(sbuf[k], vs[lo + c0 + k]);
-            sbuf[k] = wv;
-            wm = fmaxf(wm, wv);
-        }
-        wm = warp_max(wm);
-        if (lane == 0) red[warp] = wm;
-        __syncthreads();
-        if (tid == 0) wmax_s = fmaxf(fmaxf(fmaxf(0.f, red[0]), red[1]), fmaxf(red[2], red[3]));
-        __syncthreads();
-        const float wmax = wmax_s, qw = __fdiv_rn(ND_Q21, wmax);
-        for (int k = tid; k < len; k += 128) {
-            int wq = (int)roundf(__fmul_rn(sbuf[k], qw));
-            dh[k] = (int8_t)(wq >> 14);
-            dm_[k] = (int8_t)((wq >> 7) & 127);
-            dl[k] = (int8_t)(wq & 127);
+        // weights times the value scales and their max (from zero)
+        for (int idx = tid; idx < ATT_HEADS * len; idx += 256) {
+            int h = idx / len, k = idx % len;
+            sm.s[h][k] = __fmul_rn(sm.s[h][k], sm.vs[k]);
         }
         __syncthreads();
-        // P.V as three integer dots per value dimension
-        {
-            const int dm = tid & 63, half = tid >> 6;
-            int sh = 0, sm = 0, sl = 0;
-            for (int k = half; k < len; k += 2) {
-                int v = v8[(size_t)(lo + c0 + k) * 64 + dm];
-                sh += dh[k] * v;
-                sm += dm_[k] * v;
-                sl += dl[k] * v;
+        if (warp < ATT_HEADS) {
+            float wm = 0.f;
+            for (int k = lane; k < len; k += 32) wm = fmaxf(wm, sm.s[warp][k]);
+            wm = warp_max(wm);
+            if (lane == 0) sm.wmax[warp] = wm;
+        }
+        __syncthreads();
+        // 21-bit digits of round(w * Q21 / wmax), zero past the chunk's end
+        for (int idx = tid; idx < ATT_HEADS * len4; idx += 256) {
+            int h = idx / len4, k = idx % len4;
+            int wq = 0;
+            if (k < len) wq = (int)roundf(__fmul_rn(sm.s[h][k], __fdiv_rn(ND_Q21, sm.wmax[h])));
+            sm.dh[h][k] = (int8_t)(wq >> 14);
+            sm.dmid[h][k] = (int8_t)((wq >> 7) & 127);
+            sm.dl[h][k] = (int8_t)(wq & 127);
+        }
+        __syncthreads();
+        // P.V: three exact integer dots per (head, value dimension)
+        for (int idx = tid; idx < ATT_HEADS * 64; idx += 256) {
+            const int h = idx >> 6, dm = idx & 63;
+            const int* vr = (const int*)sm.vt[dm];
+            const int* ph = (const int*)sm.dh[h];
+            const int* pmid = (const int*)sm.dmid[h];
+            const int* pl = (const int*)sm.dl[h];
+            int sh = 0, smd = 0, sl = 0;
+            for (int w = 0; w < len4 / 4; w++) {
+                int v = vr[w];
+                sh = __dp4a(ph[w], v, sh);
+                smd = __dp4a(pmid[w], v, smd);
+                sl = __dp4a(pl[w], v, sl);
             }
-            pv[0][half][dm] = sh;
-            pv[1][half][dm] = sm;
-            pv[2][half][dm] = sl;
+            float cw = __fmul_rn(sm.wmax[h], ND_C21);
+            sm.po[h][ci][dm] = __fmul_rn(__fmaf_rn(16384.f, (float)sh, __fmaf_rn(128.f, (float)smd, (float)sl)), cw);
         }
-        __syncthreads();
-        if (tid < 64) {
-            int sh = pv[0][0][tid] + pv[0][1][tid], sm = pv[1][0][tid] + pv[1][1][tid], sl = pv[2][0][tid] + pv[2][1][tid];
-            float cw = __fmul_rn(wmax, ND_C21);
-            po[ci][tid] = __fmul_rn(__fmaf_rn(16384.f, (float)sh, __fmaf_rn(128.f, (float)sm, (float)sl)), cw);
-            if (tid == 0) {
-                pm[ci] = mv;
-                psum[ci] = sum_s;
-            }
-        }
-        __syncthreads();
     }
-    if (tid < 64) {
+    __syncthreads();
+    for (int idx = tid; idx < ATT_HEADS * 64; idx += 256) {
+        const int h = idx >> 6, dm = idx & 63;
         float out;
         if (count == 1) {
-            out = __fmul_rn(po[0][tid], __fdiv_rn(1.0f, psum[0]));
+            out = __fmul_rn(sm.po[h][0][dm], __fdiv_rn(1.0f, sm.psum[h][0]));
         } else {
             float big = -1e30f;
-            for (int ci = 0; ci < count; ci++) big = fmaxf(big, pm[ci]);
+            for (int ci = 0; ci < count; ci++) big = fmaxf(big, sm.pm[h][ci]);
             float acc = 0.f, total = 0.f;
             for (int ci = 0; ci < count; ci++) {
-                float wv = lexpf(__fsub_rn(pm[ci], big));
-                acc = __fmaf_rn(po[ci][tid], wv, acc);
-                total = __fmaf_rn(wv, psum[ci], total);
+                float wv = lexpf(__fsub_rn(sm.pm[h][ci], big));
+                acc = __fmaf_rn(sm.po[h][ci][dm], wv, acc);
+                total = __fmaf_rn(wv, sm.psum[h][ci], total);
             }
             out = __fmul_rn(acc, __fdiv_rn(1.0f, total));
         }
-        float g = proj[(size_t)m * 1568 + 800 + hh * 64 + tid];
-        att[(size_t)m * 768 + hh * 64 + tid] = __fdiv_rn(out, __fadd_rn(nexp(-g), 1.0f));
+        const int hh = kvh * ATT_HEADS + h;
+        float g = proj[(size_t)m * 1568 + 800 + hh * 64 + dm];
+        att[(size_t)m * 768 + hh * 64 + dm] = __fdiv_rn(out, __fadd_rn(nexp(-g), 1.0f));
     }
 }
+
+extern const size_t ATT_SMEM = sizeof(AttSmem);
 
 void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int S, int T, int p0, int window, float* att,
                       cudaStream_t st) {
     COUNT_LAUNCH();
-    attention_kernel<<<dim3(S * T, 12), 128, 0, st>>>(qbuf, proj, c, l, T, p0, window, att);
+    attention_kernel<<<dim3(S * T, 2), 256, ATT_SMEM, st>>>(qbuf, proj, c, l, T, p0, window, att);
 }
 
 // ------------------------------------------------------------ post block
 
-// infer.rs:1564-1606 with mlp_native (1610-1634), cond_weights (1640-1694),
-// kron_native / mix8 (2322-2460), silu (2463-2496), sinkhorn64 (2501-2525).
-// One CTA of 1024 threads per row; each Kronecker output is one thread's
-// fma chain over j from zero.
-__device__ __forceinline__ void kron_stage(const float* z, const float* A, const float* B, float* mt, float* t, int tid) {
-    const int r = tid >> 5, cc = tid & 31;
-    float o = 0.f;
+// fma.rn.f32x2: two independent IEEE fmas in one instruction (sm_100).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n.reg .b64 ra, rb, rc, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\nmov.b64 rc, {%6, %7};\n"
+        "fma.rn.f32x2 rd, ra, rb, rc;\nmov.b64 {%0, %1}, rd;\n}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
+// One Kronecker stage T = (A^T Z) B on 32x32 blocks (kron_native / mix8,
+// infer.rs:2322-2460): every output an fma chain over j from zero. Thread t
+// owns row r = t / 8 and columns c0 .. c0 + 3 (c0 = 4 (t % 8)): four
+// independent chains, two per f32x2 fma.
+__device__ __forceinline__ void kron_stage4(const float* z, const float* A, const float* B, float* mt, float* t, int tid) {
+    const int r = tid >> 3, c0 = (tid & 7) * 4;
+    float2 o0 = make_float2(0.f, 0.f), o1 = make_float2(0.f, 0.f);
 #pragma unroll 8
-    for (int j = 0; j < 32; j++) o = __fmaf_rn(A[j * 32 + r], z[j * 32 + cc], o);
-    mt[cc * 33 + r] = o;
+    for (int j = 0; j < 32; j++) {
+        float a = A[j * 32 + r];
+        float4 zz = *(const float4*)(z + j * 32 + c0);
+        o0 = fma2(make_float2(a, a), make_float2(zz.x, zz.y), o0);
+        o1 = fma2(make_float2(a, a), make_float2(zz.z, zz.w), o1);
+    }
+    mt[(c0 + 0) * 33 + r] = o0.x;
+    mt[(c0 + 1) * 33 + r] = o0.y;
+    mt[(c0 + 2) * 33 + r] = o1.x;
+    mt[(c0 + 3) * 33 + r] = o1.y;
     __syncthreads();
-    o = 0.f;
+    o0 = make_float2(0.f, 0.f);
+    o1 = make_float2(0.f, 0.f);
 #pragma unroll 8
-    for (int j = 0; j < 32; j++) o = __fmaf_rn(mt[j * 33 + r], B[j * 32 + cc], o);
-    t[r * 32 + cc] = o;
+    for (int j = 0; j < 32; j++) {
+        float a = mt[j * 33 + r];
+        float4 bb = *(const float4*)(B + j * 32 + c0);
+        o0 = fma2(make_float2(a, a), make_float2(bb.x, bb.y), o0);
+        o1 = fma2(make_float2(a, a), make_float2(bb.z, bb.w), o1);
+    }
+    *(float4*)(t + r * 32 + c0) = make_float4(o0.x, o0.y, o1.x, o1.y);
     __syncthreads();
 }
 
-__global__ void __launch_bounds__(1024) post_block_kernel(LayerW w, int lane_own, const float* o, const float* x1,
-                                                          const float* u, const float* p, const int32_t* perm1,
-                                                          const int32_t* perm2, float* xs) {
+// infer.rs:1564-1606 with mlp_native (1610-1634), cond_weights (1640-1694),
+// perm_fma (689-713) and silu (2463-2496). One CTA of 256 threads per row;
+// the post and residual gates (hpost, Sinkhorn) come from the mHC read.
+__global__ void __launch_bounds__(256) post_block_kernel(LayerW w, const float* o, const float* x1, const float* u,
+                                                         const float* gates, const int32_t* perm1, const int32_t* perm2,
+                                                         float* xs) {
     __shared__ __align__(16) float x2[768];
     __shared__ __align__(16) float h2[768];
     __shared__ __align__(16) float z[1024];
     __shared__ __align__(16) float t[1024];
+    __shared__ __align__(16) float kf[6][1024];
     __shared__ float mt[32 * 33];
     __shared__ float part[32];
     __shared__ float sc[2];
     __shared__ float wk[8];
-    __shared__ float hpost[4];
-    __shared__ float hres[16];
     const int m = blockIdx.x, tid = threadIdx.x;
-    if (tid < 768) x2[tid] = o[(size_t)m * 768 + tid];
+    for (int k = tid; k < 6 * 256; k += 256) {
+        int f = k >> 8, q = k & 255;
+        *(float4*)(&kf[f][q * 4]) = *(const float4*)(w.kron[f] + q * 4);
+    }
+    for (int k = tid; k < 768; k += 256) x2[k] = o[(size_t)m * 768 + k];
     __syncthreads();
     if (tid < 16) part[tid] = dot16_chain(x2, x2, 768, tid);
     __syncthreads();
     if (tid == 0) sc[0] = rinv(dot16_combine(part), 768);
     __syncthreads();
     const float ga = __fdiv_rn(1.0f, __fadd_rn(lexpf(-w.attn_gate), 1.0f));
-    if (tid < 768) {
-        float tt = __fmul_rn(x2[tid], sc[0]);
-        float on = __fmaf_rn(tt, w.post_norm[tid], tt);
-        x2[tid] = __fmaf_rn(on, ga, x1[(size_t)m * 768 + tid]);
+    for (int k = tid; k < 768; k += 256) {
+        float tt = __fmul_rn(x2[k], sc[0]);
+        float on = __fmaf_rn(tt, w.post_norm[k], tt);
+        x2[k] = __fmaf_rn(on, ga, x1[(size_t)m * 768 + k]);
     }
     __syncthreads();
     if (tid < 16) part[tid] = dot16_chain(x2, x2, 768, tid);
     __syncthreads();
     if (tid == 0) sc[1] = rinv(dot16_combine(part), 768);
     __syncthreads();
-    if (tid < 768) {
-        float tt = __fmul_rn(x2[tid], sc[1]);
-        h2[tid] = __fmaf_rn(tt, w.pre_hada[tid], tt);
+    for (int k = tid; k < 768; k += 256) {
+        float tt = __fmul_rn(x2[k], sc[1]);
+        h2[k] = __fmaf_rn(tt, w.pre_hada[k], tt);
     }
     __syncthreads();
-    // conditioning logits: 4 accumulator sets by j % 4 (fma chains over j)
+    // conditioning logits: 4 accumulator sets by j % 4, fma chains over j
     if (tid < 32) {
         const int set = tid >> 3, k = tid & 7;
         float acc = 0.f;
         for (int j = set; j < 768; j += 4) acc = __fmaf_rn(h2[j], w.cond_v[j * 8 + k], acc);
         part[tid] = acc;
     }
+    for (int j = tid; j < 1024; j += 256) z[j] = j < 768 ? __fmul_rn(h2[j], w.d1[j]) : 0.f;
     __syncthreads();
     if (tid == 0) {
         float lg[8], e[8], mx = -INFINITY;
@@ -818,53 +1099,29 @@ __global__ void __launch_bounds__(1024) post_block_kernel(LayerW w, int lane_own
         float inv = __fdiv_rn(1.0f, sum);
         for (int k = 0; k < 8; k++) wk[k] = __fmul_rn(e[k], inv);
     }
-    z[tid] = tid < 768 ? __fmul_rn(h2[tid], w.d1[tid]) : 0.f;
-    __syncthreads();
-    kron_stage(z, w.kron[0], w.kron[1], mt, t, tid);
-    {
+    kron_stage4(z, kf[0], kf[1], mt, t, tid);
+    for (int j = tid; j < 1024; j += 256) {
         float cnd = 1.0f;
 #pragma unroll
-        for (int k = 0; k < 8; k++) cnd = __fmaf_rn(w.cond_u[k * 1024 + tid], wk[k], cnd);
-        float zz = __fmaf_rn(t[perm1[tid]], __fmul_rn(cnd, w.d2[tid]), w.b2[tid]);
-        z[tid] = __fdiv_rn(zz, __fadd_rn(nexp(-zz), 1.0f));
+        for (int k = 0; k < 8; k++) cnd = __fmaf_rn(w.cond_u[k * 1024 + j], wk[k], cnd);
+        float zz = __fmaf_rn(t[perm1[j]], __fmul_rn(cnd, w.d2[j]), w.b2[j]);
+        z[j] = __fdiv_rn(zz, __fadd_rn(nexp(-zz), 1.0f));
     }
     __syncthreads();
-    kron_stage(z, w.kron[2], w.kron[3], mt, t, tid);
-    z[tid] = __fmul_rn(t[perm2[tid]], w.d3[tid]);
+    kron_stage4(z, kf[2], kf[3], mt, t, tid);
+    for (int j = tid; j < 1024; j += 256) z[j] = __fmul_rn(t[perm2[j]], w.d3[j]);
     __syncthreads();
-    kron_stage(z, w.kron[4], w.kron[5], mt, t, tid);
-    if (tid == 0) {
-        const float* pr = p + (size_t)m * 24;
-        for (int j = 0; j < 4; j++) {
-            float off = j == lane_own ? 0.0f : -4.0f;
-            float zz = __fadd_rn(__fadd_rn(__fmul_rn(pr[4 + j], w.a_post), off), w.b_post[j]);
-            hpost[j] = __fdiv_rn(2.0f, __fadd_rn(lexpf(-zz), 1.0f));
-        }
-        float zres[16];
-        for (int k = 0; k < 16; k++) zres[k] = __fmaf_rn(pr[8 + k], w.a_res, w.b_res[k]);
-        double e[16];
-        for (int r = 0; r < 4; r++) {
-            double mx = (double)fmaxf(fmaxf(zres[r * 4], zres[r * 4 + 1]), fmaxf(zres[r * 4 + 2], zres[r * 4 + 3]));
-            for (int cc = 0; cc < 4; cc++) e[r * 4 + cc] = exp(__dsub_rn((double)zres[r * 4 + cc], mx));
-        }
-        for (int it = 0; it < 20; it++) {
-            for (int r = 0; r < 4; r++) {
-                double inv = __ddiv_rn(1.0, __dadd_rn(__dadd_rn(e[r * 4], e[r * 4 + 1]), __dadd_rn(e[r * 4 + 2], e[r * 4 + 3])));
-                for (int cc = 0; cc < 4; cc++) e[r * 4 + cc] = __dmul_rn(e[r * 4 + cc], inv);
-            }
-            for (int cc = 0; cc < 4; cc++) {
-                double inv = __ddiv_rn(1.0, __dadd_rn(__dadd_rn(e[cc], e[4 + cc]), __dadd_rn(e[8 + cc], e[12 + cc])));
-                for (int r = 0; r < 4; r++) e[r * 4 + cc] = __dmul_rn(e[r * 4 + cc], inv);
-            }
-        }
-        for (int k = 0; k < 16; k++) hres[k] = (float)e[k];
-    }
-    __syncthreads();
-    if (tid < 768) {
-        const int ch = tid;
+    kron_stage4(z, kf[4], kf[5], mt, t, tid);
+    const float* gr = gates + (size_t)m * 24;
+    float hpost[4], hres[16];
+#pragma unroll
+    for (int k = 0; k < 4; k++) hpost[k] = gr[k];
+#pragma unroll
+    for (int k = 0; k < 16; k++) hres[k] = gr[4 + k];
+    float* xr = xs + (size_t)m * 3072;
+    for (int ch = tid; ch < 768; ch += 256) {
         float mlp = __fmul_rn(t[ch], w.d4[ch]);
         float y = __fsub_rn(__fadd_rn(x2[ch], mlp), u[(size_t)m * 768 + ch]);
-        float* xr = xs + (size_t)m * 3072;
         float old[4];
 #pragma unroll
         for (int b = 0; b < 4; b++) old[b] = xr[b * 768 + ch];
@@ -878,10 +1135,10 @@ __global__ void __launch_bounds__(1024) post_block_kernel(LayerW w, int lane_own
     }
 }
 
-void launch_post_block(LayerW w, int lane, const float* o, const float* x1, const float* u, const float* p,
-                       const int32_t* perm1, const int32_t* perm2, int M, float* xs, cudaStream_t st) {
+void launch_post_block(LayerW w, const float* o, const float* x1, const float* u, const float* gates, const int32_t* perm1,
+                       const int32_t* perm2, int M, float* xs, cudaStream_t st) {
     COUNT_LAUNCH();
-    post_block_kernel<<<M, 1024, 0, st>>>(w, lane, o, x1, u, p, perm1, perm2, xs);
+    post_block_kernel<<<M, 256, 0, st>>>(w, o, x1, u, gates, perm1, perm2, xs);
 }
 
 // ------------------------------------------------------------ final norm

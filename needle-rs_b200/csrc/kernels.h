@@ -16,6 +16,10 @@ struct DevMat {
     const uint8_t* codes = nullptr;
     const uint16_t* norms = nullptr;
     int out = 0, in_dim = 0, groups = 0;
+    // The same codes expanded through the int8 codebook, [out][groups*128],
+    // each group lane-major (input p = 32a + 8l + b at l*32 + a*8 + b): the
+    // operand the tensor-core kernel streams when many rows share a step.
+    const int8_t* w8 = nullptr;
 };
 
 // One layer's weights on the device (small weights widened to f32, which
@@ -66,7 +70,9 @@ void launch_cq_gemm(DevMat W, const int8_t* act, const float* sx, int M, int T, 
 void launch_engram_gather(DevMat tables, Caches c, int S, int T, int p0, int slots, float* e, cudaStream_t st);
 void launch_engram_vhist(const float* kv, Caches c, int site, int nsites, int S, int T, int p0, cudaStream_t st);
 void launch_engram_conv(const float* taps, Caches c, int site, int nsites, int S, int T, int p0, float* v, cudaStream_t st);
-void launch_mhc_read(LayerW w, int lane, const float* xs, int M, float* u, float* p, cudaStream_t st);
+// u [M][768]; gates [M][24]: the post block's hpost[4] then the Sinkhorn
+// matrix hres[16] (infer.rs:1580-1586), from this layer's gate projections.
+void launch_mhc_read(LayerW w, int lane, const float* xs, int M, float* u, float* gates, cudaStream_t st);
 void launch_input_norm(LayerW w, const float* u, const float* ekv, const float* evals, int M, float* x1, int8_t* act,
                        float* sx, cudaStream_t st);
 void launch_conv_rope_kv(LayerW w, int l, const float* proj, Caches c, int S, int T, int p0, int hist_base, const float* cosr,
@@ -74,8 +80,8 @@ void launch_conv_rope_kv(LayerW w, int l, const float* proj, Caches c, int S, in
 void launch_hist_update(const float* proj, Caches c, int l, int S, int T, int p0, cudaStream_t st);
 void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int S, int T, int p0, int window, float* att,
                       cudaStream_t st);
-void launch_post_block(LayerW w, int lane, const float* o, const float* x1, const float* u, const float* p,
-                       const int32_t* perm1, const int32_t* perm2, int M, float* xs, cudaStream_t st);
+void launch_post_block(LayerW w, const float* o, const float* x1, const float* u, const float* gates, const int32_t* perm1,
+                       const int32_t* perm2, int M, float* xs, cudaStream_t st);
 void launch_final_hidden(const float* xs, const float* final_norm, int S, int T, int all_rows, float* h, cudaStream_t st);
 void launch_rope_rows(const float* table_cos, const float* table_sin, const float* sd, const float* cd, int p0, int T,
                       int recur, float* state, float* cosr, float* sinr, cudaStream_t st);

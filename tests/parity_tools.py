@@ -43,7 +43,6 @@ def first_divergence(gpu_model, oracle_model, ids):
         b.forward(np.asarray(ids, np.int32).reshape(1, t))
         pairs = [
             ("u", b.debug("snap.u"), tr[f"L{l}.u"]),
-            ("p", b.debug("snap.p"), tr[f"L{l}.p"]),
             ("x1", b.debug("snap.x1"), tr[f"L{l}.x1"]),
             ("proj", b.debug("snap.proj"), tr[f"L{l}.proj"]),
             ("q", b.debug("snap.qbuf").reshape(t, 576), tr[f"L{l}.qkv"].reshape(t, 800)[:, :576]),
