@@ -46,6 +46,9 @@ def parse():
     ap.add_argument("--roofline-site", default="auto")
     ap.add_argument("--cpu-baseline", type=int, default=1, help="time the oracle on rank 0 (N=1 only)")
     ap.add_argument("--secondary", type=int, default=1, help="also time batch-1 decode and 256x700 prefill (N=1)")
+    ap.add_argument("--profile", action="store_true",
+                    help="untimed case for ncu: one batch of --seqs sequences, the 118-token prefill, then --warmup "
+                         "decode steps")
     return ap.parse_args()
 
 
@@ -289,6 +292,14 @@ def main():
     data = archive_bytes()
     model = nb.Model(data, device=local)
     V = model.out_rows
+    if args.profile:
+        prompts, masks = make_inputs(rank, S, W, V)
+        b = model.batch(S, PROMPT + W + 1)
+        b.forward(prompts, nb.OUT_LAST_LOGITS, out=np.zeros((S, 1, V), np.float32))
+        for k in range(W):
+            b.step(masks[k])
+        torch.cuda.synchronize()
+        return
     prompts, masks = make_inputs(rank, S, total_steps, V)
     sites = ["qkvg", "out", "lm_head", "engram_kv", "attention", "post", "mhc", "conv", "norm"]
     cap = PROMPT + total_steps + len(sites) + 2

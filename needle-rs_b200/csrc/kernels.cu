@@ -5,6 +5,7 @@
 // row of a step at once. Integer sums are exact, so their order is free; every
 // float op follows the reference's order, rounding and fusion.
 
+#include <algorithm>
 #include <atomic>
 
 #include "kernels.h"
@@ -429,7 +430,6 @@ void launch_cq_gemm(DevMat W, const int8_t* act, const float* sx, int M, int T, 
 template <bool DECODE>
 __global__ void cq_mma_kernel(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y, int ldy, int col0);
 
-struct AttSmem;
 extern const size_t ATT_SMEM;
 __global__ void attention_kernel(const float* qbuf, const float* proj, Caches c, int l, int T, int p0, int window, float* att);
 
@@ -807,190 +807,208 @@ __device__ __forceinline__ void key_chunks_dev(int n, bool nested, int* count, i
     *count = ch > 0 ? (n + ch - 1) / ch : 0;
 }
 
-// One CTA per (row, kv head) serves the kv head's 6 query heads, so each
-// key and value row of the chunk is read from HBM once: keys to shared
-// memory as stored, values transposed [dim][key] so four keys' bytes of one
-// value dimension form one word for the digit dot products.
-constexpr int ATT_HEADS = 6, ATT_VT_LD = ATT_MAXCHUNK + 4;
+// One CTA per (row, kv head) serves the kv head's 6 query heads: the chunk's
+// key rows (as stored) and value rows (transposed [dim][key], so four keys'
+// bytes of one value dimension form a word for the digit dot products) are
+// loaded once into shared memory; then warp h runs head h through scores,
+// max, numerators, the fixed-order sum, digits, P.V, merge and gate with no
+// block-wide barrier. Per-chunk parts live in dynamic shared memory sized
+// for the longest key list of the launch.
+constexpr int ATT_HEADS = 6, ATT_VT_LD = ATT_MAXCHUNK + 4, ATT_THREADS = ATT_HEADS * 32;
 struct AttSmem {
     int8_t k[ATT_MAXCHUNK][48];
     int8_t vt[64][ATT_VT_LD];
     float ks[ATT_MAXCHUNK], vs[ATT_MAXCHUNK];
     float s[ATT_HEADS][ATT_MAXCHUNK];
-    int8_t dh[ATT_HEADS][ATT_MAXCHUNK], dmid[ATT_HEADS][ATT_MAXCHUNK], dl[ATT_HEADS][ATT_MAXCHUNK];
-    float po[ATT_HEADS][ATT_MAXPARTS][64];
-    float pm[ATT_HEADS][ATT_MAXPARTS], psum[ATT_HEADS][ATT_MAXPARTS];
+    int8_t dig[ATT_HEADS][3][ATT_MAXCHUNK];
     int8_t q8[ATT_HEADS][48];
-    float qs[ATT_HEADS], mx[ATT_HEADS], wmax[ATT_HEADS];
-    float chains[ATT_HEADS][8];
+    // followed by parts: [ATT_HEADS][count][66] floats (m, sum, o[64])
 };
 
-__global__ void __launch_bounds__(256) attention_kernel(const float* qbuf, const float* proj, Caches c, int l, int T, int p0,
-                                                        int window, float* att) {
+__global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbuf, const float* proj, Caches c, int l, int T,
+                                                                int p0, int window, float* att) {
     extern __shared__ __align__(16) int8_t att_raw[];
     AttSmem& sm = *reinterpret_cast<AttSmem*>(att_raw);
-    const int m = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int m = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x, lane = tid & 31, h = tid >> 5;
     const int s = m / T, i = m % T, pos = p0 + i;
     const bool nested = T > 1;
     const int lo = window > 0 ? max(0, pos + 1 - window) : 0;
     const int n = pos + 1 - lo;
-    if (warp < ATT_HEADS) {
-        // quant_i8 of the head's query, scale folded with 1/sqrt(48) (infer.rs:1885)
-        const float* q = qbuf + (size_t)m * 576 + (kvh * ATT_HEADS + warp) * 48;
+    int count, chunk;
+    key_chunks_dev(n, nested, &count, &chunk);
+    float* parts = reinterpret_cast<float*>(att_raw + ((sizeof(AttSmem) + 15) & ~(size_t)15)) + (size_t)h * count * 66;
+    const int hh = kvh * ATT_HEADS + h;
+    float qs;
+    {
+        // quant_i8 of this head's query, scale folded with 1/sqrt(48) (infer.rs:1885)
+        const float* q = qbuf + (size_t)m * 576 + hh * 48;
         float x0 = q[lane], x1 = lane < 16 ? q[32 + lane] : 0.f;
         float a = warp_max(fmaxf(fabsf(x0), fabsf(x1)));
         float sc = a > 0.f ? __fmul_rn(a, ND_K127) : 1.0f;
         float inv = __fdiv_rn(1.0f, sc);
-        sm.q8[warp][lane] = q8_round(x0, inv);
-        if (lane < 16) sm.q8[warp][32 + lane] = q8_round(x1, inv);
-        if (lane == 0) sm.qs[warp] = __fmul_rn(sc, ND_INV_SQRT_QK);
+        sm.q8[h][lane] = q8_round(x0, inv);
+        if (lane < 16) sm.q8[h][32 + lane] = q8_round(x1, inv);
+        qs = __fmul_rn(sc, ND_INV_SQRT_QK);
     }
-    int count, chunk;
-    key_chunks_dev(n, nested, &count, &chunk);
     const size_t kvrow = (((size_t)s * c.L + l) * 2 + kvh) * c.cap;
     const int8_t* k8 = c.k8 + kvrow * 48;
     const int8_t* v8 = c.v8 + kvrow * 64;
+    float* srow = sm.s[h];
     for (int ci = 0; ci < count; ci++) {
         const int c0 = ci * chunk, len = min(chunk, n - c0), blocked = len / 4 * 4, len4 = (len + 3) / 4 * 4;
         const int base = lo + c0;
-        __syncthreads();  // the previous chunk's readers are done
-        for (int idx = tid; idx < len * 3; idx += 256) {
+        __syncthreads();  // every warp is done with the previous chunk
+        for (int idx = tid; idx < len * 3; idx += ATT_THREADS) {
             int k = idx / 3, part = idx % 3;
             *(int4*)(&sm.k[k][part * 16]) = *(const int4*)(k8 + (size_t)(base + k) * 48 + part * 16);
         }
-        for (int idx = tid; idx < len * 4; idx += 256) {
+        for (int idx = tid; idx < len * 4; idx += ATT_THREADS) {
             int k = idx >> 2, part = idx & 3;
             int4 v = *(const int4*)(v8 + (size_t)(base + k) * 64 + part * 16);
             const int8_t* b = (const int8_t*)&v;
 #pragma unroll
             for (int e = 0; e < 16; e++) sm.vt[part * 16 + e][k] = b[e];
         }
-        for (int k = tid; k < len; k += 256) {
+        for (int k = tid; k < len; k += ATT_THREADS) {
             sm.ks[k] = c.ks[kvrow + base + k];
             sm.vs[k] = c.vs[kvrow + base + k];
         }
         __syncthreads();
         // scores: (ks * dot) * qs in whole 4-blocks, (ks * qs) * dot after
-        for (int idx = tid; idx < ATT_HEADS * len; idx += 256) {
-            int h = idx / len, k = idx % len;
+        const int* qr = (const int*)sm.q8[h];
+        float mx = -INFINITY;
+        for (int k = lane; k < len; k += 32) {
             const int* kr = (const int*)sm.k[k];
-            const int* qr = (const int*)sm.q8[h];
             int dot = 0;
 #pragma unroll
             for (int e = 0; e < 12; e++) dot = __dp4a(qr[e], kr[e], dot);
-            float qs = sm.qs[h], ksv = sm.ks[k];
-            sm.s[h][k] = k < blocked ? __fmul_rn(__fmul_rn(ksv, (float)dot), qs) : __fmul_rn(__fmul_rn(ksv, qs), (float)dot);
+            float ksv = sm.ks[k];
+            float sv = k < blocked ? __fmul_rn(__fmul_rn(ksv, (float)dot), qs) : __fmul_rn(__fmul_rn(ksv, qs), (float)dot);
+            srow[k] = sv;
+            mx = fmaxf(mx, sv);
         }
-        __syncthreads();
-        if (warp < ATT_HEADS) {
-            float mx = -INFINITY;
-            for (int k = lane; k < len; k += 32) mx = fmaxf(mx, sm.s[warp][k]);
-            mx = warp_max(mx);
-            if (lane == 0) sm.mx[warp] = mx;
-        }
-        __syncthreads();
+        mx = warp_max(mx);
         // numerators: the inline exp on whole 4-blocks, libm exp for the rest
-        for (int idx = tid; idx < ATT_HEADS * len; idx += 256) {
-            int h = idx / len, k = idx % len;
-            float dlt = __fsub_rn(sm.s[h][k], sm.mx[h]);
-            sm.s[h][k] = k < blocked ? nexp(dlt) : lexpf(dlt);
+        for (int k = lane; k < len; k += 32) {
+            float dlt = __fsub_rn(srow[k], mx);
+            srow[k] = k < blocked ? nexp(dlt) : lexpf(dlt);
         }
-        __syncthreads();
-        // chunk_exp's sum order: chain j < 4 adds the first halves of the
-        // 8-blocks and the trailing 4-block, chain j >= 4 the second halves
-        if (tid < ATT_HEADS * 8) {
-            const int h = tid >> 3, j = tid & 7, n8 = len / 8 * 8;
-            float a = 0.f;
-            for (int q = 0; q < n8; q += 8) a = __fadd_rn(a, sm.s[h][q + j]);
-            if (j < 4 && blocked > n8) a = __fadd_rn(a, sm.s[h][n8 + j]);
-            sm.chains[h][j] = a;
+        __syncwarp();
+        // chunk_exp's sum order (infer.rs:2279-2317): chain j < 4 adds the
+        // first halves of the 8-blocks then the trailing 4-block, chain
+        // j >= 4 the second halves; t_k = a_k + b_k; ((t0 + t1) + (t2 + t3)),
+        // then the last 1-3 numerators one at a time.
+        float a = 0.f;
+        if (lane < 8) {
+            const int n8 = len / 8 * 8;
+            for (int q = 0; q < n8; q += 8) a = __fadd_rn(a, srow[q + lane]);
+            if (lane < 4 && blocked > n8) a = __fadd_rn(a, srow[n8 + lane]);
         }
-        __syncthreads();
-        if (tid < ATT_HEADS) {
-            const int h = tid;
-            float t[4];
-            for (int k = 0; k < 4; k++) t[k] = __fadd_rn(sm.chains[h][k], sm.chains[h][4 + k]);
-            float sum = __fadd_rn(__fadd_rn(t[0], t[1]), __fadd_rn(t[2], t[3]));
+        float tk = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 4));  // lanes 0-3: a_k + b_k
+        float t1 = __shfl_sync(0xffffffffu, tk, 1), t2 = __shfl_sync(0xffffffffu, tk, 2), t3 = __shfl_sync(0xffffffffu, tk, 3);
+        float sum = __fadd_rn(__fadd_rn(tk, t1), __fadd_rn(t2, t3));
+        {
             int ii = blocked;
             if (len - ii >= 2) {
-                sum = __fadd_rn(__fadd_rn(sm.s[h][ii], sum), sm.s[h][ii + 1]);
+                sum = __fadd_rn(__fadd_rn(srow[ii], sum), srow[ii + 1]);
                 ii += 2;
             }
-            if (len - ii == 1) sum = __fadd_rn(sum, sm.s[h][ii]);
-            sm.psum[h][ci] = sum;
-            sm.pm[h][ci] = sm.mx[h];
+            if (len - ii == 1) sum = __fadd_rn(sum, srow[ii]);
         }
-        __syncthreads();
-        // weights times the value scales and their max (from zero)
-        for (int idx = tid; idx < ATT_HEADS * len; idx += 256) {
-            int h = idx / len, k = idx % len;
-            sm.s[h][k] = __fmul_rn(sm.s[h][k], sm.vs[k]);
+        sum = __shfl_sync(0xffffffffu, sum, 0);
+        // weights times the value scales, their max from zero, 21-bit digits
+        float wm = 0.f;
+        for (int k = lane; k < len; k += 32) {
+            float wv = __fmul_rn(srow[k], sm.vs[k]);
+            srow[k] = wv;
+            wm = fmaxf(wm, wv);
         }
-        __syncthreads();
-        if (warp < ATT_HEADS) {
-            float wm = 0.f;
-            for (int k = lane; k < len; k += 32) wm = fmaxf(wm, sm.s[warp][k]);
-            wm = warp_max(wm);
-            if (lane == 0) sm.wmax[warp] = wm;
+        wm = warp_max(wm);
+        const float qw = __fdiv_rn(ND_Q21, wm);
+        for (int k = lane; k < len4; k += 32) {
+            int wq = k < len ? (int)roundf(__fmul_rn(srow[k], qw)) : 0;
+            sm.dig[h][0][k] = (int8_t)(wq >> 14);
+            sm.dig[h][1][k] = (int8_t)((wq >> 7) & 127);
+            sm.dig[h][2][k] = (int8_t)(wq & 127);
         }
-        __syncthreads();
-        // 21-bit digits of round(w * Q21 / wmax), zero past the chunk's end
-        for (int idx = tid; idx < ATT_HEADS * len4; idx += 256) {
-            int h = idx / len4, k = idx % len4;
-            int wq = 0;
-            if (k < len) wq = (int)roundf(__fmul_rn(sm.s[h][k], __fdiv_rn(ND_Q21, sm.wmax[h])));
-            sm.dh[h][k] = (int8_t)(wq >> 14);
-            sm.dmid[h][k] = (int8_t)((wq >> 7) & 127);
-            sm.dl[h][k] = (int8_t)(wq & 127);
+        __syncwarp();
+        // P.V: three exact integer dots per value dimension (lane, lane + 32)
+        const int* dh = (const int*)sm.dig[h][0];
+        const int* dmid = (const int*)sm.dig[h][1];
+        const int* dl = (const int*)sm.dig[h][2];
+        const int* v0 = (const int*)sm.vt[lane];
+        const int* v1 = (const int*)sm.vt[lane + 32];
+        int sh0 = 0, sm0 = 0, sl0 = 0, sh1 = 0, sm1 = 0, sl1 = 0;
+        for (int w = 0; w < len4 / 4; w++) {
+            int a0 = dh[w], a1 = dmid[w], a2 = dl[w], x0 = v0[w], x1 = v1[w];
+            sh0 = __dp4a(a0, x0, sh0);
+            sm0 = __dp4a(a1, x0, sm0);
+            sl0 = __dp4a(a2, x0, sl0);
+            sh1 = __dp4a(a0, x1, sh1);
+            sm1 = __dp4a(a1, x1, sm1);
+            sl1 = __dp4a(a2, x1, sl1);
         }
-        __syncthreads();
-        // P.V: three exact integer dots per (head, value dimension)
-        for (int idx = tid; idx < ATT_HEADS * 64; idx += 256) {
-            const int h = idx >> 6, dm = idx & 63;
-            const int* vr = (const int*)sm.vt[dm];
-            const int* ph = (const int*)sm.dh[h];
-            const int* pmid = (const int*)sm.dmid[h];
-            const int* pl = (const int*)sm.dl[h];
-            int sh = 0, smd = 0, sl = 0;
-            for (int w = 0; w < len4 / 4; w++) {
-                int v = vr[w];
-                sh = __dp4a(ph[w], v, sh);
-                smd = __dp4a(pmid[w], v, smd);
-                sl = __dp4a(pl[w], v, sl);
-            }
-            float cw = __fmul_rn(sm.wmax[h], ND_C21);
-            sm.po[h][ci][dm] = __fmul_rn(__fmaf_rn(16384.f, (float)sh, __fmaf_rn(128.f, (float)smd, (float)sl)), cw);
+        const float cw = __fmul_rn(wm, ND_C21);
+        float* pr = parts + ci * 66;
+        pr[2 + lane] = __fmul_rn(__fmaf_rn(16384.f, (float)sh0, __fmaf_rn(128.f, (float)sm0, (float)sl0)), cw);
+        pr[34 + lane] = __fmul_rn(__fmaf_rn(16384.f, (float)sh1, __fmaf_rn(128.f, (float)sm1, (float)sl1)), cw);
+        if (lane == 0) {
+            pr[0] = mx;
+            pr[1] = sum;
         }
     }
-    __syncthreads();
-    for (int idx = tid; idx < ATT_HEADS * 64; idx += 256) {
-        const int h = idx >> 6, dm = idx & 63;
-        float out;
-        if (count == 1) {
-            out = __fmul_rn(sm.po[h][0][dm], __fdiv_rn(1.0f, sm.psum[h][0]));
-        } else {
-            float big = -1e30f;
-            for (int ci = 0; ci < count; ci++) big = fmaxf(big, sm.pm[h][ci]);
-            float acc = 0.f, total = 0.f;
-            for (int ci = 0; ci < count; ci++) {
-                float wv = lexpf(__fsub_rn(sm.pm[h][ci], big));
-                acc = __fmaf_rn(sm.po[h][ci][dm], wv, acc);
-                total = __fmaf_rn(wv, sm.psum[h][ci], total);
-            }
-            out = __fmul_rn(acc, __fdiv_rn(1.0f, total));
+    __syncwarp();
+    // merge_parts (infer.rs:2143-2166), then the gate (1548-1552)
+    float out0, out1;
+    if (count == 1) {
+        float inv = __fdiv_rn(1.0f, parts[1]);
+        out0 = __fmul_rn(parts[2 + lane], inv);
+        out1 = __fmul_rn(parts[34 + lane], inv);
+    } else {
+        float big = -1e30f;
+        for (int ci = 0; ci < count; ci++) big = fmaxf(big, parts[ci * 66]);
+        float a0 = 0.f, a1 = 0.f, total = 0.f;
+        for (int ci = 0; ci < count; ci++) {
+            const float* pr = parts + ci * 66;
+            float wv = lexpf(__fsub_rn(pr[0], big));
+            a0 = __fmaf_rn(pr[2 + lane], wv, a0);
+            a1 = __fmaf_rn(pr[34 + lane], wv, a1);
+            total = __fmaf_rn(wv, pr[1], total);
         }
-        const int hh = kvh * ATT_HEADS + h;
-        float g = proj[(size_t)m * 1568 + 800 + hh * 64 + dm];
-        att[(size_t)m * 768 + hh * 64 + dm] = __fdiv_rn(out, __fadd_rn(nexp(-g), 1.0f));
+        float inv = __fdiv_rn(1.0f, total);
+        out0 = __fmul_rn(a0, inv);
+        out1 = __fmul_rn(a1, inv);
     }
+    const float* g = proj + (size_t)m * 1568 + 800 + hh * 64;
+    float* o = att + (size_t)m * 768 + hh * 64;
+    o[lane] = __fdiv_rn(out0, __fadd_rn(nexp(-g[lane]), 1.0f));
+    o[lane + 32] = __fdiv_rn(out1, __fadd_rn(nexp(-g[lane + 32]), 1.0f));
 }
 
-extern const size_t ATT_SMEM = sizeof(AttSmem);
+[[maybe_unused]] static int host_key_chunks(int n, bool nested) {
+    int k = nested ? 1 : 4;
+    int c = (n + 255) / 256;
+    if (k * 64 <= n && c < k) c = k;
+    int cm = c > 1 ? c : 1;
+    int ch = ((n + cm - 1) / cm + 15) / 16 * 16;
+    return ch > 0 ? (n + ch - 1) / ch : 0;
+}
+
+extern const size_t ATT_SMEM_BASE = (sizeof(AttSmem) + 15) & ~(size_t)15;
+extern const size_t ATT_SMEM = ATT_SMEM_BASE + (size_t)ATT_HEADS * ATT_MAXPARTS * 66 * 4;
 
 void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int S, int T, int p0, int window, float* att,
                       cudaStream_t st) {
     COUNT_LAUNCH();
-    attention_kernel<<<dim3(S * T, 2), 256, ATT_SMEM, st>>>(qbuf, proj, c, l, T, p0, window, att);
+    // key_chunks gives at most c = max(ceil(n / 256), k if n >= 64 k) chunks,
+    // and the launch's longest key list is its last row's
+    int nmax = p0 + T;
+    if (window > 0 && window < nmax) nmax = window;
+    int most = std::max(1, (nmax + 255) / 256);
+    if (T == 1 && nmax >= 256) most = std::max(most, 4);
+    most = std::min(most, ATT_MAXPARTS);
+    size_t smem = ATT_SMEM_BASE + (size_t)ATT_HEADS * most * 66 * 4;
+    attention_kernel<<<dim3(S * T, 2), ATT_THREADS, smem, st>>>(qbuf, proj, c, l, T, p0, window, att);
 }
 
 // ------------------------------------------------------------ post block
@@ -1083,21 +1101,26 @@ __global__ void __launch_bounds__(256) post_block_kernel(LayerW w, const float* 
     if (tid < 32) {
         const int set = tid >> 3, k = tid & 7;
         float acc = 0.f;
+#pragma unroll 16
         for (int j = set; j < 768; j += 4) acc = __fmaf_rn(h2[j], w.cond_v[j * 8 + k], acc);
         part[tid] = acc;
     }
     for (int j = tid; j < 1024; j += 256) z[j] = j < 768 ? __fmul_rn(h2[j], w.d1[j]) : 0.f;
     __syncthreads();
-    if (tid == 0) {
-        float lg[8], e[8], mx = -INFINITY;
-        for (int k = 0; k < 8; k++) {
-            lg[k] = __fadd_rn(__fadd_rn(__fadd_rn(part[16 + k], part[24 + k]), part[8 + k]), part[k]);
-            mx = fmaxf(mx, lg[k]);
-        }
-        for (int k = 0; k < 8; k++) e[k] = lexpf(__fsub_rn(lg[k], mx));
-        float sum = __fadd_rn(e[7], __fadd_rn(__fadd_rn(e[6], __fadd_rn(e[5], e[4])), __fadd_rn(__fadd_rn(e[3], e[2]), __fadd_rn(e[1], e[0]))));
-        float inv = __fdiv_rn(1.0f, sum);
-        for (int k = 0; k < 8; k++) wk[k] = __fmul_rn(e[k], inv);
+    if (tid < 32) {
+        // logits ((C + D) + B) + A, max, one libm exp per lane, the engine's
+        // sum tree e7 + ((e6 + (e5 + e4)) + ((e3 + e2) + (e1 + e0)))
+        const int k = tid & 7;
+        float lg = __fadd_rn(__fadd_rn(__fadd_rn(part[16 + k], part[24 + k]), part[8 + k]), part[k]);
+        float mx = lg;
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float e = lexpf(__fsub_rn(lg, mx));
+        float ev[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) ev[q] = __shfl_sync(0xffffffffu, e, q);
+        float sum = __fadd_rn(ev[7], __fadd_rn(__fadd_rn(ev[6], __fadd_rn(ev[5], ev[4])), __fadd_rn(__fadd_rn(ev[3], ev[2]), __fadd_rn(ev[1], ev[0]))));
+        if (tid < 8) wk[k] = __fmul_rn(e, __fdiv_rn(1.0f, sum));
     }
     kron_stage4(z, kf[0], kf[1], mt, t, tid);
     for (int j = tid; j < 1024; j += 256) {
