@@ -157,11 +157,10 @@ def site_algorithmic(site, S, n_keys):
     if site == "post":
         return S * (768 * 5 + 3072 * 2 + 24) * 4, "bytes", "hbm"
     if site == "mhc":
-        return S * (3072 + 768 + 24) * 4 + 24 * 3072, "bytes", "hbm"
+        # read xs; write u, gates, x1 and the A8 row (engram-site reads aside)
+        return S * (3072 + 768 + 24 + 768 + 6) * 4 + S * 768 + 24 * 3072, "bytes", "hbm"
     if site == "conv":
         return S * (1568 + 576) * 4 + S * 2 * (48 + 64 + 8), "bytes", "hbm"
-    if site == "norm":
-        return S * (768 * 2 + 768 + 6 * 4) * 4, "bytes", "hbm"
     raise KeyError(site)
 
 
@@ -301,7 +300,7 @@ def main():
         torch.cuda.synchronize()
         return
     prompts, masks = make_inputs(rank, S, total_steps, V)
-    sites = ["qkvg", "out", "lm_head", "engram_kv", "attention", "post", "mhc", "conv", "norm"]
+    sites = ["qkvg", "out", "lm_head", "engram_kv", "attention", "post", "mhc", "conv"]
     cap = PROMPT + total_steps + len(sites) + 2
 
     # --- device-resident run (value)

@@ -118,9 +118,8 @@ enum {
     ND_SITE_ENGRAM_KV = 4, /* engram key|value projection */
     ND_SITE_ATTENTION = 5, /* int8 KV attention + gate */
     ND_SITE_POST = 6,      /* post block: norms, Hadamard MLP, Sinkhorn, mHC write */
-    ND_SITE_MHC = 7,       /* mHC read */
-    ND_SITE_CONV = 8,      /* conv taps, head norm, RoPE, int8 KV write */
-    ND_SITE_NORM = 9       /* engram gate, input norm, A8 */
+    ND_SITE_MHC = 7,       /* mHC read, engram gate, input norm, A8 */
+    ND_SITE_CONV = 8       /* conv taps, head norm, RoPE, int8 KV write */
 };
 int nd_batch_time_site(nd_batch* b, int site);
 int nd_batch_site_time(nd_batch* b, double* total_ms, int* launches);

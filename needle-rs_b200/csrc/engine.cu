@@ -337,6 +337,13 @@ static Model* load_model(const uint8_t* bytes, size_t n, int device) {
 
 // ----------------------------------------------------------------- batch
 
+// A captured decode step: argmax under the mask, then the one-token forward.
+struct StepGraph {
+    cudaGraphExec_t exec = nullptr;
+    long long kernels = 0;  // kernels one replay launches
+    int hist_base = 0;      // the conv-history start baked into the capture
+};
+
 struct Batch {
     Model* m = nullptr;
     int S = 0, cap = 0, Mmax = 0;
@@ -353,11 +360,14 @@ struct Batch {
     int8_t* act;
     float* sx;
     int32_t *ids, *next;
+    int32_t* d_len;  // device copy of len (Caches::len)
     uint8_t* masks;
     size_t logits_cap = 0;
     std::map<std::string, std::pair<float*, size_t>> snaps;
     int last_rows = 0, last_T = 0;
     int time_site = 0;                 // launch site timed with events (ND_SITE_*)
+    bool graphs = true;                // replay decode steps as CUDA graphs (NEEDLE_GRAPHS=0 turns off)
+    StepGraph graph[2];                // without / with a mask
     std::vector<cudaEvent_t> evs;
     size_t ev_used = 0;
 
@@ -376,6 +386,8 @@ struct Batch {
         if (logits) cudaFree(logits);
         for (auto& kv : snaps) cudaFree(kv.second.first);
         for (auto e : evs) cudaEventDestroy(e);
+        for (auto& g : graph)
+            if (g.exec) cudaGraphExecDestroy(g.exec);
         if (st) cudaStreamDestroy(st);
     }
 };
@@ -392,6 +404,7 @@ static Batch* batch_new(Model* m, int S, int max_len) {
     b.cap = max_len;
     b.Mmax = S * 32;
     CK(cudaStreamCreateWithFlags(&b.st, cudaStreamNonBlocking));
+    if (const char* g = getenv("NEEDLE_GRAPHS")) b.graphs = atoi(g) != 0;
     const int L = c.L, nsites = (int)c.sites.size();
     const size_t M = b.Mmax;
     b.c.S = S;
@@ -405,6 +418,8 @@ static Batch* batch_new(Model* m, int S, int max_len) {
     b.c.ev8 = b.alloc<int8_t>((size_t)S * std::max(nsites, 1) * ENG_RING * 768);
     b.c.evs = b.alloc<float>((size_t)S * std::max(nsites, 1) * ENG_RING * 24);
     b.c.tokens = b.alloc<int32_t>((size_t)S * max_len);
+    b.d_len = b.alloc<int32_t>(1);
+    b.c.len = b.d_len;
     b.xs = b.alloc<float>(M * 3072);
     b.u = b.alloc<float>(M * 768);
     b.p = b.alloc<float>(M * 24);
@@ -471,7 +486,7 @@ static int chunk(Batch& b, const int32_t* ids, int T, int outputs) {
     if (p0 + T > b.cap) throw std::runtime_error("sequence exceeds the batch's max_len");
     launch_write_tokens(ids, S, T, p0, b.c, st);
     // infer.rs:1720: the recurrence serves one token right after the newest
-    launch_rope_rows(m.rope_cos, m.rope_sin, m.sd, m.cd, p0, T, (T == 1 && b.rope_valid) ? 1 : 0, b.rope_state, b.cosr,
+    launch_rope_rows(m.rope_cos, m.rope_sin, m.sd, m.cd, b.d_len, T, (T == 1 && b.rope_valid) ? 1 : 0, b.rope_state, b.cosr,
                      b.sinr, st);
     launch_embed(m.embedding, ids, M, b.xs, st);
     // infer.rs:1244-1328
@@ -489,23 +504,18 @@ static int chunk(Batch& b, const int32_t* ids, int T, int outputs) {
         const LayerW& w = m.layers[l];
         const int lane = l % 4, site = m.site_of_layer[l];
         tick(b, ND_SITE_MHC);
-        launch_mhc_read(w, lane, b.xs, M, b.u, b.p, st);
+        launch_mhc_read(w, lane, b.xs, M, b.u, b.p, site >= 0 ? b.ekv + (size_t)site * b.Mmax * 1536 : nullptr,
+                        site >= 0 ? b.evals + (size_t)site * b.Mmax * 768 : nullptr, b.x1, b.act, b.sx, st);
         tick(b, ND_SITE_MHC);
-        tick(b, ND_SITE_NORM);
-        launch_input_norm(w, b.u, site >= 0 ? b.ekv + (size_t)site * b.Mmax * 1536 : nullptr,
-                          site >= 0 ? b.evals + (size_t)site * b.Mmax * 768 : nullptr, M, b.x1, b.act, b.sx, st);
-        tick(b, ND_SITE_NORM);
         tick(b, ND_SITE_QKVG);
         launch_cq_gemm(w.qkvg, b.act, b.sx, M, T, b.proj, 1568, 0, st);
         tick(b, ND_SITE_QKVG);
         tick(b, ND_SITE_CONV);
         launch_conv_rope_kv(w, l, b.proj, b.c, S, T, p0, b.hist_base, b.cosr, b.sinr, b.qbuf, st);
         tick(b, ND_SITE_CONV);
-        launch_hist_update(b.proj, b.c, l, S, T, p0, st);
         tick(b, ND_SITE_ATTENTION);
-        launch_attention(b.qbuf, b.proj, b.c, l, S, T, p0, c.window(l), b.att, st);
+        launch_attention(b.qbuf, b.proj, b.c, l, S, T, p0, c.window(l), b.att, b.act, b.sx, st);
         tick(b, ND_SITE_ATTENTION);
-        launch_prep_act(b.att, 768, 768, M, b.act, b.sx, st);
         tick(b, ND_SITE_OUT);
         launch_cq_gemm(w.out, b.act, b.sx, M, T, b.o, 768, 0, st);
         tick(b, ND_SITE_OUT);
@@ -523,6 +533,7 @@ static int chunk(Batch& b, const int32_t* ids, int T, int outputs) {
         tick(b, ND_SITE_POST);
         if (l == b.debug_layer) snap(b, "snap.xs", b.xs, (size_t)M * 3072);
     }
+    launch_advance_len(b.d_len, T, st);
     b.len += T;
     b.rope_valid = true;
     b.last_T = T;
@@ -586,6 +597,7 @@ using namespace nd;
 struct nd_model {
     std::unique_ptr<Model> m;
 };
+
 struct nd_batch {
     std::unique_ptr<Batch> b;
     std::vector<int32_t> host_ids;
@@ -678,11 +690,54 @@ int nd_batch_step(nd_batch* bh, const unsigned char* allow_bits, int* next_ids, 
             CK(cudaMemcpyAsync(b.masks, allow_bits, (size_t)b.S * mb, cudaMemcpyHostToDevice, b.st));
             allow = b.masks;
         }
-        launch_masked_argmax(b.logits, b.S, c.out_rows(), allow, b.next, b.st);
+        if (allow_bits && dev) {
+            CK(cudaMemcpyAsync(b.masks, allow_bits, (size_t)b.S * mb, cudaMemcpyDeviceToDevice, b.st));
+            allow = b.masks;
+        }
+        // The step (argmax, then one decode forward) replays as a CUDA graph
+        // once captured: every kernel reads its position on the device.
+        const bool graph_ok = b.graphs && b.rope_valid && b.debug_layer < 0 && b.time_site == 0;
+        if (graph_ok) {
+            StepGraph& g = b.graph[allow ? 1 : 0];
+            if (g.exec && g.hist_base != b.hist_base) {
+                cudaGraphExecDestroy(g.exec);
+                g.exec = nullptr;
+            }
+            if (!g.exec) {
+                const long long k0 = launch_count();
+                cudaGraph_t graph = nullptr;
+                CK(cudaStreamBeginCapture(b.st, cudaStreamCaptureModeThreadLocal));
+                try {
+                    launch_masked_argmax(b.logits, b.S, c.out_rows(), allow, b.next, b.st);
+                    forward(b, b.next, 1, ND_OUT_LAST_LOGITS);  // advances the host state once
+                } catch (...) {
+                    cudaStreamEndCapture(b.st, &graph);
+                    if (graph) cudaGraphDestroy(graph);
+                    throw;
+                }
+                CK(cudaStreamEndCapture(b.st, &graph));
+                cudaError_t ie = cudaGraphInstantiate(&g.exec, graph, 0);
+                cudaGraphDestroy(graph);
+                CK(ie);
+                g.kernels = launch_count() - k0;
+                g.hist_base = b.hist_base;
+                CK(cudaGraphLaunch(g.exec, b.st));
+            } else {
+                CK(cudaGraphLaunch(g.exec, b.st));
+                add_launches(g.kernels);
+                b.len += 1;
+                b.last_T = 1;
+                b.last_rows = b.S;
+                b.have_logits = true;
+                b.logits_rows = b.S;
+            }
+        } else {
+            launch_masked_argmax(b.logits, b.S, c.out_rows(), allow, b.next, b.st);
+            forward(b, b.next, 1, ND_OUT_LAST_LOGITS);
+        }
         if (next_ids)
             CK(cudaMemcpyAsync(next_ids, b.next, (size_t)b.S * sizeof(int32_t),
                                dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, b.st));
-        forward(b, b.next, 1, ND_OUT_LAST_LOGITS);
         if (!dev) CK(cudaStreamSynchronize(b.st));
         return 0;
     } catch (std::exception& e) {

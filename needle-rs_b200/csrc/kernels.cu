@@ -15,9 +15,10 @@ namespace nd {
 
 static std::atomic<long long> g_launches{0};
 long long launch_count() { return g_launches.load(); }
+void add_launches(long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 #define COUNT_LAUNCH() g_launches.fetch_add(1, std::memory_order_relaxed)
 
-__constant__ int8_t c_vals[16];   // code -> int8 codebook value (qlinear.rs:244-265)
+__constant__ __align__(16) int8_t c_vals[16];   // code -> int8 codebook value (qlinear.rs:244-265)
 __constant__ float c_fvals[16];   // code -> f32 codebook value
 __constant__ float c_cbs;         // int8 codebook scale
 __constant__ float c_hs128;       // (float)(1/sqrt(128)), quant.rs:71-73
@@ -37,7 +38,8 @@ static inline int cdiv(int a, int b) { return (a + b - 1) / b; }
 
 // --------------------------------------------------------------- tokens
 
-__global__ void write_tokens_kernel(const int32_t* ids, int S, int T, int p0, int32_t* tokens, int cap) {
+__global__ void write_tokens_kernel(const int32_t* ids, int S, int T, const int32_t* p0p, int32_t* tokens, int cap) {
+    const int p0 = *p0p;
     int m = blockIdx.x * blockDim.x + threadIdx.x;
     if (m >= S * T) return;
     int s = m / T, i = m % T;
@@ -46,7 +48,7 @@ __global__ void write_tokens_kernel(const int32_t* ids, int S, int T, int p0, in
 
 void launch_write_tokens(const int32_t* ids, int S, int T, int p0, Caches c, cudaStream_t st) {
     COUNT_LAUNCH();
-    write_tokens_kernel<<<cdiv(S * T, 256), 256, 0, st>>>(ids, S, T, p0, c.tokens, c.cap);
+    write_tokens_kernel<<<cdiv(S * T, 256), 256, 0, st>>>(ids, S, T, c.len, c.tokens, c.cap);
 }
 
 // ------------------------------------------------------- CQ row dequant
@@ -414,9 +416,78 @@ __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* 
         }
 }
 
+// ------------------------------------------------ CQ matvec (decode, few rows)
+//
+// The decode combine for one to four activation rows straight off the 4-bit
+// codes, one warp per output row: lane i holds code words i, i + 32 and
+// i + 64 of the row (group g = 2k + i/16, word i % 16 of it: inputs p = 8 *
+// word .. + 7, decode lane (i % 16) % 4). A word's eight codes become int8
+// codebook values with three byte permutes per four codes, meet the eight
+// matching lane-major activation bytes in two dp4a, and xor-shuffles over
+// the word's four 8-input blocks give each (group, lane) sum; lanes 0-3
+// then run the reference's fma chain over groups.
+constexpr int GEMV_MAXM = 4;
+
+__device__ __forceinline__ uint32_t lut4(uint32_t nib16, uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3) {
+    uint32_t idx = nib16 & 0x7777u;
+    uint32_t lo = __byte_perm(v0, v1, idx), hi = __byte_perm(v2, v3, idx);
+    return __byte_perm(lo, hi, 0x3210u | ((nib16 & 0x8888u) >> 1));
+}
+
+__global__ void __launch_bounds__(256) cq_gemv_kernel(DevMat W, const int8_t* act, const float* sx, int M, float* y, int ldy,
+                                                      int col0) {
+    const int lane = threadIdx.x & 31;
+    const int n = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (n >= W.out) return;
+    const uint32_t* cv = (const uint32_t*)c_vals;
+    const uint32_t v0 = cv[0], v1 = cv[1], v2 = cv[2], v3 = cv[3];
+    const uint32_t* codes = (const uint32_t*)(W.codes + (size_t)n * 384);
+    uint32_t c[3];
+#pragma unroll
+    for (int k = 0; k < 3; k++) c[k] = __ldg(codes + lane + 32 * k);
+    int wl[3], wh[3];
+#pragma unroll
+    for (int k = 0; k < 3; k++) {
+        wl[k] = (int)lut4(c[k] & 0xffffu, v0, v1, v2, v3);
+        wh[k] = (int)lut4(c[k] >> 16, v0, v1, v2, v3);
+    }
+    const int wi = lane & 15, a = wi >> 2, l = wi & 3, half = lane >> 4;
+    const float cbs = c_cbs;
+    float norm_l = 0.f;  // lane g < 6 holds norm[n][g]
+    if (lane < 6) norm_l = h2f(W.norms[(size_t)n * 6 + lane]);
+    for (int m = 0; m < M; m++) {
+        const int8_t* ar = act + (size_t)m * 768;
+        int s[3];
+#pragma unroll
+        for (int k = 0; k < 3; k++) {
+            const int g = 2 * k + half;
+            const int2 x = *(const int2*)(ar + g * 128 + l * 32 + a * 8);
+            int v = __dp4a(wl[k], x.x, 0);
+            v = __dp4a(wh[k], x.y, v);
+            v += __shfl_xor_sync(0xffffffffu, v, 4);
+            v += __shfl_xor_sync(0xffffffffu, v, 8);
+            s[k] = v;  // lanes half*16 + l: the sum of group g, decode lane l
+        }
+        float sxl = lane < 6 ? sx[(size_t)m * 6 + lane] : 0.f;
+        float acc = 0.f;
+#pragma unroll
+        for (int g = 0; g < 6; g++) {
+            int sg = __shfl_sync(0xffffffffu, s[g >> 1], (g & 1) * 16 + (lane & 3));
+            float sc = __fmul_rn(__fmul_rn(__shfl_sync(0xffffffffu, sxl, g), cbs), __shfl_sync(0xffffffffu, norm_l, g));
+            acc = __fmaf_rn((float)sg, sc, acc);
+        }
+        float l1 = __shfl_sync(0xffffffffu, acc, 1), l2 = __shfl_sync(0xffffffffu, acc, 2), l3 = __shfl_sync(0xffffffffu, acc, 3);
+        if (lane == 0) y[(size_t)m * ldy + col0 + n] = __fadd_rn(__fadd_rn(acc, l1), __fadd_rn(l2, l3));
+    }
+}
+
 void launch_cq_gemm(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y, int ldy, int col0, cudaStream_t st) {
     COUNT_LAUNCH();
-    if (W.w8 && W.groups == 6 && M >= 32) {
+    if (T == 1 && M <= GEMV_MAXM && W.groups == 6) {
+        cq_gemv_kernel<<<cdiv(W.out, 8), 256, 0, st>>>(W, act, sx, M, y, ldy, col0);
+        return;
+    }
+    if (W.w8 && W.groups == 6) {
         dim3 grid(cdiv(W.out, MMA_BN), cdiv(M, MMA_BM));
         if (T == 1)
             cq_mma_kernel<true><<<grid, 256, MMA_SMEM, st>>>(W, act, sx, M, T, y, ldy, col0);
@@ -431,10 +502,15 @@ template <bool DECODE>
 __global__ void cq_mma_kernel(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y, int ldy, int col0);
 
 extern const size_t ATT_SMEM;
-__global__ void attention_kernel(const float* qbuf, const float* proj, Caches c, int l, int T, int p0, int window, float* att);
+extern const size_t POST_SMEM;
+__global__ void post_block_kernel(LayerW w, const float* o, const float* x1, const float* u, const float* gates,
+                                  const int32_t* perm1, const int32_t* perm2, int M, float* xs);
+__global__ void attention_kernel(const float* qbuf, const float* proj, Caches c, int l, int T, const int32_t* p0p, int window, float* att,
+                                 int8_t* act, float* sx);
 
 static cudaError_t init_attrs() {
     cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_SMEM);
+    cudaFuncSetAttribute(post_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)POST_SMEM);
     cudaFuncSetAttribute(cq_mma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
     cudaFuncSetAttribute(cq_mma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
     return cudaFuncSetAttribute(cq_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM);
@@ -444,7 +520,8 @@ static cudaError_t init_attrs() {
 
 // infer.rs:1257-1277: the n-gram hash of each (order, head) picks a table
 // row; rows the position is too young for stay zero.
-__global__ void engram_gather_kernel(DevMat tables, const int32_t* tokens, int cap, int T, int p0, int slots, float* e) {
+__global__ void engram_gather_kernel(DevMat tables, const int32_t* tokens, int cap, int T, const int32_t* p0p, int slots, float* e) {
+    const int p0 = *p0p;
     int m = blockIdx.x, tbl = blockIdx.y, lane = threadIdx.x;
     const int heads = 3, stride = 3, sub = 128, d = 768;
     int s = m / T, i = m % T, pos = p0 + i;
@@ -465,12 +542,13 @@ __global__ void engram_gather_kernel(DevMat tables, const int32_t* tokens, int c
 
 void launch_engram_gather(DevMat tables, Caches c, int S, int T, int p0, int slots, float* e, cudaStream_t st) {
     COUNT_LAUNCH();
-    engram_gather_kernel<<<dim3(S * T, 6), 32, 0, st>>>(tables, c.tokens, c.cap, T, p0, slots, e);
+    engram_gather_kernel<<<dim3(S * T, 6), 32, 0, st>>>(tables, c.tokens, c.cap, T, c.len, slots, e);
 }
 
 // infer.rs:1283-1303: the value half of kv, int8 in 32-wide groups, into
 // the site's history at the row's position.
-__global__ void engram_vhist_kernel(const float* kv, int8_t* ev8, float* evs, int site, int nsites, int T, int p0) {
+__global__ void engram_vhist_kernel(const float* kv, int8_t* ev8, float* evs, int site, int nsites, int T, const int32_t* p0p) {
+    const int p0 = *p0p;
     int m = blockIdx.x, g = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int s = m / T, pos = p0 + m % T;
     float v = kv[(size_t)m * 1536 + 768 + g * 32 + lane];
@@ -484,13 +562,14 @@ __global__ void engram_vhist_kernel(const float* kv, int8_t* ev8, float* evs, in
 
 void launch_engram_vhist(const float* kv, Caches c, int site, int nsites, int S, int T, int p0, cudaStream_t st) {
     COUNT_LAUNCH();
-    engram_vhist_kernel<<<S * T, 768, 0, st>>>(kv, c.ev8, c.evs, site, nsites, T, p0);
+    engram_vhist_kernel<<<S * T, 768, 0, st>>>(kv, c.ev8, c.evs, site, nsites, T, c.len);
 }
 
 // infer.rs:1310-1323 with engram_tap (663-687): four taps at dilation 3,
 // each an fma from the int8 history.
-__global__ void engram_conv_kernel(const float* taps, const int8_t* ev8, const float* evs, int site, int nsites, int T, int p0,
+__global__ void engram_conv_kernel(const float* taps, const int8_t* ev8, const float* evs, int site, int nsites, int T, const int32_t* p0p,
                                    float* v) {
+    const int p0 = *p0p;
     int m = blockIdx.x, ch = threadIdx.x;
     int s = m / T, pos = p0 + m % T;
     float o = 0.f;
@@ -506,14 +585,71 @@ __global__ void engram_conv_kernel(const float* taps, const int8_t* ev8, const f
 
 void launch_engram_conv(const float* taps, Caches c, int site, int nsites, int S, int T, int p0, float* v, cudaStream_t st) {
     COUNT_LAUNCH();
-    engram_conv_kernel<<<S * T, 768, 0, st>>>(taps, c.ev8, c.evs, site, nsites, T, p0, v);
+    engram_conv_kernel<<<S * T, 768, 0, st>>>(taps, c.ev8, c.evs, site, nsites, T, c.len, v);
+}
+
+// ------------------------------------------------ engram gate + input norm
+
+// infer.rs:1397-1426: the engram gate (when the layer has a site), the
+// input ZC-RMSNorm, and A8 of the normed row, by a CTA of 256 threads whose
+// shared x1 holds the row's u on entry (a, b: scratch rows of 768).
+__device__ __forceinline__ void input_norm_row(const LayerW& w, int m, float* x1, float* a, float* b, float* part, float* sc,
+                                               const float* ekv, const float* evals, float* x1o, int8_t* act, float* sx,
+                                               int tid) {
+    if (ekv) {
+        const float* kr = ekv + (size_t)m * 1536;
+        for (int k = tid; k < 768; k += 256) b[k] = kr[k];
+        __syncthreads();
+        if (tid < 16) part[tid] = dot16_chain(x1, x1, 768, tid);
+        else if (tid < 32) part[tid] = dot16_chain(b, b, 768, tid - 16);
+        __syncthreads();
+        if (tid == 0) {
+            sc[0] = rinv(dot16_combine(part), 768);
+            sc[1] = rinv(dot16_combine(part + 16), 768);
+        }
+        __syncthreads();
+        for (int k = tid; k < 768; k += 256) {
+            a[k] = __fmul_rn(x1[k], sc[0]);
+            b[k] = __fmul_rn(b[k], sc[1]);
+        }
+        __syncthreads();
+        if (tid < 16) part[tid] = dot16_chain(a, b, 768, tid);
+        __syncthreads();
+        if (tid == 0) {
+            float dab = dot16_combine(part);
+            sc[2] = __fdiv_rn(1.0f, __fadd_rn(lexpf(__fdiv_rn(-dab, __fsqrt_rn(768.0f))), 1.0f));
+        }
+        __syncthreads();
+        float alpha = sc[2];
+        for (int k = tid; k < 768; k += 256) x1[k] = __fmaf_rn(evals[(size_t)m * 768 + k], alpha, x1[k]);
+        __syncthreads();
+    }
+    if (tid < 16) part[tid] = dot16_chain(x1, x1, 768, tid);
+    __syncthreads();
+    if (tid == 0) sc[3] = rinv(dot16_combine(part), 768);
+    __syncthreads();
+    float r = sc[3];
+    for (int k = tid; k < 768; k += 256) {
+        x1o[(size_t)m * 768 + k] = x1[k];
+        float t = __fmul_rn(x1[k], r);
+        a[k] = __fmaf_rn(t, w.norm_in[k], t);
+    }
+    __syncthreads();
+    const int warp = tid >> 5, ln = tid & 31;
+    if (warp < 6) {
+        float v[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) v[k] = a[warp * 128 + 4 * ln + k];
+        prep_group_warp(v, ln, act + ((size_t)m * 6 + warp) * 128, sx + (size_t)m * 6 + warp);
+    }
 }
 
 // ------------------------------------------------------------ mHC read
 
 // infer.rs:1359-1393: lanes normalized by one rms, int8 (no rotation), the
 // 24 int8 gate dots, the pre gates, and the mixed block input u.
-__global__ void __launch_bounds__(256) mhc_read_kernel(LayerW w, int lane_own, const float* xs, float* u, float* p) {
+__global__ void __launch_bounds__(256) mhc_read_kernel(LayerW w, int lane_own, const float* xs, float* u, float* p, const float* ekv,
+                                                        const float* evals, float* x1o, int8_t* act, float* sx) {
     __shared__ __align__(16) float x[3072];
     __shared__ __align__(16) float nx[3072];
     __shared__ __align__(16) int8_t q8[3072];
@@ -573,12 +709,13 @@ __global__ void __launch_bounds__(256) mhc_read_kernel(LayerW w, int lane_own, c
                          fmaxf(__shfl_sync(0xffffffffu, zr, (ln & 16) + r * 4 + 2), __shfl_sync(0xffffffffu, zr, (ln & 16) + r * 4 + 3)));
         double e = exp(__dsub_rn((double)zr, (double)zm));
         for (int it = 0; it < 20; it++) {
+            // __drcp_rn is the correctly rounded 1.0 / x
             double s2 = __dadd_rn(e, __shfl_xor_sync(0xffffffffu, e, 1));
             double s4 = __dadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, 2));
-            e = __dmul_rn(e, __ddiv_rn(1.0, s4));
+            e = __dmul_rn(e, __drcp_rn(s4));
             double c2 = __dadd_rn(e, __shfl_xor_sync(0xffffffffu, e, 4));
             double c4 = __dadd_rn(c2, __shfl_xor_sync(0xffffffffu, c2, 8));
-            e = __dmul_rn(e, __ddiv_rn(1.0, c4));
+            e = __dmul_rn(e, __drcp_rn(c4));
         }
         if (ln < 16) p[(size_t)m * 24 + 4 + ln] = (float)e;
         if (ln >= 16 && ln < 20) {
@@ -589,86 +726,25 @@ __global__ void __launch_bounds__(256) mhc_read_kernel(LayerW w, int lane_own, c
         }
     }
     __syncthreads();
+    float* x1 = nx;  // the normalized stream is done with; reuse its space
     for (int ch = tid; ch < 768; ch += 256) {
         float o = __fmul_rn(x[ch], hp[0]);
         o = __fmaf_rn(x[768 + ch], hp[1], o);
         o = __fmaf_rn(x[1536 + ch], hp[2], o);
         o = __fmaf_rn(x[2304 + ch], hp[3], o);
         u[(size_t)m * 768 + ch] = o;
+        x1[ch] = o;
     }
+    __syncthreads();
+    __shared__ float part2[32];
+    __shared__ float sc2[4];
+    input_norm_row(w, m, x1, nx + 768, nx + 1536, part2, sc2, ekv, evals, x1o, act, sx, tid);
 }
 
-void launch_mhc_read(LayerW w, int lane, const float* xs, int M, float* u, float* p, cudaStream_t st) {
+void launch_mhc_read(LayerW w, int lane, const float* xs, int M, float* u, float* p, const float* ekv, const float* evals,
+                     float* x1, int8_t* act, float* sx, cudaStream_t st) {
     COUNT_LAUNCH();
-    mhc_read_kernel<<<M, 256, 0, st>>>(w, lane, xs, u, p);
-}
-
-// ------------------------------------------------ engram gate + input norm
-
-// infer.rs:1397-1426: the engram gate (when the layer has a site), the
-// input ZC-RMSNorm, and A8 of the normed row.
-__global__ void __launch_bounds__(256) input_norm_kernel(LayerW w, const float* u, const float* ekv, const float* evals,
-                                                         float* x1o, int8_t* act, float* sx) {
-    __shared__ __align__(16) float x1[768];
-    __shared__ __align__(16) float a[768];
-    __shared__ __align__(16) float b[768];
-    __shared__ float part[32];
-    __shared__ float sc[4];
-    const int m = blockIdx.x, tid = threadIdx.x;
-    for (int k = tid; k < 768; k += 256) x1[k] = u[(size_t)m * 768 + k];
-    __syncthreads();
-    if (ekv) {
-        const float* kr = ekv + (size_t)m * 1536;
-        for (int k = tid; k < 768; k += 256) b[k] = kr[k];
-        __syncthreads();
-        if (tid < 16) part[tid] = dot16_chain(x1, x1, 768, tid);
-        else if (tid < 32) part[tid] = dot16_chain(b, b, 768, tid - 16);
-        __syncthreads();
-        if (tid == 0) {
-            sc[0] = rinv(dot16_combine(part), 768);
-            sc[1] = rinv(dot16_combine(part + 16), 768);
-        }
-        __syncthreads();
-        for (int k = tid; k < 768; k += 256) {
-            a[k] = __fmul_rn(x1[k], sc[0]);
-            b[k] = __fmul_rn(b[k], sc[1]);
-        }
-        __syncthreads();
-        if (tid < 16) part[tid] = dot16_chain(a, b, 768, tid);
-        __syncthreads();
-        if (tid == 0) {
-            float dab = dot16_combine(part);
-            sc[2] = __fdiv_rn(1.0f, __fadd_rn(lexpf(__fdiv_rn(-dab, __fsqrt_rn(768.0f))), 1.0f));
-        }
-        __syncthreads();
-        float alpha = sc[2];
-        for (int k = tid; k < 768; k += 256) x1[k] = __fmaf_rn(evals[(size_t)m * 768 + k], alpha, x1[k]);
-        __syncthreads();
-    }
-    if (tid < 16) part[tid] = dot16_chain(x1, x1, 768, tid);
-    __syncthreads();
-    if (tid == 0) sc[3] = rinv(dot16_combine(part), 768);
-    __syncthreads();
-    float r = sc[3];
-    for (int k = tid; k < 768; k += 256) {
-        x1o[(size_t)m * 768 + k] = x1[k];
-        float t = __fmul_rn(x1[k], r);
-        a[k] = __fmaf_rn(t, w.norm_in[k], t);
-    }
-    __syncthreads();
-    const int warp = tid >> 5, ln = tid & 31;
-    if (warp < 6) {
-        float v[4];
-#pragma unroll
-        for (int k = 0; k < 4; k++) v[k] = a[warp * 128 + 4 * ln + k];
-        prep_group_warp(v, ln, act + ((size_t)m * 6 + warp) * 128, sx + (size_t)m * 6 + warp);
-    }
-}
-
-void launch_input_norm(LayerW w, const float* u, const float* ekv, const float* evals, int M, float* x1, int8_t* act,
-                       float* sx, cudaStream_t st) {
-    COUNT_LAUNCH();
-    input_norm_kernel<<<M, 256, 0, st>>>(w, u, ekv, evals, x1, act, sx);
+    mhc_read_kernel<<<M, 256, 0, st>>>(w, lane, xs, u, p, ekv, evals, x1, act, sx);
 }
 
 // ------------------------------------------------ conv taps, RoPE, int8 KV
@@ -676,8 +752,9 @@ void launch_input_norm(LayerW w, const float* u, const float* ekv, const float* 
 // infer.rs:1430-1526 (chunk rows) as unit work (infer/step.rs:468-516): per
 // row, 12 q heads, 2 k heads and 2 v heads, one warp each. The taps read
 // earlier rows of this chunk, else the pre-tap history, else zeros.
-__global__ void __launch_bounds__(512) conv_rope_kv_kernel(LayerW w, int l, const float* proj, Caches c, int T, int p0,
+__global__ void __launch_bounds__(512) conv_rope_kv_kernel(LayerW w, int l, const float* proj, Caches c, int T, const int32_t* p0p,
                                                            int hist_base, const float* cosr, const float* sinr, float* qbuf) {
+    const int p0 = *p0p;
     __shared__ float buf[16][64];
     const int m = blockIdx.x, unit = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int s = m / T, i = m % T, pos = p0 + i;
@@ -690,6 +767,9 @@ __global__ void __launch_bounds__(512) conv_rope_kv_kernel(LayerW w, int l, cons
     float* x = buf[unit];
     for (int k = lane; k < len; k += 32) {
         float cur = proj[(size_t)m * 1568 + start + k];
+        // this row's pre-tap value joins the history (infer.rs:1486-1488);
+        // its slot is none of the two that rows 0 and 1 read below
+        c.hist[(hrow0 + pos % HIST_RING) * 800 + start + k] = cur;
         float o = __fmul_rn(wt[cc + k], cur);
         for (int j = 1; j < 3; j++) {
             float wj = wt[j * cw + cc + k];
@@ -770,23 +850,7 @@ __global__ void __launch_bounds__(512) conv_rope_kv_kernel(LayerW w, int l, cons
 void launch_conv_rope_kv(LayerW w, int l, const float* proj, Caches c, int S, int T, int p0, int hist_base, const float* cosr,
                          const float* sinr, float* qbuf, cudaStream_t st) {
     COUNT_LAUNCH();
-    conv_rope_kv_kernel<<<S * T, 512, 0, st>>>(w, l, proj, c, T, p0, hist_base, cosr, sinr, qbuf);
-}
-
-// The pre-tap rows of this step into the history ring (after every row has
-// read its taps).
-__global__ void hist_update_kernel(const float* proj, Caches c, int l, int T, int p0) {
-    int s = blockIdx.x, i = T - 1 - blockIdx.y;
-    if (i < 0) return;
-    int pos = p0 + i;
-    size_t dst = (((size_t)s * c.L + l) * HIST_RING + pos % HIST_RING) * 800;
-    const float* src = proj + ((size_t)s * T + i) * 1568;
-    for (int k = threadIdx.x; k < 800; k += blockDim.x) c.hist[dst + k] = src[k];
-}
-
-void launch_hist_update(const float* proj, Caches c, int l, int S, int T, int p0, cudaStream_t st) {
-    COUNT_LAUNCH();
-    hist_update_kernel<<<dim3(S, T < HIST_RING ? T : HIST_RING), 256, 0, st>>>(proj, c, l, T, p0);
+    conv_rope_kv_kernel<<<S * T, 512, 0, st>>>(w, l, proj, c, T, c.len, hist_base, cosr, sinr, qbuf);
 }
 
 // ------------------------------------------------------------- attention
@@ -826,7 +890,8 @@ struct AttSmem {
 };
 
 __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbuf, const float* proj, Caches c, int l, int T,
-                                                                int p0, int window, float* att) {
+                                                                const int32_t* p0p, int window, float* att, int8_t* act, float* sx) {
+    const int p0 = *p0p;
     extern __shared__ __align__(16) int8_t att_raw[];
     AttSmem& sm = *reinterpret_cast<AttSmem*>(att_raw);
     const int m = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x, lane = tid & 31, h = tid >> 5;
@@ -981,8 +1046,24 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbu
     }
     const float* g = proj + (size_t)m * 1568 + 800 + hh * 64;
     float* o = att + (size_t)m * 768 + hh * 64;
-    o[lane] = __fdiv_rn(out0, __fadd_rn(nexp(-g[lane]), 1.0f));
-    o[lane + 32] = __fdiv_rn(out1, __fadd_rn(nexp(-g[lane + 32]), 1.0f));
+    float y0 = __fdiv_rn(out0, __fadd_rn(nexp(-g[lane]), 1.0f));
+    float y1 = __fdiv_rn(out1, __fadd_rn(nexp(-g[lane + 32]), 1.0f));
+    o[lane] = y0;
+    o[lane + 32] = y1;
+    // A8 of the out projection's input (infer.rs:1556): this CTA's six heads
+    // are exactly the 128-wide groups 3 kvh .. 3 kvh + 2.
+    __syncthreads();
+    float* gated = sm.s[0];  // [6][64] gated outputs, head-major
+    gated[h * 64 + lane] = y0;
+    gated[h * 64 + lane + 32] = y1;
+    __syncthreads();
+    if (h < 3) {
+        float v[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) v[k] = gated[h * 128 + 4 * lane + k];
+        const int grp = 3 * kvh + h;
+        prep_group_warp(v, lane, act + ((size_t)m * 6 + grp) * 128, sx + (size_t)m * 6 + grp);
+    }
 }
 
 [[maybe_unused]] static int host_key_chunks(int n, bool nested) {
@@ -998,17 +1079,19 @@ extern const size_t ATT_SMEM_BASE = (sizeof(AttSmem) + 15) & ~(size_t)15;
 extern const size_t ATT_SMEM = ATT_SMEM_BASE + (size_t)ATT_HEADS * ATT_MAXPARTS * 66 * 4;
 
 void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int S, int T, int p0, int window, float* att,
-                      cudaStream_t st) {
+                      int8_t* act, float* sx, cudaStream_t st) {
     COUNT_LAUNCH();
     // key_chunks gives at most c = max(ceil(n / 256), k if n >= 64 k) chunks,
     // and the launch's longest key list is its last row's
-    int nmax = p0 + T;
+    // sized for the batch's capacity, so a captured step stays valid at
+    // every later position
+    int nmax = c.cap;
     if (window > 0 && window < nmax) nmax = window;
     int most = std::max(1, (nmax + 255) / 256);
     if (T == 1 && nmax >= 256) most = std::max(most, 4);
     most = std::min(most, ATT_MAXPARTS);
     size_t smem = ATT_SMEM_BASE + (size_t)ATT_HEADS * most * 66 * 4;
-    attention_kernel<<<dim3(S * T, 2), ATT_THREADS, smem, st>>>(qbuf, proj, c, l, T, p0, window, att);
+    attention_kernel<<<dim3(S * T, 2), ATT_THREADS, smem, st>>>(qbuf, proj, c, l, T, c.len, window, att, act, sx);
 }
 
 // ------------------------------------------------------------ post block
@@ -1023,136 +1106,227 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
     return d;
 }
 
-// One Kronecker stage T = (A^T Z) B on 32x32 blocks (kron_native / mix8,
-// infer.rs:2322-2460): every output an fma chain over j from zero. Thread t
-// owns row r = t / 8 and columns c0 .. c0 + 3 (c0 = 4 (t % 8)): four
-// independent chains, two per f32x2 fma.
-__device__ __forceinline__ void kron_stage4(const float* z, const float* A, const float* B, float* mt, float* t, int tid) {
-    const int r = tid >> 3, c0 = (tid & 7) * 4;
-    float2 o0 = make_float2(0.f, 0.f), o1 = make_float2(0.f, 0.f);
-#pragma unroll 8
+// infer.rs:1564-1606 with mlp_native (1610-1634), cond_weights (1640-1694),
+// perm_fma (689-713), silu (2463-2496) and kron_native / mix8 (2322-2460).
+// Eight rows per CTA of 512 threads, one CTA per SM: the layer's small
+// weights (Kronecker factors, conditioning, diagonals, norms, permutations)
+// are staged once into shared memory with cp.async, so every phase reads
+// shared memory only. A row's 1024-wide vectors use a padded layout
+// (element p at (p / 32) * 36 + p % 32) and ping-pong between two buffers.
+// In a Kronecker pass thread t owns row q = t / 64 of the CTA, output row r
+// and 16 consecutive columns: 16 independent fma chains over j from zero,
+// two per f32x2 fma. The post and residual gates (hpost, Sinkhorn) were
+// computed by the mHC read.
+constexpr int POST_ROWS = 8, POST_THREADS = 512, PV = 32 * 36;
+struct PostSmem {
+    float kf[6][1024];
+    float cond_v[768 * 8];
+    float cond_u[8 * 1024];
+    float d1[768], d2[1024], b2[1024], d3[1024], d4[768];
+    float post_norm[768], pre_hada[768];
+    int perm1[1024], perm2[1024];
+    float x2[POST_ROWS][768];
+    float buf[2][POST_ROWS][PV];
+    float part[POST_ROWS][32];
+    float sc[POST_ROWS][2];
+    float wk[POST_ROWS][8];
+};
+extern const size_t POST_SMEM = sizeof(PostSmem);
+
+__device__ __forceinline__ int pv_idx(int p) { return (p >> 5) * 36 + (p & 31); }
+
+__device__ __forceinline__ void stage(void* dst, const void* src, int bytes, int tid) {
+    for (int o = tid * 16; o < bytes; o += POST_THREADS * 16) cp_async16((char*)dst + o, (const char*)src + o, true);
+}
+
+// One pass out[r-major] = sum_j coef[j][r] * rows[j][c] over the CTA's rows:
+// coef rows are 32 apart (cs == 32) or 33 apart (mt), `rows` padded (36).
+// Pass 1 (A^T Z): coef = A (stride 32), rows = z; result stored transposed
+// into mt (stride 33). Pass 2 ((.) B): coef = mt, rows = B (stride 32).
+__device__ __forceinline__ void kron_pass1(const float* A, const float* z, float* mt, int r, int c0) {
+    float2 o[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) o[k] = make_float2(0.f, 0.f);
+#pragma unroll 4
     for (int j = 0; j < 32; j++) {
         float a = A[j * 32 + r];
-        float4 zz = *(const float4*)(z + j * 32 + c0);
-        o0 = fma2(make_float2(a, a), make_float2(zz.x, zz.y), o0);
-        o1 = fma2(make_float2(a, a), make_float2(zz.z, zz.w), o1);
+        const float4* zr = (const float4*)(z + j * 36 + c0);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            float4 v = zr[k];
+            o[2 * k] = fma2(make_float2(a, a), make_float2(v.x, v.y), o[2 * k]);
+            o[2 * k + 1] = fma2(make_float2(a, a), make_float2(v.z, v.w), o[2 * k + 1]);
+        }
     }
-    mt[(c0 + 0) * 33 + r] = o0.x;
-    mt[(c0 + 1) * 33 + r] = o0.y;
-    mt[(c0 + 2) * 33 + r] = o1.x;
-    mt[(c0 + 3) * 33 + r] = o1.y;
-    __syncthreads();
-    o0 = make_float2(0.f, 0.f);
-    o1 = make_float2(0.f, 0.f);
-#pragma unroll 8
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        mt[(c0 + 2 * k) * 33 + r] = o[k].x;
+        mt[(c0 + 2 * k + 1) * 33 + r] = o[k].y;
+    }
+}
+
+__device__ __forceinline__ void kron_pass2(const float* mt, const float* B, float* t, int r, int c0) {
+    float2 o[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) o[k] = make_float2(0.f, 0.f);
+#pragma unroll 4
     for (int j = 0; j < 32; j++) {
         float a = mt[j * 33 + r];
-        float4 bb = *(const float4*)(B + j * 32 + c0);
-        o0 = fma2(make_float2(a, a), make_float2(bb.x, bb.y), o0);
-        o1 = fma2(make_float2(a, a), make_float2(bb.z, bb.w), o1);
+        const float4* br = (const float4*)(B + j * 32 + c0);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            float4 v = br[k];
+            o[2 * k] = fma2(make_float2(a, a), make_float2(v.x, v.y), o[2 * k]);
+            o[2 * k + 1] = fma2(make_float2(a, a), make_float2(v.z, v.w), o[2 * k + 1]);
+        }
     }
-    *(float4*)(t + r * 32 + c0) = make_float4(o0.x, o0.y, o1.x, o1.y);
+    float4* tr = (float4*)(t + r * 36 + c0);
+#pragma unroll
+    for (int k = 0; k < 4; k++) tr[k] = make_float4(o[2 * k].x, o[2 * k].y, o[2 * k + 1].x, o[2 * k + 1].y);
+}
+
+// A Kronecker stage of every row: z in buf[from], result t in buf[from]
+// too (pass 1 writes mt into buf[1 - from]).
+__device__ __forceinline__ void kron_stage_rows(PostSmem& sm, int fa, int fb, int from, int tid) {
+    const int q = tid >> 6, i = tid & 63, r = i >> 1, c0 = (i & 1) * 16;
+    kron_pass1(sm.kf[fa], sm.buf[from][q], sm.buf[1 - from][q], r, c0);
+    __syncthreads();
+    kron_pass2(sm.buf[1 - from][q], sm.kf[fb], sm.buf[from][q], r, c0);
     __syncthreads();
 }
 
-// infer.rs:1564-1606 with mlp_native (1610-1634), cond_weights (1640-1694),
-// perm_fma (689-713) and silu (2463-2496). One CTA of 256 threads per row;
-// the post and residual gates (hpost, Sinkhorn) come from the mHC read.
-__global__ void __launch_bounds__(256) post_block_kernel(LayerW w, const float* o, const float* x1, const float* u,
-                                                         const float* gates, const int32_t* perm1, const int32_t* perm2,
-                                                         float* xs) {
-    __shared__ __align__(16) float x2[768];
-    __shared__ __align__(16) float h2[768];
-    __shared__ __align__(16) float z[1024];
-    __shared__ __align__(16) float t[1024];
-    __shared__ __align__(16) float kf[6][1024];
-    __shared__ float mt[32 * 33];
-    __shared__ float part[32];
-    __shared__ float sc[2];
-    __shared__ float wk[8];
-    const int m = blockIdx.x, tid = threadIdx.x;
-    for (int k = tid; k < 6 * 256; k += 256) {
-        int f = k >> 8, q = k & 255;
-        *(float4*)(&kf[f][q * 4]) = *(const float4*)(w.kron[f] + q * 4);
+__global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, const float* o, const float* x1, const float* u,
+                                                                   const float* gates, const int32_t* perm1,
+                                                                   const int32_t* perm2, int M, float* xs) {
+    extern __shared__ __align__(16) int8_t post_raw[];
+    PostSmem& sm = *reinterpret_cast<PostSmem*>(post_raw);
+    const int tid = threadIdx.x, m0 = blockIdx.x * POST_ROWS;
+    const int rows = min(POST_ROWS, M - m0);
+    for (int f = 0; f < 6; f++) stage(sm.kf[f], w.kron[f], 4096, tid);
+    stage(sm.cond_v, w.cond_v, 768 * 8 * 4, tid);
+    stage(sm.cond_u, w.cond_u, 8 * 1024 * 4, tid);
+    stage(sm.d1, w.d1, 768 * 4, tid);
+    stage(sm.d2, w.d2, 4096, tid);
+    stage(sm.b2, w.b2, 4096, tid);
+    stage(sm.d3, w.d3, 4096, tid);
+    stage(sm.d4, w.d4, 768 * 4, tid);
+    stage(sm.post_norm, w.post_norm, 768 * 4, tid);
+    stage(sm.pre_hada, w.pre_hada, 768 * 4, tid);
+    stage(sm.perm1, perm1, 4096, tid);
+    stage(sm.perm2, perm2, 4096, tid);
+    asm volatile("cp.async.commit_group;\n" ::);
+    for (int k = tid; k < POST_ROWS * 192; k += POST_THREADS) {
+        int q = k / 192, c = k % 192;
+        *(float4*)(&sm.x2[q][4 * c]) = q < rows ? *(const float4*)(o + (size_t)(m0 + q) * 768 + 4 * c) : make_float4(0, 0, 0, 0);
     }
-    for (int k = tid; k < 768; k += 256) x2[k] = o[(size_t)m * 768 + k];
+    asm volatile("cp.async.wait_group 0;\n" ::);
     __syncthreads();
-    if (tid < 16) part[tid] = dot16_chain(x2, x2, 768, tid);
+    // zcn(o, post_norm): sixteen dot16 chains per row
+    if (tid < POST_ROWS * 16) {
+        const int q = tid >> 4;
+        sm.part[q][tid & 15] = dot16_chain(sm.x2[q], sm.x2[q], 768, tid & 15);
+    }
     __syncthreads();
-    if (tid == 0) sc[0] = rinv(dot16_combine(part), 768);
+    if (tid < POST_ROWS) sm.sc[tid][0] = rinv(dot16_combine(sm.part[tid]), 768);
     __syncthreads();
     const float ga = __fdiv_rn(1.0f, __fadd_rn(lexpf(-w.attn_gate), 1.0f));
-    for (int k = tid; k < 768; k += 256) {
-        float tt = __fmul_rn(x2[k], sc[0]);
-        float on = __fmaf_rn(tt, w.post_norm[k], tt);
-        x2[k] = __fmaf_rn(on, ga, x1[(size_t)m * 768 + k]);
+    for (int k = tid; k < POST_ROWS * 768; k += POST_THREADS) {
+        int q = k / 768, c = k % 768;
+        float tt = __fmul_rn(sm.x2[q][c], sm.sc[q][0]);
+        float on = __fmaf_rn(tt, sm.post_norm[c], tt);
+        sm.x2[q][c] = __fmaf_rn(on, ga, q < rows ? x1[(size_t)(m0 + q) * 768 + c] : 0.f);
     }
     __syncthreads();
-    if (tid < 16) part[tid] = dot16_chain(x2, x2, 768, tid);
+    if (tid < POST_ROWS * 16) {
+        const int q = tid >> 4;
+        sm.part[q][tid & 15] = dot16_chain(sm.x2[q], sm.x2[q], 768, tid & 15);
+    }
     __syncthreads();
-    if (tid == 0) sc[1] = rinv(dot16_combine(part), 768);
+    if (tid < POST_ROWS) sm.sc[tid][1] = rinv(dot16_combine(sm.part[tid]), 768);
     __syncthreads();
-    for (int k = tid; k < 768; k += 256) {
-        float tt = __fmul_rn(x2[k], sc[1]);
-        h2[k] = __fmaf_rn(tt, w.pre_hada[k], tt);
+    // h2 = zcn(x2, pre_hada) into buf[1] (plain layout), z = h2 * d1 into buf[0]
+    for (int k = tid; k < POST_ROWS * 768; k += POST_THREADS) {
+        int q = k / 768, c = k % 768;
+        float tt = __fmul_rn(sm.x2[q][c], sm.sc[q][1]);
+        float h = __fmaf_rn(tt, sm.pre_hada[c], tt);
+        sm.buf[1][q][c] = h;
+        sm.buf[0][q][pv_idx(c)] = __fmul_rn(h, sm.d1[c]);
+    }
+    for (int k = tid; k < POST_ROWS * 256; k += POST_THREADS) {
+        int q = k >> 8, c = 768 + (k & 255);
+        sm.buf[0][q][pv_idx(c)] = 0.f;
     }
     __syncthreads();
     // conditioning logits: 4 accumulator sets by j % 4, fma chains over j
-    if (tid < 32) {
-        const int set = tid >> 3, k = tid & 7;
+    if (tid < POST_ROWS * 32) {
+        const int q = tid >> 5, set = (tid >> 3) & 3, k = tid & 7;
+        const float* h = sm.buf[1][q];
         float acc = 0.f;
 #pragma unroll 16
-        for (int j = set; j < 768; j += 4) acc = __fmaf_rn(h2[j], w.cond_v[j * 8 + k], acc);
-        part[tid] = acc;
+        for (int j = set; j < 768; j += 4) acc = __fmaf_rn(h[j], sm.cond_v[j * 8 + k], acc);
+        sm.part[q][tid & 31] = acc;
     }
-    for (int j = tid; j < 1024; j += 256) z[j] = j < 768 ? __fmul_rn(h2[j], w.d1[j]) : 0.f;
     __syncthreads();
-    if (tid < 32) {
+    if (tid < POST_ROWS * 32) {
         // logits ((C + D) + B) + A, max, one libm exp per lane, the engine's
         // sum tree e7 + ((e6 + (e5 + e4)) + ((e3 + e2) + (e1 + e0)))
-        const int k = tid & 7;
-        float lg = __fadd_rn(__fadd_rn(__fadd_rn(part[16 + k], part[24 + k]), part[8 + k]), part[k]);
+        const int q = tid >> 5, k = tid & 7;
+        const float* pt = sm.part[q];
+        float lg = __fadd_rn(__fadd_rn(__fadd_rn(pt[16 + k], pt[24 + k]), pt[8 + k]), pt[k]);
         float mx = lg;
 #pragma unroll
-        for (int o = 1; o < 8; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        for (int off = 1; off < 8; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
         float e = lexpf(__fsub_rn(lg, mx));
         float ev[8];
 #pragma unroll
-        for (int q = 0; q < 8; q++) ev[q] = __shfl_sync(0xffffffffu, e, q);
+        for (int qq = 0; qq < 8; qq++) ev[qq] = __shfl_sync(0xffffffffu, e, qq);
         float sum = __fadd_rn(ev[7], __fadd_rn(__fadd_rn(ev[6], __fadd_rn(ev[5], ev[4])), __fadd_rn(__fadd_rn(ev[3], ev[2]), __fadd_rn(ev[1], ev[0]))));
-        if (tid < 8) wk[k] = __fmul_rn(e, __fdiv_rn(1.0f, sum));
+        if ((tid & 31) < 8) sm.wk[q][k] = __fmul_rn(e, __fdiv_rn(1.0f, sum));
     }
-    kron_stage4(z, kf[0], kf[1], mt, t, tid);
-    for (int j = tid; j < 1024; j += 256) {
-        float cnd = 1.0f;
+    kron_stage_rows(sm, 0, 1, 0, tid);  // t1 in buf[0]
+    // z = fma(t1[perm1[j]], cond[j] * d2[j], b2[j]) with cond = 1 + sum_k w_k u_k,
+    // then SiLU; into buf[1]
+    for (int j = tid; j < 1024; j += POST_THREADS) {
+        float cu[8];
 #pragma unroll
-        for (int k = 0; k < 8; k++) cnd = __fmaf_rn(w.cond_u[k * 1024 + j], wk[k], cnd);
-        float zz = __fmaf_rn(t[perm1[j]], __fmul_rn(cnd, w.d2[j]), w.b2[j]);
-        z[j] = __fdiv_rn(zz, __fadd_rn(nexp(-zz), 1.0f));
+        for (int kk = 0; kk < 8; kk++) cu[kk] = sm.cond_u[kk * 1024 + j];
+        const float d2 = sm.d2[j], b2 = sm.b2[j];
+        const int src = pv_idx(sm.perm1[j]), dst = pv_idx(j);
+#pragma unroll
+        for (int q = 0; q < POST_ROWS; q++) {
+            float cnd = 1.0f;
+#pragma unroll
+            for (int kk = 0; kk < 8; kk++) cnd = __fmaf_rn(cu[kk], sm.wk[q][kk], cnd);
+            float zz = __fmaf_rn(sm.buf[0][q][src], __fmul_rn(cnd, d2), b2);
+            sm.buf[1][q][dst] = __fdiv_rn(zz, __fadd_rn(nexp(-zz), 1.0f));
+        }
     }
     __syncthreads();
-    kron_stage4(z, kf[2], kf[3], mt, t, tid);
-    for (int j = tid; j < 1024; j += 256) z[j] = __fmul_rn(t[perm2[j]], w.d3[j]);
+    kron_stage_rows(sm, 2, 3, 1, tid);  // t2 in buf[1]
+    for (int j = tid; j < 1024; j += POST_THREADS) {
+        const float d3 = sm.d3[j];
+        const int src = pv_idx(sm.perm2[j]), dst = pv_idx(j);
+#pragma unroll
+        for (int q = 0; q < POST_ROWS; q++) sm.buf[0][q][dst] = __fmul_rn(sm.buf[1][q][src], d3);
+    }
     __syncthreads();
-    kron_stage4(z, kf[4], kf[5], mt, t, tid);
-    const float* gr = gates + (size_t)m * 24;
-    float hpost[4], hres[16];
-#pragma unroll
-    for (int k = 0; k < 4; k++) hpost[k] = gr[k];
-#pragma unroll
-    for (int k = 0; k < 16; k++) hres[k] = gr[4 + k];
-    float* xr = xs + (size_t)m * 3072;
-    for (int ch = tid; ch < 768; ch += 256) {
-        float mlp = __fmul_rn(t[ch], w.d4[ch]);
-        float y = __fsub_rn(__fadd_rn(x2[ch], mlp), u[(size_t)m * 768 + ch]);
+    kron_stage_rows(sm, 4, 5, 0, tid);  // t3 in buf[0]
+    for (int k = tid; k < POST_ROWS * 768; k += POST_THREADS) {
+        const int q = k / 768, ch = k % 768;
+        if (q >= rows) continue;
+        const int m = m0 + q;
+        const float* gr = gates + (size_t)m * 24;
+        float mlp = __fmul_rn(sm.buf[0][q][pv_idx(ch)], sm.d4[ch]);
+        float y = __fsub_rn(__fadd_rn(sm.x2[q][ch], mlp), u[(size_t)m * 768 + ch]);
+        float* xr = xs + (size_t)m * 3072;
         float old[4];
 #pragma unroll
         for (int b = 0; b < 4; b++) old[b] = xr[b * 768 + ch];
 #pragma unroll
         for (int a = 0; a < 4; a++) {
-            float v = __fmul_rn(y, hpost[a]);
+            float v = __fmul_rn(y, gr[a]);
 #pragma unroll
-            for (int b = 0; b < 4; b++) v = __fmaf_rn(old[b], hres[a * 4 + b], v);
+            for (int b = 0; b < 4; b++) v = __fmaf_rn(old[b], gr[4 + a * 4 + b], v);
             xr[a * 768 + ch] = v;
         }
     }
@@ -1161,7 +1335,7 @@ __global__ void __launch_bounds__(256) post_block_kernel(LayerW w, const float* 
 void launch_post_block(LayerW w, const float* o, const float* x1, const float* u, const float* gates, const int32_t* perm1,
                        const int32_t* perm2, int M, float* xs, cudaStream_t st) {
     COUNT_LAUNCH();
-    post_block_kernel<<<M, 256, 0, st>>>(w, o, x1, u, gates, perm1, perm2, xs);
+    post_block_kernel<<<cdiv(M, POST_ROWS), POST_THREADS, POST_SMEM, st>>>(w, o, x1, u, gates, perm1, perm2, M, xs);
 }
 
 // ------------------------------------------------------------ final norm
@@ -1198,8 +1372,9 @@ void launch_final_hidden(const float* xs, const float* final_norm, int S, int T,
 // infer.rs:1716-1744: table rows (sincosf of freq * pos, tabulated on the
 // host with the reference's f64 libm stand-in) for a chunk, or for a single
 // token right after the newest position the angle-addition recurrence.
-__global__ void rope_rows_kernel(const float* tc, const float* tsn, const float* sd, const float* cd, int p0, int T, int recur,
+__global__ void rope_rows_kernel(const float* tc, const float* tsn, const float* sd, const float* cd, const int32_t* p0p, int T, int recur,
                                  float* state, float* cosr, float* sinr) {
+    const int p0 = *p0p;
     int i = blockIdx.x, f = threadIdx.x;
     if (f >= 24) return;
     float cv, sv;
@@ -1219,10 +1394,19 @@ __global__ void rope_rows_kernel(const float* tc, const float* tsn, const float*
     }
 }
 
-void launch_rope_rows(const float* table_cos, const float* table_sin, const float* sd, const float* cd, int p0, int T,
+void launch_rope_rows(const float* table_cos, const float* table_sin, const float* sd, const float* cd, const int32_t* p0p, int T,
                       int recur, float* state, float* cosr, float* sinr, cudaStream_t st) {
     COUNT_LAUNCH();
-    rope_rows_kernel<<<T, 32, 0, st>>>(table_cos, table_sin, sd, cd, p0, T, recur, state, cosr, sinr);
+    rope_rows_kernel<<<T, 32, 0, st>>>(table_cos, table_sin, sd, cd, p0p, T, recur, state, cosr, sinr);
+}
+
+// Positions fed so far, advanced on the device so a captured step replays
+// at any position.
+__global__ void advance_len_kernel(int32_t* len, int T) { *len += T; }
+
+void launch_advance_len(int32_t* len, int T, cudaStream_t st) {
+    COUNT_LAUNCH();
+    advance_len_kernel<<<1, 1, 0, st>>>(len, T);
 }
 
 // ------------------------------------------------------- masked argmax
@@ -1237,7 +1421,19 @@ __global__ void masked_argmax_kernel(const float* logits, int V, const uint8_t* 
     const uint8_t* al = allow ? allow + (size_t)s * ((V + 7) / 8) : nullptr;
     float best = -INFINITY;
     int idx = 0x7fffffff;
-    for (int k = tid; k < V; k += blockDim.x) {
+    // whole 8-id blocks: two float4 loads and one mask byte per block
+    const int nb = (V % 8 == 0) ? V / 8 : 0;
+    for (int q = tid; q < nb; q += blockDim.x) {
+        float4 a = *(const float4*)(x + 8 * q), b = *(const float4*)(x + 8 * q + 4);
+        unsigned bits = al ? al[q] : 0xffu;
+        float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            float ve = ((bits >> e) & 1) ? v[e] : -1e30f;
+            if (ve > best) { best = ve; idx = 8 * q + e; }  // ascending ids: first index wins ties
+        }
+    }
+    for (int k = nb * 8 + tid; k < V; k += blockDim.x) {
         float v = (!al || ((al[k >> 3] >> (k & 7)) & 1)) ? x[k] : -1e30f;
         if (v > best || (v == best && k < idx)) { best = v; idx = k; }
     }
@@ -1258,7 +1454,7 @@ __global__ void masked_argmax_kernel(const float* logits, int V, const uint8_t* 
 
 void launch_masked_argmax(const float* logits, int S, int V, const uint8_t* allow, int32_t* next, cudaStream_t st) {
     COUNT_LAUNCH();
-    masked_argmax_kernel<<<S, 1024, 0, st>>>(logits, V, allow, next);
+    masked_argmax_kernel<<<S, 256, 0, st>>>(logits, V, allow, next);
 }
 
 }  // namespace nd

@@ -45,11 +45,17 @@ struct Caches {
     int8_t* ev8;          // [S][sites][ENG_RING][768] engram value history
     float* evs;           // [S][sites][ENG_RING][24]
     int32_t* tokens;      // [S][cap]
+    // positions every sequence has been fed before this step, on the device:
+    // kernels read their positions here, so a captured step replays anywhere
+    const int32_t* len;
 };
 
-// Pre-tap rows kept per (sequence, layer): the conv reads two back, and a
-// chunk's rows are written only after every row has read its taps.
-constexpr int HIST_RING = 2;
+// Pre-tap rows kept per (sequence, layer), by position modulo the ring: the
+// conv reads two back, and each row writes its own row in the same kernel,
+// so a chunk's 32 new positions must not reuse the two slots rows 0 and 1
+// read (32 + 2); it is also the reference's rollback depth plus the taps
+// (ROLLBACK = 32, model.rs:184; keep = taps - 1 + ROLLBACK, infer.rs:1489).
+constexpr int HIST_RING = 34;
 // Engram value history kept per (sequence, site), by position: a chunk's 32
 // rows are all written before the dilated conv reads 3 taps of dilation 3
 // back, so the ring must hold 32 + 9 positions.
@@ -57,6 +63,8 @@ constexpr int ENG_RING = 64;
 
 // Kernels this process has launched through the launchers below.
 long long launch_count();
+// Kernels a replayed CUDA graph launched (counted with the others).
+void add_launches(long long n);
 
 void set_constants(const int8_t vals[16], const float fvals[16], float cbs, float hs128);
 
@@ -72,19 +80,21 @@ void launch_engram_vhist(const float* kv, Caches c, int site, int nsites, int S,
 void launch_engram_conv(const float* taps, Caches c, int site, int nsites, int S, int T, int p0, float* v, cudaStream_t st);
 // u [M][768]; gates [M][24]: the post block's hpost[4] then the Sinkhorn
 // matrix hres[16] (infer.rs:1580-1586), from this layer's gate projections.
-void launch_mhc_read(LayerW w, int lane, const float* xs, int M, float* u, float* gates, cudaStream_t st);
-void launch_input_norm(LayerW w, const float* u, const float* ekv, const float* evals, int M, float* x1, int8_t* act,
-                       float* sx, cudaStream_t st);
+// The same CTA then applies the engram gate (ekv [M][1536] and evals
+// [M][768] of the layer's site, or both NULL), the input norm, and A8 of the
+// normed row: x1 [M][768] (the residual), act/sx for the q|k|v|gate matmul.
+void launch_mhc_read(LayerW w, int lane, const float* xs, int M, float* u, float* gates, const float* ekv,
+                     const float* evals, float* x1, int8_t* act, float* sx, cudaStream_t st);
 void launch_conv_rope_kv(LayerW w, int l, const float* proj, Caches c, int S, int T, int p0, int hist_base, const float* cosr,
                          const float* sinr, float* qbuf, cudaStream_t st);
-void launch_hist_update(const float* proj, Caches c, int l, int S, int T, int p0, cudaStream_t st);
 void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int S, int T, int p0, int window, float* att,
-                      cudaStream_t st);
+                      int8_t* act, float* sx, cudaStream_t st);
 void launch_post_block(LayerW w, const float* o, const float* x1, const float* u, const float* gates, const int32_t* perm1,
                        const int32_t* perm2, int M, float* xs, cudaStream_t st);
 void launch_final_hidden(const float* xs, const float* final_norm, int S, int T, int all_rows, float* h, cudaStream_t st);
-void launch_rope_rows(const float* table_cos, const float* table_sin, const float* sd, const float* cd, int p0, int T,
+void launch_rope_rows(const float* table_cos, const float* table_sin, const float* sd, const float* cd, const int32_t* p0p, int T,
                       int recur, float* state, float* cosr, float* sinr, cudaStream_t st);
+void launch_advance_len(int32_t* len, int T, cudaStream_t st);
 void launch_masked_argmax(const float* logits, int S, int V, const uint8_t* allow, int32_t* next, cudaStream_t st);
 
 }  // namespace nd

@@ -16,7 +16,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libneedle3.so")
 
 OUT_NONE, OUT_LAST_LOGITS, OUT_LAST_HIDDEN, OUT_ALL_LOGITS, OUT_HIDDEN = 0, 1, 2, 3, 4
-SITES = dict(none=0, qkvg=1, out=2, lm_head=3, engram_kv=4, attention=5, post=6, mhc=7, conv=8, norm=9)
+SITES = dict(none=0, qkvg=1, out=2, lm_head=3, engram_kv=4, attention=5, post=6, mhc=7, conv=8)
 ND_DEVICE = 1
 
 _lib = None
