@@ -124,6 +124,21 @@ enum {
 int nd_batch_time_site(nd_batch* b, int site);
 int nd_batch_site_time(nd_batch* b, double* total_ms, int* launches);
 
+/* No counterpart in the reference. nd_head_logits without any allocation,
+ * for callers that cannot call cudaMalloc (their GPU memory belongs to
+ * another allocator, or they must not take cudaMalloc's implicit device
+ * synchronisation): logits of h[rows][d_model] into out[rows][out_rows] with
+ * the decode kernel, both device pointers on the model's GPU, queued on
+ * `stream` (a cudaStream_t; NULL is the legacy default stream) and not
+ * waited for. The int8 activations live in one static device array of the
+ * library, so rows is limited to 1..64; larger requests return -1 with the
+ * reason in nd_last_error(). The first call on each device looks up that
+ * array's device address, so make it before capturing any stream into a
+ * CUDA graph. All calls share the array: calls whose work overlaps on the
+ * GPU (other streams, other threads) race; the array keeps the last call's
+ * contents, none of which the next call reads before writing. */
+int nd_head_logits_noalloc(const nd_model* m, const float* h, int rows, float* out, void* stream);
+
 /* The last failure on this thread (empty if none). */
 const char* nd_last_error(void);
 

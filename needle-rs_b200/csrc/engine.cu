@@ -590,6 +590,14 @@ static int fail(const std::exception& e) {
     return -1;
 }
 
+void set_error(const std::string& msg) { g_err = msg; }
+
+}  // namespace nd
+
+struct nd_model;
+
+namespace nd {
+bool model_head(const nd_model* m, DevMat* emb, int* device, int* out_rows);
 }  // namespace nd
 
 using namespace nd;
@@ -598,6 +606,14 @@ struct nd_model {
     std::unique_ptr<Model> m;
 };
 
+// The tied lm_head matrix of a loaded model (for noalloc.cu).
+bool nd::model_head(const nd_model* mh, DevMat* emb, int* device, int* out_rows) {
+    if (!mh || !mh->m) return false;
+    *emb = mh->m->embedding;
+    *device = mh->m->device;
+    *out_rows = mh->m->c.out_rows();
+    return true;
+}
 struct nd_batch {
     std::unique_ptr<Batch> b;
     std::vector<int32_t> host_ids;
