@@ -301,7 +301,7 @@ def main():
         return
     prompts, masks = make_inputs(rank, S, total_steps, V)
     sites = ["qkvg", "out", "lm_head", "engram_kv", "attention", "post", "mhc", "conv"]
-    cap = PROMPT + total_steps + len(sites) + 2
+    cap = PROMPT + total_steps + K + len(sites) + 2
 
     # --- device-resident run (value)
     bA = model.batch(S, cap)
@@ -340,7 +340,6 @@ def main():
         for k in range(W):
             bA.step(d_masks[k], d_next)
         barrier()
-        bA.time_site(site)
         l0 = nb.launch_count()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev0.record(stream)
@@ -350,6 +349,12 @@ def main():
         launches = nb.launch_count() - l0
         barrier()
         t_value = ev0.elapsed_time(ev1) / 1e3
+        # the roofline site's kernels, timed with events around every launch
+        # over K more steps of the same batch (each step queued whole behind
+        # a hold kernel, so the events see kernel time, not launch gaps)
+        bA.time_site(site)
+        for k in range(K):
+            bA.step(d_masks[(W + k) % total_steps], d_next)
         site_ms, site_n = bA.site_time()
         bA.time_site("none")
         # e2e: host masks in pinned memory, ids back to the host, every step
@@ -373,7 +378,7 @@ def main():
 
     if rank == 0:
         hbm, bf16, kind = peaks()
-        n_keys = PROMPT + W + K // 2 + len(sites)
+        n_keys = PROMPT + W + K + K // 2 + 1
         amount, unit, bound = site_algorithmic(site, S, n_keys)
         avg_s = site_ms / 1e3 / max(site_n, 1)
         achieved = amount / avg_s / 1e9

@@ -412,7 +412,8 @@ static Batch* batch_new(Model* m, int S, int max_len) {
     b.c.cap = max_len;
     b.c.k8 = b.alloc<int8_t>((size_t)S * L * 2 * max_len * 48);
     b.c.ks = b.alloc<float>((size_t)S * L * 2 * max_len);
-    b.c.v8 = b.alloc<int8_t>((size_t)S * L * 2 * max_len * 64);
+    b.c.vgroups = (max_len + 3) / 4;
+    b.c.v8 = b.alloc<int8_t>((size_t)S * L * 2 * b.c.vgroups * 256);
     b.c.vs = b.alloc<float>((size_t)S * L * 2 * max_len);
     b.c.hist = b.alloc<float>((size_t)S * L * HIST_RING * 800);
     b.c.ev8 = b.alloc<int8_t>((size_t)S * std::max(nsites, 1) * ENG_RING * 768);
@@ -748,6 +749,8 @@ int nd_batch_step(nd_batch* bh, const unsigned char* allow_bits, int* next_ids, 
                 b.logits_rows = b.S;
             }
         } else {
+            // with a site timed, queue the whole step behind a 5 ms hold
+            if (b.time_site) launch_hold(5000000ull, b.st);
             launch_masked_argmax(b.logits, b.S, c.out_rows(), allow, b.next, b.st);
             forward(b, b.next, 1, ND_OUT_LAST_LOGITS);
         }

@@ -37,9 +37,10 @@ struct LayerW {
 // Per-sequence caches of one batch.
 struct Caches {
     int S, L, cap;        // sequences, layers, KV slots per sequence
+    int vgroups;          // value groups per sequence and head: ceil(cap / 4)
     int8_t* k8;           // [S][L][2][cap][48]
     float* ks;            // [S][L][2][cap]
-    int8_t* v8;           // [S][L][2][cap][64]
+    int8_t* v8;           // [S][L][2][vgroups][64][4]: position 4g + j's byte j of a dimension word
     float* vs;            // [S][L][2][cap]
     float* hist;          // [S][L][HIST_RING][800] pre-tap q|k|v rows by position
     int8_t* ev8;          // [S][sites][ENG_RING][768] engram value history
@@ -95,6 +96,7 @@ void launch_final_hidden(const float* xs, const float* final_norm, int S, int T,
 void launch_rope_rows(const float* table_cos, const float* table_sin, const float* sd, const float* cd, const int32_t* p0p, int T,
                       int recur, float* state, float* cosr, float* sinr, cudaStream_t st);
 void launch_advance_len(int32_t* len, int T, cudaStream_t st);
+void launch_hold(unsigned long long ns, cudaStream_t st);
 void launch_masked_argmax(const float* logits, int S, int V, const uint8_t* allow, int32_t* next, cudaStream_t st);
 
 }  // namespace nd
