@@ -255,10 +255,21 @@ constexpr int MMA_MAGIC = 0x4B400000;
 constexpr size_t MMA_SMEM = (size_t)(MMA_BM + MMA_BN) * MMA_LD + (size_t)(2 * MMA_BM + 2 * MMA_BN) * 6 * 4;
 
 __device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2], const int (&c)[4]) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};\n"
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(c[3]));
+}
+
+// Four 8x8 b16 matrices (8 rows of 16 bytes each); lanes 8q..8q+7 give
+// matrix q's row addresses, and lane t receives row t / 4, bytes
+// 4 (t % 4) .. 4 (t % 4) + 3 of each, in r[q]: the int8 mma fragments.
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+    uint32_t s = (uint32_t)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(s)
+                 : "memory");
 }
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
@@ -359,30 +370,31 @@ __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* 
                 int cn = wn + j * 8 + tig * 2 + h;
                 cs[j][h] = s_nrm[cn * 6 + g];
             }
+        // decode: (sx * cbs) * norm for each of this thread's outputs
+        float dsc[4][4];
+        if (DECODE) {
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) dsc[j][e] = __fmul_rn(e < 2 ? rs0 : rs1, cs[j][e & 1]);
+        }
         int dsum[4][4];
 #pragma unroll
         for (int l = 0; l < 4; l++) {
-            const int kb = g * 128 + l * 32 + tig * 4;
-            uint32_t a[4];
-            a[0] = *(const uint32_t*)(as + r0 * MMA_LD + kb);
-            a[1] = *(const uint32_t*)(as + r1 * MMA_LD + kb);
-            a[2] = *(const uint32_t*)(as + r0 * MMA_LD + kb + 16);
-            a[3] = *(const uint32_t*)(as + r1 * MMA_LD + kb + 16);
+            const int kb = g * 128 + l * 32;
+            uint32_t a[4], bq[2][4];
+            ldsm_x4(a, as + (wm + (lane & 15)) * MMA_LD + kb + (lane >> 4) * 16);
+#pragma unroll
+            for (int jj = 0; jj < 2; jj++)
+                ldsm_x4(bq[jj], ws + (wn + (2 * jj + (lane >> 4)) * 8 + (lane & 7)) * MMA_LD + kb + ((lane >> 3) & 1) * 16);
 #pragma unroll
             for (int j = 0; j < 4; j++) {
-                const int nr = wn + j * 8 + gid;
-                uint32_t b[2];
-                b[0] = *(const uint32_t*)(ws + nr * MMA_LD + kb);
-                b[1] = *(const uint32_t*)(ws + nr * MMA_LD + kb + 16);
+                const uint32_t b[2] = {bq[j >> 1][(j & 1) * 2], bq[j >> 1][(j & 1) * 2 + 1]};
                 int d[4];
                 if (DECODE) {
                     mma_s8(d, a, b, magic);
 #pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        // (sx * cbs) * norm, then the lane's fma
-                        float sc = __fmul_rn(e < 2 ? rs0 : rs1, cs[j][e & 1]);
-                        acc[j][e][l] = __fmaf_rn(magic_to_float(d[e]), sc, acc[j][e][l]);
-                    }
+                    for (int e = 0; e < 4; e++) acc[j][e][l] = __fmaf_rn(magic_to_float(d[e]), dsc[j][e], acc[j][e][l]);
                 } else {
                     if (l == 0) {
                         mma_s8(d, a, b, magic);
@@ -612,17 +624,16 @@ __device__ __forceinline__ float dot16_combine_warp(float acc, int ln) {
     return __fadd_rn(__fadd_rn(t, t1), __fadd_rn(t2, t3));
 }
 
-// Eight per-lane integer sums reduced across the warp: afterwards lanes
-// 4i..4i+3 hold value i's total (i = (lane >> 2)'s bits 16, 8, 4 as 4, 2, 1).
-__device__ __forceinline__ int reduce8_scatter(const int s[8], int ln) {
+// Four per-lane integer sums reduced across the warp: afterwards lanes
+// 8i..8i+7 hold value i's total (i = (lane >> 3)'s bits 16, 8 as 2, 1).
+__device__ __forceinline__ int reduce4_scatter(const int s[4], int ln) {
     const unsigned F = 0xffffffffu;
-    int h[4], q[2];
-    const bool u16 = ln & 16, u8 = ln & 8, u4 = ln & 4;
+    int h[2];
+    const bool u16 = ln & 16, u8 = ln & 8;
 #pragma unroll
-    for (int j = 0; j < 4; j++) h[j] = (u16 ? s[j + 4] : s[j]) + __shfl_xor_sync(F, u16 ? s[j] : s[j + 4], 16);
-#pragma unroll
-    for (int j = 0; j < 2; j++) q[j] = (u8 ? h[j + 2] : h[j]) + __shfl_xor_sync(F, u8 ? h[j] : h[j + 2], 8);
-    int r = (u4 ? q[1] : q[0]) + __shfl_xor_sync(F, u4 ? q[0] : q[1], 4);
+    for (int j = 0; j < 2; j++) h[j] = (u16 ? s[j + 2] : s[j]) + __shfl_xor_sync(F, u16 ? s[j] : s[j + 2], 16);
+    int r = (u8 ? h[1] : h[0]) + __shfl_xor_sync(F, u8 ? h[0] : h[1], 8);
+    r += __shfl_xor_sync(F, r, 4);
     r += __shfl_xor_sync(F, r, 2);
     r += __shfl_xor_sync(F, r, 1);
     return r;
@@ -721,15 +732,15 @@ __global__ void __launch_bounds__(MHC_THREADS) mhc_read_kernel(LayerW w, int lan
         // the 24 gate dots: thread t owns bytes 16 t .. 16 t + 15 of the row
         const int4* wq = (const int4*)w.phi_q + tid;
 #pragma unroll
-        for (int bt = 0; bt < 3; bt++) {
-            int s8[8];
+        for (int bt = 0; bt < 6; bt++) {
+            int s4[4];
 #pragma unroll
-            for (int kk = 0; kk < 8; kk++) {
-                const int4 g = __ldg(wq + (bt * 8 + kk) * 192);
-                s8[kk] = __dp4a(g.w, wd[3], __dp4a(g.z, wd[2], __dp4a(g.y, wd[1], __dp4a(g.x, wd[0], 0))));
+            for (int kk = 0; kk < 4; kk++) {
+                const int4 g = __ldg(wq + (bt * 4 + kk) * 192);
+                s4[kk] = __dp4a(g.w, wd[3], __dp4a(g.z, wd[2], __dp4a(g.y, wd[1], __dp4a(g.x, wd[0], 0))));
             }
-            int tot = reduce8_scatter(s8, ln);
-            if ((ln & 3) == 0) red24[warp][bt * 8 + ((ln & 16) ? 4 : 0) + ((ln & 8) ? 2 : 0) + ((ln & 4) ? 1 : 0)] = tot;
+            int tot = reduce4_scatter(s4, ln);
+            if ((ln & 7) == 0) red24[warp][bt * 4 + ((ln & 16) ? 2 : 0) + ((ln & 8) ? 1 : 0)] = tot;
         }
     }
     __syncthreads();
@@ -1250,67 +1261,78 @@ __device__ __forceinline__ void stage(void* dst, const void* src, int bytes, int
     for (int o = tid * 16; o < bytes; o += POST_THREADS * 16) cp_async16((char*)dst + o, (const char*)src + o, true);
 }
 
-// The Kronecker passes: each thread a 4 x 4 tile of outputs (rows
-// r0..r0+3, columns c0..c0+3) of one CTA row, so that one j step is two
-// 16-byte shared loads for eight paired fmas; the factor's four values are
-// the same for the whole warp (a broadcast), the row's four vary by lane.
-// Every output is one fma chain over j = 0..31 from zero, as kron_native
-// (infer.rs:2442-2459) adds it. Row buffers are PV = 1160 floats apart so
-// that the four rows of a warp fall in different banks.
+// The Kronecker passes: 16 threads per CTA row, each an 8 x 8 tile of
+// outputs (rows r0..r0+7, columns c0..c0+7), so that one j step is four
+// 16-byte shared loads for 32 paired fmas. Every output is one fma chain
+// over j = 0..31 from zero, as kron_native (infer.rs:2442-2459) adds it.
+// Row buffers are PV = 1160 floats apart.
 // Pass 1: mt[c][r] = sum_j A[j][r] z[j][c] (A^T Z, stored transposed).
 __device__ __forceinline__ void kron_pass1(const float* A, const float* z, float* mt, int r0, int c0) {
-    float2 o[4][2];
+    float2 o[8][4];
 #pragma unroll
-    for (int a = 0; a < 4; a++) o[a][0] = o[a][1] = make_float2(0.f, 0.f);
-#pragma unroll 8
+    for (int a = 0; a < 8; a++)
+#pragma unroll
+        for (int b = 0; b < 4; b++) o[a][b] = make_float2(0.f, 0.f);
+#pragma unroll 2
     for (int j = 0; j < 32; j++) {
-        const float4 av = *(const float4*)(A + j * 32 + r0);
-        const float4 zv = *(const float4*)(z + j * 36 + c0);
-        const float2 z01 = make_float2(zv.x, zv.y), z23 = make_float2(zv.z, zv.w);
-        const float ar[4] = {av.x, av.y, av.z, av.w};
+        const float4 a0 = *(const float4*)(A + j * 32 + r0), a1 = *(const float4*)(A + j * 32 + r0 + 4);
+        const float4 z0 = *(const float4*)(z + j * 36 + c0), z1 = *(const float4*)(z + j * 36 + c0 + 4);
+        const float ar[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const float2 zp[4] = {make_float2(z0.x, z0.y), make_float2(z0.z, z0.w), make_float2(z1.x, z1.y), make_float2(z1.z, z1.w)};
 #pragma unroll
-        for (int a = 0; a < 4; a++) {
-            o[a][0] = fma2(make_float2(ar[a], ar[a]), z01, o[a][0]);
-            o[a][1] = fma2(make_float2(ar[a], ar[a]), z23, o[a][1]);
+        for (int a = 0; a < 8; a++)
+#pragma unroll
+            for (int b = 0; b < 4; b++) o[a][b] = fma2(make_float2(ar[a], ar[a]), zp[b], o[a][b]);
+    }
+#pragma unroll
+    for (int b = 0; b < 8; b++) {
+        float* dst = mt + (c0 + b) * 36 + r0;
+        const int bp = b >> 1;
+        if (b & 1) {
+            *(float4*)dst = make_float4(o[0][bp].y, o[1][bp].y, o[2][bp].y, o[3][bp].y);
+            *(float4*)(dst + 4) = make_float4(o[4][bp].y, o[5][bp].y, o[6][bp].y, o[7][bp].y);
+        } else {
+            *(float4*)dst = make_float4(o[0][bp].x, o[1][bp].x, o[2][bp].x, o[3][bp].x);
+            *(float4*)(dst + 4) = make_float4(o[4][bp].x, o[5][bp].x, o[6][bp].x, o[7][bp].x);
         }
     }
-    *(float4*)(mt + (c0 + 0) * 36 + r0) = make_float4(o[0][0].x, o[1][0].x, o[2][0].x, o[3][0].x);
-    *(float4*)(mt + (c0 + 1) * 36 + r0) = make_float4(o[0][0].y, o[1][0].y, o[2][0].y, o[3][0].y);
-    *(float4*)(mt + (c0 + 2) * 36 + r0) = make_float4(o[0][1].x, o[1][1].x, o[2][1].x, o[3][1].x);
-    *(float4*)(mt + (c0 + 3) * 36 + r0) = make_float4(o[0][1].y, o[1][1].y, o[2][1].y, o[3][1].y);
 }
 
 // Pass 2: t[r][c] = sum_j mt[j][r] B[j][c] ((A^T Z) B).
 __device__ __forceinline__ void kron_pass2(const float* mt, const float* B, float* t, int r0, int c0) {
-    float2 o[4][2];
+    float2 o[8][4];
 #pragma unroll
-    for (int a = 0; a < 4; a++) o[a][0] = o[a][1] = make_float2(0.f, 0.f);
-#pragma unroll 8
+    for (int a = 0; a < 8; a++)
+#pragma unroll
+        for (int b = 0; b < 4; b++) o[a][b] = make_float2(0.f, 0.f);
+#pragma unroll 2
     for (int j = 0; j < 32; j++) {
-        const float4 mv = *(const float4*)(mt + j * 36 + r0);
-        const float4 bv = *(const float4*)(B + j * 32 + c0);
-        const float2 b01 = make_float2(bv.x, bv.y), b23 = make_float2(bv.z, bv.w);
-        const float mr[4] = {mv.x, mv.y, mv.z, mv.w};
+        const float4 m0 = *(const float4*)(mt + j * 36 + r0), m1 = *(const float4*)(mt + j * 36 + r0 + 4);
+        const float4 b0 = *(const float4*)(B + j * 32 + c0), b1 = *(const float4*)(B + j * 32 + c0 + 4);
+        const float mr[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+        const float2 bp[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y), make_float2(b1.z, b1.w)};
 #pragma unroll
-        for (int a = 0; a < 4; a++) {
-            o[a][0] = fma2(make_float2(mr[a], mr[a]), b01, o[a][0]);
-            o[a][1] = fma2(make_float2(mr[a], mr[a]), b23, o[a][1]);
-        }
+        for (int a = 0; a < 8; a++)
+#pragma unroll
+            for (int b = 0; b < 4; b++) o[a][b] = fma2(make_float2(mr[a], mr[a]), bp[b], o[a][b]);
     }
 #pragma unroll
-    for (int a = 0; a < 4; a++) *(float4*)(t + (r0 + a) * 36 + c0) = make_float4(o[a][0].x, o[a][0].y, o[a][1].x, o[a][1].y);
+    for (int a = 0; a < 8; a++) {
+        float* dst = t + (r0 + a) * 36 + c0;
+        *(float4*)dst = make_float4(o[a][0].x, o[a][0].y, o[a][1].x, o[a][1].y);
+        *(float4*)(dst + 4) = make_float4(o[a][2].x, o[a][2].y, o[a][3].x, o[a][3].y);
+    }
 }
 
 // A Kronecker stage of every row: z in buf[from], result t in buf[from]
-// too (pass 1 writes mt into buf[1 - from]). Warp w serves rows
-// 4 (w / 8) .. 4 (w / 8) + 3, lane l row 4 (w / 8) + l / 8; in pass 1 the
-// warp shares r0 = 4 (w % 8) and the lane takes c0 = 4 (l % 8), in pass 2
-// the other way round.
+// too (pass 1 writes mt into buf[1 - from]). Threads 0-127: row t / 16;
+// the sixteen tiles of a row are spread so that the stores of a quarter
+// warp fall in different banks.
 __device__ __forceinline__ void kron_stage_rows(PostSmem& sm, int fa, int fb, int from, int tid) {
-    const int w = tid >> 5, ln = tid & 31, q = 4 * (w >> 3) + (ln >> 3), wu = 4 * (w & 7), lv = 4 * (ln & 7);
-    kron_pass1(sm.kf[fa], sm.buf[from][q], sm.buf[1 - from][q], wu, lv);
+    const int q = tid >> 4, i = tid & 15, lo = (i & 3) * 8, hi = (i >> 2) * 8;
+    if (tid < 128) kron_pass1(sm.kf[fa], sm.buf[from][q], sm.buf[1 - from][q], lo, hi);
     __syncthreads();
-    kron_pass2(sm.buf[1 - from][q], sm.kf[fb], sm.buf[from][q], lv, wu);
+    if (tid < 128) kron_pass2(sm.buf[1 - from][q], sm.kf[fb], sm.buf[from][q], hi, lo);
     __syncthreads();
 }
 
@@ -1451,9 +1473,8 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
     __syncthreads();
     // mHC write (infer.rs:1587-1606): y = x2 + mlp - u, stream a =
     // y * hpost[a] + sum_b old[b] * hres[a][b]. Four (row, channel) items a
-    // thread per round; the first round's 16 stream loads are issued before
-    // the last Kronecker stage, each later round's before the previous
-    // round's arithmetic.
+    // thread per round, each round's 16 stream loads issued before the
+    // previous round's arithmetic.
     constexpr int ITEMS = POST_ROWS * 768 / POST_THREADS, BATCH = 4;
     static_assert(ITEMS % BATCH == 0, "item batches");
     float cur[BATCH][4], nxt[BATCH][4];
@@ -1463,8 +1484,8 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
         const float* xr = xs + (size_t)(m0 + (q < rows ? q : 0)) * 3072 + ch;                         \
         _Pragma("unroll") for (int b = 0; b < 4; b++) dst[e][b] = xr[b * 768];                        \
     }
-    POST_LOAD_OLD(cur, 0)
     kron_stage_rows(sm, 4, 5, 0, tid);  // t3 in buf[0]
+    POST_LOAD_OLD(cur, 0)
     asm volatile("cp.async.wait_group 0;\n" ::);
     __syncthreads();
 #pragma unroll
