@@ -283,6 +283,35 @@ __device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem));
 }
 
+// fma.rn.f32x2: two independent IEEE fmas in one instruction (sm_100).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n.reg .b64 ra, rb, rc, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\nmov.b64 rc, {%6, %7};\n"
+        "fma.rn.f32x2 rd, ra, rb, rc;\nmov.b64 {%0, %1}, rd;\n}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
+// add.rn.f32x2 / sub.rn.f32x2: two independent IEEE adds (subtractions).
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n.reg .b64 ra, rb, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\n"
+        "add.rn.f32x2 rd, ra, rb;\nmov.b64 {%0, %1}, rd;\n}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n.reg .b64 ra, rb, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\n"
+        "sub.rn.f32x2 rd, ra, rb;\nmov.b64 {%0, %1}, rd;\n}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
 __device__ __forceinline__ float magic_to_float(int v) { return __fsub_rn(__int_as_float(v), 12582912.0f); }
 
 template <bool DECODE>
@@ -335,13 +364,17 @@ __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* 
         blk0 = ((m0 + r0) % T) < T / 4 * 4;
         blk1 = ((m0 + r1) % T) < T / 4 * 4;
     }
-    float acc[4][4][4];  // [n-tile][element][lane] (prefill uses lane 0)
+    float acc[4][4];       // prefill: [n-tile][element]
+    float2 accd[4][2][4];  // decode: [n-tile][row pair][lane], adjacent columns paired
 #pragma unroll
-    for (int j = 0; j < 4; j++)
+    for (int j = 0; j < 4; j++) {
 #pragma unroll
-        for (int e = 0; e < 4; e++)
+        for (int e = 0; e < 4; e++) acc[j][e] = 0.f;
 #pragma unroll
-            for (int l = 0; l < 4; l++) acc[j][e][l] = 0.f;
+        for (int pp = 0; pp < 2; pp++)
+#pragma unroll
+            for (int l = 0; l < 4; l++) accd[j][pp][l] = make_float2(0.f, 0.f);
+    }
     const int magic[4] = {MMA_MAGIC, MMA_MAGIC, MMA_MAGIC, MMA_MAGIC};
 #pragma unroll 1
     for (int g = 0; g < 6; g++) {
@@ -370,13 +403,15 @@ __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* 
                 int cn = wn + j * 8 + tig * 2 + h;
                 cs[j][h] = s_nrm[cn * 6 + g];
             }
-        // decode: (sx * cbs) * norm for each of this thread's outputs
-        float dsc[4][4];
+        // decode: (sx * cbs) * norm for each of this thread's outputs, as
+        // pairs of adjacent columns
+        float2 dsc[4][2];
         if (DECODE) {
 #pragma unroll
             for (int j = 0; j < 4; j++)
 #pragma unroll
-                for (int e = 0; e < 4; e++) dsc[j][e] = __fmul_rn(e < 2 ? rs0 : rs1, cs[j][e & 1]);
+                for (int pp = 0; pp < 2; pp++)
+                    dsc[j][pp] = make_float2(__fmul_rn(pp ? rs1 : rs0, cs[j][0]), __fmul_rn(pp ? rs1 : rs0, cs[j][1]));
         }
         int dsum[4][4];
 #pragma unroll
@@ -393,8 +428,12 @@ __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* 
                 int d[4];
                 if (DECODE) {
                     mma_s8(d, a, b, magic);
+                    const float2 mg = make_float2(12582912.0f, 12582912.0f);
 #pragma unroll
-                    for (int e = 0; e < 4; e++) acc[j][e][l] = __fmaf_rn(magic_to_float(d[e]), dsc[j][e], acc[j][e][l]);
+                    for (int pp = 0; pp < 2; pp++) {
+                        const float2 x = sub2(make_float2(__int_as_float(d[2 * pp]), __int_as_float(d[2 * pp + 1])), mg);
+                        accd[j][pp][l] = fma2(x, dsc[j][pp], accd[j][pp][l]);
+                    }
                 } else {
                     if (l == 0) {
                         mma_s8(d, a, b, magic);
@@ -417,19 +456,21 @@ __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* 
                     // block rows: (norm * cbs) * sx; remainder rows: norm * (cbs * sx)
                     float sc = blk ? __fmul_rn(s_nc[cn * 6 + g], e < 2 ? rs0 : rs1)
                                    : __fmul_rn(cs[j][e & 1], e < 2 ? rs0 : rs1);
-                    acc[j][e][0] = __fmaf_rn(magic_to_float(dsum[j][e]), sc, acc[j][e][0]);
+                    acc[j][e] = __fmaf_rn(magic_to_float(dsum[j][e]), sc, acc[j][e]);
                 }
         }
     }
 #pragma unroll
     for (int j = 0; j < 4; j++)
 #pragma unroll
-        for (int e = 0; e < 4; e++) {
-            const int m = m0 + (e < 2 ? r0 : r1), n = n0 + wn + j * 8 + tig * 2 + (e & 1);
-            if (m >= M || n >= W.out) continue;
-            float v = DECODE ? __fadd_rn(__fadd_rn(acc[j][e][0], acc[j][e][1]), __fadd_rn(acc[j][e][2], acc[j][e][3]))
-                             : acc[j][e][0];
-            y[(size_t)m * ldy + col0 + n] = v;
+        for (int pp = 0; pp < 2; pp++) {
+            // decode: the lanes summed (l0 + l1) + (l2 + l3)
+            float2 v = DECODE ? add2(add2(accd[j][pp][0], accd[j][pp][1]), add2(accd[j][pp][2], accd[j][pp][3]))
+                              : make_float2(acc[j][2 * pp], acc[j][2 * pp + 1]);
+            const int m = m0 + (pp ? r1 : r0), n = n0 + wn + j * 8 + tig * 2;
+            if (m >= M) continue;
+            if (n < W.out) y[(size_t)m * ldy + col0 + n] = v.x;
+            if (n + 1 < W.out) y[(size_t)m * ldy + col0 + n + 1] = v.y;
         }
 }
 
@@ -607,11 +648,12 @@ void launch_engram_conv(const float* taps, Caches c, int site, int nsites, int S
 
 // ------------------------------------------------------------ mHC read
 
-// The mHC read CTA: warps 0-5 (192 threads) each own 16 consecutive
-// elements of the row's 3072 and later run the input norm, synchronising
-// among themselves with a named barrier while warp 6 runs the Sinkhorn.
-constexpr int MHC_THREADS = 224, MHC_NORM_THREADS = 192, MHC_XS = 196;
-__device__ __forceinline__ void norm_bar() { asm volatile("bar.sync 1, 192;\n" ::: "memory"); }
+// The mHC read CTA: its six warps (192 threads) each own 16 consecutive
+// elements of the row's 3072 per thread; afterwards warp 5 runs the
+// Sinkhorn while warps 0-4 (160 threads) run the input norm, synchronising
+// among themselves with a named barrier.
+constexpr int MHC_THREADS = 192, MHC_NORM_THREADS = 160, MHC_XS = 196;
+__device__ __forceinline__ void norm_bar() { asm volatile("bar.sync 1, 160;\n" ::: "memory"); }
 
 // dot16_combine over lanes 0-15 of a warp (chain c in lane c); the total is
 // valid in lane 0. Every lane of the warp must call it.
@@ -642,12 +684,12 @@ __device__ __forceinline__ int reduce4_scatter(const int s[4], int ln) {
 // infer.rs:1359-1426 for one row per CTA. The lanes are normalized by one
 // rms and quantized to int8 (no rotation) in registers; the 24 int8 gate
 // dots are per-thread dp4a partials over 16-byte runs of the gate rows,
-// reduced exactly across the CTA. Then warp 6 runs the post block's gates
+// reduced exactly across the CTA. Then warp 5 runs the post block's gates
 // (hres by sinkhorn64, 2501-2525, and hpost; infer.rs:1580-1586) while warps
-// 0-5 form u from the pre gates, apply the engram gate (when the layer has a
+// 0-4 form u from the pre gates, apply the engram gate (when the layer has a
 // site: ekv [M][1536] keys, evals [M][768]), the input ZC-RMSNorm and A8 of
 // the normed row (act/sx for the q|k|v|gate matmul; x1o is the residual).
-__global__ void __launch_bounds__(MHC_THREADS) mhc_read_kernel(LayerW w, int lane_own, const float* xs, float* u, float* p,
+__global__ void __launch_bounds__(MHC_THREADS, 8) mhc_read_kernel(LayerW w, int lane_own, const float* xs, float* u, float* p,
                                                                   const float* ekv, const float* evals, float* x1o, int8_t* act,
                                                                   float* sx) {
     // the four streams chain-major: element e at (e % 16) * MHC_XS + e / 16,
@@ -662,18 +704,19 @@ __global__ void __launch_bounds__(MHC_THREADS) mhc_read_kernel(LayerW w, int lan
     __shared__ float hp[4];
     __shared__ float sc_s[4];
     const int m = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, ln = tid & 31;
-    const bool data = tid < MHC_NORM_THREADS;
     // the input norm's operands, fetched by the threads that will use them
-    if (data) {
-        cp_async16(nin + 4 * tid, w.norm_in + 4 * tid, true);
-        if (ekv) {
-            cp_async16(ek + 4 * tid, ekv + (size_t)m * 1536 + 4 * tid, true);
-            cp_async16(ev + 4 * tid, evals + (size_t)m * 768 + 4 * tid, true);
+    if (tid < MHC_NORM_THREADS) {
+        for (int k = tid; k < 192; k += MHC_NORM_THREADS) {
+            cp_async16(nin + 4 * k, w.norm_in + 4 * k, true);
+            if (ekv) {
+                cp_async16(ek + 4 * k, ekv + (size_t)m * 1536 + 4 * k, true);
+                cp_async16(ev + 4 * k, evals + (size_t)m * 768 + 4 * k, true);
+            }
         }
     }
     asm volatile("cp.async.commit_group;\n" ::);
     float v[16];
-    if (data) {
+    {
         const float4* xr = (const float4*)(xs + (size_t)m * 3072) + 4 * tid;
 #pragma unroll
         for (int i = 0; i < 4; i++) {
@@ -706,7 +749,7 @@ __global__ void __launch_bounds__(MHC_THREADS) mhc_read_kernel(LayerW w, int lan
     __syncthreads();
     const float r = sc_s[0];
     float a = 0.f;
-    if (data) {
+    {
 #pragma unroll
         for (int k = 0; k < 16; k++) {
             v[k] = __fmul_rn(v[k], r);
@@ -720,7 +763,7 @@ __global__ void __launch_bounds__(MHC_THREADS) mhc_read_kernel(LayerW w, int lan
 #pragma unroll
     for (int k = 1; k < 6; k++) mx = fmaxf(mx, red[k]);
     const float sxv = mx > 0.f ? __fmul_rn(mx, ND_K127) : 1.0f;
-    if (data) {
+    {
         const float inv = __fdiv_rn(1.0f, sxv);
         int wd[4];
 #pragma unroll
@@ -744,7 +787,7 @@ __global__ void __launch_bounds__(MHC_THREADS) mhc_read_kernel(LayerW w, int lan
         }
     }
     __syncthreads();
-    if (warp == 6) {
+    if (warp == 5) {
         // hpost (lanes 16-19) and the 4x4 Sinkhorn in f64, lanes 0-15 one
         // element each: the pairwise row and column sums are xor-shuffles,
         // which add (e0 + e1) + (e2 + e3) as the reference does
@@ -781,7 +824,7 @@ __global__ void __launch_bounds__(MHC_THREADS) mhc_read_kernel(LayerW w, int lan
         if (ln < 16) p[(size_t)m * 24 + 4 + ln] = (float)e;
         return;
     }
-    const int lt = tid;  // 0..191
+    const int lt = tid;  // 0..159
     if (lt < 4) {
         int tot = 0;
 #pragma unroll
@@ -842,11 +885,11 @@ __global__ void __launch_bounds__(MHC_THREADS) mhc_read_kernel(LayerW w, int lan
         na[k] = __fmaf_rn(t, nin[k], t);
     }
     norm_bar();
-    {
+    for (int gw = warp; gw < 6; gw += 5) {
         float vv[4];
 #pragma unroll
-        for (int k = 0; k < 4; k++) vv[k] = na[warp * 128 + 4 * ln + k];
-        prep_group_warp(vv, ln, act + ((size_t)m * 6 + warp) * 128, sx + (size_t)m * 6 + warp);
+        for (int k = 0; k < 4; k++) vv[k] = na[gw * 128 + 4 * ln + k];
+        prep_group_warp(vv, ln, act + ((size_t)m * 6 + gw) * 128, sx + (size_t)m * 6 + gw);
     }
 }
 
@@ -874,24 +917,39 @@ __global__ void __launch_bounds__(512) conv_rope_kv_kernel(LayerW w, int l, cons
     else { int vh = unit - 14; start = 672 + vh * 64; cw = 128; cc = vh * 64; len = 64; wt = w.v_taps; }
     const size_t hrow0 = ((size_t)s * c.L + l) * HIST_RING;
     float* x = buf[unit];
-    for (int k = lane; k < len; k += 32) {
-        float cur = proj[(size_t)m * 1568 + start + k];
-        // this row's pre-tap value joins the history (infer.rs:1486-1488);
-        // its slot is none of the two that rows 0 and 1 read below
-        c.hist[(hrow0 + pos % HIST_RING) * 800 + start + k] = cur;
-        float o = __fmul_rn(wt[cc + k], cur);
-        for (int j = 1; j < 3; j++) {
-            float wj = wt[j * cw + cc + k];
-            int pj = pos - j;
-            if (i - j >= 0) {
-                o = __fmaf_rn(wj, proj[(size_t)(m - j) * 1568 + start + k], o);
-            } else if (pj >= hist_base && pj >= 0) {
-                o = __fmaf_rn(wj, c.hist[(hrow0 + pj % HIST_RING) * 800 + start + k], o);
-            } else {
-                o = __fmaf_rn(wj, 0.0f, o);
+    // every load of the lane's (at most two) channels first, then the
+    // history write and the taps
+    float cur[2], prev[2][2], wv[2][3];
+#pragma unroll
+    for (int t = 0; t < 2; t++) {
+        const int k = lane + 32 * t;
+        cur[t] = 0.f;
+        prev[t][0] = prev[t][1] = 0.f;
+        wv[t][0] = wv[t][1] = wv[t][2] = 0.f;
+        if (k < len) {
+            cur[t] = proj[(size_t)m * 1568 + start + k];
+#pragma unroll
+            for (int j = 0; j < 3; j++) wv[t][j] = wt[j * cw + cc + k];
+#pragma unroll
+            for (int j = 1; j < 3; j++) {
+                const int pj = pos - j;
+                if (i - j >= 0) prev[t][j - 1] = proj[(size_t)(m - j) * 1568 + start + k];
+                else if (pj >= hist_base && pj >= 0) prev[t][j - 1] = c.hist[(hrow0 + pj % HIST_RING) * 800 + start + k];
             }
         }
-        x[k] = o;
+    }
+#pragma unroll
+    for (int t = 0; t < 2; t++) {
+        const int k = lane + 32 * t;
+        if (k < len) {
+            // this row's pre-tap value joins the history (infer.rs:1486-1488);
+            // its slot is none of the two that rows 0 and 1 read
+            c.hist[(hrow0 + pos % HIST_RING) * 800 + start + k] = cur[t];
+            float o = __fmul_rn(wv[t][0], cur[t]);
+            o = __fmaf_rn(wv[t][1], prev[t][0], o);  // zero where no earlier row exists
+            o = __fmaf_rn(wv[t][2], prev[t][1], o);
+            x[k] = o;
+        }
     }
     __syncwarp();
     if (unit < 14) {
@@ -1217,15 +1275,6 @@ void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int
 
 // ------------------------------------------------------------ post block
 
-// fma.rn.f32x2: two independent IEEE fmas in one instruction (sm_100).
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
-    float2 d;
-    asm("{\n.reg .b64 ra, rb, rc, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\nmov.b64 rc, {%6, %7};\n"
-        "fma.rn.f32x2 rd, ra, rb, rc;\nmov.b64 {%0, %1}, rd;\n}"
-        : "=f"(d.x), "=f"(d.y)
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-    return d;
-}
 
 // infer.rs:1564-1606 with mlp_native (1610-1634), cond_weights (1640-1694),
 // perm_fma (689-713), silu (2463-2496) and kron_native / mix8 (2322-2460).
