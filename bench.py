@@ -43,7 +43,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--seqs", type=int, default=1024, help="sequences per GPU")
-    ap.add_argument("--roofline-site", default="auto")
+    ap.add_argument("--roofline-site", default="attention",
+                    help="the kernel site the roofline object reports (auto: the slowest in the sweep)")
     ap.add_argument("--cpu-baseline", type=int, default=1, help="time the oracle on rank 0 (N=1 only)")
     ap.add_argument("--secondary", type=int, default=1, help="also time batch-1 decode and 256x700 prefill (N=1)")
     ap.add_argument("--profile", action="store_true",
@@ -139,6 +140,19 @@ def peaks():
         return p["hbm_gbs"], p["bf16_tflops"], "measured"
     except Exception:
         return 6650.0, 1590.0, "fallback"
+
+
+# DRAM traffic of one decode launch from one ncu capture of
+# `bench.py --profile --seqs 1024 --warmup 2` (dram__bytes_read.sum +
+# dram__bytes_write.sum; profiles/<kernel>_decode_1024.md), with the
+# algorithmic bytes of that launch: the roofline scales the traffic to this
+# run's launch by the ratio of algorithmic bytes (sequences and keys).
+PROFILED_TRAFFIC = {
+    "attention": (35_295_744, 37_896_192),
+    "post": (22_288_896, 40_992_768),
+    "qkvg": (2_047_744, 7_854_464),
+    "mhc": (12_709_120, 19_857_408),
+}
 
 
 def site_algorithmic(site, S, n_keys):
@@ -382,10 +396,21 @@ def main():
         amount, unit, bound = site_algorithmic(site, S, n_keys)
         avg_s = site_ms / 1e3 / max(site_n, 1)
         achieved = amount / avg_s / 1e9
+        traffic = None
+        if site in PROFILED_TRAFFIC:
+            dram, alg = PROFILED_TRAFFIC[site]
+            traffic = dram * amount / alg
         roofline = {"bound": bound, "kernel_site": site, "achieved": achieved, "peak": hbm,
                     "unit": "GB/s", "frac": achieved / hbm, "peak_kind": kind,
                     "algorithmic_bytes_per_launch": amount, "avg_launch_us": avg_s * 1e6, "launches": site_n,
-                    "traffic": None}
+                    "traffic": traffic}
+        # every site of the sweep (one step each, batch B at position PROMPT + k)
+        per_site = {}
+        for k, (nm, v) in enumerate(sweep.items()):
+            amt, _, _ = site_algorithmic(nm, S, PROMPT + k + 1)
+            us = v["ms_per_step"] * 1e3 / max(v["launches"], 1)
+            per_site[nm] = {"ms_per_step": round(v["ms_per_step"], 4), "us_per_launch": round(us, 2),
+                            "achieved_gbs": round(amt / (us * 1e-6) / 1e9, 1), "frac": round(amt / (us * 1e-6) / 1e9 / hbm, 4)}
         cpu = None
         if args.cpu_baseline and world == 1:
             cpu = cpu_baseline_sample(data)
@@ -403,7 +428,7 @@ def main():
                     "d2h_bytes_per_step": S * 4},
             "gpu_launches": int(launches),
             "roofline": roofline,
-            "sites_ms_per_step": {k: round(v["ms_per_step"], 4) for k, v in sweep.items()},
+            "sites": per_site,
             "cpu_baseline": cpu,
             "clocks": clk,
             "secondary": extra,
