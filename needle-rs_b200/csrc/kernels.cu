@@ -252,7 +252,7 @@ static const size_t GEMM_SMEM = (GEMM_TN + GEMM_TM) * GEMM_LD + (GEMM_TM + GEMM_
 // first groups compute while the rest arrive.
 constexpr int MMA_BM = 64, MMA_BN = 64, MMA_K = 768, MMA_LD = MMA_K + 16;
 constexpr int MMA_MAGIC = 0x4B400000;
-constexpr size_t MMA_SMEM = (size_t)(MMA_BM + MMA_BN) * MMA_LD + (size_t)(2 * MMA_BM + 2 * MMA_BN) * 6 * 4;
+constexpr size_t MMA_SMEM = (size_t)(MMA_BM + MMA_BN) * MMA_LD + (size_t)2 * MMA_BM * 6 * 4 + (size_t)2 * MMA_BN * 6 * 2;
 
 __device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2], const int (&c)[4]) {
     asm(
@@ -314,56 +314,66 @@ __device__ __forceinline__ float2 sub2(float2 a, float2 b) {
 
 __device__ __forceinline__ float magic_to_float(int v) { return __fsub_rn(__int_as_float(v), 12582912.0f); }
 
+__device__ __forceinline__ void cp_async4z(void* smem, const void* gmem, bool valid) {
+    uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+    int n = valid ? 4 : 0;
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gmem), "r"(n));
+}
+
+// Persistent: CTA b takes tiles b, b + grid, ... (n-tile fastest). Its
+// iterations k run group k % 6 of tile k / 6; the copies of iteration k + 5
+// are issued at iteration k into the slot iteration k - 1 has just freed, so
+// the next tile's operands arrive while this one computes. A tile's scales
+// (activation sx, f16 norms) come with its group 0 into one of two buffers.
 template <bool DECODE>
 __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y,
                                                         int ldy, int col0) {
     extern __shared__ __align__(16) int8_t smem[];
-    int8_t* ws = smem;                                  // [BN][LD]
-    int8_t* as = smem + MMA_BN * MMA_LD;                // [BM][LD]
-    float* s_sx = (float*)(as + MMA_BM * MMA_LD);       // [BM][6] sx
-    float* s_sxc = s_sx + MMA_BM * 6;                   // [BM][6] sx * cbs
-    float* s_nrm = s_sxc + MMA_BM * 6;                  // [BN][6] norm
-    float* s_nc = s_nrm + MMA_BN * 6;                   // [BN][6] norm * cbs
+    int8_t* ws = smem;                                        // [BN][LD]
+    int8_t* as = smem + MMA_BN * MMA_LD;                      // [BM][LD]
+    float* s_sx = (float*)(as + MMA_BM * MMA_LD);             // [2][BM][6]
+    uint16_t* s_nr = (uint16_t*)(s_sx + 2 * MMA_BM * 6);      // [2][BN][6] f16
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n0 = blockIdx.x * MMA_BN, m0 = blockIdx.y * MMA_BM;
-    // cp.async: group g of every row of both tiles (8 x 16 B per row)
-    for (int g = 0; g < 6; g++) {
-        for (int idx = tid; idx < (MMA_BN + MMA_BM) * 8; idx += 256) {
-            int r = idx >> 3, c = idx & 7;
-            if (r < MMA_BN) {
-                int n = n0 + r;
-                bool ok = n < W.out;
-                cp_async16(ws + r * MMA_LD + g * 128 + c * 16, W.w8 + (size_t)(ok ? n : 0) * MMA_K + g * 128 + c * 16, ok);
-            } else {
-                int mr = r - MMA_BN, m = m0 + mr;
-                bool ok = m < M;
-                cp_async16(as + mr * MMA_LD + g * 128 + c * 16, act + (size_t)(ok ? m : 0) * MMA_K + g * 128 + c * 16, ok);
+    const int tilesN = (W.out + MMA_BN - 1) / MMA_BN, ntiles = tilesN * ((M + MMA_BM - 1) / MMA_BM);
+    const int first = blockIdx.x, stride = gridDim.x;
+    const int iters = first < ntiles ? ((ntiles - 1 - first) / stride + 1) * 6 : 0;
+    auto issue = [&](int k) {
+        if (k < iters) {
+            const int t = first + (k / 6) * stride, g = k % 6;
+            const int tn0 = (t % tilesN) * MMA_BN, tm0 = (t / tilesN) * MMA_BM;
+            for (int idx = tid; idx < (MMA_BN + MMA_BM) * 8; idx += 256) {
+                int r = idx >> 3, c = idx & 7;
+                if (r < MMA_BN) {
+                    int n = tn0 + r;
+                    bool ok = n < W.out;
+                    cp_async16(ws + r * MMA_LD + g * 128 + c * 16, W.w8 + (size_t)(ok ? n : 0) * MMA_K + g * 128 + c * 16, ok);
+                } else {
+                    int mr = r - MMA_BN, m = tm0 + mr;
+                    bool ok = m < M;
+                    cp_async16(as + mr * MMA_LD + g * 128 + c * 16, act + (size_t)(ok ? m : 0) * MMA_K + g * 128 + c * 16, ok);
+                }
+            }
+            if (g == 0) {
+                float* bx = s_sx + ((k / 6) & 1) * MMA_BM * 6;
+                uint16_t* bn = s_nr + ((k / 6) & 1) * MMA_BN * 6;
+                for (int idx = tid; idx < MMA_BM * 6; idx += 256) {
+                    const int m = tm0 + idx / 6;
+                    cp_async4z(bx + idx, sx + (size_t)(m < M ? m : 0) * 6 + idx % 6, m < M);
+                }
+                for (int idx = tid; idx < MMA_BN * 3; idx += 256) {
+                    const int n = tn0 + idx / 3;
+                    cp_async4z(bn + 2 * idx, W.norms + (size_t)(n < W.out ? n : 0) * 6 + 2 * (idx % 3), n < W.out);
+                }
             }
         }
         asm volatile("cp.async.commit_group;\n" ::);
-    }
+    };
+#pragma unroll 1
+    for (int k = 0; k < 5; k++) issue(k);
     const float cbs = c_cbs;
-    for (int idx = tid; idx < MMA_BM * 6; idx += 256) {
-        int m = m0 + idx / 6;
-        float v = m < M ? sx[(size_t)m * 6 + idx % 6] : 0.f;
-        s_sx[idx] = v;
-        s_sxc[idx] = __fmul_rn(v, cbs);
-    }
-    for (int idx = tid; idx < MMA_BN * 6; idx += 256) {
-        int n = n0 + idx / 6;
-        float v = n < W.out ? h2f(W.norms[(size_t)n * 6 + idx % 6]) : 0.f;
-        s_nrm[idx] = v;
-        s_nc[idx] = __fmul_rn(v, cbs);
-    }
     const int wm = (warp & 3) * 16, wn = (warp >> 2) * 32;
     const int gid = lane >> 2, tig = lane & 3;
     const int r0 = wm + gid, r1 = r0 + 8;  // this thread's two rows in the tile
-    // per-row combine of the prefill kernel: block rows t < T/4*4
-    bool blk0 = true, blk1 = true;
-    if (!DECODE) {
-        blk0 = ((m0 + r0) % T) < T / 4 * 4;
-        blk1 = ((m0 + r1) % T) < T / 4 * 4;
-    }
     float acc[4][4];       // prefill: [n-tile][element]
     float2 accd[4][2][4];  // decode: [n-tile][row pair][lane], adjacent columns paired
 #pragma unroll
@@ -376,33 +386,40 @@ __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* 
             for (int l = 0; l < 4; l++) accd[j][pp][l] = make_float2(0.f, 0.f);
     }
     const int magic[4] = {MMA_MAGIC, MMA_MAGIC, MMA_MAGIC, MMA_MAGIC};
+    int n0 = 0, m0 = 0;
+    bool blk0 = true, blk1 = true;  // prefill: block rows t < T/4*4
+    const float* tsx = s_sx;
+    const uint16_t* tnr = s_nr;
 #pragma unroll 1
-    for (int g = 0; g < 6; g++) {
-        switch (g) {  // wait for group g's bytes (5 - g groups may stay in flight)
-            case 0: asm volatile("cp.async.wait_group 5;\n" ::); break;
-            case 1: asm volatile("cp.async.wait_group 4;\n" ::); break;
-            case 2: asm volatile("cp.async.wait_group 3;\n" ::); break;
-            case 3: asm volatile("cp.async.wait_group 2;\n" ::); break;
-            case 4: asm volatile("cp.async.wait_group 1;\n" ::); break;
-            default: asm volatile("cp.async.wait_group 0;\n" ::); break;
-        }
+    for (int k = 0; k < iters; k++) {
+        const int g = k % 6;
+        asm volatile("cp.async.wait_group 4;\n" ::);
         __syncthreads();
+        issue(k + 5);
+        if (g == 0) {
+            const int t = first + (k / 6) * stride;
+            n0 = (t % tilesN) * MMA_BN;
+            m0 = (t / tilesN) * MMA_BM;
+            tsx = s_sx + ((k / 6) & 1) * MMA_BM * 6;
+            tnr = s_nr + ((k / 6) & 1) * MMA_BN * 6;
+            if (!DECODE) {
+                blk0 = ((m0 + r0) % T) < T / 4 * 4;
+                blk1 = ((m0 + r1) % T) < T / 4 * 4;
+            }
+        }
         // scales of this group for this thread's rows and columns
         float rs0, rs1, cs[4][2];
         if (DECODE) {
-            rs0 = s_sxc[r0 * 6 + g];
-            rs1 = s_sxc[r1 * 6 + g];
+            rs0 = __fmul_rn(tsx[r0 * 6 + g], cbs);
+            rs1 = __fmul_rn(tsx[r1 * 6 + g], cbs);
         } else {
-            rs0 = blk0 ? s_sx[r0 * 6 + g] : s_sxc[r0 * 6 + g];
-            rs1 = blk1 ? s_sx[r1 * 6 + g] : s_sxc[r1 * 6 + g];
+            rs0 = blk0 ? tsx[r0 * 6 + g] : __fmul_rn(tsx[r0 * 6 + g], cbs);
+            rs1 = blk1 ? tsx[r1 * 6 + g] : __fmul_rn(tsx[r1 * 6 + g], cbs);
         }
 #pragma unroll
         for (int j = 0; j < 4; j++)
 #pragma unroll
-            for (int h = 0; h < 2; h++) {
-                int cn = wn + j * 8 + tig * 2 + h;
-                cs[j][h] = s_nrm[cn * 6 + g];
-            }
+            for (int h = 0; h < 2; h++) cs[j][h] = h2f(tnr[(wn + j * 8 + tig * 2 + h) * 6 + g]);
         // decode: (sx * cbs) * norm for each of this thread's outputs, as
         // pairs of adjacent columns
         float2 dsc[4][2];
@@ -452,26 +469,31 @@ __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* 
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
                     const bool blk = e < 2 ? blk0 : blk1;
-                    const int cn = wn + j * 8 + tig * 2 + (e & 1);
                     // block rows: (norm * cbs) * sx; remainder rows: norm * (cbs * sx)
-                    float sc = blk ? __fmul_rn(s_nc[cn * 6 + g], e < 2 ? rs0 : rs1)
+                    float sc = blk ? __fmul_rn(__fmul_rn(cs[j][e & 1], cbs), e < 2 ? rs0 : rs1)
                                    : __fmul_rn(cs[j][e & 1], e < 2 ? rs0 : rs1);
                     acc[j][e] = __fmaf_rn(magic_to_float(dsum[j][e]), sc, acc[j][e]);
                 }
         }
-    }
+        if (g == 5) {
 #pragma unroll
-    for (int j = 0; j < 4; j++)
+            for (int j = 0; j < 4; j++)
 #pragma unroll
-        for (int pp = 0; pp < 2; pp++) {
-            // decode: the lanes summed (l0 + l1) + (l2 + l3)
-            float2 v = DECODE ? add2(add2(accd[j][pp][0], accd[j][pp][1]), add2(accd[j][pp][2], accd[j][pp][3]))
-                              : make_float2(acc[j][2 * pp], acc[j][2 * pp + 1]);
-            const int m = m0 + (pp ? r1 : r0), n = n0 + wn + j * 8 + tig * 2;
-            if (m >= M) continue;
-            if (n < W.out) y[(size_t)m * ldy + col0 + n] = v.x;
-            if (n + 1 < W.out) y[(size_t)m * ldy + col0 + n + 1] = v.y;
+                for (int pp = 0; pp < 2; pp++) {
+                    // decode: the lanes summed (l0 + l1) + (l2 + l3)
+                    float2 v = DECODE ? add2(add2(accd[j][pp][0], accd[j][pp][1]), add2(accd[j][pp][2], accd[j][pp][3]))
+                                      : make_float2(acc[j][2 * pp], acc[j][2 * pp + 1]);
+                    const int m = m0 + (pp ? r1 : r0), n = n0 + wn + j * 8 + tig * 2;
+                    if (m < M) {
+                        if (n < W.out) y[(size_t)m * ldy + col0 + n] = v.x;
+                        if (n + 1 < W.out) y[(size_t)m * ldy + col0 + n + 1] = v.y;
+                    }
+#pragma unroll
+                    for (int l = 0; l < 4; l++) accd[j][pp][l] = make_float2(0.f, 0.f);
+                    acc[j][2 * pp] = acc[j][2 * pp + 1] = 0.f;
+                }
         }
+    }
 }
 
 // ------------------------------------------------ CQ matvec (decode, few rows)
@@ -546,7 +568,12 @@ void launch_cq_gemm(DevMat W, const int8_t* act, const float* sx, int M, int T, 
         return;
     }
     if (W.w8 && W.groups == 6) {
-        dim3 grid(cdiv(W.out, MMA_BN), cdiv(M, MMA_BM));
+        static int sms[64];
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev < 64 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+        const int per = dev < 64 && sms[dev] ? 2 * sms[dev] : 296;
+        const int grid = std::min(cdiv(W.out, MMA_BN) * cdiv(M, MMA_BM), per);
         if (T == 1)
             cq_mma_kernel<true><<<grid, 256, MMA_SMEM, st>>>(W, act, sx, M, T, y, ldy, col0);
         else
