@@ -312,6 +312,25 @@ __device__ __forceinline__ float2 sub2(float2 a, float2 b) {
     return d;
 }
 
+// The decode lane update for two adjacent outputs of one mma: the two int32
+// sums (accumulated from the magic 1.5 * 2^23) become floats with one
+// paired subtraction and join their lane chains with one paired fma. The
+// pairs stay packed in 64-bit registers.
+__device__ __forceinline__ void lane_fma2(unsigned long long& acc, int d0, int d1, unsigned long long sc) {
+    const unsigned long long mg = 0x4B4000004B400000ull;  // 12582912.0f twice
+    asm("{\n.reg .b64 x;\nmov.b64 x, {%1, %2};\nsub.rn.f32x2 x, x, %4;\nfma.rn.f32x2 %0, x, %3, %0;\n}"
+        : "+l"(acc)
+        : "r"(d0), "r"(d1), "l"(sc), "l"(mg));
+}
+
+__device__ __forceinline__ unsigned long long pack2(float a, float b) {
+    return (unsigned long long)__float_as_uint(a) | ((unsigned long long)__float_as_uint(b) << 32);
+}
+
+__device__ __forceinline__ float2 unpack2(unsigned long long v) {
+    return make_float2(__uint_as_float((unsigned)v), __uint_as_float((unsigned)(v >> 32)));
+}
+
 __device__ __forceinline__ float magic_to_float(int v) { return __fsub_rn(__int_as_float(v), 12582912.0f); }
 
 __device__ __forceinline__ void cp_async4z(void* smem, const void* gmem, bool valid) {
@@ -375,7 +394,7 @@ __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* 
     const int gid = lane >> 2, tig = lane & 3;
     const int r0 = wm + gid, r1 = r0 + 8;  // this thread's two rows in the tile
     float acc[4][4];       // prefill: [n-tile][element]
-    float2 accd[4][2][4];  // decode: [n-tile][row pair][lane], adjacent columns paired
+    unsigned long long accd[4][2][4];  // decode: [n-tile][row pair][lane], adjacent columns packed
 #pragma unroll
     for (int j = 0; j < 4; j++) {
 #pragma unroll
@@ -383,7 +402,7 @@ __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* 
 #pragma unroll
         for (int pp = 0; pp < 2; pp++)
 #pragma unroll
-            for (int l = 0; l < 4; l++) accd[j][pp][l] = make_float2(0.f, 0.f);
+            for (int l = 0; l < 4; l++) accd[j][pp][l] = 0ull;
     }
     const int magic[4] = {MMA_MAGIC, MMA_MAGIC, MMA_MAGIC, MMA_MAGIC};
     int n0 = 0, m0 = 0;
@@ -422,13 +441,13 @@ __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* 
             for (int h = 0; h < 2; h++) cs[j][h] = h2f(tnr[(wn + j * 8 + tig * 2 + h) * 6 + g]);
         // decode: (sx * cbs) * norm for each of this thread's outputs, as
         // pairs of adjacent columns
-        float2 dsc[4][2];
+        unsigned long long dsc[4][2];
         if (DECODE) {
 #pragma unroll
             for (int j = 0; j < 4; j++)
 #pragma unroll
                 for (int pp = 0; pp < 2; pp++)
-                    dsc[j][pp] = make_float2(__fmul_rn(pp ? rs1 : rs0, cs[j][0]), __fmul_rn(pp ? rs1 : rs0, cs[j][1]));
+                    dsc[j][pp] = pack2(__fmul_rn(pp ? rs1 : rs0, cs[j][0]), __fmul_rn(pp ? rs1 : rs0, cs[j][1]));
         }
         int dsum[4][4];
 #pragma unroll
@@ -445,12 +464,8 @@ __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* 
                 int d[4];
                 if (DECODE) {
                     mma_s8(d, a, b, magic);
-                    const float2 mg = make_float2(12582912.0f, 12582912.0f);
-#pragma unroll
-                    for (int pp = 0; pp < 2; pp++) {
-                        const float2 x = sub2(make_float2(__int_as_float(d[2 * pp]), __int_as_float(d[2 * pp + 1])), mg);
-                        accd[j][pp][l] = fma2(x, dsc[j][pp], accd[j][pp][l]);
-                    }
+                    lane_fma2(accd[j][0][l], d[0], d[1], dsc[j][0]);
+                    lane_fma2(accd[j][1][l], d[2], d[3], dsc[j][1]);
                 } else {
                     if (l == 0) {
                         mma_s8(d, a, b, magic);
@@ -481,7 +496,8 @@ __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* 
 #pragma unroll
                 for (int pp = 0; pp < 2; pp++) {
                     // decode: the lanes summed (l0 + l1) + (l2 + l3)
-                    float2 v = DECODE ? add2(add2(accd[j][pp][0], accd[j][pp][1]), add2(accd[j][pp][2], accd[j][pp][3]))
+                    float2 v = DECODE ? add2(add2(unpack2(accd[j][pp][0]), unpack2(accd[j][pp][1])),
+                                             add2(unpack2(accd[j][pp][2]), unpack2(accd[j][pp][3])))
                                       : make_float2(acc[j][2 * pp], acc[j][2 * pp + 1]);
                     const int m = m0 + (pp ? r1 : r0), n = n0 + wn + j * 8 + tig * 2;
                     if (m < M) {
@@ -489,7 +505,7 @@ __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* 
                         if (n + 1 < W.out) y[(size_t)m * ldy + col0 + n + 1] = v.y;
                     }
 #pragma unroll
-                    for (int l = 0; l < 4; l++) accd[j][pp][l] = make_float2(0.f, 0.f);
+                    for (int l = 0; l < 4; l++) accd[j][pp][l] = 0ull;
                     acc[j][2 * pp] = acc[j][2 * pp + 1] = 0.f;
                 }
         }
@@ -1337,63 +1353,57 @@ __device__ __forceinline__ void stage(void* dst, const void* src, int bytes, int
     for (int o = tid * 16; o < bytes; o += POST_THREADS * 16) cp_async16((char*)dst + o, (const char*)src + o, true);
 }
 
-// The Kronecker passes: 16 threads per CTA row, each an 8 x 8 tile of
-// outputs (rows r0..r0+7, columns c0..c0+7), so that one j step is four
-// 16-byte shared loads for 32 paired fmas. Every output is one fma chain
-// over j = 0..31 from zero, as kron_native (infer.rs:2442-2459) adds it.
-// Row buffers are PV = 1160 floats apart.
+// The Kronecker passes: 32 threads (one warp) per CTA row, each a 4 x 8
+// tile of outputs (rows r0..r0+3, columns c0..c0+7), so that one j step is
+// three 16-byte shared loads for 16 paired fmas. Every output is one fma
+// chain over j = 0..31 from zero, as kron_native (infer.rs:2442-2459) adds
+// it. Row buffers are PV = 1160 floats apart.
 // Pass 1: mt[c][r] = sum_j A[j][r] z[j][c] (A^T Z, stored transposed).
 __device__ __forceinline__ void kron_pass1(const float* A, const float* z, float* mt, int r0, int c0) {
-    float2 o[8][4];
+    float2 o[4][4];
 #pragma unroll
-    for (int a = 0; a < 8; a++)
+    for (int a = 0; a < 4; a++)
 #pragma unroll
         for (int b = 0; b < 4; b++) o[a][b] = make_float2(0.f, 0.f);
-#pragma unroll 2
+#pragma unroll 4
     for (int j = 0; j < 32; j++) {
-        const float4 a0 = *(const float4*)(A + j * 32 + r0), a1 = *(const float4*)(A + j * 32 + r0 + 4);
+        const float4 a0 = *(const float4*)(A + j * 32 + r0);
         const float4 z0 = *(const float4*)(z + j * 36 + c0), z1 = *(const float4*)(z + j * 36 + c0 + 4);
-        const float ar[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const float ar[4] = {a0.x, a0.y, a0.z, a0.w};
         const float2 zp[4] = {make_float2(z0.x, z0.y), make_float2(z0.z, z0.w), make_float2(z1.x, z1.y), make_float2(z1.z, z1.w)};
 #pragma unroll
-        for (int a = 0; a < 8; a++)
+        for (int a = 0; a < 4; a++)
 #pragma unroll
             for (int b = 0; b < 4; b++) o[a][b] = fma2(make_float2(ar[a], ar[a]), zp[b], o[a][b]);
     }
 #pragma unroll
     for (int b = 0; b < 8; b++) {
-        float* dst = mt + (c0 + b) * 36 + r0;
         const int bp = b >> 1;
-        if (b & 1) {
-            *(float4*)dst = make_float4(o[0][bp].y, o[1][bp].y, o[2][bp].y, o[3][bp].y);
-            *(float4*)(dst + 4) = make_float4(o[4][bp].y, o[5][bp].y, o[6][bp].y, o[7][bp].y);
-        } else {
-            *(float4*)dst = make_float4(o[0][bp].x, o[1][bp].x, o[2][bp].x, o[3][bp].x);
-            *(float4*)(dst + 4) = make_float4(o[4][bp].x, o[5][bp].x, o[6][bp].x, o[7][bp].x);
-        }
+        *(float4*)(mt + (c0 + b) * 36 + r0) = (b & 1) ? make_float4(o[0][bp].y, o[1][bp].y, o[2][bp].y, o[3][bp].y)
+                                                      : make_float4(o[0][bp].x, o[1][bp].x, o[2][bp].x, o[3][bp].x);
     }
 }
 
 // Pass 2: t[r][c] = sum_j mt[j][r] B[j][c] ((A^T Z) B).
 __device__ __forceinline__ void kron_pass2(const float* mt, const float* B, float* t, int r0, int c0) {
-    float2 o[8][4];
+    float2 o[4][4];
 #pragma unroll
-    for (int a = 0; a < 8; a++)
+    for (int a = 0; a < 4; a++)
 #pragma unroll
         for (int b = 0; b < 4; b++) o[a][b] = make_float2(0.f, 0.f);
-#pragma unroll 2
+#pragma unroll 4
     for (int j = 0; j < 32; j++) {
-        const float4 m0 = *(const float4*)(mt + j * 36 + r0), m1 = *(const float4*)(mt + j * 36 + r0 + 4);
+        const float4 m0 = *(const float4*)(mt + j * 36 + r0);
         const float4 b0 = *(const float4*)(B + j * 32 + c0), b1 = *(const float4*)(B + j * 32 + c0 + 4);
-        const float mr[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+        const float mr[4] = {m0.x, m0.y, m0.z, m0.w};
         const float2 bp[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y), make_float2(b1.z, b1.w)};
 #pragma unroll
-        for (int a = 0; a < 8; a++)
+        for (int a = 0; a < 4; a++)
 #pragma unroll
             for (int b = 0; b < 4; b++) o[a][b] = fma2(make_float2(mr[a], mr[a]), bp[b], o[a][b]);
     }
 #pragma unroll
-    for (int a = 0; a < 8; a++) {
+    for (int a = 0; a < 4; a++) {
         float* dst = t + (r0 + a) * 36 + c0;
         *(float4*)dst = make_float4(o[a][0].x, o[a][0].y, o[a][1].x, o[a][1].y);
         *(float4*)(dst + 4) = make_float4(o[a][2].x, o[a][2].y, o[a][3].x, o[a][3].y);
@@ -1401,14 +1411,12 @@ __device__ __forceinline__ void kron_pass2(const float* mt, const float* B, floa
 }
 
 // A Kronecker stage of every row: z in buf[from], result t in buf[from]
-// too (pass 1 writes mt into buf[1 - from]). Threads 0-127: row t / 16;
-// the sixteen tiles of a row are spread so that the stores of a quarter
-// warp fall in different banks.
+// too (pass 1 writes mt into buf[1 - from]). Warps 0-7, warp q for row q.
 __device__ __forceinline__ void kron_stage_rows(PostSmem& sm, int fa, int fb, int from, int tid) {
-    const int q = tid >> 4, i = tid & 15, lo = (i & 3) * 8, hi = (i >> 2) * 8;
-    if (tid < 128) kron_pass1(sm.kf[fa], sm.buf[from][q], sm.buf[1 - from][q], lo, hi);
+    const int q = tid >> 5, i = tid & 31, r0 = (i & 7) * 4, c0 = (i >> 3) * 8;
+    if (tid < 256) kron_pass1(sm.kf[fa], sm.buf[from][q], sm.buf[1 - from][q], r0, c0);
     __syncthreads();
-    if (tid < 128) kron_pass2(sm.buf[1 - from][q], sm.kf[fb], sm.buf[from][q], hi, lo);
+    if (tid < 256) kron_pass2(sm.buf[1 - from][q], sm.kf[fb], sm.buf[from][q], r0, c0);
     __syncthreads();
 }
 
