@@ -348,6 +348,12 @@ struct Batch {
     Model* m = nullptr;
     int S = 0, cap = 0, Mmax = 0;
     cudaStream_t st = nullptr;
+    // The engram sites depend only on the tokens, so each chunk runs them on
+    // a second stream, forked after the tokens are written; layer l's mHC
+    // read waits for its site's event.
+    cudaStream_t st2 = nullptr;
+    cudaEvent_t ev_fork = nullptr;
+    std::vector<cudaEvent_t> ev_site;
     int len = 0;          // positions fed to every sequence
     int hist_base = 0;    // first position whose pre-tap row the conv may read
     bool rope_valid = false;
@@ -357,8 +363,8 @@ struct Batch {
     Caches c{};
     std::vector<void*> allocs;
     float *xs, *u, *p, *x1, *proj, *qbuf, *att, *o, *e, *ekv, *evals, *cosr, *sinr, *rope_state, *h, *logits = nullptr;
-    int8_t* act;
-    float* sx;
+    int8_t *act, *act_e;  // A8 rows of the layer chain / of the engram stream
+    float *sx, *sx_e;
     int32_t *ids, *next;
     int32_t* d_len;  // device copy of len (Caches::len)
     uint8_t* masks;
@@ -388,6 +394,10 @@ struct Batch {
         for (auto e : evs) cudaEventDestroy(e);
         for (auto& g : graph)
             if (g.exec) cudaGraphExecDestroy(g.exec);
+        if (st2) cudaStreamSynchronize(st2);
+        for (auto e : ev_site) cudaEventDestroy(e);
+        if (ev_fork) cudaEventDestroy(ev_fork);
+        if (st2) cudaStreamDestroy(st2);
         if (st) cudaStreamDestroy(st);
     }
 };
@@ -404,8 +414,12 @@ static Batch* batch_new(Model* m, int S, int max_len) {
     b.cap = max_len;
     b.Mmax = S * 32;
     CK(cudaStreamCreateWithFlags(&b.st, cudaStreamNonBlocking));
+    CK(cudaStreamCreateWithFlags(&b.st2, cudaStreamNonBlocking));
+    CK(cudaEventCreateWithFlags(&b.ev_fork, cudaEventDisableTiming));
     if (const char* g = getenv("NEEDLE_GRAPHS")) b.graphs = atoi(g) != 0;
     const int L = c.L, nsites = (int)c.sites.size();
+    b.ev_site.resize(nsites);
+    for (auto& e : b.ev_site) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     const size_t M = b.Mmax;
     b.c.S = S;
     b.c.L = L;
@@ -438,6 +452,8 @@ static Batch* batch_new(Model* m, int S, int max_len) {
     b.h = b.alloc<float>(M * 768);
     b.act = b.alloc<int8_t>(M * 768);
     b.sx = b.alloc<float>(M * 8);
+    b.act_e = b.alloc<int8_t>(M * 768);
+    b.sx_e = b.alloc<float>(M * 8);
     b.ids = b.alloc<int32_t>(M);
     b.next = b.alloc<int32_t>(S);
     b.masks = b.alloc<uint8_t>((size_t)S * ((c.out_rows() + 7) / 8));
@@ -454,15 +470,15 @@ static void ensure_logits(Batch& b, size_t rows) {
     b.logits_cap = need;
 }
 
-// An event on the batch's stream around each launch of the timed site.
-static void tick(Batch& b, int site) {
+// An event on the launching stream around each launch of the timed site.
+static void tick(Batch& b, int site, cudaStream_t on = nullptr) {
     if (b.time_site != site) return;
     if (b.ev_used == b.evs.size()) {
         cudaEvent_t e;
         CK(cudaEventCreate(&e));
         b.evs.push_back(e);
     }
-    CK(cudaEventRecord(b.evs[b.ev_used++], b.st));
+    CK(cudaEventRecord(b.evs[b.ev_used++], on ? on : b.st));
 }
 
 static void snap(Batch& b, const char* name, const float* src, size_t n) {
@@ -489,21 +505,28 @@ static int chunk(Batch& b, const int32_t* ids, int T, int outputs) {
     // infer.rs:1720: the recurrence serves one token right after the newest
     launch_rope_rows(m.rope_cos, m.rope_sin, m.sd, m.cd, b.d_len, T, (T == 1 && b.rope_valid) ? 1 : 0, b.rope_state, b.cosr,
                      b.sinr, st);
-    launch_embed(m.embedding, ids, M, b.xs, st);
-    // infer.rs:1244-1328
-    for (int s = 0; s < nsites; s++) {
-        float* kv = b.ekv + (size_t)s * b.Mmax * 1536;
-        launch_engram_gather(m.etables[s], b.c, S, T, p0, c.eslots, b.e, st);
-        launch_prep_act(b.e, 768, 768, M, b.act, b.sx, st);
-        tick(b, ND_SITE_ENGRAM_KV);
-        launch_cq_gemm(m.ekv[s], b.act, b.sx, M, T, kv, 1536, 0, st);
-        tick(b, ND_SITE_ENGRAM_KV);
-        launch_engram_vhist(kv, b.c, s, nsites, S, T, p0, st);
-        launch_engram_conv(m.etaps[s], b.c, s, nsites, S, T, p0, b.evals + (size_t)s * b.Mmax * 768, st);
+    // infer.rs:1244-1328, on the engram stream
+    if (nsites > 0) {
+        cudaStream_t s2 = b.st2;
+        CK(cudaEventRecord(b.ev_fork, st));
+        CK(cudaStreamWaitEvent(s2, b.ev_fork, 0));
+        for (int s = 0; s < nsites; s++) {
+            float* kv = b.ekv + (size_t)s * b.Mmax * 1536;
+            launch_engram_gather(m.etables[s], b.c, S, T, p0, c.eslots, b.e, s2);
+            launch_prep_act(b.e, 768, 768, M, b.act_e, b.sx_e, s2);
+            tick(b, ND_SITE_ENGRAM_KV, s2);
+            launch_cq_gemm(m.ekv[s], b.act_e, b.sx_e, M, T, kv, 1536, 0, s2);
+            tick(b, ND_SITE_ENGRAM_KV, s2);
+            launch_engram_vhist(kv, b.c, s, nsites, S, T, p0, s2);
+            launch_engram_conv(m.etaps[s], b.c, s, nsites, S, T, p0, b.evals + (size_t)s * b.Mmax * 768, s2);
+            CK(cudaEventRecord(b.ev_site[s], s2));
+        }
     }
+    launch_embed(m.embedding, ids, M, b.xs, st);
     for (int l = 0; l < c.L; l++) {
         const LayerW& w = m.layers[l];
         const int lane = l % 4, site = m.site_of_layer[l];
+        if (site >= 0) CK(cudaStreamWaitEvent(st, b.ev_site[site], 0));
         tick(b, ND_SITE_MHC);
         launch_mhc_read(w, lane, b.xs, M, b.u, b.p, site >= 0 ? b.ekv + (size_t)site * b.Mmax * 1536 : nullptr,
                         site >= 0 ? b.evals + (size_t)site * b.Mmax * 768 : nullptr, b.x1, b.act, b.sx, st);
@@ -534,6 +557,8 @@ static int chunk(Batch& b, const int32_t* ids, int T, int outputs) {
         tick(b, ND_SITE_POST);
         if (l == b.debug_layer) snap(b, "snap.xs", b.xs, (size_t)M * 3072);
     }
+    // every site has joined the layer chain before the position advances
+    for (int s = 0; s < nsites; s++) CK(cudaStreamWaitEvent(st, b.ev_site[s], 0));
     launch_advance_len(b.d_len, T, st);
     b.len += T;
     b.rope_valid = true;
