@@ -6,12 +6,37 @@
 // float op follows the reference's order, rounding and fusion.
 
 #include <algorithm>
+#include <utility>
 #include <atomic>
 
 #include "kernels.h"
 #include "numerics.cuh"
 
 namespace nd {
+
+// Programmatic dependent launch: every kernel here is launched so that the
+// next kernel of its stream may start once all of this one's CTAs have
+// started (pdl_launch_dependents), and waits for its predecessor's results
+// (pdl_wait: the predecessor grid has completed and its writes are visible)
+// before touching anything the predecessor reads or writes.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+static void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = st ? 1 : 0;  // the legacy default stream keeps plain ordering
+    cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 
 static std::atomic<long long> g_launches{0};
 long long launch_count() { return g_launches.load(); }
@@ -39,6 +64,8 @@ static inline int cdiv(int a, int b) { return (a + b - 1) / b; }
 // --------------------------------------------------------------- tokens
 
 __global__ void write_tokens_kernel(const int32_t* ids, int S, int T, const int32_t* p0p, int32_t* tokens, int cap) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int p0 = *p0p;
     int m = blockIdx.x * blockDim.x + threadIdx.x;
     if (m >= S * T) return;
@@ -48,7 +75,7 @@ __global__ void write_tokens_kernel(const int32_t* ids, int S, int T, const int3
 
 void launch_write_tokens(const int32_t* ids, int S, int T, int p0, Caches c, cudaStream_t st) {
     COUNT_LAUNCH();
-    write_tokens_kernel<<<cdiv(S * T, 256), 256, 0, st>>>(ids, S, T, c.len, c.tokens, c.cap);
+    launch_pdl(write_tokens_kernel, dim3(cdiv(S * T, 256)), dim3(256), 0, st, ids, S, T, c.len, c.tokens, c.cap);
 }
 
 // ------------------------------------------------------- CQ row dequant
@@ -69,6 +96,8 @@ __device__ __forceinline__ void cq_group_row(const uint8_t* codes, const uint16_
 
 // infer.rs:1185-1194: the embedding row times sqrt(d), in every lane.
 __global__ void embed_kernel(DevMat emb, const int32_t* ids, float* xs, float scale) {
+    pdl_launch_dependents();
+    pdl_wait();
     int m = blockIdx.x, g = blockIdx.y, lane = threadIdx.x;
     int tok = ids[m];
     float v[4];
@@ -82,7 +111,7 @@ __global__ void embed_kernel(DevMat emb, const int32_t* ids, float* xs, float sc
 void launch_embed(DevMat emb, const int32_t* ids, int M, float* xs, cudaStream_t st) {
     COUNT_LAUNCH();
     float scale = __builtin_sqrtf((float)emb.in_dim);
-    embed_kernel<<<dim3(M, emb.groups), 32, 0, st>>>(emb, ids, xs, scale);
+    launch_pdl(embed_kernel, dim3(dim3(M, emb.groups)), dim3(32), 0, st, emb, ids, xs, scale);
 }
 
 // ------------------------------------------------------------ A8 prep
@@ -114,6 +143,8 @@ __device__ __forceinline__ void prep_group_warp(float v[4], int lane, int8_t* q,
 }
 
 __global__ void prep_act_kernel(const float* x, int ldx, int K, int8_t* act, float* sx, int G) {
+    pdl_launch_dependents();
+    pdl_wait();
     int m = blockIdx.x, g = blockIdx.y, lane = threadIdx.x;
     float v[4];
 #pragma unroll
@@ -127,7 +158,7 @@ __global__ void prep_act_kernel(const float* x, int ldx, int K, int8_t* act, flo
 void launch_prep_act(const float* x, int ldx, int K, int M, int8_t* act, float* sx, cudaStream_t st) {
     COUNT_LAUNCH();
     int G = cdiv(K, 128);
-    prep_act_kernel<<<dim3(M, G), 32, 0, st>>>(x, ldx, K, act, sx, G);
+    launch_pdl(prep_act_kernel, dim3(dim3(M, G)), dim3(32), 0, st, x, ldx, K, act, sx, G);
 }
 
 // ----------------------------------------------------------- CQ matmul
@@ -142,6 +173,8 @@ constexpr int GEMM_TN = 64, GEMM_TM = 16, GEMM_K = 768, GEMM_LD = GEMM_K + 4;
 
 __global__ void __launch_bounds__(256) cq_gemm_kernel(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y,
                                                       int ldy, int col0) {
+    pdl_launch_dependents();
+    pdl_wait();
     extern __shared__ __align__(16) int8_t smem[];
     int8_t* ws = smem;                               // [TN][LD]
     int8_t* as = smem + GEMM_TN * GEMM_LD;           // [TM][LD]
@@ -347,6 +380,8 @@ __device__ __forceinline__ void cp_async4z(void* smem, const void* gmem, bool va
 template <bool DECODE>
 __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y,
                                                         int ldy, int col0) {
+    pdl_launch_dependents();
+    pdl_wait();
     extern __shared__ __align__(16) int8_t smem[];
     int8_t* ws = smem;                                        // [BN][LD]
     int8_t* as = smem + MMA_BN * MMA_LD;                      // [BM][LD]
@@ -532,6 +567,8 @@ __device__ __forceinline__ uint32_t lut4(uint32_t nib16, uint32_t v0, uint32_t v
 
 __global__ void __launch_bounds__(256) cq_gemv_kernel(DevMat W, const int8_t* act, const float* sx, int M, float* y, int ldy,
                                                       int col0) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int n = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (n >= W.out) return;
@@ -580,7 +617,7 @@ __global__ void __launch_bounds__(256) cq_gemv_kernel(DevMat W, const int8_t* ac
 void launch_cq_gemm(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y, int ldy, int col0, cudaStream_t st) {
     COUNT_LAUNCH();
     if (T == 1 && M <= GEMV_MAXM && W.groups == 6) {
-        cq_gemv_kernel<<<cdiv(W.out, 8), 256, 0, st>>>(W, act, sx, M, y, ldy, col0);
+        launch_pdl(cq_gemv_kernel, dim3(cdiv(W.out, 8)), dim3(256), 0, st, W, act, sx, M, y, ldy, col0);
         return;
     }
     if (W.w8 && W.groups == 6) {
@@ -591,12 +628,12 @@ void launch_cq_gemm(DevMat W, const int8_t* act, const float* sx, int M, int T, 
         const int per = dev < 64 && sms[dev] ? 2 * sms[dev] : 296;
         const int grid = std::min(cdiv(W.out, MMA_BN) * cdiv(M, MMA_BM), per);
         if (T == 1)
-            cq_mma_kernel<true><<<grid, 256, MMA_SMEM, st>>>(W, act, sx, M, T, y, ldy, col0);
+            launch_pdl(cq_mma_kernel<true>, dim3(grid), dim3(256), MMA_SMEM, st, W, act, sx, M, T, y, ldy, col0);
         else
-            cq_mma_kernel<false><<<grid, 256, MMA_SMEM, st>>>(W, act, sx, M, T, y, ldy, col0);
+            launch_pdl(cq_mma_kernel<false>, dim3(grid), dim3(256), MMA_SMEM, st, W, act, sx, M, T, y, ldy, col0);
         return;
     }
-    cq_gemm_kernel<<<dim3(cdiv(W.out, GEMM_TN), cdiv(M, GEMM_TM)), 256, GEMM_SMEM, st>>>(W, act, sx, M, T, y, ldy, col0);
+    launch_pdl(cq_gemm_kernel, dim3(dim3(cdiv(W.out, GEMM_TN), cdiv(M, GEMM_TM))), dim3(256), GEMM_SMEM, st, W, act, sx, M, T, y, ldy, col0);
 }
 
 template <bool DECODE>
@@ -622,6 +659,8 @@ static cudaError_t init_attrs() {
 // infer.rs:1257-1277: the n-gram hash of each (order, head) picks a table
 // row; rows the position is too young for stay zero.
 __global__ void engram_gather_kernel(DevMat tables, const int32_t* tokens, int cap, int T, const int32_t* p0p, int slots, float* e) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int p0 = *p0p;
     int m = blockIdx.x, tbl = blockIdx.y, lane = threadIdx.x;
     const int heads = 3, stride = 3, sub = 128, d = 768;
@@ -643,12 +682,14 @@ __global__ void engram_gather_kernel(DevMat tables, const int32_t* tokens, int c
 
 void launch_engram_gather(DevMat tables, Caches c, int S, int T, int p0, int slots, float* e, cudaStream_t st) {
     COUNT_LAUNCH();
-    engram_gather_kernel<<<dim3(S * T, 6), 32, 0, st>>>(tables, c.tokens, c.cap, T, c.len, slots, e);
+    launch_pdl(engram_gather_kernel, dim3(dim3(S * T, 6)), dim3(32), 0, st, tables, c.tokens, c.cap, T, c.len, slots, e);
 }
 
 // infer.rs:1283-1303: the value half of kv, int8 in 32-wide groups, into
 // the site's history at the row's position.
 __global__ void engram_vhist_kernel(const float* kv, int8_t* ev8, float* evs, int site, int nsites, int T, const int32_t* p0p) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int p0 = *p0p;
     int m = blockIdx.x, g = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int s = m / T, pos = p0 + m % T;
@@ -663,13 +704,15 @@ __global__ void engram_vhist_kernel(const float* kv, int8_t* ev8, float* evs, in
 
 void launch_engram_vhist(const float* kv, Caches c, int site, int nsites, int S, int T, int p0, cudaStream_t st) {
     COUNT_LAUNCH();
-    engram_vhist_kernel<<<S * T, 768, 0, st>>>(kv, c.ev8, c.evs, site, nsites, T, c.len);
+    launch_pdl(engram_vhist_kernel, dim3(S * T), dim3(768), 0, st, kv, c.ev8, c.evs, site, nsites, T, c.len);
 }
 
 // infer.rs:1310-1323 with engram_tap (663-687): four taps at dilation 3,
 // each an fma from the int8 history.
 __global__ void engram_conv_kernel(const float* taps, const int8_t* ev8, const float* evs, int site, int nsites, int T, const int32_t* p0p,
                                    float* v) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int p0 = *p0p;
     int m = blockIdx.x, ch = threadIdx.x;
     int s = m / T, pos = p0 + m % T;
@@ -686,7 +729,7 @@ __global__ void engram_conv_kernel(const float* taps, const int8_t* ev8, const f
 
 void launch_engram_conv(const float* taps, Caches c, int site, int nsites, int S, int T, int p0, float* v, cudaStream_t st) {
     COUNT_LAUNCH();
-    engram_conv_kernel<<<S * T, 768, 0, st>>>(taps, c.ev8, c.evs, site, nsites, T, c.len, v);
+    launch_pdl(engram_conv_kernel, dim3(S * T), dim3(768), 0, st, taps, c.ev8, c.evs, site, nsites, T, c.len, v);
 }
 
 // ------------------------------------------------------------ mHC read
@@ -735,6 +778,8 @@ __device__ __forceinline__ int reduce4_scatter(const int s[4], int ln) {
 __global__ void __launch_bounds__(MHC_THREADS, 8) mhc_read_kernel(LayerW w, int lane_own, const float* xs, float* u, float* p,
                                                                   const float* ekv, const float* evals, float* x1o, int8_t* act,
                                                                   float* sx) {
+    pdl_launch_dependents();
+    pdl_wait();
     // the four streams chain-major: element e at (e % 16) * MHC_XS + e / 16,
     // so each of the sixteen chains of the rms dot reads 16-byte runs;
     // later the norm's scratch rows
@@ -939,7 +984,7 @@ __global__ void __launch_bounds__(MHC_THREADS, 8) mhc_read_kernel(LayerW w, int 
 void launch_mhc_read(LayerW w, int lane, const float* xs, int M, float* u, float* p, const float* ekv, const float* evals,
                      float* x1, int8_t* act, float* sx, cudaStream_t st) {
     COUNT_LAUNCH();
-    mhc_read_kernel<<<M, MHC_THREADS, 0, st>>>(w, lane, xs, u, p, ekv, evals, x1, act, sx);
+    launch_pdl(mhc_read_kernel, dim3(M), dim3(MHC_THREADS), 0, st, w, lane, xs, u, p, ekv, evals, x1, act, sx);
 }
 
 // ------------------------------------------------ conv taps, RoPE, int8 KV
@@ -949,6 +994,8 @@ void launch_mhc_read(LayerW w, int lane, const float* xs, int M, float* u, float
 // earlier rows of this chunk, else the pre-tap history, else zeros.
 __global__ void __launch_bounds__(512) conv_rope_kv_kernel(LayerW w, int l, const float* proj, Caches c, int T, const int32_t* p0p,
                                                            int hist_base, const float* cosr, const float* sinr, float* qbuf) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int p0 = *p0p;
     __shared__ float buf[16][64];
     const int m = blockIdx.x, unit = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1061,7 +1108,7 @@ __global__ void __launch_bounds__(512) conv_rope_kv_kernel(LayerW w, int l, cons
 void launch_conv_rope_kv(LayerW w, int l, const float* proj, Caches c, int S, int T, int p0, int hist_base, const float* cosr,
                          const float* sinr, float* qbuf, cudaStream_t st) {
     COUNT_LAUNCH();
-    conv_rope_kv_kernel<<<S * T, 512, 0, st>>>(w, l, proj, c, T, c.len, hist_base, cosr, sinr, qbuf);
+    launch_pdl(conv_rope_kv_kernel, dim3(S * T), dim3(512), 0, st, w, l, proj, c, T, c.len, hist_base, cosr, sinr, qbuf);
 }
 
 // ------------------------------------------------------------- attention
@@ -1105,6 +1152,8 @@ struct AttSmem {
 
 __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbuf, const float* proj, Caches c, int l, int T,
                                                                 const int32_t* p0p, int window, float* att, int8_t* act, float* sx) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int p0 = *p0p;
     extern __shared__ __align__(16) int8_t att_raw[];
     AttSmem& sm = *reinterpret_cast<AttSmem*>(att_raw);
@@ -1313,7 +1362,7 @@ void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int
     if (T == 1 && nmax >= 256) most = std::max(most, 4);
     most = std::min(most, ATT_MAXPARTS);
     size_t smem = ATT_SMEM_BASE + (size_t)ATT_HEADS * most * 66 * 4;
-    attention_kernel<<<dim3(S * T, 2), ATT_THREADS, smem, st>>>(qbuf, proj, c, l, T, c.len, window, att, act, sx);
+    launch_pdl(attention_kernel, dim3(dim3(S * T, 2)), dim3(ATT_THREADS), smem, st, qbuf, proj, c, l, T, c.len, window, att, act, sx);
 }
 
 // ------------------------------------------------------------ post block
@@ -1326,9 +1375,9 @@ void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int
 // are staged once into shared memory with cp.async, so every phase reads
 // shared memory only. A row's 1024-wide vectors use a padded layout
 // (element p at (p / 32) * 36 + p % 32) and ping-pong between two buffers.
-// The rows' o, x1 and gates arrive with the weights; u arrives during the
-// Kronecker stages into the space of cond_v, whose last use is the
-// conditioning logits. The post and residual gates (hpost, Sinkhorn) were
+// The weights are requested before the predecessor kernel has finished, the
+// rows' o, x1 and gates right after; u arrives during the Kronecker stages
+// into the space of cond_v, whose last use is the conditioning logits. The post and residual gates (hpost, Sinkhorn) were
 // computed by the mHC read.
 constexpr int POST_ROWS = 8, POST_THREADS = 512, PV = 32 * 36 + 8;
 struct PostSmem {
@@ -1423,26 +1472,13 @@ __device__ __forceinline__ void kron_stage_rows(PostSmem& sm, int fa, int fb, in
 __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, const float* o, const float* x1, const float* u,
                                                                    const float* gates, const int32_t* perm1,
                                                                    const int32_t* perm2, int M, float* xs) {
+    pdl_launch_dependents();
     extern __shared__ __align__(16) int8_t post_raw[];
     PostSmem& sm = *reinterpret_cast<PostSmem*>(post_raw);
     const int tid = threadIdx.x, m0 = blockIdx.x * POST_ROWS;
     const int rows = min(POST_ROWS, M - m0);
-    // group 0: the rows' o (into x2) and x1 (into buf[1], plain), gates, post_norm
-    for (int k = tid; k < POST_ROWS * 192; k += POST_THREADS) {
-        const int q = k / 192, c = k % 192;
-        const bool ok = q < rows;
-        const size_t src = (size_t)(ok ? m0 + q : 0) * 768 + 4 * c;
-        cp_async16(&sm.x2[q][4 * c], o + src, ok);
-        cp_async16(&sm.buf[1][q][4 * c], x1 + src, ok);
-    }
-    for (int k = tid; k < POST_ROWS * 6; k += POST_THREADS) {
-        const int q = k / 6, c = k % 6;
-        const bool ok = q < rows;
-        cp_async16(&sm.gates[q][4 * c], gates + (size_t)(ok ? m0 + q : 0) * 24 + 4 * c, ok);
-    }
+    // group 0, before the predecessor is done: the layer's weights
     stage(sm.post_norm, w.post_norm, 768 * 4, tid);
-    asm volatile("cp.async.commit_group;\n" ::);
-    // group 1: the rest of the layer's weights
     for (int f = 0; f < 6; f++) stage(sm.kf[f], w.kron[f], 4096, tid);
     stage(sm.cond_v, w.cond_v, 768 * 8 * 4, tid);
     stage(sm.cond_u, w.cond_u, 8 * 1024 * 4, tid);
@@ -1455,7 +1491,22 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
     stage(sm.perm1, perm1, 4096, tid);
     stage(sm.perm2, perm2, 4096, tid);
     asm volatile("cp.async.commit_group;\n" ::);
-    asm volatile("cp.async.wait_group 1;\n" ::);
+    pdl_wait();
+    // group 1: the rows' o (into x2) and x1 (into buf[1], plain), gates
+    for (int k = tid; k < POST_ROWS * 192; k += POST_THREADS) {
+        const int q = k / 192, c = k % 192;
+        const bool ok = q < rows;
+        const size_t src = (size_t)(ok ? m0 + q : 0) * 768 + 4 * c;
+        cp_async16(&sm.x2[q][4 * c], o + src, ok);
+        cp_async16(&sm.buf[1][q][4 * c], x1 + src, ok);
+    }
+    for (int k = tid; k < POST_ROWS * 6; k += POST_THREADS) {
+        const int q = k / 6, c = k % 6;
+        const bool ok = q < rows;
+        cp_async16(&sm.gates[q][4 * c], gates + (size_t)(ok ? m0 + q : 0) * 24 + 4 * c, ok);
+    }
+    asm volatile("cp.async.commit_group;\n" ::);
+    asm volatile("cp.async.wait_group 0;\n" ::);
     __syncthreads();
     // zcn(o, post_norm): sixteen dot16 chains per row
     if (tid < POST_ROWS * 16) {
@@ -1604,7 +1655,7 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
 void launch_post_block(LayerW w, const float* o, const float* x1, const float* u, const float* gates, const int32_t* perm1,
                        const int32_t* perm2, int M, float* xs, cudaStream_t st) {
     COUNT_LAUNCH();
-    post_block_kernel<<<cdiv(M, POST_ROWS), POST_THREADS, POST_SMEM, st>>>(w, o, x1, u, gates, perm1, perm2, M, xs);
+    launch_pdl(post_block_kernel, dim3(cdiv(M, POST_ROWS)), dim3(POST_THREADS), POST_SMEM, st, w, o, x1, u, gates, perm1, perm2, M, xs);
 }
 
 // ------------------------------------------------------------ final norm
@@ -1612,6 +1663,8 @@ void launch_post_block(LayerW w, const float* o, const float* x1, const float* u
 // infer.rs:1214-1225: lane mean ((x0 + x1) + x2 + x3) * 0.25, then the final
 // ZC-RMSNorm, for each sequence's last row (or every row).
 __global__ void final_hidden_kernel(const float* xs, const float* fnorm, int T, int all_rows, float* h) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ float mean[768];
     __shared__ float part[16];
     __shared__ float r_s;
@@ -1633,7 +1686,7 @@ __global__ void final_hidden_kernel(const float* xs, const float* fnorm, int T, 
 
 void launch_final_hidden(const float* xs, const float* final_norm, int S, int T, int all_rows, float* h, cudaStream_t st) {
     COUNT_LAUNCH();
-    final_hidden_kernel<<<all_rows ? S * T : S, 256, 0, st>>>(xs, final_norm, T, all_rows, h);
+    launch_pdl(final_hidden_kernel, dim3(all_rows ? S * T : S), dim3(256), 0, st, xs, final_norm, T, all_rows, h);
 }
 
 // ----------------------------------------------------------------- RoPE
@@ -1643,6 +1696,8 @@ void launch_final_hidden(const float* xs, const float* final_norm, int S, int T,
 // token right after the newest position the angle-addition recurrence.
 __global__ void rope_rows_kernel(const float* tc, const float* tsn, const float* sd, const float* cd, const int32_t* p0p, int T, int recur,
                                  float* state, float* cosr, float* sinr) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int p0 = *p0p;
     int i = blockIdx.x, f = threadIdx.x;
     if (f >= 24) return;
@@ -1666,22 +1721,26 @@ __global__ void rope_rows_kernel(const float* tc, const float* tsn, const float*
 void launch_rope_rows(const float* table_cos, const float* table_sin, const float* sd, const float* cd, const int32_t* p0p, int T,
                       int recur, float* state, float* cosr, float* sinr, cudaStream_t st) {
     COUNT_LAUNCH();
-    rope_rows_kernel<<<T, 32, 0, st>>>(table_cos, table_sin, sd, cd, p0p, T, recur, state, cosr, sinr);
+    launch_pdl(rope_rows_kernel, dim3(T), dim3(32), 0, st, table_cos, table_sin, sd, cd, p0p, T, recur, state, cosr, sinr);
 }
 
 // Positions fed so far, advanced on the device so a captured step replays
 // at any position.
-__global__ void advance_len_kernel(int32_t* len, int T) { *len += T; }
+__global__ void advance_len_kernel(int32_t* len, int T) {
+    pdl_launch_dependents();
+    pdl_wait(); *len += T; }
 
 void launch_advance_len(int32_t* len, int T, cudaStream_t st) {
     COUNT_LAUNCH();
-    advance_len_kernel<<<1, 1, 0, st>>>(len, T);
+    launch_pdl(advance_len_kernel, dim3(1), dim3(1), 0, st, len, T);
 }
 
 // Holds the stream for `ns` nanoseconds (one thread, sleeping), so that the
 // launches queued behind it start back to back: per-site event timing then
 // sees kernel time, not the host's launch rate.
 __global__ void hold_kernel(unsigned long long ns) {
+    pdl_launch_dependents();
+    pdl_wait();
     unsigned long long t0, t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
     do {
@@ -1692,7 +1751,7 @@ __global__ void hold_kernel(unsigned long long ns) {
 
 void launch_hold(unsigned long long ns, cudaStream_t st) {
     COUNT_LAUNCH();
-    hold_kernel<<<1, 1, 0, st>>>(ns);
+    launch_pdl(hold_kernel, dim3(1), dim3(1), 0, st, ns);
 }
 
 // ------------------------------------------------------- masked argmax
@@ -1700,6 +1759,8 @@ void launch_hold(unsigned long long ns, cudaStream_t st) {
 // crates/needle-engine/src/agent.rs:1114-1127: banned ids read -1e30, then
 // the first index of the maximum.
 __global__ void masked_argmax_kernel(const float* logits, int V, const uint8_t* allow, int32_t* next) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ float bv[32];
     __shared__ int bi[32];
     const int s = blockIdx.x, tid = threadIdx.x;
@@ -1740,7 +1801,7 @@ __global__ void masked_argmax_kernel(const float* logits, int V, const uint8_t* 
 
 void launch_masked_argmax(const float* logits, int S, int V, const uint8_t* allow, int32_t* next, cudaStream_t st) {
     COUNT_LAUNCH();
-    masked_argmax_kernel<<<S, 256, 0, st>>>(logits, V, allow, next);
+    launch_pdl(masked_argmax_kernel, dim3(S), dim3(256), 0, st, logits, V, allow, next);
 }
 
 }  // namespace nd
