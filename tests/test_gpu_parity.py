@@ -38,6 +38,20 @@ def test_head_logits_decode_combine(small):
             assert bits_equal(got[r], want), describe_diff("head_logits", got[r], want)
 
 
+@pytest.mark.parametrize("rows", [5, 128, 200])
+def test_head_logits_many_rows(small, rows):
+    """The decode combine at batch sizes past the one-warp GEMV (tensor-core
+    tiles, the last one partial)."""
+    g, o = small
+    rng = np.random.default_rng(100 + rows)
+    b = g.batch(8, 64)
+    h = (rng.standard_normal((rows, g.d_model)) * 3.0).astype(np.float32)
+    got = b.head_logits(h)
+    for r in range(rows):
+        want = o.head_logits(h[r])
+        assert bits_equal(got[r], want), f"row {r}: " + describe_diff("head_logits", got[r], want)
+
+
 def test_head_logits_sparse_single_row(small):
     g, o = small
     rng = np.random.default_rng(2)
@@ -104,6 +118,31 @@ def test_batched_sequences_match_single(small):
     g, o = small
     rng = np.random.default_rng(5)
     S, n, steps = 8, 37, 6
+    prompts = rng.integers(0, g.vocab, (S, n)).astype(np.int32)
+    mb = (g.out_rows + 7) // 8
+    masks = np.zeros((S, steps, mb), np.uint8)
+    for s_ in range(S):
+        for k in range(steps):
+            allow = rng.random(g.out_rows) < rng.uniform(0.05, 0.5)
+            allow[rng.integers(0, g.out_rows)] = True
+            masks[s_, k] = np.packbits(allow, bitorder="little")
+    b = g.batch(S, n + steps + 1)
+    b.forward(prompts)
+    got = np.zeros((S, steps), np.int64)
+    for k in range(steps):
+        got[:, k] = b.step(masks[:, k])
+    for s_ in range(S):
+        want = o.generate(prompts[s_].astype(np.uint32), steps, masks=masks[s_])
+        assert list(got[s_]) == list(want), f"sequence {s_}: {got[s_]} vs {want}"
+
+
+def test_batched_decode_many_sequences(small):
+    """144 sequences in one batch (matmul tiles of 64 and 128 rows, the last
+    partial) equal 144 separate oracle sessions through a 9-token prefill
+    and 4 masked greedy steps."""
+    g, o = small
+    rng = np.random.default_rng(6)
+    S, n, steps = 144, 9, 4
     prompts = rng.integers(0, g.vocab, (S, n)).astype(np.int32)
     mb = (g.out_rows + 7) // 8
     masks = np.zeros((S, steps, mb), np.uint8)
