@@ -47,6 +47,9 @@ def parse():
                     help="the kernel site the roofline object reports (auto: the slowest in the sweep)")
     ap.add_argument("--cpu-baseline", type=int, default=1, help="time the oracle on rank 0 (N=1 only)")
     ap.add_argument("--secondary", type=int, default=1, help="also time batch-1 decode and 256x700 prefill (N=1)")
+    ap.add_argument("--sweep", action="store_true",
+                    help="instead of the decode bench: the CQ-W4/A8 matmul sweep (M in 1, 16, 128, 2048 over the "
+                         "model's four matrix shapes), one JSON line")
     ap.add_argument("--profile", action="store_true",
                     help="untimed case for ncu: one batch of --seqs sequences, the 118-token prefill, then --warmup "
                          "decode steps")
@@ -232,6 +235,33 @@ def cpu_baseline_sample(data):
                       f"prefill (decode timed only)"}
 
 
+def matmul_sweep(local):
+    """The CQ-W4/A8 matmul alone (A8 of the rows + the matmul, inputs resident
+    on the GPU, nd_cqmat_apply's event timing): codes uniform over the 16
+    values, f16 norms |N(0, 0.02)|, activations N(0, 1); the decode combine
+    (T = 1) for every M. Bytes: weight codes and norms + int8 activations and
+    scales + f32 outputs; ops: 2 M N K. Weights of one matrix (<= 6.5 MB) stay
+    in L2 across the back-to-back runs."""
+    import needle_b200 as nb
+
+    rng = np.random.default_rng(3)
+    shapes = [("qkvg", 1568), ("out", 768), ("engram_kv", 1536), ("lm_head", 16384)]
+    rows = []
+    for name, n in shapes:
+        codes = rng.integers(0, 256, (n, 6, 64), dtype=np.uint8)
+        norms = np.abs(rng.standard_normal((n, 6)) * 0.02).astype(np.float16).view(np.uint16)
+        mat = nb.CQMat(codes, norms, local)
+        for M in (1, 16, 128, 2048):
+            x = rng.standard_normal((M, 768)).astype(np.float32)
+            reps = 200 if M * n <= 16 * 16384 else 50
+            _, ms = mat(x, T=1, reps=reps)
+            byt = n * 6 * (64 + 2) + M * 768 + M * 6 * 4 + M * n * 4
+            rows.append({"matrix": name, "N": n, "K": 768, "M": M, "us": round(ms * 1e3, 2),
+                         "GB_s": round(byt / (ms * 1e-3) / 1e9, 1), "int8_TOPS": round(2 * M * n * 768 / (ms * 1e-3) / 1e12, 2)})
+        del mat
+    return rows
+
+
 def secondary(model, local):
     """The other BASELINE.json throughput configs on this GPU, reported beside
     the headline: batch-1 decode (configs[0]: 118-token prompt, 45 greedy
@@ -300,6 +330,13 @@ def main():
     torch.cuda.set_device(local)
     import needle_b200 as nb
 
+    if args.sweep:
+        if rank == 0:
+            print(json.dumps({"sweep": "cq_w4a8_matmul", "combine": "decode", "rows": matmul_sweep(local)}), flush=True)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     S, W, K = args.seqs, args.warmup, args.steps
     total_steps = W + K
     data = archive_bytes()

@@ -91,6 +91,19 @@ void* nd_batch_stream(nd_batch* b);
  * w[rows][d] to codes[rows][ceil(d/128)*64] and f16 norms[rows][ceil(d/128)]. */
 int nd_cq_pack(const float* w, int rows, int d, unsigned char* codes, unsigned short* norms);
 
+/* Test and benchmark support: one CQ-4 matrix (codes [out][6][64], f16
+ * norms [out][6] as quant.rs:233-256 packs them; in_dim 768) on GPU
+ * `device`, and the engine's matmul of host rows x[M][768] into y[M][out]:
+ * each row quantized as QAct::new (qlinear.rs:152-207), then the decode
+ * combine (qlinear.rs:340-350) when T == 1, else the prefill combine
+ * (qlinear.rs:353-363) over consecutive sequences of T rows (M a multiple
+ * of T). With reps > 0 and ms != NULL it also times reps back-to-back runs
+ * (A8 + matmul, inputs resident) and stores the mean in *ms. */
+typedef struct nd_cqmat nd_cqmat;
+int nd_cqmat_new(int device, const unsigned char* codes, const unsigned short* norms, int out, int in_dim, nd_cqmat** out_mat);
+void nd_cqmat_free(nd_cqmat* mat);
+int nd_cqmat_apply(nd_cqmat* mat, const float* x, int M, int T, float* y, int reps, float* ms);
+
 /* crates/needle-core/src/cact.rs:399-475 (pack) over random-init Needle 3
  * weights: every tensor ~N(0, std^2), seeded; CQ-4 matrices, f16 small
  * weights, MT19937 Hadamard permutations. Shape knobs let tests shrink the

@@ -860,6 +860,106 @@ int nd_head_logits_sparse(nd_batch* bh, const float* h, const int* ids, int n, f
     }
 }
 
+// One CQ-4 matrix on a GPU for kernel-level tests and the matmul sweep.
+struct nd_cqmat {
+    Model m;  // owns the uploads
+    DevMat d;
+    cudaStream_t st = nullptr;
+    float *x = nullptr, *y = nullptr, *sx = nullptr;
+    int8_t* act = nullptr;
+    int cap = 0;
+    std::vector<void*> scratch;
+    ~nd_cqmat() {
+        cudaSetDevice(m.device);
+        if (st) cudaStreamSynchronize(st);
+        for (void* p : scratch) cudaFree(p);
+        if (st) cudaStreamDestroy(st);
+    }
+};
+
+int nd_cqmat_new(int device, const unsigned char* codes, const unsigned short* norms, int out, int in_dim, nd_cqmat** h) {
+    try {
+        if (!codes || !norms || !h) throw std::runtime_error("nd_cqmat_new: null argument");
+        if (in_dim != 768) throw std::runtime_error("nd_cqmat_new: the engine's matmuls take in_dim 768");
+        if (out < 1) throw std::runtime_error("nd_cqmat_new: out must be positive");
+        CK(cudaSetDevice(device));
+        std::unique_ptr<nd_cqmat> q(new nd_cqmat());
+        q->m.device = device;
+        HostMat hm;
+        hm.out = out;
+        hm.in_dim = in_dim;
+        hm.groups = 6;
+        hm.codes.assign(codes, codes + (size_t)out * 6 * 64);
+        hm.norms.assign(norms, norms + (size_t)out * 6);
+        q->d = to_dev(q->m, hm, true);
+        // the device's codebook constants (the same for every CQ-4 matrix)
+        int8_t vals[16];
+        float cbs = 0.f;
+        std::vector<float> cb;
+        int8_codebook(vals, &cbs, &cb);
+        set_constants(vals, cb.data(), cbs, (float)(1.0 / std::sqrt(128.0)));
+        CK(cudaGetLastError());
+        CK(cudaStreamCreateWithFlags(&q->st, cudaStreamNonBlocking));
+        *h = q.release();
+        return 0;
+    } catch (std::exception& e) {
+        return fail(e);
+    }
+}
+
+void nd_cqmat_free(nd_cqmat* h) { delete h; }
+
+int nd_cqmat_apply(nd_cqmat* h, const float* x, int M, int T, float* y, int reps, float* ms) {
+    try {
+        if (!h || !x || !y) throw std::runtime_error("nd_cqmat_apply: null argument");
+        if (M < 1 || T < 1 || M % T) throw std::runtime_error("nd_cqmat_apply: M must be a positive multiple of T");
+        CK(cudaSetDevice(h->m.device));
+        const int out = h->d.out;
+        if (M > h->cap) {
+            for (void* p : h->scratch) cudaFree(p);
+            h->scratch.clear();
+            auto get = [&](size_t bytes) {
+                void* p = nullptr;
+                CK(cudaMalloc(&p, bytes + 64));
+                h->scratch.push_back(p);
+                return p;
+            };
+            h->x = (float*)get((size_t)M * 768 * 4);
+            h->act = (int8_t*)get((size_t)M * 768);
+            h->sx = (float*)get((size_t)M * 8 * 4);
+            h->y = (float*)get((size_t)M * out * 4);
+            h->cap = M;
+        }
+        CK(cudaMemcpyAsync(h->x, x, (size_t)M * 768 * 4, cudaMemcpyHostToDevice, h->st));
+        auto run = [&]() {
+            launch_prep_act(h->x, 768, 768, M, h->act, h->sx, h->st);
+            launch_cq_gemm(h->d, h->act, h->sx, M, T, h->y, out, 0, h->st);
+        };
+        run();
+        if (reps > 0 && ms) {
+            cudaEvent_t e0, e1;
+            CK(cudaEventCreate(&e0));
+            CK(cudaEventCreate(&e1));
+            for (int k = 0; k < 3; k++) run();
+            CK(cudaEventRecord(e0, h->st));
+            for (int k = 0; k < reps; k++) run();
+            CK(cudaEventRecord(e1, h->st));
+            CK(cudaEventSynchronize(e1));
+            float t = 0;
+            CK(cudaEventElapsedTime(&t, e0, e1));
+            *ms = t / reps;
+            cudaEventDestroy(e0);
+            cudaEventDestroy(e1);
+        }
+        CK(cudaGetLastError());
+        CK(cudaMemcpyAsync(y, h->y, (size_t)M * out * 4, cudaMemcpyDeviceToHost, h->st));
+        CK(cudaStreamSynchronize(h->st));
+        return 0;
+    } catch (std::exception& e) {
+        return fail(e);
+    }
+}
+
 int nd_cq_pack(const float* w, int rows, int d, unsigned char* codes, unsigned short* norms) {
     try {
         cq_pack4(w, rows, d, codes, norms);

@@ -44,6 +44,9 @@ def lib():
             "nd_head_logits_sparse": (I, [P, P, P, I, P]),
             "nd_batch_stream": (P, [P]),
             "nd_cq_pack": (I, [P, I, I, P, P]),
+            "nd_cqmat_new": (I, [I, P, P, I, I, C.POINTER(P)]),
+            "nd_cqmat_free": (None, [P]),
+            "nd_cqmat_apply": (I, [P, P, I, I, P, I, C.POINTER(C.c_float)]),
             "nd_synth_cact": (I, [I, I, I, I, U64, U64, U64, C.c_float, P, U64, C.POINTER(U64)]),
             "nd_batch_debug": (I, [P, C.c_char_p, P, C.c_longlong]),
             "nd_batch_debug_layer": (I, [P, I]),
@@ -104,6 +107,35 @@ def synth_cact(seed=0, std=0.02, **shape) -> bytes:
     if lib().nd_synth_cact(*args, _p(buf), n.value, C.byref(n)) != 0:
         raise _err()
     return buf.tobytes()
+
+
+class CQMat:
+    """One CQ-4 matrix (codes [out][6][64], f16 norms [out][6]) on a GPU:
+    the engine's A8 + CQ matmul on host rows (needle_engine.h,
+    nd_cqmat_apply)."""
+
+    def __init__(self, codes, norms, device=0):
+        codes = np.ascontiguousarray(codes, np.uint8)
+        norms = np.ascontiguousarray(norms, np.uint16)
+        self.out = norms.shape[0]
+        h = C.c_void_p()
+        if lib().nd_cqmat_new(device, _p(codes), _p(norms), self.out, 768, C.byref(h)) != 0:
+            raise _err()
+        self._h = h.value
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().nd_cqmat_free(self._h)
+            self._h = None
+
+    def __call__(self, x, T=1, reps=0):
+        """y [M][out] for x [M][768]; with reps > 0 returns (y, ms per run)."""
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, 768)
+        y = np.zeros((x.shape[0], self.out), np.float32)
+        ms = C.c_float(0.0)
+        if lib().nd_cqmat_apply(self._h, _p(x), x.shape[0], T, _p(y), reps, C.byref(ms)) != 0:
+            raise _err()
+        return (y, ms.value) if reps > 0 else y
 
 
 def cq_pack(w):

@@ -1,0 +1,51 @@
+"""The CQ-W4/A8 matmul alone on the GPU (nd_cqmat_apply) against the oracle's
+restatement of qlinear.rs, bit for bit: the decode combine (T = 1) through
+the one-warp GEMV (1-4 rows) and the tensor-core tiles (5+ rows), and the
+prefill combine with its block/remainder rule for the token counts the
+reference's own kernel test uses (qlinear.rs:977-1029: T in 2, 3, 5, 9, 13,
+17) plus full chunks and several sequences at once. Output widths include a
+ragged one (100) so the last column tile is partial."""
+
+import numpy as np
+import pytest
+
+from parity_tools import bits_equal, describe_diff
+
+pytestmark = pytest.mark.gpu
+
+
+def _matrix(rng, out):
+    codes = rng.integers(0, 256, (out, 6, 64), dtype=np.uint8)
+    norms = np.abs(rng.standard_normal((out, 6)) * 0.02).astype(np.float16).view(np.uint16)
+    return codes, norms
+
+
+@pytest.fixture(scope="module")
+def mats(cuda_device):
+    import needle_b200 as nb
+
+    rng = np.random.default_rng(77)
+    out = {}
+    for n in (100, 768):
+        codes, norms = _matrix(rng, n)
+        out[n] = (codes, norms, nb.CQMat(codes, norms, cuda_device))
+    return out
+
+
+CASES = [(1, 1), (3, 1), (4, 1), (5, 1), (64, 1), (200, 1),
+         (2, 2), (3, 3), (5, 5), (9, 9), (13, 13), (17, 17), (32, 32), (64, 32), (96, 3)]
+
+
+@pytest.mark.parametrize("n", [100, 768])
+@pytest.mark.parametrize("M,T", CASES)
+def test_cq_matmul_matches_oracle(mats, n, M, T):
+    from oracle import oracle as orc
+
+    codes, norms, mat = mats[n]
+    rng = np.random.default_rng(1000 * M + T + n)
+    x = rng.standard_normal((M, 768)).astype(np.float32)
+    x[0] *= 1e-3  # one row far smaller, one far larger
+    x[-1] *= 50.0
+    got = mat(x, T=T)
+    want = np.concatenate([orc.cq_matmul(codes.reshape(n, -1), norms, 768, x[s:s + T]) for s in range(0, M, T)])
+    assert bits_equal(got, want), describe_diff(f"cq matmul M={M} T={T} n={n}", got, want)
