@@ -1377,8 +1377,8 @@ void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int
 // (element p at (p / 32) * 36 + p % 32) and ping-pong between two buffers.
 // The weights are requested before the predecessor kernel has finished, the
 // rows' o, x1 and gates right after; u arrives during the Kronecker stages
-// into the space of cond_v, whose last use is the conditioning logits. The post and residual gates (hpost, Sinkhorn) were
-// computed by the mHC read.
+// into the space of cond_v, whose last use is the conditioning logits. The
+// post and residual gates (hpost, Sinkhorn) were computed by the mHC read.
 constexpr int POST_ROWS = 8, POST_THREADS = 512, PV = 32 * 36 + 8;
 struct PostSmem {
     float kf[6][1024];
