@@ -641,6 +641,9 @@ __global__ void cq_mma_kernel(DevMat W, const int8_t* act, const float* sx, int 
 
 extern const size_t ATT_SMEM;
 extern const size_t POST_SMEM;
+extern const size_t POST_ROW_SMEM;
+__global__ void post_row_kernel(LayerW w, const float* o, const float* x1, const float* u, const float* gates, const int32_t* perm1,
+                                const int32_t* perm2, float* xs);
 __global__ void post_block_kernel(LayerW w, const float* o, const float* x1, const float* u, const float* gates,
                                   const int32_t* perm1, const int32_t* perm2, int M, float* xs);
 __global__ void attention_kernel(const float* qbuf, const float* proj, Caches c, int l, int T, const int32_t* p0p, int window, float* att,
@@ -649,6 +652,7 @@ __global__ void attention_kernel(const float* qbuf, const float* proj, Caches c,
 static cudaError_t init_attrs() {
     cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_SMEM);
     cudaFuncSetAttribute(post_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)POST_SMEM);
+    cudaFuncSetAttribute(post_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)POST_ROW_SMEM);
     cudaFuncSetAttribute(cq_mma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
     cudaFuncSetAttribute(cq_mma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
     return cudaFuncSetAttribute(cq_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM);
@@ -1652,9 +1656,172 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
 #undef POST_LOAD_OLD
 }
 
+// The same post block for small batches: one row per CTA of 512 threads,
+// the layer's small weights staged into shared memory as post_block_kernel
+// stages them (before the wait on the predecessor), every thread on the one
+// row. A Kronecker pass gives each thread two outputs: in pass 1 thread t
+// owns r = t % 32 and columns c0 = 2 (t / 32), c0 + 1 (mt stored transposed,
+// as kron_native keeps it); in pass 2 the same r and columns of t. Every
+// float op, and its order, is that of post_block_kernel.
+constexpr int POST_ROW_MAX_M = 296;
+struct PostRowSmem {
+    float kf[6][1024];
+    float cond_v[768 * 8];
+    float cond_u[8 * 1024];
+    float d1[768], d2[1024], b2[1024], d3[1024], d4[768];
+    float post_norm[768], pre_hada[768];
+    int perm1[1024], perm2[1024];
+    float x2[768], hb[768], zb[1024], mb[1024], tb[1024];
+    float part[32], sc[2], wk[8], gr[24];
+};
+extern const size_t POST_ROW_SMEM = sizeof(PostRowSmem);
+
+__device__ __forceinline__ void kron_row_pass1(const float* A, const float* z, float* mt, int r, int c0) {
+    float2 o = make_float2(0.f, 0.f);
+#pragma unroll 8
+    for (int j = 0; j < 32; j++) {
+        const float a = A[j * 32 + r];
+        o = fma2(make_float2(a, a), *(const float2*)(z + j * 32 + c0), o);
+    }
+    mt[c0 * 32 + r] = o.x;
+    mt[(c0 + 1) * 32 + r] = o.y;
+}
+
+__device__ __forceinline__ void kron_row_pass2(const float* mt, const float* B, float* t, int r, int c0) {
+    float2 o = make_float2(0.f, 0.f);
+#pragma unroll 8
+    for (int j = 0; j < 32; j++) {
+        const float m = mt[j * 32 + r];
+        o = fma2(make_float2(m, m), *(const float2*)(B + j * 32 + c0), o);
+    }
+    *(float2*)(t + r * 32 + c0) = o;
+}
+
+__global__ void __launch_bounds__(POST_THREADS, 1) post_row_kernel(LayerW w, const float* o, const float* x1, const float* u,
+                                                                 const float* gates, const int32_t* perm1, const int32_t* perm2,
+                                                                 float* xs) {
+    pdl_launch_dependents();
+    extern __shared__ __align__(16) int8_t post_row_raw[];
+    PostRowSmem& sm = *reinterpret_cast<PostRowSmem*>(post_row_raw);
+    const int tid = threadIdx.x, m = blockIdx.x, r = tid & 31, c0 = 2 * (tid >> 5);
+    for (int f = 0; f < 6; f++) stage(sm.kf[f], w.kron[f], 4096, tid);
+    stage(sm.cond_v, w.cond_v, 768 * 8 * 4, tid);
+    stage(sm.cond_u, w.cond_u, 8 * 1024 * 4, tid);
+    stage(sm.d1, w.d1, 768 * 4, tid);
+    stage(sm.d2, w.d2, 4096, tid);
+    stage(sm.b2, w.b2, 4096, tid);
+    stage(sm.d3, w.d3, 4096, tid);
+    stage(sm.d4, w.d4, 768 * 4, tid);
+    stage(sm.post_norm, w.post_norm, 768 * 4, tid);
+    stage(sm.pre_hada, w.pre_hada, 768 * 4, tid);
+    stage(sm.perm1, perm1, 4096, tid);
+    stage(sm.perm2, perm2, 4096, tid);
+    asm volatile("cp.async.commit_group;\n" ::);
+    pdl_wait();
+    const float* orow = o + (size_t)m * 768;
+    for (int c = tid; c < 768; c += POST_THREADS) sm.x2[c] = orow[c];
+    if (tid < 24) sm.gr[tid] = gates[(size_t)m * 24 + tid];
+    asm volatile("cp.async.wait_group 0;\n" ::);
+    __syncthreads();
+    // zcn(o, post_norm): sixteen dot16 chains
+    if (tid < 16) sm.part[tid] = dot16_chain(sm.x2, sm.x2, 768, tid);
+    __syncthreads();
+    if (tid == 0) sm.sc[0] = rinv(dot16_combine(sm.part), 768);
+    __syncthreads();
+    const float ga = __fdiv_rn(1.0f, __fadd_rn(lexpf(-w.attn_gate), 1.0f));
+    for (int c = tid; c < 768; c += POST_THREADS) {
+        float tt = __fmul_rn(sm.x2[c], sm.sc[0]);
+        float on = __fmaf_rn(tt, sm.post_norm[c], tt);
+        sm.x2[c] = __fmaf_rn(on, ga, x1[(size_t)m * 768 + c]);
+    }
+    __syncthreads();
+    if (tid < 16) sm.part[tid] = dot16_chain(sm.x2, sm.x2, 768, tid);
+    __syncthreads();
+    if (tid == 0) sm.sc[1] = rinv(dot16_combine(sm.part), 768);
+    __syncthreads();
+    // h2 = zcn(x2, pre_hada), z = h2 * d1 (zero past 768)
+    for (int c = tid; c < 1024; c += POST_THREADS) {
+        if (c < 768) {
+            float tt = __fmul_rn(sm.x2[c], sm.sc[1]);
+            float h = __fmaf_rn(tt, sm.pre_hada[c], tt);
+            sm.hb[c] = h;
+            sm.zb[c] = __fmul_rn(h, sm.d1[c]);
+        } else {
+            sm.zb[c] = 0.f;
+        }
+    }
+    __syncthreads();
+    // conditioning logits: 4 accumulator sets by j % 4, fma chains over j
+    if (tid < 32) {
+        const int set = (tid >> 3) & 3, k = tid & 7;
+        float acc = 0.f;
+#pragma unroll 16
+        for (int j = set; j < 768; j += 4) acc = __fmaf_rn(sm.hb[j], sm.cond_v[j * 8 + k], acc);
+        sm.part[tid] = acc;
+        __syncwarp();
+        // logits ((C + D) + B) + A, max, one libm exp per lane, the engine's
+        // sum tree e7 + ((e6 + (e5 + e4)) + ((e3 + e2) + (e1 + e0)))
+        float lg = __fadd_rn(__fadd_rn(__fadd_rn(sm.part[16 + k], sm.part[24 + k]), sm.part[8 + k]), sm.part[k]);
+        float mx = lg;
+#pragma unroll
+        for (int off = 1; off < 8; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        float e = lexpf(__fsub_rn(lg, mx));
+        float ev[8];
+#pragma unroll
+        for (int qq = 0; qq < 8; qq++) ev[qq] = __shfl_sync(0xffffffffu, e, qq);
+        float sum = __fadd_rn(ev[7], __fadd_rn(__fadd_rn(ev[6], __fadd_rn(ev[5], ev[4])), __fadd_rn(__fadd_rn(ev[3], ev[2]), __fadd_rn(ev[1], ev[0]))));
+        if (tid < 8) sm.wk[k] = __fmul_rn(e, __fdiv_rn(1.0f, sum));
+    }
+    // stage 1: t1 = (A0^T z) A1
+    kron_row_pass1(sm.kf[0], sm.zb, sm.mb, r, c0);
+    __syncthreads();
+    kron_row_pass2(sm.mb, sm.kf[1], sm.tb, r, c0);
+    __syncthreads();
+    // z = fma(t1[perm1[j]], cond[j] * d2[j], b2[j]), cond = 1 + sum_k w_k u_k, then SiLU
+    for (int j = tid; j < 1024; j += POST_THREADS) {
+        float cnd = 1.0f;
+#pragma unroll
+        for (int kk = 0; kk < 8; kk++) cnd = __fmaf_rn(sm.cond_u[kk * 1024 + j], sm.wk[kk], cnd);
+        float zz = __fmaf_rn(sm.tb[sm.perm1[j]], __fmul_rn(cnd, sm.d2[j]), sm.b2[j]);
+        sm.zb[j] = __fdiv_rn(zz, __fadd_rn(nexp(-zz), 1.0f));
+    }
+    __syncthreads();
+    kron_row_pass1(sm.kf[2], sm.zb, sm.mb, r, c0);
+    __syncthreads();
+    kron_row_pass2(sm.mb, sm.kf[3], sm.tb, r, c0);
+    __syncthreads();
+    for (int j = tid; j < 1024; j += POST_THREADS) sm.zb[j] = __fmul_rn(sm.tb[sm.perm2[j]], sm.d3[j]);
+    __syncthreads();
+    kron_row_pass1(sm.kf[4], sm.zb, sm.mb, r, c0);
+    __syncthreads();
+    kron_row_pass2(sm.mb, sm.kf[5], sm.tb, r, c0);
+    __syncthreads();
+    // mHC write (infer.rs:1587-1606): y = x2 + mlp - u, stream a =
+    // y * hpost[a] + sum_b old[b] * hres[a][b]
+    float* xr = xs + (size_t)m * 3072;
+    for (int ch = tid; ch < 768; ch += POST_THREADS) {
+        float mlp = __fmul_rn(sm.tb[ch], sm.d4[ch]);
+        float y = __fsub_rn(__fadd_rn(sm.x2[ch], mlp), u[(size_t)m * 768 + ch]);
+        float old[4];
+#pragma unroll
+        for (int bb = 0; bb < 4; bb++) old[bb] = xr[bb * 768 + ch];
+#pragma unroll
+        for (int aa = 0; aa < 4; aa++) {
+            float v = __fmul_rn(y, sm.gr[aa]);
+#pragma unroll
+            for (int bb = 0; bb < 4; bb++) v = __fmaf_rn(old[bb], sm.gr[4 + aa * 4 + bb], v);
+            xr[aa * 768 + ch] = v;
+        }
+    }
+}
+
 void launch_post_block(LayerW w, const float* o, const float* x1, const float* u, const float* gates, const int32_t* perm1,
                        const int32_t* perm2, int M, float* xs, cudaStream_t st) {
     COUNT_LAUNCH();
+    if (M <= POST_ROW_MAX_M) {
+        launch_pdl(post_row_kernel, dim3(M), dim3(POST_THREADS), POST_ROW_SMEM, st, w, o, x1, u, gates, perm1, perm2, xs);
+        return;
+    }
     launch_pdl(post_block_kernel, dim3(cdiv(M, POST_ROWS)), dim3(POST_THREADS), POST_SMEM, st, w, o, x1, u, gates, perm1, perm2, M, xs);
 }
 

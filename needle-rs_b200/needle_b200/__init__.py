@@ -124,9 +124,12 @@ class CQMat:
         self._h = h.value
 
     def __del__(self):
-        if getattr(self, "_h", None):
-            lib().nd_cqmat_free(self._h)
-            self._h = None
+        try:
+            if getattr(self, "_h", None):
+                lib().nd_cqmat_free(self._h)
+                self._h = None
+        except Exception:  # interpreter shutdown
+            pass
 
     def __call__(self, x, T=1, reps=0):
         """y [M][out] for x [M][768]; with reps > 0 returns (y, ms per run)."""
@@ -166,9 +169,12 @@ class Model:
          self.qk_head_dim, self.v_head_dim, self.max_seq_len) = (int(v) for v in dims)
 
     def __del__(self):
-        if getattr(self, "_h", None):
-            lib().nd_model_free(self._h)
-            self._h = None
+        try:
+            if getattr(self, "_h", None):
+                lib().nd_model_free(self._h)
+                self._h = None
+        except Exception:  # interpreter shutdown
+            pass
 
     def batch(self, num_seqs: int, max_len: int) -> "Batch":
         return Batch(self, num_seqs, max_len)
@@ -191,9 +197,12 @@ class Batch:
         self.max_len = max_len
 
     def __del__(self):
-        if getattr(self, "_h", None):
-            lib().nd_batch_free(self._h)
-            self._h = None
+        try:
+            if getattr(self, "_h", None):
+                lib().nd_batch_free(self._h)
+                self._h = None
+        except Exception:  # interpreter shutdown
+            pass
 
     def __len__(self):
         return lib().nd_batch_len(self._h)
