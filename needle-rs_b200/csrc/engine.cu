@@ -354,6 +354,11 @@ struct Batch {
     cudaStream_t st2 = nullptr;
     cudaEvent_t ev_fork = nullptr;
     std::vector<cudaEvent_t> ev_site;
+    // The post block's gates (hpost, Sinkhorn) depend only on the mHC read,
+    // so each layer computes them on a third stream while its matmuls and
+    // attention run; the post block waits for them.
+    cudaStream_t st3 = nullptr;
+    std::vector<cudaEvent_t> ev_mhc, ev_gates;
     int len = 0;          // positions fed to every sequence
     int hist_base = 0;    // first position whose pre-tap row the conv may read
     bool rope_valid = false;
@@ -395,7 +400,11 @@ struct Batch {
         for (auto& g : graph)
             if (g.exec) cudaGraphExecDestroy(g.exec);
         if (st2) cudaStreamSynchronize(st2);
+        if (st3) cudaStreamSynchronize(st3);
         for (auto e : ev_site) cudaEventDestroy(e);
+        for (auto e : ev_mhc) cudaEventDestroy(e);
+        for (auto e : ev_gates) cudaEventDestroy(e);
+        if (st3) cudaStreamDestroy(st3);
         if (ev_fork) cudaEventDestroy(ev_fork);
         if (st2) cudaStreamDestroy(st2);
         if (st) cudaStreamDestroy(st);
@@ -420,6 +429,11 @@ static Batch* batch_new(Model* m, int S, int max_len) {
     const int L = c.L, nsites = (int)c.sites.size();
     b.ev_site.resize(nsites);
     for (auto& e : b.ev_site) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    CK(cudaStreamCreateWithFlags(&b.st3, cudaStreamNonBlocking));
+    b.ev_mhc.resize(L);
+    b.ev_gates.resize(L);
+    for (auto& e : b.ev_mhc) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    for (auto& e : b.ev_gates) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     const size_t M = b.Mmax;
     b.c.S = S;
     b.c.L = L;
@@ -531,6 +545,10 @@ static int chunk(Batch& b, const int32_t* ids, int T, int outputs) {
         launch_mhc_read(w, lane, b.xs, M, b.u, b.p, site >= 0 ? b.ekv + (size_t)site * b.Mmax * 1536 : nullptr,
                         site >= 0 ? b.evals + (size_t)site * b.Mmax * 768 : nullptr, b.x1, b.act, b.sx, st);
         tick(b, ND_SITE_MHC);
+        CK(cudaEventRecord(b.ev_mhc[l], st));
+        CK(cudaStreamWaitEvent(b.st3, b.ev_mhc[l], 0));
+        launch_mhc_gates(w, lane, M, b.p, b.st3);
+        CK(cudaEventRecord(b.ev_gates[l], b.st3));
         tick(b, ND_SITE_QKVG);
         launch_cq_gemm(w.qkvg, b.act, b.sx, M, T, b.proj, 1568, 0, st);
         tick(b, ND_SITE_QKVG);
@@ -543,6 +561,7 @@ static int chunk(Batch& b, const int32_t* ids, int T, int outputs) {
         tick(b, ND_SITE_OUT);
         launch_cq_gemm(w.out, b.act, b.sx, M, T, b.o, 768, 0, st);
         tick(b, ND_SITE_OUT);
+        CK(cudaStreamWaitEvent(st, b.ev_gates[l], 0));
         if (l == b.debug_layer) {
             snap(b, "snap.u", b.u, (size_t)M * 768);
             snap(b, "snap.p", b.p, (size_t)M * 24);

@@ -739,9 +739,9 @@ void launch_engram_conv(const float* taps, Caches c, int site, int nsites, int S
 // ------------------------------------------------------------ mHC read
 
 // The mHC read CTA: its six warps (192 threads) each own 16 consecutive
-// elements of the row's 3072 per thread; afterwards warp 5 runs the
-// Sinkhorn while warps 0-4 (160 threads) run the input norm, synchronising
-// among themselves with a named barrier.
+// elements of the row's 3072 per thread; afterwards warp 5 stores the post
+// block's gate projections while warps 0-4 (160 threads) run the input
+// norm, synchronising among themselves with a named barrier.
 constexpr int MHC_THREADS = 192, MHC_NORM_THREADS = 160, MHC_XS = 196;
 __device__ __forceinline__ void norm_bar() { asm volatile("bar.sync 1, 160;\n" ::: "memory"); }
 
@@ -774,8 +774,8 @@ __device__ __forceinline__ int reduce4_scatter(const int s[4], int ln) {
 // infer.rs:1359-1426 for one row per CTA. The lanes are normalized by one
 // rms and quantized to int8 (no rotation) in registers; the 24 int8 gate
 // dots are per-thread dp4a partials over 16-byte runs of the gate rows,
-// reduced exactly across the CTA. Then warp 5 runs the post block's gates
-// (hres by sinkhorn64, 2501-2525, and hpost; infer.rs:1580-1586) while warps
+// reduced exactly across the CTA. Then warp 5 stores the post block's gate
+// projections for mhc_gates_kernel while warps
 // 0-4 form u from the pre gates, apply the engram gate (when the layer has a
 // site: ekv [M][1536] keys, evals [M][768]), the input ZC-RMSNorm and A8 of
 // the normed row (act/sx for the q|k|v|gate matmul; x1o is the residual).
@@ -880,40 +880,14 @@ __global__ void __launch_bounds__(MHC_THREADS, 8) mhc_read_kernel(LayerW w, int 
     }
     __syncthreads();
     if (warp == 5) {
-        // hpost (lanes 16-19) and the 4x4 Sinkhorn in f64, lanes 0-15 one
-        // element each: the pairwise row and column sums are xor-shuffles,
-        // which add (e0 + e1) + (e2 + e3) as the reference does
-        const unsigned F = 0xffffffffu;
-        float pk = 0.f;
+        // the post block's gate projections (pr[4..23]) into gates[m][4..23];
+        // mhc_gates_kernel turns them into hpost and the Sinkhorn matrix
         if (ln < 20) {
             int tot = 0;
 #pragma unroll
             for (int wp = 0; wp < 6; wp++) tot += red24[wp][4 + ln];
-            pk = __fmul_rn(__fmul_rn(sxv, w.phi_s[4 + ln]), (float)tot);
+            p[(size_t)m * 24 + 4 + ln] = __fmul_rn(__fmul_rn(sxv, w.phi_s[4 + ln]), (float)tot);
         }
-        const float pj = __shfl_sync(F, pk, ln & 3);
-        const float pres = __shfl_sync(F, pk, (ln & 15) + 4);
-        if (ln >= 16 && ln < 20) {
-            const int j = ln - 16;
-            float off = j == lane_own ? 0.0f : -4.0f;
-            float z = __fadd_rn(__fadd_rn(__fmul_rn(pj, w.a_post), off), w.b_post[j]);
-            p[(size_t)m * 24 + j] = __fdiv_rn(2.0f, __fadd_rn(lexpf(-z), 1.0f));
-        }
-        const int rr = (ln & 15) >> 2;
-        float zr = ln < 16 ? __fmaf_rn(pres, w.a_res, w.b_res[ln & 15]) : 0.f;
-        float zm = fmaxf(fmaxf(__shfl_sync(F, zr, rr * 4), __shfl_sync(F, zr, rr * 4 + 1)),
-                         fmaxf(__shfl_sync(F, zr, rr * 4 + 2), __shfl_sync(F, zr, rr * 4 + 3)));
-        double e = exp(__dsub_rn((double)zr, (double)zm));
-        for (int it = 0; it < 20; it++) {
-            // __drcp_rn is the correctly rounded 1.0 / x
-            double s2 = __dadd_rn(e, __shfl_xor_sync(F, e, 1));
-            double s4 = __dadd_rn(s2, __shfl_xor_sync(F, s2, 2));
-            e = __dmul_rn(e, __drcp_rn(s4));
-            double c2 = __dadd_rn(e, __shfl_xor_sync(F, e, 4));
-            double c4 = __dadd_rn(c2, __shfl_xor_sync(F, c2, 8));
-            e = __dmul_rn(e, __drcp_rn(c4));
-        }
-        if (ln < 16) p[(size_t)m * 24 + 4 + ln] = (float)e;
         return;
     }
     const int lt = tid;  // 0..159
@@ -989,6 +963,51 @@ void launch_mhc_read(LayerW w, int lane, const float* xs, int M, float* u, float
                      float* x1, int8_t* act, float* sx, cudaStream_t st) {
     COUNT_LAUNCH();
     launch_pdl(mhc_read_kernel, dim3(M), dim3(MHC_THREADS), 0, st, w, lane, xs, u, p, ekv, evals, x1, act, sx);
+}
+
+// infer.rs:1580-1586 for one row per warp, from the projections the mHC read
+// left in gates[m][4..23] (pr[4..7] for hpost, pr[8..23] for the residual
+// mix): lanes 16-19 hpost, lanes 0-15 the 4x4 Sinkhorn (sinkhorn64,
+// 2501-2525) in f64, one element each: the pairwise row and column sums are
+// xor-shuffles, which add (e0 + e1) + (e2 + e3) as the reference does. The
+// results replace the row's gates[0..19]: hpost[4], then hres[16].
+__global__ void __launch_bounds__(256) mhc_gates_kernel(LayerW w, int lane_own, int M, float* p) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int m = blockIdx.x * 8 + (threadIdx.x >> 5), ln = threadIdx.x & 31;
+    if (m >= M) return;
+    const unsigned F = 0xffffffffu;
+    float* g = p + (size_t)m * 24;
+    const float pk = ln < 20 ? g[4 + ln] : 0.f;
+    const float pj = __shfl_sync(F, pk, ln & 3);
+    const float pres = __shfl_sync(F, pk, (ln & 15) + 4);
+    const int rr = (ln & 15) >> 2;
+    float zr = ln < 16 ? __fmaf_rn(pres, w.a_res, w.b_res[ln & 15]) : 0.f;
+    float zm = fmaxf(fmaxf(__shfl_sync(F, zr, rr * 4), __shfl_sync(F, zr, rr * 4 + 1)),
+                     fmaxf(__shfl_sync(F, zr, rr * 4 + 2), __shfl_sync(F, zr, rr * 4 + 3)));
+    double e = exp(__dsub_rn((double)zr, (double)zm));
+    for (int it = 0; it < 20; it++) {
+        // __drcp_rn is the correctly rounded 1.0 / x
+        double s2 = __dadd_rn(e, __shfl_xor_sync(F, e, 1));
+        double s4 = __dadd_rn(s2, __shfl_xor_sync(F, s2, 2));
+        e = __dmul_rn(e, __drcp_rn(s4));
+        double c2 = __dadd_rn(e, __shfl_xor_sync(F, e, 4));
+        double c4 = __dadd_rn(c2, __shfl_xor_sync(F, c2, 8));
+        e = __dmul_rn(e, __drcp_rn(c4));
+    }
+    __syncwarp();  // every lane has read its projection before any is replaced
+    if (ln >= 16 && ln < 20) {
+        const int j = ln - 16;
+        float off = j == lane_own ? 0.0f : -4.0f;
+        float z = __fadd_rn(__fadd_rn(__fmul_rn(pj, w.a_post), off), w.b_post[j]);
+        g[j] = __fdiv_rn(2.0f, __fadd_rn(lexpf(-z), 1.0f));
+    }
+    if (ln < 16) g[4 + ln] = (float)e;
+}
+
+void launch_mhc_gates(LayerW w, int lane, int M, float* gates, cudaStream_t st) {
+    COUNT_LAUNCH();
+    launch_pdl(mhc_gates_kernel, dim3(cdiv(M, 8)), dim3(256), 0, st, w, lane, M, gates);
 }
 
 // ------------------------------------------------ conv taps, RoPE, int8 KV

@@ -79,13 +79,17 @@ void launch_cq_gemm(DevMat W, const int8_t* act, const float* sx, int M, int T, 
 void launch_engram_gather(DevMat tables, Caches c, int S, int T, int p0, int slots, float* e, cudaStream_t st);
 void launch_engram_vhist(const float* kv, Caches c, int site, int nsites, int S, int T, int p0, cudaStream_t st);
 void launch_engram_conv(const float* taps, Caches c, int site, int nsites, int S, int T, int p0, float* v, cudaStream_t st);
-// u [M][768]; gates [M][24]: the post block's hpost[4] then the Sinkhorn
-// matrix hres[16] (infer.rs:1580-1586), from this layer's gate projections.
+// u [M][768]; gates [M][24]: the gate projections the post block's gates
+// come from (see launch_mhc_gates).
 // The same CTA then applies the engram gate (ekv [M][1536] and evals
 // [M][768] of the layer's site, or both NULL), the input norm, and A8 of the
 // normed row: x1 [M][768] (the residual), act/sx for the q|k|v|gate matmul.
 void launch_mhc_read(LayerW w, int lane, const float* xs, int M, float* u, float* gates, const float* ekv,
                      const float* evals, float* x1, int8_t* act, float* sx, cudaStream_t st);
+// gates [M][24] holds the post block's gate projections in [4..23] after
+// launch_mhc_read; this turns them into hpost [0..3] and the Sinkhorn
+// matrix hres [4..19].
+void launch_mhc_gates(LayerW w, int lane, int M, float* gates, cudaStream_t st);
 void launch_conv_rope_kv(LayerW w, int l, const float* proj, Caches c, int S, int T, int p0, int hist_base, const float* cosr,
                          const float* sinr, float* qbuf, cudaStream_t st);
 void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int S, int T, int p0, int window, float* att,
