@@ -1168,8 +1168,10 @@ struct AttSmem {
     int vg[ATT_MAXGROUPS][64];
     float ks[ATT_MAXCHUNK], vs[ATT_MAXCHUNK];
     float s[ATT_HEADS][ATT_MAXCHUNK];
-    int8_t dig[ATT_HEADS][3][4 * ATT_MAXGROUPS];
-    int8_t q8[ATT_HEADS][48];
+    // digits of value group g (positions 4g..4g+3): hi, mid, lo words at
+    // bytes 16 g, 16 g + 4, 16 g + 8 (one 16-byte load per group)
+    __align__(16) int8_t dig[ATT_HEADS][16 * ATT_MAXGROUPS];
+    __align__(16) int8_t q8[ATT_HEADS][48];
     // followed by parts: [ATT_HEADS][count][66] floats (m, sum, o[64])
 };
 
@@ -1212,7 +1214,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbu
     };
     issue_chunk(0);
     const float* g = proj + (size_t)m * 1568 + 800 + hh * 64;
-    const float g0v = g[lane], g1v = g[lane + 32];
+    const float2 gv = *(const float2*)(g + 2 * lane);  // this lane's two dimensions
+    const float g0v = gv.x, g1v = gv.y;
     float qs;
     {
         // quant_i8 of this head's query, scale folded with 1/sqrt(48) (infer.rs:1885)
@@ -1232,13 +1235,27 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbu
         asm volatile("cp.async.wait_group 0;\n" ::);
         __syncthreads();
         // scores: (ks * dot) * qs in whole 4-blocks, (ks * qs) * dot after
-        const int* qr = (const int*)sm.q8[h];
+        int qr[12];
+#pragma unroll
+        for (int e = 0; e < 3; e++) {
+            const int4 v = ((const int4*)sm.q8[h])[e];
+            qr[4 * e] = v.x;
+            qr[4 * e + 1] = v.y;
+            qr[4 * e + 2] = v.z;
+            qr[4 * e + 3] = v.w;
+        }
         float mx = -INFINITY;
         for (int k = lane; k < len; k += 32) {
-            const int* kr = (const int*)sm.k[k];
+            const int4* kr = (const int4*)sm.k[k];
             int dot = 0;
 #pragma unroll
-            for (int e = 0; e < 12; e++) dot = __dp4a(qr[e], kr[e], dot);
+            for (int e = 0; e < 3; e++) {
+                const int4 kv = kr[e];
+                dot = __dp4a(qr[4 * e], kv.x, dot);
+                dot = __dp4a(qr[4 * e + 1], kv.y, dot);
+                dot = __dp4a(qr[4 * e + 2], kv.z, dot);
+                dot = __dp4a(qr[4 * e + 3], kv.w, dot);
+            }
             float ksv = sm.ks[k];
             float sv = k < blocked ? __fmul_rn(__fmul_rn(ksv, (float)dot), qs) : __fmul_rn(__fmul_rn(ksv, qs), (float)dot);
             srow[k] = sv;
@@ -1285,18 +1302,19 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbu
         for (int kk = lane; kk < 4 * ng; kk += 32) {
             const int k = kk - off;
             int wq = k >= 0 && k < len ? (int)roundf(__fmul_rn(srow[k], qw)) : 0;
-            sm.dig[h][0][kk] = (int8_t)(wq >> 14);
-            sm.dig[h][1][kk] = (int8_t)((wq >> 7) & 127);
-            sm.dig[h][2][kk] = (int8_t)(wq & 127);
+            int8_t* dg = sm.dig[h] + (kk >> 2) * 16 + (kk & 3);
+            dg[0] = (int8_t)(wq >> 14);
+            dg[4] = (int8_t)((wq >> 7) & 127);
+            dg[8] = (int8_t)(wq & 127);
         }
         __syncwarp();
-        // P.V: three exact integer dots per value dimension (lane, lane + 32)
-        const int* dh = (const int*)sm.dig[h][0];
-        const int* dmid = (const int*)sm.dig[h][1];
-        const int* dl = (const int*)sm.dig[h][2];
+        // P.V: three exact integer dots per value dimension (2 lane, 2 lane + 1)
+        const int4* dg4 = (const int4*)sm.dig[h];
         int sh0 = 0, sm0 = 0, sl0 = 0, sh1 = 0, sm1 = 0, sl1 = 0;
         for (int w = 0; w < ng; w++) {
-            int a0 = dh[w], a1 = dmid[w], a2 = dl[w], x0 = sm.vg[w][lane], x1 = sm.vg[w][lane + 32];
+            const int4 dd = dg4[w];
+            const int2 xv = *(const int2*)&sm.vg[w][2 * lane];
+            int a0 = dd.x, a1 = dd.y, a2 = dd.z, x0 = xv.x, x1 = xv.y;
             sh0 = __dp4a(a0, x0, sh0);
             sm0 = __dp4a(a1, x0, sm0);
             sl0 = __dp4a(a2, x0, sl0);
@@ -1306,8 +1324,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbu
         }
         const float cw = __fmul_rn(wm, ND_C21);
         float* pr = parts + ci * 66;
-        pr[2 + lane] = __fmul_rn(__fmaf_rn(16384.f, (float)sh0, __fmaf_rn(128.f, (float)sm0, (float)sl0)), cw);
-        pr[34 + lane] = __fmul_rn(__fmaf_rn(16384.f, (float)sh1, __fmaf_rn(128.f, (float)sm1, (float)sl1)), cw);
+        pr[2 + 2 * lane] = __fmul_rn(__fmaf_rn(16384.f, (float)sh0, __fmaf_rn(128.f, (float)sm0, (float)sl0)), cw);
+        pr[3 + 2 * lane] = __fmul_rn(__fmaf_rn(16384.f, (float)sh1, __fmaf_rn(128.f, (float)sm1, (float)sl1)), cw);
         if (lane == 0) {
             pr[0] = mx;
             pr[1] = sum;
@@ -1322,8 +1340,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbu
     float out0, out1;
     if (count == 1) {
         float inv = __fdiv_rn(1.0f, parts[1]);
-        out0 = __fmul_rn(parts[2 + lane], inv);
-        out1 = __fmul_rn(parts[34 + lane], inv);
+        out0 = __fmul_rn(parts[2 + 2 * lane], inv);
+        out1 = __fmul_rn(parts[3 + 2 * lane], inv);
     } else {
         float big = -1e30f;
         for (int ci = 0; ci < count; ci++) big = fmaxf(big, parts[ci * 66]);
@@ -1331,8 +1349,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbu
         for (int ci = 0; ci < count; ci++) {
             const float* pr = parts + ci * 66;
             float wv = lexpf(__fsub_rn(pr[0], big));
-            a0 = __fmaf_rn(pr[2 + lane], wv, a0);
-            a1 = __fmaf_rn(pr[34 + lane], wv, a1);
+            a0 = __fmaf_rn(pr[2 + 2 * lane], wv, a0);
+            a1 = __fmaf_rn(pr[3 + 2 * lane], wv, a1);
             total = __fmaf_rn(wv, pr[1], total);
         }
         float inv = __fdiv_rn(1.0f, total);
@@ -1342,14 +1360,13 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbu
     float* o = att + (size_t)m * 768 + hh * 64;
     float y0 = __fdiv_rn(out0, __fadd_rn(nexp(-g0v), 1.0f));
     float y1 = __fdiv_rn(out1, __fadd_rn(nexp(-g1v), 1.0f));
-    o[lane] = y0;
-    o[lane + 32] = y1;
+    *(float2*)(o + 2 * lane) = make_float2(y0, y1);
     // A8 of the out projection's input (infer.rs:1556): this CTA's six heads
     // are exactly the 128-wide groups 3 kvh .. 3 kvh + 2.
     __syncthreads();
     float* gated = sm.s[0];  // [6][64] gated outputs, head-major
-    gated[h * 64 + lane] = y0;
-    gated[h * 64 + lane + 32] = y1;
+    gated[h * 64 + 2 * lane] = y0;
+    gated[h * 64 + 2 * lane + 1] = y1;
     __syncthreads();
     if (h < 3) {
         float v[4];
