@@ -87,12 +87,15 @@ int nd_head_logits_sparse(nd_batch* b, const float* h, const int* ids, int n, fl
  * in the reference, which runs on the CPU. */
 void* nd_batch_stream(nd_batch* b);
 
-/* crates/needle-core/src/quant.rs:233-256 (cq_pack, bits 4, group 128):
- * w[rows][d] to codes[rows][ceil(d/128)*64] and f16 norms[rows][ceil(d/128)]. */
-int nd_cq_pack(const float* w, int rows, int d, unsigned char* codes, unsigned short* norms);
+/* crates/needle-core/src/quant.rs:233-256 (cq_pack, group 128) at bits 2,
+ * 3, 4 or 5 (ternary; quant.rs:11-12): w[rows][d] to codes[rows][G * 16 *
+ * width] (G = ceil(d/128), width = bits, 2 for ternary; LSB-first) and f16
+ * norms[rows][G]. The reference's packer takes bits 4 only; the other widths
+ * are written in the layout its loader reads (qlinear.rs:220-236). */
+int nd_cq_pack(const float* w, int rows, int d, int bits, unsigned char* codes, unsigned short* norms);
 
-/* Test and benchmark support: one CQ-4 matrix (codes [out][6][64], f16
- * norms [out][6] as quant.rs:233-256 packs them; in_dim 768) on GPU
+/* Test and benchmark support: one CQ matrix (codes [out][6][16 * width],
+ * f16 norms [out][6] as nd_cq_pack writes them at `bits`; in_dim 768) on GPU
  * `device`, and the engine's matmul of host rows x[M][768] into y[M][out]:
  * each row quantized as QAct::new (qlinear.rs:152-207), then the decode
  * combine (qlinear.rs:340-350) when T == 1, else the prefill combine
@@ -100,19 +103,23 @@ int nd_cq_pack(const float* w, int rows, int d, unsigned char* codes, unsigned s
  * of T). With reps > 0 and ms != NULL it also times reps back-to-back runs
  * (A8 + matmul, inputs resident) and stores the mean in *ms. */
 typedef struct nd_cqmat nd_cqmat;
-int nd_cqmat_new(int device, const unsigned char* codes, const unsigned short* norms, int out, int in_dim, nd_cqmat** out_mat);
+int nd_cqmat_new(int device, const unsigned char* codes, const unsigned short* norms, int out, int in_dim, int bits,
+                 nd_cqmat** out_mat);
 void nd_cqmat_free(nd_cqmat* mat);
 int nd_cqmat_apply(nd_cqmat* mat, const float* x, int M, int T, float* y, int reps, float* ms);
 
 /* crates/needle-core/src/cact.rs:399-475 (pack) over random-init Needle 3
- * weights: every tensor ~N(0, std^2), seeded; CQ-4 matrices, f16 small
+ * weights: every tensor ~N(0, std^2), seeded; CQ matrices, f16 small
  * weights, MT19937 Hadamard permutations. Shape knobs let tests shrink the
  * model (num_layers, vocab, engram_slots, sliding_window; engram_sites is
- * a bit mask of layers, global_mask likewise). With out == NULL returns the
- * byte size in *len; else writes up to cap bytes. */
+ * a bit mask of layers, global_mask likewise). cq_bits[i] is the record
+ * bits (2, 3, 4, 5 = ternary) of the i-th CQ record in record order, 4 past
+ * n_cq_bits (a mixed-width archive; the reference's packer writes one
+ * width). With out == NULL returns the byte size in *len; else writes up
+ * to cap bytes. */
 int nd_synth_cact(int num_layers, int vocab, int engram_slots, int sliding_window, unsigned long long global_mask,
-                  unsigned long long engram_sites, unsigned long long seed, float std, unsigned char* out,
-                  unsigned long long cap, unsigned long long* len);
+                  unsigned long long engram_sites, unsigned long long seed, float std, const int* cq_bits, int n_cq_bits,
+                  unsigned char* out, unsigned long long cap, unsigned long long* len);
 
 /* Kernel launches this process has issued (all batches, all devices); no
  * counterpart in the reference. */

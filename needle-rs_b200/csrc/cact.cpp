@@ -1,4 +1,4 @@
-// The `.cact` archive on the host: reader, CQ-4 packer, synthetic writer.
+// The `.cact` archive on the host: reader, CQ packer, synthetic writer.
 // See cact.h; reference citations are paths in the needle-rs repository.
 
 #include "cact.h"
@@ -93,10 +93,14 @@ static const uint64_t LM4[16] = {0xc005ae0f408928fbull, 0xc0005b0b8a516d54ull, 0
                                  0x3ff4688db93b85f1ull, 0x3ffa3164906b428full, 0x4000ace7bbde2442ull, 0x4005ed98d06f2a4aull};
 
 std::vector<float> cq_codebook(int bits, int group) {
-    const uint64_t* t = bits == 2 ? LM2 : bits == 3 ? LM3 : bits == 4 ? LM4 : nullptr;
-    if (!t) throw std::runtime_error("no CQ codebook for this width");
-    int n = 1 << bits;
     double s = std::sqrt((double)group);
+    if (bits == CQ_TERNARY) {  // quant.rs:14, 59: {-c, 0, c}
+        const double c = 1.2240064;
+        return {(float)(-c / s), (float)(0.0 / s), (float)(c / s)};
+    }
+    const uint64_t* t = bits == 2 ? LM2 : bits == 3 ? LM3 : bits == 4 ? LM4 : nullptr;
+    if (!t) throw std::runtime_error("no CQ codebook for " + std::to_string(bits) + " bits");
+    int n = 1 << bits;
     std::vector<float> out(n);
     for (int i = 0; i < n; i++) {
         double c;
@@ -104,6 +108,17 @@ std::vector<float> cq_codebook(int bits, int group) {
         out[i] = (float)(c / s);
     }
     return out;
+}
+
+int cq_width(int bits) {
+    if (bits == CQ_TERNARY) return 2;
+    if (bits >= 2 && bits <= 4) return bits;
+    throw std::runtime_error("CQ records of " + std::to_string(bits) + " bits are not supported");
+}
+
+int cq_centroid(int bits, int code) {
+    if (bits != CQ_TERNARY) return code;
+    return code == 3 ? 0 : code + 1;  // qlinear.rs:225-227
 }
 
 // quant.rs:91-115: unnormalised FWHT, then the 1/sqrt(n) scale.
@@ -119,8 +134,9 @@ static void rotate128(float* x) {
     for (int i = 0; i < 128; i++) x[i] *= s;
 }
 
-void cq_pack4(const float* w, int rows, int d, uint8_t* packed, uint16_t* norms) {
-    static const std::vector<float> cb = cq_codebook(4, 128);
+void cq_pack(const float* w, int rows, int d, int bits, uint8_t* packed, uint16_t* norms) {
+    const std::vector<float> cb = cq_codebook(bits, 128);
+    const int ncb = (int)cb.size(), width = cq_width(bits), bpg = 16 * width;
     const int groups = (d + 127) / 128;
     float g[128];
     uint8_t idx[128];
@@ -136,25 +152,48 @@ void cq_pack4(const float* w, int rows, int d, uint8_t* packed, uint16_t* norms)
             for (int i = 0; i < 128; i++) {
                 float x = g[i] / denom;
                 int pos = 0;  // quant.rs:119-124: nearest, ties to the lower centroid
-                while (pos < 16 && cb[pos] < x) pos++;
-                pos = std::min(std::max(pos, 1), 15);
-                idx[i] = (uint8_t)(std::fabs(x - cb[pos - 1]) <= std::fabs(x - cb[pos]) ? pos - 1 : pos);
+                while (pos < ncb && cb[pos] < x) pos++;
+                pos = std::min(std::max(pos, 1), ncb - 1);
+                int k = std::fabs(x - cb[pos - 1]) <= std::fabs(x - cb[pos]) ? pos - 1 : pos;
+                // a ternary record stores centroid k as code (k + 3) % 4
+                // (the inverse of qlinear.rs:225-227)
+                idx[i] = (uint8_t)(bits == CQ_TERNARY ? (k + 3) % 4 : k);
             }
             norms[(size_t)r * groups + gi] = f32_to_f16(norm);
-            uint8_t* dst = packed + ((size_t)r * groups + gi) * 64;
-            for (int j = 0; j < 64; j++) dst[j] = (uint8_t)(idx[2 * j] | (idx[2 * j + 1] << 4));  // quant.rs:185-198
+            // quant.rs:185-198: LSB-first, 8 codes per `width` bytes
+            uint8_t* dst = packed + ((size_t)r * groups + gi) * bpg;
+            for (int c8 = 0; c8 < 16; c8++) {
+                uint32_t word = 0;
+                for (int i = 0; i < 8; i++) word |= (uint32_t)idx[8 * c8 + i] << (i * width);
+                for (int b = 0; b < width; b++) dst[c8 * width + b] = (uint8_t)(word >> (8 * b));
+            }
         }
     }
 }
 
-void cq_row(const uint8_t* codes, const uint16_t* norms, int groups, int in_dim, size_t r, float* out) {
-    static const std::vector<float> cb = cq_codebook(4, 128);
+void cq_codes(const uint8_t* group_codes, int width, uint8_t out[128]) {
+    for (int c8 = 0; c8 < 16; c8++) {
+        uint32_t word = 0;
+        for (int b = 0; b < width; b++) word |= (uint32_t)group_codes[c8 * width + b] << (8 * b);
+        for (int i = 0; i < 8; i++) out[8 * c8 + i] = (uint8_t)((word >> (i * width)) & ((1u << width) - 1));
+    }
+}
+
+void cq_row(const uint8_t* codes, const uint16_t* norms, int groups, int in_dim, int bits, size_t r, float* out) {
+    const std::vector<float> cb = cq_codebook(bits, 128);
+    const int width = cq_width(bits), bpg = 16 * width;
+    float fv[16];
+    for (int c = 0; c < 16; c++) {
+        int k = cq_centroid(bits, c);
+        fv[c] = c < (1 << width) && k < (int)cb.size() ? cb[k] : 0.f;
+    }
     std::vector<float> buf((size_t)groups * 128);
+    uint8_t idx[128];
     for (int g = 0; g < groups; g++) {
         float norm = f16_to_f32(norms[r * groups + g]);
-        const uint8_t* c = codes + (r * groups + g) * 64;
+        cq_codes(codes + (r * groups + g) * bpg, width, idx);
         float* dst = buf.data() + g * 128;
-        for (int p = 0; p < 128; p++) dst[p] = cb[(p & 1) ? (c[p >> 1] >> 4) : (c[p >> 1] & 15)] * norm;
+        for (int p = 0; p < 128; p++) dst[p] = fv[idx[p]] * norm;
         rotate128(dst);
     }
     std::memcpy(out, buf.data(), sizeof(float) * in_dim);
@@ -253,6 +292,7 @@ std::vector<uint8_t> synth_cact(const SynthSpec& sp) {
     for (int s : sp.engram_sites)
         if (s < 0 || s >= L) throw std::runtime_error("engram site outside the stack");
     std::vector<Out> ts;
+    size_t ncq = 0;
     auto f16 = [&](std::vector<uint32_t> shape) {
         Out o;
         o.dtype = CACT_F16;
@@ -271,7 +311,9 @@ std::vector<uint8_t> synth_cact(const SynthSpec& sp) {
         o.rows = rows;
         o.cols = cols;
         o.group = 128;
-        o.bits = 4;
+        o.bits = (uint32_t)(ncq < sp.cq_bits.size() ? sp.cq_bits[ncq] : 4);
+        cq_width((int)o.bits);
+        ncq++;
         ts.push_back(o);
     };
     // cact.rs:279-352, the canonical order.
@@ -340,10 +382,10 @@ std::vector<uint8_t> synth_cact(const SynthSpec& sp) {
                 std::vector<float> w((size_t)o.rows * o.cols);
                 for (auto& v : w) v = (float)(sp.std * rng.normal());
                 int groups = (o.cols + 127) / 128;
-                size_t npk = (size_t)o.rows * groups * 64;
+                size_t npk = (size_t)o.rows * groups * 16 * cq_width((int)o.bits);
                 o.blob.resize(npk + (size_t)o.rows * groups * 2);
                 std::vector<uint16_t> norms((size_t)o.rows * groups);
-                cq_pack4(w.data(), o.rows, o.cols, o.blob.data(), norms.data());
+                cq_pack(w.data(), o.rows, o.cols, (int)o.bits, o.blob.data(), norms.data());
                 std::memcpy(o.blob.data() + npk, norms.data(), norms.size() * 2);
             }
         }

@@ -36,13 +36,23 @@ struct Config {
     int window(int l) const { return (sw > 0 && !((global_mask >> l) & 1)) ? sw : 0; }
 };
 
+// A projection as the engine runs it: consecutive runs of output rows, one
+// DevMat (one codebook) each; a uniform archive has one run per projection.
+struct Linear {
+    std::vector<DevMat> runs;
+    int out = 0;
+};
+
 struct Model {
     int device = 0;
     Config c;
     std::vector<void*> allocs;
     DevMat embedding;
+    DevMat head;  // the embedding's first out_rows() rows: the tied lm_head
     std::vector<LayerW> layers;
-    std::vector<DevMat> etables, ekv;
+    std::vector<Linear> qkvg, out;  // per layer
+    std::vector<DevMat> etables;
+    std::vector<Linear> ekv;
     std::vector<const float*> etaps;
     std::vector<int> site_of_layer;
     const int32_t *perm1 = nullptr, *perm2 = nullptr;
@@ -113,22 +123,24 @@ static std::vector<float> small_f32(const CactArchive& a, Cursor& cur, size_t ex
 }
 
 struct HostMat {
-    std::vector<uint8_t> codes;
-    std::vector<uint16_t> norms;
+    std::vector<uint8_t> codes;   // [out][groups][16 * width]
+    std::vector<uint16_t> norms;  // [out][groups] f16
     int out = 0, in_dim = 0, groups = 0;
+    int bits = 4;  // the record's bits: 2, 3, 4 or CQ_TERNARY
 };
 
-// qlinear.rs:220-236 (4-bit records, group 128)
+// qlinear.rs:220-236 (group 128; code widths 2, 3, 4 and ternary)
 static HostMat host_mat(const CactArchive& a, Cursor& cur, int in_dim) {
     const CactRecord& r = cur.next(CACT_CQ);
     if (r.group != 128) throw std::runtime_error("CQ group size " + std::to_string(r.group) + " is not supported");
-    if (r.bits != 4) throw std::runtime_error("only 4-bit CQ records are supported by this engine");
     if (r.shape.size() != 2 || (int)r.shape[1] != in_dim) throw std::runtime_error("CQ matrix has the wrong input width");
     HostMat m;
+    m.bits = (int)r.bits;
+    const int width = cq_width(m.bits);
     m.out = (int)r.shape[0];
     m.in_dim = in_dim;
     m.groups = (in_dim + 127) / 128;
-    size_t nc = (size_t)m.out * m.groups * 64, nn = (size_t)m.out * m.groups;
+    size_t nc = (size_t)m.out * m.groups * 16 * width, nn = (size_t)m.out * m.groups;
     if (r.nbytes < nc + nn * 2) throw std::runtime_error("CQ record is truncated");
     const uint8_t* b = a.bytes(cur.i - 1);
     m.codes.assign(b, b + nc);
@@ -137,30 +149,32 @@ static HostMat host_mat(const CactArchive& a, Cursor& cur, int in_dim) {
     return m;
 }
 
-static void append(HostMat& dst, const HostMat& src) {
-    if (dst.out == 0) { dst = src; return; }
-    dst.out += src.out;
-    dst.codes.insert(dst.codes.end(), src.codes.begin(), src.codes.end());
-    dst.norms.insert(dst.norms.end(), src.norms.begin(), src.norms.end());
-}
-
-// qlinear.rs:211-216, 244-265: the shared 4-bit codebook's int8 form.
-static void int8_codebook(int8_t vals[16], float* cbs_out, std::vector<float>* fvals) {
-    std::vector<float> cb = cq_codebook(4, 128);
+// qlinear.rs:211-216, 244-265: a record width's codebook as the kernels
+// read it: code -> int8 value (ternary codes remapped, codes past the
+// codebook 0), its scale, and code -> f32 value.
+static void code_table(int bits, DevMat& d) {
+    const std::vector<float> cb = cq_codebook(bits, 128);
     float mx = 0.f;
     for (float v : cb) mx = std::fmax(mx, std::fabs(v));
     uint32_t k127u = 0x3c010204u;
     float k127;
     std::memcpy(&k127, &k127u, 4);
-    float cbs = mx > 0.f ? mx * k127 : 1.0f;
-    float inv = 1.0f / cbs;
-    for (int i = 0; i < 16; i++) vals[i] = (int8_t)std::min(std::max(std::round(cb[i] * inv), -128.f), 127.f);
-    *cbs_out = cbs;
-    if (fvals) *fvals = cb;
+    const float cbs = mx > 0.f ? mx * k127 : 1.0f;
+    const float inv = 1.0f / cbs;
+    int8_t vals[16] = {0};
+    d.width = cq_width(bits);
+    for (int c = 0; c < 16; c++) {
+        const int k = cq_centroid(bits, c);
+        const bool in = c < (1 << d.width) && k < (int)cb.size();
+        vals[c] = in ? (int8_t)std::min(std::max(std::round(cb[k] * inv), -128.f), 127.f) : 0;
+        d.fvals[c] = in ? cb[k] : 0.f;
+    }
+    std::memcpy(d.vals4, vals, 16);
+    d.cbs = cbs;
 }
 
-// A matrix on the device: the archive's codes and norms, plus (for the
-// projections that run as tensor-core GEMMs) the codes expanded through the
+// A matrix on the device: the archive's codes and norms, its codebook, and
+// (for the projections that run as matmuls) the codes expanded through the
 // int8 codebook into lane-major groups (see DevMat::w8).
 static DevMat to_dev(Model& m, const HostMat& h, bool expand) {
     DevMat d;
@@ -169,25 +183,61 @@ static DevMat to_dev(Model& m, const HostMat& h, bool expand) {
     d.out = h.out;
     d.in_dim = h.in_dim;
     d.groups = h.groups;
+    code_table(h.bits, d);
     if (expand) {
         int8_t vals[16];
-        float cbs;
-        int8_codebook(vals, &cbs, nullptr);
-        const int K = h.groups * 128;
+        std::memcpy(vals, d.vals4, 16);
+        int slot[128];
+        for (int p = 0; p < 128; p++) slot[p] = lane_major_slot(p);
+        const int K = h.groups * 128, bpg = 16 * d.width;
         std::vector<int8_t> w((size_t)h.out * K);
+        uint8_t idx[128];
         for (size_t r = 0; r < (size_t)h.out; r++)
             for (int g = 0; g < h.groups; g++) {
-                const uint8_t* c = h.codes.data() + (r * h.groups + g) * 64;
+                cq_codes(h.codes.data() + (r * h.groups + g) * bpg, d.width, idx);
                 int8_t* dst = w.data() + r * K + g * 128;
-                for (int p = 0; p < 128; p++) {
-                    int code = (p & 1) ? (c[p >> 1] >> 4) : (c[p >> 1] & 15);
-                    int a = p >> 5, l = (p & 31) >> 3, b = p & 7;
-                    dst[l * 32 + a * 8 + b] = vals[code];
-                }
+                for (int p = 0; p < 128; p++) dst[slot[p]] = vals[idx[p]];
             }
         d.w8 = m.upload(w.data(), w.size());
     }
     return d;
+}
+
+// QLinear::new (qlinear.rs:500-518): parts side by side over one input;
+// neighbours of the same record bits share a codebook and become one run,
+// and every part must share the code width (the activation layout).
+static Linear to_linear(Model& m, const std::vector<const HostMat*>& parts) {
+    Linear lin;
+    for (size_t i = 0; i < parts.size();) {
+        if (cq_width(parts[i]->bits) != cq_width(parts[0]->bits))
+            throw std::runtime_error("fused parts must share a code width");
+        size_t j = i;
+        HostMat run;
+        while (j < parts.size() && parts[j]->bits == parts[i]->bits) {
+            const HostMat& p = *parts[j++];
+            if (run.out == 0) {
+                run = p;
+            } else {
+                run.out += p.out;
+                run.codes.insert(run.codes.end(), p.codes.begin(), p.codes.end());
+                run.norms.insert(run.norms.end(), p.norms.begin(), p.norms.end());
+            }
+        }
+        lin.runs.push_back(to_dev(m, run, true));
+        lin.out += run.out;
+        i = j;
+    }
+    return lin;
+}
+
+// Every run of a projection into y[m][col0 ..] (ldy wide), one launch each.
+static void linear(const Linear& lin, const int8_t* act, const float* sx, int M, int T, float* y, int ldy,
+                   cudaStream_t st) {
+    int col = 0;
+    for (const DevMat& d : lin.runs) {
+        CK(launch_cq_gemm(d, act, sx, M, T, y, ldy, col, st));
+        col += d.out;
+    }
 }
 
 // weights.rs:314-497 (record walk, fast mode), infer.rs:938-962 (Tables).
@@ -211,8 +261,11 @@ static Model* load_model(const uint8_t* bytes, size_t n, int device) {
     HostMat emb = host_mat(a, cur, d);
     if (emb.out != c.vocab) throw std::runtime_error("embedding shape does not match the header");
     m.embedding = to_dev(m, emb, true);
+    m.head = m.embedding;
+    m.head.out = c.out_rows();
     m.layers.resize(c.L);
-    std::vector<HostMat> qkvg(c.L);
+    m.qkvg.resize(c.L);
+    m.out.resize(c.L);
     for (int l = 0; l < c.L; l++) {
         LayerW& w = m.layers[l];
         std::memset(&w, 0, sizeof w);
@@ -227,10 +280,8 @@ static Model* load_model(const uint8_t* bytes, size_t n, int device) {
         HostMat g = host_mat(a, cur, d), o = host_mat(a, cur, 768);
         if (q.out != 576 || k.out != 96 || v.out != 128 || g.out != 768 || o.out != d)
             throw std::runtime_error("attention projection shapes do not match the header");
-        HostMat f;
-        append(f, q); append(f, k); append(f, v); append(f, g);
-        w.qkvg = to_dev(m, f, true);
-        w.out = to_dev(m, o, true);
+        m.qkvg[l] = to_linear(m, {&q, &k, &v, &g});
+        m.out[l] = to_linear(m, {&o});
         w.post_norm = m.upload(small_f32(a, cur, d).data(), d);
         w.attn_gate = small_f32(a, cur, 1)[0];
         w.pre_hada = m.upload(small_f32(a, cur, d).data(), d);
@@ -265,7 +316,8 @@ static Model* load_model(const uint8_t* bytes, size_t n, int device) {
         const int base[3] = {l * 4, l * 4, l * 16}, cnt[3] = {4, 4, 16};
         for (int part = 0; part < 3; part++)
             for (int rr = 0; rr < cnt[part]; rr++, k++) {
-                cq_row(phi[part].codes.data(), phi[part].norms.data(), phi[part].groups, nc, base[part] + rr, row.data());
+                cq_row(phi[part].codes.data(), phi[part].norms.data(), phi[part].groups, nc, phi[part].bits, base[part] + rr,
+                       row.data());
                 s[k] = quant_i8(row.data(), nc, q.data() + (size_t)k * nc);
             }
         w.phi_q = m.upload(q.data(), q.size());
@@ -285,11 +337,8 @@ static Model* load_model(const uint8_t* bytes, size_t n, int device) {
         HostMat t = host_mat(a, cur, 128);
         if (t.out != c.ntables * c.eslots) throw std::runtime_error("engram table shape does not match the header");
         HostMat k = host_mat(a, cur, d), v = host_mat(a, cur, d);
-        HostMat kv;
-        append(kv, k);
-        append(kv, v);
         m.etables.push_back(to_dev(m, t, false));
-        m.ekv.push_back(to_dev(m, kv, true));
+        m.ekv.push_back(to_linear(m, {&k, &v}));
         auto taps = small_f32(a, cur, 4 * (size_t)d);
         m.etaps.push_back(m.upload(taps.data(), taps.size()));
     }
@@ -325,11 +374,7 @@ static Model* load_model(const uint8_t* bytes, size_t n, int device) {
     m.rope_sin = m.upload(ts.data(), ts.size());
     m.sd = m.upload(m.h_sd.data(), half);
     m.cd = m.upload(m.h_cd.data(), half);
-    int8_t vals[16];
-    float cbs = 0.f;
-    std::vector<float> cb;
-    int8_codebook(vals, &cbs, &cb);
-    set_constants(vals, cb.data(), cbs, (float)(1.0 / std::sqrt(128.0)));
+    set_constants((float)(1.0 / std::sqrt(128.0)));
     CK(cudaGetLastError());
     CK(cudaDeviceSynchronize());
     return mp.release();
@@ -529,7 +574,7 @@ static int chunk(Batch& b, const int32_t* ids, int T, int outputs) {
             launch_engram_gather(m.etables[s], b.c, S, T, p0, c.eslots, b.e, s2);
             launch_prep_act(b.e, 768, 768, M, b.act_e, b.sx_e, s2);
             tick(b, ND_SITE_ENGRAM_KV, s2);
-            launch_cq_gemm(m.ekv[s], b.act_e, b.sx_e, M, T, kv, 1536, 0, s2);
+            linear(m.ekv[s], b.act_e, b.sx_e, M, T, kv, 1536, s2);
             tick(b, ND_SITE_ENGRAM_KV, s2);
             launch_engram_vhist(kv, b.c, s, nsites, S, T, p0, s2);
             launch_engram_conv(m.etaps[s], b.c, s, nsites, S, T, p0, b.evals + (size_t)s * b.Mmax * 768, s2);
@@ -550,7 +595,7 @@ static int chunk(Batch& b, const int32_t* ids, int T, int outputs) {
         launch_mhc_gates(w, lane, M, b.p, b.st3);
         CK(cudaEventRecord(b.ev_gates[l], b.st3));
         tick(b, ND_SITE_QKVG);
-        launch_cq_gemm(w.qkvg, b.act, b.sx, M, T, b.proj, 1568, 0, st);
+        linear(m.qkvg[l], b.act, b.sx, M, T, b.proj, 1568, st);
         tick(b, ND_SITE_QKVG);
         tick(b, ND_SITE_CONV);
         launch_conv_rope_kv(w, l, b.proj, b.c, S, T, p0, b.hist_base, b.cosr, b.sinr, b.qbuf, st);
@@ -559,7 +604,7 @@ static int chunk(Batch& b, const int32_t* ids, int T, int outputs) {
         launch_attention(b.qbuf, b.proj, b.c, l, S, T, p0, c.window(l), b.att, b.act, b.sx, st);
         tick(b, ND_SITE_ATTENTION);
         tick(b, ND_SITE_OUT);
-        launch_cq_gemm(w.out, b.act, b.sx, M, T, b.o, 768, 0, st);
+        linear(m.out[l], b.act, b.sx, M, T, b.o, 768, st);
         tick(b, ND_SITE_OUT);
         CK(cudaStreamWaitEvent(st, b.ev_gates[l], 0));
         if (l == b.debug_layer) {
@@ -593,7 +638,7 @@ static int chunk(Batch& b, const int32_t* ids, int T, int outputs) {
         launch_prep_act(b.h, 768, 768, rows, b.act, b.sx, st);
         // infer.rs:1135-1141: QAct of one row each, so the decode combine
         tick(b, ND_SITE_LM_HEAD);
-        launch_cq_gemm(m.embedding, b.act, b.sx, rows, 1, b.logits, c.out_rows(), 0, st);
+        CK(launch_cq_gemm(m.head, b.act, b.sx, rows, 1, b.logits, c.out_rows(), 0, st));
         tick(b, ND_SITE_LM_HEAD);
         b.have_logits = true;
         b.logits_rows = rows;
@@ -654,7 +699,7 @@ struct nd_model {
 // The tied lm_head matrix of a loaded model (for noalloc.cu).
 bool nd::model_head(const nd_model* mh, DevMat* emb, int* device, int* out_rows) {
     if (!mh || !mh->m) return false;
-    *emb = mh->m->embedding;
+    *emb = mh->m->head;
     *device = mh->m->device;
     *out_rows = mh->m->c.out_rows();
     return true;
@@ -836,7 +881,7 @@ int nd_head_logits(nd_batch* bh, const float* h, int rows, float* out, int flags
                            b.st));
         ensure_logits(b, rows);
         launch_prep_act(b.e, 768, 768, rows, b.act, b.sx, b.st);
-        launch_cq_gemm(m.embedding, b.act, b.sx, rows, 1, b.logits, m.c.out_rows(), 0, b.st);
+        CK(launch_cq_gemm(m.head, b.act, b.sx, rows, 1, b.logits, m.c.out_rows(), 0, b.st));
         b.have_logits = false;
         CK(cudaMemcpyAsync(out, b.logits, (size_t)rows * m.c.out_rows() * sizeof(float),
                            dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, b.st));
@@ -863,7 +908,7 @@ int nd_head_logits_sparse(nd_batch* bh, const float* h, const int* ids, int n, f
         CK(cudaMemcpyAsync(b.e, h4.data(), 4 * 768 * sizeof(float), cudaMemcpyHostToDevice, b.st));
         ensure_logits(b, 4);
         launch_prep_act(b.e, 768, 768, 4, b.act, b.sx, b.st);
-        launch_cq_gemm(m.embedding, b.act, b.sx, 4, 4, b.logits, V, 0, b.st);
+        CK(launch_cq_gemm(m.head, b.act, b.sx, 4, 4, b.logits, V, 0, b.st));
         b.have_logits = false;
         std::vector<float> full(V);
         CK(cudaMemcpyAsync(full.data(), b.logits, V * sizeof(float), cudaMemcpyDeviceToHost, b.st));
@@ -879,7 +924,7 @@ int nd_head_logits_sparse(nd_batch* bh, const float* h, const int* ids, int n, f
     }
 }
 
-// One CQ-4 matrix on a GPU for kernel-level tests and the matmul sweep.
+// One CQ matrix on a GPU for kernel-level tests and the matmul sweep.
 struct nd_cqmat {
     Model m;  // owns the uploads
     DevMat d;
@@ -896,11 +941,13 @@ struct nd_cqmat {
     }
 };
 
-int nd_cqmat_new(int device, const unsigned char* codes, const unsigned short* norms, int out, int in_dim, nd_cqmat** h) {
+int nd_cqmat_new(int device, const unsigned char* codes, const unsigned short* norms, int out, int in_dim, int bits,
+                 nd_cqmat** h) {
     try {
         if (!codes || !norms || !h) throw std::runtime_error("nd_cqmat_new: null argument");
         if (in_dim != 768) throw std::runtime_error("nd_cqmat_new: the engine's matmuls take in_dim 768");
         if (out < 1) throw std::runtime_error("nd_cqmat_new: out must be positive");
+        const int width = cq_width(bits);
         CK(cudaSetDevice(device));
         std::unique_ptr<nd_cqmat> q(new nd_cqmat());
         q->m.device = device;
@@ -908,15 +955,11 @@ int nd_cqmat_new(int device, const unsigned char* codes, const unsigned short* n
         hm.out = out;
         hm.in_dim = in_dim;
         hm.groups = 6;
-        hm.codes.assign(codes, codes + (size_t)out * 6 * 64);
+        hm.bits = bits;
+        hm.codes.assign(codes, codes + (size_t)out * 6 * 16 * width);
         hm.norms.assign(norms, norms + (size_t)out * 6);
         q->d = to_dev(q->m, hm, true);
-        // the device's codebook constants (the same for every CQ-4 matrix)
-        int8_t vals[16];
-        float cbs = 0.f;
-        std::vector<float> cb;
-        int8_codebook(vals, &cbs, &cb);
-        set_constants(vals, cb.data(), cbs, (float)(1.0 / std::sqrt(128.0)));
+        set_constants((float)(1.0 / std::sqrt(128.0)));
         CK(cudaGetLastError());
         CK(cudaStreamCreateWithFlags(&q->st, cudaStreamNonBlocking));
         *h = q.release();
@@ -952,7 +995,7 @@ int nd_cqmat_apply(nd_cqmat* h, const float* x, int M, int T, float* y, int reps
         CK(cudaMemcpyAsync(h->x, x, (size_t)M * 768 * 4, cudaMemcpyHostToDevice, h->st));
         auto run = [&]() {
             launch_prep_act(h->x, 768, 768, M, h->act, h->sx, h->st);
-            launch_cq_gemm(h->d, h->act, h->sx, M, T, h->y, out, 0, h->st);
+            CK(launch_cq_gemm(h->d, h->act, h->sx, M, T, h->y, out, 0, h->st));
         };
         run();
         if (reps > 0 && ms) {
@@ -979,9 +1022,9 @@ int nd_cqmat_apply(nd_cqmat* h, const float* x, int M, int T, float* y, int reps
     }
 }
 
-int nd_cq_pack(const float* w, int rows, int d, unsigned char* codes, unsigned short* norms) {
+int nd_cq_pack(const float* w, int rows, int d, int bits, unsigned char* codes, unsigned short* norms) {
     try {
-        cq_pack4(w, rows, d, codes, norms);
+        cq_pack(w, rows, d, bits, codes, norms);
         return 0;
     } catch (std::exception& e) {
         return fail(e);
@@ -989,10 +1032,12 @@ int nd_cq_pack(const float* w, int rows, int d, unsigned char* codes, unsigned s
 }
 
 int nd_synth_cact(int num_layers, int vocab, int engram_slots, int sliding_window, unsigned long long global_mask,
-                  unsigned long long engram_sites, unsigned long long seed, float std, unsigned char* out,
-                  unsigned long long cap, unsigned long long* len) {
+                  unsigned long long engram_sites, unsigned long long seed, float std, const int* cq_bits, int n_cq_bits,
+                  unsigned char* out, unsigned long long cap, unsigned long long* len) {
     try {
         SynthSpec sp;
+        if (n_cq_bits < 0 || (n_cq_bits > 0 && !cq_bits)) throw std::runtime_error("nd_synth_cact: bad code width list");
+        sp.cq_bits.assign(cq_bits, cq_bits + n_cq_bits);
         sp.num_layers = num_layers;
         sp.vocab = vocab;
         sp.engram_slots = engram_slots;

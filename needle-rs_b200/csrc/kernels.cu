@@ -43,19 +43,12 @@ long long launch_count() { return g_launches.load(); }
 void add_launches(long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 #define COUNT_LAUNCH() g_launches.fetch_add(1, std::memory_order_relaxed)
 
-__constant__ __align__(16) int8_t c_vals[16];   // code -> int8 codebook value (qlinear.rs:244-265)
-__constant__ float c_fvals[16];   // code -> f32 codebook value
-__constant__ float c_cbs;         // int8 codebook scale
 __constant__ float c_hs128;       // (float)(1/sqrt(128)), quant.rs:71-73
 
-__global__ void cq_gemm_kernel(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y, int ldy, int col0);
 static cudaError_t init_attrs();
 
-void set_constants(const int8_t vals[16], const float fvals[16], float cbs, float hs128) {
+void set_constants(float hs128) {
     init_attrs();
-    cudaMemcpyToSymbol(c_vals, vals, 16);
-    cudaMemcpyToSymbol(c_fvals, fvals, 64);
-    cudaMemcpyToSymbol(c_cbs, &cbs, 4);
     cudaMemcpyToSymbol(c_hs128, &hs128, 4);
 }
 
@@ -81,14 +74,19 @@ void launch_write_tokens(const int32_t* ids, int S, int T, int p0, Caches c, cud
 // ------------------------------------------------------- CQ row dequant
 
 // QMat::row (qlinear.rs:309-323) of one 128-wide group, by a warp: each
-// lane's four weights `fvals[code] * norm`, then the rotation.
-__device__ __forceinline__ void cq_group_row(const uint8_t* codes, const uint16_t* norms, size_t row, int groups, int g,
-                                             int lane, float v[4]) {
-    const uint8_t* c = codes + (row * groups + g) * 64 + 2 * lane;
-    uint32_t w = (uint32_t)c[0] | ((uint32_t)c[1] << 8);
-    float norm = h2f(norms[row * groups + g]);
+// lane's four weights p = 4 lane .. 4 lane + 3, `fvals[code] * norm`, then
+// the rotation. The four codes are 4 * width consecutive bits of the group.
+__device__ __forceinline__ void cq_group_row(const DevMat& W, size_t row, int g, int lane, float v[4]) {
+    const int width = W.width, bpg = 16 * width;
+    const uint8_t* c = W.codes + (row * W.groups + g) * bpg;
+    const int bit = 4 * width * lane;
+    uint32_t w = (uint32_t)c[bit >> 3];
+    if (width > 2) w |= (uint32_t)c[(bit >> 3) + 1] << 8;
+    w >>= bit & 7;
+    const uint32_t mask = (1u << width) - 1;
+    float norm = h2f(W.norms[row * W.groups + g]);
 #pragma unroll
-    for (int k = 0; k < 4; k++) v[k] = __fmul_rn(c_fvals[(w >> (4 * k)) & 15], norm);
+    for (int k = 0; k < 4; k++) v[k] = __fmul_rn(W.fvals[(w >> (width * k)) & mask], norm);
     fwht128_warp(v, lane);
 #pragma unroll
     for (int k = 0; k < 4; k++) v[k] = __fmul_rn(v[k], c_hs128);
@@ -101,7 +99,7 @@ __global__ void embed_kernel(DevMat emb, const int32_t* ids, float* xs, float sc
     int m = blockIdx.x, g = blockIdx.y, lane = threadIdx.x;
     int tok = ids[m];
     float v[4];
-    cq_group_row(emb.codes, emb.norms, (size_t)tok, emb.groups, g, lane, v);
+    cq_group_row(emb, (size_t)tok, g, lane, v);
     float4 o = make_float4(__fmul_rn(v[0], scale), __fmul_rn(v[1], scale), __fmul_rn(v[2], scale), __fmul_rn(v[3], scale));
     const int d = emb.in_dim;
 #pragma unroll
@@ -117,10 +115,20 @@ void launch_embed(DevMat emb, const int32_t* ids, int M, float* xs, cudaStream_t
 // ------------------------------------------------------------ A8 prep
 
 // prep_group (qlinear.rs:152-164): zero-pad, rotate, int8 with one scale per
-// (row, group). Stored lane-major: input p = 32a + 8l + b of a group sits at
-// l*32 + a*8 + b, so the decode kernel's lane l (qlinear.rs:333) is the
-// contiguous 32-byte slice l*32 .. l*32+31 (lane i holds p = 4i .. 4i+3).
-__device__ __forceinline__ int lane_major_pos(int i) { return ((i & 7) >> 1) * 32 + (i >> 3) * 8 + (i & 1) * 4; }
+// (row, group). Stored lane-major: input p = 32a + 8l + b of a group (a, l <
+// 4, b < 8) sits at slot l*32 + (a&1)*16 + (a>>1)*8 + b. Both decode lane
+// rules of qlinear.rs:333 are then 16-byte aligned runs of slots: the 4-bit
+// lane (p % 32) / 8 = l is the 32 bytes l*32 .., and the 2-bit lane
+// (p % 64) / 16 = 2(a&1) + (l>>1) the two 16-byte halves at
+// (2(lane&1) + h)*32 + (lane>>1)*16, h = 0, 1. The weights' w8 copy uses the
+// same slots, so any run of slots meets its own inputs. Warp lane i holds
+// p = 4i .. 4i + 3.
+__host__ __device__ __forceinline__ int lane_major_slot_of(int p) {
+    const int a = p >> 5, l = (p >> 3) & 3, b = p & 7;
+    return l * 32 + (a & 1) * 16 + (a >> 1) * 8 + b;
+}
+__device__ __forceinline__ int lane_major_pos(int i) { return lane_major_slot_of(4 * i); }
+int lane_major_slot(int p) { return lane_major_slot_of(p); }
 
 __device__ __forceinline__ void prep_group_warp(float v[4], int lane, int8_t* q, float* sx) {
     fwht128_warp(v, lane);
@@ -164,120 +172,18 @@ void launch_prep_act(const float* x, int ldx, int K, int M, int8_t* act, float* 
 // ----------------------------------------------------------- CQ matmul
 
 // The decode combine (qlinear.rs:340-350) for T == 1: four float lanes per
-// output, lane l fed by inputs p with (p % 32) / 8 == l, scale
-// (sx * cbs) * norm, lanes summed (l0 + l1) + (l2 + l3). The prefill
+// output, lane l fed by inputs p with (p % 32) / 8 == l (width 2: (p % 64)
+// / 16 == l), scale (sx * cbs) * norm, lanes summed (l0 + l1) + (l2 + l3). The prefill
 // combine (qlinear.rs:353-363) otherwise: one fma chain over groups, scale
 // (norm * cbs) * sx for a sequence's first T/4*4 rows, norm * (cbs * sx)
 // for the rest.
-constexpr int GEMM_TN = 64, GEMM_TM = 16, GEMM_K = 768, GEMM_LD = GEMM_K + 4;
-
-__global__ void __launch_bounds__(256) cq_gemm_kernel(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y,
-                                                      int ldy, int col0) {
-    pdl_launch_dependents();
-    pdl_wait();
-    extern __shared__ __align__(16) int8_t smem[];
-    int8_t* ws = smem;                               // [TN][LD]
-    int8_t* as = smem + GEMM_TN * GEMM_LD;           // [TM][LD]
-    float* sxs = (float*)(as + GEMM_TM * GEMM_LD);   // [TM][6]
-    float* nrm = sxs + GEMM_TM * 6;                  // [TN][6]
-    const int G = W.groups;
-    const int n0 = blockIdx.x * GEMM_TN, m0 = blockIdx.y * GEMM_TM;
-    const int tid = threadIdx.x;
-    // weights: codes through the LUT into int8, natural order
-    for (int idx = tid; idx < GEMM_TN * G * 16; idx += 256) {
-        int r = idx / (G * 16), wdx = idx % (G * 16);
-        int n = n0 + r;
-        uint32_t c = 0;
-        if (n < W.out) c = *(const uint32_t*)(W.codes + (size_t)n * G * 64 + wdx * 4);
-        char4 lo, hi;
-        lo.x = c_vals[c & 15]; lo.y = c_vals[(c >> 4) & 15]; lo.z = c_vals[(c >> 8) & 15]; lo.w = c_vals[(c >> 12) & 15];
-        hi.x = c_vals[(c >> 16) & 15]; hi.y = c_vals[(c >> 20) & 15]; hi.z = c_vals[(c >> 24) & 15]; hi.w = c_vals[c >> 28];
-        *(char4*)(ws + r * GEMM_LD + wdx * 8) = lo;
-        *(char4*)(ws + r * GEMM_LD + wdx * 8 + 4) = hi;
-    }
-    for (int idx = tid; idx < GEMM_TN * G; idx += 256) {
-        int r = idx / G, g = idx % G, n = n0 + r;
-        nrm[r * 6 + g] = n < W.out ? h2f(W.norms[(size_t)n * G + g]) : 0.f;
-    }
-    for (int idx = tid; idx < GEMM_TM * G * 32; idx += 256) {
-        int r = idx / (G * 32), wdx = idx % (G * 32);
-        int m = m0 + r;
-        uint32_t a = m < M ? *(const uint32_t*)(act + (size_t)m * G * 128 + wdx * 4) : 0u;
-        *(uint32_t*)(as + r * GEMM_LD + wdx * 4) = a;
-    }
-    for (int idx = tid; idx < GEMM_TM * G; idx += 256) {
-        int r = idx / G, g = idx % G, m = m0 + r;
-        sxs[r * 6 + g] = m < M ? sx[(size_t)m * G + g] : 0.f;
-    }
-    __syncthreads();
-    const int nl = tid % GEMM_TN, mq = tid / GEMM_TN;  // 4 rows of m each
-    const float cbs = c_cbs;
-    float lanes[4][4];
-    float acc[4];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        acc[i] = 0.f;
-#pragma unroll
-        for (int l = 0; l < 4; l++) lanes[i][l] = 0.f;
-    }
-    const int8_t* wr = ws + nl * GEMM_LD;
-    for (int g = 0; g < G; g++) {
-        int32_t s[4][4];
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-#pragma unroll
-            for (int l = 0; l < 4; l++) s[i][l] = 0;
-#pragma unroll
-        for (int blk = 0; blk < 4; blk++)
-#pragma unroll
-            for (int l = 0; l < 4; l++) {
-                int off = g * 128 + blk * 32 + l * 8;     // weights: natural order
-                int offa = g * 128 + l * 32 + blk * 8;    // activations: lane-major
-                int w0 = *(const int*)(wr + off), w1 = *(const int*)(wr + off + 4);
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const int8_t* ar = as + (mq * 4 + i) * GEMM_LD + offa;
-                    s[i][l] = __dp4a(w0, *(const int*)ar, s[i][l]);
-                    s[i][l] = __dp4a(w1, *(const int*)(ar + 4), s[i][l]);
-                }
-            }
-        float norm = nrm[nl * 6 + g];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            int ml = mq * 4 + i;
-            float sxv = sxs[ml * 6 + g];
-            if (T == 1) {
-                float sc = __fmul_rn(__fmul_rn(sxv, cbs), norm);
-#pragma unroll
-                for (int l = 0; l < 4; l++) lanes[i][l] = __fmaf_rn((float)s[i][l], sc, lanes[i][l]);
-            } else {
-                int ti = (m0 + ml) % T;
-                bool block = ti < T / 4 * 4;
-                float sc = block ? __fmul_rn(__fmul_rn(norm, cbs), sxv) : __fmul_rn(norm, __fmul_rn(cbs, sxv));
-                int tot = s[i][0] + s[i][1] + s[i][2] + s[i][3];
-                acc[i] = __fmaf_rn((float)tot, sc, acc[i]);
-            }
-        }
-    }
-    int n = n0 + nl;
-    if (n >= W.out) return;
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        int m = m0 + mq * 4 + i;
-        if (m >= M) continue;
-        float v = T == 1 ? __fadd_rn(__fadd_rn(lanes[i][0], lanes[i][1]), __fadd_rn(lanes[i][2], lanes[i][3])) : acc[i];
-        y[(size_t)m * ldy + col0 + n] = v;
-    }
-}
-
-static const size_t GEMM_SMEM = (GEMM_TN + GEMM_TM) * GEMM_LD + (GEMM_TM + GEMM_TN) * 6 * 4;
 
 // ---------------------------------------------- CQ matmul on tensor cores
 //
-// The same two combines with the integer sums from mma.sync m16n8k32 s8:
-// with both operands lane-major, the K-slice [g*128 + l*32, +32) is decode
-// lane l of group g, so one MMA gives exactly one lane sum (decode) and four
-// chained MMAs one group sum (prefill). Each accumulator starts at the bit
+// The two combines with the integer sums from mma.sync m16n8k32 s8: with
+// both operands lane-major, decode lane l of group g is two 16-byte runs of
+// the K axis (the A and B fragments' halves), so one MMA gives exactly one
+// lane sum (decode) and four chained MMAs one group sum (prefill). Each accumulator starts at the bit
 // pattern of 1.5 * 2^23: every sum here is below 2^22 in magnitude, so the
 // result reinterpreted as a float minus 1.5 * 2^23 is the sum, exactly, in
 // one FP32 subtract. CTA tile 64 rows x 64 outputs, K = 768 resident in
@@ -377,7 +283,13 @@ __device__ __forceinline__ void cp_async4z(void* smem, const void* gmem, bool va
 // are issued at iteration k into the slot iteration k - 1 has just freed, so
 // the next tile's operands arrive while this one computes. A tile's scales
 // (activation sx, f16 norms) come with its group 0 into one of two buffers.
-template <bool DECODE>
+// K offset within a group of half h of decode lane l (lane_major_pos).
+template <bool TWO>
+__device__ __forceinline__ int lane_half(int l, int h) {
+    return TWO ? (2 * (l & 1) + h) * 32 + (l >> 1) * 16 : l * 32 + h * 16;
+}
+
+template <bool DECODE, bool TWO>
 __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y,
                                                         int ldy, int col0) {
     pdl_launch_dependents();
@@ -424,7 +336,7 @@ __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* 
     };
 #pragma unroll 1
     for (int k = 0; k < 5; k++) issue(k);
-    const float cbs = c_cbs;
+    const float cbs = W.cbs;
     const int wm = (warp & 3) * 16, wn = (warp >> 2) * 32;
     const int gid = lane >> 2, tig = lane & 3;
     const int r0 = wm + gid, r1 = r0 + 8;  // this thread's two rows in the tile
@@ -487,12 +399,12 @@ __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* 
         int dsum[4][4];
 #pragma unroll
         for (int l = 0; l < 4; l++) {
-            const int kb = g * 128 + l * 32;
             uint32_t a[4], bq[2][4];
-            ldsm_x4(a, as + (wm + (lane & 15)) * MMA_LD + kb + (lane >> 4) * 16);
+            ldsm_x4(a, as + (wm + (lane & 15)) * MMA_LD + g * 128 + lane_half<TWO>(l, lane >> 4));
 #pragma unroll
             for (int jj = 0; jj < 2; jj++)
-                ldsm_x4(bq[jj], ws + (wn + (2 * jj + (lane >> 4)) * 8 + (lane & 7)) * MMA_LD + kb + ((lane >> 3) & 1) * 16);
+                ldsm_x4(bq[jj], ws + (wn + (2 * jj + (lane >> 4)) * 8 + (lane & 7)) * MMA_LD + g * 128 +
+                                    lane_half<TWO>(l, (lane >> 3) & 1));
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 const uint32_t b[2] = {bq[j >> 1][(j & 1) * 2], bq[j >> 1][(j & 1) * 2 + 1]};
@@ -549,14 +461,18 @@ __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* 
 
 // ------------------------------------------------ CQ matvec (decode, few rows)
 //
-// The decode combine for one to four activation rows straight off the 4-bit
-// codes, one warp per output row: lane i holds code words i, i + 32 and
-// i + 64 of the row (group g = 2k + i/16, word i % 16 of it: inputs p = 8 *
-// word .. + 7, decode lane (i % 16) % 4). A word's eight codes become int8
-// codebook values with three byte permutes per four codes, meet the eight
-// matching lane-major activation bytes in two dp4a, and xor-shuffles over
-// the word's four 8-input blocks give each (group, lane) sum; lanes 0-3
-// then run the reference's fma chain over groups.
+// The decode combine for one to four activation rows straight off the
+// codes, one warp per output row. A group is 16 blocks of 8 inputs (block w
+// = inputs p = 8w .. 8w + 7, a = w / 4, l = w % 4 in lane_major_pos's
+// terms); lane i holds blocks i, i + 32 and i + 64 of the row (group g = 2k
+// + i/16, block i % 16). A block's eight codes (a 32-bit word at 4 bits, a
+// 16-bit one at 2 bits) become int8 codebook values with byte permutes, and
+// meet their eight lane-major activation bytes in two dp4a; width 3 reads
+// the block from the expanded w8 copy instead. Xor-shuffles over the blocks
+// of one decode lane give each (group, lane) sum: for the 4-bit rule the
+// blocks of lane l are i % 16 = l + 4a (xor 4, 8), for the 2-bit rule
+// (p % 64) / 16 = 2(a&1) + (l>>1) they are i % 16 = 2 lane + {0, 1, 8, 9}
+// (xor 1, 8). Lanes 0-3 then run the reference's fma chain over groups.
 constexpr int GEMV_MAXM = 4;
 
 __device__ __forceinline__ uint32_t lut4(uint32_t nib16, uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3) {
@@ -565,6 +481,14 @@ __device__ __forceinline__ uint32_t lut4(uint32_t nib16, uint32_t v0, uint32_t v
     return __byte_perm(lo, hi, 0x3210u | ((nib16 & 0x8888u) >> 1));
 }
 
+// Four 2-bit codes (one byte) through the 4-entry table v.
+__device__ __forceinline__ uint32_t lut2(uint32_t c, uint32_t v) {
+    const uint32_t sel = (c & 3u) | ((c & 0xCu) << 2) | ((c & 0x30u) << 4) | ((c & 0xC0u) << 6);
+    return __byte_perm(v, 0u, sel);
+}
+
+// FMT: 4 or 2 = codes of that width, 8 = the w8 copy (width 3).
+template <int FMT>
 __global__ void __launch_bounds__(256) cq_gemv_kernel(DevMat W, const int8_t* act, const float* sx, int M, float* y, int ldy,
                                                       int col0) {
     pdl_launch_dependents();
@@ -572,20 +496,36 @@ __global__ void __launch_bounds__(256) cq_gemv_kernel(DevMat W, const int8_t* ac
     const int lane = threadIdx.x & 31;
     const int n = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (n >= W.out) return;
-    const uint32_t* cv = (const uint32_t*)c_vals;
-    const uint32_t v0 = cv[0], v1 = cv[1], v2 = cv[2], v3 = cv[3];
-    const uint32_t* codes = (const uint32_t*)(W.codes + (size_t)n * 384);
-    uint32_t c[3];
-#pragma unroll
-    for (int k = 0; k < 3; k++) c[k] = __ldg(codes + lane + 32 * k);
-    int wl[3], wh[3];
-#pragma unroll
-    for (int k = 0; k < 3; k++) {
-        wl[k] = (int)lut4(c[k] & 0xffffu, v0, v1, v2, v3);
-        wh[k] = (int)lut4(c[k] >> 16, v0, v1, v2, v3);
-    }
     const int wi = lane & 15, a = wi >> 2, l = wi & 3, half = lane >> 4;
-    const float cbs = c_cbs;
+    const int slot = l * 32 + (a & 1) * 16 + (a >> 1) * 8;  // lane_major_pos of the block
+    int wl[3], wh[3];
+    if (FMT == 4) {
+        const uint32_t v0 = W.vals4[0], v1 = W.vals4[1], v2 = W.vals4[2], v3 = W.vals4[3];
+        const uint32_t* codes = (const uint32_t*)(W.codes + (size_t)n * 384);
+#pragma unroll
+        for (int k = 0; k < 3; k++) {
+            const uint32_t c = __ldg(codes + lane + 32 * k);
+            wl[k] = (int)lut4(c & 0xffffu, v0, v1, v2, v3);
+            wh[k] = (int)lut4(c >> 16, v0, v1, v2, v3);
+        }
+    } else if (FMT == 2) {
+        const uint32_t v0 = W.vals4[0];
+        const uint16_t* codes = (const uint16_t*)(W.codes + (size_t)n * 192);
+#pragma unroll
+        for (int k = 0; k < 3; k++) {
+            const uint32_t c = __ldg(codes + lane + 32 * k);
+            wl[k] = (int)lut2(c & 0xffu, v0);
+            wh[k] = (int)lut2(c >> 8, v0);
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 3; k++) {
+            const int2 w = __ldg((const int2*)(W.w8 + (size_t)n * 768 + (2 * k + half) * 128 + slot));
+            wl[k] = w.x;
+            wh[k] = w.y;
+        }
+    }
+    const float cbs = W.cbs;
     float norm_l = 0.f;  // lane g < 6 holds norm[n][g]
     if (lane < 6) norm_l = h2f(W.norms[(size_t)n * 6 + lane]);
     for (int m = 0; m < M; m++) {
@@ -594,18 +534,19 @@ __global__ void __launch_bounds__(256) cq_gemv_kernel(DevMat W, const int8_t* ac
 #pragma unroll
         for (int k = 0; k < 3; k++) {
             const int g = 2 * k + half;
-            const int2 x = *(const int2*)(ar + g * 128 + l * 32 + a * 8);
+            const int2 x = *(const int2*)(ar + g * 128 + slot);
             int v = __dp4a(wl[k], x.x, 0);
             v = __dp4a(wh[k], x.y, v);
-            v += __shfl_xor_sync(0xffffffffu, v, 4);
+            v += __shfl_xor_sync(0xffffffffu, v, FMT == 2 ? 1 : 4);
             v += __shfl_xor_sync(0xffffffffu, v, 8);
-            s[k] = v;  // lanes half*16 + l: the sum of group g, decode lane l
+            s[k] = v;  // the sum of group g, one decode lane
         }
         float sxl = lane < 6 ? sx[(size_t)m * 6 + lane] : 0.f;
         float acc = 0.f;
 #pragma unroll
         for (int g = 0; g < 6; g++) {
-            int sg = __shfl_sync(0xffffffffu, s[g >> 1], (g & 1) * 16 + (lane & 3));
+            const int src = (g & 1) * 16 + (FMT == 2 ? 2 * (lane & 3) : (lane & 3));
+            int sg = __shfl_sync(0xffffffffu, s[g >> 1], src);
             float sc = __fmul_rn(__fmul_rn(__shfl_sync(0xffffffffu, sxl, g), cbs), __shfl_sync(0xffffffffu, norm_l, g));
             acc = __fmaf_rn((float)sg, sc, acc);
         }
@@ -614,30 +555,33 @@ __global__ void __launch_bounds__(256) cq_gemv_kernel(DevMat W, const int8_t* ac
     }
 }
 
-void launch_cq_gemm(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y, int ldy, int col0, cudaStream_t st) {
+cudaError_t launch_cq_gemm(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y, int ldy, int col0,
+                           cudaStream_t st) {
+    if (!W.w8 || W.groups != 6 || W.in_dim != 768 || (W.width != 2 && W.width != 3 && W.width != 4))
+        return cudaErrorInvalidValue;  // every matmul here reads 768 inputs, w8 expanded
     COUNT_LAUNCH();
-    if (T == 1 && M <= GEMV_MAXM && W.groups == 6) {
-        launch_pdl(cq_gemv_kernel, dim3(cdiv(W.out, 8)), dim3(256), 0, st, W, act, sx, M, y, ldy, col0);
-        return;
+    if (T == 1 && M <= GEMV_MAXM) {
+        const dim3 grid(cdiv(W.out, 8));
+        if (W.width == 4) launch_pdl(cq_gemv_kernel<4>, grid, dim3(256), 0, st, W, act, sx, M, y, ldy, col0);
+        else if (W.width == 2) launch_pdl(cq_gemv_kernel<2>, grid, dim3(256), 0, st, W, act, sx, M, y, ldy, col0);
+        else launch_pdl(cq_gemv_kernel<8>, grid, dim3(256), 0, st, W, act, sx, M, y, ldy, col0);
+        return cudaSuccess;
     }
-    if (W.w8 && W.groups == 6) {
-        static int sms[64];
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (dev < 64 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-        const int per = dev < 64 && sms[dev] ? 2 * sms[dev] : 296;
-        const int grid = std::min(cdiv(W.out, MMA_BN) * cdiv(M, MMA_BM), per);
-        if (T == 1)
-            launch_pdl(cq_mma_kernel<true>, dim3(grid), dim3(256), MMA_SMEM, st, W, act, sx, M, T, y, ldy, col0);
-        else
-            launch_pdl(cq_mma_kernel<false>, dim3(grid), dim3(256), MMA_SMEM, st, W, act, sx, M, T, y, ldy, col0);
-        return;
-    }
-    launch_pdl(cq_gemm_kernel, dim3(dim3(cdiv(W.out, GEMM_TN), cdiv(M, GEMM_TM))), dim3(256), GEMM_SMEM, st, W, act, sx, M, T, y, ldy, col0);
+    static int sms[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    const int per = dev < 64 && sms[dev] ? 2 * sms[dev] : 296;
+    const int grid = std::min(cdiv(W.out, MMA_BN) * cdiv(M, MMA_BM), per);
+    if (T == 1 && W.width == 2)
+        launch_pdl(cq_mma_kernel<true, true>, dim3(grid), dim3(256), MMA_SMEM, st, W, act, sx, M, T, y, ldy, col0);
+    else if (T == 1)
+        launch_pdl(cq_mma_kernel<true, false>, dim3(grid), dim3(256), MMA_SMEM, st, W, act, sx, M, T, y, ldy, col0);
+    else
+        launch_pdl(cq_mma_kernel<false, false>, dim3(grid), dim3(256), MMA_SMEM, st, W, act, sx, M, T, y, ldy, col0);
+    return cudaSuccess;
 }
 
-template <bool DECODE>
-__global__ void cq_mma_kernel(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y, int ldy, int col0);
 
 extern const size_t ATT_SMEM;
 extern const size_t POST_SMEM;
@@ -653,9 +597,9 @@ static cudaError_t init_attrs() {
     cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_SMEM);
     cudaFuncSetAttribute(post_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)POST_SMEM);
     cudaFuncSetAttribute(post_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)POST_ROW_SMEM);
-    cudaFuncSetAttribute(cq_mma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
-    cudaFuncSetAttribute(cq_mma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
-    return cudaFuncSetAttribute(cq_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM);
+    cudaFuncSetAttribute(cq_mma_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
+    cudaFuncSetAttribute(cq_mma_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
+    return cudaFuncSetAttribute(cq_mma_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
 }
 
 // ---------------------------------------------------------------- engram
@@ -679,7 +623,7 @@ __global__ void engram_gather_kernel(DevMat tables, const int32_t* tokens, int c
         }
         acc ^= acc >> 15;
         size_t row = (size_t)tbl * slots + acc % (uint32_t)slots;
-        cq_group_row(tables.codes, tables.norms, row, tables.groups, 0, lane, v);
+        cq_group_row(tables, row, 0, lane, v);
     }
     *(float4*)(e + (size_t)m * d + tbl * sub + 4 * lane) = make_float4(v[0], v[1], v[2], v[3]);
 }

@@ -10,15 +10,24 @@
 
 namespace nd {
 
-// A CQ-4 matrix as the archive stores it: codes [out][groups][64] (two codes
-// per byte, low nibble first), f16 group norms [out][groups].
+// A CQ matrix as the archive stores it: codes [out][groups][16 * width]
+// (LSB-first, 8 codes per `width` bytes), f16 group norms [out][groups],
+// and its codebook (qlinear.rs:43-61, 244-265). A fused projection whose
+// parts differ in codebook is several DevMats, one per run of equal parts.
 struct DevMat {
     const uint8_t* codes = nullptr;
     const uint16_t* norms = nullptr;
     int out = 0, in_dim = 0, groups = 0;
+    // Bits per code in memory: 2 (2-bit and ternary records), 3 or 4. Width
+    // 2 splits a group into decode lanes by (p % 64) / 16, the others by
+    // (p % 32) / 8 (qlinear.rs:333).
+    int width = 4;
+    float cbs = 1.0f;       // scale of the int8 codebook
+    uint32_t vals4[4] = {0, 0, 0, 0};  // code -> int8 codebook value (16 bytes)
+    float fvals[16] = {};   // code -> f32 codebook value (row dequant)
     // The same codes expanded through the int8 codebook, [out][groups*128],
-    // each group lane-major (input p = 32a + 8l + b at l*32 + a*8 + b): the
-    // operand the tensor-core kernel streams when many rows share a step.
+    // each group lane-major (lane_major_pos in kernels.cu): the operand the
+    // tensor-core kernel streams when many rows share a step.
     const int8_t* w8 = nullptr;
 };
 
@@ -31,7 +40,6 @@ struct LayerW {
     const float* phi_s;   // [24]
     float attn_gate, a_pre, a_post, a_res;
     float b_pre[4], b_post[4], b_res[16];
-    DevMat qkvg, out;
 };
 
 // Per-sequence caches of one batch.
@@ -67,15 +75,21 @@ long long launch_count();
 // Kernels a replayed CUDA graph launched (counted with the others).
 void add_launches(long long n);
 
-void set_constants(const int8_t vals[16], const float fvals[16], float cbs, float hs128);
+// The Hadamard scale (float)(1/sqrt(128)) and kernel attributes, once per
+// device before its first launch.
+void set_constants(float hs128);
+// Slot of input p (< 128) of a group in the lane-major A8 / w8 layout.
+int lane_major_slot(int p);
 
 void launch_write_tokens(const int32_t* ids, int S, int T, int p0, Caches c, cudaStream_t st);
 void launch_embed(DevMat emb, const int32_t* ids, int M, float* xs, cudaStream_t st);
 void launch_prep_act(const float* x, int ldx, int K, int M, int8_t* act, float* sx, cudaStream_t st);
 // y[m][col0 + n] for n < W.out. T sets the combine per row: T == 1 the
 // decode kernel, else the prefill kernel with the block/remainder rule over
-// each sequence's T rows.
-void launch_cq_gemm(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y, int ldy, int col0, cudaStream_t st);
+// each sequence's T rows. cudaErrorInvalidValue (nothing launched) unless W
+// reads 768 inputs and carries its w8 copy.
+cudaError_t launch_cq_gemm(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y, int ldy, int col0,
+                           cudaStream_t st);
 void launch_engram_gather(DevMat tables, Caches c, int S, int T, int p0, int slots, float* e, cudaStream_t st);
 void launch_engram_vhist(const float* kv, Caches c, int site, int nsites, int S, int T, int p0, cudaStream_t st);
 void launch_engram_conv(const float* taps, Caches c, int site, int nsites, int S, int T, int p0, float* v, cudaStream_t st);

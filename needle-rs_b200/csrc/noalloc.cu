@@ -22,7 +22,8 @@
 
 namespace nd {
 
-// Defined in engine.cu: the tied lm_head matrix of a loaded model.
+// Defined in engine.cu: the tied lm_head matrix of a loaded model (its
+// first out_rows rows).
 bool model_head(const nd_model* m, DevMat* emb, int* device, int* out_rows);
 void set_error(const std::string& msg);
 
@@ -81,8 +82,8 @@ extern "C" int nd_head_logits_noalloc(const nd_model* m, const float* h, int row
         // every act byte and scale of rows < `rows` is written before the
         // matmul reads it, so nothing in the array has to start at zero
         launch_prep_act(h, 768, 768, rows, act, sx, st);
-        launch_cq_gemm(emb, act, sx, rows, 1, out, out_rows, 0, st);
-        cudaError_t e = cudaGetLastError();
+        cudaError_t e = launch_cq_gemm(emb, act, sx, rows, 1, out, out_rows, 0, st);
+        if (e == cudaSuccess) e = cudaGetLastError();
         cudaSetDevice(prev);
         if (e != cudaSuccess) throw std::runtime_error(std::string("nd_head_logits_noalloc: ") + cudaGetErrorString(e));
         return 0;

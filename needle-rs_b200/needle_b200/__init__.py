@@ -43,11 +43,11 @@ def lib():
             "nd_head_logits": (I, [P, P, I, P, I]),
             "nd_head_logits_sparse": (I, [P, P, P, I, P]),
             "nd_batch_stream": (P, [P]),
-            "nd_cq_pack": (I, [P, I, I, P, P]),
-            "nd_cqmat_new": (I, [I, P, P, I, I, C.POINTER(P)]),
+            "nd_cq_pack": (I, [P, I, I, I, P, P]),
+            "nd_cqmat_new": (I, [I, P, P, I, I, I, C.POINTER(P)]),
             "nd_cqmat_free": (None, [P]),
             "nd_cqmat_apply": (I, [P, P, I, I, P, I, C.POINTER(C.c_float)]),
-            "nd_synth_cact": (I, [I, I, I, I, U64, U64, U64, C.c_float, P, U64, C.POINTER(U64)]),
+            "nd_synth_cact": (I, [I, I, I, I, U64, U64, U64, C.c_float, P, I, P, U64, C.POINTER(U64)]),
             "nd_batch_debug": (I, [P, C.c_char_p, P, C.c_longlong]),
             "nd_batch_debug_layer": (I, [P, I]),
             "nd_launch_count": (C.c_longlong, []),
@@ -91,16 +91,48 @@ def launch_count() -> int:
     return lib().nd_launch_count()
 
 
-def synth_cact(seed=0, std=0.02, **shape) -> bytes:
-    """A random-init Needle 3 archive (every tensor ~N(0, std^2)), CQ-4
+TERNARY = 5  # record bits of ternary codes (crates/needle-core/src/quant.rs:11-12)
+
+
+def cq_roles(num_layers=20, engram_sites=(3, 7, 11, 15, 19), **_):
+    """The CQ records of an archive in record order
+    (crates/needle-core/src/cact.rs:279-352): embedding; per layer q, k, v,
+    gate, out; phi_pre, phi_post, phi_res; per engram site table, key,
+    value."""
+    roles = ["embedding"]
+    for _l in range(num_layers):
+        roles += ["q", "k", "v", "gate", "out"]
+    roles += ["phi_pre", "phi_post", "phi_res"]
+    for _s in engram_sites:
+        roles += ["table", "key", "value"]
+    return roles
+
+
+def synth_cact(seed=0, std=0.02, bits=None, **shape) -> bytes:
+    """A random-init Needle 3 archive (every tensor ~N(0, std^2)), CQ
     matrices packed by the reference's quantizer, in the reference's record
-    order (crates/needle-core/src/cact.rs:279-475)."""
+    order (crates/needle-core/src/cact.rs:279-475). ``bits`` sets the record
+    bits of the CQ matrices (2, 3, 4 or TERNARY): one width for all, a dict
+    role -> width (roles as cq_roles names them, others 4), or a list in
+    record order. A fused projection's parts (q, k, v, gate; key, value)
+    must share the code width (ternary packs at 2)."""
     g = dict(NEEDLE3_DEFAULTS)
     g.update(shape)
     gm = sum(1 << l for l in g["global_layers"])
     es = sum(1 << l for l in g["engram_sites"])
+    roles = cq_roles(g["num_layers"], g["engram_sites"])
+    if bits is None:
+        plan = []
+    elif isinstance(bits, int):
+        plan = [bits] * len(roles)
+    elif isinstance(bits, dict):
+        plan = [bits.get(r, 4) for r in roles]
+    else:
+        plan = list(bits)
+    plan = np.ascontiguousarray(plan, np.int32)
     n = C.c_uint64(0)
-    args = (g["num_layers"], g["vocab"], g["engram_slots"], g["sliding_window"], gm, es, seed, std)
+    args = (g["num_layers"], g["vocab"], g["engram_slots"], g["sliding_window"], gm, es, seed, std,
+            _p(plan) if len(plan) else None, len(plan))
     if lib().nd_synth_cact(*args, None, 0, C.byref(n)) != 0:
         raise _err()
     buf = np.zeros(n.value, np.uint8)
@@ -109,17 +141,25 @@ def synth_cact(seed=0, std=0.02, **shape) -> bytes:
     return buf.tobytes()
 
 
-class CQMat:
-    """One CQ-4 matrix (codes [out][6][64], f16 norms [out][6]) on a GPU:
-    the engine's A8 + CQ matmul on host rows (needle_engine.h,
-    nd_cqmat_apply)."""
+def code_width(bits):
+    """Bits a code of a record takes in memory (ternary packs at 2)."""
+    return 2 if bits == TERNARY else bits
 
-    def __init__(self, codes, norms, device=0):
+
+class CQMat:
+    """One CQ matrix (codes [out][6][16 * width], f16 norms [out][6]) of
+    record bits 2, 3, 4 or TERNARY on a GPU: the engine's A8 + CQ matmul on
+    host rows (needle_engine.h, nd_cqmat_apply)."""
+
+    def __init__(self, codes, norms, device=0, bits=4):
         codes = np.ascontiguousarray(codes, np.uint8)
         norms = np.ascontiguousarray(norms, np.uint16)
         self.out = norms.shape[0]
+        self.bits = bits
+        if codes.size != self.out * 6 * 16 * code_width(bits):
+            raise ValueError("codes do not match out x 6 groups at this width")
         h = C.c_void_p()
-        if lib().nd_cqmat_new(device, _p(codes), _p(norms), self.out, 768, C.byref(h)) != 0:
+        if lib().nd_cqmat_new(device, _p(codes), _p(norms), self.out, 768, bits, C.byref(h)) != 0:
             raise _err()
         self._h = h.value
 
@@ -141,14 +181,15 @@ class CQMat:
         return (y, ms.value) if reps > 0 else y
 
 
-def cq_pack(w):
-    """crates/needle-core/src/quant.rs:233-256 (4-bit, group 128)."""
+def cq_pack(w, bits=4):
+    """crates/needle-core/src/quant.rs:233-256 (group 128) at record bits 2,
+    3, 4 or TERNARY."""
     w = np.ascontiguousarray(w, np.float32)
     rows, d = w.shape
     g = (d + 127) // 128
-    codes = np.zeros((rows, g * 64), np.uint8)
+    codes = np.zeros((rows, g * 16 * code_width(bits)), np.uint8)
     norms = np.zeros((rows, g), np.uint16)
-    if lib().nd_cq_pack(_p(w), rows, d, _p(codes), _p(norms)) != 0:
+    if lib().nd_cq_pack(_p(w), rows, d, bits, _p(codes), _p(norms)) != 0:
         raise _err()
     return codes, norms
 

@@ -361,15 +361,49 @@ void parse_archive(const uint8_t* data, size_t len, Archive& a) {
 
 // ---------------------------------------------------------- qlinear.rs
 
-// qlinear.rs:43-61, 211-265: a CQ-4 matrix, codes kept as stored.
-struct QMat {
-    int out = 0, in_dim = 0, groups = 0;
-    std::vector<uint8_t> codes;  // [out][groups][64]
-    std::vector<uint16_t> norms; // [out][groups] f16 bits
-    std::vector<int8_t> w8;      // codes expanded through `vals`, natural order
+// quant.rs:11-12: record bits that mark ternary codes (2-bit crumbs).
+static const int TERNARY = 5;
+
+// qlinear.rs:222-224: bits a code takes in memory.
+static int code_width(int bits) {
+    if (bits == TERNARY) return 2;
+    if (bits >= 2 && bits <= 4) return bits;
+    throw std::runtime_error("CQ records of this width are not supported");
+}
+
+// quant.rs:208-225 (unpack_lsb_into): n codes of `width` bits, LSB-first,
+// 8 codes per `width` bytes.
+static void unpack_lsb(const uint8_t* packed, int width, int n, uint8_t* out) {
+    for (int k = 0; k < n; k += 8) {
+        uint64_t word = 0;
+        for (int b = 0; b < width; b++) word |= (uint64_t)packed[k / 8 * width + b] << (8 * b);
+        for (int i = 0; i < 8 && k + i < n; i++) out[k + i] = (uint8_t)((word >> (i * width)) & ((1u << width) - 1));
+    }
+}
+
+// qlinear.rs:43-61, 211-265, 500-518: a CQ matrix, codes kept as stored,
+// plus its codebook. A fused projection concatenates parts of one code
+// width; each part keeps its own codebook (QLinear's parts), looked up by
+// output row.
+struct QPart {
+    int r0 = 0;
     int8_t vals[16];
     float cbs;
     float fvals[16];
+};
+
+struct QMat {
+    int out = 0, in_dim = 0, groups = 0;
+    int width = 4;               // bits per code in memory
+    std::vector<uint8_t> codes;  // [out][groups][16 * width]
+    std::vector<uint16_t> norms; // [out][groups] f16 bits
+    std::vector<int8_t> w8;      // codes expanded through `vals`, natural order
+    std::vector<QPart> parts;
+    const QPart& part(int r) const {
+        size_t k = parts.size() - 1;
+        while (k > 0 && parts[k].r0 > r) k--;
+        return parts[k];
+    }
 };
 
 // qlinear.rs:211-216
@@ -385,36 +419,57 @@ static void int8_codebook(const std::vector<float>& cb, int8_t* out, float* scal
     *scale = s;
 }
 
-// qlinear.rs:220-236, 244-265 (4-bit records only)
+// qlinear.rs:220-236, 244-265: the codebook of record bits `bits`
+// (ternary codes 3, 0, 1 select its centroids 0, 1, 2; a code past the
+// codebook reads 0), then codes and norms as stored.
+static void qmat_init(QMat& q, int bits, int out, int in_dim, const uint8_t* codes, const uint16_t* norms) {
+    q.width = code_width(bits);
+    q.out = out;
+    q.in_dim = in_dim;
+    q.groups = (in_dim + GROUP - 1) / GROUP;
+    const size_t bpg = 16 * (size_t)q.width, ncode = (size_t)out * q.groups * bpg;
+    q.codes.assign(codes, codes + ncode);
+    q.norms.assign(norms, norms + (size_t)out * q.groups);
+    std::vector<float> cb = codebook(bits, GROUP);
+    int8_t cb8[16];
+    QPart pt;
+    int8_codebook(cb, cb8, &pt.cbs);
+    for (int c = 0; c < 16; c++) {
+        int k = bits == TERNARY ? (c == 3 ? 0 : c + 1) : c;
+        bool in = c < (1 << q.width) && k < (int)cb.size();
+        pt.vals[c] = in ? cb8[k] : 0;
+        pt.fvals[c] = in ? cb[k] : 0.f;
+    }
+    q.parts.assign(1, pt);
+    q.w8.resize((size_t)out * q.groups * GROUP);
+    uint8_t idx[GROUP];
+    for (size_t u = 0; u < (size_t)out * q.groups; u++) {
+        unpack_lsb(q.codes.data() + u * bpg, q.width, GROUP, idx);
+        for (int p = 0; p < GROUP; p++) q.w8[u * GROUP + p] = pt.vals[idx[p]];
+    }
+}
+
 static void qmat_from_cq(const Archive& a, size_t i, QMat& q) {
     const Record& r = a.recs[i];
     if (r.dtype != CQ) throw std::runtime_error("tensor is not CQ");
     if (r.group != (uint32_t)GROUP) throw std::runtime_error("CQ group size is not supported");
-    if (r.bits != 4) throw std::runtime_error("only 4-bit CQ records are supported");
-    q.out = (int)r.shape[0];
-    q.in_dim = (int)r.shape[1];
-    q.groups = (q.in_dim + GROUP - 1) / GROUP;
-    size_t ncode = (size_t)q.out * q.groups * 64;
+    int out = (int)r.shape[0], in_dim = (int)r.shape[1], groups = (in_dim + GROUP - 1) / GROUP;
+    size_t ncode = (size_t)out * groups * 16 * code_width((int)r.bits);
+    if (r.nbytes < ncode + (size_t)out * groups * 2) throw std::runtime_error("CQ record is truncated");
     const uint8_t* blob = a.bytes(i);
-    q.codes.assign(blob, blob + ncode);
-    q.norms.resize((size_t)q.out * q.groups);
-    std::memcpy(q.norms.data(), blob + ncode, q.norms.size() * 2);
-    std::vector<float> cb = codebook(4, GROUP);
-    int8_t cb8[16];
-    int8_codebook(cb, cb8, &q.cbs);
-    for (int c = 0; c < 16; c++) {
-        q.vals[c] = cb8[c];
-        q.fvals[c] = cb[c];
-    }
-    q.w8.resize(ncode * 2);
-    for (size_t k = 0; k < ncode; k++) {
-        q.w8[2 * k] = q.vals[q.codes[k] & 15];
-        q.w8[2 * k + 1] = q.vals[q.codes[k] >> 4];
-    }
+    std::vector<uint16_t> nr((size_t)out * groups);
+    std::memcpy(nr.data(), blob + ncode, nr.size() * 2);
+    qmat_init(q, (int)r.bits, out, in_dim, blob, nr.data());
 }
 
+// qlinear.rs:503-518: parts side by side; the code width must agree.
 static void qmat_concat(QMat& dst, const QMat& src) {
     if (dst.out == 0) { dst = src; return; }
+    if (dst.width != src.width) throw std::runtime_error("fused parts must share a code width");
+    for (QPart p : src.parts) {
+        p.r0 += dst.out;
+        dst.parts.push_back(p);
+    }
     dst.out += src.out;
     dst.codes.insert(dst.codes.end(), src.codes.begin(), src.codes.end());
     dst.norms.insert(dst.norms.end(), src.norms.begin(), src.norms.end());
@@ -424,14 +479,13 @@ static void qmat_concat(QMat& dst, const QMat& src) {
 // qlinear.rs:309-323
 static void qmat_row(const QMat& q, int r, float* out) {
     std::vector<float> buf((size_t)q.groups * GROUP);
+    const QPart& pt = q.part(r);
+    uint8_t idx[GROUP];
     for (int g = 0; g < q.groups; g++) {
         float norm = f16_to_f32(q.norms[(size_t)r * q.groups + g]);
         float* dst = buf.data() + g * GROUP;
-        const uint8_t* c = q.codes.data() + ((size_t)r * q.groups + g) * 64;
-        for (int p = 0; p < GROUP; p++) {
-            int code = (p & 1) ? (c[p >> 1] >> 4) : (c[p >> 1] & 15);
-            dst[p] = q.fvals[code] * norm;
-        }
+        unpack_lsb(q.codes.data() + ((size_t)r * q.groups + g) * 16 * q.width, q.width, GROUP, idx);
+        for (int p = 0; p < GROUP; p++) dst[p] = pt.fvals[idx[p]] * norm;
         rotate(dst, GROUP);
     }
     std::memcpy(out, buf.data(), sizeof(float) * q.in_dim);
@@ -468,28 +522,26 @@ static QAct qact_new(const float* x, int rows, int in_dim) {
     return a;
 }
 
-// qlinear.rs:327-337: the 4 decode lanes of one group; lane = (p % 32) / 8.
+// qlinear.rs:327-337: the 4 decode lanes of one group; lane = (p % 64) / 16
+// for 2-bit codes, (p % 32) / 8 otherwise.
 static inline void lane_sums(const QMat& q, int r, int g, const QAct& a, int t, int32_t s[4]) {
     const int8_t* w = q.w8.data() + ((size_t)r * q.groups + g) * GROUP;
     const int8_t* x = a.xq.data() + ((size_t)t * a.groups + g) * GROUP;
-    for (int l = 0; l < 4; l++) {
-        int32_t acc = 0;
-        for (int blk = 0; blk < 4; blk++) {
-            const int8_t* wp = w + blk * 32 + l * 8;
-            const int8_t* xp = x + blk * 32 + l * 8;
-            for (int b = 0; b < 8; b++) acc += (int32_t)wp[b] * (int32_t)xp[b];
-        }
-        s[l] = acc;
+    for (int l = 0; l < 4; l++) s[l] = 0;
+    for (int p = 0; p < GROUP; p++) {
+        int lane = q.width == 2 ? (p % 64) / 16 : (p % 32) / 8;
+        s[lane] += (int32_t)w[p] * (int32_t)x[p];
     }
 }
 
 // qlinear.rs:340-350
 float decode_row_ref(const QMat& q, int r, const QAct& a) {
+    const float cbs = q.part(r).cbs;
     float lanes[4] = {0.f, 0.f, 0.f, 0.f};
     for (int g = 0; g < q.groups; g++) {
         int32_t s[4];
         lane_sums(q, r, g, a, 0, s);
-        float sc = (a.sx[g] * q.cbs) * f16_to_f32(q.norms[(size_t)r * q.groups + g]);
+        float sc = (a.sx[g] * cbs) * f16_to_f32(q.norms[(size_t)r * q.groups + g]);
         for (int l = 0; l < 4; l++) lanes[l] = std::fmaf((float)s[l], sc, lanes[l]);
     }
     return (lanes[0] + lanes[1]) + (lanes[2] + lanes[3]);
@@ -497,6 +549,7 @@ float decode_row_ref(const QMat& q, int r, const QAct& a) {
 
 // qlinear.rs:353-363
 float prefill_row_ref(const QMat& q, int r, const QAct& a, int t, bool block) {
+    const float cbs = q.part(r).cbs;
     float acc = 0.f;
     for (int g = 0; g < q.groups; g++) {
         int32_t s[4];
@@ -504,7 +557,7 @@ float prefill_row_ref(const QMat& q, int r, const QAct& a, int t, bool block) {
         int32_t tot = s[0] + s[1] + s[2] + s[3];
         float sx = a.sx[(size_t)t * a.groups + g];
         float norm = f16_to_f32(q.norms[(size_t)r * q.groups + g]);
-        float sc = block ? (norm * q.cbs) * sx : norm * (q.cbs * sx);
+        float sc = block ? (norm * cbs) * sx : norm * (cbs * sx);
         acc = std::fmaf((float)tot, sc, acc);
     }
     return acc;
@@ -1447,28 +1500,15 @@ float orc_prep_group(const float* x, int n, int g, int8_t* q) { return prep_grou
 float orc_chunk_exp(float* s, int l, float m) { return chunk_exp(s, l, m); }
 void orc_key_chunks(int64_t n, int nested, int nkv, int64_t* count, int64_t* chunk) { key_chunks(n, nested != 0, nkv, count, chunk); }
 
-// A raw CQ-4 matrix (codes as stored, f16 norm bits) times activations x
-// [T, in_dim]: the decode kernel when T == 1, else the prefill kernel with
-// the block/remainder rule (qlinear.rs:366-419). mode 2 = the single-row
-// kernel per token (qlinear.rs:454-456).
-int orc_cq_matmul(const uint8_t* codes, const uint16_t* norms, int out, int in_dim, const float* x, int T, int mode, float* y) {
+// A raw CQ matrix of record bits `bits` (codes as stored, f16 norm bits)
+// times activations x [T, in_dim]: the decode kernel when T == 1, else the
+// prefill kernel with the block/remainder rule (qlinear.rs:366-419). mode 2
+// = the single-row kernel per token (qlinear.rs:454-456).
+int orc_cq_matmul(const uint8_t* codes, const uint16_t* norms, int out, int in_dim, int bits, const float* x, int T, int mode,
+                  float* y) {
     try {
         QMat q;
-        q.out = out;
-        q.in_dim = in_dim;
-        q.groups = (in_dim + GROUP - 1) / GROUP;
-        size_t ncode = (size_t)out * q.groups * 64;
-        q.codes.assign(codes, codes + ncode);
-        q.norms.assign(norms, norms + (size_t)out * q.groups);
-        std::vector<float> cb = codebook(4, GROUP);
-        int8_t cb8[16];
-        int8_codebook(cb, cb8, &q.cbs);
-        for (int c = 0; c < 16; c++) { q.vals[c] = cb8[c]; q.fvals[c] = cb[c]; }
-        q.w8.resize(ncode * 2);
-        for (size_t k = 0; k < ncode; k++) {
-            q.w8[2 * k] = q.vals[q.codes[k] & 15];
-            q.w8[2 * k + 1] = q.vals[q.codes[k] >> 4];
-        }
+        qmat_init(q, bits, out, in_dim, codes, norms);
         if (mode == 2) {
             for (int t = 0; t < T; t++) {
                 QAct a = qact_new(x + (size_t)t * in_dim, 1, in_dim);
@@ -1485,17 +1525,20 @@ int orc_cq_matmul(const uint8_t* codes, const uint16_t* norms, int out, int in_d
     }
 }
 
-// QMat::row of a raw CQ-4 matrix (qlinear.rs:309-323).
-void orc_cq_row(const uint8_t* codes, const uint16_t* norms, int rows, int in_dim, int r, float* out) {
-    QMat q;
-    q.out = rows;
-    q.in_dim = in_dim;
-    q.groups = (in_dim + GROUP - 1) / GROUP;
-    q.codes.assign(codes + (size_t)r * q.groups * 64, codes + (size_t)(r + 1) * q.groups * 64);
-    q.norms.assign(norms + (size_t)r * q.groups, norms + (size_t)(r + 1) * q.groups);
-    std::vector<float> cb = codebook(4, GROUP);
-    for (int c = 0; c < 16; c++) q.fvals[c] = cb[c];
-    qmat_row(q, 0, out);
+// QMat::row of a raw CQ matrix of record bits `bits` (qlinear.rs:309-323).
+int orc_cq_row(const uint8_t* codes, const uint16_t* norms, int rows, int in_dim, int bits, int r, float* out) {
+    try {
+        const int groups = (in_dim + GROUP - 1) / GROUP;
+        const size_t bpr = (size_t)groups * 16 * code_width(bits);
+        QMat q;
+        qmat_init(q, bits, 1, in_dim, codes + (size_t)r * bpr, norms + (size_t)r * groups);
+        qmat_row(q, 0, out);
+        (void)rows;
+        return 0;
+    } catch (std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
 }
 
 // attend_head_ref over caller-provided caches ([slot][kvh][qk] keys,

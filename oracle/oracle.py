@@ -37,8 +37,8 @@ def lib():
             "orc_prep_group": (F, [P, I, I, P]),
             "orc_chunk_exp": (F, [P, I, F]),
             "orc_key_chunks": (None, [I64, I, I, P, P]),
-            "orc_cq_matmul": (I, [P, P, I, I, P, I, I, P]),
-            "orc_cq_row": (None, [P, P, I, I, I, P]),
+            "orc_cq_matmul": (I, [P, P, I, I, I, P, I, I, P]),
+            "orc_cq_row": (I, [P, P, I, I, I, I, P]),
             "orc_attend_head": (None, [P, P, P, P, I, I, I, P, I, P, I, I, P]),
             "orc_model_load": (P, [P, C.c_uint64]),
             "orc_model_free": (None, [P]),
@@ -157,25 +157,27 @@ def key_chunks(n, nested, nkv):
     return int(c[0]), int(k[0])
 
 
-def cq_matmul(codes, norms, in_dim, x, mode=0):
+def cq_matmul(codes, norms, in_dim, x, mode=0, bits=4):
     """y = x @ W^T with the reference's kernels: decode (T == 1), prefill
-    (block/remainder rule) otherwise; mode 2 = single-row kernel per token."""
+    (block/remainder rule) otherwise; mode 2 = single-row kernel per token.
+    ``bits`` is the record bits (2, 3, 4, or 5 = ternary)."""
     codes = np.ascontiguousarray(codes, np.uint8)
     norms = np.ascontiguousarray(norms, np.uint16)
     x = np.ascontiguousarray(x, np.float32).reshape(-1, in_dim)
     out = norms.shape[0]
     y = np.zeros((x.shape[0], out), np.float32)
-    rc = lib().orc_cq_matmul(_p(codes), _p(norms), out, in_dim, _p(x), x.shape[0], mode, _p(y))
+    rc = lib().orc_cq_matmul(_p(codes), _p(norms), out, in_dim, bits, _p(x), x.shape[0], mode, _p(y))
     if rc != 0:
         raise RuntimeError(lib().orc_last_error().decode())
     return y
 
 
-def cq_row(codes, norms, in_dim, r):
+def cq_row(codes, norms, in_dim, r, bits=4):
     codes = np.ascontiguousarray(codes, np.uint8)
     norms = np.ascontiguousarray(norms, np.uint16)
     out = np.zeros(in_dim, np.float32)
-    lib().orc_cq_row(_p(codes), _p(norms), norms.shape[0], in_dim, r, _p(out))
+    if lib().orc_cq_row(_p(codes), _p(norms), norms.shape[0], in_dim, bits, r, _p(out)) != 0:
+        raise RuntimeError(lib().orc_last_error().decode())
     return out
 
 

@@ -20,7 +20,7 @@ def _cached_archive(name, **shape):
     per process host (the writer is deterministic)."""
     import needle_b200 as nb
 
-    key = hashlib.sha1(repr(sorted(shape.items())).encode()).hexdigest()[:12]
+    key = hashlib.sha1(repr(sorted((k, repr(v)) for k, v in shape.items())).encode()).hexdigest()[:12]
     path = os.path.join(CACHE, f"{name}-{key}.cact")
     if not os.path.exists(path):
         os.makedirs(CACHE, exist_ok=True)
@@ -40,9 +40,22 @@ SMALL = dict(num_layers=3, vocab=1024, engram_slots=96, sliding_window=24, globa
 FULL = dict(seed=0)
 
 
+# Mixed code widths (record bits per CQ role; 5 = ternary): fused parts
+# share a width, ternary and 2-bit parts mix within q|k|v|gate, and every
+# width appears in a matmul, a dequantized row (embedding, engram table)
+# and the mHC rows.
+MIXED_BITS = dict(embedding=2, q=5, k=2, v=5, gate=2, out=3, phi_pre=5, phi_post=3, phi_res=2, table=5, key=3,
+                  value=3)
+
+
 @pytest.fixture(scope="session")
 def small_archive():
     return _cached_archive("small", **SMALL)
+
+
+@pytest.fixture(scope="session")
+def mixed_archive():
+    return _cached_archive("small-mixed", bits=MIXED_BITS, **SMALL)
 
 
 @pytest.fixture(scope="session")

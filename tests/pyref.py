@@ -122,42 +122,89 @@ def int8_codebook(cb):
     return out, f32(s)
 
 
-def unpack4(codes_row):
+TERNARY = 5  # quant.rs:11-12
+
+
+def code_width(bits):
+    return 2 if bits == TERNARY else bits
+
+
+def unpack_lsb(codes_row, width):
+    """quant.rs:208-225: 8 codes per `width` bytes, LSB-first."""
     c = np.asarray(codes_row, np.uint8)
-    out = np.empty(len(c) * 2, np.int64)
-    out[0::2] = c & 15
-    out[1::2] = c >> 4
-    return out
+    out = []
+    for k in range(0, len(c), width):
+        word = 0
+        for b in range(width):
+            word |= int(c[k + b]) << (8 * b)
+        out += [(word >> (i * width)) & ((1 << width) - 1) for i in range(8)]
+    return np.array(out, np.int64)
 
 
-def decode_row(codes_row, norms_row, x, cb):
-    """qlinear.rs:327-350: prep every group, lane sums by (p % 32) / 8, the
-    four-lane fma combine."""
+def unpack4(codes_row):
+    return unpack_lsb(codes_row, 4)
+
+
+def code_table(cb, bits):
+    """qlinear.rs:222-227, 244-256: code -> int8 value (ternary codes 3, 0,
+    1 select centroids 0, 1, 2; codes past the codebook read 0)."""
     vals, cbs = int8_codebook(cb)
-    codes = unpack4(codes_row)
-    groups = len(norms_row)
+    width = code_width(bits)
+    table = []
+    for c in range(1 << width):
+        k = (0 if c == 3 else c + 1) if bits == TERNARY else c
+        table.append(vals[k] if k < len(vals) else 0)
+    return table, cbs
+
+
+def act_pos(p, width):
+    """qlinear.rs:145-147."""
+    return (p % 4) * 32 + p // 4 if width == 2 else (p % 2) * 64 + p // 2
+
+
+def lane_sums(codes, table, q, width, g):
+    """qlinear.rs:327-337, literally: the group's activations stored at
+    act_pos, lane (p % 64) / 16 for width 2, (p % 32) / 8 otherwise."""
+    xq = [0] * 128
+    for p in range(128):
+        xq[act_pos(p, width)] = int(q[p])
+    s = [0, 0, 0, 0]
+    for p in range(128):
+        lane = (p % 64) // 16 if width == 2 else (p % 32) // 8
+        s[lane] += table[codes[g * 128 + p]] * xq[act_pos(p, width)]
+    return s
+
+
+def _f16(n):
+    return np.array([n], np.uint16).view(np.float16)[0].astype(np.float32)
+
+
+def decode_row(codes_row, norms_row, x, cb, bits=4):
+    """qlinear.rs:327-350: prep every group, the decode lane sums, the
+    four-lane fma combine."""
+    table, cbs = code_table(cb, bits)
+    width = code_width(bits)
+    codes = unpack_lsb(codes_row, width)
     lanes = [f32(0)] * 4
-    for g in range(groups):
+    for g in range(len(norms_row)):
         q, sx = prep_group(x, g)
-        s = [0, 0, 0, 0]
-        for p in range(128):
-            s[(p % 32) // 8] += vals[codes[g * 128 + p]] * int(q[p])
-        norm = np.array([norms_row[g]], np.uint16).view(np.float16)[0].astype(np.float32)
-        sc = (sx * cbs) * norm
+        s = lane_sums(codes, table, q, width, g)
+        sc = (sx * cbs) * _f16(norms_row[g])
         for l in range(4):
             lanes[l] = fma32(f32(s[l]), sc, lanes[l])
     return (lanes[0] + lanes[1]) + (lanes[2] + lanes[3])
 
 
-def prefill_row(codes_row, norms_row, x, cb, block):
+def prefill_row(codes_row, norms_row, x, cb, block, bits=4):
     """qlinear.rs:353-363."""
-    vals, cbs = int8_codebook(cb)
-    codes = unpack4(codes_row)
+    table, cbs = code_table(cb, bits)
+    width = code_width(bits)
+    codes = unpack_lsb(codes_row, width)
     acc = f32(0)
     for g in range(len(norms_row)):
         q, sx = prep_group(x, g)
-        s = sum(vals[codes[g * 128 + p]] * int(q[p]) for p in range(128))
-        norm = np.array([norms_row[g]], np.uint16).view(np.float16)[0].astype(np.float32)
+        s = sum(lane_sums(codes, table, q, width, g))
+        norm = _f16(norms_row[g])
         sc = (norm * cbs) * sx if block else norm * (cbs * sx)
         acc = fma32(f32(s), sc, acc)
     return acc

@@ -1,10 +1,12 @@
-"""The CQ-W4/A8 matmul alone on the GPU (nd_cqmat_apply) against the oracle's
+"""The CQ/A8 matmul alone on the GPU (nd_cqmat_apply) against the oracle's
 restatement of qlinear.rs, bit for bit: the decode combine (T = 1) through
 the one-warp GEMV (1-4 rows) and the tensor-core tiles (5+ rows), and the
 prefill combine with its block/remainder rule for the token counts the
 reference's own kernel test uses (qlinear.rs:977-1029: T in 2, 3, 5, 9, 13,
 17) plus full chunks and several sequences at once. Output widths include a
-ragged one (100) so the last column tile is partial."""
+ragged one (100) so the last column tile is partial. Codes of 2 bits
+(their own decode lane rule), 3 bits and ternary records run the same
+cases as 4-bit ones (qlinear.rs:1005-1029)."""
 
 import numpy as np
 import pytest
@@ -49,3 +51,36 @@ def test_cq_matmul_matches_oracle(mats, n, M, T):
     got = mat(x, T=T)
     want = np.concatenate([orc.cq_matmul(codes.reshape(n, -1), norms, 768, x[s:s + T]) for s in range(0, M, T)])
     assert bits_equal(got, want), describe_diff(f"cq matmul M={M} T={T} n={n}", got, want)
+
+
+@pytest.fixture(scope="module")
+def width_mats(cuda_device):
+    import needle_b200 as nb
+
+    rng = np.random.default_rng(78)
+    out = {}
+    for bits in (2, 3, 5):
+        width = nb.code_width(bits)
+        for n in (100, 768):
+            codes = rng.integers(0, 256, (n, 6 * 16 * width), dtype=np.uint8)
+            norms = np.abs(rng.standard_normal((n, 6)) * 0.02).astype(np.float16).view(np.uint16)
+            out[bits, n] = (codes, norms, nb.CQMat(codes, norms, cuda_device, bits=bits))
+    return out
+
+
+WIDTH_CASES = [(1, 1), (2, 1), (4, 1), (5, 1), (200, 1), (3, 3), (5, 5), (17, 17), (64, 32)]
+
+
+@pytest.mark.parametrize("bits", [2, 3, 5])
+@pytest.mark.parametrize("n", [100, 768])
+@pytest.mark.parametrize("M,T", WIDTH_CASES)
+def test_cq_matmul_widths_match_oracle(width_mats, bits, n, M, T):
+    from oracle import oracle as orc
+
+    codes, norms, mat = width_mats[bits, n]
+    rng = np.random.default_rng(2000 * M + T + n + bits)
+    x = rng.standard_normal((M, 768)).astype(np.float32)
+    x[-1] *= 30.0
+    got = mat(x, T=T)
+    want = np.concatenate([orc.cq_matmul(codes, norms, 768, x[s:s + T], bits=bits) for s in range(0, M, T)])
+    assert bits_equal(got, want), describe_diff(f"cq matmul bits={bits} M={M} T={T} n={n}", got, want)
