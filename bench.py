@@ -71,6 +71,40 @@ def archive_bytes():
         return f.read()
 
 
+# A low-width plan for the batch-1 decode leg (record bits per CQ role, 5 =
+# ternary): the attention projections ternary, the out and engram
+# projections 2-bit, the engram tables 3-bit, embedding and mHC rows 4-bit.
+LOW_WIDTH = dict(q=5, k=5, v=5, gate=5, out=2, key=2, value=2, table=3)
+
+
+def low_width_archive():
+    import needle_b200 as nb
+
+    path = os.path.join(CACHE, "needle3-seed0-low-width.cact")
+    if not os.path.exists(path):
+        os.makedirs(CACHE, exist_ok=True)
+        data = nb.synth_cact(seed=0, bits=LOW_WIDTH)
+        tmp = f"{path}.{os.getpid()}.tmp"
+        with open(tmp, "wb") as f:
+            f.write(data)
+        os.replace(tmp, path)
+    with open(path, "rb") as f:
+        return f.read()
+
+
+def decode_weight_bytes(bits=None, L=20, sites=5, vocab=16384):
+    """Codes and f16 norms one decode token streams through the matmuls
+    (q|k|v|gate, out, lm_head, engram key|value; 6 groups a row) plus the
+    int8 mHC rows (24 x 3072 a layer)."""
+    import needle_b200 as nb
+
+    bits = bits or {}
+    w = lambda role: nb.code_width(bits.get(role, 4))
+    row = lambda role: 6 * (16 * w(role) + 2)
+    per_layer = 576 * row("q") + 96 * row("k") + 128 * row("v") + 768 * row("gate") + 768 * row("out") + 24 * 3072
+    return L * per_layer + vocab * row("embedding") + sites * 768 * (row("key") + row("value"))
+
+
 def make_inputs(rank, S, steps, vocab):
     """Prompts [S, 118] and masks [steps, S, vocab/8] (bit set = allowed)."""
     rng = np.random.default_rng(1000 + rank)
@@ -262,21 +296,12 @@ def matmul_sweep(local):
     return rows
 
 
-def secondary(model, local):
-    """The other BASELINE.json throughput configs on this GPU, reported beside
-    the headline: batch-1 decode (configs[0]: 118-token prompt, 45 greedy
-    steps, as `needle bench --decode 45` drives the engine) and batched
-    prefill (configs[3]: 256 sequences x 700 tokens, logits of the last
-    position). CUDA events on the engine's stream."""
+def decode_b1(model, rng, dev):
+    """One sequence: the 118-token prompt, then 45 greedy steps with host
+    buffers, one call per step like the reference's bench loop; a throwaway
+    sequence first, so that no kernel runs cold in the timing."""
     import torch
 
-    import needle_b200 as nb
-
-    out = {}
-    rng = np.random.default_rng(77)
-    dev = f"cuda:{local}"
-    # batch 1, host buffers, one call per step like the reference's bench loop;
-    # a throwaway sequence first, so that no kernel runs cold in the timing
     wb = model.batch(1, PROMPT + 8)
     wb.forward(rng.integers(0, model.vocab, (1, PROMPT)).astype(np.int32))
     for _ in range(4):
@@ -295,10 +320,35 @@ def secondary(model, local):
         b.step(None, nxt)
     e[2].record(st)
     torch.cuda.synchronize()
-    out["decode_b1"] = {"prefill_tok_s": PROMPT / (e[0].elapsed_time(e[1]) / 1e3),
-                        "decode_tok_s": STEPS_CFG / (e[1].elapsed_time(e[2]) / 1e3),
-                        "decode_ms_per_token": e[1].elapsed_time(e[2]) / STEPS_CFG}
+    res = {"prefill_tok_s": PROMPT / (e[0].elapsed_time(e[1]) / 1e3),
+           "decode_tok_s": STEPS_CFG / (e[1].elapsed_time(e[2]) / 1e3),
+           "decode_ms_per_token": e[1].elapsed_time(e[2]) / STEPS_CFG}
     del b
+    return res
+
+
+def secondary(model, local):
+    """The other BASELINE.json throughput configs on this GPU, reported beside
+    the headline: batch-1 decode (configs[0]: 118-token prompt, 45 greedy
+    steps, as `needle bench --decode 45` drives the engine; again on a
+    low-width archive of the same geometry) and batched prefill (configs[3]:
+    256 sequences x 700 tokens, logits of the last position). CUDA events on
+    the engine's stream."""
+    import torch
+
+    import needle_b200 as nb
+
+    out = {}
+    rng = np.random.default_rng(77)
+    dev = f"cuda:{local}"
+    out["decode_b1"] = decode_b1(model, rng, dev)
+    out["decode_b1"]["weight_mb_per_token"] = round(decode_weight_bytes() / 1e6, 2)
+    # the same on a low-width archive (mixed 2-bit, 3-bit, ternary records)
+    low = nb.Model(low_width_archive(), local)
+    out["decode_b1_low_width"] = decode_b1(low, rng, dev)
+    out["decode_b1_low_width"]["weight_mb_per_token"] = round(decode_weight_bytes(LOW_WIDTH) / 1e6, 2)
+    out["decode_b1_low_width"]["bits"] = LOW_WIDTH
+    del low
     # 256 x 700 prefill, ids resident in HBM
     S, n = 256, 700
     b = model.batch(S, n + 1)

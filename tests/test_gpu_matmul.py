@@ -6,7 +6,7 @@ reference's own kernel test uses (qlinear.rs:977-1029: T in 2, 3, 5, 9, 13,
 17) plus full chunks and several sequences at once. Output widths include a
 ragged one (100) so the last column tile is partial. Codes of 2 bits
 (their own decode lane rule), 3 bits and ternary records run the same
-cases as 4-bit ones (qlinear.rs:1005-1029)."""
+cases as 4-bit ones (qlinear.rs:1009-1029)."""
 
 import numpy as np
 import pytest
