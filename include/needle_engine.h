@@ -83,6 +83,24 @@ int nd_head_logits(nd_batch* b, const float* h, int rows, float* out, int flags)
  * (0xf149f2ca). out[out_rows]. Host pointers. */
 int nd_head_logits_sparse(nd_batch* b, const float* h, const int* ids, int n, float* out);
 
+/* The start of the agent's grammar-constrained call step, per sequence,
+ * over logits[S][out_rows] (NULL = the batch's last logits; the agent's
+ * sparse-logit rows, agent.rs:390-420, come in this way)
+ * (crates/needle-engine/src/agent.rs:295-343):
+ * entries whose bit in `allow` is clear read -1e30 (the step's bans; NULL =
+ * none), and over that m[s] = the max and z[s] = sum exp(l - m) as
+ * softmax_stats forms them (agent.rs:1241-1252: four f32 lanes of the
+ * engine's exp over whole groups of four, then the remainder in f64).
+ * Entries whose bit in `allow_order` is also clear (the call step's further
+ * bans; NULL = none) leave the candidates: live[s] = how many logits
+ * exceed -1e30 and ids[s][0..k) the first k of them by logit, lowest id
+ * first on ties (the top-128 partial selection and sort, agent.rs:335-343),
+ * -1 past live. 1 <= k <= 128; masks [S][ceil(out_rows/8)], bit set =
+ * allowed. The grammar's accept test that walks these candidates stays on
+ * the host. Host pointers, or device pointers with ND_DEVICE. */
+int nd_batch_candidates(nd_batch* b, const float* logits, const unsigned char* allow, const unsigned char* allow_order,
+                        int k, int* ids, float* m, double* z, int* live, int flags);
+
 /* The CUDA stream a batch's work runs on (a cudaStream_t); no counterpart
  * in the reference, which runs on the CPU. */
 void* nd_batch_stream(nd_batch* b);

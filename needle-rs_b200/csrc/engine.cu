@@ -418,6 +418,12 @@ struct Batch {
     int32_t *ids, *next;
     int32_t* d_len;  // device copy of len (Caches::len)
     uint8_t* masks;
+    // the call sampler's buffers (nd_batch_candidates), made on first use
+    float* clogits = nullptr;
+    uint8_t *cmask1 = nullptr, *cmask2 = nullptr;
+    int32_t *cids = nullptr, *clive = nullptr;
+    float* cm = nullptr;
+    double* cz = nullptr;
     size_t logits_cap = 0;
     std::map<std::string, std::pair<float*, size_t>> snaps;
     int last_rows = 0, last_T = 0;
@@ -918,6 +924,61 @@ int nd_head_logits_sparse(nd_batch* bh, const float* h, const int* ids, int n, f
         std::memcpy(&neg, &negu, 4);
         for (int k = 0; k < V; k++) out[k] = neg;
         for (int k = 0; k < n; k++) out[ids[k]] = full[ids[k]];
+        return 0;
+    } catch (std::exception& e) {
+        return fail(e);
+    }
+}
+
+int nd_batch_candidates(nd_batch* bh, const float* logits, const unsigned char* allow, const unsigned char* allow_order, int k,
+                        int* ids, float* m, double* z, int* live, int flags) {
+    try {
+        if (!bh || !ids || !m || !z || !live) throw std::runtime_error("nd_batch_candidates: null argument");
+        Batch& b = *bh->b;
+        CK(cudaSetDevice(b.m->device));
+        if (!logits && (!b.have_logits || b.logits_rows != b.S))
+            throw std::runtime_error("nd_batch_candidates needs the last logits of every sequence");
+        if (k < 1 || k > 128) throw std::runtime_error("nd_batch_candidates: k must be in [1, 128]");
+        const int V = b.m->c.out_rows();
+        if (V > 32768) throw std::runtime_error("nd_batch_candidates: more than 32768 logits a row");
+        const bool dev = flags & ND_DEVICE;
+        const size_t mb = (size_t)(V + 7) / 8;
+        if (!b.cids) {
+            b.clogits = b.alloc<float>((size_t)b.S * V);
+            b.cmask1 = b.alloc<uint8_t>((size_t)b.S * mb);
+            b.cmask2 = b.alloc<uint8_t>((size_t)b.S * mb);
+            b.cids = b.alloc<int32_t>((size_t)b.S * 128);
+            b.clive = b.alloc<int32_t>((size_t)b.S);
+            b.cm = b.alloc<float>((size_t)b.S);
+            b.cz = b.alloc<double>((size_t)b.S);
+        }
+        const float* src = b.logits;
+        if (logits && dev) src = logits;
+        if (logits && !dev) {
+            CK(cudaMemcpyAsync(b.clogits, logits, (size_t)b.S * V * sizeof(float), cudaMemcpyHostToDevice, b.st));
+            src = b.clogits;
+        }
+        const uint8_t *a1 = allow, *a2 = allow_order;
+        if (allow && !dev) {
+            CK(cudaMemcpyAsync(b.cmask1, allow, (size_t)b.S * mb, cudaMemcpyHostToDevice, b.st));
+            a1 = b.cmask1;
+        }
+        if (allow_order && !dev) {
+            CK(cudaMemcpyAsync(b.cmask2, allow_order, (size_t)b.S * mb, cudaMemcpyHostToDevice, b.st));
+            a2 = b.cmask2;
+        }
+        int32_t* di = dev ? (int32_t*)ids : b.cids;
+        int32_t* dl = dev ? (int32_t*)live : b.clive;
+        float* dm = dev ? m : b.cm;
+        double* dz = dev ? z : b.cz;
+        CK(launch_candidates(src, b.S, V, a1, a2, k, di, dm, dz, dl, b.st));
+        if (!dev) {
+            CK(cudaMemcpyAsync(ids, b.cids, (size_t)b.S * k * sizeof(int32_t), cudaMemcpyDeviceToHost, b.st));
+            CK(cudaMemcpyAsync(live, b.clive, (size_t)b.S * sizeof(int32_t), cudaMemcpyDeviceToHost, b.st));
+            CK(cudaMemcpyAsync(m, b.cm, (size_t)b.S * sizeof(float), cudaMemcpyDeviceToHost, b.st));
+            CK(cudaMemcpyAsync(z, b.cz, (size_t)b.S * sizeof(double), cudaMemcpyDeviceToHost, b.st));
+            CK(cudaStreamSynchronize(b.st));
+        }
         return 0;
     } catch (std::exception& e) {
         return fail(e);

@@ -593,14 +593,6 @@ __global__ void post_block_kernel(LayerW w, const float* o, const float* x1, con
 __global__ void attention_kernel(const float* qbuf, const float* proj, Caches c, int l, int T, const int32_t* p0p, int window, float* att,
                                  int8_t* act, float* sx);
 
-static cudaError_t init_attrs() {
-    cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_SMEM);
-    cudaFuncSetAttribute(post_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)POST_SMEM);
-    cudaFuncSetAttribute(post_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)POST_ROW_SMEM);
-    cudaFuncSetAttribute(cq_mma_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
-    cudaFuncSetAttribute(cq_mma_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
-    return cudaFuncSetAttribute(cq_mma_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
-}
 
 // ---------------------------------------------------------------- engram
 
@@ -1949,6 +1941,231 @@ __global__ void masked_argmax_kernel(const float* logits, int V, const uint8_t* 
 void launch_masked_argmax(const float* logits, int S, int V, const uint8_t* allow, int32_t* next, cudaStream_t st) {
     COUNT_LAUNCH();
     launch_pdl(masked_argmax_kernel, dim3(S), dim3(256), 0, st, logits, V, allow, next);
+}
+
+// ----------------------------------------------------------- call sampler
+//
+// The statistics and candidate order the agent's grammar-constrained call
+// step starts from, per sequence (agent.rs:295-343): softmax_stats
+// (agent.rs:1241-1252) over the logits with the step's bans, then the
+// unmasked candidates by logit (lowest id first on ties) after the call
+// step's further bans, the first k of them. One CTA per sequence of 512
+// threads, each holding V / 512 logits in registers:
+//   * the max by a block reduction (exact);
+//   * engine_expf(v - max) of every element of the whole groups of four into
+//     shared memory, then the reference's four lane chains (lane j sums
+//     elements 4i + j in order, lane_exp_sums, agent.rs:1147-1198) by four
+//     threads, the lanes summed (l0 + l1) + (l2 + l3) and widened, the
+//     remainder in f64;
+//   * the k-th smallest of the 48-bit keys (~orderable(logit) << 16 | id),
+//     whose order is the reference's (logit descending, id ascending), by
+//     six 8-bit radix passes over shared histograms; the keys at or below
+//     it are the k candidates, ranked by counting.
+constexpr int CAND_THREADS = 512, CAND_MAXK = 128;
+
+// agent.rs:1130-1145: the engine's own f32 exp (its constants).
+__device__ __forceinline__ float engine_expf(float x) {
+    x = fminf(fmaxf(x, -88.37626f), 88.37626f);
+    const float n = rintf(__fmul_rn(x, 1.44269504088896340736f));
+    x = __fmaf_rn(n, -0.6933594f, x);
+    x = __fmaf_rn(n, 2.1219444e-4f, x);
+    float p = 1.9875691e-4f;
+    p = __fmaf_rn(p, x, 1.3981999e-3f);
+    p = __fmaf_rn(p, x, 8.333452e-3f);
+    p = __fmaf_rn(p, x, 4.1665796e-2f);
+    p = __fmaf_rn(p, x, 1.6666665e-1f);
+    p = __fmaf_rn(p, x, 0.5f);
+    const float y = __fmaf_rn(__fmul_rn(x, x), p, x);
+    const float two_n = __uint_as_float((unsigned)((int)n + 127) << 23);
+    return __fmaf_rn(two_n, y, two_n);
+}
+
+// Ascending 48-bit key of (logit descending, id ascending); -0 and +0 are
+// the same logit, as partial_cmp has them.
+__device__ __forceinline__ unsigned long long cand_key(float v, int i) {
+    if (v == 0.f) v = 0.f;
+    unsigned u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)(~u) << 16) | (unsigned)i;
+}
+
+__device__ __forceinline__ bool bit_clear(const uint8_t* bits, int i) { return bits && !((bits[i >> 3] >> (i & 7)) & 1); }
+
+// f32::max as the reference's platform computes it (aarch64 FMAXNM): equal
+// values keep +0 over -0, so the result does not depend on the order.
+__device__ __forceinline__ float fmaxnm(float a, float b) {
+    if (a > b) return a;
+    if (b > a) return b;
+    return signbit(a) ? b : a;
+}
+
+template <int VPT>
+__global__ void __launch_bounds__(CAND_THREADS) candidates_kernel(const float* logits, int V, const uint8_t* allow,
+                                                                  const uint8_t* allow_order, int k, int32_t* ids,
+                                                                  float* mo, double* zo, int32_t* live_out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    extern __shared__ float ex[];  // [V / 4 * 4]: engine_expf(v - max)
+    __shared__ unsigned hist[256];
+    __shared__ float redf[CAND_THREADS / 32];
+    __shared__ int redi[CAND_THREADS / 32];
+    __shared__ unsigned long long ckey[CAND_MAXK];
+    __shared__ float lane_sum[4];
+    __shared__ unsigned long long s_prefix;
+    __shared__ int s_rem, s_count;
+    const int s = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float* x = logits + (size_t)s * V;
+    const size_t mb = (size_t)(V + 7) / 8;
+    const uint8_t* a1 = allow ? allow + (size_t)s * mb : nullptr;
+    const uint8_t* a2 = allow_order ? allow_order + (size_t)s * mb : nullptr;
+    float v[VPT];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < VPT; j++) {
+        const int i = tid + j * CAND_THREADS;
+        float t = -INFINITY;
+        if (i < V) {
+            t = bit_clear(a1, i) ? -1e30f : x[i];
+            mx = fmaxnm(mx, t);
+        }
+        v[j] = t;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxnm(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) redf[warp] = mx;
+    __syncthreads();
+    float m = redf[0];
+    for (int w = 1; w < CAND_THREADS / 32; w++) m = fmaxnm(m, redf[w]);
+    const int main = V / 4 * 4;
+    int nl = 0;
+#pragma unroll
+    for (int j = 0; j < VPT; j++) {
+        const int i = tid + j * CAND_THREADS;
+        if (i < main) ex[i] = engine_expf(__fsub_rn(v[j], m));
+        if (i < V && bit_clear(a2, i)) v[j] = -1e30f;
+        nl += (i < V && v[j] > -1e30f) ? 1 : 0;
+    }
+    nl = warp_sum_i(nl);
+    if (lane == 0) redi[warp] = nl;
+    __syncthreads();
+    int live = 0;
+    for (int w = 0; w < CAND_THREADS / 32; w++) live += redi[w];
+    // the four lane chains, in element order
+    if (tid < 4) {
+        float acc = 0.f;
+#pragma unroll 8
+        for (int i = tid; i < main; i += 4) acc = __fadd_rn(acc, ex[i]);
+        lane_sum[tid] = acc;
+    }
+    const int K = min(k, live);
+    unsigned long long prefix = 0ull, pmask = 0ull;
+    int rem = K;
+    if (K > 0) {
+        for (int pass = 0; pass < 6; pass++) {
+            const int shift = 40 - 8 * pass;
+            for (int b = tid; b < 256; b += CAND_THREADS) hist[b] = 0u;
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < VPT; j++) {
+                const int i = tid + j * CAND_THREADS;
+                if (i < V && v[j] > -1e30f) {
+                    const unsigned long long key = cand_key(v[j], i);
+                    if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+                }
+            }
+            __syncthreads();
+            if (warp == 0) {
+                unsigned c[8], tot = 0;
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    c[e] = hist[8 * lane + e];
+                    tot += c[e];
+                }
+                unsigned incl = tot;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const unsigned t = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += t;
+                }
+                const unsigned excl = incl - tot;
+                if (excl < (unsigned)rem && (unsigned)rem <= incl) {
+                    unsigned run = excl;
+                    int b = 7;
+                    for (int e = 0; e < 8; e++) {
+                        if (run + c[e] >= (unsigned)rem) { b = e; break; }
+                        run += c[e];
+                    }
+                    s_prefix = prefix | ((unsigned long long)(8 * lane + b) << shift);
+                    s_rem = rem - (int)run;
+                }
+            }
+            __syncthreads();
+            prefix = s_prefix;
+            rem = s_rem;
+            pmask |= 255ull << shift;
+        }
+    }
+    if (tid == 0) s_count = 0;
+    __syncthreads();
+    if (K > 0) {
+#pragma unroll
+        for (int j = 0; j < VPT; j++) {
+            const int i = tid + j * CAND_THREADS;
+            if (i < V && v[j] > -1e30f) {
+                const unsigned long long key = cand_key(v[j], i);
+                if (key <= prefix) {
+                    const int slot = atomicAdd(&s_count, 1);
+                    if (slot < CAND_MAXK) ckey[slot] = key;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    int32_t* out = ids + (size_t)s * k;
+    if (tid < K) {
+        const unsigned long long kt = ckey[tid];
+        int r = 0;
+        for (int j = 0; j < K; j++) r += ckey[j] < kt ? 1 : 0;
+        out[r] = (int32_t)(kt & 0xffffu);
+    } else if (tid < k) {
+        out[tid] = -1;
+    }
+    if (tid == 0) {
+        double z = (double)__fadd_rn(__fadd_rn(lane_sum[0], lane_sum[1]), __fadd_rn(lane_sum[2], lane_sum[3]));
+        for (int i = main; i < V; i++) {
+            const float t = bit_clear(a1, i) ? -1e30f : x[i];
+            if (t > -1e30f) z = __dadd_rn(z, exp(__dsub_rn((double)t, (double)m)));
+        }
+        mo[s] = m;
+        zo[s] = z;
+        live_out[s] = live;
+    }
+}
+
+cudaError_t launch_candidates(const float* logits, int S, int V, const uint8_t* allow, const uint8_t* allow_order, int k,
+                              int32_t* ids, float* m, double* z, int32_t* live, cudaStream_t st) {
+    if (S < 1 || V < 1 || V > 64 * CAND_THREADS || k < 1 || k > CAND_MAXK) return cudaErrorInvalidValue;
+    COUNT_LAUNCH();
+    const size_t smem = (size_t)(V / 4 * 4) * sizeof(float);
+    if (V <= 16 * CAND_THREADS)
+        launch_pdl(candidates_kernel<16>, dim3(S), dim3(CAND_THREADS), smem, st, logits, V, allow, allow_order, k, ids, m, z, live);
+    else if (V <= 32 * CAND_THREADS)
+        launch_pdl(candidates_kernel<32>, dim3(S), dim3(CAND_THREADS), smem, st, logits, V, allow, allow_order, k, ids, m, z, live);
+    else
+        launch_pdl(candidates_kernel<64>, dim3(S), dim3(CAND_THREADS), smem, st, logits, V, allow, allow_order, k, ids, m, z, live);
+    return cudaSuccess;
+}
+
+static cudaError_t init_attrs() {
+    cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_SMEM);
+    cudaFuncSetAttribute(post_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)POST_SMEM);
+    cudaFuncSetAttribute(post_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)POST_ROW_SMEM);
+    cudaFuncSetAttribute(candidates_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 16 * CAND_THREADS * 4);
+    cudaFuncSetAttribute(candidates_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 32 * CAND_THREADS * 4);
+    cudaFuncSetAttribute(candidates_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * CAND_THREADS * 4);
+    cudaFuncSetAttribute(cq_mma_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
+    cudaFuncSetAttribute(cq_mma_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
+    return cudaFuncSetAttribute(cq_mma_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
 }
 
 }  // namespace nd

@@ -116,5 +116,13 @@ void launch_rope_rows(const float* table_cos, const float* table_sin, const floa
 void launch_advance_len(int32_t* len, int T, cudaStream_t st);
 void launch_hold(unsigned long long ns, cudaStream_t st);
 void launch_masked_argmax(const float* logits, int S, int V, const uint8_t* allow, int32_t* next, cudaStream_t st);
+// The call sampler's start, per row of logits [S][V] (V <= 32768): with the
+// entries whose `allow` bit is clear read as -1e30, the max m[s] and
+// z[s] = sum exp(l - m) as agent.rs:1241-1252 forms them; with those of
+// `allow_order` cleared too, live[s] = how many exceed -1e30 and ids[s][0..k)
+// the first k of them by (logit descending, id ascending) (agent.rs:335-343),
+// -1 past live. k <= 128. cudaErrorInvalidValue (nothing launched) otherwise.
+cudaError_t launch_candidates(const float* logits, int S, int V, const uint8_t* allow, const uint8_t* allow_order, int k,
+                              int32_t* ids, float* m, double* z, int32_t* live, cudaStream_t st);
 
 }  // namespace nd

@@ -43,6 +43,7 @@ def lib():
             "nd_head_logits": (I, [P, P, I, P, I]),
             "nd_head_logits_sparse": (I, [P, P, P, I, P]),
             "nd_batch_stream": (P, [P]),
+            "nd_batch_candidates": (I, [P, P, P, P, I, P, P, P, P, I]),
             "nd_cq_pack": (I, [P, I, I, I, P, P]),
             "nd_cqmat_new": (I, [I, P, P, I, I, I, C.POINTER(P)]),
             "nd_cqmat_free": (None, [P]),
@@ -305,6 +306,24 @@ class Batch:
         if lib().nd_head_logits_sparse(self._h, _p(h), _p(ids), len(ids), _p(out)) != 0:
             raise _err()
         return out
+
+    def candidates(self, allow=None, allow_order=None, k=128, logits=None):
+        """The call step's start over the last logits, or over host
+        ``logits`` [S][out_rows] (agent.rs:295-343): per sequence the first
+        k candidates by (logit desc, id asc), -1 past the live count, and
+        the softmax max and sum. Returns (ids [S][k], m [S], z [S], live
+        [S])."""
+        S = self.num_seqs
+        ids = np.zeros((S, k), np.int32)
+        m = np.zeros(S, np.float32)
+        z = np.zeros(S, np.float64)
+        live = np.zeros(S, np.int32)
+        a1 = None if allow is None else np.ascontiguousarray(allow, np.uint8)
+        a2 = None if allow_order is None else np.ascontiguousarray(allow_order, np.uint8)
+        lg = None if logits is None else np.ascontiguousarray(logits, np.float32).reshape(S, self.model.out_rows)
+        if lib().nd_batch_candidates(self._h, _p(lg), _p(a1), _p(a2), k, _p(ids), _p(m), _p(z), _p(live), 0) != 0:
+            raise _err()
+        return ids, m, z, live
 
     def time_site(self, site):
         """Record CUDA events around every launch of a site (see SITES)."""

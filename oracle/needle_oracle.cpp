@@ -1449,6 +1449,66 @@ static uint32_t masked_argmax(const float* x, int n, const uint8_t* allow_bits) 
     return 0;
 }
 
+// ------------------------------------------------- the call sampler (agent.rs)
+
+// agent.rs:1130-1145: the engine's f32 exp (its own constants).
+float engine_expf(float x) {
+    const float LOG2E = 1.44269504088896340736f;
+    x = std::min(std::max(x, -88.37626f), 88.37626f);
+    float n = std::nearbyint(x * LOG2E);  // round_ties_even
+    x = std::fmaf(n, -0.6933594f, x);
+    x = std::fmaf(n, 2.1219444e-4f, x);
+    float p = 1.9875691e-4f;
+    p = std::fmaf(p, x, 1.3981999e-3f);
+    p = std::fmaf(p, x, 8.333452e-3f);
+    p = std::fmaf(p, x, 4.1665796e-2f);
+    p = std::fmaf(p, x, 1.6666665e-1f);
+    p = std::fmaf(p, x, 0.5f);
+    float y = std::fmaf(x * x, p, x);
+    float two_n = bitsf((uint32_t)((int32_t)n + 127) << 23);
+    return std::fmaf(two_n, y, two_n);
+}
+
+// agent.rs:1241-1252 with lane_exp_sums (1147-1198, scalar arm): the max,
+// then four f32 lanes of engine_expf(v - m) over whole groups of four (lane
+// j takes elements 4i + j in order), summed (l0 + l1) + (l2 + l3) and
+// widened, then the remainder in f64 skipping masked logits.
+// f32::max as the reference's platform computes it (aarch64 FMAXNM: -0 < +0).
+static inline float fmaxnm(float a, float b) {
+    if (a > b) return a;
+    if (b > a) return b;
+    return std::signbit(a) ? b : a;
+}
+
+void softmax_stats(const float* x, int n, float* m_out, double* z_out) {
+    float m = -INFINITY;
+    for (int i = 0; i < n; i++) m = fmaxnm(m, x[i]);
+    const int main = n / 4 * 4;
+    float lanes[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int i = 0; i < main; i += 4)
+        for (int j = 0; j < 4; j++) lanes[j] = lanes[j] + engine_expf(x[i + j] - m);
+    double z = (double)((lanes[0] + lanes[1]) + (lanes[2] + lanes[3]));
+    for (int i = main; i < n; i++)
+        if (x[i] > -1e30f) z += lexp((double)x[i] - (double)m);
+    *m_out = m;
+    *z_out = z;
+}
+
+// agent.rs:335-343: the unmasked candidates (logit > -1e30) by logit, the
+// lowest id first on ties; the first min(k, live) of them. Returns live.
+int candidate_order(const float* x, int n, int k, int32_t* out) {
+    std::vector<int32_t> order;
+    for (int i = 0; i < n; i++)
+        if (x[i] > -1e30f) order.push_back(i);
+    const int live = (int)order.size(), head = std::min(k, live);
+    std::partial_sort(order.begin(), order.begin() + head, order.end(), [&](int32_t a, int32_t b) {
+        if (x[a] != x[b]) return x[a] > x[b];
+        return a < b;
+    });
+    for (int i = 0; i < head; i++) out[i] = order[i];
+    return live;
+}
+
 }  // namespace orc
 
 // ================================================================ C ABI
@@ -1602,6 +1662,9 @@ int orc_last_hidden(void* s, float* out) {
     return (int)ss->last_hidden.size();
 }
 uint32_t orc_masked_argmax(const float* x, int n, const uint8_t* allow_bits) { return masked_argmax(x, n, allow_bits); }
+float orc_engine_expf(float x) { return engine_expf(x); }
+void orc_softmax_stats(const float* x, int n, float* m, double* z) { softmax_stats(x, n, m, z); }
+int orc_candidate_order(const float* x, int n, int k, int32_t* out) { return candidate_order(x, n, k, out); }
 
 void orc_trace(int on) {
     g_trace.on = on != 0;

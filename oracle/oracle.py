@@ -53,6 +53,9 @@ def lib():
             "orc_head_logits_sparse": (None, [P, P, P, I, P]),
             "orc_last_hidden": (I, [P, P]),
             "orc_masked_argmax": (U32, [P, I, P]),
+            "orc_engine_expf": (C.c_float, [C.c_float]),
+            "orc_softmax_stats": (None, [P, I, P, P]),
+            "orc_candidate_order": (I, [P, I, I, P]),
             "orc_trace": (None, [I]),
             "orc_trace_get": (I, [C.c_char_p, P, I]),
             "orc_generate": (I, [P, P, I, I, P, P, P]),
@@ -192,6 +195,29 @@ def attend_head(k8, ks, v8, vs, q, kvh, slots, nested):
                           _p(np.ascontiguousarray(v8)), _p(np.ascontiguousarray(vs, np.float32)),
                           nkv, qk, vd, _p(q), kvh, _p(slots), len(slots), int(nested), _p(out))
     return out
+
+
+def engine_expf(x: float) -> float:
+    """agent.rs:1130-1145."""
+    return lib().orc_engine_expf(float(x))
+
+
+def softmax_stats(x):
+    """agent.rs:1241-1252: (max, sum exp(l - max)) as the call sampler has them."""
+    x = np.ascontiguousarray(x, np.float32)
+    m = np.zeros(1, np.float32)
+    z = np.zeros(1, np.float64)
+    lib().orc_softmax_stats(_p(x), len(x), _p(m), _p(z))
+    return m[0], z[0]
+
+
+def candidate_order(x, k=128):
+    """agent.rs:335-343: the first k unmasked candidates by (logit desc, id
+    asc), and how many are unmasked."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.zeros(k, np.int32)
+    live = lib().orc_candidate_order(_p(x), len(x), k, _p(out))
+    return out[:min(k, live)], live
 
 
 def masked_argmax(x, allow_bits=None):

@@ -270,3 +270,43 @@ def sinkhorn64(z):
             for r in range(4):
                 e[r * 4 + c] *= inv
     return np.array(e, np.float32)
+
+
+def engine_expf(x):
+    """agent.rs:1130-1145."""
+    x = f32(min(max(f32(x), f32(-88.37626)), f32(88.37626)))
+    n = f32(np.rint(x * f32(1.4426950408889634)))
+    x = fma32(n, f32(-0.6933594), x)
+    x = fma32(n, f32(2.1219444e-4), x)
+    p = f32(1.9875691e-4)
+    for c in (1.3981999e-3, 8.333452e-3, 4.1665796e-2, 1.6666665e-1, 0.5):
+        p = fma32(p, x, f32(c))
+    y = fma32(x * x, p, x)
+    two_n = np.array([((int(n) + 127) << 23) & 0xFFFFFFFF], np.uint32).view(np.float32)[0]
+    return fma32(two_n, y, two_n)
+
+
+def softmax_stats(x):
+    """agent.rs:1241-1252 with lane_exp_sums' scalar arm (1189-1197)."""
+    x = np.asarray(x, np.float32)
+    m = f32(-np.inf)
+    for v in x:  # f32::max on aarch64 (FMAXNM): -0 < +0
+        m = v if (v > m or (v == m and not np.signbit(v))) else m
+    main = len(x) // 4 * 4
+    lanes = [f32(0)] * 4
+    for i in range(0, main, 4):
+        for j in range(4):
+            lanes[j] = f32(lanes[j] + engine_expf(f32(x[i + j] - m)))
+    z = float(f32((lanes[0] + lanes[1]) + (lanes[2] + lanes[3])))
+    for v in x[main:]:
+        if v > f32(-1e30):
+            z += float(np.exp(np.float64(v) - np.float64(m)))
+    return m, z
+
+
+def candidate_order(x, k):
+    """agent.rs:335-343."""
+    x = np.asarray(x, np.float32)
+    order = [i for i in range(len(x)) if x[i] > f32(-1e30)]
+    order.sort(key=lambda i: (-float(x[i]), i))
+    return order[:k], len(order)
