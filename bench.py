@@ -327,6 +327,45 @@ def decode_b1(model, rng, dev):
     return res
 
 
+def call_candidates(model, dev, S=1024, k=128, reps=20):
+    """nd_batch_candidates over 1024 rows of Needle 3 logits in HBM (the
+    agent's call step start: softmax stats and the top 128 in the
+    reference's order), device pointers, CUDA events on the batch's stream."""
+    import ctypes
+
+    import torch
+
+    import needle_b200 as nb
+
+    V = model.out_rows
+    b = model.batch(S, 8)
+    st = torch.cuda.ExternalStream(b.stream, device=dev)
+    g = torch.Generator(device=dev).manual_seed(5)
+    logits = torch.randn((S, V), generator=g, device=dev) * 3
+    allow = torch.randint(0, 256, (S, (V + 7) // 8), generator=g, device=dev, dtype=torch.uint8)
+    ids = torch.empty((S, k), dtype=torch.int32, device=dev)
+    m = torch.empty(S, dtype=torch.float32, device=dev)
+    z = torch.empty(S, dtype=torch.float64, device=dev)
+    live = torch.empty(S, dtype=torch.int32, device=dev)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    call = lambda: nb.lib().nd_batch_candidates(b._h, P(logits), P(allow), None, k, P(ids), P(m), P(z), P(live),
+                                                nb.ND_DEVICE)
+    torch.cuda.synchronize()
+    for _ in range(3):
+        if call() != 0:
+            raise nb._err()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        call()
+    e1.record(st)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    del b
+    return {"rows": S, "vocab": V, "k": k, "us_per_call": round(us, 2),
+            "logit_gbs": round(S * V * 4 / (us * 1e-6) / 1e9, 1)}
+
+
 def secondary(model, local):
     """The other BASELINE.json throughput configs on this GPU, reported beside
     the headline: batch-1 decode (configs[0]: 118-token prompt, 45 greedy
@@ -349,6 +388,7 @@ def secondary(model, local):
     out["decode_b1_low_width"]["weight_mb_per_token"] = round(decode_weight_bytes(LOW_WIDTH) / 1e6, 2)
     out["decode_b1_low_width"]["bits"] = LOW_WIDTH
     del low
+    out["call_candidates_1024"] = call_candidates(model, dev)
     # 256 x 700 prefill, ids resident in HBM
     S, n = 256, 700
     b = model.batch(S, n + 1)

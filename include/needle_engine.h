@@ -133,11 +133,13 @@ int nd_cqmat_apply(nd_cqmat* mat, const float* x, int M, int T, float* y, int re
  * a bit mask of layers, global_mask likewise). cq_bits[i] is the record
  * bits (2, 3, 4, 5 = ternary) of the i-th CQ record in record order, 4 past
  * n_cq_bits (a mixed-width archive; the reference's packer writes one
- * width). With out == NULL returns the byte size in *len; else writes up
- * to cap bytes. */
+ * width). heads_mask bit c appends probe head c (1 embedding, 2
+ * confidence, 3 router; cact.rs:354-392: 4 probes a depth, 4 queries, the
+ * embedding head 128 wide). With out == NULL returns the byte size in
+ * *len; else writes up to cap bytes. */
 int nd_synth_cact(int num_layers, int vocab, int engram_slots, int sliding_window, unsigned long long global_mask,
                   unsigned long long engram_sites, unsigned long long seed, float std, const int* cq_bits, int n_cq_bits,
-                  unsigned char* out, unsigned long long cap, unsigned long long* len);
+                  unsigned heads_mask, unsigned char* out, unsigned long long cap, unsigned long long* len);
 
 /* Kernel launches this process has issued (all batches, all devices); no
  * counterpart in the reference. */

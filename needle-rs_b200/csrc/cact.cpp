@@ -242,7 +242,7 @@ struct Out {
     std::vector<uint8_t> blob;
     uint32_t group = 0, bits = 0;
     // generation recipe
-    enum Kind { RANDOM_F16, RANDOM_CQ, PERM } kind;
+    enum Kind { RANDOM_F16, RANDOM_CQ, PERM, VALUES } kind;
     int rows = 0, cols = 0;
     std::vector<float> perm;
 };
@@ -360,6 +360,33 @@ std::vector<uint8_t> synth_cact(const SynthSpec& sp) {
         f16({4, (uint32_t)d});               // taps
     }
     f16({(uint32_t)d});  // final_norm
+    // cact.rs:362-392: the probe heads present, in HEAD_KEYS order (codes 1
+    // embedding, 2 confidence, 3 router), after a manifest of their codes.
+    std::vector<int> head_codes;
+    for (int code = 1; code <= 3; code++)
+        if ((sp.heads_mask >> code) & 1) head_codes.push_back(code);
+    if (!head_codes.empty()) {
+        const int l1 = L + 1, k = sp.probes, q = sp.queries;
+        auto values = [&](std::vector<float> v) {
+            Out o;
+            o.dtype = CACT_F16;
+            o.kind = Out::VALUES;
+            o.shape = {(uint32_t)v.size()};
+            o.perm = v;
+            ts.push_back(o);
+        };
+        values(std::vector<float>(head_codes.begin(), head_codes.end()));
+        for (int code : head_codes) {
+            const int out = code == 1 ? sp.embedding_dim : code == 2 ? 1 : 3;
+            cq(l1 * k, d);                                           // probes [(L+1) * k, d]
+            f16({(uint32_t)l1, (uint32_t)k});                        // gain
+            cq(q, d);                                                // query
+            f16({(uint32_t)q, (uint32_t)l1, (uint32_t)k});           // row_bias
+            cq(out, q * d);                                          // proj [out, q * d]
+            f16({(uint32_t)out});                                    // bias
+            if (code == 3) values({0.90f, 0.00f, 0.60f});            // calibration
+        }
+    }
 
     // Fill the blobs, records in parallel, each from its own sub-stream.
     std::atomic<size_t> next(0);
@@ -369,7 +396,13 @@ std::vector<uint8_t> synth_cact(const SynthSpec& sp) {
             if (i >= ts.size()) return;
             Out& o = ts[i];
             Normal rng(sp.seed * 0x100000001B3ull + 0x51ED270B2A6F1C3Dull * (i + 1));
-            if (o.kind == Out::PERM) {
+            if (o.kind == Out::VALUES) {
+                o.blob.resize(o.perm.size() * 2);
+                for (size_t k2 = 0; k2 < o.perm.size(); k2++) {
+                    uint16_t h = f32_to_f16(o.perm[k2]);
+                    std::memcpy(&o.blob[2 * k2], &h, 2);
+                }
+            } else if (o.kind == Out::PERM) {
                 o.blob.resize(o.perm.size() * 4);
                 std::memcpy(o.blob.data(), o.perm.data(), o.blob.size());
             } else if (o.kind == Out::RANDOM_F16) {

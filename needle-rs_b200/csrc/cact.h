@@ -54,6 +54,11 @@ struct SynthSpec {
     // Code width of each CQ record in record order (2, 3, 4 or CQ_TERNARY);
     // records past the end of the list are 4-bit.
     std::vector<int> cq_bits;
+    // Probe heads to append (bit `code`: 1 embedding, 2 confidence, 3
+    // router), with k probes per depth, q queries, and the embedding head's
+    // width (config.rs:27-33, 72-77).
+    unsigned heads_mask = 0;
+    int probes = 4, queries = 4, embedding_dim = 128;
 };
 
 // A random-init Needle 3 archive: every tensor ~N(0, std^2) drawn in record

@@ -1094,9 +1094,11 @@ int nd_cq_pack(const float* w, int rows, int d, int bits, unsigned char* codes, 
 
 int nd_synth_cact(int num_layers, int vocab, int engram_slots, int sliding_window, unsigned long long global_mask,
                   unsigned long long engram_sites, unsigned long long seed, float std, const int* cq_bits, int n_cq_bits,
-                  unsigned char* out, unsigned long long cap, unsigned long long* len) {
+                  unsigned heads_mask, unsigned char* out, unsigned long long cap, unsigned long long* len) {
     try {
         SynthSpec sp;
+        if (heads_mask & ~0xEu) throw std::runtime_error("nd_synth_cact: probe head codes are 1, 2 and 3");
+        sp.heads_mask = heads_mask;
         if (n_cq_bits < 0 || (n_cq_bits > 0 && !cq_bits)) throw std::runtime_error("nd_synth_cact: bad code width list");
         sp.cq_bits.assign(cq_bits, cq_bits + n_cq_bits);
         sp.num_layers = num_layers;

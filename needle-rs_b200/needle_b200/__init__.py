@@ -48,7 +48,7 @@ def lib():
             "nd_cqmat_new": (I, [I, P, P, I, I, I, C.POINTER(P)]),
             "nd_cqmat_free": (None, [P]),
             "nd_cqmat_apply": (I, [P, P, I, I, P, I, C.POINTER(C.c_float)]),
-            "nd_synth_cact": (I, [I, I, I, I, U64, U64, U64, C.c_float, P, I, P, U64, C.POINTER(U64)]),
+            "nd_synth_cact": (I, [I, I, I, I, U64, U64, U64, C.c_float, P, I, C.c_uint, P, U64, C.POINTER(U64)]),
             "nd_batch_debug": (I, [P, C.c_char_p, P, C.c_longlong]),
             "nd_batch_debug_layer": (I, [P, I]),
             "nd_launch_count": (C.c_longlong, []),
@@ -109,14 +109,18 @@ def cq_roles(num_layers=20, engram_sites=(3, 7, 11, 15, 19), **_):
     return roles
 
 
-def synth_cact(seed=0, std=0.02, bits=None, **shape) -> bytes:
+HEAD_EMBEDDING, HEAD_CONFIDENCE, HEAD_ROUTER = 1, 2, 3  # probe head codes (cact.rs:354-360)
+
+
+def synth_cact(seed=0, std=0.02, bits=None, heads=(), **shape) -> bytes:
     """A random-init Needle 3 archive (every tensor ~N(0, std^2)), CQ
     matrices packed by the reference's quantizer, in the reference's record
     order (crates/needle-core/src/cact.rs:279-475). ``bits`` sets the record
     bits of the CQ matrices (2, 3, 4 or TERNARY): one width for all, a dict
     role -> width (roles as cq_roles names them, others 4), or a list in
     record order. A fused projection's parts (q, k, v, gate; key, value)
-    must share the code width (ternary packs at 2)."""
+    must share the code width (ternary packs at 2). ``heads`` lists probe
+    head codes to append (HEAD_EMBEDDING, HEAD_CONFIDENCE, HEAD_ROUTER)."""
     g = dict(NEEDLE3_DEFAULTS)
     g.update(shape)
     gm = sum(1 << l for l in g["global_layers"])
@@ -133,7 +137,7 @@ def synth_cact(seed=0, std=0.02, bits=None, **shape) -> bytes:
     plan = np.ascontiguousarray(plan, np.int32)
     n = C.c_uint64(0)
     args = (g["num_layers"], g["vocab"], g["engram_slots"], g["sliding_window"], gm, es, seed, std,
-            _p(plan) if len(plan) else None, len(plan))
+            _p(plan) if len(plan) else None, len(plan), sum(1 << c for c in set(heads)))
     if lib().nd_synth_cact(*args, None, 0, C.byref(n)) != 0:
         raise _err()
     buf = np.zeros(n.value, np.uint8)

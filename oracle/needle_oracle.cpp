@@ -94,6 +94,14 @@ static inline float rmin(float a, float b) { return std::fmin(a, b); }
 // Rust f32::round: half away from zero.
 static inline float rround(float x) { return std::round(x); }
 
+// f32::max as the reference's platform computes it (aarch64 FMAXNM: -0 < +0).
+static inline float fmaxnm(float a, float b) {
+    if (a > b) return a;
+    if (b > a) return b;
+    return std::signbit(a) ? b : a;
+}
+
+
 // crates/needle-engine/src/infer.rs:353-366
 float nexp(float x) {
     x = rmin(rmax(x, bitsf(0xc2b0c0a5u)), bitsf(0x42b0c0a5u));
@@ -620,7 +628,15 @@ struct Model {
     std::vector<int64_t> perm1, perm2;
     std::vector<float> final_norm;
     std::vector<float> freq, sd, cd;  // infer.rs:938-962
+    // weights.rs:60-76, 422-469: the probe heads the archive carries
+    // (index 0 embedding, 1 confidence, 2 router).
+    struct ProbeHead {
+        bool present = false;
+        int k = 0, q = 0, out = 0;
+        std::vector<float> probes, gain, query, row_bias, proj, bias;
+    } heads[3];
 };
+
 
 static std::vector<float> f16_tensor(const Archive& a, size_t i) {
     const Record& r = a.recs[i];
@@ -639,6 +655,19 @@ static std::vector<float> f16_tensor(const Archive& a, size_t i) {
         return v;
     }
     throw std::runtime_error("expected an f16/f32 tensor");
+}
+
+// cact.rs:620-630 (Archive::tensor): any tensor as f32 values, CQ ones
+// dequantized row by row (quant.rs:259-283 = QMat::row), with its shape.
+static std::vector<float> dense_tensor(const Archive& a, size_t i, std::vector<int64_t>* shape) {
+    const Record& r = a.recs[i];
+    if (shape) *shape = r.shape;
+    if (r.dtype != CQ) return f16_tensor(a, i);
+    QMat q;
+    qmat_from_cq(a, i, q);
+    std::vector<float> out((size_t)q.out * q.in_dim);
+    for (int row = 0; row < q.out; row++) qmat_row(q, row, out.data() + (size_t)row * q.in_dim);
+    return out;
 }
 
 // crates/needle-core/src/cact.rs:173-202 (Header::to_config) and
@@ -736,6 +765,34 @@ static void load_model(Model& m) {
         m.engrams[s].taps = f16_tensor(a, i++);
     }
     m.final_norm = f16_tensor(a, i++);
+    // weights.rs:422-469: probe heads between final_norm and the tokenizer.
+    size_t tok_index = a.recs.size();
+    for (size_t r = 0; r < a.recs.size(); r++)
+        if (a.recs[r].dtype == RAW) { tok_index = r; break; }
+    if (i < tok_index) {
+        std::vector<float> manifest = f16_tensor(a, i++);
+        const int l1 = c.L + 1;
+        for (float code : manifest) {
+            Model::ProbeHead h;
+            std::vector<int64_t> gshape, qshape, pshape;
+            h.probes = dense_tensor(a, i++, nullptr);
+            h.gain = dense_tensor(a, i++, &gshape);
+            h.query = dense_tensor(a, i++, &qshape);
+            h.row_bias = dense_tensor(a, i++, nullptr);
+            h.proj = dense_tensor(a, i++, &pshape);
+            h.bias = dense_tensor(a, i++, nullptr);
+            if (gshape.size() < 2 || qshape.empty() || pshape.empty()) throw std::runtime_error("probe head shapes");
+            h.k = (int)gshape[1];
+            h.q = (int)qshape[0];
+            h.out = (int)pshape[0];
+            if (h.probes.size() != (size_t)l1 * h.k * c.d) throw std::runtime_error("probe head rows do not match the depth");
+            h.present = true;
+            const int ci = (int)std::lround(code);
+            if (ci == 3) i++;  // the router's calibration
+            if (ci < 1 || ci > 3) throw std::runtime_error("unknown probe head code");
+            m.heads[ci - 1] = h;
+        }
+    }
     if ((int)m.perm1.size() != c.hada_n || (int)m.perm2.size() != c.hada_n)
         throw std::runtime_error("Hadamard permutations do not match hada_n");
     m.site_of_layer.assign(c.L, -1);
@@ -773,6 +830,10 @@ struct Session {
     std::vector<int64_t> slot_pos;
     bool has_attend = false;
     int64_t sink = 0, ring = 0;
+    // infer.rs:1195-1211: with want_cells, the lane mean of the residual
+    // stream of every fed position at every depth, [pos][L + 1][d].
+    bool want_cells = false;
+    std::vector<float> cells;
 };
 
 static Session* session_new(const Model& m) {
@@ -1391,13 +1452,24 @@ static int chunk_native(const Model& m, Session& s, const uint32_t* toks, int t,
             for (int k = 0; k < d; k++) xs[(size_t)i * nc + lane * d + k] = row[k] * scale;
     }
     g_trace.put("embed", xs.data(), xs.size());
+    const int l1 = c.L + 1;
+    auto record = [&](int depth) {
+        if (!s.want_cells) return;
+        s.cells.resize((size_t)(p0 + t) * l1 * d);
+        for (int i = 0; i < t; i++)
+            lane_mean(xs.data() + (size_t)i * nc, d, s.cells.data() + ((size_t)(p0 + i) * l1 + depth) * d);
+    };
+    record(0);
     std::vector<std::vector<float>> ekeys, evals;
     engram_native(m, s, p0, t, ekeys, evals);
     std::vector<float> cos, sin;
     rope_rows(m, s, p0, t, cos, sin);
     g_trace.put("cos", cos.data(), cos.size());
     g_trace.put("sin", sin.data(), sin.size());
-    for (int l = 0; l < c.L; l++) layer_native(m, l, s, p0, xs, t, cos, sin, ekeys, evals);
+    for (int l = 0; l < c.L; l++) {
+        layer_native(m, l, s, p0, xs, t, cos, sin, ekeys, evals);
+        record(l + 1);
+    }
     std::vector<int> rows;
     if (outputs == OUT_LAST_LOGITS || outputs == OUT_LAST_HIDDEN) rows.push_back(t - 1);
     else if (outputs == OUT_ALL_LOGITS || outputs == OUT_HIDDEN)
@@ -1432,6 +1504,133 @@ static int forward_native(const Model& m, Session& s, const uint32_t* ids, int n
         rows += chunk_native(m, s, ids + c0, len, want, out ? out + rows * per : nullptr);
     }
     return rows;
+}
+
+// ------------------------------------------------------- probe heads
+
+// linalg.rs:242-257: eight accumulators over whole groups of eight (x*y
+// then +, unfused), summed (a0 + a4) + (a1 + a5) + (a2 + a6) + (a3 + a7),
+// then the remainder in order.
+float dot8(const float* a, const float* b, int n) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const int chunks = n / 8;
+    for (int c = 0; c < chunks; c++)
+        for (int i = 0; i < 8; i++) acc[i] = acc[i] + a[c * 8 + i] * b[c * 8 + i];
+    float s = (((acc[0] + acc[4]) + (acc[1] + acc[5])) + (acc[2] + acc[6])) + (acc[3] + acc[7]);
+    for (int i = chunks * 8; i < n; i++) s = s + a[i] * b[i];
+    return s;
+}
+
+// linalg.rs:262-277 (the reference's own constants; round half away).
+float fast_exp(float x) {
+    x = std::min(std::max(x, -87.33654f), 88.72283f);
+    const float k = std::round(x * 1.44269504088896340736f);
+    const float r = (x - k * 0.6933594f) - k * -2.1219444e-4f;
+    float p = 1.9875691e-4f;
+    p = p * r + 1.3981999e-3f;
+    p = p * r + 8.333452e-3f;
+    p = p * r + 4.1665796e-2f;
+    p = p * r + 1.6666665e-1f;
+    p = p * r + 5e-1f;
+    const float y = ((p * r) * r + r) + 1.0f;
+    return y * bitsf((uint32_t)((int32_t)k + 127) << 23);
+}
+
+// linalg.rs:309-323
+static void softmax_inplace(float* x, int n) {
+    float m = -INFINITY;
+    for (int i = 0; i < n; i++) m = fmaxnm(m, x[i]);
+    if (m == -INFINITY) {
+        for (int i = 0; i < n; i++) x[i] = 0.f;
+        return;
+    }
+    for (int i = 0; i < n; i++) x[i] = x[i] == -INFINITY ? 0.f : fast_exp(x[i] - m);
+    float s = 0.f;
+    for (int i = 0; i < n; i++) s = s + x[i];
+    const float inv = 1.0f / s;
+    for (int i = 0; i < n; i++) x[i] = x[i] * inv;
+}
+
+// linalg.rs:291-297
+static void rms_unit(const float* x, int n, float* out) {
+    float ss = 0.f;
+    for (int i = 0; i < n; i++) ss = ss + x[i] * x[i];
+    const float ms = ss / (float)n;
+    const float r = 1.0f / std::sqrt(ms + 1e-6f);
+    for (int i = 0; i < n; i++) out[i] = x[i] * r;
+}
+
+// heads.rs:12-56 (probe_pool) over cells [t][l1][d]: the pooled [q * d].
+void probe_pool(const float* cells, int t, int l1, int d, int k, int q, const float* probes, const float* gain,
+                const float* query, const float* row_bias, float* out) {
+    const float inv = 1.0f / (float)std::sqrt((double)d);
+    const int m = l1 * k;
+    std::vector<float> r((size_t)m * d), scores(t), acc(d);
+    for (int lk = 0; lk < m; lk++) {
+        const int l = lk / k;
+        const float* probe = probes + (size_t)lk * d;
+        for (int ti = 0; ti < t; ti++) scores[ti] = dot8(cells + ((size_t)ti * l1 + l) * d, probe, d) * inv;
+        softmax_inplace(scores.data(), t);
+        for (int c = 0; c < d; c++) acc[c] = 0.f;
+        for (int ti = 0; ti < t; ti++) {
+            const float* cr = cells + ((size_t)ti * l1 + l) * d;
+            for (int c = 0; c < d; c++) acc[c] = acc[c] + scores[ti] * cr[c];
+        }
+        float* dst = r.data() + (size_t)lk * d;
+        rms_unit(acc.data(), d, dst);
+        for (int c = 0; c < d; c++) dst[c] = dst[c] * gain[lk];
+    }
+    std::vector<float> u(m);
+    for (int qi = 0; qi < q; qi++) {
+        for (int j = 0; j < m; j++) u[j] = dot8(r.data() + (size_t)j * d, query + (size_t)qi * d, d) * inv + row_bias[(size_t)qi * m + j];
+        softmax_inplace(u.data(), m);
+        float* dst = out + (size_t)qi * d;
+        for (int c = 0; c < d; c++) dst[c] = 0.f;
+        for (int j = 0; j < m; j++)
+            for (int c = 0; c < d; c++) dst[c] = dst[c] + u[j] * r[(size_t)j * d + c];
+    }
+}
+
+// heads.rs:58-61
+static void project(const Model::ProbeHead& h, const float* pooled, float* out) {
+    const int n = h.q * 768;
+    for (int o = 0; o < h.out; o++) out[o] = dot8(h.proj.data() + (size_t)o * n, pooled, n) + h.bias[o];
+}
+
+static void pool_head(const Model& m, const Model::ProbeHead& h, const float* cells, int t, std::vector<float>& pooled) {
+    pooled.assign((size_t)h.q * m.c.d, 0.f);
+    probe_pool(cells, t, m.c.L + 1, m.c.d, h.k, h.q, h.probes.data(), h.gain.data(), h.query.data(), h.row_bias.data(),
+               pooled.data());
+}
+
+// heads.rs:77-90: the retrieval embedding (embedding head, else the
+// confidence head's pool), unit norm. Empty without a head.
+static std::vector<float> embedding_of(const Model& m, const float* cells, int t) {
+    std::vector<float> v, pooled;
+    if (m.heads[0].present) {
+        pool_head(m, m.heads[0], cells, t, pooled);
+        v.resize(m.heads[0].out);
+        project(m.heads[0], pooled.data(), v.data());
+    } else if (m.heads[1].present) {
+        pool_head(m, m.heads[1], cells, t, v);
+    } else {
+        return v;
+    }
+    float ss = 0.f;
+    for (float x : v) ss = ss + x * x;
+    const float norm = std::sqrt(ss + 1e-12f);
+    for (float& x : v) x = x / norm;
+    return v;
+}
+
+// heads.rs:68-74
+static bool confidence_of(const Model& m, const float* cells, int t, float* logit) {
+    if (!m.heads[1].present) return false;
+    std::vector<float> pooled, out(m.heads[1].out);
+    pool_head(m, m.heads[1], cells, t, pooled);
+    project(m.heads[1], pooled.data(), out.data());
+    *logit = out[0];
+    return true;
 }
 
 // crates/needle-engine/src/agent.rs:1114-1127: banned ids read -1e30, then the
@@ -1473,13 +1672,6 @@ float engine_expf(float x) {
 // then four f32 lanes of engine_expf(v - m) over whole groups of four (lane
 // j takes elements 4i + j in order), summed (l0 + l1) + (l2 + l3) and
 // widened, then the remainder in f64 skipping masked logits.
-// f32::max as the reference's platform computes it (aarch64 FMAXNM: -0 < +0).
-static inline float fmaxnm(float a, float b) {
-    if (a > b) return a;
-    if (b > a) return b;
-    return std::signbit(a) ? b : a;
-}
-
 void softmax_stats(const float* x, int n, float* m_out, double* z_out) {
     float m = -INFINITY;
     for (int i = 0; i < n; i++) m = fmaxnm(m, x[i]);
@@ -1663,6 +1855,64 @@ int orc_last_hidden(void* s, float* out) {
 }
 uint32_t orc_masked_argmax(const float* x, int n, const uint8_t* allow_bits) { return masked_argmax(x, n, allow_bits); }
 float orc_engine_expf(float x) { return engine_expf(x); }
+float orc_fast_exp(float x) { return fast_exp(x); }
+float orc_dot8(const float* a, const float* b, int n) { return dot8(a, b, n); }
+void orc_probe_pool(const float* cells, int t, int l1, int d, int k, int q, const float* probes, const float* gain,
+                    const float* query, const float* row_bias, float* out) {
+    probe_pool(cells, t, l1, d, k, q, probes, gain, query, row_bias, out);
+}
+int orc_head_present(void* mp, int code) {
+    Model& m = *(Model*)mp;
+    return code >= 1 && code <= 3 && m.heads[code - 1].present ? 1 : 0;
+}
+// heads.rs:63-66 + 77-90 (needle_embed's computation over token ids): a
+// fresh session fed `ids` in chunks of 32 with cells, then the embedding.
+// Returns its width (out == NULL: only the width), -1 without a head.
+int orc_embed(void* mp, const uint32_t* ids, int n, float* out) {
+    try {
+        Model& m = *(Model*)mp;
+        if (!m.heads[0].present && !m.heads[1].present) throw std::runtime_error("this archive carries no probe head");
+        const int dim = m.heads[0].present ? m.heads[0].out : m.heads[1].q * m.c.d;
+        if (!out) return dim;
+        std::unique_ptr<Session> s(session_new(m));
+        s->want_cells = true;
+        forward_native(m, *s, ids, n, OUT_NONE, nullptr);
+        std::vector<float> v = embedding_of(m, s->cells.data(), n);
+        std::memcpy(out, v.data(), sizeof(float) * v.size());
+        return dim;
+    } catch (std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+// heads.rs:68-74: the confidence head's logit for `ids`.
+int orc_confidence(void* mp, const uint32_t* ids, int n, float* out) {
+    try {
+        Model& m = *(Model*)mp;
+        std::unique_ptr<Session> s(session_new(m));
+        s->want_cells = true;
+        forward_native(m, *s, ids, n, OUT_NONE, nullptr);
+        if (!confidence_of(m, s->cells.data(), n, out)) throw std::runtime_error("this archive carries no confidence head");
+        return 0;
+    } catch (std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+// The cells [n][L + 1][d] of a fresh session fed `ids`.
+int orc_cells(void* mp, const uint32_t* ids, int n, float* out) {
+    try {
+        Model& m = *(Model*)mp;
+        std::unique_ptr<Session> s(session_new(m));
+        s->want_cells = true;
+        forward_native(m, *s, ids, n, OUT_NONE, nullptr);
+        std::memcpy(out, s->cells.data(), sizeof(float) * s->cells.size());
+        return 0;
+    } catch (std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+}
 void orc_softmax_stats(const float* x, int n, float* m, double* z) { softmax_stats(x, n, m, z); }
 int orc_candidate_order(const float* x, int n, int k, int32_t* out) { return candidate_order(x, n, k, out); }
 

@@ -54,6 +54,13 @@ def lib():
             "orc_last_hidden": (I, [P, P]),
             "orc_masked_argmax": (U32, [P, I, P]),
             "orc_engine_expf": (C.c_float, [C.c_float]),
+            "orc_fast_exp": (C.c_float, [C.c_float]),
+            "orc_dot8": (C.c_float, [P, P, I]),
+            "orc_probe_pool": (None, [P, I, I, I, I, I, P, P, P, P, P]),
+            "orc_head_present": (I, [P, I]),
+            "orc_embed": (I, [P, P, I, P]),
+            "orc_confidence": (I, [P, P, I, P]),
+            "orc_cells": (I, [P, P, I, P]),
             "orc_softmax_stats": (None, [P, I, P, P]),
             "orc_candidate_order": (I, [P, I, I, P]),
             "orc_trace": (None, [I]),
@@ -202,6 +209,31 @@ def engine_expf(x: float) -> float:
     return lib().orc_engine_expf(float(x))
 
 
+def fast_exp(x: float) -> float:
+    """linalg.rs:262-277."""
+    return lib().orc_fast_exp(float(x))
+
+
+def dot8(a, b):
+    """linalg.rs:242-257."""
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    return np.float32(lib().orc_dot8(_p(a), _p(b), len(a)))
+
+
+def probe_pool(cells, probes, gain, query, row_bias):
+    """heads.rs:12-56 over cells [t, l1, d]; probes [l1, k, d], gain [l1,
+    k], query [q, d], row_bias [q, l1 * k]: the pooled [q * d]."""
+    cells = np.ascontiguousarray(cells, np.float32)
+    t, l1, d = cells.shape
+    k = gain.shape[1]
+    q = query.shape[0]
+    out = np.zeros(q * d, np.float32)
+    args = [np.ascontiguousarray(a, np.float32) for a in (probes, gain, query, row_bias)]
+    lib().orc_probe_pool(_p(cells), t, l1, d, k, q, *[_p(a) for a in args], _p(out))
+    return out
+
+
 def softmax_stats(x):
     """agent.rs:1241-1252: (max, sum exp(l - max)) as the call sampler has them."""
     x = np.ascontiguousarray(x, np.float32)
@@ -248,6 +280,36 @@ class Model:
 
     def session(self):
         return Session(self)
+
+    def has_head(self, code):
+        return lib().orc_head_present(self._h, code) == 1
+
+    def embed(self, ids):
+        """heads.rs:77-90 over a fresh session fed ids (needle_embed's
+        computation after tokenizing)."""
+        ids = np.ascontiguousarray(ids, np.uint32)
+        dim = lib().orc_embed(self._h, _p(ids), len(ids), None)
+        if dim < 0:
+            raise RuntimeError(lib().orc_last_error().decode())
+        out = np.zeros(dim, np.float32)
+        lib().orc_embed(self._h, _p(ids), len(ids), _p(out))
+        return out
+
+    def confidence(self, ids):
+        """heads.rs:68-74."""
+        ids = np.ascontiguousarray(ids, np.uint32)
+        out = np.zeros(1, np.float32)
+        if lib().orc_confidence(self._h, _p(ids), len(ids), _p(out)) != 0:
+            raise RuntimeError(lib().orc_last_error().decode())
+        return out[0]
+
+    def cells(self, ids):
+        """infer.rs:1195-1211: [t, L + 1, d] lane means of a fresh session."""
+        ids = np.ascontiguousarray(ids, np.uint32)
+        out = np.zeros((len(ids), self.num_layers + 1, self.d_model), np.float32)
+        if lib().orc_cells(self._h, _p(ids), len(ids), _p(out)) != 0:
+            raise RuntimeError(lib().orc_last_error().decode())
+        return out
 
     def head_logits(self, h):
         h = np.ascontiguousarray(h, np.float32)

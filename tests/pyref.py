@@ -310,3 +310,86 @@ def candidate_order(x, k):
     order = [i for i in range(len(x)) if x[i] > f32(-1e30)]
     order.sort(key=lambda i: (-float(x[i]), i))
     return order[:k], len(order)
+
+
+def fast_exp(x):
+    """linalg.rs:262-277 (round half away, unfused)."""
+    x = f32(min(max(f32(x), f32(-87.33654)), f32(88.72283)))
+    t = f32(x * f32(1.4426950408889634))
+    k = f32(np.floor(abs(t) + 0.5) * np.sign(t))
+    r = f32(f32(x - f32(k * f32(0.6933594))) - f32(k * f32(-2.1219444e-4)))
+    p = f32(1.9875691e-4)
+    for c in (1.3981999e-3, 8.333452e-3, 4.1665796e-2, 1.6666665e-1, 5e-1):
+        p = f32(f32(p * r) + f32(c))
+    y = f32(f32(f32(f32(p * r) * r) + r) + f32(1.0))
+    two = np.array([((int(k) + 127) << 23) & 0xFFFFFFFF], np.uint32).view(np.float32)[0]
+    return f32(y * two)
+
+
+def dot8(a, b):
+    """linalg.rs:242-257."""
+    a = np.asarray(a, np.float32)
+    b = np.asarray(b, np.float32)
+    acc = [f32(0)] * 8
+    ch = len(a) // 8
+    for c in range(ch):
+        for i in range(8):
+            acc[i] = f32(acc[i] + f32(a[c * 8 + i] * b[c * 8 + i]))
+    s = f32(f32(f32(f32(acc[0] + acc[4]) + f32(acc[1] + acc[5])) + f32(acc[2] + acc[6])) + f32(acc[3] + acc[7]))
+    for i in range(ch * 8, len(a)):
+        s = f32(s + f32(a[i] * b[i]))
+    return s
+
+
+def softmax_inplace(x):
+    """linalg.rs:309-323 (max as aarch64 FMAXNM)."""
+    m = f32(-np.inf)
+    for v in x:
+        m = v if (v > m or (v == m and not np.signbit(v))) else m
+    if m == -np.inf:
+        return [f32(0)] * len(x)
+    e = [f32(0) if v == -np.inf else fast_exp(f32(v - m)) for v in x]
+    s = f32(0)
+    for v in e:
+        s = f32(s + v)
+    inv = f32(f32(1.0) / s)
+    return [f32(v * inv) for v in e]
+
+
+def rms_unit(x):
+    """linalg.rs:291-297."""
+    ss = f32(0)
+    for v in x:
+        ss = f32(ss + f32(v * v))
+    ms = f32(ss / f32(len(x)))
+    r = f32(f32(1.0) / np.sqrt(f32(ms + f32(1e-6))))
+    return [f32(v * r) for v in x]
+
+
+def probe_pool(cells, probes, gain, query, row_bias):
+    """heads.rs:12-56."""
+    cells = np.asarray(cells, np.float32)
+    t, l1, d = cells.shape
+    k, q = gain.shape[1], query.shape[0]
+    inv = f32(f32(1.0) / f32(np.sqrt(np.float64(d))))
+    m = l1 * k
+    r = []
+    for lk in range(m):
+        l = lk // k
+        probe = probes.reshape(m, d)[lk]
+        scores = softmax_inplace([f32(dot8(cells[ti, l], probe) * inv) for ti in range(t)])
+        acc = [f32(0)] * d
+        for ti in range(t):
+            for c in range(d):
+                acc[c] = f32(acc[c] + f32(scores[ti] * cells[ti, l, c]))
+        g = gain.reshape(-1)[lk]
+        r.append([f32(v * g) for v in rms_unit(acc)])
+    out = []
+    for qi in range(q):
+        u = softmax_inplace([f32(f32(dot8(r[j], query[qi]) * inv) + row_bias.reshape(q, m)[qi, j]) for j in range(m)])
+        dst = [f32(0)] * d
+        for j in range(m):
+            for c in range(d):
+                dst[c] = f32(dst[c] + f32(u[j] * r[j][c]))
+        out += dst
+    return np.array(out, np.float32)
