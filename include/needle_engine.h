@@ -101,6 +101,22 @@ int nd_head_logits_sparse(nd_batch* b, const float* h, const int* ids, int n, fl
 int nd_batch_candidates(nd_batch* b, const float* logits, const unsigned char* allow, const unsigned char* allow_order,
                         int k, int* ids, float* m, double* z, int* live, int flags);
 
+/* needle_embed's computation after tokenizing (crates/needle-engine/src/
+ * heads.rs:63-90, agent.rs:259-263) for every sequence of a fresh batch
+ * (nothing fed yet): ids[S][T] are fed in chunks of 32 recording the lane
+ * mean of the residual stream at every position and depth (the cells,
+ * infer.rs:1195-1211), then the probe pool of the embedding head,
+ * projected and scaled to unit norm (without an embedding head, the
+ * confidence head's pool at unit norm). out[S][dim]; with out == NULL only
+ * *dim is set. Fails without a probe head ("this archive carries no probe
+ * head"). The batch keeps the T fed positions. Host or device pointers
+ * (ND_DEVICE). */
+int nd_batch_embed(nd_batch* b, const int* ids, int T, float* out, int* dim, int flags);
+
+/* heads.rs:68-74 (confidence_logit) the same way: out[S] = the confidence
+ * head's logit for each sequence of a fresh batch. */
+int nd_batch_confidence(nd_batch* b, const int* ids, int T, float* out, int flags);
+
 /* The CUDA stream a batch's work runs on (a cudaStream_t); no counterpart
  * in the reference, which runs on the CPU. */
 void* nd_batch_stream(nd_batch* b);

@@ -53,6 +53,8 @@ struct Model {
     std::vector<Linear> qkvg, out;  // per layer
     std::vector<DevMat> etables;
     std::vector<Linear> ekv;
+    HeadW heads[3];  // weights.rs:60-76: embedding, confidence, router
+    bool has_head[3] = {false, false, false};
     std::vector<const float*> etaps;
     std::vector<int> site_of_layer;
     const int32_t *perm1 = nullptr, *perm2 = nullptr;
@@ -343,6 +345,54 @@ static Model* load_model(const uint8_t* bytes, size_t n, int device) {
         m.etaps.push_back(m.upload(taps.data(), taps.size()));
     }
     m.final_norm = m.upload(small_f32(a, cur, d).data(), d);
+    // weights.rs:422-469: probe heads between final_norm and the tokenizer
+    size_t tok_index = a.recs.size();
+    for (size_t r = 0; r < a.recs.size(); r++)
+        if (a.recs[r].dtype == CACT_RAW) { tok_index = r; break; }
+    if (cur.i < tok_index) {
+        const int l1 = c.L + 1;
+        // any tensor as f32 (cact.rs:620-630): CQ matrices dequantized by row
+        auto dense = [&](int in_dim, int* rows) -> std::vector<float> {
+            const CactRecord& r = a.recs.at(cur.i);
+            if (r.dtype != CACT_CQ) {
+                std::vector<float> v = small_f32(a, cur, 0);
+                if (rows) *rows = r.shape.empty() ? 1 : (int)r.shape[0];
+                return v;
+            }
+            HostMat hm = host_mat(a, cur, in_dim);
+            std::vector<float> v((size_t)hm.out * in_dim);
+            for (int row = 0; row < hm.out; row++)
+                cq_row(hm.codes.data(), hm.norms.data(), hm.groups, in_dim, hm.bits, row, v.data() + (size_t)row * in_dim);
+            if (rows) *rows = hm.out;
+            return v;
+        };
+        std::vector<float> manifest = small_f32(a, cur, 1);
+        for (float code : manifest) {
+            const int ci = (int)std::lround(code);
+            if (ci < 1 || ci > 3) throw std::runtime_error("unknown probe head code " + std::to_string(ci));
+            HeadW h;
+            int prow = 0, qrow = 0, orow = 0;
+            std::vector<float> probes = dense(d, &prow), gain = dense(0, nullptr), query = dense(d, &qrow);
+            std::vector<float> row_bias = dense(0, nullptr);
+            h.q = qrow;
+            h.k = (int)(gain.size() / l1);
+            std::vector<float> proj = dense(h.q * d, &orow), bias = dense(0, nullptr);
+            h.out = orow;
+            if (ci == 3) small_f32(a, cur, 3);  // the router's calibration
+            if (h.k < 1 || probes.size() != (size_t)l1 * h.k * d || gain.size() != (size_t)l1 * h.k ||
+                query.size() != (size_t)h.q * d || row_bias.size() != (size_t)h.q * l1 * h.k ||
+                proj.size() != (size_t)h.out * h.q * d || bias.size() != (size_t)h.out)
+                throw std::runtime_error("probe head rows do not match the depth");
+            h.probes = m.upload(probes.data(), probes.size());
+            h.gain = m.upload(gain.data(), gain.size());
+            h.query = m.upload(query.data(), query.size());
+            h.row_bias = m.upload(row_bias.data(), row_bias.size());
+            h.proj = m.upload(proj.data(), proj.size());
+            h.bias = m.upload(bias.data(), bias.size());
+            m.heads[ci - 1] = h;
+            m.has_head[ci - 1] = true;
+        }
+    }
     m.site_of_layer.assign(c.L, -1);
     for (size_t s = 0; s < c.sites.size(); s++) {
         if (c.sites[s] < 0 || c.sites[s] >= c.L) throw std::runtime_error("engram site outside the stack");
@@ -419,6 +469,10 @@ struct Batch {
     int32_t* d_len;  // device copy of len (Caches::len)
     uint8_t* masks;
     // the call sampler's buffers (nd_batch_candidates), made on first use
+    // the probe heads' inputs and scratch (nd_batch_embed), made on use
+    float *cells = nullptr, *head_r = nullptr, *head_pool = nullptr, *head_out = nullptr;
+    int cells_cap = 0;       // positions per sequence the cells buffer holds
+    bool recording = false;  // chunk() records cells while set
     float* clogits = nullptr;
     uint8_t *cmask1 = nullptr, *cmask2 = nullptr;
     int32_t *cids = nullptr, *clive = nullptr;
@@ -588,6 +642,7 @@ static int chunk(Batch& b, const int32_t* ids, int T, int outputs) {
         }
     }
     launch_embed(m.embedding, ids, M, b.xs, st);
+    if (b.recording) launch_record_cells(b.xs, S, T, p0, 0, c.L + 1, b.cells_cap, b.cells, st);
     for (int l = 0; l < c.L; l++) {
         const LayerW& w = m.layers[l];
         const int lane = l % 4, site = m.site_of_layer[l];
@@ -625,6 +680,7 @@ static int chunk(Batch& b, const int32_t* ids, int T, int outputs) {
         tick(b, ND_SITE_POST);
         launch_post_block(w, b.o, b.x1, b.u, b.p, m.perm1, m.perm2, M, b.xs, st);
         tick(b, ND_SITE_POST);
+        if (b.recording) launch_record_cells(b.xs, S, T, p0, l + 1, c.L + 1, b.cells_cap, b.cells, st);
         if (l == b.debug_layer) snap(b, "snap.xs", b.xs, (size_t)M * 3072);
     }
     // every site has joined the layer chain before the position advances
@@ -979,6 +1035,98 @@ int nd_batch_candidates(nd_batch* bh, const float* logits, const unsigned char* 
             CK(cudaMemcpyAsync(z, b.cz, (size_t)b.S * sizeof(double), cudaMemcpyDeviceToHost, b.st));
             CK(cudaStreamSynchronize(b.st));
         }
+        return 0;
+    } catch (std::exception& e) {
+        return fail(e);
+    }
+}
+
+// heads.rs:63-66 for every sequence of a fresh batch: ids [S][T] fed in
+// chunks of 32 with the cells of every position and depth recorded, then
+// head h's pool (kind as launch_probe_head) into b.head_out [S][width].
+static void probe_run(Batch& b, const int* ids, int T, int flags, const HeadW& h, int kind, int width) {
+    const Config& c = b.m->c;
+    if (b.len != 0) throw std::runtime_error("the probe heads read a fresh batch (no position fed yet)");
+    if (T < 1 || T > b.cap) throw std::runtime_error("token count outside [1, max_len]");
+    const int l1 = c.L + 1;
+    if (b.cells_cap < T) {
+        b.cells = b.alloc<float>((size_t)b.S * T * l1 * c.d);
+        b.cells_cap = T;
+    }
+    if (!b.head_r) {
+        // every head here has k <= 16 probes a depth and q <= 16 queries
+        b.head_r = b.alloc<float>((size_t)b.S * l1 * 16 * c.d);
+        b.head_pool = b.alloc<float>((size_t)b.S * 16 * c.d);
+        b.head_out = b.alloc<float>((size_t)b.S * 16 * c.d);
+    }
+    if (h.k > 16 || h.q > 16 || width > 16 * c.d) throw std::runtime_error("probe head larger than this engine serves");
+    const bool dev = flags & ND_DEVICE;
+    const int32_t* dids = (const int32_t*)ids;
+    int32_t* staging = nullptr;
+    if (!dev) {
+        CK(cudaMallocAsync((void**)&staging, (size_t)b.S * T * sizeof(int32_t), b.st));
+        CK(cudaMemcpyAsync(staging, ids, (size_t)b.S * T * sizeof(int32_t), cudaMemcpyHostToDevice, b.st));
+        dids = staging;
+    }
+    b.recording = true;
+    try {
+        forward(b, dids, T, ND_OUT_NONE);
+    } catch (...) {
+        b.recording = false;
+        throw;
+    }
+    b.recording = false;
+    if (staging) CK(cudaFreeAsync(staging, b.st));
+    launch_probe_head(h, b.cells, b.S, T, b.cells_cap, l1, kind, b.head_r, b.head_pool, b.head_out, b.st);
+    CK(cudaGetLastError());
+}
+
+int nd_batch_embed(nd_batch* bh, const int* ids, int T, float* out, int* dim, int flags) {
+    try {
+        if (!bh) throw std::runtime_error("nd_batch_embed: null argument");
+        Batch& b = *bh->b;
+        Model& m = *b.m;
+        CK(cudaSetDevice(m.device));
+        // heads.rs:80-84: the embedding head, else the confidence head's pool
+        int kind, width;
+        const HeadW* h;
+        if (m.has_head[0]) {
+            h = &m.heads[0];
+            kind = 0;
+            width = h->out;
+        } else if (m.has_head[1]) {
+            h = &m.heads[1];
+            kind = 1;
+            width = h->q * m.c.d;
+        } else {
+            throw std::runtime_error("this archive carries no probe head");
+        }
+        if (dim) *dim = width;
+        if (!out) return 0;
+        if (!ids) throw std::runtime_error("nd_batch_embed: null ids");
+        probe_run(b, ids, T, flags, *h, kind, width);
+        const bool dev = flags & ND_DEVICE;
+        CK(cudaMemcpyAsync(out, b.head_out, (size_t)b.S * width * sizeof(float),
+                           dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, b.st));
+        if (!dev) CK(cudaStreamSynchronize(b.st));
+        return 0;
+    } catch (std::exception& e) {
+        return fail(e);
+    }
+}
+
+int nd_batch_confidence(nd_batch* bh, const int* ids, int T, float* out, int flags) {
+    try {
+        if (!bh || !ids || !out) throw std::runtime_error("nd_batch_confidence: null argument");
+        Batch& b = *bh->b;
+        Model& m = *b.m;
+        CK(cudaSetDevice(m.device));
+        if (!m.has_head[1]) throw std::runtime_error("this archive carries no confidence head");
+        probe_run(b, ids, T, flags, m.heads[1], 2, 1);
+        const bool dev = flags & ND_DEVICE;
+        CK(cudaMemcpyAsync(out, b.head_out, (size_t)b.S * sizeof(float), dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
+                           b.st));
+        if (!dev) CK(cudaStreamSynchronize(b.st));
         return 0;
     } catch (std::exception& e) {
         return fail(e);

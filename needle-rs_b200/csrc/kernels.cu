@@ -2156,6 +2156,208 @@ cudaError_t launch_candidates(const float* logits, int S, int V, const uint8_t* 
     return cudaSuccess;
 }
 
+// ------------------------------------------------------------ probe heads
+
+// infer.rs:1195-1211, 1707-1711: the lane mean (((x0 + x1) + x2) + x3) *
+// 0.25 of each channel of row m = (s, i), at depth `depth` of position
+// p0 + i. 192 threads, four channels each.
+__global__ void record_cells_kernel(const float* xs, int T, int p0, int depth, int l1, int ncap, float* cells) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int m = blockIdx.x, c4 = threadIdx.x;
+    const int s = m / T, i = m % T;
+    const float* x = xs + (size_t)m * 3072 + 4 * c4;
+    const float4 a = *(const float4*)x, b = *(const float4*)(x + 768), c = *(const float4*)(x + 1536),
+                 d = *(const float4*)(x + 2304);
+    float4 o;
+    o.x = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(a.x, b.x), c.x), d.x), 0.25f);
+    o.y = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(a.y, b.y), c.y), d.y), 0.25f);
+    o.z = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(a.z, b.z), c.z), d.z), 0.25f);
+    o.w = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(a.w, b.w), c.w), d.w), 0.25f);
+    *(float4*)(cells + (((size_t)s * ncap + p0 + i) * l1 + depth) * 768 + 4 * c4) = o;
+}
+
+void launch_record_cells(const float* xs, int S, int T, int p0, int depth, int l1, int ncap, float* cells, cudaStream_t st) {
+    COUNT_LAUNCH();
+    launch_pdl(record_cells_kernel, dim3(S * T), dim3(192), 0, st, xs, T, p0, depth, l1, ncap, cells);
+}
+
+// linalg.rs:262-277: the reference's own f32 exp (round half away, unfused).
+__device__ __forceinline__ float fast_exp(float x) {
+    x = fminf(fmaxf(x, -87.33654f), 88.72283f);
+    const float k = roundf(__fmul_rn(x, 1.44269504088896340736f));
+    const float r = __fsub_rn(__fsub_rn(x, __fmul_rn(k, 0.6933594f)), __fmul_rn(k, -2.1219444e-4f));
+    float p = 1.9875691e-4f;
+    p = __fadd_rn(__fmul_rn(p, r), 1.3981999e-3f);
+    p = __fadd_rn(__fmul_rn(p, r), 8.333452e-3f);
+    p = __fadd_rn(__fmul_rn(p, r), 4.1665796e-2f);
+    p = __fadd_rn(__fmul_rn(p, r), 1.6666665e-1f);
+    p = __fadd_rn(__fmul_rn(p, r), 5e-1f);
+    const float y = __fadd_rn(__fadd_rn(__fmul_rn(__fmul_rn(p, r), r), r), 1.0f);
+    return __fmul_rn(y, __uint_as_float((unsigned)((int)k + 127) << 23));
+}
+
+// linalg.rs:242-257 for n a multiple of 8, by the eight lanes 8g .. 8g + 7
+// of a warp (lane j keeps accumulator j: x*y then +, in order), the total
+// ((((a0 + a4) + (a1 + a5)) + (a2 + a6)) + (a3 + a7)) returned to all
+// eight. Every lane of the warp takes part.
+__device__ __forceinline__ float dot8_group(const float* a, const float* b, int n, int j) {
+    float acc = 0.f;
+    for (int c = 0; c < n / 8; c++) acc = __fadd_rn(acc, __fmul_rn(a[8 * c + j], b[8 * c + j]));
+    const float t = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4, 8));  // lanes j < 4: a_j + a_(j+4)
+    const float t0 = __shfl_sync(0xffffffffu, t, 0, 8), t1 = __shfl_sync(0xffffffffu, t, 1, 8);
+    const float t2 = __shfl_sync(0xffffffffu, t, 2, 8), t3 = __shfl_sync(0xffffffffu, t, 3, 8);
+    return __fadd_rn(__fadd_rn(__fadd_rn(t0, t1), t2), t3);
+}
+
+constexpr int HEAD_THREADS = 256;
+
+// linalg.rs:309-323 over x[0..n) in shared memory, by the whole block:
+// the max (order-free with FMAXNM), fast_exp(x - max) (0 for -inf), the
+// sum in order by one thread, then x * (1 / sum).
+__device__ void softmax_block(float* x, int n, float* red, float* s_val) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float mx = -INFINITY;
+    for (int i = tid; i < n; i += HEAD_THREADS) mx = fmaxnm(mx, x[i]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxnm(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    float m = red[0];
+    for (int w = 1; w < HEAD_THREADS / 32; w++) m = fmaxnm(m, red[w]);
+    const bool none = m == -INFINITY;
+    for (int i = tid; i < n; i += HEAD_THREADS) x[i] = (none || x[i] == -INFINITY) ? 0.f : fast_exp(__fsub_rn(x[i], m));
+    __syncthreads();
+    if (none) return;
+    if (tid == 0) {
+        float sum = 0.f;
+        for (int i = 0; i < n; i++) sum = __fadd_rn(sum, x[i]);
+        *s_val = __fdiv_rn(1.0f, sum);
+    }
+    __syncthreads();
+    const float inv = *s_val;
+    for (int i = tid; i < n; i += HEAD_THREADS) x[i] = __fmul_rn(x[i], inv);
+    __syncthreads();
+}
+
+// heads.rs:21-43, one CTA per (sequence, depth-probe pair lk): scores of
+// the T positions, softmax, the weighted sum of the cells in position
+// order, rms_unit, times the gain.
+__global__ void __launch_bounds__(HEAD_THREADS) probe_tokens_kernel(HeadW h, const float* cells, int T, int ncap, int l1,
+                                                                    float inv, float* r) {
+    pdl_launch_dependents();
+    pdl_wait();
+    extern __shared__ float sc[];  // [T]
+    __shared__ float acc[768];
+    __shared__ float red[HEAD_THREADS / 32];
+    __shared__ float s_val;
+    const int s = blockIdx.x, lk = blockIdx.y, l = lk / h.k, m = gridDim.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 3, j = lane & 7;
+    const float* probe = h.probes + (size_t)lk * 768;
+    const float* base = cells + ((size_t)s * ncap * l1 + l) * 768;  // position t at + t * l1 * 768
+    const size_t tstride = (size_t)l1 * 768;
+    for (int tb = 0; tb < T; tb += 32) {
+        const int t = tb + warp * 4 + g;
+        const float v = dot8_group(base + (size_t)(t < T ? t : 0) * tstride, probe, 768, j);
+        if (t < T && j == 0) sc[t] = __fmul_rn(v, inv);
+    }
+    __syncthreads();
+    softmax_block(sc, T, red, &s_val);
+    for (int c = tid; c < 768; c += HEAD_THREADS) {
+        float a = 0.f;
+        for (int t = 0; t < T; t++) a = __fadd_rn(a, __fmul_rn(sc[t], base[t * tstride + c]));
+        acc[c] = a;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float ss = 0.f;
+        for (int c = 0; c < 768; c++) ss = __fadd_rn(ss, __fmul_rn(acc[c], acc[c]));
+        s_val = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 768.0f), 1e-6f)));
+    }
+    __syncthreads();
+    const float rr = s_val, gg = h.gain[lk];
+    for (int c = tid; c < 768; c += HEAD_THREADS) r[((size_t)s * m + lk) * 768 + c] = __fmul_rn(__fmul_rn(acc[c], rr), gg);
+}
+
+// heads.rs:44-55, one CTA per (sequence, query): the m pooled rows'
+// scores plus the row bias, softmax, the weighted sum of the rows in order.
+__global__ void __launch_bounds__(HEAD_THREADS) probe_queries_kernel(HeadW h, const float* r, int m, float inv,
+                                                                     float* pooled) {
+    pdl_launch_dependents();
+    pdl_wait();
+    extern __shared__ float u[];  // [m]
+    __shared__ float red[HEAD_THREADS / 32];
+    __shared__ float s_val;
+    const int s = blockIdx.x, qi = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 3, j = lane & 7;
+    const float* rs = r + (size_t)s * m * 768;
+    const float* query = h.query + (size_t)qi * 768;
+    for (int jb = 0; jb < m; jb += 32) {
+        const int jj = jb + warp * 4 + g;
+        const float v = dot8_group(rs + (size_t)(jj < m ? jj : 0) * 768, query, 768, j);
+        if (jj < m && j == 0) u[jj] = __fadd_rn(__fmul_rn(v, inv), h.row_bias[(size_t)qi * m + jj]);
+    }
+    __syncthreads();
+    softmax_block(u, m, red, &s_val);
+    for (int c = tid; c < 768; c += HEAD_THREADS) {
+        float a = 0.f;
+        for (int jj = 0; jj < m; jj++) a = __fadd_rn(a, __fmul_rn(u[jj], rs[(size_t)jj * 768 + c]));
+        pooled[((size_t)s * h.q + qi) * 768 + c] = a;
+    }
+}
+
+// heads.rs:58-61, 68-90, one CTA per sequence: kind 0 the projection then
+// unit norm, 1 the pool at unit norm, 2 the projection's first value.
+__global__ void __launch_bounds__(HEAD_THREADS) probe_project_kernel(HeadW h, const float* pooled, int kind, float* out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    extern __shared__ float y[];  // [h.out]
+    __shared__ float s_val;
+    const int s = blockIdx.x, n = h.q * 768;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 3, j = lane & 7;
+    const float* pv = pooled + (size_t)s * n;
+    if (kind == 1) {
+        if (tid == 0) {
+            float ss = 0.f;
+            for (int c = 0; c < n; c++) ss = __fadd_rn(ss, __fmul_rn(pv[c], pv[c]));
+            s_val = __fsqrt_rn(__fadd_rn(ss, 1e-12f));
+        }
+        __syncthreads();
+        for (int c = tid; c < n; c += HEAD_THREADS) out[(size_t)s * n + c] = __fdiv_rn(pv[c], s_val);
+        return;
+    }
+    for (int ob = 0; ob < h.out; ob += 32) {
+        const int o = ob + warp * 4 + g;
+        const float v = dot8_group(h.proj + (size_t)(o < h.out ? o : 0) * n, pv, n, j);
+        if (o < h.out && j == 0) y[o] = __fadd_rn(v, h.bias[o]);
+    }
+    __syncthreads();
+    if (kind == 2) {
+        if (tid == 0) out[s] = y[0];
+        return;
+    }
+    if (tid == 0) {
+        float ss = 0.f;
+        for (int o = 0; o < h.out; o++) ss = __fadd_rn(ss, __fmul_rn(y[o], y[o]));
+        s_val = __fsqrt_rn(__fadd_rn(ss, 1e-12f));
+    }
+    __syncthreads();
+    for (int o = tid; o < h.out; o += HEAD_THREADS) out[(size_t)s * h.out + o] = __fdiv_rn(y[o], s_val);
+}
+
+void launch_probe_head(HeadW h, const float* cells, int S, int T, int ncap, int l1, int kind, float* r, float* pooled,
+                       float* out, cudaStream_t st) {
+    // heads.rs:14: inv = 1 / (float)sqrt((double)d), divided in f32
+    const float inv = 1.0f / (float)__builtin_sqrt(768.0);
+    const int m = l1 * h.k;
+    add_launches(3);
+    launch_pdl(probe_tokens_kernel, dim3(S, m), dim3(HEAD_THREADS), (size_t)T * sizeof(float), st, h, cells, T, ncap, l1, inv, r);
+    launch_pdl(probe_queries_kernel, dim3(S, h.q), dim3(HEAD_THREADS), (size_t)m * sizeof(float), st, h, (const float*)r, m, inv,
+               pooled);
+    launch_pdl(probe_project_kernel, dim3(S), dim3(HEAD_THREADS), (size_t)(h.out > 0 ? h.out : 1) * sizeof(float), st, h,
+               (const float*)pooled, kind, out);
+}
+
 static cudaError_t init_attrs() {
     cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_SMEM);
     cudaFuncSetAttribute(post_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)POST_SMEM);

@@ -42,6 +42,15 @@ struct LayerW {
     float b_pre[4], b_post[4], b_res[16];
 };
 
+// A probe-pooling head (weights.rs:60-76) on the device, dequantized to f32:
+// probes [(L+1) * k][d], gain [(L+1) * k], query [q][d], row_bias
+// [q][(L+1) * k], proj [out][q * d], bias [out].
+struct HeadW {
+    int k = 0, q = 0, out = 0;
+    const float *probes = nullptr, *gain = nullptr, *query = nullptr, *row_bias = nullptr, *proj = nullptr,
+                *bias = nullptr;
+};
+
 // Per-sequence caches of one batch.
 struct Caches {
     int S, L, cap;        // sequences, layers, KV slots per sequence
@@ -116,6 +125,17 @@ void launch_rope_rows(const float* table_cos, const float* table_sin, const floa
 void launch_advance_len(int32_t* len, int T, cudaStream_t st);
 void launch_hold(unsigned long long ns, cudaStream_t st);
 void launch_masked_argmax(const float* logits, int S, int V, const uint8_t* allow, int32_t* next, cudaStream_t st);
+// infer.rs:1195-1211: the lane mean of rows m = (s, i) of xs [M][4][768] at
+// depth `depth` into cells [S][ncap][l1][768], position p0 + i.
+void launch_record_cells(const float* xs, int S, int T, int p0, int depth, int l1, int ncap, float* cells, cudaStream_t st);
+// heads.rs:12-61, 77-90: the head over the cells of T positions of each of
+// S sequences. r [S][l1 * k][768] and pooled [S][q * 768] are scratch.
+// kind 0: the embedding (project, then unit norm) into out [S][h.out];
+// kind 1: the pool alone at unit norm, out [S][q * 768] (the embedding
+// without an embedding head); kind 2: the projection's first value (the
+// confidence logit), out [S].
+void launch_probe_head(HeadW h, const float* cells, int S, int T, int ncap, int l1, int kind, float* r, float* pooled,
+                       float* out, cudaStream_t st);
 // The call sampler's start, per row of logits [S][V] (V <= 32768): with the
 // entries whose `allow` bit is clear read as -1e30, the max m[s] and
 // z[s] = sum exp(l - m) as agent.rs:1241-1252 forms them; with those of

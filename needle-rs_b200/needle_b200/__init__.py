@@ -43,6 +43,8 @@ def lib():
             "nd_head_logits": (I, [P, P, I, P, I]),
             "nd_head_logits_sparse": (I, [P, P, P, I, P]),
             "nd_batch_stream": (P, [P]),
+            "nd_batch_embed": (I, [P, P, I, P, C.POINTER(I), I]),
+            "nd_batch_confidence": (I, [P, P, I, P, I]),
             "nd_batch_candidates": (I, [P, P, P, P, I, P, P, P, P, I]),
             "nd_cq_pack": (I, [P, I, I, I, P, P]),
             "nd_cqmat_new": (I, [I, P, P, I, I, I, C.POINTER(P)]),
@@ -308,6 +310,26 @@ class Batch:
         ids = np.ascontiguousarray(ids, np.int32)
         out = np.zeros(self.model.out_rows, np.float32)
         if lib().nd_head_logits_sparse(self._h, _p(h), _p(ids), len(ids), _p(out)) != 0:
+            raise _err()
+        return out
+
+    def embed(self, ids):
+        """needle_embed's computation for every sequence of this fresh batch
+        (heads.rs:63-90): ids [S, T]; returns [S, dim] unit vectors."""
+        ids = np.ascontiguousarray(ids, np.int32).reshape(self.num_seqs, -1)
+        dim = C.c_int(0)
+        if lib().nd_batch_embed(self._h, None, 0, None, C.byref(dim), 0) != 0:
+            raise _err()
+        out = np.zeros((self.num_seqs, dim.value), np.float32)
+        if lib().nd_batch_embed(self._h, _p(ids), ids.shape[1], _p(out), C.byref(dim), 0) != 0:
+            raise _err()
+        return out
+
+    def confidence(self, ids):
+        """heads.rs:68-74 for every sequence of this fresh batch: [S]."""
+        ids = np.ascontiguousarray(ids, np.int32).reshape(self.num_seqs, -1)
+        out = np.zeros(self.num_seqs, np.float32)
+        if lib().nd_batch_confidence(self._h, _p(ids), ids.shape[1], _p(out), 0) != 0:
             raise _err()
         return out
 
