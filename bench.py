@@ -52,7 +52,9 @@ def parse():
                          "model's four matrix shapes), one JSON line")
     ap.add_argument("--profile", action="store_true",
                     help="untimed case for ncu: one batch of --seqs sequences, the 118-token prefill, then --warmup "
-                         "decode steps")
+                         "decode steps (--profile-case decode); or three call-sampler launches over 1024 rows of "
+                         "logits (candidates); or one 256 x 64 embedding (embed)")
+    ap.add_argument("--profile-case", default="decode", choices=["decode", "candidates", "embed"])
     return ap.parse_args()
 
 
@@ -360,10 +362,45 @@ def call_candidates(model, dev, S=1024, k=128, reps=20):
         call()
     e1.record(st)
     torch.cuda.synchronize()
-    us = e0.elapsed_time(e1) * 1e3 / reps
+    us = e0.elapsed_time(e1) * 1e3 / max(reps, 1)
     del b
     return {"rows": S, "vocab": V, "k": k, "us_per_call": round(us, 2),
             "logit_gbs": round(S * V * 4 / (us * 1e-6) / 1e9, 1)}
+
+
+def embed_texts(local, dev, S=256, T=64):
+    """needle_embed's computation (heads.rs:63-90) for 256 texts of 64
+    tokens at once on a Needle 3 archive with embedding and confidence
+    heads: the forward with cells, the probe pool, the projection. Host ids
+    in, unit vectors out, one nd_batch_embed call timed by CUDA events."""
+    import torch
+
+    import needle_b200 as nb
+
+    path = os.path.join(CACHE, "needle3-seed0-heads.cact")
+    if not os.path.exists(path):
+        os.makedirs(CACHE, exist_ok=True)
+        data = nb.synth_cact(seed=0, heads=(nb.HEAD_EMBEDDING, nb.HEAD_CONFIDENCE))
+        tmp = f"{path}.{os.getpid()}.tmp"
+        with open(tmp, "wb") as f:
+            f.write(data)
+        os.replace(tmp, path)
+    with open(path, "rb") as f:
+        model = nb.Model(f.read(), local)
+    ids = np.random.default_rng(11).integers(0, model.vocab, (S, T)).astype(np.int32)
+    model.batch(S, T).embed(ids)  # warm
+    torch.cuda.synchronize()
+    b = model.batch(S, T)
+    st = torch.cuda.ExternalStream(b.stream, device=dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    v = b.embed(ids)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    del b, model
+    return {"texts": S, "tokens_per_text": T, "dim": int(v.shape[1]), "ms": round(ms, 3),
+            "texts_per_s": round(S / (ms * 1e-3), 1), "tok_s": round(S * T / (ms * 1e-3), 1)}
 
 
 def secondary(model, local):
@@ -389,6 +426,7 @@ def secondary(model, local):
     out["decode_b1_low_width"]["bits"] = LOW_WIDTH
     del low
     out["call_candidates_1024"] = call_candidates(model, dev)
+    out["embed_256x64"] = embed_texts(local, dev)
     # 256 x 700 prefill, ids resident in HBM
     S, n = 256, 700
     b = model.batch(S, n + 1)
@@ -439,6 +477,14 @@ def main():
     data = archive_bytes()
     model = nb.Model(data, device=local)
     V = model.out_rows
+    if args.profile and args.profile_case == "candidates":
+        call_candidates(model, f"cuda:{local}", reps=0)
+        torch.cuda.synchronize()
+        return
+    if args.profile and args.profile_case == "embed":
+        embed_texts(local, f"cuda:{local}")
+        torch.cuda.synchronize()
+        return
     if args.profile:
         prompts, masks = make_inputs(rank, S, W, V)
         b = model.batch(S, PROMPT + W + 1)

@@ -473,7 +473,7 @@ struct Batch {
     float *cells = nullptr, *head_r = nullptr, *head_pool = nullptr, *head_out = nullptr;
     int cells_cap = 0;       // positions per sequence the cells buffer holds
     bool recording = false;  // chunk() records cells while set
-    float* clogits = nullptr;
+    float *clogits = nullptr, *cex = nullptr;
     uint8_t *cmask1 = nullptr, *cmask2 = nullptr;
     int32_t *cids = nullptr, *clive = nullptr;
     float* cm = nullptr;
@@ -1001,6 +1001,7 @@ int nd_batch_candidates(nd_batch* bh, const float* logits, const unsigned char* 
         const size_t mb = (size_t)(V + 7) / 8;
         if (!b.cids) {
             b.clogits = b.alloc<float>((size_t)b.S * V);
+            b.cex = b.alloc<float>((size_t)b.S * V);
             b.cmask1 = b.alloc<uint8_t>((size_t)b.S * mb);
             b.cmask2 = b.alloc<uint8_t>((size_t)b.S * mb);
             b.cids = b.alloc<int32_t>((size_t)b.S * 128);
@@ -1027,7 +1028,7 @@ int nd_batch_candidates(nd_batch* bh, const float* logits, const unsigned char* 
         int32_t* dl = dev ? (int32_t*)live : b.clive;
         float* dm = dev ? m : b.cm;
         double* dz = dev ? z : b.cz;
-        CK(launch_candidates(src, b.S, V, a1, a2, k, di, dm, dz, dl, b.st));
+        CK(launch_candidates(src, b.S, V, a1, a2, k, di, dm, dz, dl, b.cex, b.st));
         if (!dev) {
             CK(cudaMemcpyAsync(ids, b.cids, (size_t)b.S * k * sizeof(int32_t), cudaMemcpyDeviceToHost, b.st));
             CK(cudaMemcpyAsync(live, b.clive, (size_t)b.S * sizeof(int32_t), cudaMemcpyDeviceToHost, b.st));

@@ -1949,19 +1949,20 @@ void launch_masked_argmax(const float* logits, int S, int V, const uint8_t* allo
 // step starts from, per sequence (agent.rs:295-343): softmax_stats
 // (agent.rs:1241-1252) over the logits with the step's bans, then the
 // unmasked candidates by logit (lowest id first on ties) after the call
-// step's further bans, the first k of them. One CTA per sequence of 512
-// threads, each holding V / 512 logits in registers:
-//   * the max by a block reduction (exact);
-//   * engine_expf(v - max) of every element of the whole groups of four into
-//     shared memory, then the reference's four lane chains (lane j sums
-//     elements 4i + j in order, lane_exp_sums, agent.rs:1147-1198) by four
-//     threads, the lanes summed (l0 + l1) + (l2 + l3) and widened, the
-//     remainder in f64;
-//   * the k-th smallest of the 48-bit keys (~orderable(logit) << 16 | id),
-//     whose order is the reference's (logit descending, id ascending), by
-//     six 8-bit radix passes over shared histograms; the keys at or below
-//     it are the k candidates, ranked by counting.
-constexpr int CAND_THREADS = 512, CAND_MAXK = 128;
+// step's further bans, the first k of them. Two kernels:
+//   * cand_select_kernel, one CTA per sequence holding its V logits in
+//     registers: the max by a block reduction (exact); engine_expf(v - max)
+//     of the whole groups of four into a lane-major scratch row (lane j =
+//     elements 4i + j, in i order); the k-th smallest of the 48-bit keys
+//     (~orderable(logit) << 16 | id), whose order is the reference's (logit
+//     descending, id ascending), by six 8-bit radix passes over a shared
+//     histogram (atomics aggregated per warp over equal bins); the keys at
+//     or below it are the k candidates, ranked by counting;
+//   * cand_sum_kernel, four threads per sequence: the reference's four lane
+//     chains (lane_exp_sums, agent.rs:1147-1198), each a dependent run of
+//     V/4 f32 adds in element order, all sequences' chains at once, then
+//     (l0 + l1) + (l2 + l3) widened and the remainder in f64.
+constexpr int CAND_MAXK = 128;
 
 // agent.rs:1130-1145: the engine's own f32 exp (its constants).
 __device__ __forceinline__ float engine_expf(float x) {
@@ -1999,18 +2000,44 @@ __device__ __forceinline__ float fmaxnm(float a, float b) {
     return signbit(a) ? b : a;
 }
 
-template <int VPT>
-__global__ void __launch_bounds__(CAND_THREADS) candidates_kernel(const float* logits, int V, const uint8_t* allow,
-                                                                  const uint8_t* allow_order, int k, int32_t* ids,
-                                                                  float* mo, double* zo, int32_t* live_out) {
+// Ascending bitonic sort of one key per thread over a block of 1024
+// threads: afterwards thread i holds the i-th smallest. Strides below 32
+// exchange by warp shuffles, larger ones through shared memory sk[1024].
+__device__ __forceinline__ unsigned long long bitonic_1024(unsigned long long key, unsigned long long* sk) {
+    const int tid = threadIdx.x;
+#pragma unroll 1
+    for (int size = 2; size <= 1024; size <<= 1) {
+        const bool asc = (tid & size) == 0;
+#pragma unroll 1
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            unsigned long long other;
+            if (stride >= 32) {
+                __syncthreads();
+                sk[tid] = key;
+                __syncthreads();
+                other = sk[tid ^ stride];
+            } else {
+                other = __shfl_xor_sync(0xffffffffu, key, stride);
+            }
+            const bool lower = (tid & stride) == 0;
+            key = (lower == asc) ? (other < key ? other : key) : (other > key ? other : key);
+        }
+    }
+    return key;
+}
+
+constexpr int CAND_CAP = 1024;  // candidates sorted directly; more fall back to radix passes
+
+template <int VPT, int THREADS>
+__global__ void __launch_bounds__(THREADS) cand_select_kernel(const float* logits, int V, const uint8_t* allow,
+                                                              const uint8_t* allow_order, int k, int32_t* ids, float* mo,
+                                                              int32_t* live_out, float* ex) {
     pdl_launch_dependents();
     pdl_wait();
-    extern __shared__ float ex[];  // [V / 4 * 4]: engine_expf(v - max)
+    __shared__ unsigned long long skey[1024];  // sort exchanges, then the candidates
     __shared__ unsigned hist[256];
-    __shared__ float redf[CAND_THREADS / 32];
-    __shared__ int redi[CAND_THREADS / 32];
-    __shared__ unsigned long long ckey[CAND_MAXK];
-    __shared__ float lane_sum[4];
+    __shared__ float redf[THREADS / 32];
+    __shared__ int redi[THREADS / 32];
     __shared__ unsigned long long s_prefix;
     __shared__ int s_rem, s_count;
     const int s = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -2022,7 +2049,7 @@ __global__ void __launch_bounds__(CAND_THREADS) candidates_kernel(const float* l
     float mx = -INFINITY;
 #pragma unroll
     for (int j = 0; j < VPT; j++) {
-        const int i = tid + j * CAND_THREADS;
+        const int i = tid + j * THREADS;
         float t = -INFINITY;
         if (i < V) {
             t = bit_clear(a1, i) ? -1e30f : x[i];
@@ -2035,42 +2062,78 @@ __global__ void __launch_bounds__(CAND_THREADS) candidates_kernel(const float* l
     if (lane == 0) redf[warp] = mx;
     __syncthreads();
     float m = redf[0];
-    for (int w = 1; w < CAND_THREADS / 32; w++) m = fmaxnm(m, redf[w]);
-    const int main = V / 4 * 4;
+    for (int w = 1; w < THREADS / 32; w++) m = fmaxnm(m, redf[w]);
+    const int Q = V / 4;
+    float* er = ex + (size_t)s * 4 * Q;
     int nl = 0;
+    unsigned long long best = ~0ull;  // this thread's smallest live key
 #pragma unroll
     for (int j = 0; j < VPT; j++) {
-        const int i = tid + j * CAND_THREADS;
-        if (i < main) ex[i] = engine_expf(__fsub_rn(v[j], m));
+        const int i = tid + j * THREADS;
+        if (i < 4 * Q) er[(i & 3) * Q + (i >> 2)] = engine_expf(__fsub_rn(v[j], m));
         if (i < V && bit_clear(a2, i)) v[j] = -1e30f;
-        nl += (i < V && v[j] > -1e30f) ? 1 : 0;
+        if (i < V && v[j] > -1e30f) {
+            nl++;
+            const unsigned long long key = cand_key(v[j], i);
+            best = key < best ? key : best;
+        }
     }
     nl = warp_sum_i(nl);
     if (lane == 0) redi[warp] = nl;
     __syncthreads();
     int live = 0;
-    for (int w = 0; w < CAND_THREADS / 32; w++) live += redi[w];
-    // the four lane chains, in element order
-    if (tid < 4) {
-        float acc = 0.f;
-#pragma unroll 8
-        for (int i = tid; i < main; i += 4) acc = __fadd_rn(acc, ex[i]);
-        lane_sum[tid] = acc;
-    }
+    for (int w = 0; w < THREADS / 32; w++) live += redi[w];
     const int K = min(k, live);
-    unsigned long long prefix = 0ull, pmask = 0ull;
-    int rem = K;
+    // At least K live keys are at or below the K-th smallest of the threads'
+    // best keys: those keys are the candidates, usually a few hundred.
+    const unsigned long long sorted_best = bitonic_1024(best, skey);
+    if (tid == K - 1) s_prefix = sorted_best;
+    if (tid == 0) s_count = 0;
+    __syncthreads();
+    const unsigned long long t0 = K > 0 ? s_prefix : 0ull;
     if (K > 0) {
+#pragma unroll
+        for (int j = 0; j < VPT; j++) {
+            const int i = tid + j * THREADS;
+            if (i < V && v[j] > -1e30f) {
+                const unsigned long long key = cand_key(v[j], i);
+                if (key <= t0) {
+                    const int slot = atomicAdd(&s_count, 1);
+                    if (slot < CAND_CAP) skey[slot] = key;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    const int C = s_count;
+    int32_t* out = ids + (size_t)s * k;
+    if (K > 0 && C <= CAND_CAP) {
+        const unsigned long long mine = tid < C ? skey[tid] : ~0ull;
+        const unsigned long long kt = bitonic_1024(mine, skey);
+        if (tid < K) out[tid] = (int32_t)(kt & 0xffffu);
+    } else if (K > 0) {
+        // the K-th smallest key by six 8-bit radix passes (histogram atomics
+        // aggregated per warp over equal bins), then the keys at or below it
+        unsigned long long prefix = 0ull, pmask = 0ull;
+        int rem = K;
         for (int pass = 0; pass < 6; pass++) {
             const int shift = 40 - 8 * pass;
-            for (int b = tid; b < 256; b += CAND_THREADS) hist[b] = 0u;
+            for (int b = tid; b < 256; b += THREADS) hist[b] = 0u;
             __syncthreads();
 #pragma unroll
             for (int j = 0; j < VPT; j++) {
-                const int i = tid + j * CAND_THREADS;
+                const int i = tid + j * THREADS;
+                bool act = false;
+                unsigned bin = 0;
                 if (i < V && v[j] > -1e30f) {
                     const unsigned long long key = cand_key(v[j], i);
-                    if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+                    act = (key & pmask) == prefix;
+                    bin = (unsigned)(key >> shift) & 255u;
+                }
+                const unsigned am = __ballot_sync(0xffffffffu, act);
+                if (act) {
+                    const unsigned same = __match_any_sync(am, bin);
+                    if (lane == __ffs(same) - 1) atomicAdd(&hist[bin], (unsigned)__popc(same));
                 }
             }
             __syncthreads();
@@ -2104,55 +2167,105 @@ __global__ void __launch_bounds__(CAND_THREADS) candidates_kernel(const float* l
             rem = s_rem;
             pmask |= 255ull << shift;
         }
-    }
-    if (tid == 0) s_count = 0;
-    __syncthreads();
-    if (K > 0) {
+        if (tid == 0) s_count = 0;
+        __syncthreads();
 #pragma unroll
         for (int j = 0; j < VPT; j++) {
-            const int i = tid + j * CAND_THREADS;
+            const int i = tid + j * THREADS;
             if (i < V && v[j] > -1e30f) {
                 const unsigned long long key = cand_key(v[j], i);
                 if (key <= prefix) {
                     const int slot = atomicAdd(&s_count, 1);
-                    if (slot < CAND_MAXK) ckey[slot] = key;
+                    if (slot < CAND_MAXK) skey[slot] = key;
                 }
             }
         }
-    }
-    __syncthreads();
-    int32_t* out = ids + (size_t)s * k;
-    if (tid < K) {
-        const unsigned long long kt = ckey[tid];
-        int r = 0;
-        for (int j = 0; j < K; j++) r += ckey[j] < kt ? 1 : 0;
-        out[r] = (int32_t)(kt & 0xffffu);
-    } else if (tid < k) {
-        out[tid] = -1;
-    }
-    if (tid == 0) {
-        double z = (double)__fadd_rn(__fadd_rn(lane_sum[0], lane_sum[1]), __fadd_rn(lane_sum[2], lane_sum[3]));
-        for (int i = main; i < V; i++) {
-            const float t = bit_clear(a1, i) ? -1e30f : x[i];
-            if (t > -1e30f) z = __dadd_rn(z, exp(__dsub_rn((double)t, (double)m)));
+        __syncthreads();
+        if (tid < K) {
+            const unsigned long long kt = skey[tid];
+            int r = 0;
+            for (int j = 0; j < K; j++) r += skey[j] < kt ? 1 : 0;
+            out[r] = (int32_t)(kt & 0xffffu);
         }
+    }
+    if (tid >= K && tid < k) out[tid] = -1;
+    if (tid == 0) {
         mo[s] = m;
-        zo[s] = z;
         live_out[s] = live;
     }
 }
 
+// One warp per sequence: lanes 0-3 sum lanes 0-3 of the exps in element
+// order, 256 elements of each lane a chunk, while the whole warp's cp.async
+// copies bring the next chunk into the other half of a shared double
+// buffer; lane 0 then forms z (agent.rs:1245-1250). A row whose lane length
+// is not a multiple of 256 is summed straight from global memory.
+__global__ void __launch_bounds__(32) cand_sum_kernel(const float* ex, const float* logits, int V, const uint8_t* allow,
+                                                      const float* mo, double* zo) {
+    pdl_launch_dependents();
+    pdl_wait();
+    __shared__ __align__(16) float buf[2][4][256];
+    const int s = blockIdx.x, lane = threadIdx.x;
+    const int Q = V / 4;
+    const float* er = ex + (size_t)s * 4 * Q;
+    float acc = 0.f;
+    if (Q % 256 == 0) {
+        const int nchunk = Q / 256, seg = lane >> 3;
+        auto fetch = [&](int c, int b) {
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int q4 = (lane & 7) + 8 * u;
+                cp_async16(&buf[b][seg][4 * q4], er + (size_t)seg * Q + c * 256 + 4 * q4, true);
+            }
+            asm volatile("cp.async.commit_group;\n" ::);
+        };
+        fetch(0, 0);
+        for (int c = 0; c < nchunk; c++) {
+            if (c + 1 < nchunk) {
+                fetch(c + 1, (c + 1) & 1);
+                asm volatile("cp.async.wait_group 1;\n" ::);
+            } else {
+                asm volatile("cp.async.wait_group 0;\n" ::);
+            }
+            __syncwarp();
+            if (lane < 4) {
+                const float4* b4 = (const float4*)buf[c & 1][lane];
+#pragma unroll 8
+                for (int q = 0; q < 64; q++) {
+                    const float4 e = b4[q];
+                    acc = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc, e.x), e.y), e.z), e.w);
+                }
+            }
+            __syncwarp();
+        }
+    } else if (lane < 4) {
+        const float* el = er + (size_t)lane * Q;
+        for (int i = 0; i < Q; i++) acc = __fadd_rn(acc, el[i]);
+    }
+    const float l1 = __shfl_sync(0xffffffffu, acc, 1), l2 = __shfl_sync(0xffffffffu, acc, 2),
+                l3 = __shfl_sync(0xffffffffu, acc, 3);
+    if (lane == 0) {
+        double z = (double)__fadd_rn(__fadd_rn(acc, l1), __fadd_rn(l2, l3));
+        const float m = mo[s];
+        const float* x = logits + (size_t)s * V;
+        const uint8_t* a1 = allow ? allow + (size_t)s * ((V + 7) / 8) : nullptr;
+        for (int i = 4 * Q; i < V; i++) {
+            const float v = bit_clear(a1, i) ? -1e30f : x[i];
+            if (v > -1e30f) z = __dadd_rn(z, exp(__dsub_rn((double)v, (double)m)));
+        }
+        zo[s] = z;
+    }
+}
+
 cudaError_t launch_candidates(const float* logits, int S, int V, const uint8_t* allow, const uint8_t* allow_order, int k,
-                              int32_t* ids, float* m, double* z, int32_t* live, cudaStream_t st) {
-    if (S < 1 || V < 1 || V > 64 * CAND_THREADS || k < 1 || k > CAND_MAXK) return cudaErrorInvalidValue;
-    COUNT_LAUNCH();
-    const size_t smem = (size_t)(V / 4 * 4) * sizeof(float);
-    if (V <= 16 * CAND_THREADS)
-        launch_pdl(candidates_kernel<16>, dim3(S), dim3(CAND_THREADS), smem, st, logits, V, allow, allow_order, k, ids, m, z, live);
-    else if (V <= 32 * CAND_THREADS)
-        launch_pdl(candidates_kernel<32>, dim3(S), dim3(CAND_THREADS), smem, st, logits, V, allow, allow_order, k, ids, m, z, live);
+                              int32_t* ids, float* m, double* z, int32_t* live, float* ex, cudaStream_t st) {
+    if (S < 1 || V < 1 || V > 32768 || k < 1 || k > CAND_MAXK) return cudaErrorInvalidValue;
+    add_launches(2);
+    if (V <= 16384)
+        launch_pdl(cand_select_kernel<16, 1024>, dim3(S), dim3(1024), 0, st, logits, V, allow, allow_order, k, ids, m, live, ex);
     else
-        launch_pdl(candidates_kernel<64>, dim3(S), dim3(CAND_THREADS), smem, st, logits, V, allow, allow_order, k, ids, m, z, live);
+        launch_pdl(cand_select_kernel<32, 1024>, dim3(S), dim3(1024), 0, st, logits, V, allow, allow_order, k, ids, m, live, ex);
+    launch_pdl(cand_sum_kernel, dim3(S), dim3(32), 0, st, (const float*)ex, logits, V, allow, (const float*)m, z);
     return cudaSuccess;
 }
 
@@ -2362,9 +2475,6 @@ static cudaError_t init_attrs() {
     cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_SMEM);
     cudaFuncSetAttribute(post_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)POST_SMEM);
     cudaFuncSetAttribute(post_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)POST_ROW_SMEM);
-    cudaFuncSetAttribute(candidates_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 16 * CAND_THREADS * 4);
-    cudaFuncSetAttribute(candidates_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 32 * CAND_THREADS * 4);
-    cudaFuncSetAttribute(candidates_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * CAND_THREADS * 4);
     cudaFuncSetAttribute(cq_mma_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
     cudaFuncSetAttribute(cq_mma_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
     return cudaFuncSetAttribute(cq_mma_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
