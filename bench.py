@@ -54,7 +54,8 @@ def parse():
                     help="untimed case for ncu: one batch of --seqs sequences, the 118-token prefill, then --warmup "
                          "decode steps (--profile-case decode); or three call-sampler launches over 1024 rows of "
                          "logits (candidates); or one 256 x 64 embedding (embed)")
-    ap.add_argument("--profile-case", default="decode", choices=["decode", "candidates", "embed"])
+    ap.add_argument("--profile-case", default="decode", choices=["decode", "candidates", "embed"],
+                    help="decode uses --seqs sequences (1 for the batch-1 step)")
     return ap.parse_args()
 
 

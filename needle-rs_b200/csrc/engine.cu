@@ -996,7 +996,7 @@ int nd_batch_candidates(nd_batch* bh, const float* logits, const unsigned char* 
             throw std::runtime_error("nd_batch_candidates needs the last logits of every sequence");
         if (k < 1 || k > 128) throw std::runtime_error("nd_batch_candidates: k must be in [1, 128]");
         const int V = b.m->c.out_rows();
-        if (V > 32768) throw std::runtime_error("nd_batch_candidates: more than 32768 logits a row");
+        if (V > 65536) throw std::runtime_error("nd_batch_candidates: more than 65536 logits a row");
         const bool dev = flags & ND_DEVICE;
         const size_t mb = (size_t)(V + 7) / 8;
         if (!b.cids) {

@@ -1949,20 +1949,23 @@ void launch_masked_argmax(const float* logits, int S, int V, const uint8_t* allo
 // step starts from, per sequence (agent.rs:295-343): softmax_stats
 // (agent.rs:1241-1252) over the logits with the step's bans, then the
 // unmasked candidates by logit (lowest id first on ties) after the call
-// step's further bans, the first k of them. Two kernels:
-//   * cand_select_kernel, one CTA per sequence holding its V logits in
-//     registers: the max by a block reduction (exact); engine_expf(v - max)
-//     of the whole groups of four into a lane-major scratch row (lane j =
-//     elements 4i + j, in i order); the k-th smallest of the 48-bit keys
-//     (~orderable(logit) << 16 | id), whose order is the reference's (logit
-//     descending, id ascending), by six 8-bit radix passes over a shared
-//     histogram (atomics aggregated per warp over equal bins); the keys at
-//     or below it are the k candidates, ranked by counting;
-//   * cand_sum_kernel, four threads per sequence: the reference's four lane
-//     chains (lane_exp_sums, agent.rs:1147-1198), each a dependent run of
-//     V/4 f32 adds in element order, all sequences' chains at once, then
-//     (l0 + l1) + (l2 + l3) widened and the remainder in f64.
-constexpr int CAND_MAXK = 128;
+// step's further bans, the first k of them. Two kernels, the row's logits
+// read from L2 a few times each:
+//   * cand_select_kernel, one 256-thread CTA per sequence: the max
+//     (order-free: f32::max as the reference's platform has it), the live
+//     count and each thread's smallest 48-bit key (~orderable(logit) << 16
+//     | id, ascending in the reference's order); the k-th smallest of those
+//     256 keys bounds the candidates (at least k keys lie at or below it,
+//     usually a couple of hundred in all), which are gathered into shared
+//     memory and sorted by a bitonic network; should more than CAND_BUF
+//     qualify, the k smallest are drawn one at a time instead;
+//     it also writes engine_expf(v - max) of every element of the whole
+//     groups of four to a lane-major scratch row (lane j: elements 4i + j);
+//   * cand_sum_kernel, one warp per sequence: lanes 0-3 add lane j's exps
+//     in i order, the reference's four lane chains (lane_exp_sums,
+//     agent.rs:1147-1198), each a dependent run of V/4 f32 adds, fed from
+//     the scratch row by cp.async double buffering.
+constexpr int CAND_MAXK = 128, CAND_BUF = 1024, CSEL_THREADS = 256;
 
 // agent.rs:1130-1145: the engine's own f32 exp (its constants).
 __device__ __forceinline__ float engine_expf(float x) {
@@ -2000,211 +2003,197 @@ __device__ __forceinline__ float fmaxnm(float a, float b) {
     return signbit(a) ? b : a;
 }
 
-// Ascending bitonic sort of one key per thread over a block of 1024
-// threads: afterwards thread i holds the i-th smallest. Strides below 32
-// exchange by warp shuffles, larger ones through shared memory sk[1024].
-__device__ __forceinline__ unsigned long long bitonic_1024(unsigned long long key, unsigned long long* sk) {
-    const int tid = threadIdx.x;
-#pragma unroll 1
-    for (int size = 2; size <= 1024; size <<= 1) {
-        const bool asc = (tid & size) == 0;
-#pragma unroll 1
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            unsigned long long other;
-            if (stride >= 32) {
-                __syncthreads();
-                sk[tid] = key;
-                __syncthreads();
-                other = sk[tid ^ stride];
-            } else {
-                other = __shfl_xor_sync(0xffffffffu, key, stride);
-            }
-            const bool lower = (tid & stride) == 0;
-            key = (lower == asc) ? (other < key ? other : key) : (other > key ? other : key);
-        }
-    }
-    return key;
+__device__ __forceinline__ unsigned long long umin64(unsigned long long a, unsigned long long b) { return a < b ? a : b; }
+__device__ __forceinline__ unsigned long long umax64(unsigned long long a, unsigned long long b) { return a < b ? b : a; }
+
+// The logit of element i as the row's bans leave it (-1e30 when banned).
+__device__ __forceinline__ float cand_logit(const float* x, const uint8_t* a1, const uint8_t* a2, int i) {
+    return (bit_clear(a1, i) || bit_clear(a2, i)) ? -1e30f : __ldg(x + i);
 }
 
-constexpr int CAND_CAP = 1024;  // candidates sorted directly; more fall back to radix passes
+constexpr int CAND_UNROLL = 8;  // elements a thread has in flight together
 
-template <int VPT, int THREADS>
-__global__ void __launch_bounds__(THREADS) cand_select_kernel(const float* logits, int V, const uint8_t* allow,
-                                                              const uint8_t* allow_order, int k, int32_t* ids, float* mo,
-                                                              int32_t* live_out, float* ex) {
+__global__ void __launch_bounds__(CSEL_THREADS) cand_select_kernel(const float* logits, int V, const uint8_t* allow,
+                                                                   const uint8_t* allow_order, int k, int32_t* ids,
+                                                                   float* mo, int32_t* live_out, float* ex) {
     pdl_launch_dependents();
     pdl_wait();
-    __shared__ unsigned long long skey[1024];  // sort exchanges, then the candidates
-    __shared__ unsigned hist[256];
-    __shared__ float redf[THREADS / 32];
-    __shared__ int redi[THREADS / 32];
-    __shared__ unsigned long long s_prefix;
-    __shared__ int s_rem, s_count;
+    __shared__ unsigned long long sk[CAND_BUF];
+    __shared__ float redf[CSEL_THREADS / 32];
+    __shared__ int redi[CSEL_THREADS / 32];
+    __shared__ unsigned long long s_t0;
+    __shared__ int s_count;
+    const unsigned FULL = 0xffffffffu;
     const int s = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float* x = logits + (size_t)s * V;
     const size_t mb = (size_t)(V + 7) / 8;
     const uint8_t* a1 = allow ? allow + (size_t)s * mb : nullptr;
     const uint8_t* a2 = allow_order ? allow_order + (size_t)s * mb : nullptr;
-    float v[VPT];
+    constexpr int STEP = CSEL_THREADS * CAND_UNROLL;
+    // the max
     float mx = -INFINITY;
+    for (int base = 0; base < V; base += STEP) {
+        float vv[CAND_UNROLL];
 #pragma unroll
-    for (int j = 0; j < VPT; j++) {
-        const int i = tid + j * THREADS;
-        float t = -INFINITY;
-        if (i < V) {
-            t = bit_clear(a1, i) ? -1e30f : x[i];
-            mx = fmaxnm(mx, t);
+        for (int u = 0; u < CAND_UNROLL; u++) {
+            const int i = base + CSEL_THREADS * u + tid;
+            vv[u] = i < V ? cand_logit(x, a1, nullptr, i) : -INFINITY;
         }
-        v[j] = t;
+#pragma unroll
+        for (int u = 0; u < CAND_UNROLL; u++) mx = fmaxnm(mx, vv[u]);
     }
 #pragma unroll
-    for (int o = 16; o; o >>= 1) mx = fmaxnm(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    for (int o = 16; o; o >>= 1) mx = fmaxnm(mx, __shfl_xor_sync(FULL, mx, o));
     if (lane == 0) redf[warp] = mx;
+    if (tid == 0) s_count = 0;
     __syncthreads();
     float m = redf[0];
-    for (int w = 1; w < THREADS / 32; w++) m = fmaxnm(m, redf[w]);
+    for (int w = 1; w < CSEL_THREADS / 32; w++) m = fmaxnm(m, redf[w]);
+    // the exps (lane-major: element 4i + j at ex[j][i]); with the order
+    // bans, the live count and each thread's best key
     const int Q = V / 4;
     float* er = ex + (size_t)s * 4 * Q;
     int nl = 0;
-    unsigned long long best = ~0ull;  // this thread's smallest live key
+    unsigned long long best = ~0ull;
+    for (int base = 0; base < V; base += STEP) {
+        float vv[CAND_UNROLL];
+        bool b2[CAND_UNROLL];
 #pragma unroll
-    for (int j = 0; j < VPT; j++) {
-        const int i = tid + j * THREADS;
-        if (i < 4 * Q) er[(i & 3) * Q + (i >> 2)] = engine_expf(__fsub_rn(v[j], m));
-        if (i < V && bit_clear(a2, i)) v[j] = -1e30f;
-        if (i < V && v[j] > -1e30f) {
-            nl++;
-            const unsigned long long key = cand_key(v[j], i);
-            best = key < best ? key : best;
+        for (int u = 0; u < CAND_UNROLL; u++) {
+            const int i = base + CSEL_THREADS * u + tid;
+            vv[u] = i < V ? cand_logit(x, a1, nullptr, i) : -INFINITY;
+            b2[u] = i < V && bit_clear(a2, i);
+        }
+#pragma unroll
+        for (int u = 0; u < CAND_UNROLL; u++) {
+            const int i = base + CSEL_THREADS * u + tid;
+            if (i < 4 * Q) er[(i & 3) * Q + (i >> 2)] = engine_expf(__fsub_rn(vv[u], m));
+            if (i < V && !b2[u] && vv[u] > -1e30f) {
+                nl++;
+                best = umin64(best, cand_key(vv[u], i));
+            }
         }
     }
-    nl = warp_sum_i(nl);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) nl += __shfl_xor_sync(FULL, nl, o);
     if (lane == 0) redi[warp] = nl;
     __syncthreads();
-    int live = 0;
-    for (int w = 0; w < THREADS / 32; w++) live += redi[w];
+    int live = redi[0];
+    for (int w = 1; w < CSEL_THREADS / 32; w++) live += redi[w];
     const int K = min(k, live);
-    // At least K live keys are at or below the K-th smallest of the threads'
-    // best keys: those keys are the candidates, usually a few hundred.
-    const unsigned long long sorted_best = bitonic_1024(best, skey);
-    if (tid == K - 1) s_prefix = sorted_best;
-    if (tid == 0) s_count = 0;
-    __syncthreads();
-    const unsigned long long t0 = K > 0 ? s_prefix : 0ull;
-    if (K > 0) {
-#pragma unroll
-        for (int j = 0; j < VPT; j++) {
-            const int i = tid + j * THREADS;
-            if (i < V && v[j] > -1e30f) {
-                const unsigned long long key = cand_key(v[j], i);
-                if (key <= t0) {
-                    const int slot = atomicAdd(&s_count, 1);
-                    if (slot < CAND_CAP) skey[slot] = key;
-                }
-            }
-        }
-    }
-    __syncthreads();
-    const int C = s_count;
     int32_t* out = ids + (size_t)s * k;
-    if (K > 0 && C <= CAND_CAP) {
-        const unsigned long long mine = tid < C ? skey[tid] : ~0ull;
-        const unsigned long long kt = bitonic_1024(mine, skey);
-        if (tid < K) out[tid] = (int32_t)(kt & 0xffffu);
-    } else if (K > 0) {
-        // the K-th smallest key by six 8-bit radix passes (histogram atomics
-        // aggregated per warp over equal bins), then the keys at or below it
-        unsigned long long prefix = 0ull, pmask = 0ull;
-        int rem = K;
-        for (int pass = 0; pass < 6; pass++) {
-            const int shift = 40 - 8 * pass;
-            for (int b = tid; b < 256; b += THREADS) hist[b] = 0u;
-            __syncthreads();
+    if (K > 0) {
+        // the threads' best keys sorted (shuffles below stride 32, shared
+        // memory above); at least K keys lie at or below the K-th of them
+        unsigned long long key = best;
 #pragma unroll
-            for (int j = 0; j < VPT; j++) {
-                const int i = tid + j * THREADS;
-                bool act = false;
-                unsigned bin = 0;
-                if (i < V && v[j] > -1e30f) {
-                    const unsigned long long key = cand_key(v[j], i);
-                    act = (key & pmask) == prefix;
-                    bin = (unsigned)(key >> shift) & 255u;
+        for (int size = 2; size <= CSEL_THREADS; size <<= 1) {
+            const bool asc = (tid & size) == 0;
+#pragma unroll
+            for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                unsigned long long o;
+                if (stride >= 32) {
+                    __syncthreads();
+                    sk[tid] = key;
+                    __syncthreads();
+                    o = sk[tid ^ stride];
+                } else {
+                    o = __shfl_xor_sync(FULL, key, stride);
                 }
-                const unsigned am = __ballot_sync(0xffffffffu, act);
-                if (act) {
-                    const unsigned same = __match_any_sync(am, bin);
-                    if (lane == __ffs(same) - 1) atomicAdd(&hist[bin], (unsigned)__popc(same));
-                }
+                key = (((tid & stride) == 0) == asc) ? umin64(key, o) : umax64(key, o);
             }
-            __syncthreads();
-            if (warp == 0) {
-                unsigned c[8], tot = 0;
+        }
+        if (tid == K - 1) s_t0 = key;
+        __syncthreads();
+        const unsigned long long t0 = s_t0;
+        // the candidates: every live key at or below t0
+        for (int base = 0; base < V; base += STEP) {
+            float vv[CAND_UNROLL];
 #pragma unroll
-                for (int e = 0; e < 8; e++) {
-                    c[e] = hist[8 * lane + e];
-                    tot += c[e];
-                }
-                unsigned incl = tot;
+            for (int u = 0; u < CAND_UNROLL; u++) {
+                const int i = base + CSEL_THREADS * u + tid;
+                vv[u] = i < V ? cand_logit(x, a1, a2, i) : -INFINITY;
+            }
 #pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const unsigned t = __shfl_up_sync(0xffffffffu, incl, o);
-                    if (lane >= o) incl += t;
+            for (int u = 0; u < CAND_UNROLL; u++) {
+                const int i = base + CSEL_THREADS * u + tid;
+                unsigned long long kk = 0;
+                bool take = false;
+                if (vv[u] > -1e30f) {
+                    kk = cand_key(vv[u], i);
+                    take = kk <= t0;
                 }
-                const unsigned excl = incl - tot;
-                if (excl < (unsigned)rem && (unsigned)rem <= incl) {
-                    unsigned run = excl;
-                    int b = 7;
-                    for (int e = 0; e < 8; e++) {
-                        if (run + c[e] >= (unsigned)rem) { b = e; break; }
-                        run += c[e];
+                const unsigned bal = __ballot_sync(FULL, take);
+                int pos0 = 0;
+                if (lane == 0 && bal) pos0 = atomicAdd(&s_count, __popc(bal));
+                pos0 = __shfl_sync(FULL, pos0, 0);
+                const int pos = pos0 + __popc(bal & ((1u << lane) - 1u));
+                if (take && pos < CAND_BUF) sk[pos] = kk;
+            }
+        }
+        __syncthreads();
+        const int C = s_count;
+        if (C <= CAND_BUF) {
+            int n = 2;
+            while (n < C) n <<= 1;
+            for (int j = C + tid; j < n; j += CSEL_THREADS) sk[j] = ~0ull;
+            for (int size = 2; size <= n; size <<= 1)
+                for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                    __syncthreads();
+                    for (int j = tid; j < n / 2; j += CSEL_THREADS) {
+                        // pair j: the element with bit `stride` clear, and its partner
+                        const int lo = ((j & ~(stride - 1)) << 1) | (j & (stride - 1)), hi = lo | stride;
+                        const unsigned long long a = sk[lo], c = sk[hi];
+                        if ((a > c) == ((lo & size) == 0)) {
+                            sk[lo] = c;
+                            sk[hi] = a;
+                        }
                     }
-                    s_prefix = prefix | ((unsigned long long)(8 * lane + b) << shift);
-                    s_rem = rem - (int)run;
                 }
-            }
             __syncthreads();
-            prefix = s_prefix;
-            rem = s_rem;
-            pmask |= 255ull << shift;
-        }
-        if (tid == 0) s_count = 0;
-        __syncthreads();
-#pragma unroll
-        for (int j = 0; j < VPT; j++) {
-            const int i = tid + j * THREADS;
-            if (i < V && v[j] > -1e30f) {
-                const unsigned long long key = cand_key(v[j], i);
-                if (key <= prefix) {
-                    const int slot = atomicAdd(&s_count, 1);
-                    if (slot < CAND_MAXK) skey[slot] = key;
+            for (int j = tid; j < K; j += CSEL_THREADS) out[j] = (int32_t)(sk[j] & 0xffffu);
+        } else {
+            // more than CAND_BUF at or below the bound: the K smallest, one
+            // at a time
+            unsigned long long prev = 0ull;
+            for (int r = 0; r < K; r++) {
+                unsigned long long b = ~0ull;
+                for (int i = tid; i < V; i += CSEL_THREADS) {
+                    const float v = cand_logit(x, a1, a2, i);
+                    if (v > -1e30f) {
+                        const unsigned long long kk = cand_key(v, i);
+                        if ((r == 0 || kk > prev) && kk < b) b = kk;
+                    }
                 }
+#pragma unroll
+                for (int o = 16; o; o >>= 1) b = umin64(b, __shfl_xor_sync(FULL, b, o));
+                __syncthreads();
+                if (lane == 0) sk[warp] = b;
+                __syncthreads();
+                b = sk[0];
+                for (int w = 1; w < CSEL_THREADS / 32; w++) b = umin64(b, sk[w]);
+                if (tid == 0) out[r] = (int32_t)(b & 0xffffu);
+                prev = b;
             }
-        }
-        __syncthreads();
-        if (tid < K) {
-            const unsigned long long kt = skey[tid];
-            int r = 0;
-            for (int j = 0; j < K; j++) r += skey[j] < kt ? 1 : 0;
-            out[r] = (int32_t)(kt & 0xffffu);
         }
     }
-    if (tid >= K && tid < k) out[tid] = -1;
+    for (int j = K + tid; j < k; j += CSEL_THREADS) out[j] = -1;
     if (tid == 0) {
         mo[s] = m;
         live_out[s] = live;
     }
 }
 
-// One warp per sequence: lanes 0-3 sum lanes 0-3 of the exps in element
-// order, 256 elements of each lane a chunk, while the whole warp's cp.async
-// copies bring the next chunk into the other half of a shared double
-// buffer; lane 0 then forms z (agent.rs:1245-1250). A row whose lane length
-// is not a multiple of 256 is summed straight from global memory.
+// One warp per sequence (see above): lanes 0-3 add lane j's exps in order,
+// 256 of each lane a chunk, while the warp's cp.async copies bring the next
+// chunk into the other half of a shared double buffer. A row whose lane
+// length is not a multiple of 256 is summed straight from global memory.
 __global__ void __launch_bounds__(32) cand_sum_kernel(const float* ex, const float* logits, int V, const uint8_t* allow,
                                                       const float* mo, double* zo) {
     pdl_launch_dependents();
     pdl_wait();
     __shared__ __align__(16) float buf[2][4][256];
+    const unsigned FULL = 0xffffffffu;
     const int s = blockIdx.x, lane = threadIdx.x;
     const int Q = V / 4;
     const float* er = ex + (size_t)s * 4 * Q;
@@ -2242,15 +2231,14 @@ __global__ void __launch_bounds__(32) cand_sum_kernel(const float* ex, const flo
         const float* el = er + (size_t)lane * Q;
         for (int i = 0; i < Q; i++) acc = __fadd_rn(acc, el[i]);
     }
-    const float l1 = __shfl_sync(0xffffffffu, acc, 1), l2 = __shfl_sync(0xffffffffu, acc, 2),
-                l3 = __shfl_sync(0xffffffffu, acc, 3);
+    const float l1 = __shfl_sync(FULL, acc, 1), l2 = __shfl_sync(FULL, acc, 2), l3 = __shfl_sync(FULL, acc, 3);
     if (lane == 0) {
-        double z = (double)__fadd_rn(__fadd_rn(acc, l1), __fadd_rn(l2, l3));
         const float m = mo[s];
         const float* x = logits + (size_t)s * V;
         const uint8_t* a1 = allow ? allow + (size_t)s * ((V + 7) / 8) : nullptr;
+        double z = (double)__fadd_rn(__fadd_rn(acc, l1), __fadd_rn(l2, l3));
         for (int i = 4 * Q; i < V; i++) {
-            const float v = bit_clear(a1, i) ? -1e30f : x[i];
+            const float v = cand_logit(x, a1, nullptr, i);
             if (v > -1e30f) z = __dadd_rn(z, exp(__dsub_rn((double)v, (double)m)));
         }
         zo[s] = z;
@@ -2259,12 +2247,9 @@ __global__ void __launch_bounds__(32) cand_sum_kernel(const float* ex, const flo
 
 cudaError_t launch_candidates(const float* logits, int S, int V, const uint8_t* allow, const uint8_t* allow_order, int k,
                               int32_t* ids, float* m, double* z, int32_t* live, float* ex, cudaStream_t st) {
-    if (S < 1 || V < 1 || V > 32768 || k < 1 || k > CAND_MAXK) return cudaErrorInvalidValue;
+    if (S < 1 || V < 1 || V > 65536 || k < 1 || k > CAND_MAXK) return cudaErrorInvalidValue;
     add_launches(2);
-    if (V <= 16384)
-        launch_pdl(cand_select_kernel<16, 1024>, dim3(S), dim3(1024), 0, st, logits, V, allow, allow_order, k, ids, m, live, ex);
-    else
-        launch_pdl(cand_select_kernel<32, 1024>, dim3(S), dim3(1024), 0, st, logits, V, allow, allow_order, k, ids, m, live, ex);
+    launch_pdl(cand_select_kernel, dim3(S), dim3(CSEL_THREADS), 0, st, logits, V, allow, allow_order, k, ids, m, live, ex);
     launch_pdl(cand_sum_kernel, dim3(S), dim3(32), 0, st, (const float*)ex, logits, V, allow, (const float*)m, z);
     return cudaSuccess;
 }

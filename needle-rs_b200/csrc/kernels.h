@@ -136,13 +136,13 @@ void launch_record_cells(const float* xs, int S, int T, int p0, int depth, int l
 // confidence logit), out [S].
 void launch_probe_head(HeadW h, const float* cells, int S, int T, int ncap, int l1, int kind, float* r, float* pooled,
                        float* out, cudaStream_t st);
-// The call sampler's start, per row of logits [S][V] (V <= 32768): with the
+// The call sampler's start, per row of logits [S][V]: with the
 // entries whose `allow` bit is clear read as -1e30, the max m[s] and
 // z[s] = sum exp(l - m) as agent.rs:1241-1252 forms them; with those of
 // `allow_order` cleared too, live[s] = how many exceed -1e30 and ids[s][0..k)
 // the first k of them by (logit descending, id ascending) (agent.rs:335-343),
-// -1 past live. k <= 128. ex [S][V] is scratch. cudaErrorInvalidValue
-// (nothing launched) otherwise.
+// -1 past live. k <= 128, V <= 65536; ex [S][V] is scratch.
+// cudaErrorInvalidValue (nothing launched) otherwise.
 cudaError_t launch_candidates(const float* logits, int S, int V, const uint8_t* allow, const uint8_t* allow_order, int k,
                               int32_t* ids, float* m, double* z, int32_t* live, float* ex, cudaStream_t st);
 

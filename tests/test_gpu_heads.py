@@ -71,3 +71,19 @@ def test_errors(heads, small_archive, cuda_device):
     plain = nb.Model(small_archive, cuda_device)
     with pytest.raises(RuntimeError, match="no probe head"):
         plain.batch(1, 8).embed(np.zeros((1, 3), np.int32))
+
+
+def test_full_geometry_embedding_and_confidence(cuda_device):
+    """Needle 3 geometry (20 layers, 21 depths): two texts of 45 tokens."""
+    import needle_b200 as nb
+    from oracle import oracle as orc
+
+    data = _cached_archive("needle3-heads", seed=0, heads=(nb.HEAD_EMBEDDING, nb.HEAD_CONFIDENCE))
+    g, o = nb.Model(data, cuda_device), orc.Model(data)
+    ids = np.random.default_rng(45).integers(0, g.vocab, (2, 45)).astype(np.int32)
+    emb = g.batch(2, 45).embed(ids)
+    conf = g.batch(2, 45).confidence(ids)
+    for s in range(2):
+        want = o.embed(ids[s].astype(np.uint32))
+        assert np.array_equal(emb[s].view(np.uint32), want.view(np.uint32))
+        assert conf[s].view(np.uint32) == np.float32(o.confidence(ids[s].astype(np.uint32))).view(np.uint32)

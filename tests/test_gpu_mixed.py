@@ -108,3 +108,28 @@ def test_engine_refuses_mixed_widths_in_a_fused_projection(cuda_device):
 
     with pytest.raises(RuntimeError, match="code width"):
         nb.Model(nb.synth_cact(bits=dict(key=2, value=4), **SMALL), cuda_device)
+
+
+def test_full_geometry_low_width_stream(cuda_device):
+    """Needle 3 geometry with ternary attention projections, 2-bit out and
+    engram projections and 3-bit engram tables: a 70-token prompt (chunks
+    32, 32, 6) and 20 greedy steps, token-identical to the oracle; first
+    logits bit-exact."""
+    import needle_b200 as nb
+    from oracle import oracle as orc
+    from conftest import _cached_archive
+
+    data = _cached_archive("needle3-low-width", seed=0, bits=dict(q=5, k=5, v=5, gate=5, out=2, key=2, value=2, table=3))
+    g, o = nb.Model(data, cuda_device), orc.Model(data)
+    rng = np.random.default_rng(70)
+    S, n, steps = 2, 70, 20
+    prompts = rng.integers(0, g.vocab, (S, n)).astype(np.int32)
+    b = g.batch(S, n + steps + 1)
+    first = b.forward(prompts)[:, 0]
+    got = np.zeros((S, steps), np.int64)
+    for k in range(steps):
+        got[:, k] = b.step()
+    for s_ in range(S):
+        want, logits = o.generate(prompts[s_].astype(np.uint32), steps, want_logits=True)
+        assert bits_equal(first[s_], logits), describe_diff("first logits", first[s_], logits)
+        assert list(got[s_]) == list(want), f"sequence {s_}: {got[s_]} vs {want}"
