@@ -188,7 +188,7 @@ def peaks():
 # algorithmic bytes of that launch: the roofline scales the traffic to this
 # run's launch by the ratio of algorithmic bytes (sequences and keys).
 PROFILED_TRAFFIC = {
-    "attention": (35_295_744, 37_896_192),
+    "attention": (35_249_152, 37_896_192),
     "post": (22_288_896, 40_992_768),
     "qkvg": (2_047_744, 7_854_464),
     "mhc": (12_709_120, 19_857_408),

@@ -535,10 +535,26 @@ static QAct qact_new(const float* x, int rows, int in_dim) {
 static inline void lane_sums(const QMat& q, int r, int g, const QAct& a, int t, int32_t s[4]) {
     const int8_t* w = q.w8.data() + ((size_t)r * q.groups + g) * GROUP;
     const int8_t* x = a.xq.data() + ((size_t)t * a.groups + g) * GROUP;
-    for (int l = 0; l < 4; l++) s[l] = 0;
-    for (int p = 0; p < GROUP; p++) {
-        int lane = q.width == 2 ? (p % 64) / 16 : (p % 32) / 8;
-        s[lane] += (int32_t)w[p] * (int32_t)x[p];
+    if (q.width == 2) {  // lane l: p = 64h + 16l + b
+        for (int l = 0; l < 4; l++) {
+            int32_t acc = 0;
+            for (int h = 0; h < 2; h++) {
+                const int8_t* wp = w + h * 64 + l * 16;
+                const int8_t* xp = x + h * 64 + l * 16;
+                for (int b = 0; b < 16; b++) acc += (int32_t)wp[b] * (int32_t)xp[b];
+            }
+            s[l] = acc;
+        }
+        return;
+    }
+    for (int l = 0; l < 4; l++) {  // lane l: p = 32a + 8l + b
+        int32_t acc = 0;
+        for (int blk = 0; blk < 4; blk++) {
+            const int8_t* wp = w + blk * 32 + l * 8;
+            const int8_t* xp = x + blk * 32 + l * 8;
+            for (int b = 0; b < 8; b++) acc += (int32_t)wp[b] * (int32_t)xp[b];
+        }
+        s[l] = acc;
     }
 }
 
