@@ -1644,6 +1644,7 @@ struct PostRowSmem {
     float post_norm[768], pre_hada[768];
     int perm1[1024], perm2[1024];
     float x2[768], hb[768], zb[1024], mb[1024], tb[1024];
+    float x1[768], ub[768], xold[3072];  // the row's residual, u and streams
     float part[32], sc[2], wk[8], gr[24];
 };
 extern const size_t POST_ROW_SMEM = sizeof(PostRowSmem);
@@ -1690,9 +1691,15 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_row_kernel(LayerW w, con
     stage(sm.perm2, perm2, 4096, tid);
     asm volatile("cp.async.commit_group;\n" ::);
     pdl_wait();
-    const float* orow = o + (size_t)m * 768;
-    for (int c = tid; c < 768; c += POST_THREADS) sm.x2[c] = orow[c];
+    // the row's inputs in one round of copies: o, the residual x1, u, the
+    // four streams the mHC write reads, the gates
+    float* xr = xs + (size_t)m * 3072;
+    stage(sm.x2, o + (size_t)m * 768, 768 * 4, tid);
+    stage(sm.x1, x1 + (size_t)m * 768, 768 * 4, tid);
+    stage(sm.ub, u + (size_t)m * 768, 768 * 4, tid);
+    stage(sm.xold, xr, 3072 * 4, tid);
     if (tid < 24) sm.gr[tid] = gates[(size_t)m * 24 + tid];
+    asm volatile("cp.async.commit_group;\n" ::);
     asm volatile("cp.async.wait_group 0;\n" ::);
     __syncthreads();
     // zcn(o, post_norm): sixteen dot16 chains
@@ -1704,7 +1711,7 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_row_kernel(LayerW w, con
     for (int c = tid; c < 768; c += POST_THREADS) {
         float tt = __fmul_rn(sm.x2[c], sm.sc[0]);
         float on = __fmaf_rn(tt, sm.post_norm[c], tt);
-        sm.x2[c] = __fmaf_rn(on, ga, x1[(size_t)m * 768 + c]);
+        sm.x2[c] = __fmaf_rn(on, ga, sm.x1[c]);
     }
     __syncthreads();
     if (tid < 16) sm.part[tid] = dot16_chain(sm.x2, sm.x2, 768, tid);
@@ -1770,13 +1777,12 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_row_kernel(LayerW w, con
     __syncthreads();
     // mHC write (infer.rs:1587-1606): y = x2 + mlp - u, stream a =
     // y * hpost[a] + sum_b old[b] * hres[a][b]
-    float* xr = xs + (size_t)m * 3072;
     for (int ch = tid; ch < 768; ch += POST_THREADS) {
         float mlp = __fmul_rn(sm.tb[ch], sm.d4[ch]);
-        float y = __fsub_rn(__fadd_rn(sm.x2[ch], mlp), u[(size_t)m * 768 + ch]);
+        float y = __fsub_rn(__fadd_rn(sm.x2[ch], mlp), sm.ub[ch]);
         float old[4];
 #pragma unroll
-        for (int bb = 0; bb < 4; bb++) old[bb] = xr[bb * 768 + ch];
+        for (int bb = 0; bb < 4; bb++) old[bb] = sm.xold[bb * 768 + ch];
 #pragma unroll
         for (int aa = 0; aa < 4; aa++) {
             float v = __fmul_rn(y, sm.gr[aa]);
