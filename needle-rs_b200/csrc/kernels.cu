@@ -1313,15 +1313,6 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbu
     }
 }
 
-[[maybe_unused]] static int host_key_chunks(int n, bool nested) {
-    int k = nested ? 1 : 4;
-    int c = (n + 255) / 256;
-    if (k * 64 <= n && c < k) c = k;
-    int cm = c > 1 ? c : 1;
-    int ch = ((n + cm - 1) / cm + 15) / 16 * 16;
-    return ch > 0 ? (n + ch - 1) / ch : 0;
-}
-
 extern const size_t ATT_SMEM_BASE = (sizeof(AttSmem) + 15) & ~(size_t)15;
 extern const size_t ATT_SMEM = ATT_SMEM_BASE + (size_t)ATT_HEADS * ATT_MAXPARTS * 66 * 4;
 
