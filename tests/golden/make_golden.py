@@ -8,6 +8,11 @@ its first logits on the small synthetic archive the tests build
 (tests/conftest.py SMALL), so a later change to the oracle, the archive
 writer or the engine shows up against a fixed record.
 
+next_rows.json: the same kind of record for the widened rows: greedy
+streams on the mixed-width small archive (conftest MIXED_BITS), the call
+sampler's statistics and candidate order on fixed logits, and the probe
+heads' embedding and confidence digests on the small archive with heads.
+
 Run: python tests/golden/make_golden.py
 """
 
@@ -64,11 +69,60 @@ def streams():
     return out
 
 
+def digest(a):
+    return hashlib.sha256(np.ascontiguousarray(a).view(np.uint8).tobytes()).hexdigest()
+
+
+def call_sampler_logits():
+    """Four rows of 1000 logits rounded to 0.1 (many exact ties), every
+    seventh of row 1 banned (-1e30)."""
+    x = np.round(np.random.default_rng(7070).standard_normal((4, 1000)) * 3, 1).astype(np.float32)
+    x[1, ::7] = np.float32(-1e30)
+    return x
+
+
+def next_rows():
+    import needle_b200 as nb
+    from conftest import MIXED_BITS, SMALL, _cached_archive
+    from oracle import oracle as orc
+
+    out = {}
+    mixed = _cached_archive("small-mixed", bits=MIXED_BITS, **SMALL)
+    m = orc.Model(mixed)
+    rng = np.random.default_rng(2025)
+    cases = []
+    for n in (7, 40):
+        prompt = rng.integers(0, m.vocab, n).astype(np.uint32)
+        toks, logits = m.generate(prompt, 10, want_logits=True)
+        cases.append({"prompt": [int(v) for v in prompt], "tokens": [int(v) for v in toks],
+                      "first_logits_sha256": digest(logits)})
+    out["mixed_width"] = {"archive_sha256": hashlib.sha256(mixed).hexdigest(), "bits": MIXED_BITS, "cases": cases}
+    # the call sampler on fixed rows: logits rounded to 0.1 (many ties)
+    x = call_sampler_logits()
+    rows = []
+    for r in range(4):
+        mx, z = orc.softmax_stats(x[r])
+        ids, live = orc.candidate_order(x[r], 128)
+        rows.append({"m": float(mx), "z": float(z), "live": int(live), "ids": [int(v) for v in ids]})
+    out["call_sampler"] = {"logits_sha256": digest(x), "rows": rows}
+    heads = _cached_archive("small-heads", heads=(nb.HEAD_EMBEDDING, nb.HEAD_CONFIDENCE), **SMALL)
+    m = orc.Model(heads)
+    texts = []
+    for n in (3, 21):
+        ids = rng.integers(0, m.vocab, n).astype(np.uint32)
+        texts.append({"ids": [int(v) for v in ids], "embedding_sha256": digest(m.embed(ids)),
+                      "confidence": float(m.confidence(ids))})
+    out["probe_heads"] = {"archive_sha256": hashlib.sha256(heads).hexdigest(), "texts": texts}
+    return out
+
+
 def main():
     with open(os.path.join(HERE, "reference_kat.json"), "w") as f:
         json.dump(REFERENCE_KAT, f, indent=1)
     with open(os.path.join(HERE, "small_model_streams.json"), "w") as f:
         json.dump(streams(), f, indent=1)
+    with open(os.path.join(HERE, "next_rows.json"), "w") as f:
+        json.dump(next_rows(), f, indent=1)
 
 
 if __name__ == "__main__":

@@ -108,3 +108,41 @@ def test_oracle_reproduces_committed_streams(small_archive):
         toks, logits = m.generate(np.array(case["prompt"], np.uint32), len(case["tokens"]), want_logits=True)
         assert [int(t) for t in toks] == case["tokens"]
         assert hashlib.sha256(logits.view(np.uint32).tobytes()).hexdigest() == case["first_logits_sha256"]
+
+
+def test_oracle_reproduces_committed_next_rows():
+    """The oracle still produces the committed records of the widened rows
+    (tests/golden/make_golden.py wrote them): mixed-width streams, the call
+    sampler on fixed rows, the probe heads."""
+    import hashlib
+    import sys
+
+    import needle_b200 as nb
+    from conftest import MIXED_BITS, SMALL, _cached_archive
+    from oracle import oracle as orc
+
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    from make_golden import call_sampler_logits, digest
+
+    g = json.load(open(os.path.join(ROOT, "tests", "golden", "next_rows.json")))
+    mixed = _cached_archive("small-mixed", bits=MIXED_BITS, **SMALL)
+    assert hashlib.sha256(mixed).hexdigest() == g["mixed_width"]["archive_sha256"]
+    m = orc.Model(mixed)
+    for case in g["mixed_width"]["cases"]:
+        toks, logits = m.generate(np.array(case["prompt"], np.uint32), len(case["tokens"]), want_logits=True)
+        assert [int(t) for t in toks] == case["tokens"]
+        assert digest(logits) == case["first_logits_sha256"]
+    x = call_sampler_logits()
+    assert digest(x) == g["call_sampler"]["logits_sha256"]
+    for r, row in enumerate(g["call_sampler"]["rows"]):
+        mx, z = orc.softmax_stats(x[r])
+        ids, live = orc.candidate_order(x[r], 128)
+        assert float(mx) == row["m"] and float(z) == row["z"] and live == row["live"]
+        assert [int(v) for v in ids] == row["ids"]
+    heads = _cached_archive("small-heads", heads=(nb.HEAD_EMBEDDING, nb.HEAD_CONFIDENCE), **SMALL)
+    assert hashlib.sha256(heads).hexdigest() == g["probe_heads"]["archive_sha256"]
+    m = orc.Model(heads)
+    for t in g["probe_heads"]["texts"]:
+        ids = np.array(t["ids"], np.uint32)
+        assert digest(m.embed(ids)) == t["embedding_sha256"]
+        assert float(m.confidence(ids)) == t["confidence"]
