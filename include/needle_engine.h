@@ -56,6 +56,16 @@ void nd_batch_free(nd_batch* b);
 /* model.rs:72-74 (Session::len): positions every sequence has been fed. */
 int nd_batch_len(const nd_batch* b);
 
+/* Session::attend (crates/needle-engine/src/model.rs:63-66, infer.rs:
+ * 1749-1825) for every sequence of the batch: each query sees the first
+ * `sink` positions within its layer's band, then the positions from
+ * max(chunk end - ring, sink) on (the engine's ring, which the band does
+ * not cut), as the agent sets it (agent.rs:583-588: sink = the static
+ * prefix, ring = the header's kv_window). ring = 0 restores plain
+ * attention. Rollbacks are not served, so every position in those runs
+ * still holds its keys (the batch's cache keeps all max_len positions). */
+int nd_batch_set_attend(nd_batch* b, int sink, int ring);
+
 /* model.rs:304-306 (Model::forward) through infer.rs:1105-1131
  * (forward_native): feed ids[S][t] to every sequence in the engine's chunks
  * of at most 32, writing `outputs` to out (may be NULL for ND_OUT_NONE).

@@ -457,6 +457,9 @@ struct Batch {
     int len = 0;          // positions fed to every sequence
     int hist_base = 0;    // first position whose pre-tap row the conv may read
     bool rope_valid = false;
+    // the attention span (sink, ring) of every sequence (model.rs:63-66);
+    // ring 0: none
+    int attend_sink = 0, attend_ring = 0;
     bool have_logits = false;
     int logits_rows = 0;
     int debug_layer = -1;
@@ -662,7 +665,7 @@ static int chunk(Batch& b, const int32_t* ids, int T, int outputs) {
         launch_conv_rope_kv(w, l, b.proj, b.c, S, T, p0, b.hist_base, b.cosr, b.sinr, b.qbuf, st);
         tick(b, ND_SITE_CONV);
         tick(b, ND_SITE_ATTENTION);
-        launch_attention(b.qbuf, b.proj, b.c, l, S, T, p0, c.window(l), b.att, b.act, b.sx, st);
+        launch_attention(b.qbuf, b.proj, b.c, l, S, T, p0, c.window(l), b.attend_sink, b.attend_ring, b.att, b.act, b.sx, st);
         tick(b, ND_SITE_ATTENTION);
         tick(b, ND_SITE_OUT);
         linear(m.out[l], b.act, b.sx, M, T, b.o, 768, st);
@@ -812,6 +815,28 @@ int nd_batch_new(nd_model* mh, int num_seqs, int max_len, nd_batch** out) {
 void nd_batch_free(nd_batch* b) { delete b; }
 
 int nd_batch_len(const nd_batch* b) { return b ? b->b->len : -1; }
+
+int nd_batch_set_attend(nd_batch* bh, int sink, int ring) {
+    try {
+        if (!bh) throw std::runtime_error("nd_batch_set_attend: null argument");
+        if (sink < 0 || ring < 0) throw std::runtime_error("nd_batch_set_attend: sink and ring must be non-negative");
+        Batch& b = *bh->b;
+        CK(cudaSetDevice(b.m->device));
+        if (b.attend_sink == (ring > 0 ? sink : 0) && b.attend_ring == ring) return 0;
+        // the captured decode steps bake the span into their launches
+        CK(cudaStreamSynchronize(b.st));
+        for (StepGraph& g : b.graph)
+            if (g.exec) {
+                cudaGraphExecDestroy(g.exec);
+                g.exec = nullptr;
+            }
+        b.attend_sink = ring > 0 ? sink : 0;
+        b.attend_ring = ring;
+        return 0;
+    } catch (std::exception& e) {
+        return fail(e);
+    }
+}
 
 void* nd_batch_stream(nd_batch* b) { return b ? (void*)b->b->st : nullptr; }
 

@@ -590,8 +590,8 @@ __global__ void post_row_kernel(LayerW w, const float* o, const float* x1, const
                                 const int32_t* perm2, float* xs);
 __global__ void post_block_kernel(LayerW w, const float* o, const float* x1, const float* u, const float* gates,
                                   const int32_t* perm1, const int32_t* perm2, int M, float* xs);
-__global__ void attention_kernel(const float* qbuf, const float* proj, Caches c, int l, int T, const int32_t* p0p, int window, float* att,
-                                 int8_t* act, float* sx);
+__global__ void attention_kernel(const float* qbuf, const float* proj, Caches c, int l, int T, const int32_t* p0p, int window,
+                                 int sink, int ring, float* att, int8_t* act, float* sx);
 
 
 // ---------------------------------------------------------------- engram
@@ -1098,7 +1098,7 @@ __device__ __forceinline__ void key_chunks_dev(int n, bool nested, int* count, i
 // offset within its first group, zero outside the chunk. Per-chunk parts
 // live in dynamic shared memory sized for the longest key list of the
 // launch.
-constexpr int ATT_HEADS = 6, ATT_THREADS = ATT_HEADS * 32, ATT_MAXGROUPS = ATT_MAXCHUNK / 4 + 2;
+constexpr int ATT_HEADS = 6, ATT_THREADS = ATT_HEADS * 32, ATT_MAXGROUPS = ATT_MAXCHUNK / 4 + 4;
 struct AttSmem {
     int8_t k[ATT_MAXCHUNK][48];
     int vg[ATT_MAXGROUPS][64];
@@ -1112,7 +1112,8 @@ struct AttSmem {
 };
 
 __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbuf, const float* proj, Caches c, int l, int T,
-                                                                const int32_t* p0p, int window, float* att, int8_t* act, float* sx) {
+                                                                const int32_t* p0p, int window, int sink, int ring, float* att,
+                                                                int8_t* act, float* sx) {
     pdl_launch_dependents();
     pdl_wait();
     const int p0 = *p0p;
@@ -1121,8 +1122,37 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbu
     const int m = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x, lane = tid & 31, h = tid >> 5;
     const int s = m / T, i = m % T, pos = p0 + i;
     const bool nested = T > 1;
+    // infer.rs:1781-1825 (key_ranges): the keys as runs of positions, A =
+    // [aS, aE) then B = [bS, bE). Without an attention span A is the layer's
+    // band; with one, A is the sink within the band and B the ring as of
+    // the chunk's end (not cut by the band, as the engine has it). The cache
+    // keeps every position, so no key of these runs has lost its slot.
     const int lo = window > 0 ? max(0, pos + 1 - window) : 0;
-    const int n = pos + 1 - lo;
+    int aE = pos + 1, bS = 0, bE = 0;
+    if (ring > 0) {
+        aE = max(lo, min(sink, pos + 1));
+        bS = min(max(max(0, p0 + T - ring), sink), pos + 1);
+        bE = pos + 1;
+    }
+    const int lenA = aE - lo, n = lenA + (bE - bS);
+    // a chunk's keys [c0, c0 + len) as a segment of A (positions pA ..,
+    // nA keys) then one of B (positions pB .., nB keys), with the value
+    // groups each spans
+    struct Seg {
+        int nA, pA, gA0, ngA, nB, pB, gB0, ngB;
+    };
+    auto seg = [&](int c0, int len) {
+        Seg g;
+        g.nA = max(0, min(c0 + len, lenA) - c0);
+        g.pA = lo + c0;
+        g.gA0 = g.pA >> 2;
+        g.ngA = g.nA > 0 ? ((g.pA + g.nA - 1) >> 2) - g.gA0 + 1 : 0;
+        g.nB = len - g.nA;
+        g.pB = bS + max(c0, lenA) - lenA;
+        g.gB0 = g.pB >> 2;
+        g.ngB = g.nB > 0 ? ((g.pB + g.nB - 1) >> 2) - g.gB0 + 1 : 0;
+        return g;
+    };
     int count, chunk;
     key_chunks_dev(n, nested, &count, &chunk);
     float* parts = reinterpret_cast<float*>(att_raw + ((sizeof(AttSmem) + 15) & ~(size_t)15)) + (size_t)h * count * 66;
@@ -1130,21 +1160,22 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbu
     const size_t kvrow = (((size_t)s * c.L + l) * 2 + kvh) * c.cap;
     const int8_t* k8 = c.k8 + kvrow * 48;
     const int8_t* v8 = c.v8 + (((size_t)s * c.L + l) * 2 + kvh) * c.vgroups * 256;
-    // the copies of chunk ci: key rows, value groups, scales
+    // the copies of chunk ci: key rows, value groups (A's, then B's), scales
     auto issue_chunk = [&](int ci) {
-        const int c0 = ci * chunk, len = min(chunk, n - c0), base = lo + c0;
-        const int g0 = base >> 2, ng = ((base + len - 1) >> 2) - g0 + 1;
+        const int c0 = ci * chunk, len = min(chunk, n - c0);
+        const Seg g = seg(c0, len);
         for (int idx = tid; idx < len * 3; idx += ATT_THREADS) {
-            const int k = idx / 3, part = idx % 3;
-            cp_async16(&sm.k[k][part * 16], k8 + (size_t)(base + k) * 48 + part * 16, true);
+            const int k = idx / 3, part = idx % 3, p = k < g.nA ? g.pA + k : g.pB + k - g.nA;
+            cp_async16(&sm.k[k][part * 16], k8 + (size_t)p * 48 + part * 16, true);
         }
-        for (int idx = tid; idx < ng * 16; idx += ATT_THREADS) {
-            const int g = idx >> 4, part = idx & 15;
-            cp_async16(&sm.vg[g][part * 4], v8 + (size_t)(g0 + g) * 256 + part * 16, true);
+        for (int idx = tid; idx < (g.ngA + g.ngB) * 16; idx += ATT_THREADS) {
+            const int w = idx >> 4, part = idx & 15, src = w < g.ngA ? g.gA0 + w : g.gB0 + w - g.ngA;
+            cp_async16(&sm.vg[w][part * 4], v8 + (size_t)src * 256 + part * 16, true);
         }
         for (int k = tid; k < len; k += ATT_THREADS) {
-            cp_async4(&sm.ks[k], c.ks + kvrow + base + k);
-            cp_async4(&sm.vs[k], c.vs + kvrow + base + k);
+            const int p = k < g.nA ? g.pA + k : g.pB + k - g.nA;
+            cp_async4(&sm.ks[k], c.ks + kvrow + p);
+            cp_async4(&sm.vs[k], c.vs + kvrow + p);
         }
         asm volatile("cp.async.commit_group;\n" ::);
     };
@@ -1167,7 +1198,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbu
     float* srow = sm.s[h];
     for (int ci = 0; ci < count; ci++) {
         const int c0 = ci * chunk, len = min(chunk, n - c0), blocked = len / 4 * 4;
-        const int base = lo + c0, off = base & 3, ng = ((base + len - 1) >> 2) - (base >> 2) + 1;
+        const Seg sg = seg(c0, len);
+        const int ng = sg.ngA + sg.ngB;
         asm volatile("cp.async.wait_group 0;\n" ::);
         __syncthreads();
         // scores: (ks * dot) * qs in whole 4-blocks, (ks * qs) * dot after
@@ -1236,8 +1268,17 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbu
         wm = warp_max(wm);
         const float qw = __fdiv_rn(ND_Q21, wm);
         for (int kk = lane; kk < 4 * ng; kk += 32) {
-            const int k = kk - off;
-            int wq = k >= 0 && k < len ? (int)roundf(__fmul_rn(srow[k], qw)) : 0;
+            // the key (chunk index) at byte kk & 3 of group word kk >> 2
+            const int w = kk >> 2, j = kk & 3;
+            int k = -1;
+            if (w < sg.ngA) {
+                const int p = (sg.gA0 + w) * 4 + j;
+                if (p >= sg.pA && p < sg.pA + sg.nA) k = p - sg.pA;
+            } else {
+                const int p = (sg.gB0 + w - sg.ngA) * 4 + j;
+                if (p >= sg.pB && p < sg.pB + sg.nB) k = sg.nA + p - sg.pB;
+            }
+            int wq = k >= 0 ? (int)roundf(__fmul_rn(srow[k], qw)) : 0;
             int8_t* dg = sm.dig[h] + (kk >> 2) * 16 + (kk & 3);
             dg[0] = (int8_t)(wq >> 14);
             dg[4] = (int8_t)((wq >> 7) & 127);
@@ -1316,20 +1357,21 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbu
 extern const size_t ATT_SMEM_BASE = (sizeof(AttSmem) + 15) & ~(size_t)15;
 extern const size_t ATT_SMEM = ATT_SMEM_BASE + (size_t)ATT_HEADS * ATT_MAXPARTS * 66 * 4;
 
-void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int S, int T, int p0, int window, float* att,
-                      int8_t* act, float* sx, cudaStream_t st) {
+void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int S, int T, int p0, int window, int sink,
+                      int ring, float* att, int8_t* act, float* sx, cudaStream_t st) {
     COUNT_LAUNCH();
     // key_chunks gives at most c = max(ceil(n / 256), k if n >= 64 k) chunks,
     // and the launch's longest key list is its last row's
     // sized for the batch's capacity, so a captured step stays valid at
     // every later position
     int nmax = c.cap;
-    if (window > 0 && window < nmax) nmax = window;
+    if (window > 0 && window < nmax && ring == 0) nmax = window;
     int most = std::max(1, (nmax + 255) / 256);
     if (T == 1 && nmax >= 256) most = std::max(most, 4);
     most = std::min(most, ATT_MAXPARTS);
     size_t smem = ATT_SMEM_BASE + (size_t)ATT_HEADS * most * 66 * 4;
-    launch_pdl(attention_kernel, dim3(dim3(S * T, 2)), dim3(ATT_THREADS), smem, st, qbuf, proj, c, l, T, c.len, window, att, act, sx);
+    launch_pdl(attention_kernel, dim3(dim3(S * T, 2)), dim3(ATT_THREADS), smem, st, qbuf, proj, c, l, T, c.len, window, sink, ring,
+               att, act, sx);
 }
 
 // ------------------------------------------------------------ post block

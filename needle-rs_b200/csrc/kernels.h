@@ -115,8 +115,10 @@ void launch_mhc_read(LayerW w, int lane, const float* xs, int M, float* u, float
 void launch_mhc_gates(LayerW w, int lane, int M, float* gates, cudaStream_t st);
 void launch_conv_rope_kv(LayerW w, int l, const float* proj, Caches c, int S, int T, int p0, int hist_base, const float* cosr,
                          const float* sinr, float* qbuf, cudaStream_t st);
-void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int S, int T, int p0, int window, float* att,
-                      int8_t* act, float* sx, cudaStream_t st);
+// window: the layer's band (0 = all); sink, ring: the attention span
+// (ring 0 = none; infer.rs:1749-1825).
+void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int S, int T, int p0, int window, int sink,
+                      int ring, float* att, int8_t* act, float* sx, cudaStream_t st);
 void launch_post_block(LayerW w, const float* o, const float* x1, const float* u, const float* gates, const int32_t* perm1,
                        const int32_t* perm2, int M, float* xs, cudaStream_t st);
 void launch_final_hidden(const float* xs, const float* final_norm, int S, int T, int all_rows, float* h, cudaStream_t st);

@@ -61,6 +61,7 @@ __device__ __forceinline__ float dot16_chain(const float* x, const float* y, int
 // (qlinear.rs:113-140).
 __device__ __forceinline__ int8_t q8_round(float v, float inv) {
     float r = roundf(__fmul_rn(v, inv));
+    if (r != r) return 0;  // NaN: Rust's saturating `as i8` (and NEON's fcvtas) give 0
     r = fminf(fmaxf(r, -128.f), 127.f);
     return (int8_t)(int)r;
 }

@@ -37,6 +37,7 @@ def lib():
             "nd_batch_new": (I, [P, I, I, C.POINTER(P)]),
             "nd_batch_free": (None, [P]),
             "nd_batch_len": (I, [P]),
+            "nd_batch_set_attend": (I, [P, I, I]),
             "nd_batch_forward": (I, [P, P, I, I, P, I]),
             "nd_batch_step": (I, [P, P, P, I]),
             "nd_batch_last_hidden": (I, [P, P, I]),
@@ -254,6 +255,12 @@ class Batch:
 
     def __len__(self):
         return lib().nd_batch_len(self._h)
+
+    def set_attend(self, sink, ring):
+        """Session::attend for every sequence (model.rs:63-66): the first
+        `sink` positions and the ring of the last `ring`; ring 0 = none."""
+        if lib().nd_batch_set_attend(self._h, sink, ring) != 0:
+            raise _err()
 
     @property
     def stream(self) -> int:

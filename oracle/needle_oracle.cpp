@@ -153,7 +153,7 @@ float quant_i8(const float* x, int n, int8_t* q) {
     for (int i = 0; i < n; i++) {
         float v = rround(x[i] * inv);
         v = std::min(std::max(v, -128.f), 127.f);
-        q[i] = (int8_t)v;
+        q[i] = v != v ? 0 : (int8_t)v;  // NaN: Rust's saturating `as i8` gives 0
     }
     return s;
 }
@@ -1349,7 +1349,8 @@ static void layer_native(const Model& m, int l, Session& st, int64_t p0, std::ve
     }
     int64_t end = p0 + t;
     {
-        int64_t need = slot_of(end - 1, st) + 1;
+        int64_t need = 0;  // the largest slot the chunk writes (the ring may wrap inside it)
+        for (int64_t p = p0; p < end; p++) need = std::max(need, slot_of(p, st) + 1);
         if ((int64_t)ls.ks.size() < need * nkv) {
             ls.k8.resize(need * nkv * qk, 0);
             ls.ks.resize(need * nkv, 0.f);

@@ -233,3 +233,37 @@ def test_oracle_forward_is_deterministic_and_chunked(small_archive):
     c.forward(ids[:30], orc.OUT_NONE)
     d = c.forward(ids[30:])
     assert not np.array_equal(a.view(np.uint32), d.view(np.uint32)), "chunk boundaries change the arithmetic"
+
+
+def test_attention_span_identity_and_ring_wrap():
+    """Session::attend in the oracle (infer.rs:1749-1825): with every layer
+    global, a sink of 0 and a ring longer than the feed, the span is plain
+    attention; a ring that wraps inside a 32-token chunk (slots reused)
+    runs and is deterministic."""
+    import needle_b200 as nb
+    from conftest import SMALL
+
+    shape = dict(SMALL)
+    shape.update(sliding_window=0, global_layers=())
+    m = orc.Model(nb.synth_cact(**shape))
+    ids = (np.arange(45) * 29 % 1000).astype(np.uint32)
+    plain = m.session().forward(ids)[0]
+    s = m.session()
+    s.set_attend(0, 1 << 20)
+    assert np.array_equal(s.forward(ids)[0].view(np.uint32), plain.view(np.uint32))
+    outs = []
+    for _ in range(2):
+        s = m.session()
+        s.set_attend(5, 20)
+        outs.append(s.forward(ids)[0])
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    assert not np.array_equal(outs[0], plain)
+
+
+def test_quant_i8_nan_is_zero():
+    """A NaN input quantizes to 0, as Rust's saturating `as i8` (and NEON's
+    fcvtas) have it: the attention of a row with no visible key under an
+    attention span (0/0) reaches the out projection's A8 this way."""
+    x = np.array([1.0, np.nan, -2.0, 0.5], np.float32)
+    q, s = orc.quant_i8(x)
+    assert q[1] == 0 and q[0] == 64 and q[2] == -127
