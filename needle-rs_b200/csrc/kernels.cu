@@ -1267,16 +1267,17 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbu
         }
         wm = warp_max(wm);
         const float qw = __fdiv_rn(ND_Q21, wm);
+        const int offA = sg.pA & 3;
         for (int kk = lane; kk < 4 * ng; kk += 32) {
-            // the key (chunk index) at byte kk & 3 of group word kk >> 2
-            const int w = kk >> 2, j = kk & 3;
-            int k = -1;
-            if (w < sg.ngA) {
-                const int p = (sg.gA0 + w) * 4 + j;
-                if (p >= sg.pA && p < sg.pA + sg.nA) k = p - sg.pA;
+            // the key (chunk index) at byte kk & 3 of group word kk >> 2:
+            // A's groups hold keys kk - offA, B's (after A's) the rest
+            int k;
+            if (kk < 4 * sg.ngA) {
+                k = kk - offA;
+                if (k < 0 || k >= sg.nA) k = -1;
             } else {
-                const int p = (sg.gB0 + w - sg.ngA) * 4 + j;
-                if (p >= sg.pB && p < sg.pB + sg.nB) k = sg.nA + p - sg.pB;
+                const int kb = kk - 4 * sg.ngA - (sg.pB & 3);
+                k = kb >= 0 && kb < sg.nB ? sg.nA + kb : -1;
             }
             int wq = k >= 0 ? (int)roundf(__fmul_rn(srow[k], qw)) : 0;
             int8_t* dg = sm.dig[h] + (kk >> 2) * 16 + (kk & 3);
