@@ -66,6 +66,26 @@ int nd_batch_len(const nd_batch* b);
  * still holds its keys (the batch's cache keeps all max_len positions). */
 int nd_batch_set_attend(nd_batch* b, int sink, int ring);
 
+/* Session::rollback (model.rs:81-113, infer.rs:1055-1077): drop the last
+ * n <= 32 positions of every sequence without recomputing; the next feed
+ * continues from there (conv and engram histories, RoPE rows and KV of the
+ * kept positions stay). Fails, changing nothing, when under the batch's
+ * attention span a kept position's ring slot holds a dropped position (the
+ * reference would skip that key and re-feed it, which is not served). */
+int nd_batch_rollback(nd_batch* b, int n);
+
+/* Session::rewind_zeroed (model.rs:116-126, infer.rs:1039-1053): forget
+ * positions len.. as the engine's context-overflow re-feed does: the KV
+ * cache keeps what it holds, the conv history and RoPE rows start over.
+ * The same refusal as nd_batch_rollback. */
+int nd_batch_rewind_zeroed(nd_batch* b, int len);
+
+/* Session::truncate (model.rs:128-145): drop everything past len; up to 32
+ * positions by nd_batch_rollback, more by feeding the first len tokens to
+ * fresh sessions again (which, as in the reference, have no attention
+ * span). */
+int nd_batch_truncate(nd_batch* b, int len);
+
 /* model.rs:304-306 (Model::forward) through infer.rs:1105-1131
  * (forward_native): feed ids[S][t] to every sequence in the engine's chunks
  * of at most 32, writing `outputs` to out (may be NULL for ND_OUT_NONE).

@@ -460,6 +460,11 @@ struct Batch {
     // the attention span (sink, ring) of every sequence (model.rs:63-66);
     // ring 0: none
     int attend_sink = 0, attend_ring = 0;
+    // the reference's slot map (infer.rs:1015-1023, 1768-1776): the
+    // position each KV slot last received, kept on the host to tell when a
+    // rollback would leave a kept position's slot to a dropped one
+    std::vector<int64_t> slot_pos;
+    int rope_from = 0;  // first position whose RoPE row the ring still holds
     bool have_logits = false;
     int logits_rows = 0;
     int debug_layer = -1;
@@ -570,7 +575,7 @@ static Batch* batch_new(Model* m, int S, int max_len) {
     b.evals = b.alloc<float>((size_t)std::max(nsites, 1) * M * 768);
     b.cosr = b.alloc<float>(32 * 24);
     b.sinr = b.alloc<float>(32 * 24);
-    b.rope_state = b.alloc<float>(48);
+    b.rope_state = b.alloc<float>((size_t)ROPE_RING * 48);
     b.h = b.alloc<float>(M * 768);
     b.act = b.alloc<int8_t>(M * 768);
     b.sx = b.alloc<float>(M * 8);
@@ -615,6 +620,30 @@ static void snap(Batch& b, const char* name, const float* src, size_t n) {
     CK(cudaMemcpyAsync(b.snaps[name].first, src, n * sizeof(float), cudaMemcpyDeviceToDevice, b.st));
 }
 
+// infer.rs:1749-1754: the KV slot of position p under the batch's span.
+static int64_t slot_of(const Batch& b, int64_t p) {
+    if (b.attend_ring > 0 && p >= b.attend_sink) return (p - b.attend_sink) % b.attend_ring + b.attend_sink;
+    return p;
+}
+
+// infer.rs:1768-1776: positions p0 .. p0 + T now hold their slots.
+static void mark_slots(Batch& b, int64_t p0, int T) {
+    for (int64_t p = p0; p < p0 + T; p++) {
+        const int64_t sl = slot_of(b, p);
+        if ((int64_t)b.slot_pos.size() <= sl) b.slot_pos.resize(sl + 1, -1);
+        b.slot_pos[sl] = p;
+    }
+}
+
+// Whether dropping positions len.. would leave a kept position (< len)
+// whose slot a dropped one holds: the reference then skips that key and
+// re-feeds from it (infer.rs:1078-1100), which this engine does not serve.
+static bool stale_below(const Batch& b, int64_t len) {
+    for (size_t sl = 0; sl < b.slot_pos.size(); sl++)
+        if (b.slot_pos[sl] >= len && (int64_t)sl < len) return true;
+    return false;
+}
+
 // infer.rs:1168-1240 (chunk_native) for every sequence's chunk of T tokens
 // at positions len .. len + T - 1; ids are device int32 [S][T].
 static int chunk(Batch& b, const int32_t* ids, int T, int outputs) {
@@ -624,6 +653,7 @@ static int chunk(Batch& b, const int32_t* ids, int T, int outputs) {
     cudaStream_t st = b.st;
     if (p0 + T > b.cap) throw std::runtime_error("sequence exceeds the batch's max_len");
     launch_write_tokens(ids, S, T, p0, b.c, st);
+    mark_slots(b, p0, T);
     // infer.rs:1720: the recurrence serves one token right after the newest
     launch_rope_rows(m.rope_cos, m.rope_sin, m.sd, m.cd, b.d_len, T, (T == 1 && b.rope_valid) ? 1 : 0, b.rope_state, b.cosr,
                      b.sinr, st);
@@ -816,6 +846,92 @@ void nd_batch_free(nd_batch* b) { delete b; }
 
 int nd_batch_len(const nd_batch* b) { return b ? b->b->len : -1; }
 
+// The positions every sequence has been fed, on the host and the device.
+static void set_len(Batch& b, int len) {
+    b.len = len;
+    CK(cudaMemcpyAsync(b.d_len, &b.len, sizeof(int32_t), cudaMemcpyHostToDevice, b.st));
+    CK(cudaStreamSynchronize(b.st));
+    b.have_logits = false;
+}
+
+int nd_batch_rollback(nd_batch* bh, int n) {
+    try {
+        if (!bh) throw std::runtime_error("nd_batch_rollback: null argument");
+        Batch& b = *bh->b;
+        CK(cudaSetDevice(b.m->device));
+        if (n < 0 || n > 32) throw std::runtime_error("rollback of " + std::to_string(n) + " exceeds 32");
+        if (n > b.len) throw std::runtime_error("rollback past the start of the sequence");
+        if (n == 0) return 0;
+        const int L = b.len - n;
+        if (stale_below(b, L))
+            throw std::runtime_error("the rollback leaves kept positions' ring slots to dropped ones (not served)");
+        // infer.rs:1055-1077: the conv rows and engram history of positions
+        // below L stay (the rings hold 32 positions more than a step reads),
+        // as do the RoPE rows; a start before the conv history's start moves
+        // it back, since the dropped positions are fed again
+        b.hist_base = std::min(b.hist_base, L);
+        b.rope_valid = L > 0 && L - 1 >= b.rope_from;
+        set_len(b, L);
+        return 0;
+    } catch (std::exception& e) {
+        return fail(e);
+    }
+}
+
+int nd_batch_rewind_zeroed(nd_batch* bh, int len) {
+    try {
+        if (!bh) throw std::runtime_error("nd_batch_rewind_zeroed: null argument");
+        Batch& b = *bh->b;
+        CK(cudaSetDevice(b.m->device));
+        if (len < 0 || len > b.len) throw std::runtime_error("rewind position outside [0, len]");
+        if (stale_below(b, len))
+            throw std::runtime_error("the rewind leaves kept positions' ring slots to dropped ones (not served)");
+        // infer.rs:1039-1053: KV slots and slot map stay, the conv history
+        // starts over (the next chunk reads zeros), the RoPE rows are dropped
+        b.hist_base = len;
+        b.rope_valid = false;
+        b.rope_from = len;
+        set_len(b, len);
+        return 0;
+    } catch (std::exception& e) {
+        return fail(e);
+    }
+}
+
+int nd_batch_truncate(nd_batch* bh, int len) {
+    try {
+        if (!bh) throw std::runtime_error("nd_batch_truncate: null argument");
+        Batch& b = *bh->b;
+        CK(cudaSetDevice(b.m->device));
+        if (len < 0) throw std::runtime_error("truncate to a negative length");
+        if (len >= b.len) return 0;
+        if (b.len - len <= 32) {
+            if (nd_batch_rollback(bh, b.len - len) != 0) throw std::runtime_error(g_err);
+            return 0;
+        }
+        // model.rs:128-145: a fresh session (no attention span) fed the
+        // first len tokens again
+        int32_t* ids = nullptr;
+        CK(cudaMallocAsync((void**)&ids, (size_t)b.S * std::max(len, 1) * sizeof(int32_t), b.st));
+        if (len > 0)
+            CK(cudaMemcpy2DAsync(ids, len * sizeof(int32_t), b.c.tokens, (size_t)b.cap * sizeof(int32_t), len * sizeof(int32_t), b.S,
+                                 cudaMemcpyDeviceToDevice, b.st));
+        if (nd_batch_set_attend(bh, 0, 0) != 0) throw std::runtime_error(g_err);
+        b.slot_pos.clear();
+        b.hist_base = 0;
+        b.rope_valid = false;
+        b.rope_from = 0;
+        set_len(b, 0);
+        if (len > 0) forward(b, ids, len, ND_OUT_NONE);
+        CK(cudaFreeAsync(ids, b.st));
+        CK(cudaStreamSynchronize(b.st));
+        b.have_logits = false;
+        return 0;
+    } catch (std::exception& e) {
+        return fail(e);
+    }
+}
+
 int nd_batch_set_attend(nd_batch* bh, int sink, int ring) {
     try {
         if (!bh) throw std::runtime_error("nd_batch_set_attend: null argument");
@@ -918,6 +1034,7 @@ int nd_batch_step(nd_batch* bh, const unsigned char* allow_bits, int* next_ids, 
             } else {
                 CK(cudaGraphLaunch(g.exec, b.st));
                 add_launches(g.kernels);
+                mark_slots(b, b.len, 1);
                 b.len += 1;
                 b.last_T = 1;
                 b.last_rows = b.S;

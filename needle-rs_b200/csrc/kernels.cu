@@ -1882,7 +1882,8 @@ __global__ void rope_rows_kernel(const float* tc, const float* tsn, const float*
     if (f >= 24) return;
     float cv, sv;
     if (recur) {
-        float c0 = state[f], s0 = state[24 + f];
+        const float* r = state + (size_t)((p0 - 1) % ROPE_RING) * 48;
+        float c0 = r[f], s0 = r[24 + f];
         cv = __fmaf_rn(-sd[f], s0, __fmul_rn(cd[f], c0));
         sv = __fmaf_rn(sd[f], c0, __fmul_rn(cd[f], s0));
     } else {
@@ -1891,10 +1892,9 @@ __global__ void rope_rows_kernel(const float* tc, const float* tsn, const float*
     }
     cosr[i * 24 + f] = cv;
     sinr[i * 24 + f] = sv;
-    if (i == T - 1) {
-        state[f] = cv;
-        state[24 + f] = sv;
-    }
+    float* w = state + (size_t)((p0 + i) % ROPE_RING) * 48;
+    w[f] = cv;
+    w[24 + f] = sv;
 }
 
 void launch_rope_rows(const float* table_cos, const float* table_sin, const float* sd, const float* cd, const int32_t* p0p, int T,

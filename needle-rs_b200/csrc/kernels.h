@@ -78,6 +78,11 @@ constexpr int HIST_RING = 34;
 // rows are all written before the dilated conv reads 3 taps of dilation 3
 // back, so the ring must hold 32 + 9 positions.
 constexpr int ENG_RING = 64;
+// RoPE rows kept by position (state of launch_rope_rows): a one-token step
+// continues the newest row by the angle-addition recurrence, and after a
+// rollback of up to 32 positions the row before the new end must still be
+// there (the reference keeps ROLLBACK + 1 rows, infer.rs:1735-1742).
+constexpr int ROPE_RING = 33;
 
 // Kernels this process has launched through the launchers below.
 long long launch_count();

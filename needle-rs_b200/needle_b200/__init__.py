@@ -38,6 +38,9 @@ def lib():
             "nd_batch_free": (None, [P]),
             "nd_batch_len": (I, [P]),
             "nd_batch_set_attend": (I, [P, I, I]),
+            "nd_batch_rollback": (I, [P, I]),
+            "nd_batch_rewind_zeroed": (I, [P, I]),
+            "nd_batch_truncate": (I, [P, I]),
             "nd_batch_forward": (I, [P, P, I, I, P, I]),
             "nd_batch_step": (I, [P, P, P, I]),
             "nd_batch_last_hidden": (I, [P, P, I]),
@@ -255,6 +258,21 @@ class Batch:
 
     def __len__(self):
         return lib().nd_batch_len(self._h)
+
+    def rollback(self, n):
+        """Session::rollback for every sequence (model.rs:81-113)."""
+        if lib().nd_batch_rollback(self._h, n) != 0:
+            raise _err()
+
+    def rewind_zeroed(self, length):
+        """Session::rewind_zeroed for every sequence (model.rs:116-126)."""
+        if lib().nd_batch_rewind_zeroed(self._h, length) != 0:
+            raise _err()
+
+    def truncate(self, length):
+        """Session::truncate for every sequence (model.rs:128-145)."""
+        if lib().nd_batch_truncate(self._h, length) != 0:
+            raise _err()
 
     def set_attend(self, sink, ring):
         """Session::attend for every sequence (model.rs:63-66): the first

@@ -1845,6 +1845,76 @@ void* orc_session_new(void* m) { return session_new(*(Model*)m); }
 void orc_session_free(void* s) { delete (Session*)s; }
 void* orc_session_clone(void* s) { return new Session(*(Session*)s); }
 int orc_session_len(void* s) { return (int)((Session*)s)->tokens.size(); }
+// model.rs:81-113 + infer.rs:1055-1077 (Session::rollback): drop the last
+// n <= ROLLBACK positions without recomputing: the conv history loses its
+// last n rows, the engram history and RoPE rows their dropped positions;
+// KV slots and the slot map stay.
+int orc_session_rollback(void* mp, void* sp, int64_t n) {
+    try {
+        const Model& m = *(const Model*)mp;
+        Session& s = *(Session*)sp;
+        if (n > ROLLBACK) throw std::runtime_error("rollback exceeds ROLLBACK");
+        if (n > (int64_t)s.tokens.size()) throw std::runtime_error("rollback past the start");
+        if (n == 0) return 0;
+        const int64_t len = (int64_t)s.tokens.size() - n;
+        s.tokens.resize(len);
+        const int64_t width = (int64_t)(m.c.nh + m.c.nkv) * m.c.qk + (int64_t)m.c.nkv * m.c.vd;
+        for (auto& ls : s.layers) {
+            const int64_t rows = (int64_t)ls.hist.size() / width;
+            ls.hist.resize((size_t)std::max<int64_t>(0, rows - n) * width);
+        }
+        for (size_t site = 0; site < s.ev8.size(); site++) {
+            if ((int64_t)s.ev8[site].size() > len * m.c.d) s.ev8[site].resize((size_t)len * m.c.d);
+            if ((int64_t)s.evs[site].size() > len * m.c.d / 32) s.evs[site].resize((size_t)len * m.c.d / 32);
+        }
+        std::vector<RopeRow> kept;
+        for (auto& r : s.rope)
+            if (r.pos < len) kept.push_back(r);
+        s.rope.swap(kept);
+        return 0;
+    } catch (std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+
+// model.rs:116-126 + infer.rs:1039-1053 (Session::rewind_zeroed): forget
+// positions len..: the conv history is emptied, the engram history
+// truncated, the RoPE rows dropped; KV slots and slot map stay.
+int orc_session_rewind_zeroed(void* mp, void* sp, int64_t len) {
+    const Model& m = *(const Model*)mp;
+    Session& s = *(Session*)sp;
+    if (len < (int64_t)s.tokens.size()) s.tokens.resize(len);
+    for (auto& ls : s.layers) ls.hist.clear();
+    for (size_t site = 0; site < s.ev8.size(); site++) {
+        if ((int64_t)s.ev8[site].size() > len * m.c.d) s.ev8[site].resize((size_t)len * m.c.d);
+        if ((int64_t)s.evs[site].size() > len * m.c.d / 32) s.evs[site].resize((size_t)len * m.c.d / 32);
+    }
+    s.rope.clear();
+    return 0;
+}
+
+// model.rs:128-145 (Session::truncate): up to ROLLBACK positions by
+// rollback, more by a fresh session (no attention span) fed the first len
+// tokens.
+int orc_session_truncate(void* mp, void* sp, int64_t len) {
+    try {
+        const Model& m = *(const Model*)mp;
+        Session& s = *(Session*)sp;
+        const int64_t have = (int64_t)s.tokens.size();
+        if (len >= have) return 0;
+        if (have - len <= ROLLBACK) return orc_session_rollback(mp, sp, have - len);
+        std::vector<uint32_t> toks(s.tokens.begin(), s.tokens.begin() + len);
+        std::unique_ptr<Session> fresh(session_new(m));
+        s = *fresh;
+        if (len > 0) forward_native(m, s, toks.data(), (int)len, OUT_NONE, nullptr);
+        return 0;
+    } catch (std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+
 void orc_session_set_attend(void* s, int64_t sink, int64_t ring) {
     Session* ss = (Session*)s;
     ss->has_attend = ring > 0;

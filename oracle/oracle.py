@@ -48,6 +48,9 @@ def lib():
             "orc_session_clone": (P, [P]),
             "orc_session_len": (I, [P]),
             "orc_session_set_attend": (None, [P, I64, I64]),
+            "orc_session_rollback": (I, [P, P, I64]),
+            "orc_session_rewind_zeroed": (I, [P, P, I64]),
+            "orc_session_truncate": (I, [P, P, I64]),
             "orc_forward": (I, [P, P, P, I, I, P]),
             "orc_head_logits": (None, [P, P, P]),
             "orc_head_logits_sparse": (None, [P, P, P, I, P]),
@@ -404,6 +407,20 @@ class Session:
 
     def set_attend(self, sink, ring):
         lib().orc_session_set_attend(self._h, sink, ring)
+
+    def rollback(self, n):
+        """model.rs:81-113."""
+        if lib().orc_session_rollback(self.model._h, self._h, n) != 0:
+            raise RuntimeError(lib().orc_last_error().decode())
+
+    def rewind_zeroed(self, length):
+        """model.rs:116-126."""
+        lib().orc_session_rewind_zeroed(self.model._h, self._h, length)
+
+    def truncate(self, length):
+        """model.rs:128-145."""
+        if lib().orc_session_truncate(self.model._h, self._h, length) != 0:
+            raise RuntimeError(lib().orc_last_error().decode())
 
     def forward(self, ids, outputs=OUT_LAST_LOGITS):
         ids = np.ascontiguousarray(ids, np.uint32)

@@ -267,3 +267,38 @@ def test_quant_i8_nan_is_zero():
     x = np.array([1.0, np.nan, -2.0, 0.5], np.float32)
     q, s = orc.quant_i8(x)
     assert q[1] == 0 and q[0] == 64 and q[2] == -127
+
+
+def test_rollback_and_refeed_reproduce_the_logits(small_archive):
+    """Session::rollback (model.rs:81-113) keeps what the dropped positions
+    did not touch: feeding the same tokens again after a rollback gives the
+    same logits, through a prefill chunk and through one-token steps (the
+    RoPE recurrence continues from the kept row)."""
+    m = orc.Model(small_archive)
+    ids = (np.arange(48) * 31 % 1000).astype(np.uint32)
+    s = m.session()
+    s.forward(ids[:33])
+    want_chunk = s.forward(ids[33:40])[0]
+    steps = [s.forward(ids[k:k + 1])[0] for k in range(40, 46)]
+    s.rollback(6)
+    again = [s.forward(ids[k:k + 1])[0] for k in range(40, 46)]
+    for a, b in zip(steps, again):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    s.rollback(13)
+    assert np.array_equal(s.forward(ids[33:40])[0].view(np.uint32), want_chunk.view(np.uint32))
+    with pytest.raises(RuntimeError):
+        s.rollback(33)
+
+
+def test_truncate_recomputes_from_scratch(small_archive):
+    m = orc.Model(small_archive)
+    ids = (np.arange(60) * 17 % 1000).astype(np.uint32)
+    s = m.session()
+    s.forward(ids)
+    s.truncate(20)
+    assert len(s) == 20
+    fresh = m.session()
+    fresh.forward(ids[:20])
+    a = s.forward(ids[20:23])[0]
+    b = fresh.forward(ids[20:23])[0]
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
