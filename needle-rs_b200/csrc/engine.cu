@@ -528,6 +528,7 @@ static Batch* batch_new(Model* m, int S, int max_len) {
     const Config& c = m->c;
     if (S < 1) throw std::runtime_error("a batch needs at least one sequence");
     if (max_len < 1 || max_len > c.max_seq) throw std::runtime_error("max_len must be in [1, max_seq_len]");
+    if (max_len > ATT_MAX_KEYS) throw std::runtime_error("max_len above 8192 positions: the attention kernel holds 32 key chunks");
     CK(cudaSetDevice(m->device));
     std::unique_ptr<Batch> bp(new Batch());
     Batch& b = *bp;

@@ -1076,7 +1076,7 @@ void launch_conv_rope_kv(LayerW w, int l, const float* proj, Caches c, int S, in
 // the engine's key chunks (key_chunks, 2093-2101), scores with the 4-block
 // order rule, chunk_exp (2222-2318), 21-bit digits (2171-2217), integer P.V,
 // and the merge (2143-2166); then the gate (1548-1552).
-constexpr int ATT_MAXCHUNK = 256, ATT_MAXPARTS = 16;
+constexpr int ATT_MAXCHUNK = 256, ATT_MAXPARTS = ATT_MAX_KEYS / ATT_MAXCHUNK;
 
 __device__ __forceinline__ void key_chunks_dev(int n, bool nested, int* count, int* chunk) {
     int k = nested ? 1 : 4;  // (2 * NATIVE_TEAM / nkv).max(1), NATIVE_TEAM = 4, nkv = 2
@@ -1095,23 +1095,44 @@ __device__ __forceinline__ void key_chunks_dev(int n, bool nested, int* count, i
 // cp.async, issued before the queries are quantized; then warp h runs head
 // h through scores, max, numerators, the fixed-order sum, digits, P.V,
 // merge and gate with no block-wide barrier. Digits sit at the chunk's
-// offset within its first group, zero outside the chunk. Per-chunk parts
-// live in dynamic shared memory sized for the longest key list of the
-// launch.
-constexpr int ATT_HEADS = 6, ATT_THREADS = ATT_HEADS * 32, ATT_MAXGROUPS = ATT_MAXCHUNK / 4 + 4;
+// offset within its first group, zero outside the chunk. P.V is an int8
+// matrix product on the tensor cores (mma.sync m16n8k32, exact int32 sums,
+// so the result is the reference's integer dot whatever the order): A =
+// the three digit planes of 32 keys (8 groups), B = the same keys' value
+// bytes, which the cache's group words already hold in the fragment's
+// 4-keys-per-register order. Rows with more than one chunk keep per-chunk
+// parts in dynamic shared memory sized for the longest key list of the
+// launch; a one-chunk row keeps its part in registers, so a launch of
+// one-chunk rows needs no parts space.
+// A chunk spans at most ATT_MAXCHUNK / 4 + 3 value groups (a group cut at
+// each end of the sink run and of the ring run); the P.V loop reads whole
+// steps of 8 groups, so the buffers hold a multiple of 8.
+constexpr int ATT_HEADS = 6, ATT_THREADS = ATT_HEADS * 32, ATT_MAXGROUPS = (ATT_MAXCHUNK / 4 + 3 + 7) / 8 * 8;
+static_assert(ATT_MAXGROUPS % 8 == 0 && ATT_MAXGROUPS >= ATT_MAXCHUNK / 4 + 3, "whole 8-group steps");
 struct AttSmem {
     int8_t k[ATT_MAXCHUNK][48];
+    // value group w: the words of dimensions 0..63, the 16-byte run of
+    // dimensions 4c..4c+3 at word (4c) ^ (8 (w & 3)), so the P.V fragment
+    // loads of four consecutive groups fall in four distinct bank octets
     int vg[ATT_MAXGROUPS][64];
     float ks[ATT_MAXCHUNK], vs[ATT_MAXCHUNK];
     float s[ATT_HEADS][ATT_MAXCHUNK];
-    // digits of value group g (positions 4g..4g+3): hi, mid, lo words at
-    // bytes 16 g, 16 g + 4, 16 g + 8 (one 16-byte load per group)
-    __align__(16) int8_t dig[ATT_HEADS][16 * ATT_MAXGROUPS];
+    // digit plane (hi, mid, lo) of value group g: one word, the four
+    // positions 4g..4g+3 in its bytes
+    int dig[ATT_HEADS][3][ATT_MAXGROUPS];
     __align__(16) int8_t q8[ATT_HEADS][48];
-    // followed by parts: [ATT_HEADS][count][66] floats (m, sum, o[64])
+    // followed, when a row of the launch has more than one chunk, by parts:
+    // [ATT_HEADS][count][66] floats (m, sum, o[64])
 };
+static_assert(3 * 72 <= ATT_MAXCHUNK, "the P.V scratch fits a score row");
 
-__global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbuf, const float* proj, Caches c, int l, int T,
+__device__ __forceinline__ void mma_s8_acc(int (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+__global__ void __launch_bounds__(ATT_THREADS, 5) attention_kernel(const float* qbuf, const float* proj, Caches c, int l, int T,
                                                                 const int32_t* p0p, int window, int sink, int ring, float* att,
                                                                 int8_t* act, float* sx) {
     pdl_launch_dependents();
@@ -1170,7 +1191,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbu
         }
         for (int idx = tid; idx < (g.ngA + g.ngB) * 16; idx += ATT_THREADS) {
             const int w = idx >> 4, part = idx & 15, src = w < g.ngA ? g.gA0 + w : g.gB0 + w - g.ngA;
-            cp_async16(&sm.vg[w][part * 4], v8 + (size_t)src * 256 + part * 16, true);
+            cp_async16(&sm.vg[w][(part * 4) ^ ((w & 3) << 3)], v8 + (size_t)src * 256 + part * 16, true);
         }
         for (int k = tid; k < len; k += ATT_THREADS) {
             const int p = k < g.nA ? g.pA + k : g.pB + k - g.nA;
@@ -1196,6 +1217,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbu
         qs = __fmul_rn(sc, ND_INV_SQRT_QK);
     }
     float* srow = sm.s[h];
+    float one0 = 0.f, one1 = 0.f, one_sum = 1.f;  // a one-chunk row's part
     for (int ci = 0; ci < count; ci++) {
         const int c0 = ci * chunk, len = min(chunk, n - c0), blocked = len / 4 * 4;
         const Seg sg = seg(c0, len);
@@ -1280,33 +1302,67 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbu
                 k = kb >= 0 && kb < sg.nB ? sg.nA + kb : -1;
             }
             int wq = k >= 0 ? (int)roundf(__fmul_rn(srow[k], qw)) : 0;
-            int8_t* dg = sm.dig[h] + (kk >> 2) * 16 + (kk & 3);
+            int8_t* dg = (int8_t*)&sm.dig[h][0][kk >> 2] + (kk & 3);
             dg[0] = (int8_t)(wq >> 14);
-            dg[4] = (int8_t)((wq >> 7) & 127);
-            dg[8] = (int8_t)(wq & 127);
+            dg[4 * ATT_MAXGROUPS] = (int8_t)((wq >> 7) & 127);
+            dg[8 * ATT_MAXGROUPS] = (int8_t)(wq & 127);
         }
         __syncwarp();
-        // P.V: three exact integer dots per value dimension (2 lane, 2 lane + 1)
-        const int4* dg4 = (const int4*)sm.dig[h];
-        int sh0 = 0, sm0 = 0, sl0 = 0, sh1 = 0, sm1 = 0, sl1 = 0;
-        for (int w = 0; w < ng; w++) {
-            const int4 dd = dg4[w];
-            const int2 xv = *(const int2*)&sm.vg[w][2 * lane];
-            int a0 = dd.x, a1 = dd.y, a2 = dd.z, x0 = xv.x, x1 = xv.y;
-            sh0 = __dp4a(a0, x0, sh0);
-            sm0 = __dp4a(a1, x0, sm0);
-            sl0 = __dp4a(a2, x0, sl0);
-            sh1 = __dp4a(a0, x1, sh1);
-            sm1 = __dp4a(a1, x1, sm1);
-            sl1 = __dp4a(a2, x1, sl1);
+        // P.V on the tensor cores, 8 groups (32 keys) a step: A rows 0-2 are
+        // the digit planes (lane gid < 3 loads plane gid's words of groups
+        // g0 = 8 ks + tig and g0 + 4, zero past the chunk's groups), the
+        // other rows zero; B column n is value dimension 8 nt + n. Two
+        // passes of four 8-dimension tiles.
+        {
+            const int gid = lane >> 2, tig = lane & 3, steps = (ng + 7) >> 3, swz = tig << 3;
+            const int* dp = sm.dig[h][gid < 3 ? gid : 0];
+            // plane gid's sums of dimensions 8 nt + 2 tig, + 1 go through the
+            // score row (done with) to the lanes that own them
+            int* scr = reinterpret_cast<int*>(srow);
+#pragma unroll 1
+            for (int half = 0; half < 2; half++) {
+                int acc[4][4];
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0;
+                for (int ks = 0; ks < steps; ks++) {
+                    const int g0 = 8 * ks + tig, g1 = g0 + 4;
+                    const uint32_t a[4] = {gid < 3 && g0 < ng ? (uint32_t)dp[g0] : 0u, 0u,
+                                           gid < 3 && g1 < ng ? (uint32_t)dp[g1] : 0u, 0u};
+                    const int* v0 = sm.vg[g0];
+                    const int* v1 = sm.vg[g1];
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const int col = ((half * 4 + j) * 8 + gid) ^ swz;
+                        const uint32_t b[2] = {(uint32_t)v0[col], (uint32_t)v1[col]};
+                        mma_s8_acc(acc[j], a, b);
+                    }
+                }
+                if (gid < 3) {
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        *(int2*)&scr[gid * 72 + (half * 4 + j) * 8 + 2 * tig] = make_int2(acc[j][0], acc[j][1]);
+                }
+            }
+            __syncwarp();
         }
+        const int* scr = reinterpret_cast<const int*>(srow);
+        const int2 dh = *(const int2*)&scr[2 * lane], dm = *(const int2*)&scr[72 + 2 * lane],
+                   dl = *(const int2*)&scr[144 + 2 * lane];
         const float cw = __fmul_rn(wm, ND_C21);
-        float* pr = parts + ci * 66;
-        pr[2 + 2 * lane] = __fmul_rn(__fmaf_rn(16384.f, (float)sh0, __fmaf_rn(128.f, (float)sm0, (float)sl0)), cw);
-        pr[3 + 2 * lane] = __fmul_rn(__fmaf_rn(16384.f, (float)sh1, __fmaf_rn(128.f, (float)sm1, (float)sl1)), cw);
-        if (lane == 0) {
-            pr[0] = mx;
-            pr[1] = sum;
+        const float pv0 = __fmul_rn(__fmaf_rn(16384.f, (float)dh.x, __fmaf_rn(128.f, (float)dm.x, (float)dl.x)), cw);
+        const float pv1 = __fmul_rn(__fmaf_rn(16384.f, (float)dh.y, __fmaf_rn(128.f, (float)dm.y, (float)dl.y)), cw);
+        if (count == 1) {
+            one0 = pv0;
+            one1 = pv1;
+            one_sum = sum;
+        } else {
+            float* pr = parts + ci * 66;
+            pr[2 + 2 * lane] = pv0;
+            pr[3 + 2 * lane] = pv1;
+            if (lane == 0) {
+                pr[0] = mx;
+                pr[1] = sum;
+            }
         }
         if (ci + 1 < count) {
             __syncthreads();  // every warp is done with this chunk's copies
@@ -1317,9 +1373,9 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* qbu
     // merge_parts (infer.rs:2143-2166), then the gate (1548-1552)
     float out0, out1;
     if (count == 1) {
-        float inv = __fdiv_rn(1.0f, parts[1]);
-        out0 = __fmul_rn(parts[2 + 2 * lane], inv);
-        out1 = __fmul_rn(parts[3 + 2 * lane], inv);
+        float inv = __fdiv_rn(1.0f, one_sum);
+        out0 = __fmul_rn(one0, inv);
+        out1 = __fmul_rn(one1, inv);
     } else {
         float big = -1e30f;
         for (int ci = 0; ci < count; ci++) big = fmaxf(big, parts[ci * 66]);
@@ -1370,7 +1426,7 @@ void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int
     int most = std::max(1, (nmax + 255) / 256);
     if (T == 1 && nmax >= 256) most = std::max(most, 4);
     most = std::min(most, ATT_MAXPARTS);
-    size_t smem = ATT_SMEM_BASE + (size_t)ATT_HEADS * most * 66 * 4;
+    size_t smem = ATT_SMEM_BASE + (most > 1 ? (size_t)ATT_HEADS * most * 66 * 4 : 0);
     launch_pdl(attention_kernel, dim3(dim3(S * T, 2)), dim3(ATT_THREADS), smem, st, qbuf, proj, c, l, T, c.len, window, sink, ring,
                att, act, sx);
 }
@@ -1380,7 +1436,8 @@ void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int
 
 // infer.rs:1564-1606 with mlp_native (1610-1634), cond_weights (1640-1694),
 // perm_fma (689-713), silu (2463-2496) and kron_native / mix8 (2322-2460).
-// Eight rows per CTA of 512 threads, one CTA per SM: the layer's small
+// Seven rows per CTA of 448 threads, one CTA per SM (a batch of 1024 rows
+// fills 147 of the 148 SMs; eight rows a CTA left 20 idle): the layer's small
 // weights (Kronecker factors, conditioning, diagonals, norms, permutations)
 // are staged once into shared memory with cp.async, so every phase reads
 // shared memory only. A row's 1024-wide vectors use a padded layout
@@ -1389,7 +1446,8 @@ void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int
 // rows' o, x1 and gates right after; u arrives during the Kronecker stages
 // into the space of cond_v, whose last use is the conditioning logits. The
 // post and residual gates (hpost, Sinkhorn) were computed by the mHC read.
-constexpr int POST_ROWS = 8, POST_THREADS = 512, PV = 32 * 36 + 8;
+constexpr int POST_ROWS = 7, POST_THREADS = 448, PV = 32 * 36 + 8;
+static_assert(POST_ROWS * 768 % (4 * POST_THREADS) == 0, "whole batches of mHC items");
 struct PostSmem {
     float kf[6][1024];
     float cond_v[768 * 8];
@@ -1397,19 +1455,21 @@ struct PostSmem {
     float d1[768], d2[1024], b2[1024], d3[1024], d4[768];
     float post_norm[768], pre_hada[768];
     int perm1[1024], perm2[1024];
-    float x2[POST_ROWS][768];
-    float buf[2][POST_ROWS][PV];
+    // the rows' buffers take 16-byte copies and loads at any row count
+    __align__(16) float x2[POST_ROWS][768];
+    __align__(16) float buf[2][POST_ROWS][PV];
+    __align__(16) float gates[POST_ROWS][24];
     float part[POST_ROWS][32];
     float sc[POST_ROWS][2];
     float wk[POST_ROWS][8];
-    float gates[POST_ROWS][24];
 };
 extern const size_t POST_SMEM = sizeof(PostSmem);
 
 __device__ __forceinline__ int pv_idx(int p) { return (p >> 5) * 36 + (p & 31); }
 
+template <int NT = POST_THREADS>
 __device__ __forceinline__ void stage(void* dst, const void* src, int bytes, int tid) {
-    for (int o = tid * 16; o < bytes; o += POST_THREADS * 16) cp_async16((char*)dst + o, (const char*)src + o, true);
+    for (int o = tid * 16; o < bytes; o += NT * 16) cp_async16((char*)dst + o, (const char*)src + o, true);
 }
 
 // The Kronecker passes: 32 threads (one warp) per CTA row, each a 4 x 8
@@ -1470,12 +1530,14 @@ __device__ __forceinline__ void kron_pass2(const float* mt, const float* B, floa
 }
 
 // A Kronecker stage of every row: z in buf[from], result t in buf[from]
-// too (pass 1 writes mt into buf[1 - from]). Warps 0-7, warp q for row q.
+// too (pass 1 writes mt into buf[1 - from]). Warp q for row q. (Tiles of
+// 4 x 4 over two warps a row measured slower: the passes are bound by
+// shared-memory wavefronts, three per 16 paired fmas here.)
 __device__ __forceinline__ void kron_stage_rows(PostSmem& sm, int fa, int fb, int from, int tid) {
     const int q = tid >> 5, i = tid & 31, r0 = (i & 7) * 4, c0 = (i >> 3) * 8;
-    if (tid < 256) kron_pass1(sm.kf[fa], sm.buf[from][q], sm.buf[1 - from][q], r0, c0);
+    if (tid < POST_ROWS * 32) kron_pass1(sm.kf[fa], sm.buf[from][q], sm.buf[1 - from][q], r0, c0);
     __syncthreads();
-    if (tid < 256) kron_pass2(sm.buf[1 - from][q], sm.kf[fb], sm.buf[from][q], r0, c0);
+    if (tid < POST_ROWS * 32) kron_pass2(sm.buf[1 - from][q], sm.kf[fb], sm.buf[from][q], r0, c0);
     __syncthreads();
 }
 
@@ -1619,7 +1681,8 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
     // mHC write (infer.rs:1587-1606): y = x2 + mlp - u, stream a =
     // y * hpost[a] + sum_b old[b] * hres[a][b]. Four (row, channel) items a
     // thread per round, each round's 16 stream loads issued before the
-    // previous round's arithmetic.
+    // previous round's arithmetic (the first round's before the last
+    // Kronecker stage).
     constexpr int ITEMS = POST_ROWS * 768 / POST_THREADS, BATCH = 4;
     static_assert(ITEMS % BATCH == 0, "item batches");
     float cur[BATCH][4], nxt[BATCH][4];
@@ -1629,8 +1692,8 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
         const float* xr = xs + (size_t)(m0 + (q < rows ? q : 0)) * 3072 + ch;                         \
         _Pragma("unroll") for (int b = 0; b < 4; b++) dst[e][b] = xr[b * 768];                        \
     }
+    POST_LOAD_OLD(cur, 0)  // in flight during the last Kronecker stage
     kron_stage_rows(sm, 4, 5, 0, tid);  // t3 in buf[0]
-    POST_LOAD_OLD(cur, 0)
     asm volatile("cp.async.wait_group 0;\n" ::);
     __syncthreads();
 #pragma unroll
@@ -1669,7 +1732,7 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
 // owns r = t % 32 and columns c0 = 2 (t / 32), c0 + 1 (mt stored transposed,
 // as kron_native keeps it); in pass 2 the same r and columns of t. Every
 // float op, and its order, is that of post_block_kernel.
-constexpr int POST_ROW_MAX_M = 296;
+constexpr int POST_ROW_MAX_M = 296, POST_ROW_THREADS = 512;
 struct PostRowSmem {
     float kf[6][1024];
     float cond_v[768 * 8];
@@ -1704,34 +1767,34 @@ __device__ __forceinline__ void kron_row_pass2(const float* mt, const float* B, 
     *(float2*)(t + r * 32 + c0) = o;
 }
 
-__global__ void __launch_bounds__(POST_THREADS, 1) post_row_kernel(LayerW w, const float* o, const float* x1, const float* u,
+__global__ void __launch_bounds__(POST_ROW_THREADS, 1) post_row_kernel(LayerW w, const float* o, const float* x1, const float* u,
                                                                  const float* gates, const int32_t* perm1, const int32_t* perm2,
                                                                  float* xs) {
     pdl_launch_dependents();
     extern __shared__ __align__(16) int8_t post_row_raw[];
     PostRowSmem& sm = *reinterpret_cast<PostRowSmem*>(post_row_raw);
     const int tid = threadIdx.x, m = blockIdx.x, r = tid & 31, c0 = 2 * (tid >> 5);
-    for (int f = 0; f < 6; f++) stage(sm.kf[f], w.kron[f], 4096, tid);
-    stage(sm.cond_v, w.cond_v, 768 * 8 * 4, tid);
-    stage(sm.cond_u, w.cond_u, 8 * 1024 * 4, tid);
-    stage(sm.d1, w.d1, 768 * 4, tid);
-    stage(sm.d2, w.d2, 4096, tid);
-    stage(sm.b2, w.b2, 4096, tid);
-    stage(sm.d3, w.d3, 4096, tid);
-    stage(sm.d4, w.d4, 768 * 4, tid);
-    stage(sm.post_norm, w.post_norm, 768 * 4, tid);
-    stage(sm.pre_hada, w.pre_hada, 768 * 4, tid);
-    stage(sm.perm1, perm1, 4096, tid);
-    stage(sm.perm2, perm2, 4096, tid);
+    for (int f = 0; f < 6; f++) stage<POST_ROW_THREADS>(sm.kf[f], w.kron[f], 4096, tid);
+    stage<POST_ROW_THREADS>(sm.cond_v, w.cond_v, 768 * 8 * 4, tid);
+    stage<POST_ROW_THREADS>(sm.cond_u, w.cond_u, 8 * 1024 * 4, tid);
+    stage<POST_ROW_THREADS>(sm.d1, w.d1, 768 * 4, tid);
+    stage<POST_ROW_THREADS>(sm.d2, w.d2, 4096, tid);
+    stage<POST_ROW_THREADS>(sm.b2, w.b2, 4096, tid);
+    stage<POST_ROW_THREADS>(sm.d3, w.d3, 4096, tid);
+    stage<POST_ROW_THREADS>(sm.d4, w.d4, 768 * 4, tid);
+    stage<POST_ROW_THREADS>(sm.post_norm, w.post_norm, 768 * 4, tid);
+    stage<POST_ROW_THREADS>(sm.pre_hada, w.pre_hada, 768 * 4, tid);
+    stage<POST_ROW_THREADS>(sm.perm1, perm1, 4096, tid);
+    stage<POST_ROW_THREADS>(sm.perm2, perm2, 4096, tid);
     asm volatile("cp.async.commit_group;\n" ::);
     pdl_wait();
     // the row's inputs in one round of copies: o, the residual x1, u, the
     // four streams the mHC write reads, the gates
     float* xr = xs + (size_t)m * 3072;
-    stage(sm.x2, o + (size_t)m * 768, 768 * 4, tid);
-    stage(sm.x1, x1 + (size_t)m * 768, 768 * 4, tid);
-    stage(sm.ub, u + (size_t)m * 768, 768 * 4, tid);
-    stage(sm.xold, xr, 3072 * 4, tid);
+    stage<POST_ROW_THREADS>(sm.x2, o + (size_t)m * 768, 768 * 4, tid);
+    stage<POST_ROW_THREADS>(sm.x1, x1 + (size_t)m * 768, 768 * 4, tid);
+    stage<POST_ROW_THREADS>(sm.ub, u + (size_t)m * 768, 768 * 4, tid);
+    stage<POST_ROW_THREADS>(sm.xold, xr, 3072 * 4, tid);
     if (tid < 24) sm.gr[tid] = gates[(size_t)m * 24 + tid];
     asm volatile("cp.async.commit_group;\n" ::);
     asm volatile("cp.async.wait_group 0;\n" ::);
@@ -1742,7 +1805,7 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_row_kernel(LayerW w, con
     if (tid == 0) sm.sc[0] = rinv(dot16_combine(sm.part), 768);
     __syncthreads();
     const float ga = __fdiv_rn(1.0f, __fadd_rn(lexpf(-w.attn_gate), 1.0f));
-    for (int c = tid; c < 768; c += POST_THREADS) {
+    for (int c = tid; c < 768; c += POST_ROW_THREADS) {
         float tt = __fmul_rn(sm.x2[c], sm.sc[0]);
         float on = __fmaf_rn(tt, sm.post_norm[c], tt);
         sm.x2[c] = __fmaf_rn(on, ga, sm.x1[c]);
@@ -1753,7 +1816,7 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_row_kernel(LayerW w, con
     if (tid == 0) sm.sc[1] = rinv(dot16_combine(sm.part), 768);
     __syncthreads();
     // h2 = zcn(x2, pre_hada), z = h2 * d1 (zero past 768)
-    for (int c = tid; c < 1024; c += POST_THREADS) {
+    for (int c = tid; c < 1024; c += POST_ROW_THREADS) {
         if (c < 768) {
             float tt = __fmul_rn(sm.x2[c], sm.sc[1]);
             float h = __fmaf_rn(tt, sm.pre_hada[c], tt);
@@ -1791,7 +1854,7 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_row_kernel(LayerW w, con
     kron_row_pass2(sm.mb, sm.kf[1], sm.tb, r, c0);
     __syncthreads();
     // z = fma(t1[perm1[j]], cond[j] * d2[j], b2[j]), cond = 1 + sum_k w_k u_k, then SiLU
-    for (int j = tid; j < 1024; j += POST_THREADS) {
+    for (int j = tid; j < 1024; j += POST_ROW_THREADS) {
         float cnd = 1.0f;
 #pragma unroll
         for (int kk = 0; kk < 8; kk++) cnd = __fmaf_rn(sm.cond_u[kk * 1024 + j], sm.wk[kk], cnd);
@@ -1803,7 +1866,7 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_row_kernel(LayerW w, con
     __syncthreads();
     kron_row_pass2(sm.mb, sm.kf[3], sm.tb, r, c0);
     __syncthreads();
-    for (int j = tid; j < 1024; j += POST_THREADS) sm.zb[j] = __fmul_rn(sm.tb[sm.perm2[j]], sm.d3[j]);
+    for (int j = tid; j < 1024; j += POST_ROW_THREADS) sm.zb[j] = __fmul_rn(sm.tb[sm.perm2[j]], sm.d3[j]);
     __syncthreads();
     kron_row_pass1(sm.kf[4], sm.zb, sm.mb, r, c0);
     __syncthreads();
@@ -1811,7 +1874,7 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_row_kernel(LayerW w, con
     __syncthreads();
     // mHC write (infer.rs:1587-1606): y = x2 + mlp - u, stream a =
     // y * hpost[a] + sum_b old[b] * hres[a][b]
-    for (int ch = tid; ch < 768; ch += POST_THREADS) {
+    for (int ch = tid; ch < 768; ch += POST_ROW_THREADS) {
         float mlp = __fmul_rn(sm.tb[ch], sm.d4[ch]);
         float y = __fsub_rn(__fadd_rn(sm.x2[ch], mlp), sm.ub[ch]);
         float old[4];
@@ -1831,7 +1894,7 @@ void launch_post_block(LayerW w, const float* o, const float* x1, const float* u
                        const int32_t* perm2, int M, float* xs, cudaStream_t st) {
     COUNT_LAUNCH();
     if (M <= POST_ROW_MAX_M) {
-        launch_pdl(post_row_kernel, dim3(M), dim3(POST_THREADS), POST_ROW_SMEM, st, w, o, x1, u, gates, perm1, perm2, xs);
+        launch_pdl(post_row_kernel, dim3(M), dim3(POST_ROW_THREADS), POST_ROW_SMEM, st, w, o, x1, u, gates, perm1, perm2, xs);
         return;
     }
     launch_pdl(post_block_kernel, dim3(cdiv(M, POST_ROWS)), dim3(POST_THREADS), POST_SMEM, st, w, o, x1, u, gates, perm1, perm2, M, xs);

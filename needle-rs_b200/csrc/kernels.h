@@ -83,6 +83,8 @@ constexpr int ENG_RING = 64;
 // rollback of up to 32 positions the row before the new end must still be
 // there (the reference keeps ROLLBACK + 1 rows, infer.rs:1735-1742).
 constexpr int ROPE_RING = 33;
+// The longest key list the attention kernel takes: 32 key chunks of 256.
+constexpr int ATT_MAX_KEYS = 8192;
 
 // Kernels this process has launched through the launchers below.
 long long launch_count();
