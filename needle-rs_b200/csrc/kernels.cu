@@ -949,125 +949,144 @@ void launch_mhc_gates(LayerW w, int lane, int M, float* gates, cudaStream_t st) 
 // ------------------------------------------------ conv taps, RoPE, int8 KV
 
 // infer.rs:1430-1526 (chunk rows) as unit work (infer/step.rs:468-516): per
-// row, 12 q heads, 2 k heads and 2 v heads, one warp each. The taps read
-// earlier rows of this chunk, else the pre-tap history, else zeros.
-__global__ void __launch_bounds__(512) conv_rope_kv_kernel(LayerW w, int l, const float* proj, Caches c, int T, const int32_t* p0p,
-                                                           int hist_base, const float* cosr, const float* sinr, float* qbuf) {
+// row, 12 q heads, 2 k heads and 2 v heads, one unit each; a CTA of eight
+// warps takes a row, warp w units w and w + 8, with every load of both
+// units issued before either is worked on (a row in 256 threads, so the
+// batch's rows are resident at once: 1024 rows fit 148 SMs x 8). The taps
+// read earlier rows of this chunk, else the pre-tap history, else zeros.
+constexpr int CONV_THREADS = 256;
+__global__ void __launch_bounds__(CONV_THREADS, 8) conv_rope_kv_kernel(LayerW w, int l, const float* proj, Caches c, int T,
+                                                                    const int32_t* p0p, int hist_base, const float* cosr,
+                                                                    const float* sinr, float* qbuf) {
     pdl_launch_dependents();
     pdl_wait();
     const int p0 = *p0p;
     __shared__ float buf[16][64];
-    const int m = blockIdx.x, unit = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int s = m / T, i = m % T, pos = p0 + i;
-    int start, cw, cc, len;
-    const float* wt;
-    if (unit < 12) { start = unit * 48; cw = 576; cc = unit * 48; len = 48; wt = w.q_taps; }
-    else if (unit < 14) { int kh = unit - 12; start = 576 + kh * 48; cw = 96; cc = kh * 48; len = 48; wt = w.k_taps; }
-    else { int vh = unit - 14; start = 672 + vh * 64; cw = 128; cc = vh * 64; len = 64; wt = w.v_taps; }
     const size_t hrow0 = ((size_t)s * c.L + l) * HIST_RING;
-    float* x = buf[unit];
-    // every load of the lane's (at most two) channels first, then the
-    // history write and the taps
-    float cur[2], prev[2][2], wv[2][3];
+    auto unit_of = [&](int unit, int& start, int& cw, int& cc, int& len, const float*& wt) {
+        if (unit < 12) { start = unit * 48; cw = 576; cc = unit * 48; len = 48; wt = w.q_taps; }
+        else if (unit < 14) { int kh = unit - 12; start = 576 + kh * 48; cw = 96; cc = kh * 48; len = 48; wt = w.k_taps; }
+        else { int vh = unit - 14; start = 672 + vh * 64; cw = 128; cc = vh * 64; len = 64; wt = w.v_taps; }
+    };
+    // every row load of the lane's (at most two) channels of both units
+    // first, then the tap weights (cache-resident), history writes and taps
+    float cur[2][2], prev[2][2][2];
 #pragma unroll
-    for (int t = 0; t < 2; t++) {
-        const int k = lane + 32 * t;
-        cur[t] = 0.f;
-        prev[t][0] = prev[t][1] = 0.f;
-        wv[t][0] = wv[t][1] = wv[t][2] = 0.f;
-        if (k < len) {
-            cur[t] = proj[(size_t)m * 1568 + start + k];
+    for (int r = 0; r < 2; r++) {
+        int start, cw, cc, len;
+        const float* wt;
+        unit_of(warp + 8 * r, start, cw, cc, len, wt);
 #pragma unroll
-            for (int j = 0; j < 3; j++) wv[t][j] = wt[j * cw + cc + k];
+        for (int t = 0; t < 2; t++) {
+            const int k = lane + 32 * t;
+            cur[r][t] = 0.f;
+            prev[r][t][0] = prev[r][t][1] = 0.f;
+            if (k < len) {
+                cur[r][t] = proj[(size_t)m * 1568 + start + k];
 #pragma unroll
-            for (int j = 1; j < 3; j++) {
-                const int pj = pos - j;
-                if (i - j >= 0) prev[t][j - 1] = proj[(size_t)(m - j) * 1568 + start + k];
-                else if (pj >= hist_base && pj >= 0) prev[t][j - 1] = c.hist[(hrow0 + pj % HIST_RING) * 800 + start + k];
+                for (int j = 1; j < 3; j++) {
+                    const int pj = pos - j;
+                    if (i - j >= 0) prev[r][t][j - 1] = proj[(size_t)(m - j) * 1568 + start + k];
+                    else if (pj >= hist_base && pj >= 0) prev[r][t][j - 1] = c.hist[(hrow0 + pj % HIST_RING) * 800 + start + k];
+                }
             }
         }
     }
 #pragma unroll
-    for (int t = 0; t < 2; t++) {
-        const int k = lane + 32 * t;
-        if (k < len) {
-            // this row's pre-tap value joins the history (infer.rs:1486-1488);
-            // its slot is none of the two that rows 0 and 1 read
-            c.hist[(hrow0 + pos % HIST_RING) * 800 + start + k] = cur[t];
-            float o = __fmul_rn(wv[t][0], cur[t]);
-            o = __fmaf_rn(wv[t][1], prev[t][0], o);  // zero where no earlier row exists
-            o = __fmaf_rn(wv[t][2], prev[t][1], o);
-            x[k] = o;
+    for (int r = 0; r < 2; r++) {
+        int start, cw, cc, len;
+        const float* wt;
+        unit_of(warp + 8 * r, start, cw, cc, len, wt);
+        float* x = buf[warp + 8 * r];
+#pragma unroll
+        for (int t = 0; t < 2; t++) {
+            const int k = lane + 32 * t;
+            if (k < len) {
+                // this row's pre-tap value joins the history (infer.rs:1486-1488);
+                // its slot is none of the two that rows 0 and 1 read
+                c.hist[(hrow0 + pos % HIST_RING) * 800 + start + k] = cur[r][t];
+                float o = __fmul_rn(wt[cc + k], cur[r][t]);
+                o = __fmaf_rn(wt[cw + cc + k], prev[r][t][0], o);  // zero where no earlier row exists
+                o = __fmaf_rn(wt[2 * cw + cc + k], prev[r][t][1], o);
+                x[k] = o;
+            }
         }
     }
     __syncwarp();
-    if (unit < 14) {
-        // zcn_inplace (infer.rs:446-452) over the 48-wide head, dot16 order.
-        float part = 0.f;
-        if (lane < 16) {
-            part = __fmaf_rn(x[lane], x[lane], 0.f);
-            part = __fmaf_rn(x[lane + 16], x[lane + 16], part);
-            part = __fmaf_rn(x[lane + 32], x[lane + 32], part);
-        }
-        float chains[16];
+#pragma unroll 1
+    for (int r = 0; r < 2; r++) {
+        const int unit = warp + 8 * r, len = unit < 14 ? 48 : 64;
+        float* x = buf[unit];
+        if (unit < 14) {
+            // zcn_inplace (infer.rs:446-452) over the 48-wide head, dot16 order.
+            float part = 0.f;
+            if (lane < 16) {
+                part = __fmaf_rn(x[lane], x[lane], 0.f);
+                part = __fmaf_rn(x[lane + 16], x[lane + 16], part);
+                part = __fmaf_rn(x[lane + 32], x[lane + 32], part);
+            }
+            float chains[16];
 #pragma unroll
-        for (int k = 0; k < 16; k++) chains[k] = __shfl_sync(0xffffffffu, part, k);
-        float r = rinv(dot16_combine(chains), 48);
-        const float* scale = unit < 12 ? w.q_norm : w.k_norm;
-        float t0 = __fmul_rn(x[lane], r);
-        float y0 = __fmaf_rn(t0, scale[lane], t0);
-        float y1 = 0.f;
-        if (lane < 16) {
-            float t1 = __fmul_rn(x[lane + 32], r);
-            y1 = __fmaf_rn(t1, scale[lane + 32], t1);
+            for (int k = 0; k < 16; k++) chains[k] = __shfl_sync(0xffffffffu, part, k);
+            float rr = rinv(dot16_combine(chains), 48);
+            const float* scale = unit < 12 ? w.q_norm : w.k_norm;
+            float t0 = __fmul_rn(x[lane], rr);
+            float y0 = __fmaf_rn(t0, scale[lane], t0);
+            float y1 = 0.f;
+            if (lane < 16) {
+                float t1 = __fmul_rn(x[lane + 32], rr);
+                y1 = __fmaf_rn(t1, scale[lane + 32], t1);
+            }
+            __syncwarp();
+            x[lane] = y0;
+            if (lane < 16) x[lane + 32] = y1;
+            __syncwarp();
+            // RoPE (infer.rs:1479-1483) on halves of 24.
+            float na = 0.f, nb = 0.f;
+            if (lane < 24) {
+                float cs = cosr[i * 24 + lane], sn = sinr[i * 24 + lane];
+                float av = x[lane], bv = x[lane + 24];
+                na = __fmaf_rn(-sn, bv, __fmul_rn(cs, av));
+                nb = __fmaf_rn(sn, av, __fmul_rn(cs, bv));
+            }
+            __syncwarp();
+            if (lane < 24) {
+                x[lane] = na;
+                x[lane + 24] = nb;
+            }
+            __syncwarp();
         }
-        __syncwarp();
-        x[lane] = y0;
-        if (lane < 16) x[lane + 32] = y1;
-        __syncwarp();
-        // RoPE (infer.rs:1479-1483) on halves of 24.
-        float na = 0.f, nb = 0.f;
-        if (lane < 24) {
-            float cs = cosr[i * 24 + lane], sn = sinr[i * 24 + lane];
-            float av = x[lane], bv = x[lane + 24];
-            na = __fmaf_rn(-sn, bv, __fmul_rn(cs, av));
-            nb = __fmaf_rn(sn, av, __fmul_rn(cs, bv));
+        if (unit < 12) {
+            for (int k = lane; k < 48; k += 32) qbuf[(size_t)m * 576 + unit * 48 + k] = x[k];
+            continue;
         }
-        __syncwarp();
-        if (lane < 24) {
-            x[lane] = na;
-            x[lane + 24] = nb;
+        // int8 KV at this position's slot (infer.rs:1508-1525).
+        float a = 0.f;
+        for (int k = lane; k < len; k += 32) a = fmaxf(a, fabsf(x[k]));
+        a = warp_max(a);
+        float sc = a > 0.f ? __fmul_rn(a, ND_K127) : 1.0f;
+        float inv = __fdiv_rn(1.0f, sc);
+        if (unit < 14) {
+            int kh = unit - 12;
+            size_t row = (((size_t)s * c.L + l) * 2 + kh) * c.cap + pos;
+            for (int k = lane; k < 48; k += 32) c.k8[row * 48 + k] = q8_round(x[k], inv);
+            if (lane == 0) c.ks[row] = sc;
+        } else {
+            int vh = unit - 14;
+            size_t row = (((size_t)s * c.L + l) * 2 + vh) * c.cap + pos;
+            int8_t* vg = c.v8 + ((((size_t)s * c.L + l) * 2 + vh) * c.vgroups + (pos >> 2)) * 256 + (pos & 3);
+            for (int k = lane; k < 64; k += 32) vg[k * 4] = q8_round(x[k], inv);
+            if (lane == 0) c.vs[row] = sc;
         }
-        __syncwarp();
-    }
-    if (unit < 12) {
-        for (int k = lane; k < 48; k += 32) qbuf[(size_t)m * 576 + unit * 48 + k] = x[k];
-        return;
-    }
-    // int8 KV at this position's slot (infer.rs:1508-1525).
-    float a = 0.f;
-    for (int k = lane; k < len; k += 32) a = fmaxf(a, fabsf(x[k]));
-    a = warp_max(a);
-    float sc = a > 0.f ? __fmul_rn(a, ND_K127) : 1.0f;
-    float inv = __fdiv_rn(1.0f, sc);
-    if (unit < 14) {
-        int kh = unit - 12;
-        size_t row = (((size_t)s * c.L + l) * 2 + kh) * c.cap + pos;
-        for (int k = lane; k < 48; k += 32) c.k8[row * 48 + k] = q8_round(x[k], inv);
-        if (lane == 0) c.ks[row] = sc;
-    } else {
-        int vh = unit - 14;
-        size_t row = (((size_t)s * c.L + l) * 2 + vh) * c.cap + pos;
-        int8_t* vg = c.v8 + ((((size_t)s * c.L + l) * 2 + vh) * c.vgroups + (pos >> 2)) * 256 + (pos & 3);
-        for (int k = lane; k < 64; k += 32) vg[k * 4] = q8_round(x[k], inv);
-        if (lane == 0) c.vs[row] = sc;
     }
 }
 
 void launch_conv_rope_kv(LayerW w, int l, const float* proj, Caches c, int S, int T, int p0, int hist_base, const float* cosr,
                          const float* sinr, float* qbuf, cudaStream_t st) {
     COUNT_LAUNCH();
-    launch_pdl(conv_rope_kv_kernel, dim3(S * T), dim3(512), 0, st, w, l, proj, c, T, c.len, hist_base, cosr, sinr, qbuf);
+    launch_pdl(conv_rope_kv_kernel, dim3(S * T), dim3(CONV_THREADS), 0, st, w, l, proj, c, T, c.len, hist_base, cosr, sinr, qbuf);
 }
 
 // ------------------------------------------------------------- attention
@@ -1181,22 +1200,25 @@ __global__ void __launch_bounds__(ATT_THREADS, 5) attention_kernel(const float* 
     const size_t kvrow = (((size_t)s * c.L + l) * 2 + kvh) * c.cap;
     const int8_t* k8 = c.k8 + kvrow * 48;
     const int8_t* v8 = c.v8 + (((size_t)s * c.L + l) * 2 + kvh) * c.vgroups * 256;
-    // the copies of chunk ci: key rows, value groups (A's, then B's), scales
+    // the copies of chunk ci in two groups: key rows (each run of positions
+    // one contiguous range of 48-byte rows) and scales, then the value
+    // groups (A's, then B's), which P.V waits for
     auto issue_chunk = [&](int ci) {
         const int c0 = ci * chunk, len = min(chunk, n - c0);
         const Seg g = seg(c0, len);
         for (int idx = tid; idx < len * 3; idx += ATT_THREADS) {
-            const int k = idx / 3, part = idx % 3, p = k < g.nA ? g.pA + k : g.pB + k - g.nA;
-            cp_async16(&sm.k[k][part * 16], k8 + (size_t)p * 48 + part * 16, true);
-        }
-        for (int idx = tid; idx < (g.ngA + g.ngB) * 16; idx += ATT_THREADS) {
-            const int w = idx >> 4, part = idx & 15, src = w < g.ngA ? g.gA0 + w : g.gB0 + w - g.ngA;
-            cp_async16(&sm.vg[w][(part * 4) ^ ((w & 3) << 3)], v8 + (size_t)src * 256 + part * 16, true);
+            const int8_t* src = idx < 3 * g.nA ? k8 + (size_t)g.pA * 48 + idx * 16 : k8 + (size_t)g.pB * 48 + (idx - 3 * g.nA) * 16;
+            cp_async16(&sm.k[0][0] + idx * 16, src, true);
         }
         for (int k = tid; k < len; k += ATT_THREADS) {
             const int p = k < g.nA ? g.pA + k : g.pB + k - g.nA;
             cp_async4(&sm.ks[k], c.ks + kvrow + p);
             cp_async4(&sm.vs[k], c.vs + kvrow + p);
+        }
+        asm volatile("cp.async.commit_group;\n" ::);
+        for (int idx = tid; idx < (g.ngA + g.ngB) * 16; idx += ATT_THREADS) {
+            const int w = idx >> 4, part = idx & 15, src = w < g.ngA ? g.gA0 + w : g.gB0 + w - g.ngA;
+            cp_async16(&sm.vg[w][(part * 4) ^ ((w & 3) << 3)], v8 + (size_t)src * 256 + part * 16, true);
         }
         asm volatile("cp.async.commit_group;\n" ::);
     };
@@ -1222,7 +1244,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 5) attention_kernel(const float* 
         const int c0 = ci * chunk, len = min(chunk, n - c0), blocked = len / 4 * 4;
         const Seg sg = seg(c0, len);
         const int ng = sg.ngA + sg.ngB;
-        asm volatile("cp.async.wait_group 0;\n" ::);
+        asm volatile("cp.async.wait_group 1;\n" ::);  // keys and scales
         __syncthreads();
         // scores: (ks * dot) * qs in whole 4-blocks, (ks * qs) * dot after
         int qr[12];
@@ -1265,6 +1287,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 5) attention_kernel(const float* 
         float a = 0.f;
         if (lane < 8) {
             const int n8 = len / 8 * 8;
+#pragma unroll 4
             for (int q = 0; q < n8; q += 8) a = __fadd_rn(a, srow[q + lane]);
             if (lane < 4 && blocked > n8) a = __fadd_rn(a, srow[n8 + lane]);
         }
@@ -1307,7 +1330,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 5) attention_kernel(const float* 
             dg[4 * ATT_MAXGROUPS] = (int8_t)((wq >> 7) & 127);
             dg[8 * ATT_MAXGROUPS] = (int8_t)(wq & 127);
         }
-        __syncwarp();
+        asm volatile("cp.async.wait_group 0;\n" ::);  // value groups
+        __syncthreads();
         // P.V on the tensor cores, 8 groups (32 keys) a step: A rows 0-2 are
         // the digit planes (lane gid < 3 loads plane gid's words of groups
         // g0 = 8 ks + tig and g0 + 4, zero past the chunk's groups), the
