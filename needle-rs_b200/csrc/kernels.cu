@@ -1481,6 +1481,7 @@ struct PostSmem {
     int perm1[1024], perm2[1024];
     // the rows' buffers take 16-byte copies and loads at any row count
     __align__(16) float x2[POST_ROWS][768];
+    __align__(16) float hs[POST_ROWS][768];  // h2 = zcn(x2, pre_hada), the conditioning input
     __align__(16) float buf[2][POST_ROWS][PV];
     __align__(16) float gates[POST_ROWS][24];
     float part[POST_ROWS][32];
@@ -1553,16 +1554,28 @@ __device__ __forceinline__ void kron_pass2(const float* mt, const float* B, floa
     }
 }
 
-// A Kronecker stage of every row: z in buf[from], result t in buf[from]
-// too (pass 1 writes mt into buf[1 - from]). Warp q for row q. (Tiles of
-// 4 x 4 over two warps a row measured slower: the passes are bound by
-// shared-memory wavefronts, three per 16 paired fmas here.)
-__device__ __forceinline__ void kron_stage_rows(PostSmem& sm, int fa, int fb, int from, int tid) {
-    const int q = tid >> 5, i = tid & 31, r0 = (i & 7) * 4, c0 = (i >> 3) * 8;
-    if (tid < POST_ROWS * 32) kron_pass1(sm.kf[fa], sm.buf[from][q], sm.buf[1 - from][q], r0, c0);
-    __syncthreads();
-    if (tid < POST_ROWS * 32) kron_pass2(sm.buf[1 - from][q], sm.kf[fb], sm.buf[from][q], r0, c0);
-    __syncthreads();
+// A Kronecker stage of row q by one warp: z in buf[from], result t in
+// buf[from] too (pass 1 writes mt into buf[1 - from]). Both passes of a row
+// are the one warp's, so only a warp barrier sits between them; the caller
+// puts a block barrier before the result is read. (Tiles of 4 x 4 over two
+// warps a row measured slower: the passes are bound by shared-memory
+// wavefronts, three per 16 paired fmas here.)
+__device__ __forceinline__ void kron_stage_row(PostSmem& sm, int fa, int fb, int from, int q, int lane) {
+    const int r0 = (lane & 7) * 4, c0 = (lane >> 3) * 8;
+    kron_pass1(sm.kf[fa], sm.buf[from][q], sm.buf[1 - from][q], r0, c0);
+    __syncwarp();
+    kron_pass2(sm.buf[1 - from][q], sm.kf[fb], sm.buf[from][q], r0, c0);
+}
+
+// dot16_combine over each half-warp (chain c in lane c of the half); the
+// total is valid in lanes 0 and 16. Every lane of the warp must call it.
+__device__ __forceinline__ float dot16_combine_half(float acc, int ln) {
+    const unsigned F = 0xffffffffu;
+    const int l = ln & 3;
+    float a4 = __shfl_sync(F, acc, 4 + l, 16), a8 = __shfl_sync(F, acc, 8 + l, 16), a12 = __shfl_sync(F, acc, 12 + l, 16);
+    float t = __fadd_rn(__fadd_rn(__fadd_rn(a8, a12), a4), acc);
+    float t1 = __shfl_sync(F, t, 1, 16), t2 = __shfl_sync(F, t, 2, 16), t3 = __shfl_sync(F, t, 3, 16);
+    return __fadd_rn(__fadd_rn(t, t1), __fadd_rn(t2, t3));
 }
 
 __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, const float* o, const float* x1, const float* u,
@@ -1604,13 +1617,14 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
     asm volatile("cp.async.commit_group;\n" ::);
     asm volatile("cp.async.wait_group 0;\n" ::);
     __syncthreads();
-    // zcn(o, post_norm): sixteen dot16 chains per row
-    if (tid < POST_ROWS * 16) {
+    // zcn(o, post_norm): sixteen dot16 chains per row, a half-warp a row
+    constexpr int NORM_THREADS = (POST_ROWS * 16 + 31) / 32 * 32;
+    if (tid < NORM_THREADS) {
         const int q = tid >> 4;
-        sm.part[q][tid & 15] = dot16_chain(sm.x2[q], sm.x2[q], 768, tid & 15);
+        const float ch = q < POST_ROWS ? dot16_chain(sm.x2[q], sm.x2[q], 768, tid & 15) : 0.f;
+        const float tot = dot16_combine_half(ch, tid & 31);
+        if ((tid & 15) == 0 && q < POST_ROWS) sm.sc[q][0] = rinv(tot, 768);
     }
-    __syncthreads();
-    if (tid < POST_ROWS) sm.sc[tid][0] = rinv(dot16_combine(sm.part[tid]), 768);
     __syncthreads();
     const float ga = __fdiv_rn(1.0f, __fadd_rn(lexpf(-w.attn_gate), 1.0f));
     for (int k = tid; k < POST_ROWS * 768; k += POST_THREADS) {
@@ -1621,19 +1635,19 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
     }
     asm volatile("cp.async.wait_group 0;\n" ::);
     __syncthreads();
-    if (tid < POST_ROWS * 16) {
+    if (tid < NORM_THREADS) {
         const int q = tid >> 4;
-        sm.part[q][tid & 15] = dot16_chain(sm.x2[q], sm.x2[q], 768, tid & 15);
+        const float ch = q < POST_ROWS ? dot16_chain(sm.x2[q], sm.x2[q], 768, tid & 15) : 0.f;
+        const float tot = dot16_combine_half(ch, tid & 31);
+        if ((tid & 15) == 0 && q < POST_ROWS) sm.sc[q][1] = rinv(tot, 768);
     }
     __syncthreads();
-    if (tid < POST_ROWS) sm.sc[tid][1] = rinv(dot16_combine(sm.part[tid]), 768);
-    __syncthreads();
-    // h2 = zcn(x2, pre_hada) into buf[1] (plain layout), z = h2 * d1 into buf[0]
+    // h2 = zcn(x2, pre_hada) into hs, z = h2 * d1 into buf[0]
     for (int k = tid; k < POST_ROWS * 768; k += POST_THREADS) {
         int q = k / 768, c = k % 768;
         float tt = __fmul_rn(sm.x2[q][c], sm.sc[q][1]);
         float h = __fmaf_rn(tt, sm.pre_hada[c], tt);
-        sm.buf[1][q][c] = h;
+        sm.hs[q][c] = h;
         sm.buf[0][q][pv_idx(c)] = __fmul_rn(h, sm.d1[c]);
     }
     for (int k = tid; k < POST_ROWS * 256; k += POST_THREADS) {
@@ -1641,14 +1655,19 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
         sm.buf[0][q][pv_idx(c)] = 0.f;
     }
     __syncthreads();
-    // conditioning logits: 4 accumulator sets by j % 4, fma chains over j
+    // conditioning logits on warps 0..R-1 (4 accumulator sets by j % 4, fma
+    // chains over j) while warps R..2R-1 run the first Kronecker stage
+    // (t1 in buf[0])
+    static_assert(2 * POST_ROWS * 32 <= POST_THREADS, "two warp sets");
     if (tid < POST_ROWS * 32) {
         const int q = tid >> 5, set = (tid >> 3) & 3, k = tid & 7;
-        const float* h = sm.buf[1][q];
+        const float* h = sm.hs[q];
         float acc = 0.f;
 #pragma unroll 16
         for (int j = set; j < 768; j += 4) acc = __fmaf_rn(h[j], sm.cond_v[j * 8 + k], acc);
         sm.part[q][tid & 31] = acc;
+    } else if (tid < 2 * POST_ROWS * 32) {
+        kron_stage_row(sm, 0, 1, 0, (tid >> 5) - POST_ROWS, tid & 31);
     }
     __syncthreads();
     // cond_v is done with: the rows' u arrive there during the MLP
@@ -1675,7 +1694,7 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
         float sum = __fadd_rn(ev[7], __fadd_rn(__fadd_rn(ev[6], __fadd_rn(ev[5], ev[4])), __fadd_rn(__fadd_rn(ev[3], ev[2]), __fadd_rn(ev[1], ev[0]))));
         if ((tid & 31) < 8) sm.wk[q][k] = __fmul_rn(e, __fdiv_rn(1.0f, sum));
     }
-    kron_stage_rows(sm, 0, 1, 0, tid);  // t1 in buf[0]
+    __syncthreads();
     // z = fma(t1[perm1[j]], cond[j] * d2[j], b2[j]) with cond = 1 + sum_k w_k u_k,
     // then SiLU; into buf[1]
     for (int j = tid; j < 1024; j += POST_THREADS) {
@@ -1694,7 +1713,8 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
         }
     }
     __syncthreads();
-    kron_stage_rows(sm, 2, 3, 1, tid);  // t2 in buf[1]
+    if (tid < POST_ROWS * 32) kron_stage_row(sm, 2, 3, 1, tid >> 5, tid & 31);  // t2 in buf[1]
+    __syncthreads();
     for (int j = tid; j < 1024; j += POST_THREADS) {
         const float d3 = sm.d3[j];
         const int src = pv_idx(sm.perm2[j]), dst = pv_idx(j);
@@ -1717,7 +1737,7 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
         _Pragma("unroll") for (int b = 0; b < 4; b++) dst[e][b] = xr[b * 768];                        \
     }
     POST_LOAD_OLD(cur, 0)  // in flight during the last Kronecker stage
-    kron_stage_rows(sm, 4, 5, 0, tid);  // t3 in buf[0]
+    if (tid < POST_ROWS * 32) kron_stage_row(sm, 4, 5, 0, tid >> 5, tid & 31);  // t3 in buf[0]
     asm volatile("cp.async.wait_group 0;\n" ::);
     __syncthreads();
 #pragma unroll
