@@ -49,7 +49,9 @@ void nd_model_free(nd_model* m);
 int nd_model_dims(const nd_model* m, int* dims);
 
 /* model.rs:264-274 (Model::session), for `num_seqs` sequences of up to
- * `max_len` positions each. */
+ * `max_len` positions each. `max_len` must lie in [1, max_seq_len] and be
+ * at most 8192 (the attention kernel holds 32 key chunks of 256); beyond
+ * that the call fails with a message, as a too-long session does. */
 int nd_batch_new(nd_model* m, int num_seqs, int max_len, nd_batch** out);
 void nd_batch_free(nd_batch* b);
 

@@ -949,15 +949,18 @@ void launch_mhc_gates(LayerW w, int lane, int M, float* gates, cudaStream_t st) 
 // ------------------------------------------------ conv taps, RoPE, int8 KV
 
 // infer.rs:1430-1526 (chunk rows) as unit work (infer/step.rs:468-516): per
-// row, 12 q heads, 2 k heads and 2 v heads, one unit each; a CTA of eight
-// warps takes a row, warp w units w and w + 8, with every load of both
-// units issued before either is worked on (a row in 256 threads, so the
-// batch's rows are resident at once: 1024 rows fit 148 SMs x 8). The taps
-// read earlier rows of this chunk, else the pre-tap history, else zeros.
-constexpr int CONV_THREADS = 256;
-__global__ void __launch_bounds__(CONV_THREADS, 8) conv_rope_kv_kernel(LayerW w, int l, const float* proj, Caches c, int T,
-                                                                    const int32_t* p0p, int hist_base, const float* cosr,
-                                                                    const float* sinr, float* qbuf) {
+// row, 12 q heads, 2 k heads and 2 v heads, one unit each. A CTA takes a
+// row: with UPW = 2, eight warps, warp w units w and w + 8, every load of
+// both units issued before either is worked on (a row in 256 threads, so a
+// large batch's rows are resident at once: 1024 rows fit 148 SMs x 8); with
+// UPW = 1, sixteen warps, one unit each (the shorter chain for small
+// batches). The taps read earlier rows of this chunk, else the pre-tap
+// history, else zeros.
+template <int UPW>
+__global__ void __launch_bounds__(512 / UPW, 8 / (3 - UPW)) conv_rope_kv_kernel(LayerW w, int l, const float* proj, Caches c,
+                                                                             int T, const int32_t* p0p, int hist_base,
+                                                                             const float* cosr, const float* sinr, float* qbuf) {
+    constexpr int WARPS = 16 / UPW;
     pdl_launch_dependents();
     pdl_wait();
     const int p0 = *p0p;
@@ -970,14 +973,15 @@ __global__ void __launch_bounds__(CONV_THREADS, 8) conv_rope_kv_kernel(LayerW w,
         else if (unit < 14) { int kh = unit - 12; start = 576 + kh * 48; cw = 96; cc = kh * 48; len = 48; wt = w.k_taps; }
         else { int vh = unit - 14; start = 672 + vh * 64; cw = 128; cc = vh * 64; len = 64; wt = w.v_taps; }
     };
-    // every row load of the lane's (at most two) channels of both units
-    // first, then the tap weights (cache-resident), history writes and taps
-    float cur[2][2], prev[2][2][2];
+    // every row load of the lane's (at most two) channels of the warp's
+    // units first, then the tap weights (cache-resident), history writes
+    // and taps
+    float cur[UPW][2], prev[UPW][2][2];
 #pragma unroll
-    for (int r = 0; r < 2; r++) {
+    for (int r = 0; r < UPW; r++) {
         int start, cw, cc, len;
         const float* wt;
-        unit_of(warp + 8 * r, start, cw, cc, len, wt);
+        unit_of(warp + WARPS * r, start, cw, cc, len, wt);
 #pragma unroll
         for (int t = 0; t < 2; t++) {
             const int k = lane + 32 * t;
@@ -995,11 +999,11 @@ __global__ void __launch_bounds__(CONV_THREADS, 8) conv_rope_kv_kernel(LayerW w,
         }
     }
 #pragma unroll
-    for (int r = 0; r < 2; r++) {
+    for (int r = 0; r < UPW; r++) {
         int start, cw, cc, len;
         const float* wt;
-        unit_of(warp + 8 * r, start, cw, cc, len, wt);
-        float* x = buf[warp + 8 * r];
+        unit_of(warp + WARPS * r, start, cw, cc, len, wt);
+        float* x = buf[warp + WARPS * r];
 #pragma unroll
         for (int t = 0; t < 2; t++) {
             const int k = lane + 32 * t;
@@ -1016,8 +1020,8 @@ __global__ void __launch_bounds__(CONV_THREADS, 8) conv_rope_kv_kernel(LayerW w,
     }
     __syncwarp();
 #pragma unroll 1
-    for (int r = 0; r < 2; r++) {
-        const int unit = warp + 8 * r, len = unit < 14 ? 48 : 64;
+    for (int r = 0; r < UPW; r++) {
+        const int unit = warp + WARPS * r, len = unit < 14 ? 48 : 64;
         float* x = buf[unit];
         if (unit < 14) {
             // zcn_inplace (infer.rs:446-452) over the 48-wide head, dot16 order.
@@ -1086,7 +1090,11 @@ __global__ void __launch_bounds__(CONV_THREADS, 8) conv_rope_kv_kernel(LayerW w,
 void launch_conv_rope_kv(LayerW w, int l, const float* proj, Caches c, int S, int T, int p0, int hist_base, const float* cosr,
                          const float* sinr, float* qbuf, cudaStream_t st) {
     COUNT_LAUNCH();
-    launch_pdl(conv_rope_kv_kernel, dim3(S * T), dim3(CONV_THREADS), 0, st, w, l, proj, c, T, c.len, hist_base, cosr, sinr, qbuf);
+    // 512-thread CTAs at 32 registers fit four an SM: one wave up to 592 rows
+    if (S * T <= 592)
+        launch_pdl(conv_rope_kv_kernel<1>, dim3(S * T), dim3(512), 0, st, w, l, proj, c, T, c.len, hist_base, cosr, sinr, qbuf);
+    else
+        launch_pdl(conv_rope_kv_kernel<2>, dim3(S * T), dim3(256), 0, st, w, l, proj, c, T, c.len, hist_base, cosr, sinr, qbuf);
 }
 
 // ------------------------------------------------------------- attention
@@ -1772,10 +1780,10 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
 // The same post block for small batches: one row per CTA of 512 threads,
 // the layer's small weights staged into shared memory as post_block_kernel
 // stages them (before the wait on the predecessor), every thread on the one
-// row. A Kronecker pass gives each thread two outputs: in pass 1 thread t
-// owns r = t % 32 and columns c0 = 2 (t / 32), c0 + 1 (mt stored transposed,
-// as kron_native keeps it); in pass 2 the same r and columns of t. Every
-// float op, and its order, is that of post_block_kernel.
+// row. A Kronecker pass runs on warps 1-4, a 2 x 4 tile of outputs a
+// thread (mt stored transposed, as kron_native keeps it), while warp 0's
+// conditioning chains may still run. Every float op, and its order, is
+// that of post_block_kernel.
 constexpr int POST_ROW_MAX_M = 296, POST_ROW_THREADS = 512;
 struct PostRowSmem {
     float kf[6][1024];
@@ -1790,25 +1798,50 @@ struct PostRowSmem {
 };
 extern const size_t POST_ROW_SMEM = sizeof(PostRowSmem);
 
-__device__ __forceinline__ void kron_row_pass1(const float* A, const float* z, float* mt, int r, int c0) {
-    float2 o = make_float2(0.f, 0.f);
+// The one-row Kronecker passes: 128 threads, each a 2 x 4 tile (rows r0,
+// r0 + 1; columns c0..c0 + 3), one 8-byte and one 16-byte shared load per
+// four paired fmas; every output one fma chain over j = 0..31 from zero.
+// Pass 1: mt[c][r] = sum_j A[j][r] z[j][c] (stored transposed).
+__device__ __forceinline__ void kron_row_pass1(const float* A, const float* z, float* mt, int r0, int c0) {
+    float2 o[2][2];
+#pragma unroll
+    for (int a = 0; a < 2; a++) o[a][0] = o[a][1] = make_float2(0.f, 0.f);
 #pragma unroll 8
     for (int j = 0; j < 32; j++) {
-        const float a = A[j * 32 + r];
-        o = fma2(make_float2(a, a), *(const float2*)(z + j * 32 + c0), o);
+        const float2 a2 = *(const float2*)(A + j * 32 + r0);
+        const float4 z4 = *(const float4*)(z + j * 32 + c0);
+        const float ar[2] = {a2.x, a2.y};
+#pragma unroll
+        for (int a = 0; a < 2; a++) {
+            o[a][0] = fma2(make_float2(ar[a], ar[a]), make_float2(z4.x, z4.y), o[a][0]);
+            o[a][1] = fma2(make_float2(ar[a], ar[a]), make_float2(z4.z, z4.w), o[a][1]);
+        }
     }
-    mt[c0 * 32 + r] = o.x;
-    mt[(c0 + 1) * 32 + r] = o.y;
+    *(float2*)(mt + c0 * 32 + r0) = make_float2(o[0][0].x, o[1][0].x);
+    *(float2*)(mt + (c0 + 1) * 32 + r0) = make_float2(o[0][0].y, o[1][0].y);
+    *(float2*)(mt + (c0 + 2) * 32 + r0) = make_float2(o[0][1].x, o[1][1].x);
+    *(float2*)(mt + (c0 + 3) * 32 + r0) = make_float2(o[0][1].y, o[1][1].y);
 }
 
-__device__ __forceinline__ void kron_row_pass2(const float* mt, const float* B, float* t, int r, int c0) {
-    float2 o = make_float2(0.f, 0.f);
+// Pass 2: t[r][c] = sum_j mt[j][r] B[j][c].
+__device__ __forceinline__ void kron_row_pass2(const float* mt, const float* B, float* t, int r0, int c0) {
+    float2 o[2][2];
+#pragma unroll
+    for (int a = 0; a < 2; a++) o[a][0] = o[a][1] = make_float2(0.f, 0.f);
 #pragma unroll 8
     for (int j = 0; j < 32; j++) {
-        const float m = mt[j * 32 + r];
-        o = fma2(make_float2(m, m), *(const float2*)(B + j * 32 + c0), o);
+        const float2 m2 = *(const float2*)(mt + j * 32 + r0);
+        const float4 b4 = *(const float4*)(B + j * 32 + c0);
+        const float mr[2] = {m2.x, m2.y};
+#pragma unroll
+        for (int a = 0; a < 2; a++) {
+            o[a][0] = fma2(make_float2(mr[a], mr[a]), make_float2(b4.x, b4.y), o[a][0]);
+            o[a][1] = fma2(make_float2(mr[a], mr[a]), make_float2(b4.z, b4.w), o[a][1]);
+        }
     }
-    *(float2*)(t + r * 32 + c0) = o;
+#pragma unroll
+    for (int a = 0; a < 2; a++)
+        *(float4*)(t + (r0 + a) * 32 + c0) = make_float4(o[a][0].x, o[a][0].y, o[a][1].x, o[a][1].y);
 }
 
 __global__ void __launch_bounds__(POST_ROW_THREADS, 1) post_row_kernel(LayerW w, const float* o, const float* x1, const float* u,
@@ -1817,7 +1850,10 @@ __global__ void __launch_bounds__(POST_ROW_THREADS, 1) post_row_kernel(LayerW w,
     pdl_launch_dependents();
     extern __shared__ __align__(16) int8_t post_row_raw[];
     PostRowSmem& sm = *reinterpret_cast<PostRowSmem*>(post_row_raw);
-    const int tid = threadIdx.x, m = blockIdx.x, r = tid & 31, c0 = 2 * (tid >> 5);
+    const int tid = threadIdx.x, m = blockIdx.x;
+    // the Kronecker passes run on warps 1-4 (warp 0 has the conditioning chains)
+    const int kt = tid - 32, r0 = 2 * (kt & 15), c0 = 4 * (kt >> 4);
+    const bool kw = kt >= 0 && kt < 128;
     for (int f = 0; f < 6; f++) stage<POST_ROW_THREADS>(sm.kf[f], w.kron[f], 4096, tid);
     stage<POST_ROW_THREADS>(sm.cond_v, w.cond_v, 768 * 8 * 4, tid);
     stage<POST_ROW_THREADS>(sm.cond_u, w.cond_u, 8 * 1024 * 4, tid);
@@ -1893,9 +1929,9 @@ __global__ void __launch_bounds__(POST_ROW_THREADS, 1) post_row_kernel(LayerW w,
         if (tid < 8) sm.wk[k] = __fmul_rn(e, __fdiv_rn(1.0f, sum));
     }
     // stage 1: t1 = (A0^T z) A1
-    kron_row_pass1(sm.kf[0], sm.zb, sm.mb, r, c0);
+    if (kw) kron_row_pass1(sm.kf[0], sm.zb, sm.mb, r0, c0);
     __syncthreads();
-    kron_row_pass2(sm.mb, sm.kf[1], sm.tb, r, c0);
+    if (kw) kron_row_pass2(sm.mb, sm.kf[1], sm.tb, r0, c0);
     __syncthreads();
     // z = fma(t1[perm1[j]], cond[j] * d2[j], b2[j]), cond = 1 + sum_k w_k u_k, then SiLU
     for (int j = tid; j < 1024; j += POST_ROW_THREADS) {
@@ -1906,15 +1942,15 @@ __global__ void __launch_bounds__(POST_ROW_THREADS, 1) post_row_kernel(LayerW w,
         sm.zb[j] = __fdiv_rn(zz, __fadd_rn(nexp(-zz), 1.0f));
     }
     __syncthreads();
-    kron_row_pass1(sm.kf[2], sm.zb, sm.mb, r, c0);
+    if (kw) kron_row_pass1(sm.kf[2], sm.zb, sm.mb, r0, c0);
     __syncthreads();
-    kron_row_pass2(sm.mb, sm.kf[3], sm.tb, r, c0);
+    if (kw) kron_row_pass2(sm.mb, sm.kf[3], sm.tb, r0, c0);
     __syncthreads();
     for (int j = tid; j < 1024; j += POST_ROW_THREADS) sm.zb[j] = __fmul_rn(sm.tb[sm.perm2[j]], sm.d3[j]);
     __syncthreads();
-    kron_row_pass1(sm.kf[4], sm.zb, sm.mb, r, c0);
+    if (kw) kron_row_pass1(sm.kf[4], sm.zb, sm.mb, r0, c0);
     __syncthreads();
-    kron_row_pass2(sm.mb, sm.kf[5], sm.tb, r, c0);
+    if (kw) kron_row_pass2(sm.mb, sm.kf[5], sm.tb, r0, c0);
     __syncthreads();
     // mHC write (infer.rs:1587-1606): y = x2 + mlp - u, stream a =
     // y * hpost[a] + sum_b old[b] * hres[a][b]
