@@ -293,7 +293,6 @@ template <bool DECODE, bool TWO>
 __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y,
                                                         int ldy, int col0) {
     pdl_launch_dependents();
-    pdl_wait();
     extern __shared__ __align__(16) int8_t smem[];
     int8_t* ws = smem;                                        // [BN][LD]
     int8_t* as = smem + MMA_BN * MMA_LD;                      // [BM][LD]
@@ -303,7 +302,9 @@ __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* 
     const int tilesN = (W.out + MMA_BN - 1) / MMA_BN, ntiles = tilesN * ((M + MMA_BM - 1) / MMA_BM);
     const int first = blockIdx.x, stride = gridDim.x;
     const int iters = first < ntiles ? ((ntiles - 1 - first) / stride + 1) * 6 : 0;
-    auto issue = [&](int k) {
+    // the copies of iteration k: the weight rows (and the tile's norms) when
+    // W, the activation rows (and their scales) when A
+    auto issue_part = [&](int k, bool wpart, bool apart) {
         if (k < iters) {
             const int t = first + (k / 6) * stride, g = k % 6;
             const int tn0 = (t % tilesN) * MMA_BN, tm0 = (t / tilesN) * MMA_BM;
@@ -312,30 +313,46 @@ __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* 
                 if (r < MMA_BN) {
                     int n = tn0 + r;
                     bool ok = n < W.out;
-                    cp_async16(ws + r * MMA_LD + g * 128 + c * 16, W.w8 + (size_t)(ok ? n : 0) * MMA_K + g * 128 + c * 16, ok);
+                    if (wpart)
+                        cp_async16(ws + r * MMA_LD + g * 128 + c * 16, W.w8 + (size_t)(ok ? n : 0) * MMA_K + g * 128 + c * 16, ok);
                 } else {
                     int mr = r - MMA_BN, m = tm0 + mr;
                     bool ok = m < M;
-                    cp_async16(as + mr * MMA_LD + g * 128 + c * 16, act + (size_t)(ok ? m : 0) * MMA_K + g * 128 + c * 16, ok);
+                    if (apart)
+                        cp_async16(as + mr * MMA_LD + g * 128 + c * 16, act + (size_t)(ok ? m : 0) * MMA_K + g * 128 + c * 16, ok);
                 }
             }
             if (g == 0) {
                 float* bx = s_sx + ((k / 6) & 1) * MMA_BM * 6;
                 uint16_t* bn = s_nr + ((k / 6) & 1) * MMA_BN * 6;
-                for (int idx = tid; idx < MMA_BM * 6; idx += 256) {
-                    const int m = tm0 + idx / 6;
-                    cp_async4z(bx + idx, sx + (size_t)(m < M ? m : 0) * 6 + idx % 6, m < M);
-                }
-                for (int idx = tid; idx < MMA_BN * 3; idx += 256) {
-                    const int n = tn0 + idx / 3;
-                    cp_async4z(bn + 2 * idx, W.norms + (size_t)(n < W.out ? n : 0) * 6 + 2 * (idx % 3), n < W.out);
-                }
+                if (apart)
+                    for (int idx = tid; idx < MMA_BM * 6; idx += 256) {
+                        const int m = tm0 + idx / 6;
+                        cp_async4z(bx + idx, sx + (size_t)(m < M ? m : 0) * 6 + idx % 6, m < M);
+                    }
+                if (wpart)
+                    for (int idx = tid; idx < MMA_BN * 3; idx += 256) {
+                        const int n = tn0 + idx / 3;
+                        cp_async4z(bn + 2 * idx, W.norms + (size_t)(n < W.out ? n : 0) * 6 + 2 * (idx % 3), n < W.out);
+                    }
             }
         }
+    };
+    auto issue = [&](int k) {
+        issue_part(k, true, true);
         asm volatile("cp.async.commit_group;\n" ::);
     };
+    // the first five iterations' weight copies go out before the wait on the
+    // predecessor (they join the first commit group), their activation
+    // copies after it, one commit group each
 #pragma unroll 1
-    for (int k = 0; k < 5; k++) issue(k);
+    for (int k = 0; k < 5; k++) issue_part(k, true, false);
+    pdl_wait();
+#pragma unroll 1
+    for (int k = 0; k < 5; k++) {
+        issue_part(k, false, true);
+        asm volatile("cp.async.commit_group;\n" ::);
+    }
     const float cbs = W.cbs;
     const int wm = (warp & 3) * 16, wn = (warp >> 2) * 32;
     const int gid = lane >> 2, tig = lane & 3;
@@ -492,10 +509,14 @@ template <int FMT>
 __global__ void __launch_bounds__(256) cq_gemv_kernel(DevMat W, const int8_t* act, const float* sx, int M, float* y, int ldy,
                                                       int col0) {
     pdl_launch_dependents();
-    pdl_wait();
+    // the weight row's codes and norms are the layer's, not the predecessor's:
+    // they are read and decoded before the wait on it
     const int lane = threadIdx.x & 31;
     const int n = blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (n >= W.out) return;
+    if (n >= W.out) {
+        pdl_wait();
+        return;
+    }
     const int wi = lane & 15, a = wi >> 2, l = wi & 3, half = lane >> 4;
     const int slot = l * 32 + (a & 1) * 16 + (a >> 1) * 8;  // lane_major_pos of the block
     int wl[3], wh[3];
@@ -528,6 +549,7 @@ __global__ void __launch_bounds__(256) cq_gemv_kernel(DevMat W, const int8_t* ac
     const float cbs = W.cbs;
     float norm_l = 0.f;  // lane g < 6 holds norm[n][g]
     if (lane < 6) norm_l = h2f(W.norms[(size_t)n * 6 + lane]);
+    pdl_wait();
     for (int m = 0; m < M; m++) {
         const int8_t* ar = act + (size_t)m * 768;
         int s[3];
