@@ -1726,20 +1726,34 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
     }
     __syncthreads();
     // z = fma(t1[perm1[j]], cond[j] * d2[j], b2[j]) with cond = 1 + sum_k w_k u_k,
-    // then SiLU; into buf[1]
-    for (int j = tid; j < 1024; j += POST_THREADS) {
+    // then SiLU; into buf[1]. Whole strides of j take every row; the last,
+    // partial stride's (j, row) items are spread over all threads, RT rows
+    // a thread, so no warp runs a third stride alone.
+    auto silu_item = [&](int j, int q0, int nq) {
         float cu[8];
 #pragma unroll
         for (int kk = 0; kk < 8; kk++) cu[kk] = sm.cond_u[kk * 1024 + j];
         const float d2 = sm.d2[j], b2 = sm.b2[j];
         const int src = pv_idx(sm.perm1[j]), dst = pv_idx(j);
 #pragma unroll
-        for (int q = 0; q < POST_ROWS; q++) {
+        for (int qq = 0; qq < POST_ROWS; qq++) {
+            if (qq >= nq) break;
+            const int q = q0 + qq;
             float cnd = 1.0f;
 #pragma unroll
             for (int kk = 0; kk < 8; kk++) cnd = __fmaf_rn(cu[kk], sm.wk[q][kk], cnd);
             float zz = __fmaf_rn(sm.buf[0][q][src], __fmul_rn(cnd, d2), b2);
             sm.buf[1][q][dst] = __fdiv_rn(zz, __fadd_rn(nexp(-zz), 1.0f));
+        }
+    };
+    {
+        constexpr int FULL = 1024 / POST_THREADS * POST_THREADS, TAIL = 1024 - FULL;
+        for (int j = tid; j < FULL; j += POST_THREADS) silu_item(j, 0, POST_ROWS);
+        if (TAIL > 0) {
+            // POST_THREADS / TAIL thread sets, each taking RT rows of the tail
+            constexpr int SETS = POST_THREADS / (TAIL > 0 ? TAIL : 1), RT = (POST_ROWS + SETS - 1) / SETS;
+            const int set = tid / (TAIL > 0 ? TAIL : 1), q0 = set * RT;
+            if (set < SETS && q0 < POST_ROWS) silu_item(FULL + tid % TAIL, q0, min(RT, POST_ROWS - q0));
         }
     }
     __syncthreads();
