@@ -94,6 +94,29 @@ def test_chunks_then_decode(small):
         assert bits_equal(got, want), f"step {k}: " + describe_diff("decode logits", got, want)
 
 
+def test_long_context_key_chunks(small):
+    """A 300-token feed in two sequences, then 6 decode steps: the global
+    layer's rows pass 256 keys, so prefill rows split their keys into two
+    chunks and decode rows into four (key_chunks' rule for one-token steps),
+    and the per-chunk parts are merged; logits bit for bit every step."""
+    g, o = small
+    rng = np.random.default_rng(11)
+    S, n, steps = 2, 300, 6
+    ids = rng.integers(0, g.vocab, (S, n)).astype(np.int32)
+    b = g.batch(S, n + steps + 1)
+    sess = [o.session() for _ in range(S)]
+    got = b.forward(ids)[:, 0]
+    want = [sess[s_].forward(ids[s_].astype(np.uint32))[0] for s_ in range(S)]
+    for s_ in range(S):
+        assert bits_equal(got[s_], want[s_]), describe_diff(f"prefill seq {s_}", got[s_], want[s_])
+    for k in range(steps):
+        nxt = np.array([[int(np.argmax(want[s_]))] for s_ in range(S)], np.int32)
+        got = b.forward(nxt)[:, 0]
+        want = [sess[s_].forward(nxt[s_].astype(np.uint32))[0] for s_ in range(S)]
+        for s_ in range(S):
+            assert bits_equal(got[s_], want[s_]), f"step {k}: " + describe_diff(f"decode seq {s_}", got[s_], want[s_])
+
+
 def test_all_logits_and_hidden(small):
     g, o = small
     from oracle import oracle as orc
