@@ -21,11 +21,13 @@ def small(small_archive, cuda_device):
     return nb.Model(small_archive, cuda_device), orc.Model(small_archive)
 
 
-@pytest.mark.parametrize("sink,ring", [(5, 20), (9, 40), (0, 16), (50, 30)])
-def test_span_prefill_and_decode(small, sink, ring):
+@pytest.mark.parametrize("sink,ring,n", [(5, 20, 70), (9, 40, 70), (0, 16, 70), (50, 30, 70), (40, 260, 320)])
+def test_span_prefill_and_decode(small, sink, ring, n):
+    """The last case passes 256 keys in the global layer: key chunks that
+    hold the end of the sink run and the start of the ring run together."""
     g, o = small
     rng = np.random.default_rng(sink * 100 + ring)
-    S, n, steps = 3, 70, 10
+    S, steps = 3, 10
     prompts = rng.integers(0, g.vocab, (S, n)).astype(np.int32)
     b = g.batch(S, n + steps + 1)
     b.set_attend(sink, ring)
