@@ -159,13 +159,16 @@ def test_batched_sequences_match_single(small):
         assert list(got[s_]) == list(want), f"sequence {s_}: {got[s_]} vs {want}"
 
 
-def test_batched_decode_many_sequences(small):
-    """144 sequences in one batch (matmul tiles of 64 and 128 rows, the last
-    partial) equal 144 separate oracle sessions through a 9-token prefill
-    and 4 masked greedy steps."""
+@pytest.mark.parametrize("S", [144, 600])
+def test_batched_decode_many_sequences(small, S):
+    """S sequences in one batch (matmul tiles of 64 rows, the last partial)
+    equal S separate oracle sessions through a 9-token prefill and 4 masked
+    greedy steps. At 144 the decode steps take the one-row post block and
+    the one-unit-a-warp conv; at 600 the seven-row post block and the
+    two-units-a-warp conv, as the bench's 1024 do."""
     g, o = small
     rng = np.random.default_rng(6)
-    S, n, steps = 144, 9, 4
+    n, steps = 9, 4
     prompts = rng.integers(0, g.vocab, (S, n)).astype(np.int32)
     mb = (g.out_rows + 7) // 8
     masks = np.zeros((S, steps, mb), np.uint8)
