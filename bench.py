@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Needle 3 batched agent decode on B200.
+"""Needle 3 batched agent decode on B200 (the headline throughput workload).
 
 Each GPU holds the 121M CQ-W4 model and 1024 independent sequences (weak
 scaling: sequences are partitioned across GPUs, no collective on the data
@@ -405,11 +405,11 @@ def embed_texts(local, dev, S=256, T=64):
 
 
 def secondary(model, local):
-    """The other BASELINE.json throughput configs on this GPU, reported beside
-    the headline: batch-1 decode (configs[0]: 118-token prompt, 45 greedy
+    """The other throughput workloads on this GPU, reported beside the
+    headline: batch-1 decode (118-token prompt, 45 greedy
     steps, as `needle bench --decode 45` drives the engine; again on a
-    low-width archive of the same geometry) and batched prefill (configs[3]:
-    256 sequences x 700 tokens, logits of the last position). CUDA events on
+    low-width archive of the same geometry) and batched prefill (256
+    sequences x 700 tokens, logits of the last position). CUDA events on
     the engine's stream."""
     import torch
 
