@@ -173,6 +173,13 @@ int nd_cqmat_new(int device, const unsigned char* codes, const unsigned short* n
                  nd_cqmat** out_mat);
 void nd_cqmat_free(nd_cqmat* mat);
 int nd_cqmat_apply(nd_cqmat* mat, const float* x, int M, int T, float* y, int reps, float* ms);
+/* Benchmark support: the matmul alone (no A8), launched back to back over
+ * the n matrices in turn, `reps` rounds after one untimed round, on the
+ * activations the last nd_cqmat_apply of mats[0] quantized (M <= its rows).
+ * When the matrices together exceed L2 every launch streams its weights
+ * from HBM. *ms = mean time per launch. The matrices share device and
+ * shape. */
+int nd_cqmat_time_rotating(nd_cqmat* const* mats, int n, int M, int T, int reps, float* ms);
 
 /* crates/needle-core/src/cact.rs:399-475 (pack) over random-init Needle 3
  * weights: every tensor ~N(0, std^2), seeded; CQ matrices, f16 small

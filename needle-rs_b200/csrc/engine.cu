@@ -1375,6 +1375,40 @@ int nd_cqmat_apply(nd_cqmat* h, const float* x, int M, int T, float* y, int reps
     }
 }
 
+int nd_cqmat_time_rotating(nd_cqmat* const* mats, int n, int M, int T, int reps, float* ms) {
+    try {
+        if (!mats || n < 1 || !ms || reps < 1) throw std::runtime_error("nd_cqmat_time_rotating: bad arguments");
+        nd_cqmat* h = mats[0];
+        if (!h || M < 1 || T < 1 || M % T || M > h->cap)
+            throw std::runtime_error("nd_cqmat_time_rotating: M must be a multiple of T within the last apply's rows");
+        for (int i = 0; i < n; i++)
+            if (!mats[i] || mats[i]->m.device != h->m.device || mats[i]->d.out != h->d.out)
+                throw std::runtime_error("nd_cqmat_time_rotating: matrices must share the device and shape");
+        CK(cudaSetDevice(h->m.device));
+        const int out = h->d.out;
+        auto round = [&]() {
+            for (int i = 0; i < n; i++) CK(launch_cq_gemm(mats[i]->d, h->act, h->sx, M, T, h->y, out, 0, h->st));
+        };
+        cudaEvent_t e0, e1;
+        CK(cudaEventCreate(&e0));
+        CK(cudaEventCreate(&e1));
+        round();
+        CK(cudaEventRecord(e0, h->st));
+        for (int k = 0; k < reps; k++) round();
+        CK(cudaEventRecord(e1, h->st));
+        CK(cudaEventSynchronize(e1));
+        float t = 0;
+        CK(cudaEventElapsedTime(&t, e0, e1));
+        *ms = t / ((float)reps * n);
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        CK(cudaGetLastError());
+        return 0;
+    } catch (std::exception& e) {
+        return fail(e);
+    }
+}
+
 int nd_cq_pack(const float* w, int rows, int d, int bits, unsigned char* codes, unsigned short* norms) {
     try {
         cq_pack(w, rows, d, bits, codes, norms);

@@ -54,6 +54,22 @@ void set_constants(float hs128) {
 
 static inline int cdiv(int a, int b) { return (a + b - 1) / b; }
 
+// SM count of the current device, looked up once per device id. Launchers
+// run on any host thread, so the cache is atomic: two threads that both
+// miss store the same value.
+static int sm_count() {
+    static std::atomic<int> sms[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    int v = sms[dev].load(std::memory_order_relaxed);
+    if (!v) {
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+        sms[dev].store(v, std::memory_order_relaxed);
+    }
+    return v;
+}
+
 // --------------------------------------------------------------- tokens
 
 __global__ void write_tokens_kernel(const int32_t* ids, int S, int T, const int32_t* p0p, int32_t* tokens, int cap) {
@@ -589,11 +605,7 @@ cudaError_t launch_cq_gemm(DevMat W, const int8_t* act, const float* sx, int M, 
         else launch_pdl(cq_gemv_kernel<8>, grid, dim3(256), 0, st, W, act, sx, M, y, ldy, col0);
         return cudaSuccess;
     }
-    static int sms[64];
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 64 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    const int per = dev < 64 && sms[dev] ? 2 * sms[dev] : 296;
+    const int per = 2 * sm_count();
     const int grid = std::min(cdiv(W.out, MMA_BN) * cdiv(M, MMA_BM), per);
     if (T == 1 && W.width == 2)
         launch_pdl(cq_mma_kernel<true, true>, dim3(grid), dim3(256), MMA_SMEM, st, W, act, sx, M, T, y, ldy, col0);

@@ -54,6 +54,7 @@ def lib():
             "nd_cqmat_new": (I, [I, P, P, I, I, I, C.POINTER(P)]),
             "nd_cqmat_free": (None, [P]),
             "nd_cqmat_apply": (I, [P, P, I, I, P, I, C.POINTER(C.c_float)]),
+            "nd_cqmat_time_rotating": (I, [P, I, I, I, I, C.POINTER(C.c_float)]),
             "nd_synth_cact": (I, [I, I, I, I, U64, U64, U64, C.c_float, P, I, C.c_uint, P, U64, C.POINTER(U64)]),
             "nd_batch_debug": (I, [P, C.c_char_p, P, C.c_longlong]),
             "nd_batch_debug_layer": (I, [P, I]),
@@ -190,6 +191,18 @@ class CQMat:
         if lib().nd_cqmat_apply(self._h, _p(x), x.shape[0], T, _p(y), reps, C.byref(ms)) != 0:
             raise _err()
         return (y, ms.value) if reps > 0 else y
+
+    @staticmethod
+    def time_rotating(mats, M, T=1, reps=10):
+        """Mean ms per matmul launch over the CQMats in turn, back to back,
+        on the activations of mats[0]'s last call (nd_cqmat_time_rotating):
+        with the matrices together larger than L2 each launch reads its
+        weights from HBM."""
+        arr = (C.c_void_p * len(mats))(*[m._h for m in mats])
+        ms = C.c_float(0.0)
+        if lib().nd_cqmat_time_rotating(arr, len(mats), M, T, reps, C.byref(ms)) != 0:
+            raise _err()
+        return ms.value
 
 
 def cq_pack(w, bits=4):

@@ -1718,6 +1718,313 @@ int candidate_order(const float* x, int n, int k, int32_t* out) {
     return live;
 }
 
+// ------------------------------------------------- synthetic archive writer
+//
+// The archive the tests and the CPU baseline load, written here from the
+// reference's exporter so that the engine's own writer is checked against it
+// byte for byte rather than shared by both sides.
+//
+// Weights: every tensor of the checkpoint is drawn ~N(0, std^2) from its own
+// stream, record i (in archive order, 0-based) seeded by
+// seed * 0x100000001B3 + 0x51ED270B2A6F1C3D * (i + 1): SplitMix64 words,
+// uniforms (w >> 11 + 0.5) / 2^53, normals by Box-Muller in double (the
+// cosine value first, then the sine one), each times std and rounded to
+// f32, in the record's row-major layout. That stream is this build's own
+// definition of "random init, seed 0"; everything after it follows the
+// reference.
+
+namespace {
+
+struct SynthRng {
+    uint64_t state;
+    double spare = 0;
+    bool have_spare = false;
+    explicit SynthRng(uint64_t s) : state(s) {}
+    uint64_t word() {
+        state += 0x9E3779B97F4A7C15ull;
+        uint64_t z = state;
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        return z ^ (z >> 31);
+    }
+    double gauss() {
+        if (have_spare) {
+            have_spare = false;
+            return spare;
+        }
+        const double u1 = ((double)(word() >> 11) + 0.5) / 9007199254740992.0;
+        const double u2 = ((double)(word() >> 11) + 0.5) / 9007199254740992.0;
+        const double r = std::sqrt(-2.0 * std::log(u1)), a = 6.283185307179586 * u2;
+        spare = r * std::sin(a);
+        have_spare = true;
+        return r * std::cos(a);
+    }
+};
+
+// cact.rs:254-266 (Out) with the generation recipe of its values.
+struct SynthTensor {
+    uint8_t dtype = 1;             // 1 f16, 2 f32, 3 CQ (cact.rs:26-31)
+    std::vector<uint32_t> shape;
+    uint32_t group = 0, bits = 0;
+    int rows = 1, cols = 1;        // CQ: [out, d]; others: numel in cols
+    std::vector<float> fixed;      // values known up front (perms, head codes)
+    bool random = true;
+    std::vector<uint8_t> blob;
+};
+
+// quant.rs:184-197 (pack_lsb): one row of codes LSB-first, 8 per `width`
+// bytes.
+void pack_lsb(const uint8_t* idx, int n, int width, uint8_t* out) {
+    for (int c = 0; c < n / 8; c++) {
+        uint64_t word = 0;
+        for (int i = 0; i < 8; i++) word |= (uint64_t)idx[8 * c + i] << (i * width);
+        for (int b = 0; b < width; b++) out[c * width + b] = (uint8_t)(word >> (8 * b));
+    }
+}
+
+// quant.rs:233-256 (cq_pack) at record bits 2, 3, 4 or 5 (ternary). The
+// reference packs 4-bit records only; the other widths store the nearest
+// centroid of their codebook in the layout its loader reads
+// (qlinear.rs:220-236, quant.rs:270-271: a ternary code c selects centroid
+// c == 3 ? 0 : c + 1, so centroid k is stored as (k + 3) % 4).
+void cq_pack_bits(const float* w, int rows, int d, int bits, uint8_t* packed, uint16_t* norms) {
+    const std::vector<float> cb = codebook(bits, GROUP);
+    const int width = code_width(bits), in_pad = (d + GROUP - 1) / GROUP * GROUP, groups = in_pad / GROUP;
+    const size_t per_row = (size_t)in_pad * width / 8;
+    std::vector<uint8_t> idx(in_pad);
+    float g[GROUP];
+    for (int r = 0; r < rows; r++) {
+        const float* src = w + (size_t)r * d;
+        for (int gi = 0; gi < groups; gi++) {
+            const int start = gi * GROUP, take = std::min(GROUP, std::max(0, d - start));
+            for (int i = 0; i < GROUP; i++) g[i] = i < take ? src[start + i] : 0.f;
+            const float norm = quantize_group(g, cb.data(), (int)cb.size(), idx.data() + start);
+            norms[(size_t)r * groups + gi] = f32_to_f16(norm);
+        }
+        if (bits == TERNARY)
+            for (auto& v : idx) v = (uint8_t)((v + 3) % 4);
+        pack_lsb(idx.data(), in_pad, width, packed + (size_t)r * per_row);
+    }
+}
+
+}  // namespace
+
+struct SynthSpec {
+    int L = 20, vocab = 16384, slots = 18432, window = 1024, max_seq = 4096;
+    uint64_t global_mask = 0, site_mask = 0, seed = 0;
+    float std = 0.02f;
+    std::vector<int> cq_bits;  // record bits of the i-th CQ record, 4 past the list
+    unsigned heads = 0;        // bit c: probe head code c (1 embedding, 2 confidence, 3 router)
+    int probes = 4, queries = 4, embedding_dim = 128;  // config.rs:27-33
+};
+
+// cact.rs:279-352 (tensors) and 362-392 (head_tensors) for the Needle 3
+// geometry of config.rs:60-103 at the spec's shape knobs, then
+// cact.rs:399-475 (pack) with kv_window = config.rs:452-482.
+std::vector<uint8_t> synth_archive(const SynthSpec& sp) {
+    const int d = 768, nh = 12, nkv = 2, qk = 48, vd = 64, lanes = 4, taps = 3, rank = 8;
+    const int hn = 1024;  // config.rs:291-293: d_model's next power of two
+    // config.rs:274-284 (engram_geometry): orders [2, 3], heads 768 / (2 * 128) = 3, sub_dim 128
+    const int sub = 128, n_orders = 2, heads = 3, ntables = n_orders * heads;
+    std::vector<int> sites;
+    for (int l = 0; l < 64; l++)
+        if ((sp.site_mask >> l) & 1) sites.push_back(l);
+    if (sp.L < 1 || sp.L > 64) throw std::runtime_error("cact global_mask holds 64 layers");
+    for (int s : sites)
+        if (s >= sp.L) throw std::runtime_error("engram site outside the stack");
+    if (sites.size() > 16) throw std::runtime_error("cact header holds 16 engram sites");
+    std::vector<SynthTensor> ts;
+    size_t n_cq = 0;
+    auto row = [&](std::vector<uint32_t> shape) {
+        SynthTensor t;
+        t.shape = shape;
+        for (auto v : shape) t.cols *= (int)v;
+        ts.push_back(t);
+    };
+    auto cq = [&](int out, int in) {
+        SynthTensor t;
+        t.dtype = 3;
+        t.shape = {(uint32_t)out, (uint32_t)in};
+        t.rows = out;
+        t.cols = in;
+        t.group = GROUP;
+        t.bits = (uint32_t)(n_cq < sp.cq_bits.size() ? sp.cq_bits[n_cq] : 4);
+        code_width((int)t.bits);
+        n_cq++;
+        ts.push_back(t);
+    };
+    auto values = [&](uint8_t dtype, std::vector<float> v) {
+        SynthTensor t;
+        t.dtype = dtype;
+        t.shape = {(uint32_t)v.size()};
+        t.fixed = v;
+        t.random = false;
+        ts.push_back(t);
+    };
+    cq(sp.vocab, d);  // embedding/embedding
+    for (int l = 0; l < sp.L; l++) {
+        row({(uint32_t)d});                              // ZCRMSNorm_0/scale
+        cq(nh * qk, d);                                  // q_proj
+        cq(nkv * qk, d);                                 // k_proj
+        cq(nkv * vd, d);                                 // v_proj
+        row({(uint32_t)taps, (uint32_t)(nh * qk)});      // q_taps
+        row({(uint32_t)taps, (uint32_t)(nkv * qk)});     // k_taps
+        row({(uint32_t)taps, (uint32_t)(nkv * vd)});     // v_taps
+        row({(uint32_t)qk});                             // q_norm
+        row({(uint32_t)qk});                             // k_norm
+        cq(nh * vd, d);                                  // gate_proj
+        cq(d, nh * vd);                                  // out_proj
+        row({(uint32_t)d});                              // post_attn_norm
+        row({1});                                        // attn_gate
+        row({(uint32_t)d});                              // pre_hada_norm
+        for (int k = 0; k < 5; k++) row({(uint32_t)hn});  // d1 d2 b2 d3 d4
+        for (int k = 0; k < 6; k++) row({32, 32});        // w1a .. w3b (config.rs hada_blocks(1024))
+        row({(uint32_t)d, (uint32_t)rank});              // cond_v
+        row({(uint32_t)rank, (uint32_t)hn});             // cond_u
+    }
+    for (int k = 0; k < 3; k++) row({(uint32_t)sp.L});                      // mhc_a_pre, _post, _res
+    for (int k = 0; k < 2; k++) row({(uint32_t)sp.L, (uint32_t)lanes});     // mhc_b_pre, _post
+    row({(uint32_t)sp.L, (uint32_t)(lanes * lanes)});                       // mhc_b_res
+    cq(sp.L * lanes, lanes * d);                                             // mhc_phi_pre
+    cq(sp.L * lanes, lanes * d);                                             // mhc_phi_post
+    cq(sp.L * lanes * lanes, lanes * d);                                     // mhc_phi_res
+    for (uint32_t seed : {11u, 13u}) {                                       // rng.rs:77-88 (unsplit)
+        auto p = Mt19937(seed).permutation(hn);
+        values(2, std::vector<float>(p.begin(), p.end()));
+    }
+    for (size_t s = 0; s < sites.size(); s++) {
+        cq(ntables * sp.slots, sub);  // engrams_s/embedding
+        cq(d, d);                     // key_proj
+        cq(d, d);                     // value_proj
+        row({4, (uint32_t)d});        // taps (ENGRAM_CONV_TAPS = 4)
+    }
+    row({(uint32_t)d});  // final_norm
+    std::vector<float> codes;
+    for (int c = 1; c <= 3; c++)
+        if ((sp.heads >> c) & 1) codes.push_back((float)c);
+    if (!codes.empty()) {
+        const int l1 = sp.L + 1, k = sp.probes, q = sp.queries;
+        values(1, codes);
+        for (float c : codes) {
+            const int out = c == 1.f ? sp.embedding_dim : c == 2.f ? 1 : 3;
+            cq(l1 * k, d);                                            // probes
+            row({(uint32_t)l1, (uint32_t)k});                         // gain
+            cq(q, d);                                                 // query
+            row({(uint32_t)q, (uint32_t)l1, (uint32_t)k});            // row_bias
+            cq(out, q * d);                                           // proj kernel, transposed
+            row({(uint32_t)out});                                     // proj bias
+            if (c == 3.f) values(1, {0.90f, 0.00f, 0.60f});           // calibration
+        }
+    }
+    // values and blobs (cact.rs:241-266: fp16 little-endian, f32, or CQ
+    // codes followed by the f16 norms)
+    std::atomic<size_t> next(0);
+    auto fill = [&]() {
+        for (size_t i; (i = next.fetch_add(1)) < ts.size();) {
+            SynthTensor& t = ts[i];
+            std::vector<float> v = t.fixed;
+            if (t.random) {
+                SynthRng rng(sp.seed * 0x100000001B3ull + 0x51ED270B2A6F1C3Dull * (i + 1));
+                v.resize((size_t)t.rows * t.cols);
+                for (auto& x : v) x = (float)(sp.std * rng.gauss());
+            }
+            if (t.dtype == 3) {
+                const int groups = (t.cols + GROUP - 1) / GROUP;
+                const size_t codes_bytes = (size_t)t.rows * groups * GROUP * code_width((int)t.bits) / 8;
+                std::vector<uint16_t> norms((size_t)t.rows * groups);
+                t.blob.assign(codes_bytes + norms.size() * 2, 0);
+                cq_pack_bits(v.data(), t.rows, t.cols, (int)t.bits, t.blob.data(), norms.data());
+                std::memcpy(t.blob.data() + codes_bytes, norms.data(), norms.size() * 2);
+            } else if (t.dtype == 2) {
+                t.blob.resize(v.size() * 4);
+                std::memcpy(t.blob.data(), v.data(), t.blob.size());
+            } else {
+                t.blob.resize(v.size() * 2);
+                for (size_t k = 0; k < v.size(); k++) {
+                    const uint16_t h = f32_to_f16(v[k]);
+                    std::memcpy(&t.blob[2 * k], &h, 2);
+                }
+            }
+        }
+    };
+    {
+        std::vector<std::thread> th;
+        const unsigned n = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+        for (unsigned k = 0; k < n; k++) th.emplace_back(fill);
+        for (auto& t : th) t.join();
+    }
+    // config.rs:448-482 (kv_budget_window; the config's kv_window is 0)
+    const int64_t per_layer = nkv * qk + nkv * vd + (nkv * qk / 32 + nkv * vd / 32) * 4;
+    const int64_t per_site = d + (d / 32) * 4, budget = 11 * 1024 * 1024 + 512 * 1024;
+    int n_global = 0;
+    for (int l = 0; l < sp.L; l++) n_global += (int)((sp.global_mask >> l) & 1);
+    auto floor_div = [](int64_t a, int64_t b) { return a / b - ((a % b != 0) && ((a < 0) != (b < 0)) ? 1 : 0); };
+    int64_t kv_window;
+    if (sp.window > 0) {
+        const int64_t local = std::min(sp.window, sp.max_seq);
+        const int64_t fixed = ((sp.L - n_global) * per_layer + (int64_t)sites.size() * per_site) * local;
+        if (n_global == 0) {
+            kv_window = fixed <= budget ? sp.max_seq : std::max<int64_t>(160, local);
+        } else {
+            const int64_t ctx = floor_div(floor_div(budget - fixed, n_global * per_layer), 32) * 32;
+            kv_window = std::max<int64_t>(160, std::min<int64_t>(ctx, sp.max_seq));
+        }
+    } else {
+        const int64_t per_pos = sp.L * per_layer + (int64_t)sites.size() * per_site;
+        kv_window = std::max<int64_t>(160, std::min<int64_t>(budget / per_pos / 32 * 32, sp.max_seq));
+    }
+    // cact.rs:82-119 (Header::to_bytes)
+    std::vector<uint32_t> h = {TAG, (uint32_t)ts.size(), 0, (uint32_t)kv_window, 8, (uint32_t)sp.vocab, 0, d, nh, nkv,
+                               (uint32_t)sp.L, qk, vd, (uint32_t)sp.max_seq, hn, lanes, (uint32_t)sp.window,
+                               (uint32_t)(sp.global_mask & 0xFFFFFFFFu), (uint32_t)(sp.global_mask >> 32), taps,
+                               (uint32_t)sp.slots, sub, ntables,
+                               4,              // engram_conv_taps (ENGRAM_CONV_TAPS)
+                               3,              // engram_conv_dilation: the largest order
+                               0,              // engram_seed_heads (config.rs:85)
+                               n_orders, 2, 3, 0, 0,  // the orders, padded to four
+                               (uint32_t)sites.size()};
+    for (int k = 0; k < 16; k++) h.push_back(k < (int)sites.size() ? (uint32_t)sites[k] : 0u);
+    h.push_back(fbits(100000.0f));  // rope_theta
+    std::vector<float> cbs;  // CB_BITS = [2, 3, 4] (quant.rs), each codebook(b, 128)
+    for (int b : {2, 3, 4}) {
+        auto c = codebook(b, GROUP);
+        cbs.insert(cbs.end(), c.begin(), c.end());
+    }
+    h[2] = (uint32_t)cbs.size();
+    if (h.size() * 4 != (size_t)HEADER_BYTES) throw std::runtime_error("header layout");
+    std::vector<uint8_t> buf(HEADER_BYTES);
+    std::memcpy(buf.data(), h.data(), HEADER_BYTES);
+    for (float c : cbs) {
+        const uint32_t u = fbits(c);
+        buf.insert(buf.end(), (const uint8_t*)&u, (const uint8_t*)&u + 4);
+    }
+    // cact.rs:441-474: records, then 64-byte aligned blobs
+    size_t pos = buf.size() + ts.size() * REC_SIZE;
+    std::vector<uint64_t> offset(ts.size());
+    for (size_t i = 0; i < ts.size(); i++) {
+        pos = (pos + 63) / 64 * 64;
+        offset[i] = pos;
+        pos += ts[i].blob.size();
+    }
+    for (size_t i = 0; i < ts.size(); i++) {
+        uint8_t r[REC_SIZE] = {};
+        r[0] = ts[i].dtype;
+        r[1] = (uint8_t)ts[i].shape.size();
+        for (size_t k = 0; k < ts[i].shape.size() && k < 4; k++) std::memcpy(r + 4 + 4 * k, &ts[i].shape[k], 4);
+        const uint64_t nbytes = ts[i].blob.size();
+        std::memcpy(r + 20, &offset[i], 8);
+        std::memcpy(r + 28, &nbytes, 8);
+        std::memcpy(r + 36, &ts[i].group, 4);
+        std::memcpy(r + 40, &ts[i].bits, 4);
+        buf.insert(buf.end(), r, r + REC_SIZE);
+    }
+    for (size_t i = 0; i < ts.size(); i++) {
+        buf.resize(offset[i], 0);
+        buf.insert(buf.end(), ts[i].blob.begin(), ts[i].blob.end());
+    }
+    return buf;
+}
+
 }  // namespace orc
 
 // ================================================================ C ABI
@@ -2154,6 +2461,36 @@ int orc_prefill_batch(void* mp, int S, const uint32_t* prompts, int n, float* ou
     for (int k = 0; k < std::max(1, threads); k++) th.emplace_back(work);
     for (auto& t : th) t.join();
     return bad.load() ? -1 : 0;
+}
+
+// The synthetic archive (synth_archive) for the shape knobs: with out ==
+// NULL only *len is set. 0 on success, -1 with orc_last_error.
+int orc_synth_cact(int L, int vocab, int slots, int window, uint64_t global_mask, uint64_t site_mask, uint64_t seed,
+                   float std_, const int* cq_bits, int n_cq_bits, unsigned heads, uint8_t* out, uint64_t cap,
+                   uint64_t* len) {
+    try {
+        SynthSpec sp;
+        sp.L = L;
+        sp.vocab = vocab;
+        sp.slots = slots;
+        sp.window = window;
+        sp.global_mask = global_mask;
+        sp.site_mask = site_mask;
+        sp.seed = seed;
+        sp.std = std_;
+        if (n_cq_bits > 0) sp.cq_bits.assign(cq_bits, cq_bits + n_cq_bits);
+        sp.heads = heads;
+        std::vector<uint8_t> b = synth_archive(sp);
+        if (len) *len = b.size();
+        if (out) {
+            if (cap < b.size()) throw std::runtime_error("buffer too small");
+            std::memcpy(out, b.data(), b.size());
+        }
+        return 0;
+    } catch (std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
 }
 
 }  // extern "C"

@@ -75,6 +75,8 @@ def lib():
             "orc_batch_free": (None, [P]),
             "orc_batch_prefill": (I, [P, P, I, I]),
             "orc_batch_step": (I, [P, P, P, I]),
+            "orc_synth_cact": (I, [I, I, I, I, C.c_uint64, C.c_uint64, C.c_uint64, F, P, I, C.c_uint, P, C.c_uint64,
+                                   C.POINTER(C.c_uint64)]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -86,6 +88,48 @@ def lib():
 
 def _p(a):
     return a.ctypes.data_as(C.c_void_p) if a is not None else None
+
+
+# Needle 3's geometry knobs (crates/needle-core/src/config.rs:60-103).
+NEEDLE3 = dict(num_layers=20, vocab=16384, engram_slots=18432, sliding_window=1024, global_layers=(4, 9, 14, 19),
+               engram_sites=(3, 7, 11, 15, 19))
+TERNARY = 5
+
+
+def cq_roles(num_layers=20, engram_sites=(3, 7, 11, 15, 19), **_):
+    """Role of each CQ record in archive order (cact.rs:279-352)."""
+    roles = ["embedding"] + ["q", "k", "v", "gate", "out"] * num_layers + ["phi_pre", "phi_post", "phi_res"]
+    return roles + ["table", "key", "value"] * len(engram_sites)
+
+
+def synth_cact(seed=0, std=0.02, bits=None, heads=(), **shape) -> bytes:
+    """The random-init archive written from the reference's exporter
+    (cact.rs:279-475) by the oracle, independently of the engine's writer:
+    the same knobs as the engine's synth_cact (bits: one width, a dict role
+    -> bits, or a list in record order; heads: probe head codes 1-3)."""
+    g = dict(NEEDLE3)
+    g.update(shape)
+    roles = cq_roles(g["num_layers"], g["engram_sites"])
+    if bits is None:
+        plan = []
+    elif isinstance(bits, int):
+        plan = [bits] * len(roles)
+    elif isinstance(bits, dict):
+        plan = [bits.get(r, 4) for r in roles]
+    else:
+        plan = list(bits)
+    plan = np.ascontiguousarray(plan, np.int32)
+    gm = sum(1 << l for l in g["global_layers"])
+    es = sum(1 << l for l in g["engram_sites"])
+    n = C.c_uint64(0)
+    args = (g["num_layers"], g["vocab"], g["engram_slots"], g["sliding_window"], gm, es, seed, std,
+            _p(plan) if len(plan) else None, len(plan), sum(1 << c for c in set(heads)))
+    if lib().orc_synth_cact(*args, None, 0, C.byref(n)) != 0:
+        raise RuntimeError(lib().orc_last_error().decode())
+    buf = np.zeros(n.value, np.uint8)
+    if lib().orc_synth_cact(*args, _p(buf), n.value, C.byref(n)) != 0:
+        raise RuntimeError(lib().orc_last_error().decode())
+    return buf.tobytes()
 
 
 def f32_to_f16_bits(x: float) -> int:

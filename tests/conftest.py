@@ -16,15 +16,16 @@ def pytest_configure(config):
 
 
 def _cached_archive(name, **shape):
-    """A synthetic archive written by the engine's own writer, cached on disk
-    per process host (the writer is deterministic)."""
-    import needle_b200 as nb
+    """A synthetic archive written by the oracle's writer (the engine's own
+    writer is checked against it byte for byte in test_archive_writer.py),
+    cached on disk per process host (the writer is deterministic)."""
+    from oracle import oracle as orc
 
     key = hashlib.sha1(repr(sorted((k, repr(v)) for k, v in shape.items())).encode()).hexdigest()[:12]
-    path = os.path.join(CACHE, f"{name}-{key}.cact")
+    path = os.path.join(CACHE, f"{name}-{key}-oracle.cact")
     if not os.path.exists(path):
         os.makedirs(CACHE, exist_ok=True)
-        data = nb.synth_cact(**shape)
+        data = orc.synth_cact(**shape)
         tmp = path + f".{os.getpid()}.tmp"
         with open(tmp, "wb") as f:
             f.write(data)

@@ -84,3 +84,44 @@ def test_cq_matmul_widths_match_oracle(width_mats, bits, n, M, T):
     got = mat(x, T=T)
     want = np.concatenate([orc.cq_matmul(codes, norms, 768, x[s:s + T], bits=bits) for s in range(0, M, T)])
     assert bits_equal(got, want), describe_diff(f"cq matmul bits={bits} M={M} T={T} n={n}", got, want)
+
+
+@pytest.fixture(scope="module")
+def model_shapes(cuda_device):
+    """The model's matrix shapes: q|k|v|gate (1568), engram key|value (1536)
+    and the tied lm_head (16384), 768 inputs each."""
+    import needle_b200 as nb
+
+    rng = np.random.default_rng(79)
+    out = {}
+    for n in (1568, 1536, 16384):
+        codes, norms = _matrix(rng, n)
+        out[n] = (codes, norms, nb.CQMat(codes, norms, cuda_device))
+    return out
+
+
+@pytest.mark.parametrize("n", [1568, 1536, 16384])
+@pytest.mark.parametrize("M,T", [(2048, 1), (2048, 32), (2046, 31), (1, 1), (16, 1), (128, 32)])
+def test_cq_matmul_model_shapes(model_shapes, n, M, T):
+    """The matmul sweep's sizes (M in 1, 16, 128, 2048)
+    at the model's real output widths, both combines: M = 2048 as 2048
+    decode rows, as 64 prefill chunks of 32, and as 66 chunks of 31 (three
+    remainder rows each). The oracle checks a sample of whole sequences
+    (rows are independent across sequences): the first, the last and three
+    between."""
+    from oracle import oracle as orc
+
+    codes, norms, mat = model_shapes[n]
+    rng = np.random.default_rng(3000 + M + T + n)
+    x = rng.standard_normal((M, 768)).astype(np.float32)
+    x[0] *= 1e-3
+    x[-1] *= 50.0
+    got = mat(x, T=T)
+    nseq = M // T
+    picks = sorted({0, nseq - 1, *rng.choice(nseq, min(3, nseq), replace=False).tolist()})
+    if T == 1:
+        picks = sorted(set(picks) | set(range(min(8, M))))
+    for s in picks:
+        rows = slice(s * T, (s + 1) * T)
+        want = orc.cq_matmul(codes.reshape(n, -1), norms, 768, x[rows])
+        assert bits_equal(got[rows], want), describe_diff(f"cq matmul n={n} M={M} T={T} seq {s}", got[rows], want)

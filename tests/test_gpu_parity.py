@@ -2,6 +2,8 @@
 the same archive and ids. Logits and hidden states must agree bit for bit,
 and greedy token streams exactly."""
 
+import os
+
 import numpy as np
 import pytest
 
@@ -221,3 +223,63 @@ def test_full_model_greedy_stream(full):
         want, logits = o.generate(prompts[s_].astype(np.uint32), steps, want_logits=True)
         assert bits_equal(first[s_], logits), describe_diff("first logits", first[s_], logits)
         assert list(got[s_]) == list(want), f"sequence {s_}: {got[s_]} vs {want}"
+
+
+def _oracle_streams(o, prompts, steps, masks=None):
+    """Greedy (optionally masked) streams and first logits of the oracle for
+    each prompt, one host thread per sequence."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    def one(s_):
+        m = masks[:, s_] if masks is not None else None
+        return o.generate(prompts[s_].astype(np.uint32), steps, masks=m, want_logits=True)
+
+    with ThreadPoolExecutor(max_workers=min(len(prompts), os.cpu_count() or 1)) as ex:
+        return list(ex.map(one, range(len(prompts))))
+
+
+def test_full_model_prefill_700(full):
+    """BASELINE configs[3]'s sequences at the Needle 3 geometry: three
+    sequences of 700 tokens fed as 22 chunks (the last 28 tokens, all block
+    rows), so the late prefill rows split their keys into three chunks
+    (key_chunks, infer.rs:2093-2101: ceil(700 / 256) = 3, 240 keys each);
+    last-position logits bit for bit, then four greedy decode steps whose
+    rows take four key chunks of up to 704 keys (every layer global or
+    windowed, the band of 1024 not cutting), tokens and logits exact."""
+    g, o = full
+    rng = np.random.default_rng(700)
+    S, n, steps = 3, 700, 4
+    prompts = rng.integers(0, g.vocab, (S, n)).astype(np.int32)
+    b = g.batch(S, n + steps + 1)
+    first = b.forward(prompts)[:, 0]
+    got = np.zeros((S, steps), np.int64)
+    for k in range(steps):
+        got[:, k] = b.step()
+    for s_, (want, logits) in enumerate(_oracle_streams(o, prompts, steps)):
+        assert bits_equal(first[s_], logits), describe_diff(f"seq {s_} logits after 700 tokens", first[s_], logits)
+        assert list(got[s_]) == list(want), f"sequence {s_}: {got[s_]} vs {want}"
+
+
+def test_headline_batch_sampled_streams(full):
+    """BASELINE configs[4] as the bench runs it: 1024 sequences in one batch
+    at the Needle 3 geometry, the bench's own 118-token prompts and seeded
+    masks (bench.make_inputs), 45 masked greedy steps (graph-replayed). A
+    sample of 24 sequences spread over the batch (both ends, every matmul
+    row tile) must give the oracle's token streams exactly."""
+    import bench
+
+    g, o = full
+    S, steps = 1024, 45
+    prompts, masks = bench.make_inputs(0, S, steps, g.out_rows)
+    b = g.batch(S, bench.PROMPT + steps + 1)
+    first = b.forward(prompts)[:, 0]
+    got = np.zeros((S, steps), np.int64)
+    for k in range(steps):
+        got[:, k] = b.step(masks[k])
+    sample = np.unique(np.concatenate([[0, 1, 63, 64, 511, 512, 1022, 1023],
+                                       np.random.default_rng(45).choice(S, 16, replace=False)]))
+    want = _oracle_streams(o, prompts[sample], steps, masks=masks[:, sample])
+    for i, s_ in enumerate(sample):
+        toks, logits = want[i]
+        assert bits_equal(first[s_], logits), describe_diff(f"seq {s_} prompt logits", first[s_], logits)
+        assert list(got[s_]) == list(toks), f"sequence {s_}: {got[s_]} vs {toks}"

@@ -1,8 +1,10 @@
-"""The multi-GPU path's host logic on CPU ranks (gloo, world size 2): each
-rank builds its own shard of sequences the way bench.py does, runs it with
-no collective on the data path, and the max-over-ranks timing and a gather
-of token streams are the only collectives. The gathered streams must equal
-single-process runs of the same sequences."""
+"""The multi-GPU path's host logic on CPU ranks (gloo, world size 2): the
+workload's sequences are partitioned across the ranks the way bench.py does
+it (contiguous shares, the first ranks taking one more when the count does
+not divide), each rank runs its share with no collective on the data path,
+and the max-over-ranks timing and a gather of token streams are the only
+collectives. The gathered streams, in sequence order, must equal a
+single-process run of the whole workload."""
 
 import os
 import socket
@@ -17,6 +19,9 @@ def _free_port():
     port = s.getsockname()[1]
     s.close()
     return port
+
+
+TOTAL = 5  # sequences in the workload: 3 on rank 0, 2 on rank 1
 
 
 def _worker(rank, world, port, archive, steps, results):
@@ -35,8 +40,8 @@ def _worker(rank, world, port, archive, steps, results):
     from oracle import oracle as orc
 
     m = orc.Model(archive)
-    S = 2
-    prompts, masks = bench.make_inputs(rank, S, steps, m.out_rows)
+    first, S = bench.shard(TOTAL, world, rank)
+    prompts, masks = bench.make_inputs(first, S, steps, m.out_rows)
     b = orc.Batch(m, S, threads=1)
     b.prefill(prompts)
     import time
@@ -46,7 +51,7 @@ def _worker(rank, world, port, archive, steps, results):
     t = torch.tensor([time.perf_counter() - t0], dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     gathered = [None] * world
-    dist.all_gather_object(gathered, (rank, toks.tolist(), float(t.item())))
+    dist.all_gather_object(gathered, (first, toks.tolist(), float(t.item())))
     if rank == 0:
         results.put(gathered)
     dist.barrier()
@@ -73,11 +78,14 @@ def test_two_ranks_shard_sequences(small_archive):
     m = orc.Model(small_archive)
     times = {g[2] for g in gathered}
     assert len(times) == 1, "every rank sees the same max-over-ranks time"
-    seen = set()
-    for rank, toks, _ in gathered:
-        prompts, masks = bench.make_inputs(rank, 2, steps, m.out_rows)
-        for s in range(2):
-            want = m.generate(prompts[s].astype(np.uint32), steps, masks=masks[:, s])
-            assert toks[s] == [int(v) for v in want]
-            seen.add(tuple(prompts[s][:8]))
-    assert len(seen) == 4, "ranks hold distinct sequences"
+    assert [bench.shard(TOTAL, world, r) for r in range(world)] == [(0, 3), (3, 2)]
+    streams = [row for _, toks, _ in sorted(gathered) for row in toks]
+    assert len(streams) == TOTAL, "the shares cover every sequence once"
+    prompts, masks = bench.make_inputs(0, TOTAL, steps, m.out_rows)
+    one = orc.Batch(m, TOTAL, threads=1)
+    one.prefill(prompts)
+    want = np.stack([one.step(masks[k]) for k in range(steps)], 1)
+    assert streams == want.tolist(), "a partitioned run equals the single-process run"
+    # a share's inputs are the same rows of the whole workload's
+    p1, m1 = bench.make_inputs(3, 2, steps, m.out_rows)
+    assert np.array_equal(p1, prompts[3:]) and np.array_equal(m1, masks[:, 3:])
