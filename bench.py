@@ -53,11 +53,14 @@ def parse():
     ap.add_argument("--sweep", action="store_true",
                     help="instead of the decode bench: the CQ-W4/A8 matmul sweep (M in 1, 16, 128, 2048 over the "
                          "model's four matrix shapes), one JSON line")
+    ap.add_argument("--ops", action="store_true",
+                    help="instead of the decode bench: the fused-ops sweep (RMSNorm, RoPE, SiLU, embedding gather at "
+                         "T in 1, 64, 1024, 8192), L2 flushed before every timed launch, one JSON line")
     ap.add_argument("--profile", action="store_true",
                     help="untimed case for ncu: one batch of --seqs sequences, the 118-token prefill, then --warmup "
                          "decode steps (--profile-case decode); or three call-sampler launches over 1024 rows of "
                          "logits (candidates); or one 256 x 64 embedding (embed)")
-    ap.add_argument("--profile-case", default="decode", choices=["decode", "candidates", "embed"],
+    ap.add_argument("--profile-case", default="decode", choices=["decode", "candidates", "embed", "ops"],
                     help="decode uses --seqs sequences (1 for the batch-1 step)")
     return ap.parse_args()
 
@@ -319,6 +322,88 @@ def matmul_sweep(local):
                          "GB_s": round(byt / (ms * 1e-3) / 1e9, 1), "int8_TOPS": round(2 * M * n * 768 / (ms * 1e-3) / 1e12, 2)})
         del mat
     return rows
+
+
+OPS_T = (1, 64, 1024, 8192)
+
+
+def ops_inputs(T, rng):
+    """BASELINE configs[2]'s inputs at T tokens: rows N(0, 1) of the model
+    width (RMSNorm), of the q|k heads (RoPE) and of the MLP's 1024 (SiLU);
+    RMSNorm weights N(1, 0.1) rounded to f16; uniform-random token ids."""
+    return {"zcn": rng.standard_normal((T, 768)).astype(np.float32),
+            "s": (1.0 + 0.1 * rng.standard_normal(768)).astype(np.float16).astype(np.float32),
+            "rope": rng.standard_normal((T, 672)).astype(np.float32),
+            "silu": rng.standard_normal((T, 1024)).astype(np.float32),
+            "ids": rng.integers(0, 16384, T).astype(np.int32)}
+
+
+def ops_bytes(op, T):
+    """Algorithmic bytes of one launch: every input and output once."""
+    return {"zcn": 2 * T * 768 * 4 + 768 * 4, "rope": 2 * T * 672 * 4, "silu": 2 * T * 1024 * 4,
+            "gather": T * (6 * 66 + 768 * 4 + 4)}[op]
+
+
+def ops_sweep(local, model, reps=20, profile=False):
+    """Each fused row op alone through its C entry (device buffers): `reps`
+    launches, each after a 256 MB write that evicts L2 (126 MB), timed by
+    CUDA events around the launch alone; GB/s of the algorithmic bytes
+    against the measured HBM copy bandwidth. The oracle's single-thread time
+    for the same op and T is the CPU baseline."""
+    import torch
+
+    import needle_b200 as nb
+    from oracle import oracle as orc
+
+    dev = f"cuda:{local}"
+    hbm, _, kind = peaks()
+    rng = np.random.default_rng(2)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    rows = []
+    orc_model = None
+    for T in OPS_T:
+        inp = ops_inputs(T, rng)
+        d = {k: torch.from_numpy(v).to(dev) for k, v in inp.items()}
+        outs = {"zcn": torch.empty_like(d["zcn"]), "rope": torch.empty_like(d["rope"]),
+                "silu": torch.empty_like(d["silu"]), "gather": torch.empty((T, 768), dtype=torch.float32, device=dev)}
+        calls = {"zcn": lambda: nb.op_zcn(d["zcn"], d["s"], outs["zcn"]),
+                 "rope": lambda: nb.op_rope(d["rope"], 100000.0, outs["rope"]),
+                 "silu": lambda: nb.op_silu(d["silu"], outs["silu"]),
+                 "gather": lambda: nb.op_gather(model, d["ids"], outs["gather"])}
+        for op, call in calls.items():
+            call()
+            if profile:
+                continue
+            times = []
+            for _ in range(reps):
+                flush.fill_(float(len(times)))
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                call()
+                e1.record()
+                torch.cuda.synchronize()
+                times.append(e0.elapsed_time(e1))
+            us = float(np.median(times)) * 1e3
+            byt = ops_bytes(op, T)
+            t0 = time.perf_counter()
+            if op == "zcn":
+                orc.op_zcn(inp["zcn"], inp["s"])
+            elif op == "rope":
+                orc.op_rope(inp["rope"])
+            elif op == "silu":
+                orc.op_silu(inp["silu"])
+            else:
+                if orc_model is None:
+                    orc_model = orc.Model(archive_bytes("oracle"))
+                orc_model.gather(inp["ids"].astype(np.uint32))
+            cpu_s = time.perf_counter() - t0
+            rows.append({"op": op, "T": T, "us": round(us, 2), "bytes": byt, "gb_s": round(byt / (us * 1e-6) / 1e9, 1),
+                         "frac": round(byt / (us * 1e-6) / 1e9 / hbm, 4),
+                         "cpu_gb_s": round(byt / cpu_s / 1e9, 2), "cpu_us": round(cpu_s * 1e6, 1)})
+    torch.cuda.synchronize()
+    return {"peak": hbm, "peak_kind": kind, "l2": "flushed before every timed launch (256 MB write)",
+            "cpu_baseline": {"kind": "port", "cores": 1, "sample": "the same op and T, once, one host thread"},
+            "rows": rows}
 
 
 def decode_b1(model, rng, dev):
@@ -588,6 +673,14 @@ def main():
     data = archive_bytes()
     model = nb.Model(data, device=local)
     V = model.out_rows
+    if args.ops or (args.profile and args.profile_case == "ops"):
+        res = ops_sweep(local, model, profile=args.profile)
+        if rank == 0 and not args.profile:
+            print(json.dumps({"sweep": "fused_row_ops", **res}), flush=True)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.profile and args.profile_case == "candidates":
         call_candidates(model, f"cuda:{local}", reps=0)
         torch.cuda.synchronize()

@@ -234,6 +234,34 @@ int nd_batch_site_time(nd_batch* b, double* total_ms, int* launches);
  * contents, none of which the next call reads before writing. */
 int nd_head_logits_noalloc(const nd_model* m, const float* h, int rows, float* out, void* stream);
 
+/* The fused row ops of a layer as standalone kernels (BASELINE's fused-ops
+ * sweep; in the forward pass they are fused into larger kernels). Device
+ * pointers, queued on `stream` (a cudaStream_t; NULL = the legacy default
+ * stream) and not waited for; 0 on success, -1 with nd_last_error().
+ * Float pointers must be 16-byte aligned. */
+
+/* infer.rs:426-443 (zcn, the zero-centred RMSNorm) with infer.rs:372-417
+ * (dot16): out[t] = fma(x[t] r, s, x[t] r), r = 1 / sqrt(dot16(x[t],
+ * x[t]) / 768 + 1e-6), for rows x[T][768] and weights s[768]. */
+int nd_op_zcn(const float* x, const float* s, int T, float* out, void* stream);
+
+/* The rotary embedding of a chunk's rows (infer.rs:1474-1483 with the
+ * tables of infer.rs:938-946 and 1716-1744) at positions 0 .. T-1: x[T][672]
+ * holds 12 query heads then 2 key heads of 48; in each, x[f] and x[f + 24]
+ * (f < 24) rotate by the angle freq[f] * t, freq[f] = powf(theta,
+ * f * (-2 / 48)). out may equal x. */
+int nd_op_rope(const float* x, int T, float theta, float* out, void* stream);
+
+/* infer.rs:2463-2496 (silu_native): out[i] = x[i] / (nexp(-x[i]) + 1) for
+ * n elements (the Hadamard MLP's activation). */
+int nd_op_silu(const float* x, long long n, float* out, void* stream);
+
+/* qlinear.rs:309-323 (QMat::row) of the model's token embedding for each of
+ * ids[T] (device int32): out[T][d_model], the codes dequantized by their
+ * f16 group norms and rotated back (without the forward's sqrt(d_model)
+ * scale). An id outside [0, vocab) gives a row of zeros. */
+int nd_op_gather(const nd_model* m, const int* ids, int T, float* out, void* stream);
+
 /* The last failure on this thread (empty if none). */
 const char* nd_last_error(void);
 

@@ -784,6 +784,7 @@ struct nd_model;
 
 namespace nd {
 bool model_head(const nd_model* m, DevMat* emb, int* device, int* out_rows);
+bool model_embedding(const nd_model* m, DevMat* emb, int* device);
 }  // namespace nd
 
 using namespace nd;
@@ -798,6 +799,14 @@ bool nd::model_head(const nd_model* mh, DevMat* emb, int* device, int* out_rows)
     *emb = mh->m->head;
     *device = mh->m->device;
     *out_rows = mh->m->c.out_rows();
+    return true;
+}
+
+// The whole token embedding of a loaded model, vocab rows (for ops.cu).
+bool nd::model_embedding(const nd_model* mh, DevMat* emb, int* device) {
+    if (!mh || !mh->m) return false;
+    *emb = mh->m->embedding;
+    *device = mh->m->device;
     return true;
 }
 struct nd_batch {

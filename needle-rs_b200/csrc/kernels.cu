@@ -11,6 +11,7 @@
 
 #include "kernels.h"
 #include "numerics.cuh"
+#include "cqrow.cuh"
 
 namespace nd {
 
@@ -88,25 +89,6 @@ void launch_write_tokens(const int32_t* ids, int S, int T, int p0, Caches c, cud
 }
 
 // ------------------------------------------------------- CQ row dequant
-
-// QMat::row (qlinear.rs:309-323) of one 128-wide group, by a warp: each
-// lane's four weights p = 4 lane .. 4 lane + 3, `fvals[code] * norm`, then
-// the rotation. The four codes are 4 * width consecutive bits of the group.
-__device__ __forceinline__ void cq_group_row(const DevMat& W, size_t row, int g, int lane, float v[4]) {
-    const int width = W.width, bpg = 16 * width;
-    const uint8_t* c = W.codes + (row * W.groups + g) * bpg;
-    const int bit = 4 * width * lane;
-    uint32_t w = (uint32_t)c[bit >> 3];
-    if (width > 2) w |= (uint32_t)c[(bit >> 3) + 1] << 8;
-    w >>= bit & 7;
-    const uint32_t mask = (1u << width) - 1;
-    float norm = h2f(W.norms[row * W.groups + g]);
-#pragma unroll
-    for (int k = 0; k < 4; k++) v[k] = __fmul_rn(W.fvals[(w >> (width * k)) & mask], norm);
-    fwht128_warp(v, lane);
-#pragma unroll
-    for (int k = 0; k < 4; k++) v[k] = __fmul_rn(v[k], c_hs128);
-}
 
 // infer.rs:1185-1194: the embedding row times sqrt(d), in every lane.
 __global__ void embed_kernel(DevMat emb, const int32_t* ids, float* xs, float scale) {

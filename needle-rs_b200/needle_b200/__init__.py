@@ -55,6 +55,10 @@ def lib():
             "nd_cqmat_free": (None, [P]),
             "nd_cqmat_apply": (I, [P, P, I, I, P, I, C.POINTER(C.c_float)]),
             "nd_cqmat_time_rotating": (I, [P, I, I, I, I, C.POINTER(C.c_float)]),
+            "nd_op_zcn": (I, [P, P, I, P, P]),
+            "nd_op_rope": (I, [P, I, C.c_float, P, P]),
+            "nd_op_silu": (I, [P, C.c_longlong, P, P]),
+            "nd_op_gather": (I, [P, P, I, P, P]),
             "nd_synth_cact": (I, [I, I, I, I, U64, U64, U64, C.c_float, P, I, C.c_uint, P, U64, C.POINTER(U64)]),
             "nd_batch_debug": (I, [P, C.c_char_p, P, C.c_longlong]),
             "nd_batch_debug_layer": (I, [P, I]),
@@ -412,3 +416,54 @@ class Batch:
 
     def debug_layer(self, layer):
         lib().nd_batch_debug_layer(self._h, layer)
+
+
+# ------------------------------------------------------- standalone row ops
+
+
+def _stream_of(t):
+    import torch
+
+    return C.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def op_zcn(x, s, out=None):
+    """infer.rs:426-443 on the GPU: rows x [T, 768] (a float32 CUDA tensor),
+    weights s [768]; returns out [T, 768] (nd_op_zcn)."""
+    import torch
+
+    out = torch.empty_like(x) if out is None else out
+    if lib().nd_op_zcn(_p(x), _p(s), x.shape[0], _p(out), _stream_of(x)) != 0:
+        raise _err()
+    return out
+
+
+def op_rope(x, theta=100000.0, out=None):
+    """RoPE at positions 0..T-1 of x [T, 672] (12 q heads, 2 k heads of 48)."""
+    import torch
+
+    out = torch.empty_like(x) if out is None else out
+    if lib().nd_op_rope(_p(x), x.shape[0], theta, _p(out), _stream_of(x)) != 0:
+        raise _err()
+    return out
+
+
+def op_silu(x, out=None):
+    """silu_native elementwise over a float32 CUDA tensor."""
+    import torch
+
+    out = torch.empty_like(x) if out is None else out
+    if lib().nd_op_silu(_p(x), x.numel(), _p(out), _stream_of(x)) != 0:
+        raise _err()
+    return out
+
+
+def op_gather(model, ids, out=None):
+    """QMat::row of the model's embedding for int32 CUDA ids [T]."""
+    import torch
+
+    T = ids.shape[0]
+    out = torch.empty((T, model.d_model), dtype=torch.float32, device=ids.device) if out is None else out
+    if lib().nd_op_gather(model._h, _p(ids), T, _p(out), _stream_of(ids)) != 0:
+        raise _err()
+    return out

@@ -2493,4 +2493,50 @@ int orc_synth_cact(int L, int vocab, int slots, int window, uint64_t global_mask
     }
 }
 
+// ---- the fused row ops alone (the fused-ops sweep's checker)
+
+// infer.rs:426-443 (zcn) over rows x [T][n].
+void orc_op_zcn(const float* x, const float* s, int T, int n, float* out) {
+    for (int t = 0; t < T; t++) zcn(x + (size_t)t * n, s, out + (size_t)t * n, n);
+}
+
+// infer.rs:1716-1744 (chunk rows: sincosf of freq * pos) and the rotation of
+// infer.rs:1474-1483 over 12 query heads then 2 key heads of 48, at
+// positions 0 .. T-1; freq per infer.rs:938-946.
+void orc_op_rope(const float* x, int T, float theta, float* out) {
+    const int qk = 48, half = 24, heads = 14;
+    const float coef = -2.0f / (float)qk;
+    float freq[24];
+    for (int i = 0; i < half; i++) freq[i] = lpowf(theta, (float)i * coef);
+    for (int t = 0; t < T; t++) {
+        float cs[24], sn[24];
+        for (int f = 0; f < half; f++) lsincosf(freq[f] * (float)t, &sn[f], &cs[f]);
+        for (int h = 0; h < heads; h++) {
+            const float* xi = x + (size_t)t * heads * qk + h * qk;
+            float* o = out + (size_t)t * heads * qk + h * qk;
+            for (int f = 0; f < half; f++) {
+                const float a = xi[f], b = xi[f + half];
+                o[f] = std::fmaf(-sn[f], b, cs[f] * a);
+                o[f + half] = std::fmaf(sn[f], a, cs[f] * b);
+            }
+        }
+    }
+}
+
+// infer.rs:2463-2496 (silu_native, scalar arm).
+void orc_op_silu(const float* x, int64_t n, float* out) {
+    for (int64_t i = 0; i < n; i++) out[i] = x[i] / (nexp(-x[i]) + 1.0f);
+}
+
+// qlinear.rs:309-323 (QMat::row) of the model's embedding for each id.
+int orc_op_gather(void* mp, const uint32_t* ids, int T, float* out) {
+    const Model& m = *(const Model*)mp;
+    const int d = m.c.d;
+    for (int t = 0; t < T; t++) {
+        if ((int)ids[t] >= m.embedding.out) return -1;
+        qmat_row(m.embedding, (int)ids[t], out + (size_t)t * d);
+    }
+    return 0;
+}
+
 }  // extern "C"

@@ -75,6 +75,10 @@ def lib():
             "orc_batch_free": (None, [P]),
             "orc_batch_prefill": (I, [P, P, I, I]),
             "orc_batch_step": (I, [P, P, P, I]),
+            "orc_op_zcn": (None, [P, P, I, I, P]),
+            "orc_op_rope": (None, [P, I, F, P]),
+            "orc_op_silu": (None, [P, C.c_int64, P]),
+            "orc_op_gather": (I, [P, P, I, P]),
             "orc_synth_cact": (I, [I, I, I, I, C.c_uint64, C.c_uint64, C.c_uint64, F, P, I, C.c_uint, P, C.c_uint64,
                                    C.POINTER(C.c_uint64)]),
         }
@@ -299,6 +303,32 @@ def candidate_order(x, k=128):
     return out[:min(k, live)], live
 
 
+def op_zcn(x, s):
+    """infer.rs:426-443 over rows x [T, n] with weights s [n]."""
+    x = np.ascontiguousarray(x, np.float32)
+    s = np.ascontiguousarray(s, np.float32)
+    out = np.zeros_like(x)
+    lib().orc_op_zcn(_p(x), _p(s), x.shape[0], x.shape[1], _p(out))
+    return out
+
+
+def op_rope(x, theta=100000.0):
+    """RoPE of rows x [T, 672] (12 q heads, 2 k heads of 48) at positions
+    0..T-1 (infer.rs:1474-1483, 1716-1744)."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.zeros_like(x)
+    lib().orc_op_rope(_p(x), x.shape[0], float(theta), _p(out))
+    return out
+
+
+def op_silu(x):
+    """infer.rs:2463-2496."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.zeros_like(x)
+    lib().orc_op_silu(_p(x), x.size, _p(out))
+    return out
+
+
 def masked_argmax(x, allow_bits=None):
     x = np.ascontiguousarray(x, np.float32)
     return lib().orc_masked_argmax(_p(x), len(x), _p(allow_bits) if allow_bits is not None else None)
@@ -356,6 +386,14 @@ class Model:
         out = np.zeros((len(ids), self.num_layers + 1, self.d_model), np.float32)
         if lib().orc_cells(self._h, _p(ids), len(ids), _p(out)) != 0:
             raise RuntimeError(lib().orc_last_error().decode())
+        return out
+
+    def gather(self, ids):
+        """qlinear.rs:309-323 (QMat::row) of the embedding for each id."""
+        ids = np.ascontiguousarray(ids, np.uint32)
+        out = np.zeros((len(ids), self.d_model), np.float32)
+        if lib().orc_op_gather(self._h, _p(ids), len(ids), _p(out)) != 0:
+            raise RuntimeError("id outside the vocabulary")
         return out
 
     def head_logits(self, h):
