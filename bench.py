@@ -346,8 +346,9 @@ def ops_bytes(op, T):
 
 def ops_sweep(local, model, reps=20, profile=False):
     """Each fused row op alone through its C entry (device buffers): `reps`
-    launches, each after a 256 MB write that evicts L2 (126 MB), timed by
-    CUDA events around the launch alone; GB/s of the algorithmic bytes
+    launches, each after a 256 MB write that evicts L2 (126 MB) and a short
+    device spin (so the launch is queued before its start event), timed by
+    CUDA events around the launch alone (median); GB/s of the algorithmic bytes
     against the measured HBM copy bandwidth. The oracle's single-thread time
     for the same op and T is the CPU baseline."""
     import torch
@@ -377,6 +378,9 @@ def ops_sweep(local, model, reps=20, profile=False):
             times = []
             for _ in range(reps):
                 flush.fill_(float(len(times)))
+                # a 100 us device spin first, so the launch is queued before
+                # the start event fires and the events see the kernel alone
+                torch.cuda._sleep(200000)
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record()
                 call()

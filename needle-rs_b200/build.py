@@ -18,7 +18,7 @@ OUT_DIR = os.path.join(HERE, "needle_b200")
 LIB = os.path.join(OUT_DIR, "libneedle3.so")
 BUILD = os.path.join(HERE, "_build")
 
-CU = ["kernels.cu", "engine.cu", "ops.cu", "noalloc.cu"]
+CU = ["kernels.cu", "tc_prefill.cu", "engine.cu", "ops.cu", "noalloc.cu"]
 CPP = ["cact.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -771,6 +771,16 @@ static int forward(Batch& b, const int32_t* dev_ids, int t, int outputs) {
 
 // ----------------------------------------------------------- the C ABI
 
+// After a synchronisation: the tensor-core prefill matmul records in a
+// device word when one of its bounded waits expired (its results are then
+// incomplete); report that as an error.
+static void check_tc_waits() {
+    const int e = tc_prefill_error();
+    if (e > 0)
+        throw std::runtime_error("tensor-core prefill matmul: a pipeline wait expired (stage " + std::to_string(e) +
+                                 "); results of this call are incomplete");
+}
+
 static int fail(const std::exception& e) {
     g_err = e.what();
     return -1;
@@ -988,7 +998,11 @@ int nd_batch_forward(nd_batch* bh, const int* ids, int t, int outputs, float* ou
             size_t n = (size_t)b.last_rows * width;
             CK(cudaMemcpyAsync(out, src, n * sizeof(float), dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, b.st));
         }
-        if (!dev) CK(cudaStreamSynchronize(b.st));
+        if (!dev) {
+            CK(cudaStreamSynchronize(b.st));
+            CK(cudaStreamSynchronize(b.st2));
+            check_tc_waits();
+        }
         return rows;
     } catch (std::exception& e) {
         return fail(e);
@@ -1378,6 +1392,7 @@ int nd_cqmat_apply(nd_cqmat* h, const float* x, int M, int T, float* y, int reps
         CK(cudaGetLastError());
         CK(cudaMemcpyAsync(y, h->y, (size_t)M * out * 4, cudaMemcpyDeviceToHost, h->st));
         CK(cudaStreamSynchronize(h->st));
+        check_tc_waits();
         return 0;
     } catch (std::exception& e) {
         return fail(e);

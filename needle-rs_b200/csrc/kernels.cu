@@ -587,14 +587,13 @@ cudaError_t launch_cq_gemm(DevMat W, const int8_t* act, const float* sx, int M, 
         else launch_pdl(cq_gemv_kernel<8>, grid, dim3(256), 0, st, W, act, sx, M, y, ldy, col0);
         return cudaSuccess;
     }
+    if (T > 1) return launch_cq_prefill_tc(W, act, sx, M, T, y, ldy, col0, st);
     const int per = 2 * sm_count();
     const int grid = std::min(cdiv(W.out, MMA_BN) * cdiv(M, MMA_BM), per);
-    if (T == 1 && W.width == 2)
+    if (W.width == 2)
         launch_pdl(cq_mma_kernel<true, true>, dim3(grid), dim3(256), MMA_SMEM, st, W, act, sx, M, T, y, ldy, col0);
-    else if (T == 1)
-        launch_pdl(cq_mma_kernel<true, false>, dim3(grid), dim3(256), MMA_SMEM, st, W, act, sx, M, T, y, ldy, col0);
     else
-        launch_pdl(cq_mma_kernel<false, false>, dim3(grid), dim3(256), MMA_SMEM, st, W, act, sx, M, T, y, ldy, col0);
+        launch_pdl(cq_mma_kernel<true, false>, dim3(grid), dim3(256), MMA_SMEM, st, W, act, sx, M, T, y, ldy, col0);
     return cudaSuccess;
 }
 
@@ -2675,7 +2674,7 @@ static cudaError_t init_attrs() {
     cudaFuncSetAttribute(post_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)POST_ROW_SMEM);
     cudaFuncSetAttribute(cq_mma_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
     cudaFuncSetAttribute(cq_mma_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
-    return cudaFuncSetAttribute(cq_mma_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
+    return tc_prefill_init();
 }
 
 }  // namespace nd

@@ -101,11 +101,21 @@ void launch_write_tokens(const int32_t* ids, int S, int T, int p0, Caches c, cud
 void launch_embed(DevMat emb, const int32_t* ids, int M, float* xs, cudaStream_t st);
 void launch_prep_act(const float* x, int ldx, int K, int M, int8_t* act, float* sx, cudaStream_t st);
 // y[m][col0 + n] for n < W.out. T sets the combine per row: T == 1 the
-// decode kernel, else the prefill kernel with the block/remainder rule over
-// each sequence's T rows. cudaErrorInvalidValue (nothing launched) unless W
-// reads 768 inputs and carries its w8 copy.
+// decode combine (the code-reading GEMV for up to 4 rows, int8 mma.sync tiles
+// beyond), else the prefill combine with the block/remainder rule over each
+// sequence's T rows on tcgen05 (launch_cq_prefill_tc). cudaErrorInvalidValue
+// (nothing launched) unless W reads 768 inputs and carries its w8 copy.
 cudaError_t launch_cq_gemm(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y, int ldy, int col0,
                            cudaStream_t st);
+// The prefill combine (T > 1) on tcgen05 tensor cores fed by TMA (tc_prefill.cu);
+// launch_cq_gemm routes T > 1 here. tc_prefill_init sets its kernel
+// attributes on the current device; tc_prefill_error returns (and clears)
+// the current device's error word: nonzero when a bounded wait of the
+// kernel expired (read it after synchronising the stream).
+cudaError_t launch_cq_prefill_tc(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y, int ldy, int col0,
+                                 cudaStream_t st);
+cudaError_t tc_prefill_init();
+int tc_prefill_error();
 void launch_engram_gather(DevMat tables, Caches c, int S, int T, int p0, int slots, float* e, cudaStream_t st);
 void launch_engram_vhist(const float* kv, Caches c, int site, int nsites, int S, int T, int p0, cudaStream_t st);
 void launch_engram_conv(const float* taps, Caches c, int site, int nsites, int S, int T, int p0, float* v, cudaStream_t st);

@@ -99,6 +99,17 @@ __global__ void __launch_bounds__(256) op_rope_kernel(const float* __restrict__ 
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (row >= T) return;
+    constexpr int K = (ROPE_PAIRS + 31) / 32;
+    const float* xr = x + (size_t)row * ROPE_W;
+    float* orow = out + (size_t)row * ROPE_W;
+    // the row's values first (independent of the angles), then the sincos
+    float a[K], b[K];
+#pragma unroll
+    for (int k = 0; k < K; k++) {
+        const int p = lane + 32 * k, h = p / 24, f = p % 24;
+        a[k] = p < ROPE_PAIRS ? __ldg(xr + h * 48 + f) : 0.f;
+        b[k] = p < ROPE_PAIRS ? __ldg(xr + h * 48 + f + 24) : 0.f;
+    }
     float cs = 0.f, sn = 0.f;
     if (lane < 24) {
         double sd, cd;
@@ -106,16 +117,13 @@ __global__ void __launch_bounds__(256) op_rope_kernel(const float* __restrict__ 
         cs = (float)cd;
         sn = (float)sd;
     }
-    const float* xr = x + (size_t)row * ROPE_W;
-    float* orow = out + (size_t)row * ROPE_W;
 #pragma unroll
-    for (int k = 0; k < (ROPE_PAIRS + 31) / 32; k++) {
+    for (int k = 0; k < K; k++) {
         const int p = lane + 32 * k, h = p / 24, f = p % 24;
         const float c = __shfl_sync(0xffffffffu, cs, f), sv = __shfl_sync(0xffffffffu, sn, f);
         if (p < ROPE_PAIRS) {
-            const float a = __ldg(xr + h * 48 + f), b = __ldg(xr + h * 48 + f + 24);
-            orow[h * 48 + f] = __fmaf_rn(-sv, b, __fmul_rn(c, a));
-            orow[h * 48 + f + 24] = __fmaf_rn(sv, a, __fmul_rn(c, b));
+            orow[h * 48 + f] = __fmaf_rn(-sv, b[k], __fmul_rn(c, a[k]));
+            orow[h * 48 + f + 24] = __fmaf_rn(sv, a[k], __fmul_rn(c, b[k]));
         }
     }
 }
@@ -144,18 +152,43 @@ __global__ void __launch_bounds__(256) op_silu_kernel(const float* __restrict__ 
 // --------------------------------------------------------------- gather
 
 // qlinear.rs:309-323 (QMat::row) of the embedding for each id: a warp per
-// row, group g's 128 values dequantized and rotated by the warp
-// (cq_group_row), written as one 512-byte run.
+// row. The row's codes and norms for all groups are loaded first (each
+// lane's 4 codes of every group), then each group's 128 values are
+// dequantized and rotated by the warp and written as one 512-byte run.
+constexpr int GATHER_MAXG = 8;
+
 __global__ void __launch_bounds__(256) op_gather_kernel(DevMat emb, const int32_t* __restrict__ ids, int T, float* __restrict__ out) {
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (t >= T) return;
-    const int id = ids[t];
+    const int id = __ldg(ids + t);
     const bool ok = id >= 0 && id < emb.out;  // an id past the vocabulary gives a row of zeros
-    const int d = emb.in_dim;
-    for (int g = 0; g < emb.groups; g++) {
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
-        if (ok) cq_group_row(emb, (size_t)id, g, lane, v);
+    const int d = emb.in_dim, G = emb.groups, width = emb.width, bpg = 16 * width;
+    const size_t row = ok ? (size_t)id : 0;
+    const uint8_t* codes = emb.codes + row * G * bpg;
+    const int bit = 4 * width * lane;
+    uint32_t w[GATHER_MAXG];
+    float norm[GATHER_MAXG];
+#pragma unroll
+    for (int g = 0; g < GATHER_MAXG; g++) {
+        if (g < G) {
+            const uint8_t* c = codes + g * bpg;
+            uint32_t v = __ldg(c + (bit >> 3));
+            if (width > 2) v |= (uint32_t)__ldg(c + (bit >> 3) + 1) << 8;
+            w[g] = v >> (bit & 7);
+            norm[g] = h2f(__ldg(emb.norms + row * G + g));
+        }
+    }
+    const uint32_t mask = (1u << width) - 1;
+#pragma unroll
+    for (int g = 0; g < GATHER_MAXG; g++) {
+        if (g >= G) break;
+        float v[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) v[k] = __fmul_rn(emb.fvals[(w[g] >> (width * k)) & mask], norm[g]);
+        fwht128_warp(v, lane);
+#pragma unroll
+        for (int k = 0; k < 4; k++) v[k] = ok ? __fmul_rn(v[k], ND_HS128) : 0.f;
         const int col = g * 128 + 4 * lane;
         if (col + 3 < d) *(float4*)(out + (size_t)t * d + col) = make_float4(v[0], v[1], v[2], v[3]);
     }
@@ -244,7 +277,8 @@ int nd_op_gather(const nd_model* m, const int* ids, int T, float* out, void* str
         if (!m || !ids) throw std::runtime_error("nd_op_gather: null argument");
         check_aligned(out, "nd_op_gather");
         if (!model_embedding(m, &emb, &device)) throw std::runtime_error("nd_op_gather: no model");
-        if (emb.in_dim % 128) throw std::runtime_error("nd_op_gather: d_model must be a multiple of 128");
+        if (emb.in_dim % 128 || emb.groups > GATHER_MAXG)
+            throw std::runtime_error("nd_op_gather: d_model must be a multiple of 128, at most 1024");
         if (T < 1) throw std::runtime_error("nd_op_gather: T must be positive");
         int prev = 0;
         cudaGetDevice(&prev);
