@@ -60,7 +60,7 @@ def parse():
                     help="untimed case for ncu: one batch of --seqs sequences, the 118-token prefill, then --warmup "
                          "decode steps (--profile-case decode); or three call-sampler launches over 1024 rows of "
                          "logits (candidates); or one 256 x 64 embedding (embed)")
-    ap.add_argument("--profile-case", default="decode", choices=["decode", "candidates", "embed", "ops"],
+    ap.add_argument("--profile-case", default="decode", choices=["decode", "candidates", "embed", "ops", "prefill_matmul"],
                     help="decode uses --seqs sequences (1 for the batch-1 step)")
     return ap.parse_args()
 
@@ -300,11 +300,14 @@ def cpu_baseline_sample(data):
 def matmul_sweep(local):
     """The CQ-W4/A8 matmul alone (A8 of the rows + the matmul, inputs resident
     on the GPU, nd_cqmat_apply's event timing): codes uniform over the 16
-    values, f16 norms |N(0, 0.02)|, activations N(0, 1); the decode combine
-    (T = 1) for every M. Bytes: weight codes and norms + int8 activations and
-    scales + f32 outputs; ops: 2 M N K. Weights of one matrix (<= 6.5 MB) stay
-    in L2 across the back-to-back runs."""
+    values, f16 norms |N(0, 0.02)|, activations N(0, 1). Every M runs the
+    decode combine (T = 1, one token a row); M >= 16 also runs the prefill
+    combine as chunks of T = min(M, 32) tokens (the tensor-core kernel). One
+    matrix (at most 6.5 MB) stays in L2 across the runs. Bytes: weight codes and norms +
+    int8 activations and scales + f32 outputs; ops: 2 M N K. The oracle's
+    single-thread time for a sample of the same rows is the CPU baseline."""
     import needle_b200 as nb
+    from oracle import oracle as orc
 
     rng = np.random.default_rng(3)
     shapes = [("qkvg", 1568), ("out", 768), ("engram_kv", 1536), ("lm_head", 16384)]
@@ -315,13 +318,37 @@ def matmul_sweep(local):
         mat = nb.CQMat(codes, norms, local)
         for M in (1, 16, 128, 2048):
             x = rng.standard_normal((M, 768)).astype(np.float32)
-            reps = 200 if M * n <= 16 * 16384 else 50
-            _, ms = mat(x, T=1, reps=reps)
-            byt = n * 6 * (64 + 2) + M * 768 + M * 6 * 4 + M * n * 4
-            rows.append({"matrix": name, "N": n, "K": 768, "M": M, "us": round(ms * 1e3, 2),
-                         "GB_s": round(byt / (ms * 1e-3) / 1e9, 1), "int8_TOPS": round(2 * M * n * 768 / (ms * 1e-3) / 1e12, 2)})
+            for T in ([1] if M == 1 else [1, min(M, 32)]):
+                reps = 200 if M * n <= 16 * 16384 else 50
+                _, ms = mat(x, T=T, reps=reps)
+                byt = n * 6 * (64 + 2) + M * 768 + M * 6 * 4 + M * n * 4
+                sample = min(M, 32 if T > 1 else 4)
+                t0 = time.perf_counter()
+                orc.cq_matmul(codes.reshape(n, -1), norms, 768, x[:sample] if T > 1 else x[:1])
+                cpu_s = (time.perf_counter() - t0) * (M / sample if T > 1 else M)
+                rows.append({"matrix": name, "N": n, "K": 768, "M": M, "T": T,
+                             "combine": "decode" if T == 1 else "prefill", "us": round(ms * 1e3, 2),
+                             "GB_s": round(byt / (ms * 1e-3) / 1e9, 1),
+                             "int8_TOPS": round(2 * M * n * 768 / (ms * 1e-3) / 1e12, 2),
+                             "cpu_us": round(cpu_s * 1e6, 1)})
         del mat
     return rows
+
+
+def prefill_matmul_case(local, reps=20):
+    """The q|k|v|gate matmul of one 256-sequence prefill chunk (M = 8192 rows,
+    T = 32, the prefill combine on the tensor cores) through nd_cqmat_apply,
+    for a one-kernel profiler capture: one run, 3 warm-up runs, `reps` timed."""
+    import needle_b200 as nb
+
+    rng = np.random.default_rng(1)
+    n, M, T = 1568, 8192, 32
+    codes = rng.integers(0, 256, (n, 6, 64), dtype=np.uint8)
+    norms = np.abs(rng.standard_normal((n, 6)) * 0.02).astype(np.float16).view(np.uint16)
+    mat = nb.CQMat(codes, norms, local)
+    x = rng.standard_normal((M, 768)).astype(np.float32)
+    _, ms = mat(x, T=T, reps=reps)
+    return {"matrix": "qkvg 1568 x 768", "M": M, "T": T, "us_a8_and_matmul": round(ms * 1e3, 2)}
 
 
 OPS_T = (1, 64, 1024, 8192)
@@ -665,9 +692,16 @@ def main():
     torch.cuda.set_device(local)
     import needle_b200 as nb
 
+    if args.profile and args.profile_case == "prefill_matmul":
+        if rank == 0:
+            print(json.dumps(prefill_matmul_case(local)), flush=True)
+        return
     if args.sweep:
         if rank == 0:
-            print(json.dumps({"sweep": "cq_w4a8_matmul", "combine": "decode", "rows": matmul_sweep(local)}), flush=True)
+            print(json.dumps({"sweep": "cq_w4a8_matmul", "cpu_baseline": {"kind": "port", "cores": 1,
+                                                                           "sample": "the oracle on 1-32 rows of the same "
+                                                                                     "matmul, scaled to M rows"},
+                              "rows": matmul_sweep(local)}), flush=True)
         if dist:
             dist.barrier()
             dist.destroy_process_group()

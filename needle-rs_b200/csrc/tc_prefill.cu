@@ -9,18 +9,29 @@
 // The integer sums come from tcgen05.mma.kind::i8 (A = 128 weight rows,
 // B = 128 tokens, K = 32 bytes an instruction, four per group) into an s32
 // accumulator in tensor memory: one 128 x 128 accumulator per group, so the
-// float chain sees each group's sum exactly as the reference forms it. The
+// float chain sees each group's sum exactly as the reference forms it. Each
+// accumulator starts at the int32 bit pattern of 1.5 * 2^23 (written by
+// tcgen05.st), which turns the sum into a float with one exact subtraction
+// instead of a quarter-rate int-to-float conversion. The
 // operands arrive by TMA (cp.async.bulk.tensor, 128-byte swizzle) from this
 // GPU's own HBM: the weights' int8 copy [out][768] and the A8 rows [M][768]
 // (both in the engine's lane-major slot order within a group, which a full
 // group sum does not see). No cluster multicast.
 //
-// One CTA per SM, persistent over 128 x 128 output tiles, warp-specialised:
-// warp 0 issues the TMA loads into a 4-stage ring, warp 1 issues the MMAs
-// into 4 tensor-memory buffers of 128 columns, warps 2-9 read each group's
+// One CTA per SM, persistent over a contiguous run of the 128 x 128 output
+// tiles in weight-tile-major order, warp-specialised: warp 0 issues the TMA
+// loads (a run's 128 weight rows stay resident in shared memory, all of K,
+// reloaded only when the run reaches the next weight tile; the tokens'
+// activations stream through a 3-stage ring one group at a time), warp 1
+// issues the MMAs into 4 tensor-memory buffers of 128 columns, warp 10 writes each tile's
+// column factors (the tokens' sx, or cbs * sx for remainder rows, per
+// group) a tile ahead into a double buffer, and warps 2-9 read each group's
 // sums back with tcgen05.ld (warp w reads lanes 32 (w % 4) .. + 31, i.e. 32
-// weight rows, and half of the 128 token columns) and run the fma chains in
-// registers; the tile's outputs leave as coalesced 128-byte rows of y.
+// weight rows, and a quarter of the 128 token columns) and run the fma
+// chains in registers, paired in f32x2; a tile's outputs are staged in
+// shared memory and written by one TMA bulk store (when y's rows are
+// 16-byte aligned; else by coalesced plain stores), which overlaps the next
+// tile's work.
 //
 // Every wait on an mbarrier is bounded: on expiry the kernel records an
 // error code in *err, every role stops issuing work, waits (bounded) for
@@ -41,16 +52,22 @@ namespace nd {
 
 constexpr int TC_ROWS = 128;     // weight rows a tile (MMA M, tensor-memory lanes)
 constexpr int TC_TOK = 128;      // tokens a tile (MMA N, tensor-memory columns)
-constexpr int TC_STAGES = 4;     // shared-memory ring of (weights, activations) group tiles
+constexpr int TC_STAGES = 3;     // shared-memory ring of activation group tiles
 constexpr int TC_BUFS = 4;       // tensor-memory accumulators of 128 columns (all 512)
-constexpr int TC_THREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
-constexpr int TC_EPI_WARPS = 8;
-constexpr uint32_t TC_TILE_BYTES = TC_ROWS * 128;                   // one group of 128 rows: 16 KB
-constexpr uint32_t TC_STAGE_BYTES = 2 * TC_TILE_BYTES;              // weights + activations
-constexpr size_t TC_SMEM = 1024 + (size_t)TC_STAGES * TC_STAGE_BYTES  // ring (1024-aligned)
-                           + 6 * TC_TOK * 4                           // column factors [6][128]
-                           + TC_TOK * 4                               // remainder flags
-                           + 16 * 8 + 16;                             // barriers, tmem address, abort
+constexpr int TC_EPI_WARPS = 16;  // warps 2-17: 4 lane quarters x 4 column quarters
+constexpr int TC_SCALE_WARP = 2 + TC_EPI_WARPS;
+constexpr int TC_THREADS = 32 * (TC_SCALE_WARP + 1);  // + warp 0 TMA, warp 1 MMA, warp 18 column factors
+constexpr uint32_t TC_TILE_BYTES = TC_ROWS * 128;   // one group of 128 rows: 16 KB
+constexpr uint32_t TC_W_BYTES = 6 * TC_TILE_BYTES;   // a weight tile, all of K: 96 KB
+constexpr uint32_t TC_STAGE_BYTES = TC_TILE_BYTES;   // an activation group tile
+constexpr int TC_NBARS = 2 * TC_STAGES + 2 * TC_BUFS + 6;
+constexpr uint32_t TC_OUT_BYTES = TC_TOK * TC_ROWS * 4;  // the output tile [128 tokens][128 rows] f32
+constexpr size_t TC_SMEM = 1024 + TC_W_BYTES                          // weight tile (1024-aligned)
+                           + (size_t)TC_STAGES * TC_STAGE_BYTES        // activation ring
+                           + TC_OUT_BYTES                             // output staging
+                           + 2 * 6 * TC_TOK * 4                       // column factors [2][6][128]
+                           + 2 * TC_TOK * 4                           // remainder flags [2][128]
+                           + TC_NBARS * 8 + 16;                       // barriers, tmem address, abort
 constexpr uint32_t TC_SPIN = 1u << 20;  // try_wait rounds before a wait counts as failed
 
 // --------------------------------------------------------------- PTX helpers
@@ -101,6 +118,20 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// A 2-D tiled TMA store of the f32 box {128 rows of y, 128 tokens} from
+// shared memory at (x = weight row, y = token); parts outside y's extents
+// are not written.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];\n" ::"l"((uint64_t)map),
+                 "r"(src), "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;\n" ::"n"(TC_EPI_WARPS * 32) : "memory"); }
+
 __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];\n" ::"l"((uint64_t)map) : "memory");
 }
@@ -148,39 +179,89 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+// Wait for this thread's tensor-memory loads; the loaded registers are
+// tied to the wait so no use of them is scheduled before it.
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+                   "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                   "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
+}
 
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;\n" ::"n"(TC_EPI_WARPS * 32) : "memory"); }
+// Every group sum s has |s| <= 128 * 128 * 128 < 2^22, so the int32 word
+// s + bits(1.5 * 2^23) read as a float is 1.5 * 2^23 + s exactly, and one
+// f32 subtraction gives float(s) without an int-to-float conversion.
+constexpr uint32_t TC_MAGIC = 0x4B400000u;
+
+__device__ __forceinline__ float2 tc_sub2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n.reg .b64 ra, rb, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\nsub.rn.f32x2 rd, ra, rb;\nmov.b64 {%0, %1}, rd;\n}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
+// Two independent IEEE products / fmas (sm_100 f32x2).
+__device__ __forceinline__ float2 tc_mul2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n.reg .b64 ra, rb, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\nmul.rn.f32x2 rd, ra, rb;\nmov.b64 {%0, %1}, rd;\n}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 tc_fma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n.reg .b64 ra, rb, rc, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\nmov.b64 rc, {%6, %7};\n"
+        "fma.rn.f32x2 rd, ra, rb, rc;\nmov.b64 {%0, %1}, rd;\n}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
 
 __device__ __forceinline__ void pdl_wait_tc() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_tc() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
 
 // ------------------------------------------------------------------ kernel
 
-// REM: some token rows are remainder rows (T % 4 != 0).
-template <bool REM>
+// REM: some token rows are remainder rows (T % 4 != 0). BULK: the output
+// tile leaves by a TMA store through map_y (y + col0 as [M][W.out] f32 rows
+// ldy apart); else by plain stores.
+template <bool REM, bool BULK>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-    cq_tc_prefill_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a, DevMat W,
-                         const float* __restrict__ sx, int M, int T, float* __restrict__ y, int ldy, int col0, int* err) {
+    cq_tc_prefill_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a,
+                         const __grid_constant__ CUtensorMap map_y, DevMat W, const float* __restrict__ sx, int M, int T,
+                         float* __restrict__ y, int ldy, int col0, int* err) {
     pdl_launch_tc();
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
-    const uint32_t ring = (raw + 1023u) & ~1023u;  // 1024-aligned for the 128-byte swizzle
+    const uint32_t wtile = (raw + 1023u) & ~1023u;  // 1024-aligned for the 128-byte swizzle
+    const uint32_t ring = wtile + TC_W_BYTES;
     uint8_t* gring = smem_raw + (ring - raw);
-    float* colv = (float*)(gring + TC_STAGES * TC_STAGE_BYTES);  // [6][128]
-    int* remf = (int*)(colv + 6 * TC_TOK);                       // [128]
-    uint64_t* bars = (uint64_t*)(remf + TC_TOK);                 // full[4] empty[4] tfull[4] tempty[4]
-    uint32_t* tmem_slot = (uint32_t*)(bars + 16);
+    float* stage_out = (float*)(gring + TC_STAGES * TC_STAGE_BYTES);  // [128 tokens][128 rows]
+    float* colv = stage_out + TC_TOK * TC_ROWS;                       // [2][6][128]
+    int* remf = (int*)(colv + 2 * 6 * TC_TOK);                   // [2][128]
+    // full[STAGES] empty[STAGES] tfull[BUFS] tempty[BUFS] cfull[2] cempty[2] wfull wempty
+    uint64_t* bars = (uint64_t*)(remf + 2 * TC_TOK);
+    uint32_t* tmem_slot = (uint32_t*)(bars + TC_NBARS);
     volatile int* abort = (volatile int*)(tmem_slot + 1);
     const uint32_t bar0 = smem_u32(bars);
     auto full = [&](int s) { return bar0 + 8u * s; };
-    auto empty = [&](int s) { return bar0 + 8u * (4 + s); };
-    auto tfull = [&](int b) { return bar0 + 8u * (8 + b); };
-    auto tempty = [&](int b) { return bar0 + 8u * (12 + b); };
+    auto empty = [&](int s) { return bar0 + 8u * (TC_STAGES + s); };
+    auto tfull = [&](int b) { return bar0 + 8u * (2 * TC_STAGES + b); };
+    auto tempty = [&](int b) { return bar0 + 8u * (2 * TC_STAGES + TC_BUFS + b); };
+    auto cfull = [&](int t) { return bar0 + 8u * (2 * TC_STAGES + 2 * TC_BUFS + t); };
+    auto cempty = [&](int t) { return bar0 + 8u * (2 * TC_STAGES + 2 * TC_BUFS + 2 + t); };
+    const uint32_t wfull = bar0 + 8u * (2 * TC_STAGES + 2 * TC_BUFS + 4), wempty = wfull + 8u;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tilesN = (W.out + TC_ROWS - 1) / TC_ROWS, tilesM = (M + TC_TOK - 1) / TC_TOK;
     const int ntiles = tilesN * tilesM;
+    // this CTA's run of tiles t0 .. t1 - 1; tile t is weight tile t / tilesM,
+    // token tile t % tilesM
+    const int t0 = (int)((long long)blockIdx.x * ntiles / gridDim.x), t1 = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < TC_STAGES; s++) {
@@ -191,10 +272,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_init(tfull(b), 1);
             mbar_init(tempty(b), TC_EPI_WARPS);
         }
+        for (int t = 0; t < 2; t++) {
+            mbar_init(cfull(t), 1);
+            mbar_init(cempty(t), TC_EPI_WARPS);
+        }
+        mbar_init(wfull, 1);
+        mbar_init(wempty, 1);
         *abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         tma_prefetch_map(&map_w);
         tma_prefetch_map(&map_a);
+        if (BULK) tma_prefetch_map(&map_y);
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
@@ -206,25 +294,38 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-
     if (warp == 0) {
         // ---- TMA producer: lane 0 waits and issues, the warp stays converged
-        int G = 0;  // group counter across this CTA's tiles
+        int G = 0, wk = 0, cur_n = -1;  // activation groups, weight tiles loaded
         bool ok = true, waited = false;
-        for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-            const int n0 = (tile % tilesN) * TC_ROWS, m0 = (tile / tilesN) * TC_TOK;
+        for (int t = t0; t < t1 && ok; t++) {
+            const int nt = t / tilesM, m0 = (t % tilesM) * TC_TOK;
+            int good = 1;
+            if (nt != cur_n) {
+                // the weight tile, all six groups; the previous one must be
+                // done with (its last MMAs committed to wempty)
+                if (lane == 0) {
+                    if (wk > 0) good = mbar_wait(wempty, (wk - 1) & 1, abort, err, 9);
+                    if (good) {
+                        mbar_expect_tx(wfull, TC_W_BYTES);
+                        for (int g = 0; g < 6; g++) tma_load_2d(wtile + g * TC_TILE_BYTES, &map_w, g * 128, nt * TC_ROWS, wfull);
+                    }
+                }
+                ok = __shfl_sync(0xffffffffu, good, 0) != 0;
+                if (!ok) break;
+                cur_n = nt;
+                wk++;
+            }
             for (int g = 0; g < 6; g++, G++) {
                 const int s = G % TC_STAGES;
-                int good = 1;
+                good = 1;
                 if (lane == 0) {
                     if (G >= TC_STAGES) good = mbar_wait(empty(s), ((G / TC_STAGES) - 1) & 1, abort, err, 1);
                     if (good) {
-                        const uint32_t dst = ring + s * TC_STAGE_BYTES;
-                        mbar_expect_tx(full(s), TC_STAGE_BYTES);
-                        tma_load_2d(dst, &map_w, g * 128, n0, full(s));
                         // the activations are the predecessor kernel's output
                         if (!waited) pdl_wait_tc();
-                        tma_load_2d(dst + TC_TILE_BYTES, &map_a, g * 128, m0, full(s));
+                        mbar_expect_tx(full(s), TC_STAGE_BYTES);
+                        tma_load_2d(ring + s * TC_STAGE_BYTES, &map_a, g * 128, m0, full(s));
                     }
                 }
                 waited = true;
@@ -239,27 +340,39 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const int Gk = G - 1 - k, s = Gk % TC_STAGES;
                 mbar_wait(full(s), (Gk / TC_STAGES) & 1, abort, err, 5);
             }
+            if (wk > 0) mbar_wait(wfull, (wk - 1) & 1, abort, err, 5);
         }
         __syncwarp();
     } else if (warp == 1) {
         // ---- MMA issuer: lane 0 waits and issues, the warp stays converged
-        int G = 0;
+        int G = 0, wk = 0, cur_n = -1;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        for (int t = t0; t < t1 && ok; t++) {
+            const int nt = t / tilesM;
+            const bool last_of_w = t + 1 == t1 || (t + 1) / tilesM != nt;
+            int good = 1;
+            if (nt != cur_n) {
+                if (lane == 0) good = mbar_wait(wfull, wk & 1, abort, err, 10);
+                ok = __shfl_sync(0xffffffffu, good, 0) != 0;
+                if (!ok) break;
+                cur_n = nt;
+                wk++;
+            }
             for (int g = 0; g < 6; g++, G++) {
                 const int s = G % TC_STAGES, b = G % TC_BUFS;
-                int good = 1;
+                good = 1;
                 if (lane == 0) {
                     good = mbar_wait(full(s), (G / TC_STAGES) & 1, abort, err, 2);
                     if (good && G >= TC_BUFS) good = mbar_wait(tempty(b), ((G / TC_BUFS) - 1) & 1, abort, err, 3);
                     if (good) {
                         tc_fence_after();
-                        const uint32_t wa = ring + s * TC_STAGE_BYTES, aa = wa + TC_TILE_BYTES;
+                        const uint32_t wa = wtile + g * TC_TILE_BYTES, aa = ring + s * TC_STAGE_BYTES;
                         const uint32_t d = tmem + (uint32_t)(b * TC_TOK);
 #pragma unroll
                         for (int kk = 0; kk < 4; kk++) mma_i8(d, sw128_desc(wa + 32 * kk), sw128_desc(aa + 32 * kk), kk);
                         mma_commit(empty(s));  // the stage is free once these MMAs have read it
                         mma_commit(tfull(b));  // the group's sums are in buffer b
+                        if (g == 5 && last_of_w) mma_commit(wempty);  // the weight tile is done with
                     }
                 }
                 ok = __shfl_sync(0xffffffffu, good, 0) != 0;
@@ -272,77 +385,145 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_wait(tfull(Gl % TC_BUFS), (Gl / TC_BUFS) & 1, abort, err, 6);
         }
         __syncwarp();
-    } else {
-        // ---- epilogue: warps 2-9
+    } else if (warp == TC_SCALE_WARP) {
+        // ---- column factors, a tile ahead: sx of each token and group for
+        // block rows, cbs * sx for remainder rows (0 past M), and the
+        // remainder flags, into buffer (tile count) % 2
         pdl_wait_tc();
-        const int e = warp - 2, q = warp & 3, half = e >> 2;
-        const int et = threadIdx.x - 64;  // 0..255
         const float cbs = W.cbs;
         const int blocked = T / 4 * 4;
-        int G = 0;
+        int it = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-            const int n0 = (tile % tilesN) * TC_ROWS, m0 = (tile / tilesN) * TC_TOK;
-            const int n = n0 + q * 32 + lane;  // this thread's weight row
-            // the tile's column factors: sx (block rows) or cbs * sx
-            // (remainder rows) of each token and group
-            epi_bar();
-            for (int i = et; i < 6 * TC_TOK; i += TC_EPI_WARPS * 32) {
-                const int g = i / TC_TOK, j = i % TC_TOK, m = m0 + j;
-                float v = 0.f;
-                if (m < M) {
-                    const float s = __ldg(sx + (size_t)m * 6 + g);
-                    v = (m % T) < blocked ? s : __fmul_rn(cbs, s);
-                }
-                colv[g * TC_TOK + j] = v;
+        for (int tile = t0; tile < t1 && ok; tile++, it++) {
+            const int m0 = (tile % tilesM) * TC_TOK, tb = it & 1;
+            int good = 1;
+            if (lane == 0 && it >= 2) good = mbar_wait(cempty(tb), ((it >> 1) - 1) & 1, abort, err, 7);
+            ok = __shfl_sync(0xffffffffu, good, 0) != 0;
+            if (!ok) break;
+            float v[24];
+#pragma unroll
+            for (int k = 0; k < 24; k++) {
+                const int i = lane + 32 * k, j = i / 6, g = i % 6, m = m0 + j;  // sx is [M][6]: contiguous per tile
+                v[k] = m < M ? __ldg(sx + (size_t)m0 * 6 + i) : 0.f;
+                if ((m % T) >= blocked) v[k] = __fmul_rn(cbs, v[k]);
+                (void)g;
+            }
+            float* cv = colv + tb * 6 * TC_TOK;
+#pragma unroll
+            for (int k = 0; k < 24; k++) {
+                const int i = lane + 32 * k, j = i / 6, g = i % 6;
+                cv[g * TC_TOK + j] = v[k];
             }
             if (REM)
-                for (int j = et; j < TC_TOK; j += TC_EPI_WARPS * 32) remf[j] = ((m0 + j) % T) >= blocked;
-            // the row factors: norm * cbs (block rows), norm (remainder rows)
-            float nrm[6], nc[6];
 #pragma unroll
-            for (int g = 0; g < 6; g++) {
-                nrm[g] = n < W.out ? h2f(__ldg(W.norms + (size_t)n * 6 + g)) : 0.f;
-                nc[g] = __fmul_rn(nrm[g], cbs);
+                for (int k = 0; k < 4; k++) {
+                    const int j = lane + 32 * k;
+                    remf[tb * TC_TOK + j] = ((m0 + j) % T) >= blocked;
+                }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(cfull(tb));
+        }
+    } else {
+        // ---- epilogue: warps 2-17; warp w reads lanes 32 (w % 4) .. + 31 (its
+        // weight rows) and the column quarter c of the 128 tokens
+        pdl_wait_tc();
+        const int e = warp - 2, q = warp & 3, c = e >> 2;
+        const bool leader = e == 0 && lane == 0;  // issues the tile's bulk store
+        const float cbs = W.cbs;
+        int G = 0, it = 0;
+        bool ok = true;
+        // the row factors of this thread's weight row for the first tile; each
+        // tile then loads the next tile's
+        float nrm[6];
+        {
+            const int n = (t0 / tilesM) * TC_ROWS + q * 32 + lane;
+#pragma unroll
+            for (int g = 0; g < 6; g++) nrm[g] = (t0 < t1 && n < W.out) ? h2f(__ldg(W.norms + (size_t)n * 6 + g)) : 0.f;
+        }
+        for (int tile = t0; tile < t1; tile++, it++) {
+            const int n0 = (tile / tilesM) * TC_ROWS, m0 = (tile % tilesM) * TC_TOK, tb = it & 1;
+            const int n = n0 + q * 32 + lane;  // this thread's weight row
+            float nc[6];  // norm * cbs (block rows); remainder rows use norm alone
+#pragma unroll
+            for (int g = 0; g < 6; g++) nc[g] = __fmul_rn(nrm[g], cbs);
+            float nrm_next[6];
+            {
+                const int t2 = tile + 1, n2 = (t2 / tilesM) * TC_ROWS + q * 32 + lane;
+#pragma unroll
+                for (int g = 0; g < 6; g++) nrm_next[g] = (t2 < t1 && n2 < W.out) ? h2f(__ldg(W.norms + (size_t)n2 * 6 + g)) : 0.f;
             }
-            epi_bar();
-            float acc[64];
+            int good = 1;
+            if (lane == 0 && ok) good = mbar_wait(cfull(tb), (it >> 1) & 1, abort, err, 8);
+            ok = ok && __shfl_sync(0xffffffffu, good, 0) != 0;
+            const float* cvt = colv + tb * 6 * TC_TOK + c * 32;
+            const int* rf = remf + tb * TC_TOK + c * 32;
+            float2 acc[16];
 #pragma unroll
-            for (int j = 0; j < 64; j++) acc[j] = 0.f;
+            for (int j = 0; j < 16; j++) acc[j] = make_float2(0.f, 0.f);
             for (int g = 0; g < 6; g++, G++) {
                 const int b = G % TC_BUFS;
-                if (ok) ok = mbar_wait(tfull(b), (G / TC_BUFS) & 1, abort, err, 4);
+                good = 1;
+                if (lane == 0 && ok) good = mbar_wait(tfull(b), (G / TC_BUFS) & 1, abort, err, 4);
+                ok = ok && __shfl_sync(0xffffffffu, good, 0) != 0;
                 tc_fence_after();
-                uint32_t r0[32], r1[32];
-                const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * TC_TOK + half * 64);
+                uint32_t r[32];
                 if (ok) {
-                    tmem_ld32(ta, r0);
-                    tmem_ld32(ta + 32, r1);
-                    tmem_ld_wait();
+                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * TC_TOK + c * 32), r);
+                    tmem_ld_wait(r);
                 } else {
 #pragma unroll
-                    for (int j = 0; j < 32; j++) r0[j] = r1[j] = 0u;
+                    for (int j = 0; j < 32; j++) r[j] = 0u;
                 }
+                // the sums are in registers: the buffer is free
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(tempty(b));
-                const float* cv = colv + g * TC_TOK + half * 64;
+                const float* cv = cvt + g * TC_TOK;
+                const float2 mg = make_float2(12582912.0f, 12582912.0f);
 #pragma unroll
-                for (int j = 0; j < 64; j++) {
-                    const float s = (float)(int)(j < 32 ? r0[j] : r1[j - 32]);
-                    float f = nc[g];
-                    if (REM && remf[half * 64 + j]) f = nrm[g];
-                    acc[j] = __fmaf_rn(s, __fmul_rn(f, cv[j]), acc[j]);
+                for (int j = 0; j < 16; j++) {  // token pair (2j, 2j + 1) of this quarter
+                    const float2 s2 = tc_sub2(make_float2(__uint_as_float(r[2 * j] + TC_MAGIC), __uint_as_float(r[2 * j + 1] + TC_MAGIC)), mg);
+                    const float2 c2 = *(const float2*)(cv + 2 * j);
+                    float2 f2 = make_float2(nc[g], nc[g]);
+                    if (REM) {
+                        if (rf[2 * j]) f2.x = nrm[g];
+                        if (rf[2 * j + 1]) f2.y = nrm[g];
+                    }
+                    acc[j] = tc_fma2(s2, tc_mul2(f2, c2), acc[j]);
                 }
             }
-            if (ok && n < W.out) {
+            // the column factors of this tile are read: free the buffer
+            __syncwarp();
+            if (lane == 0) mbar_arrive(cempty(tb));
+            if (BULK) {
+                // stage the tile [token][row] and let one thread store it; the
+                // previous tile's store must have read the staging first
+                if (leader) bulk_wait_read();
+                epi_sync();
+                float* so = stage_out + (c * 32) * TC_ROWS + q * 32 + lane;
 #pragma unroll
-                for (int j = 0; j < 64; j++) {
-                    const int m = m0 + half * 64 + j;
-                    if (m < M) y[(size_t)m * ldy + col0 + n] = acc[j];
+                for (int j = 0; j < 16; j++) {
+                    so[(2 * j) * TC_ROWS] = acc[j].x;
+                    so[(2 * j + 1) * TC_ROWS] = acc[j].y;
+                }
+                fence_async_smem();
+                epi_sync();
+                if (leader && ok) {
+                    tma_store_2d(&map_y, smem_u32(stage_out), n0, m0);
+                    bulk_commit();
+                }
+            } else if (ok && n < W.out) {
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    const int m = m0 + c * 32 + 2 * j;
+                    if (m < M) y[(size_t)m * ldy + col0 + n] = acc[j].x;
+                    if (m + 1 < M) y[(size_t)(m + 1) * ldy + col0 + n] = acc[j].y;
                 }
             }
+#pragma unroll
+            for (int g = 0; g < 6; g++) nrm[g] = nrm_next[g];
         }
+        if (BULK && leader) bulk_wait_all();
     }
     tc_fence_before();
     __syncthreads();
@@ -382,6 +563,22 @@ static bool int8_rows_map(CUtensorMap* map, const void* base, int rows) {
     const cuuint32_t estr[2] = {1, 1};
     return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The tensor map of y + col0 as [M][out] f32 rows `ldy` floats apart, stored
+// in boxes of 128 rows x 128 tokens; false when the rows are not 16-byte
+// aligned (the kernel then stores without TMA).
+static bool f32_out_map(CUtensorMap* map, float* y, int col0, int out, int M, int ldy) {
+    EncodeTiled enc = encode_fn();
+    const float* base = y + col0;
+    if (!enc || ((uintptr_t)base & 15) || ((size_t)ldy * 4) % 16 || out < 1 || M < 1) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)out, (cuuint64_t)M};
+    const cuuint64_t strides[1] = {(cuuint64_t)ldy * 4};
+    const cuuint32_t box[2] = {TC_ROWS, TC_TOK};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -428,9 +625,14 @@ int tc_prefill_error() {
 }
 
 cudaError_t tc_prefill_init() {
-    cudaError_t e = cudaFuncSetAttribute(cq_tc_prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(cq_tc_prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM);
+    cudaError_t e = cudaSuccess;
+    auto set = [&](const void* f) {
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM);
+    };
+    set((const void*)cq_tc_prefill_kernel<false, false>);
+    set((const void*)cq_tc_prefill_kernel<false, true>);
+    set((const void*)cq_tc_prefill_kernel<true, false>);
+    set((const void*)cq_tc_prefill_kernel<true, true>);
     return e;
 }
 
@@ -438,8 +640,10 @@ cudaError_t launch_cq_prefill_tc(DevMat W, const int8_t* act, const float* sx, i
                                  cudaStream_t st) {
     int* err = tc_err_ptr();
     if (!W.w8 || W.in_dim != 768 || W.groups != 6 || M < 1 || T < 2 || !err) return cudaErrorInvalidValue;
-    CUtensorMap mw, ma;
+    CUtensorMap mw, ma, my;
     if (!int8_rows_map(&mw, W.w8, W.out) || !int8_rows_map(&ma, act, M)) return cudaErrorInvalidValue;
+    const bool bulk = f32_out_map(&my, y, col0, W.out, M, ldy);
+    if (!bulk) my = mw;  // unused by the plain-store variant
     const int ntiles = ((W.out + TC_ROWS - 1) / TC_ROWS) * ((M + TC_TOK - 1) / TC_TOK);
     const int grid = std::min(ntiles, sm_count_tc());
     cudaLaunchConfig_t cfg{};
@@ -452,9 +656,11 @@ cudaError_t launch_cq_prefill_tc(DevMat W, const int8_t* act, const float* sx, i
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = st ? 1 : 0;
-    if (T % 4)
-        return cudaLaunchKernelEx(&cfg, cq_tc_prefill_kernel<true>, mw, ma, W, sx, M, T, y, ldy, col0, err);
-    return cudaLaunchKernelEx(&cfg, cq_tc_prefill_kernel<false>, mw, ma, W, sx, M, T, y, ldy, col0, err);
+    const bool rem = T % 4 != 0;
+    if (rem && bulk) return cudaLaunchKernelEx(&cfg, cq_tc_prefill_kernel<true, true>, mw, ma, my, W, sx, M, T, y, ldy, col0, err);
+    if (rem) return cudaLaunchKernelEx(&cfg, cq_tc_prefill_kernel<true, false>, mw, ma, my, W, sx, M, T, y, ldy, col0, err);
+    if (bulk) return cudaLaunchKernelEx(&cfg, cq_tc_prefill_kernel<false, true>, mw, ma, my, W, sx, M, T, y, ldy, col0, err);
+    return cudaLaunchKernelEx(&cfg, cq_tc_prefill_kernel<false, false>, mw, ma, my, W, sx, M, T, y, ldy, col0, err);
 }
 
 }  // namespace nd
