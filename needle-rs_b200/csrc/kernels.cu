@@ -489,6 +489,12 @@ __global__ void __launch_bounds__(256, 2) cq_mma_kernel(DevMat W, const int8_t* 
 // (p % 64) / 16 = 2(a&1) + (l>>1) they are i % 16 = 2 lane + {0, 1, 8, 9}
 // (xor 1, 8). Lanes 0-3 then run the reference's fma chain over groups.
 constexpr int GEMV_MAXM = 4;
+// From this many one-token rows the decode combine runs on the tensor-core
+// kernel (tc_prefill.cu); between GEMV_MAXM and it, on int8 mma.sync tiles.
+// The prefill combine likewise from TC_PREFILL_MIN_ROWS rows (a few chunks of
+// 32: below that the tensor-core kernel has too few tiles to fill the GPU).
+constexpr int TC_DECODE_MIN_ROWS = 64;
+constexpr int TC_PREFILL_MIN_ROWS = 256;
 
 __device__ __forceinline__ uint32_t lut4(uint32_t nib16, uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3) {
     uint32_t idx = nib16 & 0x7777u;
@@ -587,10 +593,13 @@ cudaError_t launch_cq_gemm(DevMat W, const int8_t* act, const float* sx, int M, 
         else launch_pdl(cq_gemv_kernel<8>, grid, dim3(256), 0, st, W, act, sx, M, y, ldy, col0);
         return cudaSuccess;
     }
-    if (T > 1) return launch_cq_prefill_tc(W, act, sx, M, T, y, ldy, col0, st);
+    if (T > 1 && M >= TC_PREFILL_MIN_ROWS) return launch_cq_prefill_tc(W, act, sx, M, T, y, ldy, col0, st);
+    if (T == 1 && M >= TC_DECODE_MIN_ROWS && W.width != 2) return launch_cq_decode_tc(W, act, sx, M, y, ldy, col0, st);
     const int per = 2 * sm_count();
     const int grid = std::min(cdiv(W.out, MMA_BN) * cdiv(M, MMA_BM), per);
-    if (W.width == 2)
+    if (T > 1)
+        launch_pdl(cq_mma_kernel<false, false>, dim3(grid), dim3(256), MMA_SMEM, st, W, act, sx, M, T, y, ldy, col0);
+    else if (W.width == 2)
         launch_pdl(cq_mma_kernel<true, true>, dim3(grid), dim3(256), MMA_SMEM, st, W, act, sx, M, T, y, ldy, col0);
     else
         launch_pdl(cq_mma_kernel<true, false>, dim3(grid), dim3(256), MMA_SMEM, st, W, act, sx, M, T, y, ldy, col0);
@@ -2674,6 +2683,7 @@ static cudaError_t init_attrs() {
     cudaFuncSetAttribute(post_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)POST_ROW_SMEM);
     cudaFuncSetAttribute(cq_mma_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
     cudaFuncSetAttribute(cq_mma_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
+    cudaFuncSetAttribute(cq_mma_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
     return tc_prefill_init();
 }
 

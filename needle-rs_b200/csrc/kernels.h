@@ -102,9 +102,10 @@ void launch_embed(DevMat emb, const int32_t* ids, int M, float* xs, cudaStream_t
 void launch_prep_act(const float* x, int ldx, int K, int M, int8_t* act, float* sx, cudaStream_t st);
 // y[m][col0 + n] for n < W.out. T sets the combine per row: T == 1 the
 // decode combine (the code-reading GEMV for up to 4 rows, int8 mma.sync tiles
-// beyond), else the prefill combine with the block/remainder rule over each
-// sequence's T rows on tcgen05 (launch_cq_prefill_tc). cudaErrorInvalidValue
-// (nothing launched) unless W reads 768 inputs and carries its w8 copy.
+// up to 63, the tcgen05 kernel from 64, 2-bit matrices on mma.sync), else the
+// prefill combine with the block/remainder rule over each sequence's T rows
+// (mma.sync below 256 rows, tcgen05 from 256). cudaErrorInvalidValue (nothing
+// launched) unless W reads 768 inputs and carries its w8 copy.
 cudaError_t launch_cq_gemm(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y, int ldy, int col0,
                            cudaStream_t st);
 // The prefill combine (T > 1) on tcgen05 tensor cores fed by TMA (tc_prefill.cu);
@@ -114,6 +115,11 @@ cudaError_t launch_cq_gemm(DevMat W, const int8_t* act, const float* sx, int M, 
 // kernel expired (read it after synchronising the stream).
 cudaError_t launch_cq_prefill_tc(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y, int ldy, int col0,
                                  cudaStream_t st);
+// The decode combine on the same tensor-core kernel (launch_cq_gemm routes
+// batched one-token steps here); not for 2-bit matrices, whose decode lanes
+// are split runs of the group.
+cudaError_t launch_cq_decode_tc(DevMat W, const int8_t* act, const float* sx, int M, float* y, int ldy, int col0,
+                                cudaStream_t st);
 cudaError_t tc_prefill_init();
 int tc_prefill_error();
 void launch_engram_gather(DevMat tables, Caches c, int S, int T, int p0, int slots, float* e, cudaStream_t st);

@@ -1,37 +1,48 @@
-// The CQ/A8 matmul's prefill combine on the 5th-generation tensor cores.
+// The CQ/A8 matmul on the 5th-generation tensor cores, both combines.
 //
-// qlinear.rs:353-363 (prefill_row_ref) with the block/remainder rule of
-// qlinear.rs:395-419: for output row n and token m, each 128-wide group g
-// gives an exact int32 sum s of int8 weight x int8 activation products, and
-// acc = fma(float(s), sc, acc) over g = 0..5 in order, sc = (norm * cbs) * sx
-// for a sequence's first T/4*4 tokens and norm * (cbs * sx) for the rest.
+// Prefill combine, qlinear.rs:353-363 (prefill_row_ref) with the
+// block/remainder rule of qlinear.rs:395-419: for output row n and token m,
+// each 128-wide group g gives an exact int32 sum s of int8 weight x int8
+// activation products, and acc = fma(float(s), sc, acc) over g = 0..5 in
+// order, sc = (norm * cbs) * sx for a sequence's first T/4*4 tokens and
+// norm * (cbs * sx) for the rest.
+//
+// Decode combine, qlinear.rs:340-350 (decode_row_ref) for one-token rows:
+// each group splits into four decode lanes (inputs p with (p % 32) / 8 ==
+// l), lane l's int32 sum s_l feeds its own chain lanes[l] = fma(float(s_l),
+// sc, lanes[l]) with sc = (sx * cbs) * norm, and the row is (l0 + l1) +
+// (l2 + l3). In the engine's lane-major slot order decode lane l of a group
+// is the 32 contiguous bytes l*32 .. l*32 + 31 (the 4-bit lane rule, which
+// 3-bit records share; 2-bit records' split lanes stay on mma.sync).
 //
 // The integer sums come from tcgen05.mma.kind::i8 (A = 128 weight rows,
-// B = 128 tokens, K = 32 bytes an instruction, four per group) into an s32
-// accumulator in tensor memory: one 128 x 128 accumulator per group, so the
-// float chain sees each group's sum exactly as the reference forms it. Each
-// accumulator starts at the int32 bit pattern of 1.5 * 2^23 (written by
-// tcgen05.st), which turns the sum into a float with one exact subtraction
-// instead of a quarter-rate int-to-float conversion. The
+// B = the tile's tokens, K = 32 bytes an instruction, one per decode lane
+// of a group) into s32 accumulators in tensor memory: the prefill combine
+// chains a group's four MMAs into one accumulator (the group sum), the
+// decode combine gives each its own (the lane sums), so the float chains
+// see each sum exactly as the reference forms it. Each sum becomes a float
+// by an integer add of the bit pattern of 1.5 * 2^23 and one exact f32
+// subtraction instead of a quarter-rate int-to-float conversion. The
 // operands arrive by TMA (cp.async.bulk.tensor, 128-byte swizzle) from this
-// GPU's own HBM: the weights' int8 copy [out][768] and the A8 rows [M][768]
-// (both in the engine's lane-major slot order within a group, which a full
-// group sum does not see). No cluster multicast.
+// GPU's own HBM: the weights' int8 copy [out][768] and the A8 rows [M][768].
+// No cluster multicast.
 //
-// One CTA per SM, persistent over a contiguous run of the 128 x 128 output
-// tiles in weight-tile-major order, warp-specialised: warp 0 issues the TMA
-// loads (a run's 128 weight rows stay resident in shared memory, all of K,
-// reloaded only when the run reaches the next weight tile; the tokens'
-// activations stream through a 3-stage ring one group at a time), warp 1
-// issues the MMAs into 4 tensor-memory buffers of 128 columns, warp 10 writes each tile's
-// column factors (the tokens' sx, or cbs * sx for remainder rows, per
-// group) a tile ahead into a double buffer, and warps 2-9 read each group's
-// sums back with tcgen05.ld (warp w reads lanes 32 (w % 4) .. + 31, i.e. 32
-// weight rows, and a quarter of the 128 token columns) and run the fma
-// chains in registers, paired in f32x2; a tile's outputs are staged in
-// shared memory and written by one TMA bulk store (when y's rows are
-// 16-byte aligned; else by coalesced plain stores), which overlaps the next
-// tile's work.
+// One CTA per SM, persistent over a contiguous run of the output tiles
+// (128 weight rows x 64 tokens for the prefill combine, x 32 tokens for
+// the decode combine) in weight-tile-major order, warp-specialised: warp 0
+// issues the TMA loads (a run's 128 weight rows stay resident in shared
+// memory, all of K, one 96 KB box, reloaded only when the run reaches the
+// next weight tile; each tile's activations, all of K, arrive as one 3-D
+// box into a ring: the TMA cost here goes by loads more than by bytes, so
+// few large boxes), warp 1 issues the MMAs into tensor-memory group
+// buffers (all 512 columns), warp 18 writes each tile's column factors (per
+// token and group: sx or cbs * sx) a tile ahead into a double buffer, and
+// warps 2-17 read each group's sums back with tcgen05.ld (warp w reads
+// lanes 32 (w % 4) .. + 31, i.e. 32 weight rows, and a quarter of the
+// tile's token columns) and run the fma chains in registers, paired in
+// f32x2; a tile's outputs are staged in shared memory and written by one
+// TMA bulk store (when y's rows are 16-byte aligned; else by plain stores),
+// which overlaps the next tile's work.
 //
 // Every wait on an mbarrier is bounded: on expiry the kernel records an
 // error code in *err, every role stops issuing work, waits (bounded) for
@@ -50,24 +61,47 @@
 
 namespace nd {
 
-constexpr int TC_ROWS = 128;     // weight rows a tile (MMA M, tensor-memory lanes)
-constexpr int TC_TOK = 128;      // tokens a tile (MMA N, tensor-memory columns)
-constexpr int TC_STAGES = 3;     // shared-memory ring of activation group tiles
-constexpr int TC_BUFS = 4;       // tensor-memory accumulators of 128 columns (all 512)
+constexpr int TC_ROWS = 128;      // weight rows a tile (MMA M, tensor-memory lanes)
 constexpr int TC_EPI_WARPS = 16;  // warps 2-17: 4 lane quarters x 4 column quarters
 constexpr int TC_SCALE_WARP = 2 + TC_EPI_WARPS;
 constexpr int TC_THREADS = 32 * (TC_SCALE_WARP + 1);  // + warp 0 TMA, warp 1 MMA, warp 18 column factors
-constexpr uint32_t TC_TILE_BYTES = TC_ROWS * 128;   // one group of 128 rows: 16 KB
-constexpr uint32_t TC_W_BYTES = 6 * TC_TILE_BYTES;   // a weight tile, all of K: 96 KB
-constexpr uint32_t TC_STAGE_BYTES = TC_TILE_BYTES;   // an activation group tile
-constexpr int TC_NBARS = 2 * TC_STAGES + 2 * TC_BUFS + 6;
-constexpr uint32_t TC_OUT_BYTES = TC_TOK * TC_ROWS * 4;  // the output tile [128 tokens][128 rows] f32
-constexpr size_t TC_SMEM = 1024 + TC_W_BYTES                          // weight tile (1024-aligned)
-                           + (size_t)TC_STAGES * TC_STAGE_BYTES        // activation ring
-                           + TC_OUT_BYTES                             // output staging
-                           + 2 * 6 * TC_TOK * 4                       // column factors [2][6][128]
-                           + 2 * TC_TOK * 4                           // remainder flags [2][128]
-                           + TC_NBARS * 8 + 16;                       // barriers, tmem address, abort
+constexpr uint32_t TC_TILE_BYTES = TC_ROWS * 128;     // one group of 128 weight rows: 16 KB
+constexpr uint32_t TC_W_BYTES = 6 * TC_TILE_BYTES;    // a weight tile, all of K: 96 KB
+
+// Per combine: tokens a tile (the MMA's N), the tensor-memory columns of a
+// group's accumulators and how many group buffers fit the 512 columns, the
+// activation ring depth (a stage is one tile's activations, all of K, one
+// TMA box), and the kernel's shared memory.
+template <bool DEC>
+struct TcCfg {
+    static constexpr int TOK = DEC ? 32 : 64;
+    static constexpr int SLICE = DEC ? TOK : 0;         // columns between a group's lane accumulators
+    static constexpr int GROUP_COLS = DEC ? 4 * TOK : TOK;
+    static constexpr int BUFS = 512 / GROUP_COLS;
+    // The MMA warp and the epilogue hand tensor memory over two groups at a
+    // time (an acquire-ordered wait right after MMA issue costs ~300 cycles,
+    // so per-group hand-offs would pace the pipeline): a slot is two group
+    // buffers.
+    static constexpr int SLOTS = BUFS / 2;
+    static constexpr int CPT = TOK / 4;                  // token columns an epilogue thread reads
+    static constexpr int STAGES = DEC ? 4 : 2;
+    static constexpr uint32_t GRP_BYTES = TOK * 128;     // one group of the tile's tokens
+    static constexpr uint32_t STAGE_BYTES = 6 * GRP_BYTES;
+    static constexpr int OUT_HALVES = DEC ? 1 : 2;       // the output tile leaves in this many stores
+    static constexpr uint32_t OUT_BYTES = TOK / OUT_HALVES * TC_ROWS * 4;
+    static constexpr int NBARS = 2 * STAGES + 2 * BUFS + 6;
+    static constexpr size_t SMEM = 1024 + TC_W_BYTES     // weight tile (1024-aligned)
+                                   + (size_t)STAGES * STAGE_BYTES  // activation ring
+                                   + OUT_BYTES                     // output staging [TOK / OUT_HALVES][128] f32
+                                   + 2 * 6 * TOK * 4               // column factors [2][6][TOK]
+                                   + 2 * TOK * 4                   // remainder flags [2][TOK]
+                                   + NBARS * 8 + 16;               // barriers, tmem address, abort
+    // kind::i8: s32 accumulator (c_format 2), signed A and B (formats 1),
+    // both K-major, N = TOK (n_dim = N >> 3), M = 128 (m_dim = M >> 4)
+    static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TOK >> 3) << 17) | ((uint32_t)(TC_ROWS >> 4) << 24);
+};
+static_assert(TcCfg<false>::SMEM <= 227 * 1024 && TcCfg<true>::SMEM <= 227 * 1024, "shared memory per CTA");
+static_assert(TcCfg<true>::SLOTS >= 2 && TcCfg<false>::SLOTS >= 2, "double-buffered slots of two group accumulators");
 constexpr uint32_t TC_SPIN = 1u << 20;  // try_wait rounds before a wait counts as failed
 
 // --------------------------------------------------------------- PTX helpers
@@ -109,16 +143,7 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
 }
 
-// A 2-D tiled TMA load of box {128 bytes, 128 rows} at (x bytes, y rows),
-// completing `bar`'s transaction count. x is a multiple of 128.
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(dst),
-        "l"((uint64_t)map), "r"(x), "r"(y), "r"(bar)
-        : "memory");
-}
-
-// A 2-D tiled TMA store of the f32 box {128 rows of y, 128 tokens} from
+// A 2-D tiled TMA store of the f32 box {128 rows of y, the tile's tokens} from
 // shared memory at (x = weight row, y = token); parts outside y's extents
 // are not written.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
@@ -132,6 +157,16 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;\n" ::"n"(TC_EPI_WARPS * 32) : "memory"); }
 
+// A 3-D tiled TMA load of box {128 bytes, rows, 6 groups} at (0, y rows, 0):
+// a tile's rows over all of K, laid out group after group, each group the
+// [rows][128 bytes] tile the MMA descriptors address.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];\n" ::"r"(dst),
+        "l"((uint64_t)map), "r"(0), "r"(y), "r"(0), "r"(bar)
+        : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];\n" ::"l"((uint64_t)map) : "memory");
 }
@@ -144,16 +179,11 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
            ((uint64_t)2 << 61);
 }
 
-// Instruction descriptor, kind::i8: s32 accumulator (c_format 2), signed A
-// and B (formats 1), both K-major, N = 128 (n_dim = N >> 3), M = 128
-// (m_dim = M >> 4).
-constexpr uint32_t TC_IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TC_TOK >> 3) << 17) | ((uint32_t)(TC_ROWS >> 4) << 24);
-
-__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(TC_IDESC), "r"(accumulate)
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
@@ -166,27 +196,41 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
 
-// 32 consecutive 32-bit columns of this warp's 32 lanes.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+// 16 consecutive 32-bit columns of this warp's 32 lanes, and the wait for
+// them (the registers tied to it, so no use is scheduled before it).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,"
-        "%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr)
         : "memory");
 }
-
-// Wait for this thread's tensor-memory loads; the loaded registers are
-// tied to the wait so no use of them is scheduled before it.
-__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
+__device__ __forceinline__ void tmem_ld_wait16(uint32_t (&r)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;\n"
                  : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
-                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
-                   "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
-                   "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
+}
+
+// 8 consecutive 32-bit columns of this warp's 32 lanes.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr)
+                 : "memory");
+}
+
+// Wait for this thread's tensor-memory loads, the four 8-column reads of a
+// decode group tied to it.
+__device__ __forceinline__ void tmem_ld_wait4x8(uint32_t (&r)[4][8]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+                 : "+r"(r[0][0]), "+r"(r[0][1]), "+r"(r[0][2]), "+r"(r[0][3]), "+r"(r[0][4]), "+r"(r[0][5]), "+r"(r[0][6]),
+                   "+r"(r[0][7]), "+r"(r[1][0]), "+r"(r[1][1]), "+r"(r[1][2]), "+r"(r[1][3]), "+r"(r[1][4]), "+r"(r[1][5]),
+                   "+r"(r[1][6]), "+r"(r[1][7]), "+r"(r[2][0]), "+r"(r[2][1]), "+r"(r[2][2]), "+r"(r[2][3]), "+r"(r[2][4]),
+                   "+r"(r[2][5]), "+r"(r[2][6]), "+r"(r[2][7]), "+r"(r[3][0]), "+r"(r[3][1]), "+r"(r[3][2]), "+r"(r[3][3]),
+                   "+r"(r[3][4]), "+r"(r[3][5]), "+r"(r[3][6]), "+r"(r[3][7])
                  :
                  : "memory");
 }
@@ -226,49 +270,52 @@ __device__ __forceinline__ void pdl_launch_tc() { asm volatile("griddepcontrol.l
 
 // ------------------------------------------------------------------ kernel
 
-// REM: some token rows are remainder rows (T % 4 != 0). BULK: the output
-// tile leaves by a TMA store through map_y (y + col0 as [M][W.out] f32 rows
-// ldy apart); else by plain stores.
-template <bool REM, bool BULK>
+// DEC: the decode combine (one-token rows) instead of the prefill combine.
+// REM (prefill only): some token rows are remainder rows (T % 4 != 0).
+// BULK: the output tile leaves by a TMA store through map_y (y + col0 as
+// [M][W.out] f32 rows ldy apart); else by plain stores.
+template <bool DEC, bool REM, bool BULK>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-    cq_tc_prefill_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a,
-                         const __grid_constant__ CUtensorMap map_y, DevMat W, const float* __restrict__ sx, int M, int T,
-                         float* __restrict__ y, int ldy, int col0, int* err) {
+    cq_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a,
+                 const __grid_constant__ CUtensorMap map_y, DevMat W, const float* __restrict__ sx, int M, int T,
+                 float* __restrict__ y, int ldy, int col0, int* err) {
+    using C = TcCfg<DEC>;
+    constexpr int TOK = C::TOK, STAGES = C::STAGES, CPT = C::CPT, BUFS = C::BUFS;
     pdl_launch_tc();
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t wtile = (raw + 1023u) & ~1023u;  // 1024-aligned for the 128-byte swizzle
     const uint32_t ring = wtile + TC_W_BYTES;
     uint8_t* gring = smem_raw + (ring - raw);
-    float* stage_out = (float*)(gring + TC_STAGES * TC_STAGE_BYTES);  // [128 tokens][128 rows]
-    float* colv = stage_out + TC_TOK * TC_ROWS;                       // [2][6][128]
-    int* remf = (int*)(colv + 2 * 6 * TC_TOK);                   // [2][128]
+    float* stage_out = (float*)(gring + STAGES * C::STAGE_BYTES);  // [TOK / OUT_HALVES tokens][128 rows]
+    float* colv = stage_out + TOK / C::OUT_HALVES * TC_ROWS;         // [2][6][TOK]
+    int* remf = (int*)(colv + 2 * 6 * TOK);                         // [2][TOK]
     // full[STAGES] empty[STAGES] tfull[BUFS] tempty[BUFS] cfull[2] cempty[2] wfull wempty
-    uint64_t* bars = (uint64_t*)(remf + 2 * TC_TOK);
-    uint32_t* tmem_slot = (uint32_t*)(bars + TC_NBARS);
+    uint64_t* bars = (uint64_t*)(remf + 2 * TOK);
+    uint32_t* tmem_slot = (uint32_t*)(bars + C::NBARS);
     volatile int* abort = (volatile int*)(tmem_slot + 1);
     const uint32_t bar0 = smem_u32(bars);
     auto full = [&](int s) { return bar0 + 8u * s; };
-    auto empty = [&](int s) { return bar0 + 8u * (TC_STAGES + s); };
-    auto tfull = [&](int b) { return bar0 + 8u * (2 * TC_STAGES + b); };
-    auto tempty = [&](int b) { return bar0 + 8u * (2 * TC_STAGES + TC_BUFS + b); };
-    auto cfull = [&](int t) { return bar0 + 8u * (2 * TC_STAGES + 2 * TC_BUFS + t); };
-    auto cempty = [&](int t) { return bar0 + 8u * (2 * TC_STAGES + 2 * TC_BUFS + 2 + t); };
-    const uint32_t wfull = bar0 + 8u * (2 * TC_STAGES + 2 * TC_BUFS + 4), wempty = wfull + 8u;
+    auto empty = [&](int s) { return bar0 + 8u * (STAGES + s); };
+    auto tfull = [&](int b) { return bar0 + 8u * (2 * STAGES + b); };
+    auto tempty = [&](int b) { return bar0 + 8u * (2 * STAGES + BUFS + b); };
+    auto cfull = [&](int t) { return bar0 + 8u * (2 * STAGES + 2 * BUFS + t); };
+    auto cempty = [&](int t) { return bar0 + 8u * (2 * STAGES + 2 * BUFS + 2 + t); };
+    const uint32_t wfull = bar0 + 8u * (2 * STAGES + 2 * BUFS + 4), wempty = wfull + 8u;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tilesN = (W.out + TC_ROWS - 1) / TC_ROWS, tilesM = (M + TC_TOK - 1) / TC_TOK;
+    const int tilesN = (W.out + TC_ROWS - 1) / TC_ROWS, tilesM = (M + TOK - 1) / TOK;
     const int ntiles = tilesN * tilesM;
     // this CTA's run of tiles t0 .. t1 - 1; tile t is weight tile t / tilesM,
     // token tile t % tilesM
     const int t0 = (int)((long long)blockIdx.x * ntiles / gridDim.x), t1 = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < TC_STAGES; s++) {
+        for (int s = 0; s < STAGES; s++) {
             mbar_init(full(s), 1);
             mbar_init(empty(s), 1);
         }
-        for (int b = 0; b < TC_BUFS; b++) {
+        for (int b = 0; b < BUFS; b++) {
             mbar_init(tfull(b), 1);
             mbar_init(tempty(b), TC_EPI_WARPS);
         }
@@ -286,7 +333,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
-                     "r"(TC_BUFS * TC_TOK)
+                     "r"(512)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
     }
@@ -294,85 +341,93 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+
     if (warp == 0) {
-        // ---- TMA producer: lane 0 waits and issues, the warp stays converged
-        int G = 0, wk = 0, cur_n = -1;  // activation groups, weight tiles loaded
+        // ---- TMA producer: lane 0 waits and issues, the warp stays converged;
+        // one 3-D box a weight tile, one a tile's activations
+        int it = 0, wk = 0, cur_n = -1;  // tiles, weight tiles loaded
         bool ok = true, waited = false;
-        for (int t = t0; t < t1 && ok; t++) {
-            const int nt = t / tilesM, m0 = (t % tilesM) * TC_TOK;
+        for (int t = t0; t < t1 && ok; t++, it++) {
+            const int nt = t / tilesM, m0 = (t % tilesM) * TOK, s = it % STAGES;
             int good = 1;
-            if (nt != cur_n) {
-                // the weight tile, all six groups; the previous one must be
-                // done with (its last MMAs committed to wempty)
-                if (lane == 0) {
+            if (lane == 0) {
+                if (nt != cur_n) {
+                    // the previous weight tile must be done with (its last
+                    // MMAs committed to wempty)
                     if (wk > 0) good = mbar_wait(wempty, (wk - 1) & 1, abort, err, 9);
                     if (good) {
                         mbar_expect_tx(wfull, TC_W_BYTES);
-                        for (int g = 0; g < 6; g++) tma_load_2d(wtile + g * TC_TILE_BYTES, &map_w, g * 128, nt * TC_ROWS, wfull);
+                        tma_load_3d(wtile, &map_w, nt * TC_ROWS, wfull);
                     }
                 }
-                ok = __shfl_sync(0xffffffffu, good, 0) != 0;
-                if (!ok) break;
+                if (good && it >= STAGES) good = mbar_wait(empty(s), ((it / STAGES) - 1) & 1, abort, err, 1);
+                if (good) {
+                    // the activations are the predecessor kernel's output
+                    if (!waited) pdl_wait_tc();
+                    mbar_expect_tx(full(s), C::STAGE_BYTES);
+                    tma_load_3d(ring + s * C::STAGE_BYTES, &map_a, m0, full(s));
+                }
+            }
+            waited = true;
+            if (nt != cur_n) {
                 cur_n = nt;
                 wk++;
             }
-            for (int g = 0; g < 6; g++, G++) {
-                const int s = G % TC_STAGES;
-                good = 1;
-                if (lane == 0) {
-                    if (G >= TC_STAGES) good = mbar_wait(empty(s), ((G / TC_STAGES) - 1) & 1, abort, err, 1);
-                    if (good) {
-                        // the activations are the predecessor kernel's output
-                        if (!waited) pdl_wait_tc();
-                        mbar_expect_tx(full(s), TC_STAGE_BYTES);
-                        tma_load_2d(ring + s * TC_STAGE_BYTES, &map_a, g * 128, m0, full(s));
-                    }
-                }
-                waited = true;
-                ok = __shfl_sync(0xffffffffu, good, 0) != 0;
-                if (!ok) break;
-            }
+            ok = __shfl_sync(0xffffffffu, good, 0) != 0;
         }
         if (lane == 0) {
             if (!waited) pdl_wait_tc();
             // drain: every load issued has landed before the CTA may exit
-            for (int k = 0; k < TC_STAGES && k < G; k++) {
-                const int Gk = G - 1 - k, s = Gk % TC_STAGES;
-                mbar_wait(full(s), (Gk / TC_STAGES) & 1, abort, err, 5);
+            for (int k = 0; k < STAGES && k < it; k++) {
+                const int ik = it - 1 - k;
+                mbar_wait(full(ik % STAGES), (ik / STAGES) & 1, abort, err, 5);
             }
             if (wk > 0) mbar_wait(wfull, (wk - 1) & 1, abort, err, 5);
         }
         __syncwarp();
     } else if (warp == 1) {
         // ---- MMA issuer: lane 0 waits and issues, the warp stays converged
-        int G = 0, wk = 0, cur_n = -1;
+        int P = 0, it = 0, wk = 0, cur_n = -1;  // group pairs, tiles, weight tiles
         bool ok = true;
-        for (int t = t0; t < t1 && ok; t++) {
-            const int nt = t / tilesM;
+        for (int t = t0; t < t1 && ok; t++, it++) {
+            const int nt = t / tilesM, s = it % STAGES;
             const bool last_of_w = t + 1 == t1 || (t + 1) / tilesM != nt;
             int good = 1;
+            if (lane == 0) {
+                if (nt != cur_n) good = mbar_wait(wfull, wk & 1, abort, err, 10);
+                if (good) good = mbar_wait(full(s), (it / STAGES) & 1, abort, err, 2);
+            }
             if (nt != cur_n) {
-                if (lane == 0) good = mbar_wait(wfull, wk & 1, abort, err, 10);
-                ok = __shfl_sync(0xffffffffu, good, 0) != 0;
-                if (!ok) break;
                 cur_n = nt;
                 wk++;
             }
-            for (int g = 0; g < 6; g++, G++) {
-                const int s = G % TC_STAGES, b = G % TC_BUFS;
+            ok = __shfl_sync(0xffffffffu, good, 0) != 0;
+            if (!ok) break;
+            for (int pr = 0; pr < 3; pr++, P++) {
+                const int sl = P % C::SLOTS;
                 good = 1;
                 if (lane == 0) {
-                    good = mbar_wait(full(s), (G / TC_STAGES) & 1, abort, err, 2);
-                    if (good && G >= TC_BUFS) good = mbar_wait(tempty(b), ((G / TC_BUFS) - 1) & 1, abort, err, 3);
+                    if (P >= C::SLOTS) good = mbar_wait(tempty(sl), ((P / C::SLOTS) - 1) & 1, abort, err, 3);
                     if (good) {
                         tc_fence_after();
-                        const uint32_t wa = wtile + g * TC_TILE_BYTES, aa = ring + s * TC_STAGE_BYTES;
-                        const uint32_t d = tmem + (uint32_t)(b * TC_TOK);
 #pragma unroll
-                        for (int kk = 0; kk < 4; kk++) mma_i8(d, sw128_desc(wa + 32 * kk), sw128_desc(aa + 32 * kk), kk);
-                        mma_commit(empty(s));  // the stage is free once these MMAs have read it
-                        mma_commit(tfull(b));  // the group's sums are in buffer b
-                        if (g == 5 && last_of_w) mma_commit(wempty);  // the weight tile is done with
+                        for (int h = 0; h < 2; h++) {
+                            const int g = 2 * pr + h;
+                            const uint32_t wa = wtile + g * TC_TILE_BYTES, aa = ring + s * C::STAGE_BYTES + g * C::GRP_BYTES;
+                            const uint32_t d = tmem + (uint32_t)((2 * sl + h) * C::GROUP_COLS);
+                            // K slice kk = decode lane kk of the group: the prefill
+                            // combine sums the four into one accumulator, the decode
+                            // combine keeps each in its own (TOK columns apart)
+#pragma unroll
+                            for (int kk = 0; kk < 4; kk++)
+                                mma_i8(d + (uint32_t)(kk * C::SLICE), sw128_desc(wa + 32 * kk), sw128_desc(aa + 32 * kk), C::IDESC,
+                                       DEC ? 0u : (uint32_t)kk);
+                        }
+                        mma_commit(tfull(sl));  // the two groups' sums are in slot sl
+                        if (pr == 2) {
+                            mma_commit(empty(s));                 // the tile's activations are read
+                            if (last_of_w) mma_commit(wempty);    // the weight tile is done with
+                        }
                     }
                 }
                 ok = __shfl_sync(0xffffffffu, good, 0) != 0;
@@ -380,60 +435,62 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
         }
         // every MMA issued has completed before the memory is freed
-        if (lane == 0 && G > 0) {
-            const int Gl = G - 1;
-            mbar_wait(tfull(Gl % TC_BUFS), (Gl / TC_BUFS) & 1, abort, err, 6);
+        if (lane == 0 && P > 0) {
+            const int Pl = P - 1;
+            mbar_wait(tfull(Pl % C::SLOTS), (Pl / C::SLOTS) & 1, abort, err, 6);
         }
         __syncwarp();
     } else if (warp == TC_SCALE_WARP) {
-        // ---- column factors, a tile ahead: sx of each token and group for
-        // block rows, cbs * sx for remainder rows (0 past M), and the
-        // remainder flags, into buffer (tile count) % 2
+        // ---- column factors, a tile ahead, into buffer (tile count) % 2:
+        // prefill, sx of each token and group for block rows and cbs * sx
+        // for remainder rows (with the remainder flags); decode, sx * cbs
+        // (0 past M)
         pdl_wait_tc();
         const float cbs = W.cbs;
         const int blocked = T / 4 * 4;
         int it = 0;
         bool ok = true;
         for (int tile = t0; tile < t1 && ok; tile++, it++) {
-            const int m0 = (tile % tilesM) * TC_TOK, tb = it & 1;
+            const int m0 = (tile % tilesM) * TOK, tb = it & 1;
             int good = 1;
             if (lane == 0 && it >= 2) good = mbar_wait(cempty(tb), ((it >> 1) - 1) & 1, abort, err, 7);
             ok = __shfl_sync(0xffffffffu, good, 0) != 0;
             if (!ok) break;
-            float v[24];
+            constexpr int PER = 6 * TOK / 32;  // factors a lane
+            float v[PER];
 #pragma unroll
-            for (int k = 0; k < 24; k++) {
-                const int i = lane + 32 * k, j = i / 6, g = i % 6, m = m0 + j;  // sx is [M][6]: contiguous per tile
+            for (int k = 0; k < PER; k++) {
+                const int i = lane + 32 * k, m = m0 + i / 6;  // sx is [M][6]: contiguous per tile
                 v[k] = m < M ? __ldg(sx + (size_t)m0 * 6 + i) : 0.f;
-                if ((m % T) >= blocked) v[k] = __fmul_rn(cbs, v[k]);
-                (void)g;
+                if (DEC) v[k] = __fmul_rn(v[k], cbs);
+                else if ((m % T) >= blocked) v[k] = __fmul_rn(cbs, v[k]);
             }
-            float* cv = colv + tb * 6 * TC_TOK;
+            float* cv = colv + tb * 6 * TOK;
 #pragma unroll
-            for (int k = 0; k < 24; k++) {
+            for (int k = 0; k < PER; k++) {
                 const int i = lane + 32 * k, j = i / 6, g = i % 6;
-                cv[g * TC_TOK + j] = v[k];
+                cv[g * TOK + j] = v[k];
             }
             if (REM)
 #pragma unroll
-                for (int k = 0; k < 4; k++) {
+                for (int k = 0; k < TOK / 32; k++) {
                     const int j = lane + 32 * k;
-                    remf[tb * TC_TOK + j] = ((m0 + j) % T) >= blocked;
+                    remf[tb * TOK + j] = ((m0 + j) % T) >= blocked;
                 }
             __syncwarp();
             if (lane == 0) mbar_arrive(cfull(tb));
         }
     } else {
         // ---- epilogue: warps 2-17; warp w reads lanes 32 (w % 4) .. + 31 (its
-        // weight rows) and the column quarter c of the 128 tokens
+        // weight rows) and the column quarter c of the tile's tokens
         pdl_wait_tc();
         const int e = warp - 2, q = warp & 3, c = e >> 2;
         const bool leader = e == 0 && lane == 0;  // issues the tile's bulk store
         const float cbs = W.cbs;
-        int G = 0, it = 0;
+        int P = 0, it = 0;  // group pairs, tiles
         bool ok = true;
-        // the row factors of this thread's weight row for the first tile; each
-        // tile then loads the next tile's
+        // the norms of this thread's weight row for the first tile; each tile
+        // then loads the next tile's
         float nrm[6];
         {
             const int n = (t0 / tilesM) * TC_ROWS + q * 32 + lane;
@@ -441,9 +498,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int g = 0; g < 6; g++) nrm[g] = (t0 < t1 && n < W.out) ? h2f(__ldg(W.norms + (size_t)n * 6 + g)) : 0.f;
         }
         for (int tile = t0; tile < t1; tile++, it++) {
-            const int n0 = (tile / tilesM) * TC_ROWS, m0 = (tile % tilesM) * TC_TOK, tb = it & 1;
+            const int n0 = (tile / tilesM) * TC_ROWS, m0 = (tile % tilesM) * TOK, tb = it & 1;
             const int n = n0 + q * 32 + lane;  // this thread's weight row
-            float nc[6];  // norm * cbs (block rows); remainder rows use norm alone
+            float nc[6];  // prefill: norm * cbs (block rows); remainder rows use norm alone
 #pragma unroll
             for (int g = 0; g < 6; g++) nc[g] = __fmul_rn(nrm[g], cbs);
             float nrm_next[6];
@@ -455,69 +512,127 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             int good = 1;
             if (lane == 0 && ok) good = mbar_wait(cfull(tb), (it >> 1) & 1, abort, err, 8);
             ok = ok && __shfl_sync(0xffffffffu, good, 0) != 0;
-            const float* cvt = colv + tb * 6 * TC_TOK + c * 32;
-            const int* rf = remf + tb * TC_TOK + c * 32;
-            float2 acc[16];
+            const float* cvt = colv + tb * 6 * TOK + c * CPT;
+            const int* rf = remf + tb * TOK + c * CPT;
+            const float2 mg = make_float2(12582912.0f, 12582912.0f);
+            // prefill: acc[j] = the chain of tokens 2j, 2j + 1; decode: lanes[l][j]
+            float2 acc[DEC ? 4 : 1][CPT / 2];
 #pragma unroll
-            for (int j = 0; j < 16; j++) acc[j] = make_float2(0.f, 0.f);
-            for (int g = 0; g < 6; g++, G++) {
-                const int b = G % TC_BUFS;
-                good = 1;
-                if (lane == 0 && ok) good = mbar_wait(tfull(b), (G / TC_BUFS) & 1, abort, err, 4);
-                ok = ok && __shfl_sync(0xffffffffu, good, 0) != 0;
-                tc_fence_after();
-                uint32_t r[32];
-                if (ok) {
-                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * TC_TOK + c * 32), r);
-                    tmem_ld_wait(r);
-                } else {
+            for (int l = 0; l < (DEC ? 4 : 1); l++)
 #pragma unroll
-                    for (int j = 0; j < 32; j++) r[j] = 0u;
+                for (int j = 0; j < CPT / 2; j++) acc[l][j] = make_float2(0.f, 0.f);
+            for (int g = 0; g < 6; g++) {
+                const int h = g & 1, sl = P % C::SLOTS, b = 2 * sl + h;
+                if (h == 0) {
+                    good = 1;
+                    if (lane == 0 && ok) good = mbar_wait(tfull(sl), (P / C::SLOTS) & 1, abort, err, 4);
+                    ok = ok && __shfl_sync(0xffffffffu, good, 0) != 0;
+                    tc_fence_after();
                 }
-                // the sums are in registers: the buffer is free
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(tempty(b));
-                const float* cv = cvt + g * TC_TOK;
-                const float2 mg = make_float2(12582912.0f, 12582912.0f);
-#pragma unroll
-                for (int j = 0; j < 16; j++) {  // token pair (2j, 2j + 1) of this quarter
-                    const float2 s2 = tc_sub2(make_float2(__uint_as_float(r[2 * j] + TC_MAGIC), __uint_as_float(r[2 * j + 1] + TC_MAGIC)), mg);
-                    const float2 c2 = *(const float2*)(cv + 2 * j);
-                    float2 f2 = make_float2(nc[g], nc[g]);
-                    if (REM) {
-                        if (rf[2 * j]) f2.x = nrm[g];
-                        if (rf[2 * j + 1]) f2.y = nrm[g];
+                const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * C::GROUP_COLS + c * CPT);
+                const float* cv = cvt + g * TOK;
+                // after the pair's second group is in registers, the slot is free
+                auto release = [&]() {
+                    if (h == 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(tempty(sl));
+                        P++;
                     }
-                    acc[j] = tc_fma2(s2, tc_mul2(f2, c2), acc[j]);
+                };
+                if constexpr (DEC) {
+                    uint32_t r[4][8];
+                    if (ok) {
+#pragma unroll
+                        for (int l = 0; l < 4; l++) tmem_ld8(ta + (uint32_t)(l * C::SLICE), r[l]);
+                        tmem_ld_wait4x8(r);
+                    } else {
+#pragma unroll
+                        for (int l = 0; l < 4; l++)
+#pragma unroll
+                            for (int j = 0; j < 8; j++) r[l][j] = 0u;
+                    }
+                    release();
+                    const float2 nn = make_float2(nrm[g], nrm[g]);
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {  // token pair (2j, 2j + 1)
+                        // sc = (sx * cbs) * norm, shared by the four lanes
+                        const float2 sc = tc_mul2(*(const float2*)(cv + 2 * j), nn);
+#pragma unroll
+                        for (int l = 0; l < 4; l++) {
+                            const float2 s2 = tc_sub2(make_float2(__uint_as_float(r[l][2 * j] + TC_MAGIC),
+                                                                  __uint_as_float(r[l][2 * j + 1] + TC_MAGIC)), mg);
+                            acc[l][j] = tc_fma2(s2, sc, acc[l][j]);
+                        }
+                    }
+                } else {
+                    uint32_t r[CPT];
+                    if (ok) {
+                        tmem_ld16(ta, r);
+                        tmem_ld_wait16(r);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < CPT; j++) r[j] = 0u;
+                    }
+                    release();
+#pragma unroll
+                    for (int j = 0; j < CPT / 2; j++) {  // token pair (2j, 2j + 1) of this quarter
+                        const float2 s2 = tc_sub2(make_float2(__uint_as_float(r[2 * j] + TC_MAGIC), __uint_as_float(r[2 * j + 1] + TC_MAGIC)), mg);
+                        const float2 c2 = *(const float2*)(cv + 2 * j);
+                        float2 f2 = make_float2(nc[g], nc[g]);
+                        if (REM) {
+                            if (rf[2 * j]) f2.x = nrm[g];
+                            if (rf[2 * j + 1]) f2.y = nrm[g];
+                        }
+                        acc[0][j] = tc_fma2(s2, tc_mul2(f2, c2), acc[0][j]);
+                    }
                 }
             }
             // the column factors of this tile are read: free the buffer
             __syncwarp();
             if (lane == 0) mbar_arrive(cempty(tb));
-            if (BULK) {
-                // stage the tile [token][row] and let one thread store it; the
-                // previous tile's store must have read the staging first
-                if (leader) bulk_wait_read();
-                epi_sync();
-                float* so = stage_out + (c * 32) * TC_ROWS + q * 32 + lane;
+            // the outputs of tokens 2j, 2j + 1: prefill, the chain; decode,
+            // (l0 + l1) + (l2 + l3)
+            float2 out[CPT / 2];
 #pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    so[(2 * j) * TC_ROWS] = acc[j].x;
-                    so[(2 * j + 1) * TC_ROWS] = acc[j].y;
+            for (int j = 0; j < CPT / 2; j++) {
+                if constexpr (DEC) {
+                    out[j].x = __fadd_rn(__fadd_rn(acc[0][j].x, acc[1][j].x), __fadd_rn(acc[2][j].x, acc[3][j].x));
+                    out[j].y = __fadd_rn(__fadd_rn(acc[0][j].y, acc[1][j].y), __fadd_rn(acc[2][j].y, acc[3][j].y));
+                } else {
+                    out[j] = acc[0][j];
                 }
-                fence_async_smem();
-                epi_sync();
-                if (leader && ok) {
-                    tma_store_2d(&map_y, smem_u32(stage_out), n0, m0);
-                    bulk_commit();
+            }
+            if (BULK) {
+                // stage the tile [token][row] (in OUT_HALVES rounds of token
+                // quarters) and let one thread store each round; the previous
+                // store must have read the staging first
+                constexpr int QPH = 4 / C::OUT_HALVES;  // column quarters a round
+#pragma unroll 1
+                for (int hh = 0; hh < C::OUT_HALVES; hh++) {
+                    if (leader) bulk_wait_read();
+                    epi_sync();
+                    if (c / QPH == hh) {
+                        float* so = stage_out + ((c % QPH) * CPT) * TC_ROWS + q * 32 + lane;
+#pragma unroll
+                        for (int j = 0; j < CPT / 2; j++) {
+                            so[(2 * j) * TC_ROWS] = out[j].x;
+                            so[(2 * j + 1) * TC_ROWS] = out[j].y;
+                        }
+                        fence_async_smem();
+                    }
+                    epi_sync();
+                    if (leader && ok) {
+                        tma_store_2d(&map_y, smem_u32(stage_out), n0, m0 + hh * (TOK / C::OUT_HALVES));
+                        bulk_commit();
+                    }
                 }
             } else if (ok && n < W.out) {
 #pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    const int m = m0 + c * 32 + 2 * j;
-                    if (m < M) y[(size_t)m * ldy + col0 + n] = acc[j].x;
-                    if (m + 1 < M) y[(size_t)(m + 1) * ldy + col0 + n] = acc[j].y;
+                for (int j = 0; j < CPT / 2; j++) {
+                    const int m = m0 + c * CPT + 2 * j;
+                    if (m < M) y[(size_t)m * ldy + col0 + n] = out[j].x;
+                    if (m + 1 < M) y[(size_t)(m + 1) * ldy + col0 + n] = out[j].y;
                 }
             }
 #pragma unroll
@@ -529,7 +644,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(TC_BUFS * TC_TOK) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(512) : "memory");
     }
 }
 
@@ -552,30 +667,33 @@ static EncodeTiled encode_fn() {
     return fn;
 }
 
-// The tensor map of an int8 [rows][768] matrix read in boxes of 128 bytes x
-// 128 rows with the 128-byte swizzle; rows past the end read as zeros.
-static bool int8_rows_map(CUtensorMap* map, const void* base, int rows) {
+// The tensor map of an int8 [rows][768] matrix as 3-D boxes {128 bytes,
+// box_rows rows, 6 groups} with the 128-byte swizzle: the groups (128 bytes
+// apart in memory) are the outermost box dimension, so a box lands as six
+// [box_rows][128 bytes] tiles, one per group. Rows past the end read as
+// zeros.
+static bool int8_rows_map(CUtensorMap* map, const void* base, int rows, int box_rows) {
     EncodeTiled enc = encode_fn();
     if (!enc || ((uintptr_t)base & 15) || rows < 1) return false;
-    const cuuint64_t dims[2] = {768, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {768};
-    const cuuint32_t box[2] = {128, 128};
-    const cuuint32_t estr[2] = {1, 1};
-    return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+    const cuuint64_t dims[3] = {128, (cuuint64_t)rows, 6};
+    const cuuint64_t strides[2] = {768, 128};
+    const cuuint32_t box[3] = {128, (cuuint32_t)box_rows, 6};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // The tensor map of y + col0 as [M][out] f32 rows `ldy` floats apart, stored
-// in boxes of 128 rows x 128 tokens; false when the rows are not 16-byte
-// aligned (the kernel then stores without TMA).
-static bool f32_out_map(CUtensorMap* map, float* y, int col0, int out, int M, int ldy) {
+// in boxes of 128 rows x box_tok tokens; false when the rows are not
+// 16-byte aligned (the kernel then stores without TMA).
+static bool f32_out_map(CUtensorMap* map, float* y, int col0, int out, int M, int ldy, int box_tok) {
     EncodeTiled enc = encode_fn();
     const float* base = y + col0;
     if (!enc || ((uintptr_t)base & 15) || ((size_t)ldy * 4) % 16 || out < 1 || M < 1) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)out, (cuuint64_t)M};
     const cuuint64_t strides[1] = {(cuuint64_t)ldy * 4};
-    const cuuint32_t box[2] = {TC_ROWS, TC_TOK};
+    const cuuint32_t box[2] = {TC_ROWS, (cuuint32_t)box_tok};
     const cuuint32_t estr[2] = {1, 1};
     return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -626,41 +744,63 @@ int tc_prefill_error() {
 
 cudaError_t tc_prefill_init() {
     cudaError_t e = cudaSuccess;
-    auto set = [&](const void* f) {
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM);
+    auto set = [&](const void* f, size_t smem) {
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     };
-    set((const void*)cq_tc_prefill_kernel<false, false>);
-    set((const void*)cq_tc_prefill_kernel<false, true>);
-    set((const void*)cq_tc_prefill_kernel<true, false>);
-    set((const void*)cq_tc_prefill_kernel<true, true>);
+    set((const void*)cq_tc_kernel<false, false, false>, TcCfg<false>::SMEM);
+    set((const void*)cq_tc_kernel<false, false, true>, TcCfg<false>::SMEM);
+    set((const void*)cq_tc_kernel<false, true, false>, TcCfg<false>::SMEM);
+    set((const void*)cq_tc_kernel<false, true, true>, TcCfg<false>::SMEM);
+    set((const void*)cq_tc_kernel<true, false, false>, TcCfg<true>::SMEM);
+    set((const void*)cq_tc_kernel<true, false, true>, TcCfg<true>::SMEM);
+    // the error word's address, looked up now (before any stream capture)
+    if (e == cudaSuccess && !tc_err_ptr()) e = cudaErrorInvalidSymbol;
     return e;
 }
 
-cudaError_t launch_cq_prefill_tc(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y, int ldy, int col0,
-                                 cudaStream_t st) {
+template <bool DEC>
+static cudaError_t launch_tc(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y, int ldy, int col0,
+                             cudaStream_t st) {
+    using C = TcCfg<DEC>;
     int* err = tc_err_ptr();
-    if (!W.w8 || W.in_dim != 768 || W.groups != 6 || M < 1 || T < 2 || !err) return cudaErrorInvalidValue;
+    if (!W.w8 || W.in_dim != 768 || W.groups != 6 || M < 1 || !err) return cudaErrorInvalidValue;
     CUtensorMap mw, ma, my;
-    if (!int8_rows_map(&mw, W.w8, W.out) || !int8_rows_map(&ma, act, M)) return cudaErrorInvalidValue;
-    const bool bulk = f32_out_map(&my, y, col0, W.out, M, ldy);
+    if (!int8_rows_map(&mw, W.w8, W.out, TC_ROWS) || !int8_rows_map(&ma, act, M, C::TOK)) return cudaErrorInvalidValue;
+    const bool bulk = f32_out_map(&my, y, col0, W.out, M, ldy, C::TOK / C::OUT_HALVES);
     if (!bulk) my = mw;  // unused by the plain-store variant
-    const int ntiles = ((W.out + TC_ROWS - 1) / TC_ROWS) * ((M + TC_TOK - 1) / TC_TOK);
+    const int ntiles = ((W.out + TC_ROWS - 1) / TC_ROWS) * ((M + C::TOK - 1) / C::TOK);
     const int grid = std::min(ntiles, sm_count_tc());
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(TC_THREADS);
-    cfg.dynamicSmemBytes = TC_SMEM;
+    cfg.dynamicSmemBytes = C::SMEM;
     cfg.stream = st;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = st ? 1 : 0;
+    if (DEC) {
+        if (bulk) return cudaLaunchKernelEx(&cfg, cq_tc_kernel<true, false, true>, mw, ma, my, W, sx, M, T, y, ldy, col0, err);
+        return cudaLaunchKernelEx(&cfg, cq_tc_kernel<true, false, false>, mw, ma, my, W, sx, M, T, y, ldy, col0, err);
+    }
     const bool rem = T % 4 != 0;
-    if (rem && bulk) return cudaLaunchKernelEx(&cfg, cq_tc_prefill_kernel<true, true>, mw, ma, my, W, sx, M, T, y, ldy, col0, err);
-    if (rem) return cudaLaunchKernelEx(&cfg, cq_tc_prefill_kernel<true, false>, mw, ma, my, W, sx, M, T, y, ldy, col0, err);
-    if (bulk) return cudaLaunchKernelEx(&cfg, cq_tc_prefill_kernel<false, true>, mw, ma, my, W, sx, M, T, y, ldy, col0, err);
-    return cudaLaunchKernelEx(&cfg, cq_tc_prefill_kernel<false, false>, mw, ma, my, W, sx, M, T, y, ldy, col0, err);
+    if (rem && bulk) return cudaLaunchKernelEx(&cfg, cq_tc_kernel<false, true, true>, mw, ma, my, W, sx, M, T, y, ldy, col0, err);
+    if (rem) return cudaLaunchKernelEx(&cfg, cq_tc_kernel<false, true, false>, mw, ma, my, W, sx, M, T, y, ldy, col0, err);
+    if (bulk) return cudaLaunchKernelEx(&cfg, cq_tc_kernel<false, false, true>, mw, ma, my, W, sx, M, T, y, ldy, col0, err);
+    return cudaLaunchKernelEx(&cfg, cq_tc_kernel<false, false, false>, mw, ma, my, W, sx, M, T, y, ldy, col0, err);
+}
+
+cudaError_t launch_cq_prefill_tc(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y, int ldy, int col0,
+                                 cudaStream_t st) {
+    if (T < 2) return cudaErrorInvalidValue;
+    return launch_tc<false>(W, act, sx, M, T, y, ldy, col0, st);
+}
+
+cudaError_t launch_cq_decode_tc(DevMat W, const int8_t* act, const float* sx, int M, float* y, int ldy, int col0,
+                                cudaStream_t st) {
+    if (W.width == 2) return cudaErrorInvalidValue;  // the 2-bit lane rule splits a lane's 32 bytes
+    return launch_tc<true>(W, act, sx, M, 1, y, ldy, col0, st);
 }
 
 }  // namespace nd
