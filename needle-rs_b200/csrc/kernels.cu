@@ -608,12 +608,10 @@ cudaError_t launch_cq_gemm(DevMat W, const int8_t* act, const float* sx, int M, 
 
 
 extern const size_t ATT_SMEM;
-extern const size_t POST_SMEM;
 extern const size_t POST_ROW_SMEM;
 __global__ void post_row_kernel(LayerW w, const float* o, const float* x1, const float* u, const float* gates, const int32_t* perm1,
                                 const int32_t* perm2, float* xs);
-__global__ void post_block_kernel(LayerW w, const float* o, const float* x1, const float* u, const float* gates,
-                                  const int32_t* perm1, const int32_t* perm2, int M, float* xs);
+cudaError_t post_block_init();
 __global__ void attention_kernel(const float* qbuf, const float* proj, Caches c, int l, int T, const int32_t* p0p, int window,
                                  int sink, int ring, float* att, int8_t* act, float* sx);
 
@@ -876,8 +874,8 @@ __global__ void __launch_bounds__(MHC_THREADS, 8) mhc_read_kernel(LayerW w, int 
     float* na = xt;
     float* nb = xt + 768;
     if (ekv) {
-        if (lt < 16) part[lt] = dot16_chain(x1, x1, 768, lt);
-        else if (lt < 32) part[lt] = dot16_chain(ek, ek, 768, lt - 16);
+        if (lt < 16) part[lt] = dot16_sq<768>(x1, lt);
+        else if (lt < 32) part[lt] = dot16_sq<768>(ek, lt - 16);
         norm_bar();
         if (lt == 0) sc_s[1] = rinv(dot16_combine(part), 768);
         if (lt == 1) sc_s[2] = rinv(dot16_combine(part + 16), 768);
@@ -887,7 +885,7 @@ __global__ void __launch_bounds__(MHC_THREADS, 8) mhc_read_kernel(LayerW w, int 
             nb[k] = __fmul_rn(ek[k], sc_s[2]);
         }
         norm_bar();
-        if (lt < 16) part[lt] = dot16_chain(na, nb, 768, lt);
+        if (lt < 16) part[lt] = dot16_chain<768>(na, nb, lt);
         norm_bar();
         if (lt == 0) {
             float dab = dot16_combine(part);
@@ -899,7 +897,7 @@ __global__ void __launch_bounds__(MHC_THREADS, 8) mhc_read_kernel(LayerW w, int 
         norm_bar();
     }
     if (warp == 0) {
-        float acc = ln < 16 ? dot16_chain(x1, x1, 768, ln) : 0.f;
+        float acc = ln < 16 ? dot16_sq<768>(x1, ln) : 0.f;
         float ss = dot16_combine_warp(acc, ln);
         if (ln == 0) sc_s[0] = rinv(ss, 768);
     }
@@ -1149,9 +1147,11 @@ __device__ __forceinline__ void key_chunks_dev(int n, bool nested, int* count, i
 // offset within its first group, zero outside the chunk. P.V is an int8
 // matrix product on the tensor cores (mma.sync m16n8k32, exact int32 sums,
 // so the result is the reference's integer dot whatever the order): A =
-// the three digit planes of 32 keys (8 groups), B = the same keys' value
-// bytes, which the cache's group words already hold in the fragment's
-// 4-keys-per-register order. Rows with more than one chunk keep per-chunk
+// the value bytes of 16 dimensions by 32 keys (8 groups), which the cache's
+// group words already hold in the fragment's 4-keys-per-register order,
+// B = the same keys' three digit planes. A key's score, numerator and
+// weight stay in the registers of the lane that owns it until the weights
+// go to shared memory for the digits. Rows with more than one chunk keep per-chunk
 // parts in dynamic shared memory sized for the longest key list of the
 // launch; a one-chunk row keeps its part in registers, so a launch of
 // one-chunk rows needs no parts space.
@@ -1176,6 +1176,19 @@ struct AttSmem {
     // [ATT_HEADS][count][66] floats (m, sum, o[64])
 };
 static_assert(3 * 72 <= ATT_MAXCHUNK, "the P.V scratch fits a score row");
+
+// Numerators a lane holds: key k = lane + 32 i in slot i.
+constexpr int ATT_KPL = ATT_MAXCHUNK / 32;
+// Key k's value from the lane that holds it; every lane of the warp calls
+// it, with keys of one slot (k / 32 the same in every lane).
+__device__ __forceinline__ float att_key_val(const float (&ev)[ATT_KPL], int k) {
+    const int slot = k >> 5;
+    float v = 0.f;
+#pragma unroll
+    for (int i = 0; i < ATT_KPL; i++)
+        if (i == slot) v = ev[i];
+    return __shfl_sync(0xffffffffu, v, k & 31);
+}
 
 __device__ __forceinline__ void mma_s8_acc(int (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
     asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
@@ -1254,15 +1267,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 5) attention_kernel(const float* 
         }
         asm volatile("cp.async.commit_group;\n" ::);
     };
-    issue_chunk(0);
+    // this head's query and gate rows are loaded before the chunk's copies
+    // are issued, so their latency runs under the copies' issue
     const float* g = proj + (size_t)m * 1568 + 800 + hh * 64;
     const float2 gv = *(const float2*)(g + 2 * lane);  // this lane's two dimensions
     const float g0v = gv.x, g1v = gv.y;
+    const float* qrow = qbuf + (size_t)m * 576 + hh * 48;
+    const float x0 = qrow[lane], x1 = lane < 16 ? qrow[32 + lane] : 0.f;
+    issue_chunk(0);
     float qs;
     {
         // quant_i8 of this head's query, scale folded with 1/sqrt(48) (infer.rs:1885)
-        const float* q = qbuf + (size_t)m * 576 + hh * 48;
-        float x0 = q[lane], x1 = lane < 16 ? q[32 + lane] : 0.f;
         float a = warp_max(fmaxf(fabsf(x0), fabsf(x1)));
         float sc = a > 0.f ? __fmul_rn(a, ND_K127) : 1.0f;
         float inv = __fdiv_rn(1.0f, sc);
@@ -1288,40 +1303,61 @@ __global__ void __launch_bounds__(ATT_THREADS, 5) attention_kernel(const float* 
             qr[4 * e + 2] = v.z;
             qr[4 * e + 3] = v.w;
         }
+        // this lane's keys k = lane + 32 i stay in registers (ev[i]) from
+        // the scores through the numerators, their sum and the weights
+        float ev[ATT_KPL];
         float mx = -INFINITY;
-        for (int k = lane; k < len; k += 32) {
-            const int4* kr = (const int4*)sm.k[k];
-            int dot = 0;
 #pragma unroll
-            for (int e = 0; e < 3; e++) {
-                const int4 kv = kr[e];
-                dot = __dp4a(qr[4 * e], kv.x, dot);
-                dot = __dp4a(qr[4 * e + 1], kv.y, dot);
-                dot = __dp4a(qr[4 * e + 2], kv.z, dot);
-                dot = __dp4a(qr[4 * e + 3], kv.w, dot);
+        for (int i = 0; i < ATT_KPL; i++) {
+            const int k = lane + 32 * i;
+            ev[i] = 0.f;
+            if (k < len) {
+                const int4* kr = (const int4*)sm.k[k];
+                int dot = 0;
+#pragma unroll
+                for (int e = 0; e < 3; e++) {
+                    const int4 kv = kr[e];
+                    dot = __dp4a(qr[4 * e], kv.x, dot);
+                    dot = __dp4a(qr[4 * e + 1], kv.y, dot);
+                    dot = __dp4a(qr[4 * e + 2], kv.z, dot);
+                    dot = __dp4a(qr[4 * e + 3], kv.w, dot);
+                }
+                float ksv = sm.ks[k];
+                float sv = k < blocked ? __fmul_rn(__fmul_rn(ksv, (float)dot), qs) : __fmul_rn(__fmul_rn(ksv, qs), (float)dot);
+                ev[i] = sv;
+                mx = fmaxf(mx, sv);
             }
-            float ksv = sm.ks[k];
-            float sv = k < blocked ? __fmul_rn(__fmul_rn(ksv, (float)dot), qs) : __fmul_rn(__fmul_rn(ksv, qs), (float)dot);
-            srow[k] = sv;
-            mx = fmaxf(mx, sv);
         }
         mx = warp_max(mx);
         // numerators: the inline exp on whole 4-blocks, libm exp for the rest
-        for (int k = lane; k < len; k += 32) {
-            float dlt = __fsub_rn(srow[k], mx);
-            srow[k] = k < blocked ? nexp(dlt) : lexpf(dlt);
+#pragma unroll
+        for (int i = 0; i < ATT_KPL; i++) {
+            const int k = lane + 32 * i;
+            if (k < len) {
+                float dlt = __fsub_rn(ev[i], mx);
+                ev[i] = k < blocked ? nexp(dlt) : lexpf(dlt);
+            }
         }
-        __syncwarp();
         // chunk_exp's sum order (infer.rs:2279-2317): chain j < 4 adds the
         // first halves of the 8-blocks then the trailing 4-block, chain
         // j >= 4 the second halves; t_k = a_k + b_k; ((t0 + t1) + (t2 + t3)),
-        // then the last 1-3 numerators one at a time.
+        // then the last 1-3 numerators one at a time. Chain j (lane j < 8)
+        // takes block q's element q + j from lane (q + j) % 32, slot q / 32.
+        const int n8 = len / 8 * 8;
         float a = 0.f;
-        if (lane < 8) {
-            const int n8 = len / 8 * 8;
-#pragma unroll 4
-            for (int q = 0; q < n8; q += 8) a = __fadd_rn(a, srow[q + lane]);
-            if (lane < 4 && blocked > n8) a = __fadd_rn(a, srow[n8 + lane]);
+#pragma unroll
+        for (int i = 0; i < ATT_KPL; i++) {
+            if (32 * i >= n8) break;
+            const float y1 = __shfl_down_sync(0xffffffffu, ev[i], 8), y2 = __shfl_down_sync(0xffffffffu, ev[i], 16),
+                        y3 = __shfl_down_sync(0xffffffffu, ev[i], 24);
+            a = __fadd_rn(a, ev[i]);
+            if (32 * i + 8 < n8) a = __fadd_rn(a, y1);
+            if (32 * i + 16 < n8) a = __fadd_rn(a, y2);
+            if (32 * i + 24 < n8) a = __fadd_rn(a, y3);
+        }
+        {
+            const float yt = att_key_val(ev, n8 + (lane & 3));
+            if (lane < 4 && blocked > n8) a = __fadd_rn(a, yt);
         }
         float tk = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 4));  // lanes 0-3: a_k + b_k
         float t1 = __shfl_sync(0xffffffffu, tk, 1), t2 = __shfl_sync(0xffffffffu, tk, 2), t3 = __shfl_sync(0xffffffffu, tk, 3);
@@ -1329,18 +1365,23 @@ __global__ void __launch_bounds__(ATT_THREADS, 5) attention_kernel(const float* 
         {
             int ii = blocked;
             if (len - ii >= 2) {
-                sum = __fadd_rn(__fadd_rn(srow[ii], sum), srow[ii + 1]);
+                const float r0 = att_key_val(ev, ii), r1 = att_key_val(ev, ii + 1);
+                sum = __fadd_rn(__fadd_rn(r0, sum), r1);
                 ii += 2;
             }
-            if (len - ii == 1) sum = __fadd_rn(sum, srow[ii]);
+            if (len - ii == 1) sum = __fadd_rn(sum, att_key_val(ev, ii));
         }
         sum = __shfl_sync(0xffffffffu, sum, 0);
         // weights times the value scales, their max from zero, 21-bit digits
         float wm = 0.f;
-        for (int k = lane; k < len; k += 32) {
-            float wv = __fmul_rn(srow[k], sm.vs[k]);
-            srow[k] = wv;
-            wm = fmaxf(wm, wv);
+#pragma unroll
+        for (int i = 0; i < ATT_KPL; i++) {
+            const int k = lane + 32 * i;
+            if (k < len) {
+                float wv = __fmul_rn(ev[i], sm.vs[k]);
+                srow[k] = wv;
+                wm = fmaxf(wm, wv);
+            }
         }
         wm = warp_max(wm);
         const float qw = __fdiv_rn(ND_Q21, wm);
@@ -1364,39 +1405,47 @@ __global__ void __launch_bounds__(ATT_THREADS, 5) attention_kernel(const float* 
         }
         asm volatile("cp.async.wait_group 0;\n" ::);  // value groups
         __syncthreads();
-        // P.V on the tensor cores, 8 groups (32 keys) a step: A rows 0-2 are
-        // the digit planes (lane gid < 3 loads plane gid's words of groups
-        // g0 = 8 ks + tig and g0 + 4, zero past the chunk's groups), the
-        // other rows zero; B column n is value dimension 8 nt + n. Two
-        // passes of four 8-dimension tiles.
+        // P.V on the tensor cores, 8 groups (32 keys) a step, as D = V x P:
+        // A (16 x 32) is value dimensions 16 t .. 16 t + 15 by the step's
+        // keys, which the cache's group words already hold four keys a
+        // register (lane gid, tig: dimensions 16 t + gid, + 8 of groups
+        // g0 = 8 ks + tig and g0 + 4); B (32 x 8) is the keys by the digit
+        // planes, columns 0-2 (lane gid < 3 loads plane gid's words of g0
+        // and g0 + 4, zero past the chunk's groups), the other columns zero.
+        // Four m tiles cover the 64 dimensions; every sum is exact int32.
         {
             const int gid = lane >> 2, tig = lane & 3, steps = (ng + 7) >> 3, swz = tig << 3;
             const int* dp = sm.dig[h][gid < 3 ? gid : 0];
-            // plane gid's sums of dimensions 8 nt + 2 tig, + 1 go through the
-            // score row (done with) to the lanes that own them
-            int* scr = reinterpret_cast<int*>(srow);
-#pragma unroll 1
-            for (int half = 0; half < 2; half++) {
-                int acc[4][4];
+            int acc[4][4];
 #pragma unroll
-                for (int j = 0; j < 4; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0;
-                for (int ks = 0; ks < steps; ks++) {
-                    const int g0 = 8 * ks + tig, g1 = g0 + 4;
-                    const uint32_t a[4] = {gid < 3 && g0 < ng ? (uint32_t)dp[g0] : 0u, 0u,
-                                           gid < 3 && g1 < ng ? (uint32_t)dp[g1] : 0u, 0u};
-                    const int* v0 = sm.vg[g0];
-                    const int* v1 = sm.vg[g1];
+            for (int t = 0; t < 4; t++) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0;
+            for (int ks = 0; ks < steps; ks++) {
+                const int g0 = 8 * ks + tig, g1 = g0 + 4;
+                const uint32_t b[2] = {gid < 3 && g0 < ng ? (uint32_t)dp[g0] : 0u, gid < 3 && g1 < ng ? (uint32_t)dp[g1] : 0u};
+                const int* v0 = sm.vg[g0];
+                const int* v1 = sm.vg[g1];
 #pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        const int col = ((half * 4 + j) * 8 + gid) ^ swz;
-                        const uint32_t b[2] = {(uint32_t)v0[col], (uint32_t)v1[col]};
-                        mma_s8_acc(acc[j], a, b);
-                    }
+                for (int t = 0; t < 4; t++) {
+                    const int d0 = (16 * t + gid) ^ swz, d1 = (16 * t + gid + 8) ^ swz;
+                    const uint32_t a[4] = {(uint32_t)v0[d0], (uint32_t)v0[d1], (uint32_t)v1[d0], (uint32_t)v1[d1]};
+                    mma_s8_acc(acc[t], a, b);
                 }
-                if (gid < 3) {
+            }
+            // plane p's sums of dimension d go through the score row (done
+            // with) to the lanes that own them: D (d, p) is lane (d % 8,
+            // p / 2), element p % 2 (+ 2 for d % 16 >= 8)
+            int* scr = reinterpret_cast<int*>(srow);
 #pragma unroll
-                    for (int j = 0; j < 4; j++)
-                        *(int2*)&scr[gid * 72 + (half * 4 + j) * 8 + 2 * tig] = make_int2(acc[j][0], acc[j][1]);
+            for (int t = 0; t < 4; t++) {
+                const int da = 16 * t + gid, db = da + 8;
+                if (tig == 0) {
+                    scr[da] = acc[t][0];
+                    scr[72 + da] = acc[t][1];
+                    scr[db] = acc[t][2];
+                    scr[72 + db] = acc[t][3];
+                } else if (tig == 1) {
+                    scr[144 + da] = acc[t][0];
+                    scr[144 + db] = acc[t][2];
                 }
             }
             __syncwarp();
@@ -1492,8 +1541,11 @@ void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int
 
 // infer.rs:1564-1606 with mlp_native (1610-1634), cond_weights (1640-1694),
 // perm_fma (689-713), silu (2463-2496) and kron_native / mix8 (2322-2460).
-// Seven rows per CTA of 448 threads, one CTA per SM (a batch of 1024 rows
-// fills 147 of the 148 SMs; eight rows a CTA left 20 idle): the layer's small
+// POST_ROWS rows per CTA of 64 POST_ROWS threads (a conditioning warp and a
+// Kronecker warp a row), one CTA per SM: seven rows for a batch of 1024 (147
+// of the 148 SMs; eight rows a CTA left 20 idle), four or two for batches
+// that would leave SMs idle at seven (512 rows: 128 CTAs of four, not 74 of
+// seven; each CTA's time shrinks with its rows). The layer's small
 // weights (Kronecker factors, conditioning, diagonals, norms, permutations)
 // are staged once into shared memory with cp.async, so every phase reads
 // shared memory only. A row's 1024-wide vectors use a padded layout
@@ -1502,8 +1554,8 @@ void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int
 // rows' o, x1 and gates right after; u arrives during the Kronecker stages
 // into the space of cond_v, whose last use is the conditioning logits. The
 // post and residual gates (hpost, Sinkhorn) were computed by the mHC read.
-constexpr int POST_ROWS = 7, POST_THREADS = 448, PV = 32 * 36 + 8;
-static_assert(POST_ROWS * 768 % (4 * POST_THREADS) == 0, "whole batches of mHC items");
+constexpr int PV = 32 * 36 + 8;
+template <int POST_ROWS>
 struct PostSmem {
     float kf[6][1024];
     float cond_v[768 * 8];
@@ -1520,11 +1572,10 @@ struct PostSmem {
     float sc[POST_ROWS][2];
     float wk[POST_ROWS][8];
 };
-extern const size_t POST_SMEM = sizeof(PostSmem);
 
 __device__ __forceinline__ int pv_idx(int p) { return (p >> 5) * 36 + (p & 31); }
 
-template <int NT = POST_THREADS>
+template <int NT>
 __device__ __forceinline__ void stage(void* dst, const void* src, int bytes, int tid) {
     for (int o = tid * 16; o < bytes; o += NT * 16) cp_async16((char*)dst + o, (const char*)src + o, true);
 }
@@ -1592,11 +1643,43 @@ __device__ __forceinline__ void kron_pass2(const float* mt, const float* B, floa
 // puts a block barrier before the result is read. (Tiles of 4 x 4 over two
 // warps a row measured slower: the passes are bound by shared-memory
 // wavefronts, three per 16 paired fmas here.)
-__device__ __forceinline__ void kron_stage_row(PostSmem& sm, int fa, int fb, int from, int q, int lane) {
+template <int R>
+__device__ __forceinline__ void kron_stage_row(PostSmem<R>& sm, int fa, int fb, int from, int q, int lane) {
     const int r0 = (lane & 7) * 4, c0 = (lane >> 3) * 8;
     kron_pass1(sm.kf[fa], sm.buf[from][q], sm.buf[1 - from][q], r0, c0);
     __syncwarp();
     kron_pass2(sm.buf[1 - from][q], sm.kf[fb], sm.buf[from][q], r0, c0);
+}
+
+// One conditioning logit chain (cond_weights, infer.rs:1640-1694): set s,
+// output k: acc = fma(h[j], cv[8 j + k], acc) over j = s, s + 4, .., 764 in
+// order, from zero. The 192 steps are one dependent fma chain, so its
+// operands are loaded 16 steps ahead into registers (two buffers) and a step
+// waits on the previous fma alone.
+__device__ __forceinline__ void cond_load16(const float* h, const float* cv, int set, int k, int b, float (&hx)[16],
+                                            float (&cx)[16]) {
+#pragma unroll
+    for (int e = 0; e < 16; e++) {
+        const int j = set + 4 * (16 * b + e);
+        hx[e] = h[j];
+        cx[e] = cv[j * 8 + k];
+    }
+}
+
+__device__ __forceinline__ float cond_chain(const float* h, const float* cv, int set, int k) {
+    float ha[16], ca[16], hb[16], cb[16];
+    float acc = 0.f;
+    cond_load16(h, cv, set, k, 0, ha, ca);
+#pragma unroll 1
+    for (int b = 0; b < 12; b += 2) {
+        cond_load16(h, cv, set, k, b + 1, hb, cb);
+#pragma unroll
+        for (int e = 0; e < 16; e++) acc = __fmaf_rn(ha[e], ca[e], acc);
+        if (b + 2 < 12) cond_load16(h, cv, set, k, b + 2, ha, ca);
+#pragma unroll
+        for (int e = 0; e < 16; e++) acc = __fmaf_rn(hb[e], cb[e], acc);
+    }
+    return acc;
 }
 
 // dot16_combine over each half-warp (chain c in lane c of the half); the
@@ -1610,27 +1693,29 @@ __device__ __forceinline__ float dot16_combine_half(float acc, int ln) {
     return __fadd_rn(__fadd_rn(t, t1), __fadd_rn(t2, t3));
 }
 
+template <int POST_ROWS, int POST_THREADS = 64 * POST_ROWS>
 __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, const float* o, const float* x1, const float* u,
                                                                    const float* gates, const int32_t* perm1,
                                                                    const int32_t* perm2, int M, float* xs) {
+    static_assert(POST_ROWS * 768 % (4 * POST_THREADS) == 0, "whole batches of mHC items");
     pdl_launch_dependents();
     extern __shared__ __align__(16) int8_t post_raw[];
-    PostSmem& sm = *reinterpret_cast<PostSmem*>(post_raw);
+    PostSmem<POST_ROWS>& sm = *reinterpret_cast<PostSmem<POST_ROWS>*>(post_raw);
     const int tid = threadIdx.x, m0 = blockIdx.x * POST_ROWS;
     const int rows = min(POST_ROWS, M - m0);
     // group 0, before the predecessor is done: the layer's weights
-    stage(sm.post_norm, w.post_norm, 768 * 4, tid);
-    for (int f = 0; f < 6; f++) stage(sm.kf[f], w.kron[f], 4096, tid);
-    stage(sm.cond_v, w.cond_v, 768 * 8 * 4, tid);
-    stage(sm.cond_u, w.cond_u, 8 * 1024 * 4, tid);
-    stage(sm.d1, w.d1, 768 * 4, tid);
-    stage(sm.d2, w.d2, 4096, tid);
-    stage(sm.b2, w.b2, 4096, tid);
-    stage(sm.d3, w.d3, 4096, tid);
-    stage(sm.d4, w.d4, 768 * 4, tid);
-    stage(sm.pre_hada, w.pre_hada, 768 * 4, tid);
-    stage(sm.perm1, perm1, 4096, tid);
-    stage(sm.perm2, perm2, 4096, tid);
+    stage<POST_THREADS>(sm.post_norm, w.post_norm, 768 * 4, tid);
+    for (int f = 0; f < 6; f++) stage<POST_THREADS>(sm.kf[f], w.kron[f], 4096, tid);
+    stage<POST_THREADS>(sm.cond_v, w.cond_v, 768 * 8 * 4, tid);
+    stage<POST_THREADS>(sm.cond_u, w.cond_u, 8 * 1024 * 4, tid);
+    stage<POST_THREADS>(sm.d1, w.d1, 768 * 4, tid);
+    stage<POST_THREADS>(sm.d2, w.d2, 4096, tid);
+    stage<POST_THREADS>(sm.b2, w.b2, 4096, tid);
+    stage<POST_THREADS>(sm.d3, w.d3, 4096, tid);
+    stage<POST_THREADS>(sm.d4, w.d4, 768 * 4, tid);
+    stage<POST_THREADS>(sm.pre_hada, w.pre_hada, 768 * 4, tid);
+    stage<POST_THREADS>(sm.perm1, perm1, 4096, tid);
+    stage<POST_THREADS>(sm.perm2, perm2, 4096, tid);
     asm volatile("cp.async.commit_group;\n" ::);
     pdl_wait();
     // group 1: the rows' o (into x2) and x1 (into buf[1], plain), gates
@@ -1653,7 +1738,7 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
     constexpr int NORM_THREADS = (POST_ROWS * 16 + 31) / 32 * 32;
     if (tid < NORM_THREADS) {
         const int q = tid >> 4;
-        const float ch = q < POST_ROWS ? dot16_chain(sm.x2[q], sm.x2[q], 768, tid & 15) : 0.f;
+        const float ch = q < POST_ROWS ? dot16_sq<768>(sm.x2[q], tid & 15) : 0.f;
         const float tot = dot16_combine_half(ch, tid & 31);
         if ((tid & 15) == 0 && q < POST_ROWS) sm.sc[q][0] = rinv(tot, 768);
     }
@@ -1669,7 +1754,7 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
     __syncthreads();
     if (tid < NORM_THREADS) {
         const int q = tid >> 4;
-        const float ch = q < POST_ROWS ? dot16_chain(sm.x2[q], sm.x2[q], 768, tid & 15) : 0.f;
+        const float ch = q < POST_ROWS ? dot16_sq<768>(sm.x2[q], tid & 15) : 0.f;
         const float tot = dot16_combine_half(ch, tid & 31);
         if ((tid & 15) == 0 && q < POST_ROWS) sm.sc[q][1] = rinv(tot, 768);
     }
@@ -1693,11 +1778,7 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
     static_assert(2 * POST_ROWS * 32 <= POST_THREADS, "two warp sets");
     if (tid < POST_ROWS * 32) {
         const int q = tid >> 5, set = (tid >> 3) & 3, k = tid & 7;
-        const float* h = sm.hs[q];
-        float acc = 0.f;
-#pragma unroll 16
-        for (int j = set; j < 768; j += 4) acc = __fmaf_rn(h[j], sm.cond_v[j * 8 + k], acc);
-        sm.part[q][tid & 31] = acc;
+        sm.part[q][tid & 31] = cond_chain(sm.hs[q], sm.cond_v, set, k);
     } else if (tid < 2 * POST_ROWS * 32) {
         kron_stage_row(sm, 0, 1, 0, (tid >> 5) - POST_ROWS, tid & 31);
     }
@@ -1751,7 +1832,7 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
     {
         constexpr int FULL = 1024 / POST_THREADS * POST_THREADS, TAIL = 1024 - FULL;
         for (int j = tid; j < FULL; j += POST_THREADS) silu_item(j, 0, POST_ROWS);
-        if (TAIL > 0) {
+        if constexpr (TAIL > 0) {
             // POST_THREADS / TAIL thread sets, each taking RT rows of the tail
             constexpr int SETS = POST_THREADS / (TAIL > 0 ? TAIL : 1), RT = (POST_ROWS + SETS - 1) / SETS;
             const int set = tid / (TAIL > 0 ? TAIL : 1), q0 = set * RT;
@@ -1822,7 +1903,7 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
 // thread (mt stored transposed, as kron_native keeps it), while warp 0's
 // conditioning chains may still run. Every float op, and its order, is
 // that of post_block_kernel.
-constexpr int POST_ROW_MAX_M = 296, POST_ROW_THREADS = 512;
+constexpr int POST_ROW_THREADS = 512;
 struct PostRowSmem {
     float kf[6][1024];
     float cond_v[768 * 8];
@@ -1918,7 +1999,7 @@ __global__ void __launch_bounds__(POST_ROW_THREADS, 1) post_row_kernel(LayerW w,
     asm volatile("cp.async.wait_group 0;\n" ::);
     __syncthreads();
     // zcn(o, post_norm): sixteen dot16 chains
-    if (tid < 16) sm.part[tid] = dot16_chain(sm.x2, sm.x2, 768, tid);
+    if (tid < 16) sm.part[tid] = dot16_sq<768>(sm.x2, tid);
     __syncthreads();
     if (tid == 0) sm.sc[0] = rinv(dot16_combine(sm.part), 768);
     __syncthreads();
@@ -1929,7 +2010,7 @@ __global__ void __launch_bounds__(POST_ROW_THREADS, 1) post_row_kernel(LayerW w,
         sm.x2[c] = __fmaf_rn(on, ga, sm.x1[c]);
     }
     __syncthreads();
-    if (tid < 16) sm.part[tid] = dot16_chain(sm.x2, sm.x2, 768, tid);
+    if (tid < 16) sm.part[tid] = dot16_sq<768>(sm.x2, tid);
     __syncthreads();
     if (tid == 0) sm.sc[1] = rinv(dot16_combine(sm.part), 768);
     __syncthreads();
@@ -1948,10 +2029,7 @@ __global__ void __launch_bounds__(POST_ROW_THREADS, 1) post_row_kernel(LayerW w,
     // conditioning logits: 4 accumulator sets by j % 4, fma chains over j
     if (tid < 32) {
         const int set = (tid >> 3) & 3, k = tid & 7;
-        float acc = 0.f;
-#pragma unroll 16
-        for (int j = set; j < 768; j += 4) acc = __fmaf_rn(sm.hb[j], sm.cond_v[j * 8 + k], acc);
-        sm.part[tid] = acc;
+        sm.part[tid] = cond_chain(sm.hb, sm.cond_v, set, k);
         __syncwarp();
         // logits ((C + D) + B) + A, max, one libm exp per lane, the engine's
         // sum tree e7 + ((e6 + (e5 + e4)) + ((e3 + e2) + (e1 + e0)))
@@ -2011,11 +2089,24 @@ __global__ void __launch_bounds__(POST_ROW_THREADS, 1) post_row_kernel(LayerW w,
 void launch_post_block(LayerW w, const float* o, const float* x1, const float* u, const float* gates, const int32_t* perm1,
                        const int32_t* perm2, int M, float* xs, cudaStream_t st) {
     COUNT_LAUNCH();
-    if (M <= POST_ROW_MAX_M) {
+    // The fewest rows a CTA (1, 2, 4 or 7) whose CTAs fit one wave of one
+    // CTA an SM; seven (the most shared memory allows) past that.
+    const int sms = sm_count();
+    if (M <= sms) {
         launch_pdl(post_row_kernel, dim3(M), dim3(POST_ROW_THREADS), POST_ROW_SMEM, st, w, o, x1, u, gates, perm1, perm2, xs);
-        return;
+    } else if (cdiv(M, 2) <= sms) {
+        launch_pdl(post_block_kernel<2>, dim3(cdiv(M, 2)), dim3(128), sizeof(PostSmem<2>), st, w, o, x1, u, gates, perm1, perm2, M, xs);
+    } else if (cdiv(M, 4) <= sms) {
+        launch_pdl(post_block_kernel<4>, dim3(cdiv(M, 4)), dim3(256), sizeof(PostSmem<4>), st, w, o, x1, u, gates, perm1, perm2, M, xs);
+    } else {
+        launch_pdl(post_block_kernel<7>, dim3(cdiv(M, 7)), dim3(448), sizeof(PostSmem<7>), st, w, o, x1, u, gates, perm1, perm2, M, xs);
     }
-    launch_pdl(post_block_kernel, dim3(cdiv(M, POST_ROWS)), dim3(POST_THREADS), POST_SMEM, st, w, o, x1, u, gates, perm1, perm2, M, xs);
+}
+
+cudaError_t post_block_init() {
+    cudaFuncSetAttribute(post_block_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PostSmem<2>));
+    cudaFuncSetAttribute(post_block_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PostSmem<4>));
+    return cudaFuncSetAttribute(post_block_kernel<7>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PostSmem<7>));
 }
 
 // ------------------------------------------------------------ final norm
@@ -2034,7 +2125,7 @@ __global__ void final_hidden_kernel(const float* xs, const float* fnorm, int T, 
     for (int ch = tid; ch < 768; ch += 256)
         mean[ch] = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(x[ch], x[768 + ch]), x[1536 + ch]), x[2304 + ch]), 0.25f);
     __syncthreads();
-    if (tid < 16) part[tid] = dot16_chain(mean, mean, 768, tid);
+    if (tid < 16) part[tid] = dot16_sq<768>(mean, tid);
     __syncthreads();
     if (tid == 0) r_s = rinv(dot16_combine(part), 768);
     __syncthreads();
@@ -2679,7 +2770,7 @@ void launch_probe_head(HeadW h, const float* cells, int S, int T, int ncap, int 
 
 static cudaError_t init_attrs() {
     cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_SMEM);
-    cudaFuncSetAttribute(post_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)POST_SMEM);
+    post_block_init();
     cudaFuncSetAttribute(post_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)POST_ROW_SMEM);
     cudaFuncSetAttribute(cq_mma_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
     cudaFuncSetAttribute(cq_mma_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);

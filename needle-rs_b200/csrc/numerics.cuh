@@ -50,10 +50,36 @@ __device__ __forceinline__ float dot16_combine(const float* a /*[16]*/) {
     return __fadd_rn(__fadd_rn(t[0], t[1]), __fadd_rn(t[2], t[3]));
 }
 
-// One of the sixteen chains of dot16 (element i = c*16 + chain, fma from 0).
-__device__ __forceinline__ float dot16_chain(const float* x, const float* y, int n, int chain) {
+// One of the sixteen chains of dot16 (element i = c*16 + chain, fma from 0)
+// over N elements. Every operand is loaded before the first fma, so the
+// chain waits on its own fmas only, not on a shared-memory load per step.
+template <int N>
+__device__ __forceinline__ float dot16_chain(const float* x, const float* y, int chain) {
+    static_assert(N % 16 == 0, "whole chains");
+    constexpr int E = N / 16;
+    float a[E], b[E];
+#pragma unroll
+    for (int e = 0; e < E; e++) {
+        a[e] = x[chain + 16 * e];
+        b[e] = y[chain + 16 * e];
+    }
     float acc = 0.f;
-    for (int i = chain; i < n; i += 16) acc = __fmaf_rn(x[i], y[i], acc);
+#pragma unroll
+    for (int e = 0; e < E; e++) acc = __fmaf_rn(a[e], b[e], acc);
+    return acc;
+}
+
+// dot16_chain<N>(x, x, chain) with one load per element.
+template <int N>
+__device__ __forceinline__ float dot16_sq(const float* x, int chain) {
+    static_assert(N % 16 == 0, "whole chains");
+    constexpr int E = N / 16;
+    float a[E];
+#pragma unroll
+    for (int e = 0; e < E; e++) a[e] = x[chain + 16 * e];
+    float acc = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; e++) acc = __fmaf_rn(a[e], a[e], acc);
     return acc;
 }
 

@@ -161,13 +161,14 @@ def test_batched_sequences_match_single(small):
         assert list(got[s_]) == list(want), f"sequence {s_}: {got[s_]} vs {want}"
 
 
-@pytest.mark.parametrize("S", [144, 600])
+@pytest.mark.parametrize("S", [144, 201, 301, 600])
 def test_batched_decode_many_sequences(small, S):
     """S sequences in one batch (matmul tiles of 64 rows, the last partial)
     equal S separate oracle sessions through a 9-token prefill and 4 masked
     greedy steps. At 144 the decode steps take the one-row post block and
-    the one-unit-a-warp conv; at 600 the seven-row post block and the
-    two-units-a-warp conv, as the bench's 1024 do."""
+    the one-unit-a-warp conv; at 201 the two-row post block and at 301 the
+    four-row one (each with a last CTA of one row); at 600 the seven-row
+    post block and the two-units-a-warp conv, as the bench's 1024 do."""
     g, o = small
     rng = np.random.default_rng(6)
     n, steps = 9, 4
