@@ -295,7 +295,17 @@ static Model* load_model(const uint8_t* bytes, size_t n, int device) {
         w.d3 = m.upload(d3.data(), d3.size());
         w.d4 = m.upload(d4.data(), d4.size());
         for (int k6 = 0; k6 < 6; k6++) w.kron[k6] = m.upload(small_f32(a, cur, 1024).data(), 1024);
-        w.cond_v = m.upload(small_f32(a, cur, (size_t)d * 8).data(), (size_t)d * 8);
+        {
+            // cond_v [768][8] as the post block's conditioning chains read
+            // it: chain (set, k) = row 8 set + k holds cond_v[set + 4 n][k]
+            // at column n (n < 192), rows COND_LD floats apart
+            const auto cv = small_f32(a, cur, (size_t)d * 8);
+            std::vector<float> cx((size_t)32 * COND_LD, 0.f);
+            for (int set = 0; set < 4; set++)
+                for (int k = 0; k < 8; k++)
+                    for (int n = 0; n < 192; n++) cx[(size_t)(set * 8 + k) * COND_LD + n] = cv[(size_t)(set + 4 * n) * 8 + k];
+            w.cond_v = m.upload(cx.data(), cx.size());
+        }
         w.cond_u = m.upload(small_f32(a, cur, 8 * 1024).data(), 8 * 1024);
     }
     const int nl = c.lanes, nc = nl * d;

@@ -1558,20 +1558,22 @@ constexpr int PV = 32 * 36 + 8;
 template <int POST_ROWS>
 struct PostSmem {
     float kf[6][1024];
-    float cond_v[768 * 8];
+    __align__(16) float cond_v[32 * COND_LD];  // later the rows' u
     float cond_u[8 * 1024];
     float d1[768], d2[1024], b2[1024], d3[1024], d4[768];
     float post_norm[768], pre_hada[768];
     int perm1[1024], perm2[1024];
     // the rows' buffers take 16-byte copies and loads at any row count
     __align__(16) float x2[POST_ROWS][768];
-    __align__(16) float hs[POST_ROWS][768];  // h2 = zcn(x2, pre_hada), the conditioning input
+    __align__(16) float hs[POST_ROWS][4 * COND_LD];  // h2 = zcn(x2, pre_hada) chain-major, the conditioning input
     __align__(16) float buf[2][POST_ROWS][PV];
     __align__(16) float gates[POST_ROWS][24];
     float part[POST_ROWS][32];
     float sc[POST_ROWS][2];
     float wk[POST_ROWS][8];
 };
+
+static_assert(sizeof(PostSmem<7>) <= 232448, "seven rows fit one CTA's 227 KB of shared memory");
 
 __device__ __forceinline__ int pv_idx(int p) { return (p >> 5) * 36 + (p & 31); }
 
@@ -1652,32 +1654,43 @@ __device__ __forceinline__ void kron_stage_row(PostSmem<R>& sm, int fa, int fb, 
 }
 
 // One conditioning logit chain (cond_weights, infer.rs:1640-1694): set s,
-// output k: acc = fma(h[j], cv[8 j + k], acc) over j = s, s + 4, .., 764 in
-// order, from zero. The 192 steps are one dependent fma chain, so its
-// operands are loaded 16 steps ahead into registers (two buffers) and a step
-// waits on the previous fma alone.
-__device__ __forceinline__ void cond_load16(const float* h, const float* cv, int set, int k, int b, float (&hx)[16],
-                                            float (&cx)[16]) {
+// output k: acc = fma(h[j], cond_v[j][k], acc) over j = s, s + 4, .., 764
+// in order, from zero. The input is kept chain-major (element s + 4 n at
+// hx[s * COND_LD + n]) and the weights one chain a row (row 8 s + k), so a
+// chain's operands are 16-byte runs: four steps a load, loaded 16 steps
+// ahead of the fma chain (two register buffers), which then waits on its
+// own fmas alone.
+__device__ __forceinline__ void cond_load16(const float* hr, const float* cr, int b, float4 (&hx)[4], float4 (&cx)[4]) {
 #pragma unroll
-    for (int e = 0; e < 16; e++) {
-        const int j = set + 4 * (16 * b + e);
-        hx[e] = h[j];
-        cx[e] = cv[j * 8 + k];
+    for (int e = 0; e < 4; e++) {
+        hx[e] = *(const float4*)(hr + 16 * b + 4 * e);
+        cx[e] = *(const float4*)(cr + 16 * b + 4 * e);
     }
 }
 
-__device__ __forceinline__ float cond_chain(const float* h, const float* cv, int set, int k) {
-    float ha[16], ca[16], hb[16], cb[16];
+__device__ __forceinline__ float cond_fma16(const float4 (&hx)[4], const float4 (&cx)[4], float acc) {
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        acc = __fmaf_rn(hx[e].x, cx[e].x, acc);
+        acc = __fmaf_rn(hx[e].y, cx[e].y, acc);
+        acc = __fmaf_rn(hx[e].z, cx[e].z, acc);
+        acc = __fmaf_rn(hx[e].w, cx[e].w, acc);
+    }
+    return acc;
+}
+
+__device__ __forceinline__ float cond_chain(const float* hx, const float* cv, int set, int k) {
+    const float* hr = hx + set * COND_LD;
+    const float* cr = cv + (set * 8 + k) * COND_LD;
+    float4 ha[4], ca[4], hb[4], cb[4];
     float acc = 0.f;
-    cond_load16(h, cv, set, k, 0, ha, ca);
+    cond_load16(hr, cr, 0, ha, ca);
 #pragma unroll 1
     for (int b = 0; b < 12; b += 2) {
-        cond_load16(h, cv, set, k, b + 1, hb, cb);
-#pragma unroll
-        for (int e = 0; e < 16; e++) acc = __fmaf_rn(ha[e], ca[e], acc);
-        if (b + 2 < 12) cond_load16(h, cv, set, k, b + 2, ha, ca);
-#pragma unroll
-        for (int e = 0; e < 16; e++) acc = __fmaf_rn(hb[e], cb[e], acc);
+        cond_load16(hr, cr, b + 1, hb, cb);
+        acc = cond_fma16(ha, ca, acc);
+        if (b + 2 < 12) cond_load16(hr, cr, b + 2, ha, ca);
+        acc = cond_fma16(hb, cb, acc);
     }
     return acc;
 }
@@ -1706,7 +1719,7 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
     // group 0, before the predecessor is done: the layer's weights
     stage<POST_THREADS>(sm.post_norm, w.post_norm, 768 * 4, tid);
     for (int f = 0; f < 6; f++) stage<POST_THREADS>(sm.kf[f], w.kron[f], 4096, tid);
-    stage<POST_THREADS>(sm.cond_v, w.cond_v, 768 * 8 * 4, tid);
+    stage<POST_THREADS>(sm.cond_v, w.cond_v, 32 * COND_LD * 4, tid);
     stage<POST_THREADS>(sm.cond_u, w.cond_u, 8 * 1024 * 4, tid);
     stage<POST_THREADS>(sm.d1, w.d1, 768 * 4, tid);
     stage<POST_THREADS>(sm.d2, w.d2, 4096, tid);
@@ -1764,7 +1777,7 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
         int q = k / 768, c = k % 768;
         float tt = __fmul_rn(sm.x2[q][c], sm.sc[q][1]);
         float h = __fmaf_rn(tt, sm.pre_hada[c], tt);
-        sm.hs[q][c] = h;
+        sm.hs[q][(c & 3) * COND_LD + (c >> 2)] = h;
         sm.buf[0][q][pv_idx(c)] = __fmul_rn(h, sm.d1[c]);
     }
     for (int k = tid; k < POST_ROWS * 256; k += POST_THREADS) {
@@ -1906,12 +1919,14 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
 constexpr int POST_ROW_THREADS = 512;
 struct PostRowSmem {
     float kf[6][1024];
-    float cond_v[768 * 8];
+    __align__(16) float cond_v[32 * COND_LD];
     float cond_u[8 * 1024];
     float d1[768], d2[1024], b2[1024], d3[1024], d4[768];
     float post_norm[768], pre_hada[768];
     int perm1[1024], perm2[1024];
-    float x2[768], hb[768], zb[1024], mb[1024], tb[1024];
+    float x2[768];
+    __align__(16) float hb[4 * COND_LD];  // the conditioning input, chain-major
+    float zb[1024], mb[1024], tb[1024];
     float x1[768], ub[768], xold[3072];  // the row's residual, u and streams
     float part[32], sc[2], wk[8], gr[24];
 };
@@ -1974,7 +1989,7 @@ __global__ void __launch_bounds__(POST_ROW_THREADS, 1) post_row_kernel(LayerW w,
     const int kt = tid - 32, r0 = 2 * (kt & 15), c0 = 4 * (kt >> 4);
     const bool kw = kt >= 0 && kt < 128;
     for (int f = 0; f < 6; f++) stage<POST_ROW_THREADS>(sm.kf[f], w.kron[f], 4096, tid);
-    stage<POST_ROW_THREADS>(sm.cond_v, w.cond_v, 768 * 8 * 4, tid);
+    stage<POST_ROW_THREADS>(sm.cond_v, w.cond_v, 32 * COND_LD * 4, tid);
     stage<POST_ROW_THREADS>(sm.cond_u, w.cond_u, 8 * 1024 * 4, tid);
     stage<POST_ROW_THREADS>(sm.d1, w.d1, 768 * 4, tid);
     stage<POST_ROW_THREADS>(sm.d2, w.d2, 4096, tid);
@@ -2019,7 +2034,7 @@ __global__ void __launch_bounds__(POST_ROW_THREADS, 1) post_row_kernel(LayerW w,
         if (c < 768) {
             float tt = __fmul_rn(sm.x2[c], sm.sc[1]);
             float h = __fmaf_rn(tt, sm.pre_hada[c], tt);
-            sm.hb[c] = h;
+            sm.hb[(c & 3) * COND_LD + (c >> 2)] = h;
             sm.zb[c] = __fmul_rn(h, sm.d1[c]);
         } else {
             sm.zb[c] = 0.f;

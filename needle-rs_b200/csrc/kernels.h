@@ -31,11 +31,19 @@ struct DevMat {
     const int8_t* w8 = nullptr;
 };
 
+// Row stride (floats) of the conditioning weights and of the conditioning
+// input as the post block keeps them: chain (set, k) of cond_weights reads
+// element set + 4 n at column n, so a chain's operands are 16-byte runs;
+// 192 columns padded to 196 so the eight chains of a quarter-warp start in
+// distinct bank quads.
+constexpr int COND_LD = 196;
+
 // One layer's weights on the device (small weights widened to f32, which
 // is exact for the archive's f16 values).
 struct LayerW {
     const float *norm_in, *q_taps, *k_taps, *v_taps, *q_norm, *k_norm, *post_norm, *pre_hada;
-    const float *d1, *d2, *b2, *d3, *d4, *kron[6], *cond_v, *cond_u;
+    const float *d1, *d2, *b2, *d3, *d4, *kron[6], *cond_u;
+    const float* cond_v;  // [32][COND_LD]: row 8 set + k, column n = cond_v[set + 4 n][k]
     const int8_t* phi_q;  // [24][3072]
     const float* phi_s;   // [24]
     float attn_gate, a_pre, a_post, a_res;
