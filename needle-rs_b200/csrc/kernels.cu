@@ -612,6 +612,7 @@ extern const size_t POST_ROW_SMEM;
 __global__ void post_row_kernel(LayerW w, const float* o, const float* x1, const float* u, const float* gates, const int32_t* perm1,
                                 const int32_t* perm2, float* xs);
 cudaError_t post_block_init();
+template <int MINB>
 __global__ void attention_kernel(const float* qbuf, const float* proj, Caches c, int l, int T, const int32_t* p0p, int window,
                                  int sink, int ring, float* att, int8_t* act, float* sx);
 
@@ -703,6 +704,51 @@ void launch_engram_conv(const float* taps, Caches c, int site, int nsites, int S
 constexpr int MHC_THREADS = 192, MHC_NORM_THREADS = 160, MHC_XS = 196;
 __device__ __forceinline__ void norm_bar() { asm volatile("bar.sync 1, 160;\n" ::: "memory"); }
 
+// fma(x[n], x[n], acc) over n = 0 .. N - 1 in order from zero, x a
+// 16-byte-aligned run in shared memory. DEEP: loads 16 steps ahead of the
+// chain (two register buffers of four float4), for kernels with registers
+// to spare; else four steps a load as the loop comes.
+__device__ __forceinline__ void ld16f(const float* x, int b, float4 (&r)[4]) {
+#pragma unroll
+    for (int e = 0; e < 4; e++) r[e] = *(const float4*)(x + 16 * b + 4 * e);
+}
+__device__ __forceinline__ float sqfma16(const float4 (&r)[4], float acc) {
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        acc = __fmaf_rn(r[e].x, r[e].x, acc);
+        acc = __fmaf_rn(r[e].y, r[e].y, acc);
+        acc = __fmaf_rn(r[e].z, r[e].z, acc);
+        acc = __fmaf_rn(r[e].w, r[e].w, acc);
+    }
+    return acc;
+}
+template <int N, bool DEEP>
+__device__ __forceinline__ float sq_chain(const float* x) {
+    static_assert(N % 32 == 0, "pairs of 16-step batches");
+    float acc = 0.f;
+    if (!DEEP) {
+#pragma unroll 4
+        for (int k4 = 0; k4 < N / 4; k4++) {
+            const float4 t = *(const float4*)(x + 4 * k4);
+            acc = __fmaf_rn(t.x, t.x, acc);
+            acc = __fmaf_rn(t.y, t.y, acc);
+            acc = __fmaf_rn(t.z, t.z, acc);
+            acc = __fmaf_rn(t.w, t.w, acc);
+        }
+        return acc;
+    }
+    float4 a[4], b[4];
+    ld16f(x, 0, a);
+#pragma unroll 1
+    for (int s = 0; s < N / 16; s += 2) {
+        ld16f(x, s + 1, b);
+        acc = sqfma16(a, acc);
+        if (s + 2 < N / 16) ld16f(x, s + 2, a);
+        acc = sqfma16(b, acc);
+    }
+    return acc;
+}
+
 // dot16_combine over lanes 0-15 of a warp (chain c in lane c); the total is
 // valid in lane 0. Every lane of the warp must call it.
 __device__ __forceinline__ float dot16_combine_warp(float acc, int ln) {
@@ -737,7 +783,8 @@ __device__ __forceinline__ int reduce4_scatter(const int s[4], int ln) {
 // 0-4 form u from the pre gates, apply the engram gate (when the layer has a
 // site: ekv [M][1536] keys, evals [M][768]), the input ZC-RMSNorm and A8 of
 // the normed row (act/sx for the q|k|v|gate matmul; x1o is the residual).
-__global__ void __launch_bounds__(MHC_THREADS, 8) mhc_read_kernel(LayerW w, int lane_own, const float* xs, float* u, float* p,
+template <int MINB>
+__global__ void __launch_bounds__(MHC_THREADS, MINB) mhc_read_kernel(LayerW w, int lane_own, const float* xs, float* u, float* p,
                                                                   const float* ekv, const float* evals, float* x1o, int8_t* act,
                                                                   float* sx) {
     pdl_launch_dependents();
@@ -782,17 +829,7 @@ __global__ void __launch_bounds__(MHC_THREADS, 8) mhc_read_kernel(LayerW w, int 
     __syncthreads();
     if (warp == 0) {
         float acc = 0.f;
-        if (ln < 16) {
-            const float4* cr = (const float4*)(xt + ln * MHC_XS);
-#pragma unroll 4
-            for (int k4 = 0; k4 < 48; k4++) {
-                const float4 t = cr[k4];
-                acc = __fmaf_rn(t.x, t.x, acc);
-                acc = __fmaf_rn(t.y, t.y, acc);
-                acc = __fmaf_rn(t.z, t.z, acc);
-                acc = __fmaf_rn(t.w, t.w, acc);
-            }
-        }
+        if (ln < 16) acc = sq_chain<192, MINB == 1>(xt + ln * MHC_XS);
         float ss = dot16_combine_warp(acc, ln);
         if (ln == 0) sc_s[0] = rinv(ss, 3072);
     }
@@ -920,7 +957,13 @@ __global__ void __launch_bounds__(MHC_THREADS, 8) mhc_read_kernel(LayerW w, int 
 void launch_mhc_read(LayerW w, int lane, const float* xs, int M, float* u, float* p, const float* ekv, const float* evals,
                      float* x1, int8_t* act, float* sx, cudaStream_t st) {
     COUNT_LAUNCH();
-    launch_pdl(mhc_read_kernel, dim3(M), dim3(MHC_THREADS), 0, st, w, lane, xs, u, p, ekv, evals, x1, act, sx);
+    // eight CTAs an SM (42 registers a thread) keep a batch of up to 1184
+    // rows in one wave; a batch of at most one row an SM takes the variant
+    // with the registers to run its chains from registers
+    if (M <= sm_count())
+        launch_pdl(mhc_read_kernel<1>, dim3(M), dim3(MHC_THREADS), 0, st, w, lane, xs, u, p, ekv, evals, x1, act, sx);
+    else
+        launch_pdl(mhc_read_kernel<8>, dim3(M), dim3(MHC_THREADS), 0, st, w, lane, xs, u, p, ekv, evals, x1, act, sx);
 }
 
 // infer.rs:1580-1586 for one row per warp, from the projections the mHC read
@@ -1196,7 +1239,8 @@ __device__ __forceinline__ void mma_s8_acc(int (&d)[4], const uint32_t (&a)[4], 
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
-__global__ void __launch_bounds__(ATT_THREADS, 5) attention_kernel(const float* qbuf, const float* proj, Caches c, int l, int T,
+template <int MINB>
+__global__ void __launch_bounds__(ATT_THREADS, MINB) attention_kernel(const float* qbuf, const float* proj, Caches c, int l, int T,
                                                                 const int32_t* p0p, int window, int sink, int ring, float* att,
                                                                 int8_t* act, float* sx) {
     pdl_launch_dependents();
@@ -1532,8 +1576,14 @@ void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int
     if (T == 1 && nmax >= 256) most = std::max(most, 4);
     most = std::min(most, ATT_MAXPARTS);
     size_t smem = ATT_SMEM_BASE + (most > 1 ? (size_t)ATT_HEADS * most * 66 * 4 : 0);
-    launch_pdl(attention_kernel, dim3(dim3(S * T, 2)), dim3(ATT_THREADS), smem, st, qbuf, proj, c, l, T, c.len, window, sink, ring,
-               att, act, sx);
+    // five CTAs an SM (64 registers a thread) for batches; a launch of at
+    // most one CTA an SM takes the variant with registers to spare
+    if (2 * S * T <= sm_count())
+        launch_pdl(attention_kernel<1>, dim3(dim3(S * T, 2)), dim3(ATT_THREADS), smem, st, qbuf, proj, c, l, T, c.len, window, sink,
+                   ring, att, act, sx);
+    else
+        launch_pdl(attention_kernel<5>, dim3(dim3(S * T, 2)), dim3(ATT_THREADS), smem, st, qbuf, proj, c, l, T, c.len, window, sink,
+                   ring, att, act, sx);
 }
 
 // ------------------------------------------------------------ post block
@@ -2784,7 +2834,8 @@ void launch_probe_head(HeadW h, const float* cells, int S, int T, int ncap, int 
 }
 
 static cudaError_t init_attrs() {
-    cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_SMEM);
+    cudaFuncSetAttribute(attention_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_SMEM);
+    cudaFuncSetAttribute(attention_kernel<5>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_SMEM);
     post_block_init();
     cudaFuncSetAttribute(post_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)POST_ROW_SMEM);
     cudaFuncSetAttribute(cq_mma_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM);
