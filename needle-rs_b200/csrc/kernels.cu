@@ -1416,36 +1416,38 @@ __global__ void __launch_bounds__(ATT_THREADS, MINB) attention_kernel(const floa
             if (len - ii == 1) sum = __fadd_rn(sum, att_key_val(ev, ii));
         }
         sum = __shfl_sync(0xffffffffu, sum, 0);
-        // weights times the value scales, their max from zero, 21-bit digits
+        // weights times the value scales (in the registers), their max from zero
         float wm = 0.f;
 #pragma unroll
         for (int i = 0; i < ATT_KPL; i++) {
             const int k = lane + 32 * i;
             if (k < len) {
-                float wv = __fmul_rn(ev[i], sm.vs[k]);
-                srow[k] = wv;
-                wm = fmaxf(wm, wv);
+                ev[i] = __fmul_rn(ev[i], sm.vs[k]);
+                wm = fmaxf(wm, ev[i]);
             }
         }
         wm = warp_max(wm);
         const float qw = __fdiv_rn(ND_Q21, wm);
-        const int offA = sg.pA & 3;
-        for (int kk = lane; kk < 4 * ng; kk += 32) {
-            // the key (chunk index) at byte kk & 3 of group word kk >> 2:
-            // A's groups hold keys kk - offA, B's (after A's) the rest
-            int k;
-            if (kk < 4 * sg.ngA) {
-                k = kk - offA;
-                if (k < 0 || k >= sg.nA) k = -1;
-            } else {
-                const int kb = kk - 4 * sg.ngA - (sg.pB & 3);
-                k = kb >= 0 && kb < sg.nB ? sg.nA + kb : -1;
+        // 21-bit digits: the chunk's group words start zero, then each lane
+        // writes its keys' three digit bytes at the key's byte of the group
+        // words (A's keys from byte pA % 4 on, B's after A's groups from
+        // byte pB % 4 on); bytes of positions outside the chunk stay zero
+        for (int g = lane; g < ng; g += 32) sm.dig[h][0][g] = sm.dig[h][1][g] = sm.dig[h][2][g] = 0;
+        __syncwarp();
+        {
+            const int offA = sg.pA & 3, offB = 4 * sg.ngA + (sg.pB & 3) - sg.nA;
+            int8_t* dg0 = (int8_t*)sm.dig[h][0];
+#pragma unroll
+            for (int i = 0; i < ATT_KPL; i++) {
+                const int k = lane + 32 * i;
+                if (k < len) {
+                    const int kk = k < sg.nA ? k + offA : k + offB;
+                    const int wq = (int)roundf(__fmul_rn(ev[i], qw));
+                    dg0[kk] = (int8_t)(wq >> 14);
+                    dg0[4 * ATT_MAXGROUPS + kk] = (int8_t)((wq >> 7) & 127);
+                    dg0[8 * ATT_MAXGROUPS + kk] = (int8_t)(wq & 127);
+                }
             }
-            int wq = k >= 0 ? (int)roundf(__fmul_rn(srow[k], qw)) : 0;
-            int8_t* dg = (int8_t*)&sm.dig[h][0][kk >> 2] + (kk & 3);
-            dg[0] = (int8_t)(wq >> 14);
-            dg[4 * ATT_MAXGROUPS] = (int8_t)((wq >> 7) & 127);
-            dg[8 * ATT_MAXGROUPS] = (int8_t)(wq & 127);
         }
         asm volatile("cp.async.wait_group 0;\n" ::);  // value groups
         __syncthreads();
