@@ -787,6 +787,9 @@ template <int MINB>
 __global__ void __launch_bounds__(MHC_THREADS, MINB) mhc_read_kernel(LayerW w, int lane_own, const float* xs, float* u, float* p,
                                                                   const float* ekv, const float* evals, float* x1o, int8_t* act,
                                                                   float* sx) {
+    // dot16 operands loaded 16 at a time in the eight-CTA variant (42
+    // registers), all 48 at once in the other
+    constexpr int MHC_B16 = MINB == 1 ? 48 : 16;
     pdl_launch_dependents();
     pdl_wait();
     // the four streams chain-major: element e at (e % 16) * MHC_XS + e / 16,
@@ -911,8 +914,8 @@ __global__ void __launch_bounds__(MHC_THREADS, MINB) mhc_read_kernel(LayerW w, i
     float* na = xt;
     float* nb = xt + 768;
     if (ekv) {
-        if (lt < 16) part[lt] = dot16_sq<768>(x1, lt);
-        else if (lt < 32) part[lt] = dot16_sq<768>(ek, lt - 16);
+        if (lt < 16) part[lt] = dot16_sq<768, MHC_B16>(x1, lt);
+        else if (lt < 32) part[lt] = dot16_sq<768, MHC_B16>(ek, lt - 16);
         norm_bar();
         if (lt == 0) sc_s[1] = rinv(dot16_combine(part), 768);
         if (lt == 1) sc_s[2] = rinv(dot16_combine(part + 16), 768);
@@ -922,7 +925,7 @@ __global__ void __launch_bounds__(MHC_THREADS, MINB) mhc_read_kernel(LayerW w, i
             nb[k] = __fmul_rn(ek[k], sc_s[2]);
         }
         norm_bar();
-        if (lt < 16) part[lt] = dot16_chain<768>(na, nb, lt);
+        if (lt < 16) part[lt] = dot16_chain<768, MHC_B16 / 2>(na, nb, lt);
         norm_bar();
         if (lt == 0) {
             float dab = dot16_combine(part);
@@ -934,7 +937,7 @@ __global__ void __launch_bounds__(MHC_THREADS, MINB) mhc_read_kernel(LayerW w, i
         norm_bar();
     }
     if (warp == 0) {
-        float acc = ln < 16 ? dot16_sq<768>(x1, ln) : 0.f;
+        float acc = ln < 16 ? dot16_sq<768, MHC_B16>(x1, ln) : 0.f;
         float ss = dot16_combine_warp(acc, ln);
         if (ln == 0) sc_s[0] = rinv(ss, 768);
     }

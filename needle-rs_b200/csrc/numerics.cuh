@@ -51,35 +51,41 @@ __device__ __forceinline__ float dot16_combine(const float* a /*[16]*/) {
 }
 
 // One of the sixteen chains of dot16 (element i = c*16 + chain, fma from 0)
-// over N elements. Every operand is loaded before the first fma, so the
-// chain waits on its own fmas only, not on a shared-memory load per step.
-template <int N>
+// over N elements. The operands are loaded BATCH elements at a time before
+// their fmas (all of them, by default), so the chain waits on its own fmas,
+// not on a shared-memory load per step; kernels short of registers take
+// smaller batches.
+template <int N, int BATCH = N / 16>
 __device__ __forceinline__ float dot16_chain(const float* x, const float* y, int chain) {
-    static_assert(N % 16 == 0, "whole chains");
-    constexpr int E = N / 16;
-    float a[E], b[E];
-#pragma unroll
-    for (int e = 0; e < E; e++) {
-        a[e] = x[chain + 16 * e];
-        b[e] = y[chain + 16 * e];
-    }
+    static_assert(N % 16 == 0 && (N / 16) % BATCH == 0, "whole chains and batches");
     float acc = 0.f;
+#pragma unroll 1
+    for (int e0 = 0; e0 < N / 16; e0 += BATCH) {
+        float a[BATCH], b[BATCH];
 #pragma unroll
-    for (int e = 0; e < E; e++) acc = __fmaf_rn(a[e], b[e], acc);
+        for (int e = 0; e < BATCH; e++) {
+            a[e] = x[chain + 16 * (e0 + e)];
+            b[e] = y[chain + 16 * (e0 + e)];
+        }
+#pragma unroll
+        for (int e = 0; e < BATCH; e++) acc = __fmaf_rn(a[e], b[e], acc);
+    }
     return acc;
 }
 
 // dot16_chain<N>(x, x, chain) with one load per element.
-template <int N>
+template <int N, int BATCH = N / 16>
 __device__ __forceinline__ float dot16_sq(const float* x, int chain) {
-    static_assert(N % 16 == 0, "whole chains");
-    constexpr int E = N / 16;
-    float a[E];
-#pragma unroll
-    for (int e = 0; e < E; e++) a[e] = x[chain + 16 * e];
+    static_assert(N % 16 == 0 && (N / 16) % BATCH == 0, "whole chains and batches");
     float acc = 0.f;
+#pragma unroll 1
+    for (int e0 = 0; e0 < N / 16; e0 += BATCH) {
+        float a[BATCH];
 #pragma unroll
-    for (int e = 0; e < E; e++) acc = __fmaf_rn(a[e], a[e], acc);
+        for (int e = 0; e < BATCH; e++) a[e] = x[chain + 16 * (e0 + e)];
+#pragma unroll
+        for (int e = 0; e < BATCH; e++) acc = __fmaf_rn(a[e], a[e], acc);
+    }
     return acc;
 }
 
