@@ -237,8 +237,30 @@ __device__ __forceinline__ void tmem_ld_wait4x8(uint32_t (&r)[4][8]) {
 
 // Every group sum s has |s| <= 128 * 128 * 128 < 2^22, so the int32 word
 // s + bits(1.5 * 2^23) read as a float is 1.5 * 2^23 + s exactly, and one
-// f32 subtraction gives float(s) without an int-to-float conversion.
+// f32 subtraction gives float(s) without an int-to-float conversion. The
+// accumulators start at bits(1.5 * 2^23) (written by the epilogue into every
+// buffer before first use and again after reading it) and every MMA
+// accumulates, so the words read back are already the biased floats.
 constexpr uint32_t TC_MAGIC = 0x4B400000u;
+
+// The bias into 4 / 8 / 16 consecutive 32-bit columns of this warp's 32 lanes
+// (four columns a store: a store takes its columns' values in as many
+// registers),
+// and the wait for this thread's tensor-memory stores. (The stores touch
+// tensor memory only; as volatile asm they stay ordered with the loads,
+// waits and fences around them.)
+__device__ __forceinline__ void tmem_bias4(uint32_t taddr) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%1,%1,%1};\n" ::"r"(taddr), "r"(TC_MAGIC));
+}
+__device__ __forceinline__ void tmem_bias8(uint32_t taddr) {
+    tmem_bias4(taddr);
+    tmem_bias4(taddr + 4);
+}
+__device__ __forceinline__ void tmem_bias16(uint32_t taddr) {
+#pragma unroll
+    for (int k = 0; k < 4; k++) tmem_bias4(taddr + 4 * k);
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
 
 __device__ __forceinline__ float2 tc_sub2(float2 a, float2 b) {
     float2 d;
@@ -341,6 +363,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // every accumulator buffer starts at the bias: epilogue warp e writes
+    // its lane quarter and column quarter of each, before any MMA is issued
+    if (warp >= 2 && warp < TC_SCALE_WARP) {
+        const int q = warp & 3, c = (warp - 2) >> 2;
+#pragma unroll 1
+        for (int b = 0; b < C::BUFS; b++) {
+            const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * C::GROUP_COLS + c * C::CPT);
+            if constexpr (DEC) {
+#pragma unroll
+                for (int l = 0; l < 4; l++) tmem_bias8(ta + (uint32_t)(l * C::SLICE));
+            } else {
+                tmem_bias16(ta);
+            }
+        }
+        tmem_st_wait();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
 
     if (warp == 0) {
         // ---- TMA producer: lane 0 waits and issues, the warp stays converged;
@@ -421,7 +462,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
                             for (int kk = 0; kk < 4; kk++)
                                 mma_i8(d + (uint32_t)(kk * C::SLICE), sw128_desc(wa + 32 * kk), sw128_desc(aa + 32 * kk), C::IDESC,
-                                       DEC ? 0u : (uint32_t)kk);
+                                       1u);
                         }
                         mma_commit(tfull(sl));  // the two groups' sums are in slot sl
                         if (pr == 2) {
@@ -534,6 +575,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 // after the pair's second group is in registers, the slot is free
                 auto release = [&]() {
                     if (h == 1) {
+                        tmem_st_wait();  // the pair's buffers hold the bias again
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(tempty(sl));
@@ -546,6 +588,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
                         for (int l = 0; l < 4; l++) tmem_ld8(ta + (uint32_t)(l * C::SLICE), r[l]);
                         tmem_ld_wait4x8(r);
+#pragma unroll
+                        for (int l = 0; l < 4; l++) tmem_bias8(ta + (uint32_t)(l * C::SLICE));
                     } else {
 #pragma unroll
                         for (int l = 0; l < 4; l++)
@@ -560,8 +604,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         const float2 sc = tc_mul2(*(const float2*)(cv + 2 * j), nn);
 #pragma unroll
                         for (int l = 0; l < 4; l++) {
-                            const float2 s2 = tc_sub2(make_float2(__uint_as_float(r[l][2 * j] + TC_MAGIC),
-                                                                  __uint_as_float(r[l][2 * j + 1] + TC_MAGIC)), mg);
+                            const float2 s2 = tc_sub2(make_float2(__uint_as_float(r[l][2 * j]), __uint_as_float(r[l][2 * j + 1])), mg);
                             acc[l][j] = tc_fma2(s2, sc, acc[l][j]);
                         }
                     }
@@ -570,6 +613,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     if (ok) {
                         tmem_ld16(ta, r);
                         tmem_ld_wait16(r);
+                        tmem_bias16(ta);
                     } else {
 #pragma unroll
                         for (int j = 0; j < CPT; j++) r[j] = 0u;
@@ -577,7 +621,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     release();
 #pragma unroll
                     for (int j = 0; j < CPT / 2; j++) {  // token pair (2j, 2j + 1) of this quarter
-                        const float2 s2 = tc_sub2(make_float2(__uint_as_float(r[2 * j] + TC_MAGIC), __uint_as_float(r[2 * j + 1] + TC_MAGIC)), mg);
+                        const float2 s2 = tc_sub2(make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), mg);
                         const float2 c2 = *(const float2*)(cv + 2 * j);
                         float2 f2 = make_float2(nc[g], nc[g]);
                         if (REM) {
