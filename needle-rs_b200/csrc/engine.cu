@@ -699,12 +699,20 @@ static int chunk(Batch& b, const int32_t* ids, int T, int outputs) {
         CK(cudaStreamWaitEvent(b.st3, b.ev_mhc[l], 0));
         launch_mhc_gates(w, lane, M, b.p, b.st3);
         CK(cudaEventRecord(b.ev_gates[l], b.st3));
-        tick(b, ND_SITE_QKVG);
-        linear(m.qkvg[l], b.act, b.sx, M, T, b.proj, 1568, st);
-        tick(b, ND_SITE_QKVG);
-        tick(b, ND_SITE_CONV);
-        launch_conv_rope_kv(w, l, b.proj, b.c, S, T, p0, b.hist_base, b.cosr, b.sinr, b.qbuf, st);
-        tick(b, ND_SITE_CONV);
+        if (T == 1 && M <= QKVG_CONV_MAX_ROWS && m.qkvg[l].runs.size() == 1) {
+            // a one-token step of a few sequences: the projection and the
+            // conv in one launch (its time counts as the q|k|v|gate site's)
+            tick(b, ND_SITE_QKVG);
+            CK(launch_qkvg_conv(m.qkvg[l].runs[0], b.act, b.sx, M, b.proj, w, l, b.c, b.hist_base, b.cosr, b.sinr, b.qbuf, st));
+            tick(b, ND_SITE_QKVG);
+        } else {
+            tick(b, ND_SITE_QKVG);
+            linear(m.qkvg[l], b.act, b.sx, M, T, b.proj, 1568, st);
+            tick(b, ND_SITE_QKVG);
+            tick(b, ND_SITE_CONV);
+            launch_conv_rope_kv(w, l, b.proj, b.c, S, T, p0, b.hist_base, b.cosr, b.sinr, b.qbuf, st);
+            tick(b, ND_SITE_CONV);
+        }
         tick(b, ND_SITE_ATTENTION);
         launch_attention(b.qbuf, b.proj, b.c, l, S, T, p0, c.window(l), b.attend_sink, b.attend_ring, b.att, b.act, b.sx, st);
         tick(b, ND_SITE_ATTENTION);

@@ -508,7 +508,84 @@ __device__ __forceinline__ uint32_t lut2(uint32_t c, uint32_t v) {
     return __byte_perm(v, 0u, sel);
 }
 
-// FMT: 4 or 2 = codes of that width, 8 = the w8 copy (width 3).
+// One weight row of the GEMV as a warp holds it: lane i's three blocks
+// (codes turned into int8 codebook values) and, in lanes g < 6, the row's
+// group norms.
+struct GemvRow {
+    int wl[3], wh[3];
+    float norm_l;
+};
+
+// FMT: 4 or 2 = codes of that width, 8 = the w8 copy (width 3). The load
+// reads and decodes weight row n (the layer's, not a predecessor's output:
+// callers issue it before their wait on the predecessor).
+template <int FMT>
+__device__ __forceinline__ void gemv_row_load(const DevMat& W, int n, int lane, GemvRow& r) {
+    const int wi = lane & 15, a = wi >> 2, l = wi & 3, half = lane >> 4;
+    const int slot = l * 32 + (a & 1) * 16 + (a >> 1) * 8;  // lane_major_pos of the block
+    if (FMT == 4) {
+        const uint32_t v0 = W.vals4[0], v1 = W.vals4[1], v2 = W.vals4[2], v3 = W.vals4[3];
+        const uint32_t* codes = (const uint32_t*)(W.codes + (size_t)n * 384);
+#pragma unroll
+        for (int k = 0; k < 3; k++) {
+            const uint32_t c = __ldg(codes + lane + 32 * k);
+            r.wl[k] = (int)lut4(c & 0xffffu, v0, v1, v2, v3);
+            r.wh[k] = (int)lut4(c >> 16, v0, v1, v2, v3);
+        }
+    } else if (FMT == 2) {
+        const uint32_t v0 = W.vals4[0];
+        const uint16_t* codes = (const uint16_t*)(W.codes + (size_t)n * 192);
+#pragma unroll
+        for (int k = 0; k < 3; k++) {
+            const uint32_t c = __ldg(codes + lane + 32 * k);
+            r.wl[k] = (int)lut2(c & 0xffu, v0);
+            r.wh[k] = (int)lut2(c >> 8, v0);
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 3; k++) {
+            const int2 w = __ldg((const int2*)(W.w8 + (size_t)n * 768 + (2 * k + half) * 128 + slot));
+            r.wl[k] = w.x;
+            r.wh[k] = w.y;
+        }
+    }
+    r.norm_l = lane < 6 ? h2f(W.norms[(size_t)n * 6 + lane]) : 0.f;
+}
+
+// The decode combine of a loaded row against M activation rows: y[m][col0 + n].
+template <int FMT>
+__device__ __forceinline__ void gemv_row_out(const DevMat& W, const GemvRow& r, int n, int lane, const int8_t* act, const float* sx,
+                                             int M, float* y, int ldy, int col0) {
+    const int wi = lane & 15, a = wi >> 2, l = wi & 3, half = lane >> 4;
+    const int slot = l * 32 + (a & 1) * 16 + (a >> 1) * 8;
+    const float cbs = W.cbs;
+    for (int m = 0; m < M; m++) {
+        const int8_t* ar = act + (size_t)m * 768;
+        int s[3];
+#pragma unroll
+        for (int k = 0; k < 3; k++) {
+            const int g = 2 * k + half;
+            const int2 x = *(const int2*)(ar + g * 128 + slot);
+            int v = __dp4a(r.wl[k], x.x, 0);
+            v = __dp4a(r.wh[k], x.y, v);
+            v += __shfl_xor_sync(0xffffffffu, v, FMT == 2 ? 1 : 4);
+            v += __shfl_xor_sync(0xffffffffu, v, 8);
+            s[k] = v;  // the sum of group g, one decode lane
+        }
+        float sxl = lane < 6 ? sx[(size_t)m * 6 + lane] : 0.f;
+        float acc = 0.f;
+#pragma unroll
+        for (int g = 0; g < 6; g++) {
+            const int src = (g & 1) * 16 + (FMT == 2 ? 2 * (lane & 3) : (lane & 3));
+            int sg = __shfl_sync(0xffffffffu, s[g >> 1], src);
+            float sc = __fmul_rn(__fmul_rn(__shfl_sync(0xffffffffu, sxl, g), cbs), __shfl_sync(0xffffffffu, r.norm_l, g));
+            acc = __fmaf_rn((float)sg, sc, acc);
+        }
+        float l1 = __shfl_sync(0xffffffffu, acc, 1), l2 = __shfl_sync(0xffffffffu, acc, 2), l3 = __shfl_sync(0xffffffffu, acc, 3);
+        if (lane == 0) y[(size_t)m * ldy + col0 + n] = __fadd_rn(__fadd_rn(acc, l1), __fadd_rn(l2, l3));
+    }
+}
+
 template <int FMT>
 __global__ void __launch_bounds__(256) cq_gemv_kernel(DevMat W, const int8_t* act, const float* sx, int M, float* y, int ldy,
                                                       int col0) {
@@ -521,64 +598,10 @@ __global__ void __launch_bounds__(256) cq_gemv_kernel(DevMat W, const int8_t* ac
         pdl_wait();
         return;
     }
-    const int wi = lane & 15, a = wi >> 2, l = wi & 3, half = lane >> 4;
-    const int slot = l * 32 + (a & 1) * 16 + (a >> 1) * 8;  // lane_major_pos of the block
-    int wl[3], wh[3];
-    if (FMT == 4) {
-        const uint32_t v0 = W.vals4[0], v1 = W.vals4[1], v2 = W.vals4[2], v3 = W.vals4[3];
-        const uint32_t* codes = (const uint32_t*)(W.codes + (size_t)n * 384);
-#pragma unroll
-        for (int k = 0; k < 3; k++) {
-            const uint32_t c = __ldg(codes + lane + 32 * k);
-            wl[k] = (int)lut4(c & 0xffffu, v0, v1, v2, v3);
-            wh[k] = (int)lut4(c >> 16, v0, v1, v2, v3);
-        }
-    } else if (FMT == 2) {
-        const uint32_t v0 = W.vals4[0];
-        const uint16_t* codes = (const uint16_t*)(W.codes + (size_t)n * 192);
-#pragma unroll
-        for (int k = 0; k < 3; k++) {
-            const uint32_t c = __ldg(codes + lane + 32 * k);
-            wl[k] = (int)lut2(c & 0xffu, v0);
-            wh[k] = (int)lut2(c >> 8, v0);
-        }
-    } else {
-#pragma unroll
-        for (int k = 0; k < 3; k++) {
-            const int2 w = __ldg((const int2*)(W.w8 + (size_t)n * 768 + (2 * k + half) * 128 + slot));
-            wl[k] = w.x;
-            wh[k] = w.y;
-        }
-    }
-    const float cbs = W.cbs;
-    float norm_l = 0.f;  // lane g < 6 holds norm[n][g]
-    if (lane < 6) norm_l = h2f(W.norms[(size_t)n * 6 + lane]);
+    GemvRow r;
+    gemv_row_load<FMT>(W, n, lane, r);
     pdl_wait();
-    for (int m = 0; m < M; m++) {
-        const int8_t* ar = act + (size_t)m * 768;
-        int s[3];
-#pragma unroll
-        for (int k = 0; k < 3; k++) {
-            const int g = 2 * k + half;
-            const int2 x = *(const int2*)(ar + g * 128 + slot);
-            int v = __dp4a(wl[k], x.x, 0);
-            v = __dp4a(wh[k], x.y, v);
-            v += __shfl_xor_sync(0xffffffffu, v, FMT == 2 ? 1 : 4);
-            v += __shfl_xor_sync(0xffffffffu, v, 8);
-            s[k] = v;  // the sum of group g, one decode lane
-        }
-        float sxl = lane < 6 ? sx[(size_t)m * 6 + lane] : 0.f;
-        float acc = 0.f;
-#pragma unroll
-        for (int g = 0; g < 6; g++) {
-            const int src = (g & 1) * 16 + (FMT == 2 ? 2 * (lane & 3) : (lane & 3));
-            int sg = __shfl_sync(0xffffffffu, s[g >> 1], src);
-            float sc = __fmul_rn(__fmul_rn(__shfl_sync(0xffffffffu, sxl, g), cbs), __shfl_sync(0xffffffffu, norm_l, g));
-            acc = __fmaf_rn((float)sg, sc, acc);
-        }
-        float l1 = __shfl_sync(0xffffffffu, acc, 1), l2 = __shfl_sync(0xffffffffu, acc, 2), l3 = __shfl_sync(0xffffffffu, acc, 3);
-        if (lane == 0) y[(size_t)m * ldy + col0 + n] = __fadd_rn(__fadd_rn(acc, l1), __fadd_rn(l2, l3));
-    }
+    gemv_row_out<FMT>(W, r, n, lane, act, sx, M, y, ldy, col0);
 }
 
 cudaError_t launch_cq_gemm(DevMat W, const int8_t* act, const float* sx, int M, int T, float* y, int ldy, int col0,
@@ -1024,6 +1047,102 @@ void launch_mhc_gates(LayerW w, int lane, int M, float* gates, cudaStream_t st) 
 // UPW = 1, sixteen warps, one unit each (the shorter chain for small
 // batches). The taps read earlier rows of this chunk, else the pre-tap
 // history, else zeros.
+// Unit u of a row's pre-tap values: its first column in the q|k|v part of
+// the projection, its taps' row stride and column, its width, its taps.
+__device__ __forceinline__ void conv_unit_of(const LayerW& w, int unit, int& start, int& cw, int& cc, int& len, const float*& wt) {
+    if (unit < 12) { start = unit * 48; cw = 576; cc = unit * 48; len = 48; wt = w.q_taps; }
+    else if (unit < 14) { int kh = unit - 12; start = 576 + kh * 48; cw = 96; cc = kh * 48; len = 48; wt = w.k_taps; }
+    else { int vh = unit - 14; start = 672 + vh * 64; cw = 128; cc = vh * 64; len = 64; wt = w.v_taps; }
+}
+
+// One (row, unit) of the conv by one warp, the lane's channels k = lane,
+// lane + 32 (< the unit's width) given with their current pre-tap value
+// and the two before (zero where no earlier row exists): the row's pre-tap
+// values join the history ring (infer.rs:1486-1488; its slot is none of the
+// two that rows 0 and 1 read), the taps run into x (64 floats of shared
+// memory), then q and k heads take zcn and RoPE (qbuf for q), k and v heads
+// int8 at this position's cache slot.
+__device__ __forceinline__ void conv_unit(const LayerW& w, int l, int unit, const Caches& c, int s, int i, int pos, int m,
+                                          size_t hrow0, const float (&cur)[2], const float (&prev)[2][2], float* x,
+                                          const float* cosr, const float* sinr, float* qbuf, int lane) {
+    int start, cw, cc, len;
+    const float* wt;
+    conv_unit_of(w, unit, start, cw, cc, len, wt);
+#pragma unroll
+    for (int t = 0; t < 2; t++) {
+        const int k = lane + 32 * t;
+        if (k < len) {
+            c.hist[(hrow0 + pos % HIST_RING) * 800 + start + k] = cur[t];
+            float o = __fmul_rn(wt[cc + k], cur[t]);
+            o = __fmaf_rn(wt[cw + cc + k], prev[t][0], o);
+            o = __fmaf_rn(wt[2 * cw + cc + k], prev[t][1], o);
+            x[k] = o;
+        }
+    }
+    __syncwarp();
+    if (unit < 14) {
+        // zcn_inplace (infer.rs:446-452) over the 48-wide head, dot16 order.
+        float part = 0.f;
+        if (lane < 16) {
+            part = __fmaf_rn(x[lane], x[lane], 0.f);
+            part = __fmaf_rn(x[lane + 16], x[lane + 16], part);
+            part = __fmaf_rn(x[lane + 32], x[lane + 32], part);
+        }
+        float chains[16];
+#pragma unroll
+        for (int k = 0; k < 16; k++) chains[k] = __shfl_sync(0xffffffffu, part, k);
+        float rr = rinv(dot16_combine(chains), 48);
+        const float* scale = unit < 12 ? w.q_norm : w.k_norm;
+        float t0 = __fmul_rn(x[lane], rr);
+        float y0 = __fmaf_rn(t0, scale[lane], t0);
+        float y1 = 0.f;
+        if (lane < 16) {
+            float t1 = __fmul_rn(x[lane + 32], rr);
+            y1 = __fmaf_rn(t1, scale[lane + 32], t1);
+        }
+        __syncwarp();
+        x[lane] = y0;
+        if (lane < 16) x[lane + 32] = y1;
+        __syncwarp();
+        // RoPE (infer.rs:1479-1483) on halves of 24.
+        float na = 0.f, nb = 0.f;
+        if (lane < 24) {
+            float cs = cosr[i * 24 + lane], sn = sinr[i * 24 + lane];
+            float av = x[lane], bv = x[lane + 24];
+            na = __fmaf_rn(-sn, bv, __fmul_rn(cs, av));
+            nb = __fmaf_rn(sn, av, __fmul_rn(cs, bv));
+        }
+        __syncwarp();
+        if (lane < 24) {
+            x[lane] = na;
+            x[lane + 24] = nb;
+        }
+        __syncwarp();
+    }
+    if (unit < 12) {
+        for (int k = lane; k < 48; k += 32) qbuf[(size_t)m * 576 + unit * 48 + k] = x[k];
+        return;
+    }
+    // int8 KV at this position's slot (infer.rs:1508-1525).
+    float a = 0.f;
+    for (int k = lane; k < len; k += 32) a = fmaxf(a, fabsf(x[k]));
+    a = warp_max(a);
+    float sc = a > 0.f ? __fmul_rn(a, ND_K127) : 1.0f;
+    float inv = __fdiv_rn(1.0f, sc);
+    if (unit < 14) {
+        int kh = unit - 12;
+        size_t row = (((size_t)s * c.L + l) * 2 + kh) * c.cap + pos;
+        for (int k = lane; k < 48; k += 32) c.k8[row * 48 + k] = q8_round(x[k], inv);
+        if (lane == 0) c.ks[row] = sc;
+    } else {
+        int vh = unit - 14;
+        size_t row = (((size_t)s * c.L + l) * 2 + vh) * c.cap + pos;
+        int8_t* vg = c.v8 + ((((size_t)s * c.L + l) * 2 + vh) * c.vgroups + (pos >> 2)) * 256 + (pos & 3);
+        for (int k = lane; k < 64; k += 32) vg[k * 4] = q8_round(x[k], inv);
+        if (lane == 0) c.vs[row] = sc;
+    }
+}
+
 template <int UPW>
 __global__ void __launch_bounds__(512 / UPW, 8 / (3 - UPW)) conv_rope_kv_kernel(LayerW w, int l, const float* proj, Caches c,
                                                                              int T, const int32_t* p0p, int hist_base,
@@ -1036,11 +1155,6 @@ __global__ void __launch_bounds__(512 / UPW, 8 / (3 - UPW)) conv_rope_kv_kernel(
     const int m = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int s = m / T, i = m % T, pos = p0 + i;
     const size_t hrow0 = ((size_t)s * c.L + l) * HIST_RING;
-    auto unit_of = [&](int unit, int& start, int& cw, int& cc, int& len, const float*& wt) {
-        if (unit < 12) { start = unit * 48; cw = 576; cc = unit * 48; len = 48; wt = w.q_taps; }
-        else if (unit < 14) { int kh = unit - 12; start = 576 + kh * 48; cw = 96; cc = kh * 48; len = 48; wt = w.k_taps; }
-        else { int vh = unit - 14; start = 672 + vh * 64; cw = 128; cc = vh * 64; len = 64; wt = w.v_taps; }
-    };
     // every row load of the lane's (at most two) channels of the warp's
     // units first, then the tap weights (cache-resident), history writes
     // and taps
@@ -1049,7 +1163,7 @@ __global__ void __launch_bounds__(512 / UPW, 8 / (3 - UPW)) conv_rope_kv_kernel(
     for (int r = 0; r < UPW; r++) {
         int start, cw, cc, len;
         const float* wt;
-        unit_of(warp + WARPS * r, start, cw, cc, len, wt);
+        conv_unit_of(w, warp + WARPS * r, start, cw, cc, len, wt);
 #pragma unroll
         for (int t = 0; t < 2; t++) {
             const int k = lane + 32 * t;
@@ -1067,92 +1181,86 @@ __global__ void __launch_bounds__(512 / UPW, 8 / (3 - UPW)) conv_rope_kv_kernel(
         }
     }
 #pragma unroll
-    for (int r = 0; r < UPW; r++) {
-        int start, cw, cc, len;
-        const float* wt;
-        unit_of(warp + WARPS * r, start, cw, cc, len, wt);
-        float* x = buf[warp + WARPS * r];
+    for (int r = 0; r < UPW; r++)
+        conv_unit(w, l, warp + WARPS * r, c, s, i, pos, m, hrow0, cur[r], prev[r], buf[warp + WARPS * r], cosr, sinr, qbuf, lane);
+}
+
+// The q|k|v|gate GEMV and the conv in one launch, for one-token steps of up
+// to GEMV_MAXM rows (row m is sequence m): CTA u < 16 computes unit u's
+// pre-tap rows of the projection (q heads 0-11: 48 rows, k heads: 48, v
+// heads: 64; two rows a warp of 32), then warp m runs that unit's conv for
+// row m; CTAs 16-27 compute the gate rows, 64 each. Every weight row's codes are read before
+// the wait on the predecessor, as in the GEMV; the history rows (earlier
+// steps') after it. Each value is computed as cq_gemv_kernel and
+// conv_rope_kv_kernel compute it.
+constexpr int QKVC_CTAS = 16 + 768 / 64, QKVC_WARPS = 32;
+template <int FMT>
+__global__ void __launch_bounds__(32 * QKVC_WARPS) qkvg_conv_kernel(DevMat W, const int8_t* act, const float* sx, int M, float* proj, LayerW w,
+                                                        int l, Caches c, const int32_t* p0p, int hist_base, const float* cosr,
+                                                        const float* sinr, float* qbuf) {
+    pdl_launch_dependents();
+    __shared__ float buf[GEMV_MAXM][64];
+    const int u = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int r0, nr;
+    if (u < 12) r0 = 48 * u, nr = 48;
+    else if (u < 14) r0 = 576 + 48 * (u - 12), nr = 48;
+    else if (u < 16) r0 = 672 + 64 * (u - 14), nr = 64;
+    else r0 = 800 + 64 * (u - 16), nr = 64;
+    // two weight rows a warp (a unit has at most 64)
+    GemvRow rr[2];
 #pragma unroll
-        for (int t = 0; t < 2; t++) {
-            const int k = lane + 32 * t;
-            if (k < len) {
-                // this row's pre-tap value joins the history (infer.rs:1486-1488);
-                // its slot is none of the two that rows 0 and 1 read
-                c.hist[(hrow0 + pos % HIST_RING) * 800 + start + k] = cur[r][t];
-                float o = __fmul_rn(wt[cc + k], cur[r][t]);
-                o = __fmaf_rn(wt[cw + cc + k], prev[r][t][0], o);  // zero where no earlier row exists
-                o = __fmaf_rn(wt[2 * cw + cc + k], prev[r][t][1], o);
-                x[k] = o;
-            }
-        }
-    }
-    __syncwarp();
-#pragma unroll 1
-    for (int r = 0; r < UPW; r++) {
-        const int unit = warp + WARPS * r, len = unit < 14 ? 48 : 64;
-        float* x = buf[unit];
-        if (unit < 14) {
-            // zcn_inplace (infer.rs:446-452) over the 48-wide head, dot16 order.
-            float part = 0.f;
-            if (lane < 16) {
-                part = __fmaf_rn(x[lane], x[lane], 0.f);
-                part = __fmaf_rn(x[lane + 16], x[lane + 16], part);
-                part = __fmaf_rn(x[lane + 32], x[lane + 32], part);
-            }
-            float chains[16];
+    for (int k = 0; k < 2; k++)
+        if (warp + QKVC_WARPS * k < nr) gemv_row_load<FMT>(W, r0 + warp + QKVC_WARPS * k, lane, rr[k]);
+    pdl_wait();
+    // the conv warps (warp m of a unit CTA) request their history rows
+    // first, so the loads run under the GEMV
+    const bool conv_warp = u < 16 && warp < M;
+    const int m = warp, pos = *p0p;
+    const size_t hrow0 = ((size_t)m * c.L + l) * HIST_RING;
+    int start = 0, cw, cc, len = 0;
+    const float* wt;
+    if (u < 16) conv_unit_of(w, u, start, cw, cc, len, wt);
+    float cur[2], prev[2][2];
 #pragma unroll
-            for (int k = 0; k < 16; k++) chains[k] = __shfl_sync(0xffffffffu, part, k);
-            float rr = rinv(dot16_combine(chains), 48);
-            const float* scale = unit < 12 ? w.q_norm : w.k_norm;
-            float t0 = __fmul_rn(x[lane], rr);
-            float y0 = __fmaf_rn(t0, scale[lane], t0);
-            float y1 = 0.f;
-            if (lane < 16) {
-                float t1 = __fmul_rn(x[lane + 32], rr);
-                y1 = __fmaf_rn(t1, scale[lane + 32], t1);
+    for (int t = 0; t < 2; t++) {
+        const int k = lane + 32 * t;
+        cur[t] = 0.f;
+        prev[t][0] = prev[t][1] = 0.f;
+        if (conv_warp && k < len)
+#pragma unroll
+            for (int j = 1; j < 3; j++) {
+                const int pj = pos - j;
+                if (pj >= hist_base && pj >= 0) prev[t][j - 1] = c.hist[(hrow0 + pj % HIST_RING) * 800 + start + k];
             }
-            __syncwarp();
-            x[lane] = y0;
-            if (lane < 16) x[lane + 32] = y1;
-            __syncwarp();
-            // RoPE (infer.rs:1479-1483) on halves of 24.
-            float na = 0.f, nb = 0.f;
-            if (lane < 24) {
-                float cs = cosr[i * 24 + lane], sn = sinr[i * 24 + lane];
-                float av = x[lane], bv = x[lane + 24];
-                na = __fmaf_rn(-sn, bv, __fmul_rn(cs, av));
-                nb = __fmaf_rn(sn, av, __fmul_rn(cs, bv));
-            }
-            __syncwarp();
-            if (lane < 24) {
-                x[lane] = na;
-                x[lane + 24] = nb;
-            }
-            __syncwarp();
-        }
-        if (unit < 12) {
-            for (int k = lane; k < 48; k += 32) qbuf[(size_t)m * 576 + unit * 48 + k] = x[k];
-            continue;
-        }
-        // int8 KV at this position's slot (infer.rs:1508-1525).
-        float a = 0.f;
-        for (int k = lane; k < len; k += 32) a = fmaxf(a, fabsf(x[k]));
-        a = warp_max(a);
-        float sc = a > 0.f ? __fmul_rn(a, ND_K127) : 1.0f;
-        float inv = __fdiv_rn(1.0f, sc);
-        if (unit < 14) {
-            int kh = unit - 12;
-            size_t row = (((size_t)s * c.L + l) * 2 + kh) * c.cap + pos;
-            for (int k = lane; k < 48; k += 32) c.k8[row * 48 + k] = q8_round(x[k], inv);
-            if (lane == 0) c.ks[row] = sc;
-        } else {
-            int vh = unit - 14;
-            size_t row = (((size_t)s * c.L + l) * 2 + vh) * c.cap + pos;
-            int8_t* vg = c.v8 + ((((size_t)s * c.L + l) * 2 + vh) * c.vgroups + (pos >> 2)) * 256 + (pos & 3);
-            for (int k = lane; k < 64; k += 32) vg[k * 4] = q8_round(x[k], inv);
-            if (lane == 0) c.vs[row] = sc;
-        }
     }
+#pragma unroll
+    for (int k = 0; k < 2; k++)
+        if (warp + QKVC_WARPS * k < nr) gemv_row_out<FMT>(W, rr[k], r0 + warp + QKVC_WARPS * k, lane, act, sx, M, proj, 1568, 0);
+    if (u >= 16) return;
+    __syncthreads();  // the unit's pre-tap rows are in proj
+    if (!conv_warp) return;
+#pragma unroll
+    for (int t = 0; t < 2; t++) {
+        const int k = lane + 32 * t;
+        if (k < len) cur[t] = proj[(size_t)m * 1568 + start + k];
+    }
+    conv_unit(w, l, u, c, m, 0, pos, m, hrow0, cur, prev, buf[m], cosr, sinr, qbuf, lane);
+}
+
+cudaError_t launch_qkvg_conv(DevMat W, const int8_t* act, const float* sx, int M, float* proj, LayerW w, int l, Caches c,
+                             int hist_base, const float* cosr, const float* sinr, float* qbuf, cudaStream_t st) {
+    static_assert(QKVG_CONV_MAX_ROWS <= GEMV_MAXM, "the GEMV's rows");
+    if (!W.w8 || W.groups != 6 || W.in_dim != 768 || W.out != 1568 || M < 1 || M > QKVG_CONV_MAX_ROWS ||
+        (W.width != 2 && W.width != 3 && W.width != 4))
+        return cudaErrorInvalidValue;
+    COUNT_LAUNCH();
+    if (W.width == 4)
+        launch_pdl(qkvg_conv_kernel<4>, dim3(QKVC_CTAS), dim3(32 * QKVC_WARPS), 0, st, W, act, sx, M, proj, w, l, c, c.len, hist_base, cosr, sinr, qbuf);
+    else if (W.width == 2)
+        launch_pdl(qkvg_conv_kernel<2>, dim3(QKVC_CTAS), dim3(32 * QKVC_WARPS), 0, st, W, act, sx, M, proj, w, l, c, c.len, hist_base, cosr, sinr, qbuf);
+    else
+        launch_pdl(qkvg_conv_kernel<8>, dim3(QKVC_CTAS), dim3(32 * QKVC_WARPS), 0, st, W, act, sx, M, proj, w, l, c, c.len, hist_base, cosr, sinr, qbuf);
+    return cudaSuccess;
 }
 
 void launch_conv_rope_kv(LayerW w, int l, const float* proj, Caches c, int S, int T, int p0, int hist_base, const float* cosr,

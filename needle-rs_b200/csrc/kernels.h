@@ -146,6 +146,13 @@ void launch_mhc_read(LayerW w, int lane, const float* xs, int M, float* u, float
 void launch_mhc_gates(LayerW w, int lane, int M, float* gates, cudaStream_t st);
 void launch_conv_rope_kv(LayerW w, int l, const float* proj, Caches c, int S, int T, int p0, int hist_base, const float* cosr,
                          const float* sinr, float* qbuf, cudaStream_t st);
+// The q|k|v|gate projection (W: one run of all 1568 rows) and the conv in
+// one launch for a one-token step of 1 .. QKVG_CONV_MAX_ROWS rows, as launch_cq_gemm(W, act,
+// sx, M, 1, proj, 1568, 0) then launch_conv_rope_kv(w, l, proj, c, M, 1, ..)
+// compute them; cudaErrorInvalidValue (nothing launched) outside that.
+constexpr int QKVG_CONV_MAX_ROWS = 4;
+cudaError_t launch_qkvg_conv(DevMat W, const int8_t* act, const float* sx, int M, float* proj, LayerW w, int l, Caches c,
+                             int hist_base, const float* cosr, const float* sinr, float* qbuf, cudaStream_t st);
 // window: the layer's band (0 = all); sink, ring: the attention span
 // (ring 0 = none; infer.rs:1749-1825).
 void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int S, int T, int p0, int window, int sink,
