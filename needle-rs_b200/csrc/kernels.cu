@@ -1281,14 +1281,24 @@ void launch_conv_rope_kv(LayerW w, int l, const float* proj, Caches c, int S, in
 // and the merge (2143-2166); then the gate (1548-1552).
 constexpr int ATT_MAXCHUNK = 256, ATT_MAXPARTS = ATT_MAX_KEYS / ATT_MAXCHUNK;
 
+// a / b for 0 <= a < 2^24 and 0 < b: a float quotient, then one step of
+// correction each way, exact (the integer divide's generic sequence is
+// several times longer, and every warp of the attention kernel runs these)
+__device__ __forceinline__ int small_div(int a, int b) {
+    int q = (int)__fdividef((float)a, (float)b);
+    if ((q + 1) * b <= a) q++;
+    if (q * b > a) q--;
+    return q;
+}
+
 __device__ __forceinline__ void key_chunks_dev(int n, bool nested, int* count, int* chunk) {
     int k = nested ? 1 : 4;  // (2 * NATIVE_TEAM / nkv).max(1), NATIVE_TEAM = 4, nkv = 2
     int c = (n + 255) / 256;
     if (k * 64 <= n && c < k) c = k;
     int cm = c > 1 ? c : 1;
-    int ch = ((n + cm - 1) / cm + 15) / 16 * 16;
+    int ch = (small_div(n + cm - 1, cm) + 15) / 16 * 16;
     *chunk = ch;
-    *count = ch > 0 ? (n + ch - 1) / ch : 0;
+    *count = ch > 0 ? small_div(n + ch - 1, ch) : 0;
 }
 
 // One CTA per (row, kv head) serves the kv head's 6 query heads: the chunk's
@@ -1360,7 +1370,7 @@ __global__ void __launch_bounds__(ATT_THREADS, MINB) attention_kernel(const floa
     extern __shared__ __align__(16) int8_t att_raw[];
     AttSmem& sm = *reinterpret_cast<AttSmem*>(att_raw);
     const int m = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x, lane = tid & 31, h = tid >> 5;
-    const int s = m / T, i = m % T, pos = p0 + i;
+    const int s = T == 1 ? m : m / T, i = T == 1 ? 0 : m % T, pos = p0 + i;
     const bool nested = T > 1;
     // infer.rs:1781-1825 (key_ranges): the keys as runs of positions, A =
     // [aS, aE) then B = [bS, bE). Without an attention span A is the layer's
