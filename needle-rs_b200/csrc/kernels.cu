@@ -1153,7 +1153,7 @@ __global__ void __launch_bounds__(512 / UPW, 8 / (3 - UPW)) conv_rope_kv_kernel(
     const int p0 = *p0p;
     __shared__ float buf[16][64];
     const int m = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int s = m / T, i = m % T, pos = p0 + i;
+    const int s = T == 1 ? m : m / T, i = T == 1 ? 0 : m % T, pos = p0 + i;
     const size_t hrow0 = ((size_t)s * c.L + l) * HIST_RING;
     // every row load of the lane's (at most two) channels of the warp's
     // units first, then the tap weights (cache-resident), history writes
