@@ -1331,6 +1331,8 @@ struct AttSmem {
     // loads of four consecutive groups fall in four distinct bank octets
     int vg[ATT_MAXGROUPS][64];
     float ks[ATT_MAXCHUNK], vs[ATT_MAXCHUNK];
+    // per head: the P.V plane sums on their way to the lanes that own
+    // them (3 x 72 words), at the end the gated outputs (6 x 64 in all)
     float s[ATT_HEADS][ATT_MAXCHUNK];
     // digit plane (hi, mid, lo) of value group g: one word, the four
     // positions 4g..4g+3 in its bytes
@@ -1598,8 +1600,8 @@ __global__ void __launch_bounds__(ATT_THREADS, MINB) attention_kernel(const floa
                     mma_s8_acc(acc[t], a, b);
                 }
             }
-            // plane p's sums of dimension d go through the score row (done
-            // with) to the lanes that own them: D (d, p) is lane (d % 8,
+            // plane p's sums of dimension d go through the head's scratch row
+            // to the lanes that own them: D (d, p) is lane (d % 8,
             // p / 2), element p % 2 (+ 2 for d % 16 >= 8)
             int* scr = reinterpret_cast<int*>(srow);
 #pragma unroll
