@@ -1723,17 +1723,19 @@ void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int
 // seven; each CTA's time shrinks with its rows). The layer's small
 // weights (Kronecker factors, conditioning, diagonals, norms, permutations)
 // are staged once into shared memory with cp.async, so every phase reads
-// shared memory only. A row's 1024-wide vectors use a padded layout
-// (element p at (p / 32) * 36 + p % 32) and ping-pong between two buffers.
-// The weights are requested before the predecessor kernel has finished, the
-// rows' o, x1 and gates right after; u arrives during the Kronecker stages
-// into the space of cond_v, whose last use is the conditioning logits. The
-// post and residual gates (hpost, Sinkhorn) were computed by the mHC read.
+// shared memory only (but the mHC write's inputs). A row's 1024-wide
+// vectors use a padded layout (element p at (p / 32) * 36 + p % 32) and
+// ping-pong between two buffers. The weights are requested before the
+// predecessor kernel has finished, the rows' o, x1 and gates right after;
+// u and the old streams are read by the mHC write itself, a round ahead
+// (staging u in shared memory stalled its copies' issue for 1.9 K cycles).
+// The post and residual gates (hpost, Sinkhorn) were computed by the mHC
+// read.
 constexpr int PV = 32 * 36 + 8;
 template <int POST_ROWS>
 struct PostSmem {
     float kf[6][1024];
-    __align__(16) float cond_v[32 * COND_LD];  // later the rows' u
+    __align__(16) float cond_v[32 * COND_LD];
     float cond_u[8 * 1024];
     float d1[768], d2[1024], b2[1024], d3[1024], d4[768];
     float post_norm[768], pre_hada[768];
@@ -1971,14 +1973,6 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
         kron_stage_row(sm, 0, 1, 0, (tid >> 5) - POST_ROWS, tid & 31);
     }
     __syncthreads();
-    // cond_v is done with: the rows' u arrive there during the MLP
-    float* us = sm.cond_v;
-    for (int k = tid; k < POST_ROWS * 192; k += POST_THREADS) {
-        const int q = k / 192, c = k % 192;
-        const bool ok = q < rows;
-        cp_async16(us + q * 768 + 4 * c, u + (size_t)(ok ? m0 + q : 0) * 768 + 4 * c, ok);
-    }
-    asm volatile("cp.async.commit_group;\n" ::);
     if (tid < POST_ROWS * 32) {
         // logits ((C + D) + B) + A, max, one libm exp per lane, the engine's
         // sum tree e7 + ((e6 + (e5 + e4)) + ((e3 + e2) + (e1 + e0)))
@@ -2039,17 +2033,19 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
     __syncthreads();
     // mHC write (infer.rs:1587-1606): y = x2 + mlp - u, stream a =
     // y * hpost[a] + sum_b old[b] * hres[a][b]. Four (row, channel) items a
-    // thread per round, each round's 16 stream loads issued before the
-    // previous round's arithmetic (the first round's before the last
-    // Kronecker stage).
+    // thread per round, each round's loads (four old streams and u an item)
+    // issued before the previous round's arithmetic (the first round's
+    // before the last Kronecker stage).
     constexpr int ITEMS = POST_ROWS * 768 / POST_THREADS, BATCH = 4;
     static_assert(ITEMS % BATCH == 0, "item batches");
-    float cur[BATCH][4], nxt[BATCH][4];
+    float cur[BATCH][5], nxt[BATCH][5];  // per item the four old streams, then u
 #define POST_LOAD_OLD(dst, it0)                                                                       \
     _Pragma("unroll") for (int e = 0; e < BATCH; e++) {                                               \
         const int k = tid + ((it0) + e) * POST_THREADS, q = k / 768, ch = k % 768;                    \
-        const float* xr = xs + (size_t)(m0 + (q < rows ? q : 0)) * 3072 + ch;                         \
+        const size_t mq = (size_t)(m0 + (q < rows ? q : 0));                                          \
+        const float* xr = xs + mq * 3072 + ch;                                                        \
         _Pragma("unroll") for (int b = 0; b < 4; b++) dst[e][b] = xr[b * 768];                        \
+        dst[e][4] = u[mq * 768 + ch];                                                                 \
     }
     POST_LOAD_OLD(cur, 0)  // in flight during the last Kronecker stage
     if (tid < POST_ROWS * 32) kron_stage_row(sm, 4, 5, 0, tid >> 5, tid & 31);  // t3 in buf[0]
@@ -2066,7 +2062,7 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
             if (q >= rows) continue;
             const float* gr = sm.gates[q];
             float mlp = __fmul_rn(sm.buf[0][q][pv_idx(ch)], sm.d4[ch]);
-            float y = __fsub_rn(__fadd_rn(sm.x2[q][ch], mlp), us[q * 768 + ch]);
+            float y = __fsub_rn(__fadd_rn(sm.x2[q][ch], mlp), cur[e][4]);
             float* xr = xs + (size_t)(m0 + q) * 3072 + ch;
 #pragma unroll
             for (int a = 0; a < 4; a++) {
@@ -2079,7 +2075,7 @@ __global__ void __launch_bounds__(POST_THREADS, 1) post_block_kernel(LayerW w, c
 #pragma unroll
         for (int e = 0; e < BATCH; e++)
 #pragma unroll
-            for (int b = 0; b < 4; b++) cur[e][b] = nxt[e][b];
+            for (int b = 0; b < 5; b++) cur[e][b] = nxt[e][b];
     }
 #undef POST_LOAD_OLD
 }
