@@ -687,14 +687,22 @@ static int chunk(Batch& b, const int32_t* ids, int T, int outputs) {
     }
     launch_embed(m.embedding, ids, M, b.xs, st);
     if (b.recording) launch_record_cells(b.xs, S, T, p0, 0, c.L + 1, b.cells_cap, b.cells, st);
+    // batches of at most one row an SM run each layer's post block and the
+    // next layer's mHC read in one launch (the cells a recording batch
+    // keeps, and the debug snapshots, read xs and the layer's buffers
+    // before or after that launch as they would around the post block)
+    const bool fuse_post_mhc = M <= device_sm_count();
+    bool mhc_done = false;  // this layer's mHC read ran with the last post block
     for (int l = 0; l < c.L; l++) {
         const LayerW& w = m.layers[l];
         const int lane = l % 4, site = m.site_of_layer[l];
-        if (site >= 0) CK(cudaStreamWaitEvent(st, b.ev_site[site], 0));
-        tick(b, ND_SITE_MHC);
-        launch_mhc_read(w, lane, b.xs, M, b.u, b.p, site >= 0 ? b.ekv + (size_t)site * b.Mmax * 1536 : nullptr,
-                        site >= 0 ? b.evals + (size_t)site * b.Mmax * 768 : nullptr, b.x1, b.act, b.sx, st);
-        tick(b, ND_SITE_MHC);
+        if (!mhc_done) {
+            if (site >= 0) CK(cudaStreamWaitEvent(st, b.ev_site[site], 0));
+            tick(b, ND_SITE_MHC);
+            launch_mhc_read(w, lane, b.xs, M, b.u, b.p, site >= 0 ? b.ekv + (size_t)site * b.Mmax * 1536 : nullptr,
+                            site >= 0 ? b.evals + (size_t)site * b.Mmax * 768 : nullptr, b.x1, b.act, b.sx, st);
+            tick(b, ND_SITE_MHC);
+        }
         CK(cudaEventRecord(b.ev_mhc[l], st));
         CK(cudaStreamWaitEvent(b.st3, b.ev_mhc[l], 0));
         launch_mhc_gates(w, lane, M, b.p, b.st3);
@@ -729,8 +737,17 @@ static int chunk(Batch& b, const int32_t* ids, int T, int outputs) {
             snap(b, "snap.att", b.att, (size_t)M * 768);
             snap(b, "snap.o", b.o, (size_t)M * 768);
         }
+        mhc_done = fuse_post_mhc && l + 1 < c.L;
         tick(b, ND_SITE_POST);
-        launch_post_block(w, b.o, b.x1, b.u, b.p, m.perm1, m.perm2, M, b.xs, st);
+        if (mhc_done) {
+            const int ln = l + 1, nsite = m.site_of_layer[ln];
+            if (nsite >= 0) CK(cudaStreamWaitEvent(st, b.ev_site[nsite], 0));
+            CK(launch_post_mhc(w, b.o, b.x1, b.u, b.p, m.perm1, m.perm2, M, b.xs, m.layers[ln], ln % 4, b.u, b.p,
+                               nsite >= 0 ? b.ekv + (size_t)nsite * b.Mmax * 1536 : nullptr,
+                               nsite >= 0 ? b.evals + (size_t)nsite * b.Mmax * 768 : nullptr, b.x1, b.act, b.sx, st));
+        } else {
+            launch_post_block(w, b.o, b.x1, b.u, b.p, m.perm1, m.perm2, M, b.xs, st);
+        }
         tick(b, ND_SITE_POST);
         if (b.recording) launch_record_cells(b.xs, S, T, p0, l + 1, c.L + 1, b.cells_cap, b.cells, st);
         if (l == b.debug_layer) snap(b, "snap.xs", b.xs, (size_t)M * 3072);

@@ -71,6 +71,8 @@ static int sm_count() {
     return v;
 }
 
+int device_sm_count() { return sm_count(); }
+
 // --------------------------------------------------------------- tokens
 
 __global__ void write_tokens_kernel(const int32_t* ids, int S, int T, const int32_t* p0p, int32_t* tokens, int cap) {
@@ -798,23 +800,31 @@ __device__ __forceinline__ int reduce4_scatter(const int s[4], int ln) {
     return r;
 }
 
-// infer.rs:1359-1426 for one row per CTA. The lanes are normalized by one
-// rms and quantized to int8 (no rotation) in registers; the 24 int8 gate
-// dots are per-thread dp4a partials over 16-byte runs of the gate rows,
-// reduced exactly across the CTA. Then warp 5 stores the post block's gate
-// projections for mhc_gates_kernel while warps
+// The mHC read's block barrier: PART when its MHC_THREADS threads are part
+// of a wider CTA whose other threads may have left.
+template <bool PART>
+__device__ __forceinline__ void mhc_bar() {
+    if (PART)
+        asm volatile("bar.sync 2, %0;\n" ::"n"(MHC_THREADS) : "memory");
+    else
+        __syncthreads();
+}
+
+// infer.rs:1359-1426 for row m, by threads 0 .. MHC_THREADS - 1 of a CTA
+// (MINB: the CTAs an SM its launch bounds allow). The lanes are normalized
+// by one rms and quantized to int8 (no rotation) in registers; the 24 int8
+// gate dots are per-thread dp4a partials over 16-byte runs of the gate
+// rows, reduced exactly across the CTA. Then warp 5 stores the post block's
+// gate projections for mhc_gates_kernel while warps
 // 0-4 form u from the pre gates, apply the engram gate (when the layer has a
 // site: ekv [M][1536] keys, evals [M][768]), the input ZC-RMSNorm and A8 of
 // the normed row (act/sx for the q|k|v|gate matmul; x1o is the residual).
-template <int MINB>
-__global__ void __launch_bounds__(MHC_THREADS, MINB) mhc_read_kernel(LayerW w, int lane_own, const float* xs, float* u, float* p,
-                                                                  const float* ekv, const float* evals, float* x1o, int8_t* act,
-                                                                  float* sx) {
+template <int MINB, bool PART = false>
+__device__ __forceinline__ void mhc_read_row(const LayerW& w, int lane_own, const float* xs, float* u, float* p, const float* ekv,
+                                             const float* evals, float* x1o, int8_t* act, float* sx, int m) {
     // dot16 operands loaded 16 at a time in the eight-CTA variant (42
     // registers), all 48 at once in the other
     constexpr int MHC_B16 = MINB == 1 ? 48 : 16;
-    pdl_launch_dependents();
-    pdl_wait();
     // the four streams chain-major: element e at (e % 16) * MHC_XS + e / 16,
     // so each of the sixteen chains of the rms dot reads 16-byte runs;
     // later the norm's scratch rows
@@ -826,7 +836,7 @@ __global__ void __launch_bounds__(MHC_THREADS, MINB) mhc_read_kernel(LayerW w, i
     __shared__ float part[32];
     __shared__ float hp[4];
     __shared__ float sc_s[4];
-    const int m = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, ln = tid & 31;
+    const int tid = threadIdx.x, warp = tid >> 5, ln = tid & 31;
     // the input norm's operands, fetched by the threads that will use them
     if (tid < MHC_NORM_THREADS) {
         for (int k = tid; k < 192; k += MHC_NORM_THREADS) {
@@ -852,14 +862,14 @@ __global__ void __launch_bounds__(MHC_THREADS, MINB) mhc_read_kernel(LayerW w, i
 #pragma unroll
         for (int j = 0; j < 16; j++) xt[j * MHC_XS + tid] = v[j];  // element 16 tid + j
     }
-    __syncthreads();
+    mhc_bar<PART>();
     if (warp == 0) {
         float acc = 0.f;
         if (ln < 16) acc = sq_chain<192, MINB == 1>(xt + ln * MHC_XS);
         float ss = dot16_combine_warp(acc, ln);
         if (ln == 0) sc_s[0] = rinv(ss, 3072);
     }
-    __syncthreads();
+    mhc_bar<PART>();
     const float r = sc_s[0];
     float a = 0.f;
     {
@@ -871,7 +881,7 @@ __global__ void __launch_bounds__(MHC_THREADS, MINB) mhc_read_kernel(LayerW w, i
         a = warp_max(a);
         if (ln == 0) red[warp] = a;
     }
-    __syncthreads();
+    mhc_bar<PART>();
     float mx = red[0];
 #pragma unroll
     for (int k = 1; k < 6; k++) mx = fmaxf(mx, red[k]);
@@ -899,7 +909,7 @@ __global__ void __launch_bounds__(MHC_THREADS, MINB) mhc_read_kernel(LayerW w, i
             if ((ln & 7) == 0) red24[warp][bt * 4 + ((ln & 16) ? 2 : 0) + ((ln & 8) ? 1 : 0)] = tot;
         }
     }
-    __syncthreads();
+    mhc_bar<PART>();
     if (warp == 5) {
         // the post block's gate projections (pr[4..23]) into gates[m][4..23];
         // mhc_gates_kernel turns them into hpost and the Sinkhorn matrix
@@ -978,6 +988,15 @@ __global__ void __launch_bounds__(MHC_THREADS, MINB) mhc_read_kernel(LayerW w, i
         for (int k = 0; k < 4; k++) vv[k] = na[gw * 128 + 4 * ln + k];
         prep_group_warp(vv, ln, act + ((size_t)m * 6 + gw) * 128, sx + (size_t)m * 6 + gw);
     }
+}
+
+template <int MINB>
+__global__ void __launch_bounds__(MHC_THREADS, MINB) mhc_read_kernel(LayerW w, int lane_own, const float* xs, float* u, float* p,
+                                                                  const float* ekv, const float* evals, float* x1o, int8_t* act,
+                                                                  float* sx) {
+    pdl_launch_dependents();
+    pdl_wait();
+    mhc_read_row<MINB>(w, lane_own, xs, u, p, ekv, evals, x1o, act, sx, blockIdx.x);
 }
 
 void launch_mhc_read(LayerW w, int lane, const float* xs, int M, float* u, float* p, const float* ekv, const float* evals,
@@ -2149,13 +2168,14 @@ __device__ __forceinline__ void kron_row_pass2(const float* mt, const float* B, 
         *(float4*)(t + (r0 + a) * 32 + c0) = make_float4(o[a][0].x, o[a][0].y, o[a][1].x, o[a][1].y);
 }
 
-__global__ void __launch_bounds__(POST_ROW_THREADS, 1) post_row_kernel(LayerW w, const float* o, const float* x1, const float* u,
-                                                                 const float* gates, const int32_t* perm1, const int32_t* perm2,
-                                                                 float* xs) {
+// The one-row post block of row m by a CTA of POST_ROW_THREADS threads
+// with PostRowSmem as its dynamic shared memory.
+__device__ __forceinline__ void post_row_row(const LayerW& w, const float* o, const float* x1, const float* u, const float* gates,
+                                             const int32_t* perm1, const int32_t* perm2, float* xs, int m) {
     pdl_launch_dependents();
     extern __shared__ __align__(16) int8_t post_row_raw[];
     PostRowSmem& sm = *reinterpret_cast<PostRowSmem*>(post_row_raw);
-    const int tid = threadIdx.x, m = blockIdx.x;
+    const int tid = threadIdx.x;
     // the Kronecker passes run on warps 1-4 (warp 0 has the conditioning chains)
     const int kt = tid - 32, r0 = 2 * (kt & 15), c0 = 4 * (kt >> 4);
     const bool kw = kt >= 0 && kt < 128;
@@ -2272,6 +2292,29 @@ __global__ void __launch_bounds__(POST_ROW_THREADS, 1) post_row_kernel(LayerW w,
     }
 }
 
+__global__ void __launch_bounds__(POST_ROW_THREADS, 1) post_row_kernel(LayerW w, const float* o, const float* x1, const float* u,
+                                                                 const float* gates, const int32_t* perm1, const int32_t* perm2,
+                                                                 float* xs) {
+    post_row_row(w, o, x1, u, gates, perm1, perm2, xs, blockIdx.x);
+}
+
+// The post block of one layer and the mHC read of the next for the same
+// row, one CTA a row (batches of at most one row an SM): one launch fewer a
+// layer. The post block has staged this layer's u, x1 and gates before the
+// mHC read overwrites those buffers with the next layer's, and the row's
+// new streams it wrote to xs are visible to the CTA's threads after the
+// barrier. Each value is computed as post_row_kernel and mhc_read_kernel
+// compute it.
+__global__ void __launch_bounds__(POST_ROW_THREADS, 1) post_mhc_kernel(LayerW w, const float* o, const float* x1, const float* u,
+                                                                 const float* gates, const int32_t* perm1, const int32_t* perm2,
+                                                                 float* xs, LayerW wn, int lane_next, float* un, float* pn,
+                                                                 const float* ekv, const float* evals, float* x1n, int8_t* act,
+                                                                 float* sx) {
+    post_row_row(w, o, x1, u, gates, perm1, perm2, xs, blockIdx.x);
+    __syncthreads();
+    if (threadIdx.x < MHC_THREADS) mhc_read_row<1, true>(wn, lane_next, xs, un, pn, ekv, evals, x1n, act, sx, blockIdx.x);
+}
+
 void launch_post_block(LayerW w, const float* o, const float* x1, const float* u, const float* gates, const int32_t* perm1,
                        const int32_t* perm2, int M, float* xs, cudaStream_t st) {
     COUNT_LAUNCH();
@@ -2289,7 +2332,18 @@ void launch_post_block(LayerW w, const float* o, const float* x1, const float* u
     }
 }
 
+cudaError_t launch_post_mhc(LayerW w, const float* o, const float* x1, const float* u, const float* gates, const int32_t* perm1,
+                            const int32_t* perm2, int M, float* xs, LayerW wn, int lane_next, float* un, float* pn, const float* ekv,
+                            const float* evals, float* x1n, int8_t* act, float* sx, cudaStream_t st) {
+    if (M < 1 || M > sm_count()) return cudaErrorInvalidValue;
+    COUNT_LAUNCH();
+    launch_pdl(post_mhc_kernel, dim3(M), dim3(POST_ROW_THREADS), POST_ROW_SMEM, st, w, o, x1, u, gates, perm1, perm2, xs, wn, lane_next,
+               un, pn, ekv, evals, x1n, act, sx);
+    return cudaSuccess;
+}
+
 cudaError_t post_block_init() {
+    cudaFuncSetAttribute(post_mhc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)POST_ROW_SMEM);
     cudaFuncSetAttribute(post_block_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PostSmem<2>));
     cudaFuncSetAttribute(post_block_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PostSmem<4>));
     return cudaFuncSetAttribute(post_block_kernel<7>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PostSmem<7>));

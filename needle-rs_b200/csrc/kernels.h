@@ -94,6 +94,8 @@ constexpr int ROPE_RING = 33;
 // The longest key list the attention kernel takes: 32 key chunks of 256.
 constexpr int ATT_MAX_KEYS = 8192;
 
+// The current device's SM count (looked up once per device).
+int device_sm_count();
 // Kernels this process has launched through the launchers below.
 long long launch_count();
 // Kernels a replayed CUDA graph launched (counted with the others).
@@ -159,6 +161,14 @@ void launch_attention(const float* qbuf, const float* proj, Caches c, int l, int
                       int ring, float* att, int8_t* act, float* sx, cudaStream_t st);
 void launch_post_block(LayerW w, const float* o, const float* x1, const float* u, const float* gates, const int32_t* perm1,
                        const int32_t* perm2, int M, float* xs, cudaStream_t st);
+// The post block of a layer (w) and the mHC read of the next (wn, lane
+// lane_next, its engram rows ekv/evals or NULL) for the same M rows, as
+// launch_post_block then launch_mhc_read compute them, in one launch:
+// batches of at most one row an SM (cudaErrorInvalidValue, nothing
+// launched, otherwise). u/un, x1/x1n and gates/pn may be the same buffers.
+cudaError_t launch_post_mhc(LayerW w, const float* o, const float* x1, const float* u, const float* gates, const int32_t* perm1,
+                            const int32_t* perm2, int M, float* xs, LayerW wn, int lane_next, float* un, float* pn, const float* ekv,
+                            const float* evals, float* x1n, int8_t* act, float* sx, cudaStream_t st);
 void launch_final_hidden(const float* xs, const float* final_norm, int S, int T, int all_rows, float* h, cudaStream_t st);
 void launch_rope_rows(const float* table_cos, const float* table_sin, const float* sd, const float* cd, const int32_t* p0p, int T,
                       int recur, float* state, float* cosr, float* sinr, cudaStream_t st);
