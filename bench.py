@@ -735,6 +735,9 @@ def main():
             b.step(masks[k])
         torch.cuda.synchronize()
         return
+    # Per-kernel sites. With at most one sequence an SM on a GPU (the
+    # 8-GPU partition), each layer's post block launch also runs the next
+    # layer's mHC read: "post" then includes it and "mhc" is layer 0's alone.
     sites = ["qkvg", "out", "lm_head", "engram_kv", "attention", "post", "mhc", "conv"]
     # The config's 45 steps: W warm-up, K timed, the rest untimed after them
     # (per-kernel site timing runs there); past 45 only when W + K leaves
