@@ -1,9 +1,10 @@
 """Build recipe for the CPU oracle (test infrastructure only).
 
-Compiles ``needle_oracle.cpp`` — the scalar C++ restatement of needle-rs's
-packed CPU path — into ``oracle/liboracle.so``. Float contraction is off so
-every fused multiply-add is the explicit ``fmaf`` the reference's ``mul_add``
-calls for; ``-mfma`` only lets those calls compile to the hardware instruction.
+Compiles ``needle_oracle.cpp`` — the C++ restatement of needle-rs's packed
+CPU path — into ``oracle/liboracle.so``. Float contraction is off so every
+fused multiply-add is the explicit ``fmaf`` (or vector fma, one rounding a
+lane) the reference's ``mul_add`` calls for; ``-mfma -mavx2`` let those
+compile to the hardware instructions and enable the vector integer sums.
 """
 
 import os

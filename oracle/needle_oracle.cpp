@@ -1,8 +1,8 @@
 // TEST INFRASTRUCTURE ONLY — never linked into or called by the product path.
 //
-// A scalar C++ restatement of ddrscott/needle-rs's packed CPU inference path
-// (the native-exact `needle-engine` forward pass on a `.cact` archive), used
-// by tests/ as the parity checker for the CUDA engine and by bench.py as the
+// A C++ restatement of ddrscott/needle-rs's packed CPU inference path (the
+// native-exact `needle-engine` forward pass on a `.cact` archive), used by
+// tests/ as the parity checker for the CUDA engine and by bench.py as the
 // timed CPU baseline ("port"). The reference is Rust and cannot be built in
 // this image (no cargo/rustc), so this file restates its arithmetic from the
 // source. Every function names the reference file:line it follows; paths are
@@ -13,6 +13,13 @@
 // Float discipline: compiled with -ffp-contract=off; every `mul_add` of the
 // reference is an explicit fmaf here, every other op is a single IEEE op in
 // the reference's order. Integer sums are exact and computed in any order.
+// Where the build has AVX2 the hot loops run vectorised without changing a
+// result: the int8 lane sums and dots (4-bit codes looked up from their
+// packed bytes; int16 pair products summed into int32, no saturation), the
+// decode combine eight rows side by side and the Kronecker passes eight
+// outputs side by side (each row's or output's float ops the same single
+// roundings in the same order). orc_lane_sums_check compares the vector
+// integer sums with the plain loops.
 // libm stand-ins follow the reference's non-Apple `sys` module
 // (crates/needle-engine/src/infer.rs:83-102): f32 exp/pow/sincos are f64 libm
 // rounded once; this file uses glibc's f64 functions where the reference links
@@ -30,6 +37,9 @@
 #include <algorithm>
 #include <functional>
 #include <stdexcept>
+#if defined(__AVX2__)
+#include <immintrin.h>
+#endif
 
 namespace orc {
 
@@ -405,6 +415,7 @@ struct QMat {
     int width = 4;               // bits per code in memory
     std::vector<uint8_t> codes;  // [out][groups][16 * width]
     std::vector<uint16_t> norms; // [out][groups] f16 bits
+    std::vector<float> normf;    // the same norms widened (exact)
     std::vector<int8_t> w8;      // codes expanded through `vals`, natural order
     std::vector<QPart> parts;
     const QPart& part(int r) const {
@@ -438,6 +449,8 @@ static void qmat_init(QMat& q, int bits, int out, int in_dim, const uint8_t* cod
     const size_t bpg = 16 * (size_t)q.width, ncode = (size_t)out * q.groups * bpg;
     q.codes.assign(codes, codes + ncode);
     q.norms.assign(norms, norms + (size_t)out * q.groups);
+    q.normf.resize(q.norms.size());
+    for (size_t i = 0; i < q.norms.size(); i++) q.normf[i] = f16_to_f32(q.norms[i]);
     std::vector<float> cb = codebook(bits, GROUP);
     int8_t cb8[16];
     QPart pt;
@@ -481,6 +494,7 @@ static void qmat_concat(QMat& dst, const QMat& src) {
     dst.out += src.out;
     dst.codes.insert(dst.codes.end(), src.codes.begin(), src.codes.end());
     dst.norms.insert(dst.norms.end(), src.norms.begin(), src.norms.end());
+    dst.normf.insert(dst.normf.end(), src.normf.begin(), src.normf.end());
     dst.w8.insert(dst.w8.end(), src.w8.begin(), src.w8.end());
 }
 
@@ -505,6 +519,9 @@ struct QAct {
     int rows = 0, groups = 0;
     std::vector<int8_t> xq;  // [rows][groups*128], natural order
     std::vector<float> sx;   // [rows][groups]
+    // xq widened to int16, each 32-wide block as its 16 even elements then
+    // its 16 odd ones (the order the 4-bit code bytes hold the weights in)
+    std::vector<int16_t> xeo;
 };
 
 // qlinear.rs:152-164
@@ -527,15 +544,20 @@ static QAct qact_new(const float* x, int rows, int in_dim) {
         for (int g = 0; g < a.groups; g++)
             a.sx[(size_t)r * a.groups + g] =
                 prep_group(x + (size_t)r * in_dim, in_dim, g, a.xq.data() + ((size_t)r * a.groups + g) * GROUP);
+    a.xeo.resize(a.xq.size());
+    for (size_t b = 0; b < a.xq.size(); b += 32)
+        for (int j = 0; j < 16; j++) {
+            a.xeo[b + j] = a.xq[b + 2 * j];
+            a.xeo[b + 16 + j] = a.xq[b + 2 * j + 1];
+        }
     return a;
 }
 
-// qlinear.rs:327-337: the 4 decode lanes of one group; lane = (p % 64) / 16
-// for 2-bit codes, (p % 32) / 8 otherwise.
-static inline void lane_sums(const QMat& q, int r, int g, const QAct& a, int t, int32_t s[4]) {
-    const int8_t* w = q.w8.data() + ((size_t)r * q.groups + g) * GROUP;
-    const int8_t* x = a.xq.data() + ((size_t)t * a.groups + g) * GROUP;
-    if (q.width == 2) {  // lane l: p = 64h + 16l + b
+// qlinear.rs:327-337: the 4 decode lanes of one group of 128 int8 weights
+// w and activations x (natural order); lane = (p % 64) / 16 for 2-bit
+// codes, (p % 32) / 8 otherwise.
+static inline void lane_sums_scalar(const int8_t* w, const int8_t* x, int width, int32_t s[4]) {
+    if (width == 2) {  // lane l: p = 64h + 16l + b
         for (int l = 0; l < 4; l++) {
             int32_t acc = 0;
             for (int h = 0; h < 2; h++) {
@@ -558,14 +580,118 @@ static inline void lane_sums(const QMat& q, int r, int g, const QAct& a, int t, 
     }
 }
 
+#if defined(__AVX2__)
+static inline int32_t hsum_i32x4(__m128i v) {
+    v = _mm_add_epi32(v, _mm_shuffle_epi32(v, 0x4E));
+    v = _mm_add_epi32(v, _mm_shuffle_epi32(v, 0xB1));
+    return _mm_cvtsi128_si32(v);
+}
+
+// lane_sums_scalar's integer sums, sixteen products at a time: int8 widened
+// to int16, adjacent products summed into int32 (vpmaddwd, exact: no
+// saturation), a lane's pair sums added at the end. Integer addition is
+// exact in any order, so the sums are the scalar ones.
+static inline void lane_sums_avx2(const int8_t* w, const int8_t* x, int width, int32_t s[4]) {
+    auto prod16 = [](const int8_t* a, const int8_t* b) {
+        __m256i a16 = _mm256_cvtepi8_epi16(_mm_loadu_si128((const __m128i*)a));
+        __m256i b16 = _mm256_cvtepi8_epi16(_mm_loadu_si128((const __m128i*)b));
+        return _mm256_madd_epi16(a16, b16);  // int32 i: products 2i and 2i + 1
+    };
+    if (width == 2) {  // lane l: bytes 64h + 16l .. + 15
+        for (int l = 0; l < 4; l++) {
+            __m256i acc = _mm256_add_epi32(prod16(w + l * 16, x + l * 16), prod16(w + 64 + l * 16, x + 64 + l * 16));
+            s[l] = hsum_i32x4(_mm_add_epi32(_mm256_castsi256_si128(acc), _mm256_extracti128_si256(acc, 1)));
+        }
+        return;
+    }
+    // lane l: bytes 32a + 8l .. + 7; a 16-byte half of a 32-byte block
+    // holds two lanes, one in each 128-bit half of the int32 pair sums
+    __m256i a01 = _mm256_setzero_si256(), a23 = _mm256_setzero_si256();
+    for (int blk = 0; blk < 4; blk++) {
+        a01 = _mm256_add_epi32(a01, prod16(w + blk * 32, x + blk * 32));
+        a23 = _mm256_add_epi32(a23, prod16(w + blk * 32 + 16, x + blk * 32 + 16));
+    }
+    s[0] = hsum_i32x4(_mm256_castsi256_si128(a01));
+    s[1] = hsum_i32x4(_mm256_extracti128_si256(a01, 1));
+    s[2] = hsum_i32x4(_mm256_castsi256_si128(a23));
+    s[3] = hsum_i32x4(_mm256_extracti128_si256(a23, 1));
+}
+#endif
+
+// Σ a[e] b[e] over n int8 pairs, exact (int32; any order).
+static inline int32_t dot_i8(const int8_t* a, const int8_t* b, int n) {
+    int e = 0;
+    int32_t acc = 0;
+#if defined(__AVX2__)
+    __m256i v = _mm256_setzero_si256();
+    for (; e + 16 <= n; e += 16)
+        v = _mm256_add_epi32(v, _mm256_madd_epi16(_mm256_cvtepi8_epi16(_mm_loadu_si128((const __m128i*)(a + e))),
+                                                  _mm256_cvtepi8_epi16(_mm_loadu_si128((const __m128i*)(b + e)))));
+    acc = hsum_i32x4(_mm_add_epi32(_mm256_castsi256_si128(v), _mm256_extracti128_si256(v, 1)));
+#endif
+    for (; e < n; e++) acc += (int32_t)a[e] * (int32_t)b[e];
+    return acc;
+}
+
+static inline void lane_sums_of(const int8_t* w, const int8_t* x, int width, int32_t s[4]) {
+#if defined(__AVX2__)
+    lane_sums_avx2(w, x, width, s);
+#else
+    lane_sums_scalar(w, x, width, s);
+#endif
+}
+
+#if defined(__AVX2__)
+// The lane sums of a 4-bit group read from its 64 code bytes (byte k holds
+// the codes of p = 2k, low nibble, and 2k + 1) against the group's
+// activations as QAct::xeo holds them: the codebook's int8 values looked up
+// sixteen at a time (pshufb) for the even and for the odd elements of a
+// 32-wide block, widened, multiplied with the matching activations and
+// summed in pairs into int32 (vpmaddwd, exact); in a block, code bytes
+// 4l .. 4l + 3 are lane l's, so int32 pair sums 2l and 2l + 1 are too. The
+// same exact integers as expanding the codes through `vals` first.
+static inline void lane_sums_codes4_avx2(const uint8_t* codes, const int8_t* vals, const int16_t* xeo, int32_t s[4]) {
+    const __m128i tbl = _mm_loadu_si128((const __m128i*)vals), m4 = _mm_set1_epi8(0x0F);
+    __m256i acc = _mm256_setzero_si256();
+    for (int blk = 0; blk < 4; blk++) {
+        const __m128i c = _mm_loadu_si128((const __m128i*)(codes + 16 * blk));
+        const __m256i we = _mm256_cvtepi8_epi16(_mm_shuffle_epi8(tbl, _mm_and_si128(c, m4)));
+        const __m256i wo = _mm256_cvtepi8_epi16(_mm_shuffle_epi8(tbl, _mm_and_si128(_mm_srli_epi16(c, 4), m4)));
+        acc = _mm256_add_epi32(acc, _mm256_madd_epi16(we, _mm256_loadu_si256((const __m256i*)(xeo + 32 * blk))));
+        acc = _mm256_add_epi32(acc, _mm256_madd_epi16(wo, _mm256_loadu_si256((const __m256i*)(xeo + 32 * blk + 16))));
+    }
+    const __m256i h = _mm256_hadd_epi32(acc, acc);  // lanes 0, 1 in the low half, 2, 3 in the high
+    alignas(32) int32_t v[8];
+    _mm256_store_si256((__m256i*)v, h);
+    s[0] = v[0];
+    s[1] = v[1];
+    s[2] = v[4];
+    s[3] = v[5];
+}
+#endif
+
+// The lane sums of row r (part pt), group g against activation row t.
+static inline void lane_sums(const QMat& q, const QPart& pt, int r, int g, const QAct& a, int t, int32_t s[4]) {
+    const size_t ag = ((size_t)t * a.groups + g) * GROUP;
+#if defined(__AVX2__)
+    if (q.width == 4) {
+        lane_sums_codes4_avx2(q.codes.data() + ((size_t)r * q.groups + g) * 64, pt.vals, a.xeo.data() + ag, s);
+        return;
+    }
+#endif
+    (void)pt;
+    lane_sums_of(q.w8.data() + ((size_t)r * q.groups + g) * GROUP, a.xq.data() + ag, q.width, s);
+}
+
 // qlinear.rs:340-350
 float decode_row_ref(const QMat& q, int r, const QAct& a) {
-    const float cbs = q.part(r).cbs;
+    const QPart& pt = q.part(r);
+    const float cbs = pt.cbs;
     float lanes[4] = {0.f, 0.f, 0.f, 0.f};
     for (int g = 0; g < q.groups; g++) {
         int32_t s[4];
-        lane_sums(q, r, g, a, 0, s);
-        float sc = (a.sx[g] * cbs) * f16_to_f32(q.norms[(size_t)r * q.groups + g]);
+        lane_sums(q, pt, r, g, a, 0, s);
+        float sc = (a.sx[g] * cbs) * q.normf[(size_t)r * q.groups + g];
         for (int l = 0; l < 4; l++) lanes[l] = std::fmaf((float)s[l], sc, lanes[l]);
     }
     return (lanes[0] + lanes[1]) + (lanes[2] + lanes[3]);
@@ -573,25 +699,61 @@ float decode_row_ref(const QMat& q, int r, const QAct& a) {
 
 // qlinear.rs:353-363
 float prefill_row_ref(const QMat& q, int r, const QAct& a, int t, bool block) {
-    const float cbs = q.part(r).cbs;
+    const QPart& pt = q.part(r);
+    const float cbs = pt.cbs;
     float acc = 0.f;
     for (int g = 0; g < q.groups; g++) {
         int32_t s[4];
-        lane_sums(q, r, g, a, t, s);
+        lane_sums(q, pt, r, g, a, t, s);
         int32_t tot = s[0] + s[1] + s[2] + s[3];
         float sx = a.sx[(size_t)t * a.groups + g];
-        float norm = f16_to_f32(q.norms[(size_t)r * q.groups + g]);
+        float norm = q.normf[(size_t)r * q.groups + g];
         float sc = block ? (norm * cbs) * sx : norm * (cbs * sx);
         acc = std::fmaf((float)tot, sc, acc);
     }
     return acc;
 }
 
+// decode_row_ref for every row of q into y[0 .. q.out): with AVX2, eight
+// rows side by side, each row's floats the same single ops in the same
+// order (its scale product, its four lane fma chains over the groups, the
+// final two-level sum).
+static void decode_rows(const QMat& q, const QAct& a, float* y) {
+    int r = 0;
+#if defined(__AVX2__)
+    for (; r + 8 <= q.out; r += 8) {
+        const QPart* pts[8];
+        float cbs[8];
+        for (int k = 0; k < 8; k++) {
+            pts[k] = &q.part(r + k);
+            cbs[k] = pts[k]->cbs;
+        }
+        const __m256 cbv = _mm256_loadu_ps(cbs);
+        __m256 ln[4] = {_mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps()};
+        for (int g = 0; g < q.groups; g++) {
+            alignas(32) int32_t s[4][8];
+            alignas(32) float nf[8];
+            for (int k = 0; k < 8; k++) {
+                int32_t t4[4];
+                lane_sums(q, *pts[k], r + k, g, a, 0, t4);
+                for (int l = 0; l < 4; l++) s[l][k] = t4[l];
+                nf[k] = q.normf[(size_t)(r + k) * q.groups + g];
+            }
+            const __m256 sc = _mm256_mul_ps(_mm256_mul_ps(_mm256_set1_ps(a.sx[g]), cbv), _mm256_load_ps(nf));
+            for (int l = 0; l < 4; l++)
+                ln[l] = _mm256_fmadd_ps(_mm256_cvtepi32_ps(_mm256_load_si256((const __m256i*)s[l])), sc, ln[l]);
+        }
+        _mm256_storeu_ps(y + r, _mm256_add_ps(_mm256_add_ps(ln[0], ln[1]), _mm256_add_ps(ln[2], ln[3])));
+    }
+#endif
+    for (; r < q.out; r++) y[r] = decode_row_ref(q, r, a);
+}
+
 // qlinear.rs:366-419, 460-487: decode kernel for one token, prefill kernel
 // (block tokens t < T/4*4, remainder tokens after) for more.
 static void qmat_matmul(const QMat& q, const QAct& a, float* y, int ldy, int col0) {
     if (a.rows == 1) {
-        for (int r = 0; r < q.out; r++) y[col0 + r] = decode_row_ref(q, r, a);
+        decode_rows(q, a, y + col0);
     } else {
         int blocked = a.rows / 4 * 4;
         for (int t = 0; t < a.rows; t++)
@@ -984,10 +1146,7 @@ void attend_head_ref(const KVView& kv, const float* qh, int kvh, const std::vect
         const int64_t* sl = slots.data() + c0;
         int blocked = len / 4 * 4;
         for (int i = 0; i < len; i++) {
-            const int8_t* kr = kv.k8 + (sl[i] * nkv + kvh) * qk;
-            int32_t acc = 0;
-            for (int e = 0; e < qk; e++) acc += (int32_t)q8[e] * (int32_t)kr[e];
-            dots[i] = acc;
+            dots[i] = dot_i8(q8, kv.k8 + (sl[i] * nkv + kvh) * qk, qk);
             scale[i] = kv.ks[sl[i] * nkv + kvh];
         }
         for (int i = 0; i < blocked; i++) s[i] = (scale[i] * (float)dots[i]) * qs;
@@ -1006,16 +1165,31 @@ void attend_head_ref(const KVView& kv, const float* qh, int kvh, const std::vect
         Part p;
         p.m = m;
         p.sum = sum;
-        for (int dm = 0; dm < vd; dm++) {
-            int32_t sh = 0, sm = 0, sl2 = 0;
-            for (int i = 0; i < len; i++) {
-                int32_t v = kv.v8[(sl[i] * nkv + kvh) * vd + dm];
-                sh += hi[i] * v;
-                sm += mid[i] * v;
-                sl2 += lo[i] * v;
+        // the three digit planes' exact integer sums, key by key
+        int32_t sh[64] = {0}, sm[64] = {0}, sl2[64] = {0};
+        for (int i = 0; i < len; i++) {
+            const int8_t* vr = kv.v8 + (sl[i] * nkv + kvh) * vd;
+            int dm = 0;
+#if defined(__AVX2__)
+            const __m256i h8 = _mm256_set1_epi32(hi[i]), m8 = _mm256_set1_epi32(mid[i]), l8 = _mm256_set1_epi32(lo[i]);
+            for (; dm + 8 <= vd; dm += 8) {
+                const __m256i v = _mm256_cvtepi8_epi32(_mm_loadl_epi64((const __m128i*)(vr + dm)));
+                _mm256_storeu_si256((__m256i*)(sh + dm), _mm256_add_epi32(_mm256_loadu_si256((const __m256i*)(sh + dm)),
+                                                                          _mm256_mullo_epi32(h8, v)));
+                _mm256_storeu_si256((__m256i*)(sm + dm), _mm256_add_epi32(_mm256_loadu_si256((const __m256i*)(sm + dm)),
+                                                                          _mm256_mullo_epi32(m8, v)));
+                _mm256_storeu_si256((__m256i*)(sl2 + dm), _mm256_add_epi32(_mm256_loadu_si256((const __m256i*)(sl2 + dm)),
+                                                                           _mm256_mullo_epi32(l8, v)));
             }
-            p.o[dm] = std::fmaf(16384.f, (float)sh, std::fmaf(128.f, (float)sm, (float)sl2)) * cw;
+#endif
+            for (; dm < vd; dm++) {
+                sh[dm] += hi[i] * vr[dm];
+                sm[dm] += mid[i] * vr[dm];
+                sl2[dm] += lo[i] * vr[dm];
+            }
         }
+        for (int dm = 0; dm < vd; dm++)
+            p.o[dm] = std::fmaf(16384.f, (float)sh[dm], std::fmaf(128.f, (float)sm[dm], (float)sl2[dm])) * cw;
         parts.push_back(p);
     }
     if (parts.size() == 1) {
@@ -1084,8 +1258,29 @@ static void cond_weights(const float* h2, int d, const float* cond_v, float w[8]
 }
 
 // infer.rs:2322-2330, 2343-2460 (scalar arm 2442-2459): T = (A^T Z) B.
+// Each output is one fma chain over j = 0..31 from 0; the AVX2 form runs
+// eight outputs' chains side by side (a vector fma rounds once per lane,
+// as fmaf does), in the same j order.
 static void kron_native(const float* z, const float* a, const float* b, float* t) {
     float mt[1024];
+#if defined(__AVX2__)
+    for (int c = 0; c < 32; c++) {  // mt[c][r] for r = 0..31
+        __m256 o[4] = {_mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps()};
+        for (int j = 0; j < 32; j++) {
+            const __m256 zj = _mm256_set1_ps(z[j * 32 + c]);
+            for (int k = 0; k < 4; k++) o[k] = _mm256_fmadd_ps(_mm256_loadu_ps(a + j * 32 + 8 * k), zj, o[k]);
+        }
+        for (int k = 0; k < 4; k++) _mm256_storeu_ps(mt + c * 32 + 8 * k, o[k]);
+    }
+    for (int r = 0; r < 32; r++) {  // t[r][c] for c = 0..31
+        __m256 o[4] = {_mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps()};
+        for (int j = 0; j < 32; j++) {
+            const __m256 mj = _mm256_set1_ps(mt[j * 32 + r]);
+            for (int k = 0; k < 4; k++) o[k] = _mm256_fmadd_ps(mj, _mm256_loadu_ps(b + j * 32 + 8 * k), o[k]);
+        }
+        for (int k = 0; k < 4; k++) _mm256_storeu_ps(t + r * 32 + 8 * k, o[k]);
+    }
+#else
     for (int r = 0; r < 32; r++)
         for (int c = 0; c < 32; c++) {
             float o = 0.f;
@@ -1098,6 +1293,7 @@ static void kron_native(const float* z, const float* a, const float* b, float* t
             for (int j = 0; j < 32; j++) o = std::fmaf(mt[j * 32 + r], b[j * 32 + c], o);
             t[r * 32 + c] = o;
         }
+#endif
 }
 
 // infer.rs:1610-1634 with axpy16 (494-528), perm_fma (689-713), silu (2463-2496)
@@ -1249,9 +1445,7 @@ static void layer_native(const Model& m, int l, Session& st, int64_t p0, std::ve
             float sx = quant_i8(nx.data(), nc, q8.data());
             float* pr = p.data() + (size_t)i * ncols;
             for (int k = 0; k < ncols; k++) {
-                const int8_t* w = L.phi_q.data() + (size_t)k * nc;
-                int32_t acc = 0;
-                for (int e = 0; e < nc; e++) acc += (int32_t)w[e] * (int32_t)q8[e];
+                const int32_t acc = dot_i8(L.phi_q.data() + (size_t)k * nc, q8.data(), nc);
                 pr[k] = (sx * L.phi_s[k]) * (float)acc;
             }
             float hp[4];
@@ -1442,7 +1636,7 @@ enum Outputs { OUT_NONE = 0, OUT_LAST_LOGITS = 1, OUT_LAST_HIDDEN = 2, OUT_ALL_L
 // infer.rs:1135-1141
 static void head_logits(const Model& m, const float* h, float* out) {
     QAct act = qact_new(h, 1, m.c.d);
-    for (int r = 0; r < m.c.out_rows(); r++) out[r] = decode_row_ref(m.embedding, r, act);
+    decode_rows(m.embedding, act, out);
 }
 
 // infer.rs:1145-1166
@@ -2099,6 +2293,61 @@ int orc_cq_matmul(const uint8_t* codes, const uint16_t* norms, int out, int in_d
         g_err = e.what();
         return -1;
     }
+}
+
+// The lane sums the matmuls use (AVX2 where the build has it) against the
+// scalar loop, on n groups of weights and activations drawn from a
+// seeded generator over all of int8 (both extremes forced into the
+// first groups), for the 2-bit lane rule and the other one. Returns the
+// groups whose four sums differ (0 when they all agree).
+int orc_lane_sums_check(uint64_t seed, int n) {
+    uint64_t st = seed * 0x9E3779B97F4A7C15ull + 1;
+    auto next = [&]() {
+        st ^= st << 13;
+        st ^= st >> 7;
+        st ^= st << 17;
+        return st;
+    };
+    int bad = 0;
+    int8_t w[GROUP], x[GROUP];
+    for (int k = 0; k < n; k++) {
+        for (int p = 0; p < GROUP; p++) {
+            w[p] = (int8_t)(next() & 0xFF);
+            x[p] = (int8_t)(next() & 0xFF);
+            if (k == 0) w[p] = x[p] = -128;
+            if (k == 1) { w[p] = -128; x[p] = 127; }
+            if (k == 2) w[p] = x[p] = 127;
+        }
+        bool differ = false;
+        for (int width : {2, 4}) {
+            int32_t a[4], b[4];
+            lane_sums_of(w, x, width, a);
+            lane_sums_scalar(w, x, width, b);
+            differ |= std::memcmp(a, b, sizeof a) != 0;
+        }
+#if defined(__AVX2__)
+        // 4-bit codes through a codebook of sixteen int8 values: the first
+        // groups' codebooks hold the extremes
+        uint8_t codes[64], idx[GROUP];
+        int8_t vals[16], wv[GROUP];
+        for (int c = 0; c < 16; c++) vals[c] = k < 3 ? (int8_t)(c & 1 ? 127 : -128) : (int8_t)(next() & 0xFF);
+        for (int b = 0; b < 64; b++) codes[b] = (uint8_t)(next() & 0xFF);
+        unpack_lsb(codes, 4, GROUP, idx);
+        for (int p = 0; p < GROUP; p++) wv[p] = vals[idx[p]];
+        int16_t xeo[GROUP];
+        for (int b0 = 0; b0 < GROUP; b0 += 32)
+            for (int j = 0; j < 16; j++) {
+                xeo[b0 + j] = x[b0 + 2 * j];
+                xeo[b0 + 16 + j] = x[b0 + 2 * j + 1];
+            }
+        int32_t a[4], b[4];
+        lane_sums_codes4_avx2(codes, vals, xeo, a);
+        lane_sums_scalar(wv, x, 4, b);
+        differ |= std::memcmp(a, b, sizeof a) != 0;
+#endif
+        bad += differ;
+    }
+    return bad;
 }
 
 // QMat::row of a raw CQ matrix of record bits `bits` (qlinear.rs:309-323).

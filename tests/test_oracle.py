@@ -120,6 +120,12 @@ def test_row_matches_unpack():
 
 # ---- crates/needle-engine/src/infer.rs:3018-3032, 3078-3084
 
+def test_vector_lane_sums_equal_the_scalar_loop():
+    # the matmuls' exact int8 lane sums (vectorised where the host allows)
+    # against the plain loop of qlinear.rs:327-337, extremes included
+    assert orc.lib().orc_lane_sums_check(7, 4096) == 0
+
+
 def test_dot16_matches_the_scalar_order():
     i = np.arange(768)
     x = ((((i * 37) % 101).astype(np.float32) - np.float32(50.0)) * np.float32(0.013)).astype(np.float32)
