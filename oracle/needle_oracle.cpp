@@ -15,7 +15,8 @@
 // the reference's order. Integer sums are exact and computed in any order.
 // Where the build has AVX2 the hot loops run vectorised without changing a
 // result: the int8 lane sums and dots (4-bit codes looked up from their
-// packed bytes; int16 pair products summed into int32, no saturation), the
+// packed bytes; byte pair products into int16 only when no operand is -128,
+// else int16 pair products into int32: nothing saturates), the
 // decode combine eight rows side by side and the Kronecker passes eight
 // outputs side by side (each row's or output's float ops the same single
 // roundings in the same order). orc_lane_sums_check compares the vector
@@ -418,6 +419,7 @@ struct QMat {
     std::vector<float> normf;    // the same norms widened (exact)
     std::vector<int8_t> w8;      // codes expanded through `vals`, natural order
     std::vector<QPart> parts;
+    bool no_min = false;         // no part's `vals` holds -128
     const QPart& part(int r) const {
         size_t k = parts.size() - 1;
         while (k > 0 && parts[k].r0 > r) k--;
@@ -462,6 +464,8 @@ static void qmat_init(QMat& q, int bits, int out, int in_dim, const uint8_t* cod
         pt.fvals[c] = in ? cb[k] : 0.f;
     }
     q.parts.assign(1, pt);
+    q.no_min = true;
+    for (int c = 0; c < 16; c++) q.no_min &= pt.vals[c] != -128;
     q.w8.resize((size_t)out * q.groups * GROUP);
     uint8_t idx[GROUP];
     for (size_t u = 0; u < (size_t)out * q.groups; u++) {
@@ -492,6 +496,7 @@ static void qmat_concat(QMat& dst, const QMat& src) {
         dst.parts.push_back(p);
     }
     dst.out += src.out;
+    dst.no_min = dst.no_min && src.no_min;
     dst.codes.insert(dst.codes.end(), src.codes.begin(), src.codes.end());
     dst.norms.insert(dst.norms.end(), src.norms.begin(), src.norms.end());
     dst.normf.insert(dst.normf.end(), src.normf.begin(), src.normf.end());
@@ -522,6 +527,12 @@ struct QAct {
     // xq widened to int16, each 32-wide block as its 16 even elements then
     // its 16 odd ones (the order the 4-bit code bytes hold the weights in)
     std::vector<int16_t> xeo;
+    // xq as int8 and as magnitudes, each pair of 32-wide blocks as the even
+    // elements of both, then the odd elements of both; no_min: xq holds no
+    // -128 (every magnitude fits a signed byte)
+    std::vector<int8_t> x8eo;
+    std::vector<uint8_t> ax8eo;
+    bool no_min = false;
 };
 
 // qlinear.rs:152-164
@@ -550,6 +561,19 @@ static QAct qact_new(const float* x, int rows, int in_dim) {
             a.xeo[b + j] = a.xq[b + 2 * j];
             a.xeo[b + 16 + j] = a.xq[b + 2 * j + 1];
         }
+    a.x8eo.resize(a.xq.size());
+    a.ax8eo.resize(a.xq.size());
+    a.no_min = true;
+    for (size_t b = 0; b < a.xq.size(); b += 64)  // two 32-wide blocks
+        for (int h = 0; h < 2; h++)
+            for (int j = 0; j < 16; j++)
+                for (int odd = 0; odd < 2; odd++) {
+                    const int8_t v = a.xq[b + 32 * h + 2 * j + odd];
+                    const size_t at = b + 32 * odd + 16 * h + j;
+                    a.x8eo[at] = v;
+                    a.ax8eo[at] = (uint8_t)std::abs((int)v);
+                    a.no_min &= v != -128;
+                }
     return a;
 }
 
@@ -670,10 +694,41 @@ static inline void lane_sums_codes4_avx2(const uint8_t* codes, const int8_t* val
 }
 #endif
 
+#if defined(__AVX2__)
+// lane_sums_codes4_avx2's integers two 32-wide blocks at a time, when no
+// weight value and no activation is -128: byte products |x| * (w signed by
+// x) summed in pairs into int16 (vpmaddubsw: a pair is at most 2 * 127 *
+// 127 = 32258, so nothing saturates), then pairs of those into int32. In a
+// 128-bit half (one block) int32 m is lane m. x8/ax8: the group's
+// activations and magnitudes as QAct::x8eo / ax8eo hold them; tbl: `vals`
+// in both 128-bit halves. Returns the four lanes.
+static inline __m128i lane_sums_codes4_ub(const uint8_t* codes, __m256i tbl, const int8_t* x8, const uint8_t* ax8) {
+    const __m256i m4 = _mm256_set1_epi8(0x0F), ones = _mm256_set1_epi16(1);
+    __m256i acc = _mm256_setzero_si256();
+    for (int pr = 0; pr < 2; pr++) {
+        const __m256i c = _mm256_loadu_si256((const __m256i*)(codes + 32 * pr));
+        const __m256i we = _mm256_shuffle_epi8(tbl, _mm256_and_si256(c, m4));
+        const __m256i wo = _mm256_shuffle_epi8(tbl, _mm256_and_si256(_mm256_srli_epi16(c, 4), m4));
+        const __m256i xe = _mm256_loadu_si256((const __m256i*)(x8 + 64 * pr));
+        const __m256i xo = _mm256_loadu_si256((const __m256i*)(x8 + 64 * pr + 32));
+        const __m256i pe = _mm256_maddubs_epi16(_mm256_loadu_si256((const __m256i*)(ax8 + 64 * pr)), _mm256_sign_epi8(we, xe));
+        const __m256i po = _mm256_maddubs_epi16(_mm256_loadu_si256((const __m256i*)(ax8 + 64 * pr + 32)), _mm256_sign_epi8(wo, xo));
+        acc = _mm256_add_epi32(acc, _mm256_add_epi32(_mm256_madd_epi16(pe, ones), _mm256_madd_epi16(po, ones)));
+    }
+    return _mm_add_epi32(_mm256_castsi256_si128(acc), _mm256_extracti128_si256(acc, 1));
+}
+#endif
+
 // The lane sums of row r (part pt), group g against activation row t.
 static inline void lane_sums(const QMat& q, const QPart& pt, int r, int g, const QAct& a, int t, int32_t s[4]) {
     const size_t ag = ((size_t)t * a.groups + g) * GROUP;
 #if defined(__AVX2__)
+    if (q.width == 4 && q.no_min && a.no_min) {
+        const __m256i tbl = _mm256_broadcastsi128_si256(_mm_loadu_si128((const __m128i*)pt.vals));
+        _mm_storeu_si128((__m128i*)s, lane_sums_codes4_ub(q.codes.data() + ((size_t)r * q.groups + g) * 64, tbl,
+                                                          a.x8eo.data() + ag, a.ax8eo.data() + ag));
+        return;
+    }
     if (q.width == 4) {
         lane_sums_codes4_avx2(q.codes.data() + ((size_t)r * q.groups + g) * 64, pt.vals, a.xeo.data() + ag, s);
         return;
@@ -730,6 +785,42 @@ static void decode_rows(const QMat& q, const QAct& a, float* y) {
         }
         const __m256 cbv = _mm256_loadu_ps(cbs);
         __m256 ln[4] = {_mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps()};
+        if (q.width == 4 && q.no_min && a.no_min) {
+            // the code bytes of the block two blocks on, into the caches
+            // while this one is summed (rows r .. r + 7 are contiguous)
+            if (r + 24 <= q.out) {
+                const uint8_t* nxt = q.codes.data() + (size_t)(r + 16) * q.groups * 64;
+                for (int b = 0; b < 8 * q.groups * 64; b += 64) _mm_prefetch((const char*)(nxt + b), _MM_HINT_T0);
+            }
+            __m256i tbl[8];
+            for (int k = 0; k < 8; k++) tbl[k] = _mm256_broadcastsi128_si256(_mm_loadu_si128((const __m128i*)pts[k]->vals));
+            for (int g = 0; g < q.groups; g++) {
+                const size_t ag = (size_t)g * GROUP;
+                __m128i v[8];  // row k's four lane sums
+                for (int k = 0; k < 8; k++)
+                    v[k] = lane_sums_codes4_ub(q.codes.data() + ((size_t)(r + k) * q.groups + g) * 64, tbl[k], a.x8eo.data() + ag,
+                                               a.ax8eo.data() + ag);
+                // transposed: lane l of rows 0..7
+                __m128i lo[4], hi[4];
+                for (int h = 0; h < 2; h++) {
+                    const __m128i* w = v + 4 * h;
+                    const __m128i t0 = _mm_unpacklo_epi32(w[0], w[1]), t1 = _mm_unpackhi_epi32(w[0], w[1]);
+                    const __m128i t2 = _mm_unpacklo_epi32(w[2], w[3]), t3 = _mm_unpackhi_epi32(w[2], w[3]);
+                    __m128i* o = h ? hi : lo;
+                    o[0] = _mm_unpacklo_epi64(t0, t2);
+                    o[1] = _mm_unpackhi_epi64(t0, t2);
+                    o[2] = _mm_unpacklo_epi64(t1, t3);
+                    o[3] = _mm_unpackhi_epi64(t1, t3);
+                }
+                alignas(32) float nf[8];
+                for (int k = 0; k < 8; k++) nf[k] = q.normf[(size_t)(r + k) * q.groups + g];
+                const __m256 sc = _mm256_mul_ps(_mm256_mul_ps(_mm256_set1_ps(a.sx[g]), cbv), _mm256_load_ps(nf));
+                for (int l = 0; l < 4; l++)
+                    ln[l] = _mm256_fmadd_ps(_mm256_cvtepi32_ps(_mm256_set_m128i(hi[l], lo[l])), sc, ln[l]);
+            }
+            _mm256_storeu_ps(y + r, _mm256_add_ps(_mm256_add_ps(ln[0], ln[1]), _mm256_add_ps(ln[2], ln[3])));
+            continue;
+        }
         for (int g = 0; g < q.groups; g++) {
             alignas(32) int32_t s[4][8];
             alignas(32) float nf[8];
@@ -2343,6 +2434,25 @@ int orc_lane_sums_check(uint64_t seed, int n) {
         int32_t a[4], b[4];
         lane_sums_codes4_avx2(codes, vals, xeo, a);
         lane_sums_scalar(wv, x, 4, b);
+        differ |= std::memcmp(a, b, sizeof a) != 0;
+        // the byte-product form, on values without -128 (its precondition):
+        // the same draws with -128 moved to -127, the extremes included
+        int8_t xn[GROUP], vn[16], wn[GROUP], x8[GROUP];
+        uint8_t ax[GROUP];
+        for (int p = 0; p < GROUP; p++) xn[p] = x[p] == -128 ? -127 : x[p];
+        for (int c = 0; c < 16; c++) vn[c] = vals[c] == -128 ? -127 : vals[c];
+        for (int p = 0; p < GROUP; p++) wn[p] = vn[idx[p]];
+        for (int b0 = 0; b0 < GROUP; b0 += 64)
+            for (int h = 0; h < 2; h++)
+                for (int j = 0; j < 16; j++)
+                    for (int odd = 0; odd < 2; odd++) {
+                        const int8_t v = xn[b0 + 32 * h + 2 * j + odd];
+                        x8[b0 + 32 * odd + 16 * h + j] = v;
+                        ax[b0 + 32 * odd + 16 * h + j] = (uint8_t)std::abs((int)v);
+                    }
+        _mm_storeu_si128((__m128i*)a,
+                         lane_sums_codes4_ub(codes, _mm256_broadcastsi128_si256(_mm_loadu_si128((const __m128i*)vn)), x8, ax));
+        lane_sums_scalar(wn, xn, 4, b);
         differ |= std::memcmp(a, b, sizeof a) != 0;
 #endif
         bad += differ;
