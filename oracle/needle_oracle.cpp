@@ -17,10 +17,11 @@
 // result: the int8 lane sums and dots (4-bit codes looked up from their
 // packed bytes; byte pair products into int16 only when no operand is -128,
 // else int16 pair products into int32: nothing saturates), the
-// decode combine eight rows side by side and the Kronecker passes eight
-// outputs side by side (each row's or output's float ops the same single
-// roundings in the same order). orc_lane_sums_check compares the vector
-// integer sums with the plain loops.
+// decode combine eight rows side by side, the Kronecker passes eight
+// outputs side by side and the inline exp eight values at a time (each
+// row's, output's or value's float ops the same single roundings in the
+// same order). orc_lane_sums_check and orc_nexp_check compare the vector
+// forms with the plain loops.
 // libm stand-ins follow the reference's non-Apple `sys` module
 // (crates/needle-engine/src/infer.rs:83-102): f32 exp/pow/sincos are f64 libm
 // rounded once; this file uses glibc's f64 functions where the reference links
@@ -127,6 +128,41 @@ float nexp(float x) {
     float y = std::fmaf(r * r, p, r);
     float s = bitsf((uint32_t)(((int32_t)k << 23) + 0x3f800000));
     return std::fmaf(s, y, s);
+}
+
+#if defined(__AVX2__)
+// nexp on eight values, each step the same single rounding as above: the
+// clamp (max, then min; a NaN takes the lower bound as fmax gives it),
+// round to nearest even, the fma chain, the exponent bits from k.
+static inline __m256 nexp8(__m256 x) {
+    x = _mm256_min_ps(_mm256_max_ps(x, _mm256_set1_ps(bitsf(0xc2b0c0a5u))), _mm256_set1_ps(bitsf(0x42b0c0a5u)));
+    const __m256 k = _mm256_round_ps(_mm256_mul_ps(x, _mm256_set1_ps(bitsf(0x3fb8aa3bu))), _MM_FROUND_TO_NEAREST_INT | _MM_FROUND_NO_EXC);
+    __m256 r = _mm256_fmadd_ps(k, _mm256_set1_ps(bitsf(0xbf318000u)), x);
+    r = _mm256_fmadd_ps(k, _mm256_set1_ps(bitsf(0x395e8083u)), r);
+    __m256 p = _mm256_fmadd_ps(_mm256_set1_ps(bitsf(0x39506967u)), r, _mm256_set1_ps(bitsf(0x3ab743ceu)));
+    p = _mm256_fmadd_ps(r, p, _mm256_set1_ps(bitsf(0x3c088908u)));
+    p = _mm256_fmadd_ps(r, p, _mm256_set1_ps(bitsf(0x3d2aa9c1u)));
+    p = _mm256_fmadd_ps(r, p, _mm256_set1_ps(bitsf(0x3e2aaaaau)));
+    p = _mm256_fmadd_ps(r, p, _mm256_set1_ps(0.5f));
+    const __m256 y = _mm256_fmadd_ps(_mm256_mul_ps(r, r), p, r);
+    const __m256 s = _mm256_castsi256_ps(
+        _mm256_add_epi32(_mm256_slli_epi32(_mm256_cvttps_epi32(k), 23), _mm256_set1_epi32(0x3f800000)));
+    return _mm256_fmadd_ps(s, y, s);
+}
+#endif
+
+// x[i] / (nexp(-x[i]) + 1) over n values in place (SiLU; the attention
+// gate's divide with g = x), each value's ops as the scalar form's.
+static void silu_div(float* x, const float* g, int64_t n) {
+    int64_t i = 0;
+#if defined(__AVX2__)
+    const __m256 one = _mm256_set1_ps(1.0f), neg = _mm256_set1_ps(-0.0f);
+    for (; i + 8 <= n; i += 8) {
+        const __m256 gv = _mm256_xor_ps(_mm256_loadu_ps(g + i), neg);
+        _mm256_storeu_ps(x + i, _mm256_div_ps(_mm256_loadu_ps(x + i), _mm256_add_ps(nexp8(gv), one)));
+    }
+#endif
+    for (; i < n; i++) x[i] /= nexp(-g[i]) + 1.0f;
 }
 
 // crates/needle-engine/src/infer.rs:372-417 (scalar arm 405-416)
@@ -1178,8 +1214,14 @@ float chunk_exp(float* s, int l, float m) {
     int i = 0;
     float a[4] = {0, 0, 0, 0}, b[4] = {0, 0, 0, 0};
     while (i + 8 <= l) {
+#if defined(__AVX2__)
+        _mm256_storeu_ps(s + i, nexp8(_mm256_sub_ps(_mm256_loadu_ps(s + i), _mm256_set1_ps(m))));
+        for (int k = 0; k < 4; k++) a[k] += s[i + k];
+        for (int k = 0; k < 4; k++) b[k] += s[i + 4 + k];
+#else
         for (int k = 0; k < 4; k++) { float e = nexp(s[i + k] - m); s[i + k] = e; a[k] += e; }
         for (int k = 0; k < 4; k++) { float e = nexp(s[i + 4 + k] - m); s[i + 4 + k] = e; b[k] += e; }
+#endif
         i += 8;
     }
     while (i + 4 <= l) {
@@ -1227,11 +1269,21 @@ void attend_head_ref(const KVView& kv, const float* qh, int kvh, const std::vect
     int64_t n = (int64_t)slots.size();
     int64_t count, chunk;
     key_chunks(n, nested, nkv, &count, &chunk);
-    std::vector<float> s(chunk), scale(chunk);
-    std::vector<int32_t> dots(chunk);
-    std::vector<int8_t> hi(chunk), mid(chunk), lo(chunk);
+    // per-thread scratch, grown to the largest chunk seen
+    thread_local std::vector<float> s, scale;
+    thread_local std::vector<int32_t> dots;
+    thread_local std::vector<int8_t> hi, mid, lo;
+    if ((int64_t)s.size() < chunk) {
+        s.resize(chunk);
+        scale.resize(chunk);
+        dots.resize(chunk);
+        hi.resize(chunk);
+        mid.resize(chunk);
+        lo.resize(chunk);
+    }
     struct Part { float m, sum; float o[64]; };
     std::vector<Part> parts;
+    parts.reserve((size_t)count);
     for (int64_t c0 = 0; c0 < n; c0 += chunk) {
         int len = (int)std::min(chunk, n - c0);
         const int64_t* sl = slots.data() + c0;
@@ -1399,7 +1451,7 @@ static void mlp_native(const Model& m, const Layer& L, const float* h2, float* o
     for (int k = 0; k < 8; k++)
         for (int j = 0; j < 1024; j++) cond[j] = std::fmaf(L.cond_u[k * 1024 + j], w[k], cond[j]);
     for (int j = 0; j < 1024; j++) z[j] = std::fmaf(t[m.perm1[j]], cond[j] * L.d2[j], L.b2[j]);
-    for (int j = 0; j < 1024; j++) z[j] /= nexp(-z[j]) + 1.0f;
+    silu_div(z, z, 1024);
     kron_native(z, L.kron[2].data(), L.kron[3].data(), t);
     for (int j = 0; j < 1024; j++) z[j] = t[m.perm2[j]] * L.d3[j];
     kron_native(z, L.kron[4].data(), L.kron[5].data(), t);
@@ -1671,11 +1723,7 @@ static void layer_native(const Model& m, int l, Session& st, int64_t p0, std::ve
         }
     }
     g_trace.put(tag + "attn", att.data(), att.size());
-    for (int i = 0; i < t; i++)
-        for (int k = 0; k < nh * vd; k++) {
-            float g = proj[(size_t)i * pout + width + k];
-            att[(size_t)i * nh * vd + k] /= nexp(-g) + 1.0f;
-        }
+    for (int i = 0; i < t; i++) silu_div(att.data() + (size_t)i * nh * vd, proj.data() + (size_t)i * pout + width, nh * vd);
     g_trace.put(tag + "att", att.data(), att.size());
 
     // (j) A8 + out projection
@@ -2460,6 +2508,43 @@ int orc_lane_sums_check(uint64_t seed, int n) {
     return bad;
 }
 
+// silu_div (vectorised where the build has AVX2) against the scalar
+// x / (nexp(-g) + 1) on n values from a seeded generator spread over the
+// clamp range and past it, plus the specials (zeros, infinities, NaN, the
+// clamp bounds, halfway points of the rounding). Returns the values whose
+// bits differ. Signalling NaNs are left out of the raw-bit draws: no
+// arithmetic produces one, and glibc's fmaxf turns one into NaN where the
+// vector max (as CUDA's fmaxf) takes the bound.
+int orc_nexp_check(uint64_t seed, int n) {
+    uint64_t st = seed * 0x9E3779B97F4A7C15ull + 1;
+    auto next = [&]() {
+        st ^= st << 13;
+        st ^= st >> 7;
+        st ^= st << 17;
+        return st;
+    };
+    std::vector<float> g;
+    const float specials[] = {0.f, -0.f, INFINITY, -INFINITY, NAN, bitsf(0xc2b0c0a5u), bitsf(0x42b0c0a5u), 88.8f, -88.8f,
+                              0.5f * 0.6931472f, -0.5f * 0.6931472f, 1e-30f, -1e-30f, 1.5f * 0.6931472f};
+    for (float v : specials) g.push_back(v);
+    while ((int)g.size() < n) {
+        const uint64_t u = next();
+        g.push_back(((float)(u >> 40) / (float)(1u << 24) - 0.5f) * 240.f);  // [-120, 120)
+        uint32_t b = (uint32_t)u;
+        if ((b & 0x7f800000u) == 0x7f800000u && (b & 0x007fffffu)) b |= 0x00400000u;  // NaNs quiet
+        g.push_back(bitsf(b));                                                         // any other bits
+    }
+    std::vector<float> x(g.size()), a(g.size());
+    for (size_t i = 0; i < g.size(); i++) x[i] = a[i] = bitsf((uint32_t)(next() >> 7) & 0x3fffffffu);
+    silu_div(a.data(), g.data(), (int64_t)g.size());
+    int bad = 0;
+    for (size_t i = 0; i < g.size(); i++) {
+        const float b = x[i] / (nexp(-g[i]) + 1.0f);
+        bad += fbits(a[i]) != fbits(b) && !(a[i] != a[i] && b != b);
+    }
+    return bad;
+}
+
 // QMat::row of a raw CQ matrix of record bits `bits` (qlinear.rs:309-323).
 int orc_cq_row(const uint8_t* codes, const uint16_t* norms, int rows, int in_dim, int bits, int r, float* out) {
     try {
@@ -2884,7 +2969,8 @@ void orc_op_rope(const float* x, int T, float theta, float* out) {
 
 // infer.rs:2463-2496 (silu_native, scalar arm).
 void orc_op_silu(const float* x, int64_t n, float* out) {
-    for (int64_t i = 0; i < n; i++) out[i] = x[i] / (nexp(-x[i]) + 1.0f);
+    std::memcpy(out, x, sizeof(float) * n);
+    silu_div(out, x, n);
 }
 
 // qlinear.rs:309-323 (QMat::row) of the model's embedding for each id.

@@ -126,6 +126,12 @@ def test_vector_lane_sums_equal_the_scalar_loop():
     assert orc.lib().orc_lane_sums_check(7, 4096) == 0
 
 
+def test_vector_inline_exp_equals_the_scalar_one():
+    # the SiLU / gate divide through the eight-wide inline exp against the
+    # scalar nexp of infer.rs:353-366, specials included, bit for bit
+    assert orc.lib().orc_nexp_check(11, 200000) == 0
+
+
 def test_dot16_matches_the_scalar_order():
     i = np.arange(768)
     x = ((((i * 37) % 101).astype(np.float32) - np.float32(50.0)) * np.float32(0.013)).astype(np.float32)
