@@ -18,10 +18,10 @@
 // packed bytes; byte pair products into int16 only when no operand is -128,
 // else int16 pair products into int32: nothing saturates), the
 // decode combine eight rows side by side, the Kronecker passes eight
-// outputs side by side and the inline exp eight values at a time (each
-// row's, output's or value's float ops the same single roundings in the
-// same order). orc_lane_sums_check and orc_nexp_check compare the vector
-// forms with the plain loops.
+// outputs side by side, the inline exp and the int8 quantizer eight values
+// at a time (each row's, output's or value's float ops the same single
+// roundings in the same order). orc_lane_sums_check, orc_nexp_check and
+// orc_quant_check compare the vector forms with the plain loops.
 // libm stand-ins follow the reference's non-Apple `sys` module
 // (crates/needle-engine/src/infer.rs:83-102): f32 exp/pow/sincos are f64 libm
 // rounded once; this file uses glibc's f64 functions where the reference links
@@ -192,7 +192,73 @@ void zcn(const float* x, const float* s, float* out, int n) {
 }
 
 // qlinear.rs:77-88, 113-140 (scalar arms): absmax int8, round half away, saturate.
+#if defined(__AVX2__)
+// Rust's f32::round (half away from zero) on eight values, exactly: the
+// truncation (signed zeros kept), or one further from zero when the
+// remainder (exact for every finite value) is at least one half;
+// infinities pass through.
+static inline __m256 round_away8(__m256 v) {
+    const __m256 t = _mm256_round_ps(v, _MM_FROUND_TO_ZERO | _MM_FROUND_NO_EXC);
+    const __m256 absmask = _mm256_castsi256_ps(_mm256_set1_epi32(0x7fffffff));
+    const __m256 f = _mm256_and_ps(_mm256_sub_ps(v, t), absmask);
+    const __m256 one = _mm256_or_ps(_mm256_set1_ps(1.0f), _mm256_andnot_ps(absmask, v));  // ±1 with v's sign
+    return _mm256_blendv_ps(t, _mm256_add_ps(t, one), _mm256_cmp_ps(f, _mm256_set1_ps(0.5f), _CMP_GE_OQ));
+}
+#endif
+
+float quant_i8_scalar(const float* x, int n, int8_t* q);
+
+// qlinear.rs:77-88: as quant_i8_scalar; eight values at a time where the
+// build has AVX2 and the row holds no NaN (the scalar loop takes those).
 float quant_i8(const float* x, int n, int8_t* q) {
+#if defined(__AVX2__)
+    const __m256 absmask = _mm256_castsi256_ps(_mm256_set1_epi32(0x7fffffff));
+    __m256 mv = _mm256_setzero_ps(), nan = _mm256_setzero_ps();
+    int i = 0;
+    for (; i + 8 <= n; i += 8) {
+        const __m256 v = _mm256_loadu_ps(x + i);
+        nan = _mm256_or_ps(nan, _mm256_cmp_ps(v, v, _CMP_UNORD_Q));
+        mv = _mm256_max_ps(mv, _mm256_and_ps(v, absmask));
+    }
+    bool any_nan = _mm256_movemask_ps(nan) != 0;
+    alignas(32) float mm[8];
+    _mm256_store_ps(mm, mv);
+    float m = 0.f;
+    for (int k = 0; k < 8; k++) m = rmax(m, mm[k]);  // max is exact in any order
+    for (; i < n; i++) {
+        any_nan |= x[i] != x[i];
+        m = rmax(m, std::fabs(x[i]));
+    }
+    if (any_nan) return quant_i8_scalar(x, n, q);
+    const float s = m > 0.f ? m * K127 : 1.0f;
+    const float inv = 1.0f / s;
+    const __m256 iv = _mm256_set1_ps(inv), lo = _mm256_set1_ps(-128.f), hi = _mm256_set1_ps(127.f);
+    i = 0;
+    for (; i + 8 <= n; i += 8) {
+        // a NaN product (an infinite element times a zero inverse) gives 0,
+        // as the scalar loop's saturating conversion does
+        const __m256 p = _mm256_mul_ps(_mm256_loadu_ps(x + i), iv);
+        const __m256 r = _mm256_andnot_ps(_mm256_cmp_ps(p, p, _CMP_UNORD_Q),
+                                          _mm256_min_ps(_mm256_max_ps(round_away8(p), lo), hi));
+        const __m256i w = _mm256_cvttps_epi32(r);
+        const __m256i b = _mm256_packs_epi16(_mm256_packs_epi32(w, w), _mm256_setzero_si256());  // bytes 0-3 | 16-19
+        const int32_t lo4 = _mm_cvtsi128_si32(_mm256_castsi256_si128(b)), hi4 = _mm_cvtsi128_si32(_mm256_extracti128_si256(b, 1));
+        std::memcpy(q + i, &lo4, 4);
+        std::memcpy(q + i + 4, &hi4, 4);
+    }
+    for (; i < n; i++) {
+        float v = rround(x[i] * inv);
+        v = std::min(std::max(v, -128.f), 127.f);
+        q[i] = v != v ? 0 : (int8_t)v;
+    }
+    return s;
+#else
+    return quant_i8_scalar(x, n, q);
+#endif
+}
+
+// qlinear.rs:77-88
+float quant_i8_scalar(const float* x, int n, int8_t* q) {
     float m = 0.f;
     for (int i = 0; i < n; i++) m = rmax(m, std::fabs(x[i]));
     float s = m > 0.f ? m * K127 : 1.0f;
@@ -2542,6 +2608,51 @@ int orc_nexp_check(uint64_t seed, int n) {
         const float b = x[i] / (nexp(-g[i]) + 1.0f);
         bad += fbits(a[i]) != fbits(b) && !(a[i] != a[i] && b != b);
     }
+    return bad;
+}
+
+// quant_i8 (vectorised where the build has AVX2) against the scalar loop
+// on n rows of seeded values (row lengths 1-200, magnitudes from 1e-40 to
+// 1e30, infinities, quiet NaNs, zeros), and the vector rounding against
+// std::round on exact halves and raw bits. Returns the mismatches.
+int orc_quant_check(uint64_t seed, int n) {
+    uint64_t st = seed * 0x9E3779B97F4A7C15ull + 1;
+    auto next = [&]() {
+        st ^= st << 13;
+        st ^= st >> 7;
+        st ^= st << 17;
+        return st;
+    };
+    int bad = 0;
+    std::vector<float> x(200);
+    std::vector<int8_t> a(200), b(200);
+    for (int k = 0; k < n; k++) {
+        const int len = 1 + (int)(next() % 200);
+        const float scale = std::ldexp(1.0f, (int)(next() % 230) - 133);
+        for (int i = 0; i < len; i++) {
+            const uint64_t u = next();
+            float v = ((float)(u >> 40) / (float)(1u << 24) - 0.5f) * scale;
+            if (u % 97 == 0) v = (u & 1) ? INFINITY : -INFINITY;
+            if (u % 89 == 0) v = 0.f;
+            if (k % 50 == 0 && u % 83 == 0) v = NAN;
+            x[i] = v;
+        }
+        const float s1 = quant_i8(x.data(), len, a.data()), s2 = quant_i8_scalar(x.data(), len, b.data());
+        bad += fbits(s1) != fbits(s2) || std::memcmp(a.data(), b.data(), len) != 0;
+    }
+#if defined(__AVX2__)
+    for (int k = 0; k < n; k++) {
+        alignas(32) float v[8], r[8];
+        for (int j = 0; j < 8; j++) {
+            const uint64_t u = next();
+            uint32_t bits = (uint32_t)u;
+            if ((bits & 0x7f800000u) == 0x7f800000u) bits &= 0xff800000u;  // infinities, no NaNs
+            v[j] = (j & 1) ? bitsf(bits) : ((float)(int)(u % 2001) - 1000.f) * 0.5f;  // exact halves
+        }
+        _mm256_store_ps(r, round_away8(_mm256_load_ps(v)));
+        for (int j = 0; j < 8; j++) bad += fbits(r[j]) != fbits(std::round(v[j]));
+    }
+#endif
     return bad;
 }
 

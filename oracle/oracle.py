@@ -41,6 +41,7 @@ def lib():
             "orc_cq_row": (I, [P, P, I, I, I, I, P]),
             "orc_lane_sums_check": (I, [C.c_uint64, I]),
             "orc_nexp_check": (I, [C.c_uint64, I]),
+            "orc_quant_check": (I, [C.c_uint64, I]),
             "orc_attend_head": (None, [P, P, P, P, I, I, I, P, I, P, I, I, P]),
             "orc_model_load": (P, [P, C.c_uint64]),
             "orc_model_free": (None, [P]),

@@ -132,6 +132,12 @@ def test_vector_inline_exp_equals_the_scalar_one():
     assert orc.lib().orc_nexp_check(11, 200000) == 0
 
 
+def test_vector_quantizer_equals_the_scalar_one():
+    # quant_i8 (qlinear.rs:77-88) eight values at a time against the plain
+    # loop, and its half-away rounding against std::round, bit for bit
+    assert orc.lib().orc_quant_check(5, 20000) == 0
+
+
 def test_dot16_matches_the_scalar_order():
     i = np.arange(768)
     x = ((((i * 37) % 101).astype(np.float32) - np.float32(50.0)) * np.float32(0.013)).astype(np.float32)
