@@ -39,11 +39,116 @@
 #include <algorithm>
 #include <functional>
 #include <stdexcept>
+#include <mutex>
+#include <condition_variable>
 #if defined(__AVX2__)
 #include <immintrin.h>
 #endif
 
 namespace orc {
+
+// ---------------------------------------------------------------- the team
+
+// What the reference's worker team (crates/needle-engine/src/team.rs) does
+// for one sequence: the rows of a matmul, the heads of attention and the
+// rows of a chunk's post block split over host threads. Every item is
+// computed by one thread exactly as the single-threaded loop computes it,
+// so results do not depend on the team's size. One thread (no team) unless
+// orc_set_team asks for more; the threads of a sequence-parallel batch
+// (run_parallel) never use it.
+thread_local bool t_no_team = false;
+
+class Team {
+public:
+    ~Team() { resize(1); }
+    int size() const { return (int)workers_.size() + 1; }
+    void resize(int n) {
+        stop_.store(true);
+        gen_.fetch_add(1);
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            cv_.notify_all();
+        }
+        for (auto& w : workers_) w.join();
+        workers_.clear();
+        stop_.store(false);
+        // each worker starts from the counter as it is now, read here: a
+        // job published before a new thread first runs is still its job
+        const uint64_t start = gen_.load();
+        for (int k = 1; k < n; k++) workers_.emplace_back([this, start] { loop(start); });
+    }
+    // f(i0, i1) over contiguous slices of [0, items), the calling thread
+    // taking slices too; returns when every slice is done.
+    void run(int items, const std::function<void(int, int)>& f) {
+        if (items <= 0) return;
+        if (workers_.empty() || t_no_team || items == 1) {
+            f(0, items);
+            return;
+        }
+        job_ = &f;
+        items_ = items;
+        slices_ = std::min(items, 4 * size());
+        next_.store(0);
+        busy_.store((int)workers_.size());
+        gen_.fetch_add(1);  // publishes the job (sequentially consistent)
+        if (sleeping_.load() > 0) {
+            std::lock_guard<std::mutex> lk(mu_);
+            cv_.notify_all();
+        }
+        work();
+        while (busy_.load() != 0) pause();
+        job_ = nullptr;
+    }
+
+private:
+    static void pause() {
+#if defined(__x86_64__)
+        __builtin_ia32_pause();
+#endif
+    }
+    void work() {
+        for (;;) {
+            const int k = next_.fetch_add(1);
+            if (k >= slices_) return;
+            (*job_)((int)((int64_t)items_ * k / slices_), (int)((int64_t)items_ * (k + 1) / slices_));
+        }
+    }
+    // A worker spins on the job counter for a while after each job (a
+    // sequence's parallel regions come tens of microseconds apart), then
+    // sleeps; a sleeper counts itself before it tests the counter, and run()
+    // bumps the counter before it reads the sleepers, so one of the two
+    // always sees the other.
+    void loop(uint64_t seen) {
+        t_no_team = true;
+        for (;;) {
+            int spins = 0;
+            while (gen_.load() == seen && spins < (1 << 16)) {
+                pause();
+                spins++;
+            }
+            if (gen_.load() == seen) {
+                std::unique_lock<std::mutex> lk(mu_);
+                sleeping_.fetch_add(1);
+                cv_.wait(lk, [&] { return gen_.load() != seen; });
+                sleeping_.fetch_sub(1);
+            }
+            seen = gen_.load();
+            if (stop_.load()) return;
+            work();
+            busy_.fetch_sub(1);
+        }
+    }
+    std::vector<std::thread> workers_;
+    std::mutex mu_;
+    std::condition_variable cv_;
+    const std::function<void(int, int)>* job_ = nullptr;
+    int items_ = 0, slices_ = 0;
+    std::atomic<int> next_{0}, busy_{0}, sleeping_{0};
+    std::atomic<uint64_t> gen_{0};
+    std::atomic<bool> stop_{false};
+};
+
+static Team g_team;
 
 // ---------------------------------------------------------------- numerics
 
@@ -875,10 +980,9 @@ float prefill_row_ref(const QMat& q, int r, const QAct& a, int t, bool block) {
 // rows side by side, each row's floats the same single ops in the same
 // order (its scale product, its four lane fma chains over the groups, the
 // final two-level sum).
-static void decode_rows(const QMat& q, const QAct& a, float* y) {
-    int r = 0;
+static void decode_rows_range(const QMat& q, const QAct& a, float* y, int r, int r_end) {
 #if defined(__AVX2__)
-    for (; r + 8 <= q.out; r += 8) {
+    for (; r + 8 <= r_end; r += 8) {
         const QPart* pts[8];
         float cbs[8];
         for (int k = 0; k < 8; k++) {
@@ -890,7 +994,7 @@ static void decode_rows(const QMat& q, const QAct& a, float* y) {
         if (q.width == 4 && q.no_min && a.no_min) {
             // the code bytes of the block two blocks on, into the caches
             // while this one is summed (rows r .. r + 7 are contiguous)
-            if (r + 24 <= q.out) {
+            if (r + 24 <= r_end) {
                 const uint8_t* nxt = q.codes.data() + (size_t)(r + 16) * q.groups * 64;
                 for (int b = 0; b < 8 * q.groups * 64; b += 64) _mm_prefetch((const char*)(nxt + b), _MM_HINT_T0);
             }
@@ -939,7 +1043,16 @@ static void decode_rows(const QMat& q, const QAct& a, float* y) {
         _mm256_storeu_ps(y + r, _mm256_add_ps(_mm256_add_ps(ln[0], ln[1]), _mm256_add_ps(ln[2], ln[3])));
     }
 #endif
-    for (; r < q.out; r++) y[r] = decode_row_ref(q, r, a);
+    for (; r < r_end; r++) y[r] = decode_row_ref(q, r, a);
+}
+
+static void decode_rows(const QMat& q, const QAct& a, float* y) {
+    const int blocks = q.out / 8;
+    if (q.out < 256) {
+        decode_rows_range(q, a, y, 0, q.out);
+        return;
+    }
+    g_team.run(blocks, [&](int b0, int b1) { decode_rows_range(q, a, y, 8 * b0, b1 == blocks ? q.out : 8 * b1); });
 }
 
 // qlinear.rs:366-419, 460-487: decode kernel for one token, prefill kernel
@@ -949,8 +1062,10 @@ static void qmat_matmul(const QMat& q, const QAct& a, float* y, int ldy, int col
         decode_rows(q, a, y + col0);
     } else {
         int blocked = a.rows / 4 * 4;
-        for (int t = 0; t < a.rows; t++)
-            for (int r = 0; r < q.out; r++) y[(size_t)t * ldy + col0 + r] = prefill_row_ref(q, r, a, t, t < blocked);
+        g_team.run(q.out, [&](int r0, int r1) {
+            for (int t = 0; t < a.rows; t++)
+                for (int r = r0; r < r1; r++) y[(size_t)t * ldy + col0 + r] = prefill_row_ref(q, r, a, t, t < blocked);
+        });
     }
 }
 
@@ -1777,16 +1892,20 @@ static void layer_native(const Model& m, int l, Session& st, int64_t p0, std::ve
         int group = nh / nkv;
         bool nested = t > 1;
         int window = c.window(l);
+        std::vector<std::vector<int64_t>> slots(t);
         for (int i = 0; i < t; i++) {
             int64_t pos = p0 + i;
             std::vector<Range> keys = key_ranges(pos, end, window, st);
-            std::vector<int64_t> slots;
             for (auto& r : keys)
-                for (int64_t q = r.a; q < r.b; q++) slots.push_back(slot_of(q, st));
-            for (int hh = 0; hh < nh; hh++)
-                attend_head_ref(kv, qkv.data() + (size_t)i * width + hh * qk, hh / group, slots, nested,
-                                att.data() + ((size_t)i * nh + hh) * vd);
+                for (int64_t q = r.a; q < r.b; q++) slots[i].push_back(slot_of(q, st));
         }
+        g_team.run(t * nh, [&](int j0, int j1) {
+            for (int j = j0; j < j1; j++) {
+                const int i = j / nh, hh = j % nh;
+                attend_head_ref(kv, qkv.data() + (size_t)i * width + hh * qk, hh / group, slots[i], nested,
+                                att.data() + ((size_t)i * nh + hh) * vd);
+            }
+        });
     }
     g_trace.put(tag + "attn", att.data(), att.size());
     for (int i = 0; i < t; i++) silu_div(att.data() + (size_t)i * nh * vd, proj.data() + (size_t)i * pout + width, nh * vd);
@@ -1803,7 +1922,8 @@ static void layer_native(const Model& m, int l, Session& st, int64_t p0, std::ve
     // (k) post block
     float ga = 1.0f / (lexpf(-L.attn_gate) + 1.0f);
     std::vector<float> mlpv((size_t)t * d);
-    for (int i = 0; i < t; i++) {
+    g_team.run(t, [&](int i0, int i1) {
+    for (int i = i0; i < i1; i++) {
         std::vector<float> on(d), x2(d), h2(d), mlp(d);
         zcn(o.data() + (size_t)i * d, L.post_norm.data(), on.data(), d);
         for (int k = 0; k < d; k++) x2[k] = std::fmaf(on[k], ga, x1[(size_t)i * d + k]);
@@ -1832,6 +1952,7 @@ static void layer_native(const Model& m, int l, Session& st, int64_t p0, std::ve
             }
         }
     }
+    });
     g_trace.put(tag + "mlp", mlpv.data(), mlpv.size());
     g_trace.put(tag + "xs", xs.data(), xs.size());
 }
@@ -2656,6 +2777,32 @@ int orc_quant_check(uint64_t seed, int n) {
     return bad;
 }
 
+// The team one sequence's forward splits its matmul rows, attention heads
+// and post-block rows over (1: the calling thread alone). Not to be called
+// while a forward runs.
+void orc_set_team(int threads) { g_team.resize(std::max(1, std::min(threads, 256))); }
+
+// Resizes the team and runs small jobs on it `rounds` times in quick
+// succession (a job right after each resize included); returns the jobs
+// whose sum came out wrong. The team is left at one thread.
+int orc_team_stress(int rounds) {
+    int bad = 0;
+    for (int k = 0; k < rounds; k++) {
+        g_team.resize(2 + k % 7);
+        for (int j = 0; j < 4; j++) {
+            const int items = 1 + (k * 7 + j * 13) % 200;
+            std::vector<int> hit(items, 0);
+            g_team.run(items, [&](int i0, int i1) {
+                for (int i = i0; i < i1; i++) hit[i]++;
+            });
+            for (int i = 0; i < items; i++) bad += hit[i] != 1;
+        }
+    }
+    g_team.resize(1);
+    return bad;
+}
+int orc_team_size() { return g_team.size(); }
+
 // QMat::row of a raw CQ matrix of record bits `bits` (qlinear.rs:309-323).
 int orc_cq_row(const uint8_t* codes, const uint16_t* norms, int rows, int in_dim, int bits, int r, float* out) {
     try {
@@ -2913,6 +3060,7 @@ int orc_generate_batch(void* mp, int S, const uint32_t* prompts, int n, int step
     size_t mb = (m.c.out_rows() + 7) / 8;
     std::atomic<int> next(0), bad(0);
     auto work = [&]() {
+        t_no_team = true;  // a sequence a thread: no team inside
         for (;;) {
             int s = next.fetch_add(1);
             if (s >= S) return;
@@ -2939,6 +3087,7 @@ struct OrcBatch {
 static void run_parallel(int S, int threads, const std::function<void(int)>& f) {
     std::atomic<int> next(0);
     auto work = [&]() {
+        t_no_team = true;  // a sequence a thread: no team inside
         for (;;) {
             int s = next.fetch_add(1);
             if (s >= S) return;
@@ -3000,6 +3149,7 @@ int orc_prefill_batch(void* mp, int S, const uint32_t* prompts, int n, float* ou
     Model& m = *(Model*)mp;
     std::atomic<int> next(0), bad(0);
     auto work = [&]() {
+        t_no_team = true;  // a sequence a thread: no team inside
         for (;;) {
             int s = next.fetch_add(1);
             if (s >= S) return;

@@ -42,6 +42,9 @@ def lib():
             "orc_lane_sums_check": (I, [C.c_uint64, I]),
             "orc_nexp_check": (I, [C.c_uint64, I]),
             "orc_quant_check": (I, [C.c_uint64, I]),
+            "orc_set_team": (None, [I]),
+            "orc_team_size": (I, []),
+            "orc_team_stress": (I, [I]),
             "orc_attend_head": (None, [P, P, P, P, I, I, I, P, I, P, I, I, P]),
             "orc_model_load": (P, [P, C.c_uint64]),
             "orc_model_free": (None, [P]),
@@ -137,6 +140,17 @@ def synth_cact(seed=0, std=0.02, bits=None, heads=(), **shape) -> bytes:
     if lib().orc_synth_cact(*args, _p(buf), n.value, C.byref(n)) != 0:
         raise RuntimeError(lib().orc_last_error().decode())
     return buf.tobytes()
+
+
+def set_team(threads: int) -> None:
+    """Split one sequence's matmul rows, attention heads and post-block rows
+    over `threads` host threads (1: none), as the reference's worker team
+    does; results do not depend on it."""
+    lib().orc_set_team(int(threads))
+
+
+def team_size() -> int:
+    return lib().orc_team_size()
 
 
 def f32_to_f16_bits(x: float) -> int:

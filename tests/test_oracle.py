@@ -320,3 +320,36 @@ def test_truncate_recomputes_from_scratch(small_archive):
     a = s.forward(ids[20:23])[0]
     b = fresh.forward(ids[20:23])[0]
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+@pytest.mark.timeout(120)
+def test_team_resizes_and_runs_back_to_back():
+    # every slice of every job runs exactly once, with jobs issued straight
+    # after each resize (new threads that have not yet run included)
+    assert orc.lib().orc_team_stress(300) == 0
+    assert orc.team_size() == 1
+
+
+@pytest.mark.timeout(300)
+def test_team_does_not_change_a_result(small_archive):
+    """One sequence's forward split over a worker team (the reference's
+    team.rs role: matmul rows, attention heads, post-block rows) gives the
+    single thread's logits and tokens bit for bit, through prefill chunks,
+    one-token steps and a sequence-parallel batch."""
+    m = orc.Model(small_archive)
+    ids = (np.arange(70) * 37 % 1000).astype(np.uint32)
+    runs = []
+    try:
+        for team in (1, 3, 8):
+            orc.set_team(team)
+            assert orc.team_size() == team
+            s = m.session()
+            first = s.forward(ids[:45])[0]
+            steps = [s.forward(ids[k:k + 1])[0] for k in range(45, 52)]
+            toks = m.generate(ids[:33], 9)
+            batch = m.prefill_batch(np.stack([ids[:40], ids[10:50]]), threads=2)
+            runs.append([first.view(np.uint32), *(x.view(np.uint32) for x in steps), toks, batch.view(np.uint32)])
+    finally:
+        orc.set_team(1)
+    for other in runs[1:]:
+        assert all(np.array_equal(a, b) for a, b in zip(runs[0], other))
