@@ -1429,7 +1429,27 @@ float chunk_exp(float* s, int l, float m) {
 
 // infer.rs:2171-2217 (scalar tail, which the SIMD arms match)
 static void digits21(const float* w, int n, float qw, int8_t* hi, int8_t* mid, int8_t* lo) {
-    for (int i = 0; i < n; i++) {
+    int i = 0;
+#if defined(__AVX2__)
+    // eight at a time: the product and its half-away rounding as single
+    // ops, the conversion truncating (a NaN or out-of-range value gives
+    // INT32_MIN as cvttss2si does), the digits by arithmetic shifts and
+    // masks, then narrowed to bytes by truncation
+    const __m256 qv = _mm256_set1_ps(qw);
+    for (; i + 8 <= n; i += 8) {
+        const __m256i wq = _mm256_cvttps_epi32(round_away8(_mm256_mul_ps(_mm256_loadu_ps(w + i), qv)));
+        alignas(32) int32_t h[8], md[8], l[8];
+        _mm256_store_si256((__m256i*)h, _mm256_srai_epi32(wq, 14));
+        _mm256_store_si256((__m256i*)md, _mm256_and_si256(_mm256_srai_epi32(wq, 7), _mm256_set1_epi32(127)));
+        _mm256_store_si256((__m256i*)l, _mm256_and_si256(wq, _mm256_set1_epi32(127)));
+        for (int k = 0; k < 8; k++) {
+            hi[i + k] = (int8_t)h[k];
+            mid[i + k] = (int8_t)md[k];
+            lo[i + k] = (int8_t)l[k];
+        }
+    }
+#endif
+    for (; i < n; i++) {
         int32_t wq = (int32_t)rround(w[i] * qw);
         hi[i] = (int8_t)(wq >> 14);
         mid[i] = (int8_t)((wq >> 7) & 127);
@@ -1473,13 +1493,50 @@ void attend_head_ref(const KVView& kv, const float* qh, int kvh, const std::vect
             dots[i] = dot_i8(q8, kv.k8 + (sl[i] * nkv + kvh) * qk, qk);
             scale[i] = kv.ks[sl[i] * nkv + kvh];
         }
-        for (int i = 0; i < blocked; i++) s[i] = (scale[i] * (float)dots[i]) * qs;
+        // the scores, their max, the value-scaled weights and their max:
+        // eight keys at a time where the build has AVX2 (each value the same
+        // single ops; a max ignores a NaN as fmax does, and the order of a
+        // max changes at most the sign of a zero maximum, which no later
+        // result depends on)
+        int i0 = 0;
+        float m = -INFINITY, wmax = 0.f;
+#if defined(__AVX2__)
+        __m256 mv = _mm256_set1_ps(-INFINITY);
+        const __m256 qsv = _mm256_set1_ps(qs);
+        for (; i0 + 8 <= blocked; i0 += 8) {
+            const __m256 sc = _mm256_mul_ps(_mm256_mul_ps(_mm256_loadu_ps(scale.data() + i0),
+                                                          _mm256_cvtepi32_ps(_mm256_loadu_si256((const __m256i*)(dots.data() + i0)))),
+                                            qsv);
+            _mm256_storeu_ps(s.data() + i0, sc);
+            mv = _mm256_max_ps(sc, mv);
+        }
+        {
+            alignas(32) float mm[8];
+            _mm256_store_ps(mm, mv);
+            for (int k = 0; k < 8; k++) m = rmax(m, mm[k]);
+        }
+#endif
+        for (int i = i0; i < blocked; i++) s[i] = (scale[i] * (float)dots[i]) * qs;
         for (int i = blocked; i < len; i++) s[i] = (scale[i] * qs) * (float)dots[i];
-        float m = -INFINITY;
-        for (int i = 0; i < len; i++) m = rmax(m, s[i]);
+        for (int i = i0; i < len; i++) m = rmax(m, s[i]);
         float sum = chunk_exp(s.data(), len, m);
-        float wmax = 0.f;
-        for (int i = 0; i < len; i++) {
+        i0 = 0;
+#if defined(__AVX2__)
+        __m256 wv = _mm256_setzero_ps();
+        for (; i0 + 8 <= len; i0 += 8) {
+            alignas(32) float vsc[8];
+            for (int k = 0; k < 8; k++) vsc[k] = kv.vs[sl[i0 + k] * nkv + kvh];
+            const __m256 w = _mm256_mul_ps(_mm256_loadu_ps(s.data() + i0), _mm256_load_ps(vsc));
+            _mm256_storeu_ps(s.data() + i0, w);
+            wv = _mm256_max_ps(w, wv);
+        }
+        {
+            alignas(32) float ww[8];
+            _mm256_store_ps(ww, wv);
+            for (int k = 0; k < 8; k++) wmax = rmax(wmax, ww[k]);
+        }
+#endif
+        for (int i = i0; i < len; i++) {
             s[i] *= kv.vs[sl[i] * nkv + kvh];
             wmax = rmax(wmax, s[i]);
         }
