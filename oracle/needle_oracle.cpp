@@ -41,6 +41,7 @@
 #include <stdexcept>
 #include <mutex>
 #include <condition_variable>
+#include <exception>
 #if defined(__AVX2__)
 #include <immintrin.h>
 #endif
@@ -78,7 +79,8 @@ public:
         for (int k = 1; k < n; k++) workers_.emplace_back([this, start] { loop(start); });
     }
     // f(i0, i1) over contiguous slices of [0, items), the calling thread
-    // taking slices too; returns when every slice is done.
+    // taking slices too; returns when every slice is done, then rethrows
+    // the first exception a slice threw (the other slices still ran).
     void run(int items, const std::function<void(int, int)>& f) {
         if (items <= 0) return;
         if (workers_.empty() || t_no_team || items == 1) {
@@ -98,6 +100,11 @@ public:
         work();
         while (busy_.load() != 0) pause();
         job_ = nullptr;
+        if (error_) {
+            std::exception_ptr e = error_;
+            error_ = nullptr;
+            std::rethrow_exception(e);
+        }
     }
 
 private:
@@ -110,7 +117,12 @@ private:
         for (;;) {
             const int k = next_.fetch_add(1);
             if (k >= slices_) return;
-            (*job_)((int)((int64_t)items_ * k / slices_), (int)((int64_t)items_ * (k + 1) / slices_));
+            try {
+                (*job_)((int)((int64_t)items_ * k / slices_), (int)((int64_t)items_ * (k + 1) / slices_));
+            } catch (...) {
+                std::lock_guard<std::mutex> lk(err_mu_);
+                if (!error_) error_ = std::current_exception();
+            }
         }
     }
     // A worker spins on the job counter for a while after each job (a
@@ -139,7 +151,8 @@ private:
         }
     }
     std::vector<std::thread> workers_;
-    std::mutex mu_;
+    std::mutex mu_, err_mu_;
+    std::exception_ptr error_;
     std::condition_variable cv_;
     const std::function<void(int, int)>* job_ = nullptr;
     int items_ = 0, slices_ = 0;
@@ -2854,6 +2867,21 @@ int orc_team_stress(int rounds) {
             });
             for (int i = 0; i < items; i++) bad += hit[i] != 1;
         }
+        // a slice that throws: every other slice still runs, and the
+        // caller gets the exception
+        const int items = 64;
+        std::vector<int> hit(items, 0);
+        bool caught = false;
+        try {
+            g_team.run(items, [&](int i0, int i1) {
+                for (int i = i0; i < i1; i++) hit[i]++;
+                if (i0 == 0) throw std::runtime_error("slice 0");
+            });
+        } catch (const std::runtime_error&) {
+            caught = true;
+        }
+        bad += !caught;
+        for (int i = 0; i < items; i++) bad += hit[i] != 1;
     }
     g_team.resize(1);
     return bad;
