@@ -16,7 +16,8 @@
 // Where the build has AVX2 the hot loops run vectorised without changing a
 // result: the int8 lane sums and dots (4-bit codes looked up from their
 // packed bytes; byte pair products into int16 only when no operand is -128,
-// else int16 pair products into int32: nothing saturates), the
+// else int16 pair products into int32, or AVX-512 VNNI byte products into
+// int32 where the host has it: nothing saturates), the
 // decode combine eight rows side by side, the Kronecker passes eight
 // outputs side by side, the inline exp and the int8 quantizer eight values
 // at a time (each row's, output's or value's float ops the same single
@@ -30,6 +31,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <cstdlib>
 #include <cstdio>
 #include <string>
 #include <vector>
@@ -627,6 +629,7 @@ static void unpack_lsb(const uint8_t* packed, int width, int n, uint8_t* out) {
 struct QPart {
     int r0 = 0;
     int8_t vals[16];
+    uint8_t vals_b[16];  // vals + 128, as unsigned bytes
     float cbs;
     float fvals[16];
 };
@@ -681,6 +684,7 @@ static void qmat_init(QMat& q, int bits, int out, int in_dim, const uint8_t* cod
         int k = bits == TERNARY ? (c == 3 ? 0 : c + 1) : c;
         bool in = c < (1 << q.width) && k < (int)cb.size();
         pt.vals[c] = in ? cb8[k] : 0;
+        pt.vals_b[c] = (uint8_t)(pt.vals[c] + 128);
         pt.fvals[c] = in ? cb[k] : 0.f;
     }
     q.parts.assign(1, pt);
@@ -753,6 +757,10 @@ struct QAct {
     std::vector<int8_t> x8eo;
     std::vector<uint8_t> ax8eo;
     bool no_min = false;
+    // each group's 64 even elements, then its 64 odd ones; and per group the
+    // sums of xq over the four 4-bit decode lanes (lane (p % 32) / 8)
+    std::vector<int8_t> x8v;
+    std::vector<int32_t> sumx;  // [rows][groups][4]
 };
 
 // qlinear.rs:152-164
@@ -794,6 +802,14 @@ static QAct qact_new(const float* x, int rows, int in_dim) {
                     a.ax8eo[at] = (uint8_t)std::abs((int)v);
                     a.no_min &= v != -128;
                 }
+    a.x8v.resize(a.xq.size());
+    a.sumx.assign(a.xq.size() / GROUP * 4, 0);
+    for (size_t g = 0; g < a.xq.size() / GROUP; g++)
+        for (int p = 0; p < GROUP; p++) {
+            const int8_t v = a.xq[g * GROUP + p];
+            a.x8v[g * GROUP + (p & 1) * 64 + p / 2] = v;
+            a.sumx[g * 4 + (p % 32) / 8] += v;
+        }
     return a;
 }
 
@@ -939,9 +955,51 @@ static inline __m128i lane_sums_codes4_ub(const uint8_t* codes, __m256i tbl, con
 }
 #endif
 
+#if defined(__AVX2__) && defined(__x86_64__)
+// AVX-512 VNNI, chosen at run time where the host has it (the rest of this
+// file needs only AVX2).
+#define ORC_VNNI __attribute__((target("avx512f,avx512bw,avx512vl,avx512vnni")))
+static const bool g_vnni = __builtin_cpu_supports("avx512f") && __builtin_cpu_supports("avx512bw") &&
+                           __builtin_cpu_supports("avx512vl") && __builtin_cpu_supports("avx512vnni") &&
+                           !std::getenv("ORC_NO_VNNI");
+
+// The four lane sums of a 4-bit group from its 64 code bytes: the codebook
+// looked up sixty-four codes at a time into unsigned bytes w + 128 (tblb:
+// vals_b in every 128-bit quarter), then vpdpbusd adds each four adjacent
+// (w + 128) * x byte products into an int32, exactly (no saturation). In
+// the even and the odd half alike int32 e holds p in [8e, 8e + 8), lane
+// e % 4, so the four quarters summed are the lanes, less 128 times the
+// lane's activation sum. x8v, sumx4: the group as QAct::x8v / sumx hold it.
+ORC_VNNI static inline __m128i lane_sums_codes4_vnni(const uint8_t* codes, __m512i tblb, const int8_t* x8v, __m128i sumx4) {
+    const __m512i c = _mm512_loadu_si512(codes), m4 = _mm512_set1_epi8(0x0F);
+    const __m512i we = _mm512_shuffle_epi8(tblb, _mm512_and_si512(c, m4));
+    const __m512i wo = _mm512_shuffle_epi8(tblb, _mm512_and_si512(_mm512_srli_epi16(c, 4), m4));
+    __m512i acc = _mm512_dpbusd_epi32(_mm512_setzero_si512(), we, _mm512_loadu_si512(x8v));
+    acc = _mm512_dpbusd_epi32(acc, wo, _mm512_loadu_si512(x8v + 64));
+    const __m256i h = _mm256_add_epi32(_mm512_castsi512_si256(acc), _mm512_extracti64x4_epi64(acc, 1));
+    const __m128i l = _mm_add_epi32(_mm256_castsi256_si128(h), _mm256_extracti128_si256(h, 1));
+    return _mm_sub_epi32(l, _mm_slli_epi32(sumx4, 7));
+}
+
+ORC_VNNI static void lane_sums_vnni(const uint8_t* codes, const uint8_t* vals_b, const int8_t* x8v, const int32_t* sumx,
+                                    int32_t s[4]) {
+    _mm_storeu_si128((__m128i*)s, lane_sums_codes4_vnni(codes, _mm512_broadcast_i32x4(_mm_loadu_si128((const __m128i*)vals_b)),
+                                                        x8v, _mm_loadu_si128((const __m128i*)sumx)));
+}
+#else
+static const bool g_vnni = false;
+#endif
+
 // The lane sums of row r (part pt), group g against activation row t.
 static inline void lane_sums(const QMat& q, const QPart& pt, int r, int g, const QAct& a, int t, int32_t s[4]) {
     const size_t ag = ((size_t)t * a.groups + g) * GROUP;
+#if defined(__AVX2__) && defined(__x86_64__)
+    if (q.width == 4 && g_vnni) {
+        lane_sums_vnni(q.codes.data() + ((size_t)r * q.groups + g) * 64, pt.vals_b, a.x8v.data() + ag, a.sumx.data() + ag / GROUP * 4,
+                       s);
+        return;
+    }
+#endif
 #if defined(__AVX2__)
     if (q.width == 4 && q.no_min && a.no_min) {
         const __m256i tbl = _mm256_broadcastsi128_si256(_mm_loadu_si128((const __m128i*)pt.vals));
@@ -993,7 +1051,57 @@ float prefill_row_ref(const QMat& q, int r, const QAct& a, int t, bool block) {
 // rows side by side, each row's floats the same single ops in the same
 // order (its scale product, its four lane fma chains over the groups, the
 // final two-level sum).
+#if defined(__AVX2__) && defined(__x86_64__)
+// decode_rows_range's eight-row blocks of a 4-bit matrix with the lane sums
+// on AVX-512 VNNI (lane_sums_codes4_vnni), the floats as there. Returns the
+// first row it left (the block tail) for the caller.
+ORC_VNNI static int decode_rows_vnni(const QMat& q, const QAct& a, float* y, int r, int r_end) {
+    for (; r + 8 <= r_end; r += 8) {
+        if (r + 24 <= r_end) {
+            const uint8_t* nxt = q.codes.data() + (size_t)(r + 16) * q.groups * 64;
+            for (int b = 0; b < 8 * q.groups * 64; b += 64) _mm_prefetch((const char*)(nxt + b), _MM_HINT_T0);
+        }
+        float cbs[8];
+        __m512i tbl[8];
+        for (int k = 0; k < 8; k++) {
+            const QPart& pt = q.part(r + k);
+            cbs[k] = pt.cbs;
+            tbl[k] = _mm512_broadcast_i32x4(_mm_loadu_si128((const __m128i*)pt.vals_b));
+        }
+        const __m256 cbv = _mm256_loadu_ps(cbs);
+        __m256 ln[4] = {_mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps()};
+        for (int g = 0; g < q.groups; g++) {
+            const size_t ag = (size_t)g * GROUP;
+            const __m128i sx4 = _mm_loadu_si128((const __m128i*)(a.sumx.data() + (size_t)g * 4));
+            __m128i v[8];  // row k's four lane sums
+            for (int k = 0; k < 8; k++)
+                v[k] = lane_sums_codes4_vnni(q.codes.data() + ((size_t)(r + k) * q.groups + g) * 64, tbl[k], a.x8v.data() + ag, sx4);
+            __m128i lo[4], hi[4];  // transposed: lane l of rows 0..7
+            for (int h = 0; h < 2; h++) {
+                const __m128i* w = v + 4 * h;
+                const __m128i t0 = _mm_unpacklo_epi32(w[0], w[1]), t1 = _mm_unpackhi_epi32(w[0], w[1]);
+                const __m128i t2 = _mm_unpacklo_epi32(w[2], w[3]), t3 = _mm_unpackhi_epi32(w[2], w[3]);
+                __m128i* o = h ? hi : lo;
+                o[0] = _mm_unpacklo_epi64(t0, t2);
+                o[1] = _mm_unpackhi_epi64(t0, t2);
+                o[2] = _mm_unpacklo_epi64(t1, t3);
+                o[3] = _mm_unpackhi_epi64(t1, t3);
+            }
+            alignas(32) float nf[8];
+            for (int k = 0; k < 8; k++) nf[k] = q.normf[(size_t)(r + k) * q.groups + g];
+            const __m256 sc = _mm256_mul_ps(_mm256_mul_ps(_mm256_set1_ps(a.sx[g]), cbv), _mm256_load_ps(nf));
+            for (int l = 0; l < 4; l++) ln[l] = _mm256_fmadd_ps(_mm256_cvtepi32_ps(_mm256_set_m128i(hi[l], lo[l])), sc, ln[l]);
+        }
+        _mm256_storeu_ps(y + r, _mm256_add_ps(_mm256_add_ps(ln[0], ln[1]), _mm256_add_ps(ln[2], ln[3])));
+    }
+    return r;
+}
+#endif
+
 static void decode_rows_range(const QMat& q, const QAct& a, float* y, int r, int r_end) {
+#if defined(__AVX2__) && defined(__x86_64__)
+    if (q.width == 4 && g_vnni) r = decode_rows_vnni(q, a, y, r, r_end);
+#endif
 #if defined(__AVX2__)
     for (; r + 8 <= r_end; r += 8) {
         const QPart* pts[8];
@@ -2759,6 +2867,21 @@ int orc_lane_sums_check(uint64_t seed, int n) {
                          lane_sums_codes4_ub(codes, _mm256_broadcastsi128_si256(_mm_loadu_si128((const __m128i*)vn)), x8, ax));
         lane_sums_scalar(wn, xn, 4, b);
         differ |= std::memcmp(a, b, sizeof a) != 0;
+#if defined(__x86_64__)
+        if (g_vnni) {  // the VNNI form over all of int8 (no -128 restriction)
+            uint8_t vb[16];
+            for (int c = 0; c < 16; c++) vb[c] = (uint8_t)(vals[c] + 128);
+            int8_t x8v[GROUP];
+            int32_t sumx[4] = {0, 0, 0, 0};
+            for (int p = 0; p < GROUP; p++) {
+                x8v[(p & 1) * 64 + p / 2] = x[p];
+                sumx[(p % 32) / 8] += x[p];
+            }
+            lane_sums_vnni(codes, vb, x8v, sumx, a);
+            lane_sums_scalar(wv, x, 4, b);
+            differ |= std::memcmp(a, b, sizeof a) != 0;
+        }
+#endif
 #endif
         bad += differ;
     }
@@ -2887,6 +3010,9 @@ int orc_team_stress(int rounds) {
     return bad;
 }
 int orc_team_size() { return g_team.size(); }
+
+// 1 when the 4-bit matmuls run their lane sums on AVX-512 VNNI.
+int orc_vnni() { return g_vnni ? 1 : 0; }
 
 // QMat::row of a raw CQ matrix of record bits `bits` (qlinear.rs:309-323).
 int orc_cq_row(const uint8_t* codes, const uint16_t* norms, int rows, int in_dim, int bits, int r, float* out) {
