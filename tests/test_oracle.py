@@ -12,6 +12,7 @@ import pyref
 from oracle import oracle as orc
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def golden(name):
@@ -353,3 +354,36 @@ def test_team_does_not_change_a_result(small_archive):
         orc.set_team(1)
     for other in runs[1:]:
         assert all(np.array_equal(a, b) for a, b in zip(runs[0], other))
+
+
+@pytest.mark.timeout(300)
+def test_avx2_and_vnni_lane_sums_give_the_same_streams(small_archive, tmp_path):
+    """The 4-bit matmuls run their lane sums on AVX-512 VNNI where the host
+    has it and on AVX2 otherwise (ORC_NO_VNNI forces the latter; the choice
+    is made when the library loads, so the AVX2 run is a subprocess): both
+    give the same logits and tokens bit for bit."""
+    import hashlib
+    import subprocess
+    import sys
+
+    path = tmp_path / "small.cact"
+    path.write_bytes(small_archive)
+    code = (
+        "import sys, hashlib, numpy as np\n"
+        f"sys.path.insert(0, {ROOT!r})\n"
+        "from oracle import oracle as orc\n"
+        "m = orc.Model(open(sys.argv[1], 'rb').read())\n"
+        "ids = (np.arange(60) * 41 % 1000).astype(np.uint32)\n"
+        "toks, lg = m.generate(ids, 8, want_logits=True)\n"
+        "print(orc.lib().orc_vnni(), hashlib.sha256(lg.tobytes() + toks.tobytes()).hexdigest())\n"
+    )
+    runs = {}
+    for off in ("0", "1"):
+        env = dict(os.environ)
+        env.pop("ORC_NO_VNNI", None)
+        if off == "1":
+            env["ORC_NO_VNNI"] = "1"
+        out = subprocess.check_output([sys.executable, "-c", code, str(path)], env=env, text=True).split()
+        runs[off] = out
+    assert runs["1"][0] == "0"
+    assert runs["0"][1] == runs["1"][1]
