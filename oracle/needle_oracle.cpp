@@ -1098,6 +1098,52 @@ ORC_VNNI static int decode_rows_vnni(const QMat& q, const QAct& a, float* y, int
 }
 #endif
 
+#if defined(__AVX2__) && defined(__x86_64__)
+// prefill_row_ref for rows r .. r_end - 1 (whole eight-row blocks; returns
+// the first row left) of a 4-bit matrix and every token t of a, on AVX-512
+// VNNI: per token and group the eight rows' lane sums, their totals (exact
+// integer adds), the scale by the block or remainder rule and the fma, each
+// row's ops as the scalar form's in its order.
+ORC_VNNI static int prefill_rows_vnni(const QMat& q, const QAct& a, float* y, int ldy, int col0, int r, int r_end) {
+    const int blocked = a.rows / 4 * 4;
+    for (; r + 8 <= r_end; r += 8) {
+        float cbs[8];
+        __m512i tbl[8];
+        for (int k = 0; k < 8; k++) {
+            const QPart& pt = q.part(r + k);
+            cbs[k] = pt.cbs;
+            tbl[k] = _mm512_broadcast_i32x4(_mm_loadu_si128((const __m128i*)pt.vals_b));
+        }
+        const __m256 cbv = _mm256_loadu_ps(cbs);
+        for (int t = 0; t < a.rows; t++) {
+            __m256 acc = _mm256_setzero_ps();
+            for (int g = 0; g < q.groups; g++) {
+                const size_t ag = ((size_t)t * a.groups + g) * GROUP;
+                const __m128i sx4 = _mm_loadu_si128((const __m128i*)(a.sumx.data() + ag / GROUP * 4));
+                __m128i v[8];
+                for (int k = 0; k < 8; k++)
+                    v[k] = lane_sums_codes4_vnni(q.codes.data() + ((size_t)(r + k) * q.groups + g) * 64, tbl[k], a.x8v.data() + ag, sx4);
+                __m128i tot[2];  // rows 0-3, 4-7: the four lanes' sum
+                for (int h = 0; h < 2; h++) {
+                    const __m128i* w = v + 4 * h;
+                    const __m128i t0 = _mm_unpacklo_epi32(w[0], w[1]), t1 = _mm_unpackhi_epi32(w[0], w[1]);
+                    const __m128i t2 = _mm_unpacklo_epi32(w[2], w[3]), t3 = _mm_unpackhi_epi32(w[2], w[3]);
+                    tot[h] = _mm_add_epi32(_mm_add_epi32(_mm_unpacklo_epi64(t0, t2), _mm_unpackhi_epi64(t0, t2)),
+                                           _mm_add_epi32(_mm_unpacklo_epi64(t1, t3), _mm_unpackhi_epi64(t1, t3)));
+                }
+                alignas(32) float nf[8];
+                for (int k = 0; k < 8; k++) nf[k] = q.normf[(size_t)(r + k) * q.groups + g];
+                const __m256 nv = _mm256_load_ps(nf), sxv = _mm256_set1_ps(a.sx[(size_t)t * a.groups + g]);
+                const __m256 sc = t < blocked ? _mm256_mul_ps(_mm256_mul_ps(nv, cbv), sxv) : _mm256_mul_ps(nv, _mm256_mul_ps(cbv, sxv));
+                acc = _mm256_fmadd_ps(_mm256_cvtepi32_ps(_mm256_set_m128i(tot[1], tot[0])), sc, acc);
+            }
+            _mm256_storeu_ps(y + (size_t)t * ldy + col0 + r, acc);
+        }
+    }
+    return r;
+}
+#endif
+
 static void decode_rows_range(const QMat& q, const QAct& a, float* y, int r, int r_end) {
 #if defined(__AVX2__) && defined(__x86_64__)
     if (q.width == 4 && g_vnni) r = decode_rows_vnni(q, a, y, r, r_end);
@@ -1183,7 +1229,13 @@ static void qmat_matmul(const QMat& q, const QAct& a, float* y, int ldy, int col
         decode_rows(q, a, y + col0);
     } else {
         int blocked = a.rows / 4 * 4;
-        g_team.run(q.out, [&](int r0, int r1) {
+        const int blocks = (q.out + 7) / 8;
+        g_team.run(blocks, [&](int b0, int b1) {
+            int r0 = 8 * b0;
+            const int r1 = std::min(q.out, 8 * b1);
+#if defined(__AVX2__) && defined(__x86_64__)
+            if (q.width == 4 && g_vnni) r0 = prefill_rows_vnni(q, a, y, ldy, col0, r0, r1);
+#endif
             for (int t = 0; t < a.rows; t++)
                 for (int r = r0; r < r1; r++) y[(size_t)t * ldy + col0 + r] = prefill_row_ref(q, r, a, t, t < blocked);
         });
