@@ -1635,6 +1635,47 @@ struct KVView {
     int nkv, qk, vd;
 };
 
+#if defined(__AVX2__) && defined(__x86_64__)
+// The P·V digit-plane sums of attend_head_ref for vd = 64 on AVX-512 VNNI:
+// four keys at a time, their value rows interleaved so that each int32 holds
+// one dimension's four bytes, then vpdpbusd adds digit_j * v_j over the four
+// keys (digits 0..127 as unsigned bytes; exact). Int32 e of product m holds
+// dimension 16 (e / 4) + 4 m + e % 4. Missing keys of the last four take
+// digit 0. Adds into sh, sm, sl [64].
+ORC_VNNI static void pv_sums_vnni(const KVView& kv, const int64_t* slots, int len, int kvh, const int8_t* hi, const int8_t* mid,
+                                  const int8_t* lo, int32_t* sh, int32_t* sm, int32_t* sl) {
+    __m512i acc[3][4];
+    for (int d = 0; d < 3; d++)
+        for (int m = 0; m < 4; m++) acc[d][m] = _mm512_setzero_si512();
+    const int8_t* dg[3] = {hi, mid, lo};
+    for (int i = 0; i < len; i += 4) {
+        __m512i r[4];
+        uint32_t pat[3] = {0, 0, 0};
+        for (int j = 0; j < 4; j++) {
+            const int key = i + j < len ? i + j : i;  // a missing key reads key i, with digit 0
+            r[j] = _mm512_loadu_si512(kv.v8 + (slots[key] * kv.nkv + kvh) * 64);
+            if (i + j < len)
+                for (int d = 0; d < 3; d++) pat[d] |= (uint32_t)(uint8_t)dg[d][i + j] << (8 * j);
+        }
+        const __m512i u01l = _mm512_unpacklo_epi8(r[0], r[1]), u01h = _mm512_unpackhi_epi8(r[0], r[1]);
+        const __m512i u23l = _mm512_unpacklo_epi8(r[2], r[3]), u23h = _mm512_unpackhi_epi8(r[2], r[3]);
+        const __m512i w[4] = {_mm512_unpacklo_epi16(u01l, u23l), _mm512_unpackhi_epi16(u01l, u23l),
+                              _mm512_unpacklo_epi16(u01h, u23h), _mm512_unpackhi_epi16(u01h, u23h)};
+        for (int d = 0; d < 3; d++) {
+            const __m512i p = _mm512_set1_epi32((int)pat[d]);
+            for (int m = 0; m < 4; m++) acc[d][m] = _mm512_dpbusd_epi32(acc[d][m], p, w[m]);
+        }
+    }
+    int32_t* out[3] = {sh, sm, sl};
+    for (int d = 0; d < 3; d++)
+        for (int m = 0; m < 4; m++) {
+            alignas(64) int32_t v[16];
+            _mm512_store_si512(v, acc[d][m]);
+            for (int e = 0; e < 16; e++) out[d][16 * (e / 4) + 4 * m + e % 4] += v[e];
+        }
+}
+#endif
+
 // infer.rs:1871-2004 (attend_head_ref), with the merge of 2143-2166.
 void attend_head_ref(const KVView& kv, const float* qh, int kvh, const std::vector<int64_t>& slots, bool nested, float* out) {
     const int qk = kv.qk, vd = kv.vd, nkv = kv.nkv;
@@ -1721,7 +1762,18 @@ void attend_head_ref(const KVView& kv, const float* qh, int kvh, const std::vect
         p.sum = sum;
         // the three digit planes' exact integer sums, key by key
         int32_t sh[64] = {0}, sm[64] = {0}, sl2[64] = {0};
-        for (int i = 0; i < len; i++) {
+        int i_pv = 0;
+#if defined(__AVX2__) && defined(__x86_64__)
+        if (g_vnni && vd == 64) {
+            bool nonneg = true;  // every finite weight's digits are 0..127
+            for (int i = 0; i < len; i++) nonneg &= (hi[i] | mid[i] | lo[i]) >= 0;
+            if (nonneg) {
+                pv_sums_vnni(kv, sl, len, kvh, hi.data(), mid.data(), lo.data(), sh, sm, sl2);
+                i_pv = len;
+            }
+        }
+#endif
+        for (int i = i_pv; i < len; i++) {
             const int8_t* vr = kv.v8 + (sl[i] * nkv + kvh) * vd;
             int dm = 0;
 #if defined(__AVX2__)
@@ -3065,6 +3117,55 @@ int orc_team_size() { return g_team.size(); }
 
 // 1 when the 4-bit matmuls run their lane sums on AVX-512 VNNI.
 int orc_vnni() { return g_vnni ? 1 : 0; }
+
+// The attention's P·V digit-plane sums on VNNI (where the host has it)
+// against the plain key loop: n cases of 1-300 keys in shuffled slots of a
+// two-head cache, values over all of int8, digits 0..127. Returns the cases
+// whose sums differ (0 also where there is no VNNI form to check).
+int orc_pv_check(uint64_t seed, int n) {
+    int bad = 0;
+#if defined(__AVX2__) && defined(__x86_64__)
+    if (!g_vnni) return 0;
+    uint64_t st = seed * 0x9E3779B97F4A7C15ull + 1;
+    auto next = [&]() {
+        st ^= st << 13;
+        st ^= st >> 7;
+        st ^= st << 17;
+        return st;
+    };
+    for (int k = 0; k < n; k++) {
+        const int len = 1 + (int)(next() % 300), cap = len + 7, nkv = 2, kvh = (int)(next() & 1);
+        std::vector<int8_t> v8((size_t)cap * nkv * 64), hi(len), mid(len), lo(len);
+        for (auto& v : v8) v = (int8_t)(next() & 0xFF);
+        if (k == 0) std::fill(v8.begin(), v8.end(), (int8_t)-128);
+        std::vector<int64_t> slots(cap);
+        for (int i = 0; i < cap; i++) slots[i] = i;
+        for (int i = cap - 1; i > 0; i--) std::swap(slots[i], slots[next() % (i + 1)]);
+        slots.resize(len);
+        for (int i = 0; i < len; i++) {
+            hi[i] = (int8_t)(k == 0 ? 127 : next() % 128);
+            mid[i] = (int8_t)(next() % 128);
+            lo[i] = (int8_t)(next() % 128);
+        }
+        KVView kv{nullptr, nullptr, v8.data(), nullptr, nkv, 48, 64};
+        int32_t a[3][64] = {{0}}, b[3][64] = {{0}};
+        pv_sums_vnni(kv, slots.data(), len, kvh, hi.data(), mid.data(), lo.data(), a[0], a[1], a[2]);
+        for (int i = 0; i < len; i++) {
+            const int8_t* vr = v8.data() + (slots[i] * nkv + kvh) * 64;
+            for (int dm = 0; dm < 64; dm++) {
+                b[0][dm] += hi[i] * vr[dm];
+                b[1][dm] += mid[i] * vr[dm];
+                b[2][dm] += lo[i] * vr[dm];
+            }
+        }
+        bad += std::memcmp(a, b, sizeof a) != 0;
+    }
+#else
+    (void)seed;
+    (void)n;
+#endif
+    return bad;
+}
 
 // QMat::row of a raw CQ matrix of record bits `bits` (qlinear.rs:309-323).
 int orc_cq_row(const uint8_t* codes, const uint16_t* norms, int rows, int in_dim, int bits, int r, float* out) {

@@ -356,6 +356,12 @@ def test_team_does_not_change_a_result(small_archive):
         assert all(np.array_equal(a, b) for a, b in zip(runs[0], other))
 
 
+def test_vector_attention_value_sums_equal_the_key_loop():
+    # attention's P·V digit-plane sums (infer.rs:1871-2004) on VNNI hosts
+    # against the plain key loop, values over all of int8
+    assert orc.lib().orc_pv_check(9, 2000) == 0
+
+
 @pytest.mark.timeout(300)
 def test_avx2_and_vnni_lane_sums_give_the_same_streams(small_archive, tmp_path):
     """The 4-bit matmuls run their lane sums on AVX-512 VNNI where the host
