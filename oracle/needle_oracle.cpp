@@ -17,12 +17,13 @@
 // result: the int8 lane sums and dots (4-bit codes looked up from their
 // packed bytes; byte pair products into int16 only when no operand is -128,
 // else int16 pair products into int32, or AVX-512 VNNI byte products into
-// int32 where the host has it: nothing saturates), the
-// decode combine eight rows side by side, the Kronecker passes eight
-// outputs side by side, the inline exp and the int8 quantizer eight values
-// at a time (each row's, output's or value's float ops the same single
-// roundings in the same order). orc_lane_sums_check, orc_nexp_check and
-// orc_quant_check compare the vector forms with the plain loops.
+// int32 where the host has it: nothing saturates; attention's P·V sums
+// likewise on VNNI), the decode combine eight rows side by side, the
+// Kronecker passes eight outputs side by side, the inline exp and the int8
+// quantizer eight values at a time (each row's, output's or value's float
+// ops the same single roundings in the same order). orc_lane_sums_check,
+// orc_nexp_check, orc_quant_check and orc_pv_check compare the vector forms
+// with the plain loops.
 // libm stand-ins follow the reference's non-Apple `sys` module
 // (crates/needle-engine/src/infer.rs:83-102): f32 exp/pow/sincos are f64 libm
 // rounded once; this file uses glibc's f64 functions where the reference links
