@@ -166,6 +166,19 @@ private:
 
 static Team g_team;
 
+// AVX-512 VNNI on this host (the 4-bit lane sums and attention's P·V sums
+// use it where present; ORC_NO_VNNI in the environment turns it off).
+static bool vnni_host() {
+#if defined(__AVX2__) && defined(__x86_64__)
+    static const bool v = __builtin_cpu_supports("avx512f") && __builtin_cpu_supports("avx512bw") &&
+                          __builtin_cpu_supports("avx512vl") && __builtin_cpu_supports("avx512vnni") &&
+                          !std::getenv("ORC_NO_VNNI");
+    return v;
+#else
+    return false;
+#endif
+}
+
 // ---------------------------------------------------------------- numerics
 
 static inline uint32_t fbits(float f) { uint32_t u; std::memcpy(&u, &f, 4); return u; }
@@ -423,8 +436,44 @@ std::vector<float> codebook(int bits, int group) {
 // quant.rs:71-73
 static inline float hadamard_scale(int n) { return (float)(1.0 / std::sqrt((double)n)); }
 
-// quant.rs:91-105
+void fwht_scalar(float* x, int n);
+
+// quant.rs:91-105: as fwht_scalar; a 128-point transform eight values at a
+// time where the build has AVX2 (a stage's butterflies are independent, and
+// each output is the same single add or subtract of the same two values).
 void fwht(float* x, int n) {
+#if defined(__AVX2__)
+    if (n == 128) {
+        __m256 v[16];
+        for (int k = 0; k < 16; k++) v[k] = _mm256_loadu_ps(x + 8 * k);
+        // h = 1, 2, 4 inside a vector: s holds each element's partner; the
+        // lower element takes x + s (= a + b), the upper s - x (= a - b)
+        const __m256 up1 = _mm256_castsi256_ps(_mm256_setr_epi32(0, -1, 0, -1, 0, -1, 0, -1));
+        const __m256 up2 = _mm256_castsi256_ps(_mm256_setr_epi32(0, 0, -1, -1, 0, 0, -1, -1));
+        const __m256 up4 = _mm256_castsi256_ps(_mm256_setr_epi32(0, 0, 0, 0, -1, -1, -1, -1));
+        for (int k = 0; k < 16; k++) {
+            __m256 t = v[k], sw = _mm256_permute_ps(t, 0xB1);
+            t = _mm256_blendv_ps(_mm256_add_ps(t, sw), _mm256_sub_ps(sw, t), up1);
+            sw = _mm256_permute_ps(t, 0x4E);
+            t = _mm256_blendv_ps(_mm256_add_ps(t, sw), _mm256_sub_ps(sw, t), up2);
+            sw = _mm256_permute2f128_ps(t, t, 1);
+            v[k] = _mm256_blendv_ps(_mm256_add_ps(t, sw), _mm256_sub_ps(sw, t), up4);
+        }
+        for (int hv = 1; hv < 16; hv *= 2)  // h = 8 hv: whole vectors
+            for (int i = 0; i < 16; i += 2 * hv)
+                for (int j = i; j < i + hv; j++) {
+                    const __m256 a = v[j], b = v[j + hv];
+                    v[j] = _mm256_add_ps(a, b);
+                    v[j + hv] = _mm256_sub_ps(a, b);
+                }
+        for (int k = 0; k < 16; k++) _mm256_storeu_ps(x + 8 * k, v[k]);
+        return;
+    }
+#endif
+    fwht_scalar(x, n);
+}
+
+void fwht_scalar(float* x, int n) {
     for (int h = 1; h < n; h *= 2)
         for (int i = 0; i < n; i += 2 * h)
             for (int j = i; j < i + h; j++) {
@@ -784,6 +833,18 @@ static QAct qact_new(const float* x, int rows, int in_dim) {
         for (int g = 0; g < a.groups; g++)
             a.sx[(size_t)r * a.groups + g] =
                 prep_group(x + (size_t)r * in_dim, in_dim, g, a.xq.data() + ((size_t)r * a.groups + g) * GROUP);
+    // the layouts the host's 4-bit path reads: VNNI's, or AVX2's
+    if (vnni_host()) {
+        a.x8v.resize(a.xq.size());
+        a.sumx.assign(a.xq.size() / GROUP * 4, 0);
+        for (size_t g = 0; g < a.xq.size() / GROUP; g++)
+            for (int p = 0; p < GROUP; p++) {
+                const int8_t v = a.xq[g * GROUP + p];
+                a.x8v[g * GROUP + (p & 1) * 64 + p / 2] = v;
+                a.sumx[g * 4 + (p % 32) / 8] += v;
+            }
+        return a;
+    }
     a.xeo.resize(a.xq.size());
     for (size_t b = 0; b < a.xq.size(); b += 32)
         for (int j = 0; j < 16; j++) {
@@ -803,14 +864,6 @@ static QAct qact_new(const float* x, int rows, int in_dim) {
                     a.ax8eo[at] = (uint8_t)std::abs((int)v);
                     a.no_min &= v != -128;
                 }
-    a.x8v.resize(a.xq.size());
-    a.sumx.assign(a.xq.size() / GROUP * 4, 0);
-    for (size_t g = 0; g < a.xq.size() / GROUP; g++)
-        for (int p = 0; p < GROUP; p++) {
-            const int8_t v = a.xq[g * GROUP + p];
-            a.x8v[g * GROUP + (p & 1) * 64 + p / 2] = v;
-            a.sumx[g * 4 + (p % 32) / 8] += v;
-        }
     return a;
 }
 
@@ -960,9 +1013,7 @@ static inline __m128i lane_sums_codes4_ub(const uint8_t* codes, __m256i tbl, con
 // AVX-512 VNNI, chosen at run time where the host has it (the rest of this
 // file needs only AVX2).
 #define ORC_VNNI __attribute__((target("avx512f,avx512bw,avx512vl,avx512vnni")))
-static const bool g_vnni = __builtin_cpu_supports("avx512f") && __builtin_cpu_supports("avx512bw") &&
-                           __builtin_cpu_supports("avx512vl") && __builtin_cpu_supports("avx512vnni") &&
-                           !std::getenv("ORC_NO_VNNI");
+static const bool g_vnni = vnni_host();
 
 // The four lane sums of a 4-bit group from its 64 code bytes: the codebook
 // looked up sixty-four codes at a time into unsigned bytes w + 128 (tblb:
@@ -3115,6 +3166,36 @@ int orc_team_stress(int rounds) {
     return bad;
 }
 int orc_team_size() { return g_team.size(); }
+
+// fwht on 128 points (vectorised where the build has AVX2) against the
+// scalar butterflies, bit for bit, on n seeded vectors (raw bits without
+// signalling NaNs, and ordinary values). Returns the vectors that differ.
+int orc_fwht_check(uint64_t seed, int n) {
+    uint64_t st = seed * 0x9E3779B97F4A7C15ull + 1;
+    auto next = [&]() {
+        st ^= st << 13;
+        st ^= st >> 7;
+        st ^= st << 17;
+        return st;
+    };
+    int bad = 0;
+    for (int k = 0; k < n; k++) {
+        float a[128], b[128];
+        for (int i = 0; i < 128; i++) {
+            uint32_t u = (uint32_t)next();
+            if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x007fffffu)) u |= 0x00400000u;
+            a[i] = b[i] = (k % 2) ? bitsf(u) : ((float)(int)(u % 20001) - 10000.f) * 1e-3f;
+        }
+        fwht(a, 128);
+        fwht_scalar(b, 128);
+        for (int i = 0; i < 128; i++)
+            if (fbits(a[i]) != fbits(b[i]) && !(a[i] != a[i] && b[i] != b[i])) {
+                bad++;
+                break;
+            }
+    }
+    return bad;
+}
 
 // 1 when the 4-bit matmuls run their lane sums on AVX-512 VNNI.
 int orc_vnni() { return g_vnni ? 1 : 0; }

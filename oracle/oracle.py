@@ -47,6 +47,7 @@ def lib():
             "orc_team_stress": (I, [I]),
             "orc_vnni": (I, []),
             "orc_pv_check": (I, [C.c_uint64, I]),
+            "orc_fwht_check": (I, [C.c_uint64, I]),
             "orc_attend_head": (None, [P, P, P, P, I, I, I, P, I, P, I, I, P]),
             "orc_model_load": (P, [P, C.c_uint64]),
             "orc_model_free": (None, [P]),

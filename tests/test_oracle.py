@@ -356,6 +356,11 @@ def test_team_does_not_change_a_result(small_archive):
         assert all(np.array_equal(a, b) for a, b in zip(runs[0], other))
 
 
+def test_vector_fwht_equals_the_scalar_butterflies():
+    # quant.rs:91-105 on 128 points eight values at a time, bit for bit
+    assert orc.lib().orc_fwht_check(13, 5000) == 0
+
+
 def test_vector_attention_value_sums_equal_the_key_loop():
     # attention's P·V digit-plane sums (infer.rs:1871-2004) on VNNI hosts
     # against the plain key loop, values over all of int8
