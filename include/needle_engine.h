@@ -204,7 +204,12 @@ long long nd_launch_count(void);
  * stream (no counterpart in the reference): nd_batch_time_site(b, site)
  * starts recording every launch of that site (clearing earlier records;
  * ND_SITE_NONE stops), nd_batch_site_time() waits for the stream and
- * returns the summed kernel time and the number of launches. */
+ * returns the summed kernel time and the number of launches. Two sites share
+ * launches in small batches: with at most one row an SM, each layer's post
+ * block launch also runs the next layer's mHC read (ND_SITE_POST covers
+ * both; ND_SITE_MHC times layer 0's alone), and one-token steps of up to
+ * four sequences run the q|k|v|gate projection with the conv (ND_SITE_QKVG
+ * covers both; ND_SITE_CONV records none). */
 enum {
     ND_SITE_NONE = 0,
     ND_SITE_QKVG = 1,      /* q|k|v|gate projection */
