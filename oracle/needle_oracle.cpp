@@ -288,15 +288,16 @@ static inline __m256 nexp8(__m256 x) {
 // x[i] / (nexp(-x[i]) + 1) over n values in place (SiLU; the attention
 // gate's divide with g = x), each value's ops as the scalar form's.
 static void silu_div(float* x, const float* g, int64_t n) {
-    int64_t i = 0;
+    int64_t head = 0;  // values done eight at a time
 #if defined(__AVX2__)
+    head = n / 8 * 8;
     const __m256 one = _mm256_set1_ps(1.0f), neg = _mm256_set1_ps(-0.0f);
-    for (; i + 8 <= n; i += 8) {
+    for (int64_t i = 0; i < head; i += 8) {
         const __m256 gv = _mm256_xor_ps(_mm256_loadu_ps(g + i), neg);
         _mm256_storeu_ps(x + i, _mm256_div_ps(_mm256_loadu_ps(x + i), _mm256_add_ps(nexp8(gv), one)));
     }
 #endif
-    for (; i < n; i++) x[i] /= nexp(-g[i]) + 1.0f;
+    for (int64_t i = head; i < n; i++) x[i] /= nexp(-g[i]) + 1.0f;
 }
 
 // crates/needle-engine/src/infer.rs:372-417 (scalar arm 405-416)
