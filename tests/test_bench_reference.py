@@ -1,5 +1,6 @@
 """bench.py's reference arm (the oracle on the host's cores) prints the one
-JSON line the contract asks for, with no GPU."""
+JSON line the contract asks for, with no GPU, and never loads the product
+library."""
 
 import json
 import os
@@ -15,8 +16,14 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 def test_reference_arm_prints_its_line():
     env = dict(os.environ)
     env.setdefault("NEEDLE_BENCH_CACHE", os.environ.get("NEEDLE_TEST_CACHE", "/tmp/needle_b200_test_cache"))
-    out = subprocess.check_output([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
-                                   "--warmup", "1"], env=env, text=True, cwd=ROOT)
+    # run the arm in a process that then reports whether the product
+    # library was ever mapped into it (the arm must not load it)
+    code = ("import runpy, sys\n"
+            f"sys.argv = [{os.path.join(ROOT, 'bench.py')!r}, '--impl', 'reference', '--steps', '1', '--warmup', '1']\n"
+            "runpy.run_path(sys.argv[0], run_name='__main__')\n"
+            "print('product mapped:', 'libneedle3' in open('/proc/self/maps').read())\n")
+    out = subprocess.check_output([sys.executable, "-c", code], env=env, text=True, cwd=ROOT)
+    assert "product mapped: False" in out
     lines = [ln for ln in out.splitlines() if ln.startswith("{")]
     assert len(lines) == 1
     d = json.loads(lines[0])
