@@ -46,6 +46,11 @@ REFERENCE_KAT = {
         "out": 37, "in": 384, "tolerance": "0.02 * (1 + |want|)", "prefill_rows": [2, 3, 5, 9, 13, 17],
     },
     "kv_window_default": {"source": "crates/needle-core/src/config.rs:448-482", "expect": 3456},
+    "two_bit_kernels_match_reference": {
+        "source": "crates/needle-engine/src/qlinear.rs:1008-1033",
+        "out": 9, "in": 256, "code_byte": "(i * 37) % 251 over out * in / 4 bytes",
+        "norm": "f16(0.5 + 0.01 * i) over out * groups", "x": "cos(0.21 * i) over 5 * in", "block_rows": 4,
+    },
 }
 
 

@@ -103,6 +103,29 @@ def test_kernels_match_reference_tolerance():
                 assert pyref.prefill_row(codes[r], norms[r], xs[t], cb, t < rows // 4 * 4) == yy[t, r]
 
 
+def test_two_bit_kernels_match_reference():
+    """qlinear.rs:1008-1033 on its own inputs: a hand-built 2-bit matrix
+    (byte codes (37 i) % 251, f16 norms 0.5 + 0.01 i) and inputs cos(0.21 i);
+    the decode combine of one row and the prefill combine of five (the
+    first four block tokens, the fifth the remainder) agree bit for bit
+    with the pure-Python restatement of decode_row_ref / prefill_row_ref."""
+    kat = golden("reference_kat.json")["two_bit_kernels_match_reference"]
+    out, din = kat["out"], kat["in"]
+    groups = din // 128
+    codes = ((np.arange(out * din // 4) * 37) % 251).astype(np.uint8).reshape(out, din // 4)
+    norms = (np.float32(0.5) + np.arange(out * groups, dtype=np.float32) * np.float32(0.01)).astype(np.float16)
+    norms = norms.view(np.uint16).reshape(out, groups)
+    xs = np.cos(np.arange(5 * din, dtype=np.float32) * np.float32(0.21)).astype(np.float32).reshape(5, din)
+    cb = orc.codebook(2, 128)
+    y1 = orc.cq_matmul(codes, norms, din, xs[:1], bits=2)[0]
+    for o in range(out):
+        assert pyref.decode_row(codes[o], norms[o], xs[0], cb, bits=2) == y1[o]
+    y5 = orc.cq_matmul(codes, norms, din, xs, bits=2)
+    for t in range(5):
+        for o in range(out):
+            assert pyref.prefill_row(codes[o], norms[o], xs[t], cb, t < kat["block_rows"], bits=2) == y5[t, o]
+
+
 def test_row_matches_unpack():
     rng = np.random.default_rng(1)
     w = (rng.standard_normal((4, 384)) * 0.02).astype(np.float32)
