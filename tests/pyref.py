@@ -393,3 +393,72 @@ def probe_pool(cells, probes, gain, query, row_bias):
                 dst[c] = f32(dst[c] + f32(u[j] * r[j][c]))
         out += dst
     return np.array(out, np.float32)
+
+
+INV_SQRT_QK = bits(0x3E13CD3A)
+Q21 = bits(0x49FFFFF8)
+C21 = bits(0x35000004)
+
+
+def round_away(v):
+    """Rust's f32::round on a finite value: half away from zero."""
+    t = float(v)
+    return int(np.floor(abs(t) + 0.5) * np.sign(t))
+
+
+def attend_head(k8, ks, v8, vs, q, kvh, slots, nested):
+    """infer.rs:1871-2004 (attend_head_ref): the int8 query, the key chunks,
+    per chunk the scores ((ks * dot) * qs for the block keys, (ks * qs) * dot
+    for the last len % 4), chunk_exp, the value-scaled weights, the 21-bit
+    digits (2208-2214), the digit planes' integer P.V sums and their fma
+    combine, then the merge of the chunks. Caches k8 [slot][nkv][qk], v8
+    [slot][nkv][vd], ks / vs [slot][nkv] (the reference keeps V transposed;
+    the integer sums are the same)."""
+    nkv = k8.shape[1]
+    vd = v8.shape[2]
+    q8, s = quant_i8(q)
+    qs = f32(s * INV_SQRT_QK)
+    n = len(slots)
+    _, chunk = key_chunks(n, nested, nkv)
+    parts = []
+    for c0 in range(0, n, chunk):
+        sl = list(slots[c0:c0 + chunk])
+        ln = len(sl)
+        blocked = ln // 4 * 4
+        dots = [int(np.dot(q8.astype(np.int64), k8[p, kvh].astype(np.int64))) for p in sl]
+        sc = [f32(ks[p, kvh]) for p in sl]
+        sv = [f32(f32(sc[i] * f32(dots[i])) * qs) if i < blocked else f32(f32(sc[i] * qs) * f32(dots[i]))
+              for i in range(ln)]
+        m = f32(-np.inf)
+        for v in sv:
+            m = max(m, v)
+        e, total = chunk_exp(sv, m)
+        w = [f32(e[i] * f32(vs[sl[i], kvh])) for i in range(ln)]
+        wmax = f32(0)
+        for v in w:
+            wmax = max(wmax, v)
+        qw = f32(Q21 / wmax)
+        wq = [round_away(f32(w[i] * qw)) for i in range(ln)]
+        hi = np.array([v >> 14 for v in wq], np.int64)
+        mid = np.array([(v >> 7) & 127 for v in wq], np.int64)
+        lo = np.array([v & 127 for v in wq], np.int64)
+        cw = f32(wmax * C21)
+        vals = v8[sl, kvh, :].astype(np.int64)
+        sh, sm, sl_ = hi @ vals, mid @ vals, lo @ vals
+        o = [f32(fma32(f32(16384), f32(sh[d]), fma32(f32(128), f32(sm[d]), f32(sl_[d]))) * cw) for d in range(vd)]
+        parts.append((m, total, o))
+    if len(parts) == 1:
+        _, total, o = parts[0]
+        inv = f32(f32(1) / total)
+        return np.array([f32(v * inv) for v in o], np.float32)
+    big = f32(-1e30)
+    for m, _, _ in parts:
+        big = max(big, m)
+    acc = [f32(0)] * vd
+    total = f32(0)
+    for m, sm_, o in parts:
+        wgt = lexpf(f32(m - big))
+        acc = [fma32(o[d], wgt, acc[d]) for d in range(vd)]
+        total = fma32(wgt, sm_, total)
+    inv = f32(f32(1) / total)
+    return np.array([f32(a * inv) for a in acc], np.float32)

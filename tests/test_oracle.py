@@ -126,6 +126,51 @@ def test_two_bit_kernels_match_reference():
             assert pyref.prefill_row(codes[o], norms[o], xs[t], cb, t < kat["block_rows"], bits=2) == y5[t, o]
 
 
+def _reference_attention_caches():
+    """The caches infer.rs:3035-3051 fills (LayerState::reserve(800, 2, 48,
+    64): keys [slot][kvh][48], values transposed [kvh * 64 + d][1600]), as
+    [slot][kvh][...] arrays."""
+    nkv, qk, vd, slots, cap = 2, 48, 64, 800, 1600
+    i = np.arange(slots * nkv * qk)
+    k8 = (((i * 37) % 251) - 125).astype(np.int8).reshape(slots, nkv, qk)
+    i = np.arange(nkv * vd * cap + 16)
+    v8t = (((i * 53) % 249) - 124).astype(np.int8)
+    v8 = v8t[: nkv * vd * cap].reshape(nkv, vd, cap)[:, :, :slots].transpose(2, 0, 1).copy()
+    i = np.arange(slots * nkv)
+    ks = (np.float32(0.01) + (i % 7).astype(np.float32) * np.float32(0.003)).astype(np.float32).reshape(slots, nkv)
+    vs = (np.float32(0.02) + (i % 5).astype(np.float32) * np.float32(0.002)).astype(np.float32).reshape(slots, nkv)
+    q = (np.sin(np.arange(qk, dtype=np.float32) * np.float32(0.3)) * np.float32(3.0)).astype(np.float32)
+    return k8, ks, v8, vs, q
+
+
+def _slot_of(p, attend):
+    """infer.rs:1748-1753."""
+    if attend is not None and p >= attend[0]:
+        return (p - attend[0]) % attend[1] + attend[0]
+    return p
+
+
+@pytest.mark.timeout(600)
+def test_attention_matches_reference_cases():
+    """infer.rs:3035-3075's seven key sets and spans (one key; 37 and 300
+    keys; 416 + 44 keys under a (416, 256) span; two runs under a (41, 256)
+    span, one of them wrapping the ring; a run with an empty second one),
+    nested and not, both kv heads, on the caches that test builds: the
+    oracle's attend_head_ref agrees bit for bit with the pure-Python
+    restatement of infer.rs:1871-2004."""
+    k8, ks, v8, vs, q = _reference_attention_caches()
+    cases = [((0, 1), (0, 0), None), ((0, 37), (0, 0), None), ((0, 300), (0, 0), None),
+             ((0, 416), (416, 460), (416, 256)), ((0, 41), (250, 297), (41, 256)),
+             ((0, 41), (290, 560), (41, 256)), ((0, 20), (20, 20), (41, 256))]
+    for a, b, attend in cases:
+        slots = np.array([_slot_of(p, attend) for p in list(range(*a)) + list(range(*b))], np.int64)
+        for nested in (False, True):
+            for kvh in (0, 1):
+                got = orc.attend_head(k8, ks, v8, vs, q, kvh, slots, nested)
+                want = pyref.attend_head(k8, ks, v8, vs, q, kvh, slots, nested)
+                assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), (a, b, attend, nested, kvh)
+
+
 def test_row_matches_unpack():
     rng = np.random.default_rng(1)
     w = (rng.standard_normal((4, 384)) * 0.02).astype(np.float32)
