@@ -3198,6 +3198,33 @@ int orc_fwht_check(uint64_t seed, int n) {
     return bad;
 }
 
+// infer.rs:1610-1634 (mlp_native) on one pre-MLP row h2 [d] with the
+// layer's MLP weights given directly (values of f16 weights as floats):
+// d1, d4 [d]; d2, b2, d3 [1024]; kron [6][1024]; cond_v [d][8];
+// cond_u [8][1024]; perm1, perm2 [1024]. out [d].
+int orc_mlp(const float* h2, int d, const float* d1, const float* d2, const float* b2, const float* d3, const float* d4,
+            const float* kron, const float* cond_v, const float* cond_u, const int64_t* perm1, const int64_t* perm2,
+            float* out) {
+    if (d < 1 || d > 1024) return -1;
+    Model m;
+    m.c.d = d;
+    m.perm1.assign(perm1, perm1 + 1024);
+    m.perm2.assign(perm2, perm2 + 1024);
+    for (int j = 0; j < 1024; j++)
+        if (m.perm1[j] < 0 || m.perm1[j] >= 1024 || m.perm2[j] < 0 || m.perm2[j] >= 1024) return -1;
+    Layer L;
+    L.d1.assign(d1, d1 + d);
+    L.d4.assign(d4, d4 + d);
+    L.d2.assign(d2, d2 + 1024);
+    L.b2.assign(b2, b2 + 1024);
+    L.d3.assign(d3, d3 + 1024);
+    for (int k = 0; k < 6; k++) L.kron[k].assign(kron + k * 1024, kron + (k + 1) * 1024);
+    L.cond_v.assign(cond_v, cond_v + (size_t)d * 8);
+    L.cond_u.assign(cond_u, cond_u + 8 * 1024);
+    mlp_native(m, L, h2, out);
+    return 0;
+}
+
 // 1 when the 4-bit matmuls run their lane sums on AVX-512 VNNI.
 int orc_vnni() { return g_vnni ? 1 : 0; }
 

@@ -48,6 +48,7 @@ def lib():
             "orc_vnni": (I, []),
             "orc_pv_check": (I, [C.c_uint64, I]),
             "orc_fwht_check": (I, [C.c_uint64, I]),
+            "orc_mlp": (I, [P, I, P, P, P, P, P, P, P, P, P, P, P]),
             "orc_attend_head": (None, [P, P, P, P, I, I, I, P, I, P, I, I, P]),
             "orc_model_load": (P, [P, C.c_uint64]),
             "orc_model_free": (None, [P]),
@@ -143,6 +144,19 @@ def synth_cact(seed=0, std=0.02, bits=None, heads=(), **shape) -> bytes:
     if lib().orc_synth_cact(*args, _p(buf), n.value, C.byref(n)) != 0:
         raise RuntimeError(lib().orc_last_error().decode())
     return buf.tobytes()
+
+
+def mlp(h2, d1, d2, b2, d3, d4, kron, cond_v, cond_u, perm1, perm2):
+    """mlp_native (infer.rs:1610-1634) on one row with the given weights."""
+    h2 = np.ascontiguousarray(h2, np.float32)
+    d = len(h2)
+    f = lambda a: np.ascontiguousarray(a, np.float32)
+    i64 = lambda a: np.ascontiguousarray(a, np.int64)
+    out = np.zeros(d, np.float32)
+    args = [f(d1), f(d2), f(b2), f(d3), f(d4), f(kron), f(cond_v), f(cond_u), i64(perm1), i64(perm2)]
+    if lib().orc_mlp(_p(h2), d, *[_p(a) for a in args], _p(out)) != 0:
+        raise ValueError("bad MLP arguments")
+    return out
 
 
 def set_team(threads: int) -> None:

@@ -462,3 +462,62 @@ def attend_head(k8, ks, v8, vs, q, kvh, slots, nested):
         total = fma32(wgt, sm_, total)
     inv = f32(f32(1) / total)
     return np.array([f32(a * inv) for a in acc], np.float32)
+
+
+def cond_weights(h2, cond_v):
+    """infer.rs:1640-1694 (scalar arm): logits in four accumulator sets by
+    j % 4 (fma chains over j), ((C + D) + B) + A, then the softmax with the
+    engine's sum tree."""
+    acc = [[f32(0)] * 8 for _ in range(4)]
+    for j, hv in enumerate(h2):
+        for k in range(8):
+            acc[j % 4][k] = fma32(hv, cond_v[j * 8 + k], acc[j % 4][k])
+    lg = [((acc[2][k] + acc[3][k]) + acc[1][k]) + acc[0][k] for k in range(8)]
+    m = f32(-np.inf)
+    for v in lg:
+        m = max(m, v)
+    e = [lexpf(f32(v - m)) for v in lg]
+    total = e[7] + ((e[6] + (e[5] + e[4])) + ((e[3] + e[2]) + (e[1] + e[0])))
+    inv = f32(f32(1) / total)
+    return [f32(v * inv) for v in e]
+
+
+def mix8(ct, rows, transpose):
+    """infer.rs:2343-2460 (scalar arm 2442-2459): out[r][c] = sum over j of
+    ct[j][r] * rows[j][c], an fma chain over j from 0; with transpose the
+    value lands at out[c][r]."""
+    out = [f32(0)] * 1024
+    for r in range(32):
+        for c in range(32):
+            o = f32(0)
+            for j in range(32):
+                o = fma32(ct[j * 32 + r], rows[j * 32 + c], o)
+            out[c * 32 + r if transpose else r * 32 + c] = o
+    return out
+
+
+def kron_native(z, a, b):
+    """infer.rs:2322-2330."""
+    return mix8(mix8(a, z, True), b, False)
+
+
+def mlp_native(h2, d1, d2, b2, d3, d4, kron, cond_v, cond_u, perm1, perm2):
+    """infer.rs:1610-1634, with axpy16 (494-528), perm_fma (689-713) and
+    silu_native (2463-2496) in their scalar forms."""
+    h2 = [f32(v) for v in h2]
+    d = len(h2)
+    w = cond_weights(h2, cond_v)
+    z = [f32(0)] * 1024
+    for j in range(d):
+        z[j] = f32(h2[j] * f32(d1[j]))
+    t = kron_native(z, kron[0], kron[1])
+    cond = [f32(1)] * 1024
+    for k in range(8):
+        for i in range(1024):
+            cond[i] = fma32(f32(cond_u[k * 1024 + i]), w[k], cond[i])
+    z = [fma32(t[perm1[j]], f32(cond[j] * f32(d2[j])), f32(b2[j])) for j in range(1024)]
+    z = [f32(v / f32(nexp(f32(-v)) + f32(1))) for v in z]
+    t = kron_native(z, kron[2], kron[3])
+    z = [f32(t[perm2[j]] * f32(d3[j])) for j in range(1024)]
+    t = kron_native(z, kron[4], kron[5])
+    return np.array([f32(t[j] * f32(d4[j])) for j in range(d)], np.float32)

@@ -171,6 +171,29 @@ def test_attention_matches_reference_cases():
                 assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), (a, b, attend, nested, kvh)
 
 
+@pytest.mark.timeout(600)
+@pytest.mark.parametrize("scale", [1.0, 12.0])
+def test_mlp_matches_python(scale):
+    """The post block's Hadamard MLP (infer.rs:1610-1634: conditioning
+    softmax, three Kronecker stages of two 32 x 32 x 32 passes, perm_fma,
+    SiLU) on one 768-wide row with seeded weights held as f16 values: the
+    oracle against the pure-Python restatement, bit for bit. scale 12 drives
+    the SiLU and the softmax into their saturated ranges."""
+    rng = np.random.default_rng(int(scale * 10))
+    h16 = lambda a: np.asarray(a, np.float32).astype(np.float16).astype(np.float32)
+    d = 768
+    h2 = (rng.standard_normal(d) * scale).astype(np.float32)
+    w = dict(d1=h16(1 + 0.1 * rng.standard_normal(d)), d2=h16(1 + 0.1 * rng.standard_normal(1024)),
+             b2=h16(0.1 * rng.standard_normal(1024)), d3=h16(1 + 0.1 * rng.standard_normal(1024)),
+             d4=h16(1 + 0.1 * rng.standard_normal(d)), kron=h16(0.2 * rng.standard_normal((6, 1024))),
+             cond_v=h16(0.05 * rng.standard_normal(d * 8)), cond_u=h16(0.1 * rng.standard_normal(8 * 1024)),
+             perm1=rng.permutation(1024), perm2=rng.permutation(1024))
+    got = orc.mlp(h2, **w)
+    want = pyref.mlp_native(h2, w["d1"], w["d2"], w["b2"], w["d3"], w["d4"], w["kron"], w["cond_v"], w["cond_u"],
+                            w["perm1"], w["perm2"])
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
 def test_row_matches_unpack():
     rng = np.random.default_rng(1)
     w = (rng.standard_normal((4, 384)) * 0.02).astype(np.float32)
