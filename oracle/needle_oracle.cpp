@@ -2080,6 +2080,45 @@ static void engram_native(const Model& m, Session& st, int64_t p0, int t, std::v
 }
 
 // infer.rs:1331-1606
+// infer.rs:1359-1393 for one row: the lanes x [4 d] normalised by one rms,
+// int8 (no rotation), the gate projections p [phi_rows] (int8 dots), the
+// pre gates (own lane `lane`) and the block input u [d].
+static void mhc_read_row(const Layer& L, int lane, const float* x, int d, float* pr, float* ur) {
+    const int nc = 4 * d, ncols = L.phi_rows;
+    std::vector<float> nx(nc);
+    std::vector<int8_t> q8(nc);
+    float r = rinv(dot16(x, x, nc), nc);
+    for (int k = 0; k < nc; k++) nx[k] = x[k] * r;
+    float sx = quant_i8(nx.data(), nc, q8.data());
+    for (int k = 0; k < ncols; k++) {
+        const int32_t acc = dot_i8(L.phi_q.data() + (size_t)k * nc, q8.data(), nc);
+        pr[k] = (sx * L.phi_s[k]) * (float)acc;
+    }
+    float hp[4];
+    for (int j = 0; j < 4; j++) {
+        float off = j == lane ? 4.0f : -4.0f;
+        float z = ((pr[j] * L.a_pre) + off) + L.b_pre[j];
+        hp[j] = 1.0f / (lexpf(-z) + 1.0f);
+    }
+    for (int k = 0; k < d; k++) ur[k] = x[k] * hp[0];
+    for (int b = 1; b < 4; b++)
+        for (int k = 0; k < d; k++) ur[k] = std::fmaf(x[b * d + k], hp[b], ur[k]);
+}
+
+// infer.rs:1397-1418 for one row: the engram gate (when kr / vr, the site's
+// key and value rows, are given) on xr in place, then the input ZC-RMSNorm
+// into hr.
+static void gate_norm_row(const Layer& L, float* xr, const float* kr, const float* vr, int d, float* hr) {
+    if (kr) {
+        float rx = rinv(dot16(xr, xr, d), d), rk = rinv(dot16(kr, kr, d), d);
+        std::vector<float> a(d), b(d);
+        for (int k = 0; k < d; k++) { a[k] = xr[k] * rx; b[k] = kr[k] * rk; }
+        float alpha = 1.0f / (lexpf((-dot16(a.data(), b.data(), d)) / std::sqrt((float)d)) + 1.0f);
+        for (int k = 0; k < d; k++) xr[k] = std::fmaf(vr[k], alpha, xr[k]);
+    }
+    zcn(xr, L.norm_in.data(), hr, d);
+}
+
 static void layer_native(const Model& m, int l, Session& st, int64_t p0, std::vector<float>& xs, int t,
                          const std::vector<float>& cos, const std::vector<float>& sin,
                          const std::vector<std::vector<float>>& ekeys, const std::vector<std::vector<float>>& evals) {
@@ -2094,50 +2133,17 @@ static void layer_native(const Model& m, int l, Session& st, int64_t p0, std::ve
 
     // (a) mHC read
     std::vector<float> u((size_t)t * d), p((size_t)t * ncols);
-    {
-        std::vector<float> nx(nc);
-        std::vector<int8_t> q8(nc);
-        for (int i = 0; i < t; i++) {
-            const float* x = xs.data() + (size_t)i * nc;
-            float r = rinv(dot16(x, x, nc), nc);
-            for (int k = 0; k < nc; k++) nx[k] = x[k] * r;
-            float sx = quant_i8(nx.data(), nc, q8.data());
-            float* pr = p.data() + (size_t)i * ncols;
-            for (int k = 0; k < ncols; k++) {
-                const int32_t acc = dot_i8(L.phi_q.data() + (size_t)k * nc, q8.data(), nc);
-                pr[k] = (sx * L.phi_s[k]) * (float)acc;
-            }
-            float hp[4];
-            for (int j = 0; j < 4; j++) {
-                float off = j == lane ? 4.0f : -4.0f;
-                float z = ((pr[j] * L.a_pre) + off) + L.b_pre[j];
-                hp[j] = 1.0f / (lexpf(-z) + 1.0f);
-            }
-            float* ur = u.data() + (size_t)i * d;
-            for (int k = 0; k < d; k++) ur[k] = x[k] * hp[0];
-            for (int b = 1; b < 4; b++)
-                for (int k = 0; k < d; k++) ur[k] = std::fmaf(x[b * d + k], hp[b], ur[k]);
-        }
-    }
+    for (int i = 0; i < t; i++)
+        mhc_read_row(L, lane, xs.data() + (size_t)i * nc, d, p.data() + (size_t)i * ncols, u.data() + (size_t)i * d);
     g_trace.put(tag + "u", u.data(), u.size());
     g_trace.put(tag + "p", p.data(), p.size());
 
     // (b) engram gate, (c) input norm, (d) A8 + qkvg
     std::vector<float> x1 = u, h((size_t)t * d);
     int site = m.site_of_layer[l];
-    for (int i = 0; i < t; i++) {
-        float* xr = x1.data() + (size_t)i * d;
-        if (site >= 0) {
-            const float* kr = ekeys[site].data() + (size_t)i * d;
-            float rx = rinv(dot16(xr, xr, d), d), rk = rinv(dot16(kr, kr, d), d);
-            std::vector<float> a(d), b(d);
-            for (int k = 0; k < d; k++) { a[k] = xr[k] * rx; b[k] = kr[k] * rk; }
-            float alpha = 1.0f / (lexpf((-dot16(a.data(), b.data(), d)) / std::sqrt((float)d)) + 1.0f);
-            const float* vr = evals[site].data() + (size_t)i * d;
-            for (int k = 0; k < d; k++) xr[k] = std::fmaf(vr[k], alpha, xr[k]);
-        }
-        zcn(xr, L.norm_in.data(), h.data() + (size_t)i * d, d);
-    }
+    for (int i = 0; i < t; i++)
+        gate_norm_row(L, x1.data() + (size_t)i * d, site >= 0 ? ekeys[site].data() + (size_t)i * d : nullptr,
+                      site >= 0 ? evals[site].data() + (size_t)i * d : nullptr, d, h.data() + (size_t)i * d);
     g_trace.put(tag + "x1", x1.data(), x1.size());
     g_trace.put(tag + "h", h.data(), h.size());
     std::vector<float> proj((size_t)t * pout);
@@ -3222,6 +3228,28 @@ int orc_mlp(const float* h2, int d, const float* d1, const float* d2, const floa
     L.cond_v.assign(cond_v, cond_v + (size_t)d * 8);
     L.cond_u.assign(cond_u, cond_u + 8 * 1024);
     mlp_native(m, L, h2, out);
+    return 0;
+}
+
+// infer.rs:1359-1418 on one row with given weights: the mHC read of the
+// lanes x [4 d] (gate rows phi_q [24][4 d] int8 with scales phi_s [24],
+// a_pre, b_pre [4], own lane `lane`) into p [24] and u [d]; then the engram
+// gate with the site's key / value rows kr, vr [d] (both NULL: no site) and
+// the input norm (norm_in [d]) into x1 [d] and h [d].
+int orc_mhc_read(const float* x, int d, const int8_t* phi_q, const float* phi_s, float a_pre, const float* b_pre, int lane,
+                 const float* kr, const float* vr, const float* norm_in, float* p, float* u, float* x1, float* h) {
+    if (d < 16 || d % 16 || lane < 0 || lane > 3 || (!kr) != (!vr)) return -1;
+    Layer L;
+    L.phi_rows = 24;
+    L.phi_width = 4 * d;
+    L.phi_q.assign(phi_q, phi_q + (size_t)24 * 4 * d);
+    L.phi_s.assign(phi_s, phi_s + 24);
+    L.a_pre = a_pre;
+    L.b_pre.assign(b_pre, b_pre + 4);
+    L.norm_in.assign(norm_in, norm_in + d);
+    mhc_read_row(L, lane, x, d, p, u);
+    std::memcpy(x1, u, sizeof(float) * d);
+    gate_norm_row(L, x1, kr, vr, d, h);
     return 0;
 }
 

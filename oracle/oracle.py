@@ -49,6 +49,7 @@ def lib():
             "orc_pv_check": (I, [C.c_uint64, I]),
             "orc_fwht_check": (I, [C.c_uint64, I]),
             "orc_mlp": (I, [P, I, P, P, P, P, P, P, P, P, P, P, P]),
+            "orc_mhc_read": (I, [P, I, P, P, F, P, I, P, P, P, P, P, P, P]),
             "orc_attend_head": (None, [P, P, P, P, I, I, I, P, I, P, I, I, P]),
             "orc_model_load": (P, [P, C.c_uint64]),
             "orc_model_free": (None, [P]),
@@ -157,6 +158,21 @@ def mlp(h2, d1, d2, b2, d3, d4, kron, cond_v, cond_u, perm1, perm2):
     if lib().orc_mlp(_p(h2), d, *[_p(a) for a in args], _p(out)) != 0:
         raise ValueError("bad MLP arguments")
     return out
+
+
+def mhc_read(x, phi_q, phi_s, a_pre, b_pre, lane, norm_in, kr=None, vr=None):
+    """The mHC read, engram gate and input norm of one row (infer.rs:
+    1359-1418): (p [24], u, x1, h)."""
+    x = np.ascontiguousarray(x, np.float32)
+    d = len(x) // 4
+    f = lambda a: np.ascontiguousarray(a, np.float32)
+    p, u, x1, h = np.zeros(24, np.float32), np.zeros(d, np.float32), np.zeros(d, np.float32), np.zeros(d, np.float32)
+    rc = lib().orc_mhc_read(_p(x), d, _p(np.ascontiguousarray(phi_q, np.int8)), _p(f(phi_s)), float(a_pre), _p(f(b_pre)),
+                            int(lane), _p(f(kr)) if kr is not None else None, _p(f(vr)) if vr is not None else None,
+                            _p(f(norm_in)), _p(p), _p(u), _p(x1), _p(h))
+    if rc != 0:
+        raise ValueError("bad mHC read arguments")
+    return p, u, x1, h
 
 
 def set_team(threads: int) -> None:

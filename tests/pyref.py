@@ -521,3 +521,55 @@ def mlp_native(h2, d1, d2, b2, d3, d4, kron, cond_v, cond_u, perm1, perm2):
     z = [f32(t[perm2[j]] * f32(d3[j])) for j in range(1024)]
     t = kron_native(z, kron[4], kron[5])
     return np.array([f32(t[j] * f32(d4[j])) for j in range(d)], np.float32)
+
+
+def rinv(ss, n):
+    """infer.rs:420-422: 1 / sqrtf(ss / n + 1e-6)."""
+    return f32(f32(1) / np.sqrt(f32(f32(ss) / f32(n)) + f32(1e-6)))
+
+
+def zcn(x, s):
+    """infer.rs:425-443 (scalar arm): t = x * r, out = fma(t, s, t)."""
+    r = rinv(dot16(x, x), len(x))
+    out = []
+    for v, w in zip(x, s):
+        t = f32(f32(v) * r)
+        out.append(fma32(t, f32(w), t))
+    return out
+
+
+def mhc_read_row(x, phi_q, phi_s, a_pre, b_pre, lane):
+    """infer.rs:1359-1393 for one row: the lanes normalised by one rms, int8
+    without rotation, the gate projections (int8 dots), the pre gates (own
+    lane +4, the others -4), the block input u."""
+    x = [f32(v) for v in x]
+    nc = len(x)
+    d = nc // 4
+    r = rinv(dot16(x, x), nc)
+    q8, sx = quant_i8([f32(v * r) for v in x])
+    q8 = q8.astype(np.int64)
+    p = [f32(f32(sx * f32(phi_s[k])) * f32(int(np.dot(np.asarray(phi_q[k], np.int64), q8)))) for k in range(len(phi_s))]
+    hp = []
+    for j in range(4):
+        off = f32(4.0) if j == lane else f32(-4.0)
+        z = f32(f32(f32(p[j] * f32(a_pre)) + off) + f32(b_pre[j]))
+        hp.append(f32(f32(1) / f32(lexpf(f32(-z)) + f32(1))))
+    u = [f32(x[k] * hp[0]) for k in range(d)]
+    for b in range(1, 4):
+        u = [fma32(x[b * d + k], hp[b], u[k]) for k in range(d)]
+    return p, u
+
+
+def gate_norm_row(u, norm_in, kr=None, vr=None):
+    """infer.rs:1397-1418 for one row: the engram gate (the site's key and
+    value rows), then the input ZC-RMSNorm. Returns (x1, h)."""
+    xr = [f32(v) for v in u]
+    d = len(xr)
+    if kr is not None:
+        kr = [f32(v) for v in kr]
+        rx, rk = rinv(dot16(xr, xr), d), rinv(dot16(kr, kr), d)
+        a = [f32(v * rx) for v in xr]
+        b = [f32(v * rk) for v in kr]
+        alpha = f32(f32(1) / f32(lexpf(f32(f32(-dot16(a, b)) / np.sqrt(f32(d)))) + f32(1)))
+        xr = [fma32(f32(vr[k]), alpha, xr[k]) for k in range(d)]
+    return xr, zcn(xr, norm_in)

@@ -194,6 +194,32 @@ def test_mlp_matches_python(scale):
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
+@pytest.mark.timeout(600)
+@pytest.mark.parametrize("site", [False, True])
+def test_mhc_read_matches_python(site):
+    """The mHC read (infer.rs:1359-1393: rms of the four lanes, int8 without
+    rotation, the 24 int8 gate dots, the pre gates, u), the engram gate and
+    the input norm (1397-1418) on one seeded 4 x 768 row: the oracle against
+    the pure-Python restatement, bit for bit, with and without an engram
+    site."""
+    rng = np.random.default_rng(41 + int(site))
+    d = 768
+    h16 = lambda a: np.asarray(a, np.float32).astype(np.float16).astype(np.float32)
+    x = (rng.standard_normal(4 * d) * 0.7).astype(np.float32)
+    phi_q = rng.integers(-127, 128, (24, 4 * d), dtype=np.int8)
+    phi_s = (np.abs(rng.standard_normal(24)) * 1e-3 + 1e-4).astype(np.float32)
+    a_pre, b_pre = np.float32(0.8), h16(0.3 * rng.standard_normal(4))
+    norm_in = h16(0.1 * rng.standard_normal(d))
+    kr = (rng.standard_normal(d) * 0.5).astype(np.float32) if site else None
+    vr = (rng.standard_normal(d) * 0.2).astype(np.float32) if site else None
+    lane = 2
+    p, u, x1, h = orc.mhc_read(x, phi_q, phi_s, a_pre, b_pre, lane, norm_in, kr, vr)
+    pw, uw = pyref.mhc_read_row(x, phi_q, phi_s, a_pre, b_pre, lane)
+    x1w, hw = pyref.gate_norm_row(uw, norm_in, kr, vr)
+    for got, want in ((p, pw), (u, uw), (x1, x1w), (h, hw)):
+        assert np.array_equal(got.view(np.uint32), np.asarray(want, np.float32).view(np.uint32))
+
+
 def test_row_matches_unpack():
     rng = np.random.default_rng(1)
     w = (rng.standard_normal((4, 384)) * 0.02).astype(np.float32)
