@@ -2119,6 +2119,40 @@ static void gate_norm_row(const Layer& L, float* xr, const float* kr, const floa
     zcn(xr, L.norm_in.data(), hr, d);
 }
 
+// infer.rs:1564-1606 for one row: o's post norm and the gated residual
+// (ga: the attention gate) into x2, the pre-MLP norm, the Hadamard MLP
+// (into mlp_out), the post gates (own lane `lane`) and the Sinkhorn mix of
+// the gate projections pr, then the mHC write of the lanes x [4 d] in place
+// from u and the old lanes.
+static void post_row(const Model& m, const Layer& L, int lane, float ga, const float* o, const float* x1, const float* pr,
+                     const float* ur, float* x, float* mlp_out) {
+    const int d = m.c.d, n = 4, nc = n * d;
+    std::vector<float> on(d), x2(d), h2(d), mlp(d);
+    zcn(o, L.post_norm.data(), on.data(), d);
+    for (int k = 0; k < d; k++) x2[k] = std::fmaf(on[k], ga, x1[k]);
+    zcn(x2.data(), L.pre_hada.data(), h2.data(), d);
+    mlp_native(m, L, h2.data(), mlp.data());
+    std::memcpy(mlp_out, mlp.data(), sizeof(float) * d);
+    float hpost[4];
+    for (int j = 0; j < 4; j++) {
+        float off = j == lane ? 0.0f : -4.0f;
+        float z = ((pr[n + j] * L.a_post) + off) + L.b_post[j];
+        hpost[j] = 2.0f / (lexpf(-z) + 1.0f);
+    }
+    float zres[16], hres[16];
+    for (int k = 0; k < 16; k++) zres[k] = std::fmaf(pr[2 * n + k], L.a_res, L.b_res[k]);
+    sinkhorn64(zres, hres);
+    std::vector<float> old(x, x + nc);
+    for (int ch = 0; ch < d; ch++) {
+        float y = (x2[ch] + mlp[ch]) - ur[ch];
+        for (int a = 0; a < n; a++) {
+            float v = y * hpost[a];
+            for (int b = 0; b < n; b++) v = std::fmaf(old[b * d + ch], hres[a * n + b], v);
+            x[a * d + ch] = v;
+        }
+    }
+}
+
 static void layer_native(const Model& m, int l, Session& st, int64_t p0, std::vector<float>& xs, int t,
                          const std::vector<float>& cos, const std::vector<float>& sin,
                          const std::vector<std::vector<float>>& ekeys, const std::vector<std::vector<float>>& evals) {
@@ -2264,35 +2298,9 @@ static void layer_native(const Model& m, int l, Session& st, int64_t p0, std::ve
     float ga = 1.0f / (lexpf(-L.attn_gate) + 1.0f);
     std::vector<float> mlpv((size_t)t * d);
     g_team.run(t, [&](int i0, int i1) {
-    for (int i = i0; i < i1; i++) {
-        std::vector<float> on(d), x2(d), h2(d), mlp(d);
-        zcn(o.data() + (size_t)i * d, L.post_norm.data(), on.data(), d);
-        for (int k = 0; k < d; k++) x2[k] = std::fmaf(on[k], ga, x1[(size_t)i * d + k]);
-        zcn(x2.data(), L.pre_hada.data(), h2.data(), d);
-        mlp_native(m, L, h2.data(), mlp.data());
-        std::memcpy(&mlpv[(size_t)i * d], mlp.data(), sizeof(float) * d);
-        const float* pr = p.data() + (size_t)i * ncols;
-        float hpost[4];
-        for (int j = 0; j < 4; j++) {
-            float off = j == lane ? 0.0f : -4.0f;
-            float z = ((pr[n + j] * L.a_post) + off) + L.b_post[j];
-            hpost[j] = 2.0f / (lexpf(-z) + 1.0f);
-        }
-        float zres[16], hres[16];
-        for (int k = 0; k < 16; k++) zres[k] = std::fmaf(pr[2 * n + k], L.a_res, L.b_res[k]);
-        sinkhorn64(zres, hres);
-        float* x = xs.data() + (size_t)i * nc;
-        std::vector<float> old(x, x + nc);
-        const float* ur = u.data() + (size_t)i * d;
-        for (int ch = 0; ch < d; ch++) {
-            float y = (x2[ch] + mlp[ch]) - ur[ch];
-            for (int a = 0; a < n; a++) {
-                float v = y * hpost[a];
-                for (int b = 0; b < n; b++) v = std::fmaf(old[b * d + ch], hres[a * n + b], v);
-                x[a * d + ch] = v;
-            }
-        }
-    }
+        for (int i = i0; i < i1; i++)
+            post_row(m, L, lane, ga, o.data() + (size_t)i * d, x1.data() + (size_t)i * d, p.data() + (size_t)i * ncols,
+                     u.data() + (size_t)i * d, xs.data() + (size_t)i * nc, &mlpv[(size_t)i * d]);
     });
     g_trace.put(tag + "mlp", mlpv.data(), mlpv.size());
     g_trace.put(tag + "xs", xs.data(), xs.size());
@@ -3250,6 +3258,43 @@ int orc_mhc_read(const float* x, int d, const int8_t* phi_q, const float* phi_s,
     mhc_read_row(L, lane, x, d, p, u);
     std::memcpy(x1, u, sizeof(float) * d);
     gate_norm_row(L, x1, kr, vr, d, h);
+    return 0;
+}
+
+// infer.rs:1564-1606 on one row with given weights: post_norm, pre_hada
+// [d], attn_gate, a_post, b_post [4], a_res, b_res [16], the MLP weights as
+// orc_mlp takes them, own lane `lane`; o, x1, u [d] and the gate
+// projections pr [24]; the lanes x [4 d] updated in place, mlp_out [d].
+int orc_post_row(int d, const float* post_norm, const float* pre_hada, float attn_gate, float a_post, const float* b_post,
+                 float a_res, const float* b_res, const float* d1, const float* d2, const float* b2, const float* d3,
+                 const float* d4, const float* kron, const float* cond_v, const float* cond_u, const int64_t* perm1,
+                 const int64_t* perm2, int lane, const float* o, const float* x1, const float* pr, const float* u, float* x,
+                 float* mlp_out) {
+    if (d < 16 || d % 16 || d > 1024 || lane < 0 || lane > 3) return -1;
+    Model m;
+    m.c.d = d;
+    m.perm1.assign(perm1, perm1 + 1024);
+    m.perm2.assign(perm2, perm2 + 1024);
+    for (int j = 0; j < 1024; j++)
+        if (m.perm1[j] < 0 || m.perm1[j] >= 1024 || m.perm2[j] < 0 || m.perm2[j] >= 1024) return -1;
+    Layer L;
+    L.post_norm.assign(post_norm, post_norm + d);
+    L.pre_hada.assign(pre_hada, pre_hada + d);
+    L.attn_gate = attn_gate;
+    L.a_post = a_post;
+    L.b_post.assign(b_post, b_post + 4);
+    L.a_res = a_res;
+    L.b_res.assign(b_res, b_res + 16);
+    L.d1.assign(d1, d1 + d);
+    L.d4.assign(d4, d4 + d);
+    L.d2.assign(d2, d2 + 1024);
+    L.b2.assign(b2, b2 + 1024);
+    L.d3.assign(d3, d3 + 1024);
+    for (int k = 0; k < 6; k++) L.kron[k].assign(kron + k * 1024, kron + (k + 1) * 1024);
+    L.cond_v.assign(cond_v, cond_v + (size_t)d * 8);
+    L.cond_u.assign(cond_u, cond_u + 8 * 1024);
+    const float ga = 1.0f / (lexpf(-L.attn_gate) + 1.0f);
+    post_row(m, L, lane, ga, o, x1, pr, u, x, mlp_out);
     return 0;
 }
 

@@ -50,6 +50,7 @@ def lib():
             "orc_fwht_check": (I, [C.c_uint64, I]),
             "orc_mlp": (I, [P, I, P, P, P, P, P, P, P, P, P, P, P]),
             "orc_mhc_read": (I, [P, I, P, P, F, P, I, P, P, P, P, P, P, P]),
+            "orc_post_row": (I, [I, P, P, F, F, P, F, P, P, P, P, P, P, P, P, P, P, P, I, P, P, P, P, P, P]),
             "orc_attend_head": (None, [P, P, P, P, I, I, I, P, I, P, I, I, P]),
             "orc_model_load": (P, [P, C.c_uint64]),
             "orc_model_free": (None, [P]),
@@ -173,6 +174,24 @@ def mhc_read(x, phi_q, phi_s, a_pre, b_pre, lane, norm_in, kr=None, vr=None):
     if rc != 0:
         raise ValueError("bad mHC read arguments")
     return p, u, x1, h
+
+
+def post_row(x, o, x1, pr, u, lane, post_norm, pre_hada, attn_gate, a_post, b_post, a_res, b_res, d1, d2, b2, d3, d4,
+             kron, cond_v, cond_u, perm1, perm2):
+    """The post block of one row (infer.rs:1564-1606): (the new lanes
+    [4 d], the MLP output [d])."""
+    f = lambda a: np.ascontiguousarray(a, np.float32)
+    i64 = lambda a: np.ascontiguousarray(a, np.int64)
+    xs = f(x).copy()
+    d = len(xs) // 4
+    mlp_out = np.zeros(d, np.float32)
+    rc = lib().orc_post_row(d, _p(f(post_norm)), _p(f(pre_hada)), float(attn_gate), float(a_post), _p(f(b_post)),
+                            float(a_res), _p(f(b_res)), _p(f(d1)), _p(f(d2)), _p(f(b2)), _p(f(d3)), _p(f(d4)), _p(f(kron)),
+                            _p(f(cond_v)), _p(f(cond_u)), _p(i64(perm1)), _p(i64(perm2)), int(lane), _p(f(o)), _p(f(x1)),
+                            _p(f(pr)), _p(f(u)), _p(xs), _p(mlp_out))
+    if rc != 0:
+        raise ValueError("bad post block arguments")
+    return xs, mlp_out
 
 
 def set_team(threads: int) -> None:

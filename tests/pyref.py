@@ -573,3 +573,33 @@ def gate_norm_row(u, norm_in, kr=None, vr=None):
         alpha = f32(f32(1) / f32(lexpf(f32(f32(-dot16(a, b)) / np.sqrt(f32(d)))) + f32(1)))
         xr = [fma32(f32(vr[k]), alpha, xr[k]) for k in range(d)]
     return xr, zcn(xr, norm_in)
+
+
+def post_row(x, o, x1, pr, u, lane, post_norm, pre_hada, attn_gate, a_post, b_post, a_res, b_res, mlp_weights):
+    """infer.rs:1564-1606 for one row: the gated residual x2, the pre-MLP
+    norm, the MLP, the post gates (own lane 0, others -4), the residual gates
+    through Sinkhorn, then the mHC write of each lane from y = (x2 + mlp) - u
+    and the old lanes. Returns (the new lanes, the MLP output)."""
+    x = [f32(v) for v in x]
+    d = len(x) // 4
+    ga = f32(f32(1) / f32(lexpf(f32(-f32(attn_gate))) + f32(1)))
+    on = zcn(o, post_norm)
+    x2 = [fma32(on[k], ga, f32(x1[k])) for k in range(d)]
+    h2 = zcn(x2, pre_hada)
+    mlp = mlp_native(h2, *mlp_weights)
+    hpost = []
+    for j in range(4):
+        off = f32(0.0) if j == lane else f32(-4.0)
+        z = f32(f32(f32(f32(pr[4 + j]) * f32(a_post)) + off) + f32(b_post[j]))
+        hpost.append(f32(f32(2) / f32(lexpf(f32(-z)) + f32(1))))
+    zres = [fma32(f32(pr[8 + k]), f32(a_res), f32(b_res[k])) for k in range(16)]
+    hres = sinkhorn64(zres)
+    y = [f32(f32(x2[ch] + mlp[ch]) - f32(u[ch])) for ch in range(d)]
+    new = list(x)
+    for a in range(4):
+        for ch in range(d):
+            v = f32(y[ch] * hpost[a])
+            for b in range(4):
+                v = fma32(x[b * d + ch], f32(hres[a * 4 + b]), v)
+            new[a * d + ch] = v
+    return np.array(new, np.float32), mlp
