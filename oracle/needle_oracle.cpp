@@ -2153,6 +2153,48 @@ static void post_row(const Model& m, const Layer& L, int lane, float ga, const f
     }
 }
 
+// infer.rs:1437-1486 for one row: the three conv taps over the projection
+// rows (rows[j]: the row j positions back, its q | k | v columns first;
+// NULL before position 0: the tap multiplies zero), then each q and k
+// head's ZC-RMSNorm and RoPE with that position's cos / sin [qk / 2]. out:
+// the q | k | v row [nh qk + nkv qk + nkv vd].
+static void conv_rope_row(const Layer& L, const float* const rows[3], int nh, int nkv, int qk, int vd, const float* cs,
+                          const float* sn, float* out) {
+    const int qd = nh * qk, kd = nkv * qk, vdim = nkv * vd, half = qk / 2;
+    const struct { int start, cw; const std::vector<float>* w; } parts[3] = {
+        {0, qd, &L.q_taps}, {qd, kd, &L.k_taps}, {qd + kd, vdim, &L.v_taps}};
+    for (auto& pt : parts) {
+        float* o = out + pt.start;
+        const float* cur = rows[0] + pt.start;
+        const float* w = pt.w->data();
+        for (int k = 0; k < pt.cw; k++) o[k] = w[k] * cur[k];
+        for (int j = 1; j < 3; j++) {
+            const float* wj = w + (size_t)j * pt.cw;
+            const float* r = rows[j];
+            if (r) {
+                for (int k = 0; k < pt.cw; k++) o[k] = std::fmaf(wj[k], r[pt.start + k], o[k]);
+            } else {
+                for (int k = 0; k < pt.cw; k++) o[k] = std::fmaf(wj[k], 0.0f, o[k]);
+            }
+        }
+    }
+    for (int hh = 0; hh < nh + nkv; hh++) {
+        int off = hh < nh ? hh * qk : qd + (hh - nh) * qk;
+        const float* scale = hh < nh ? L.q_norm.data() : L.k_norm.data();
+        float* x = out + off;
+        float r = rinv(dot16(x, x, qk), qk);
+        for (int k = 0; k < qk; k++) {
+            float tt = x[k] * r;
+            x[k] = std::fmaf(tt, scale[k], tt);
+        }
+        for (int f = 0; f < half; f++) {
+            float a = x[f], b = x[f + half];
+            x[f] = std::fmaf(-sn[f], b, cs[f] * a);
+            x[f + half] = std::fmaf(sn[f], a, cs[f] * b);
+        }
+    }
+}
+
 static void layer_native(const Model& m, int l, Session& st, int64_t p0, std::vector<float>& xs, int t,
                          const std::vector<float>& cos, const std::vector<float>& sin,
                          const std::vector<std::vector<float>>& ekeys, const std::vector<std::vector<float>>& evals) {
@@ -2197,41 +2239,9 @@ static void layer_native(const Model& m, int l, Session& st, int64_t p0, std::ve
             if (hrows + i >= j) return ls.hist.data() + (size_t)(hrows + i - j) * width;
             return nullptr;
         };
-        float* out = qkv.data() + (size_t)i * width;
-        const struct { int start, cw; const std::vector<float>* w; } parts[3] = {
-            {0, qd, &L.q_taps}, {qd, kd, &L.k_taps}, {qd + kd, vdim, &L.v_taps}};
-        for (auto& pt : parts) {
-            float* o = out + pt.start;
-            const float* cur = prev(0) + pt.start;
-            const float* w = pt.w->data();
-            for (int k = 0; k < pt.cw; k++) o[k] = w[k] * cur[k];
-            for (int j = 1; j < c.taps; j++) {
-                const float* wj = w + (size_t)j * pt.cw;
-                const float* r = prev(j);
-                if (r) {
-                    for (int k = 0; k < pt.cw; k++) o[k] = std::fmaf(wj[k], r[pt.start + k], o[k]);
-                } else {
-                    for (int k = 0; k < pt.cw; k++) o[k] = std::fmaf(wj[k], 0.0f, o[k]);
-                }
-            }
-        }
-        const float* cs = cos.data() + (size_t)i * half;
-        const float* sn = sin.data() + (size_t)i * half;
-        for (int hh = 0; hh < nh + nkv; hh++) {
-            int off = hh < nh ? hh * qk : qd + (hh - nh) * qk;
-            const float* scale = hh < nh ? L.q_norm.data() : L.k_norm.data();
-            float* x = out + off;
-            float r = rinv(dot16(x, x, qk), qk);
-            for (int k = 0; k < qk; k++) {
-                float tt = x[k] * r;
-                x[k] = std::fmaf(tt, scale[k], tt);
-            }
-            for (int f = 0; f < half; f++) {
-                float a = x[f], b = x[f + half];
-                x[f] = std::fmaf(-sn[f], b, cs[f] * a);
-                x[f + half] = std::fmaf(sn[f], a, cs[f] * b);
-            }
-        }
+        const float* rows[3] = {prev(0), prev(1), prev(2)};
+        conv_rope_row(L, rows, nh, nkv, qk, vd, cos.data() + (size_t)i * half, sin.data() + (size_t)i * half,
+                      qkv.data() + (size_t)i * width);
     }
     g_trace.put(tag + "qkv", qkv.data(), qkv.size());
     for (int i = 0; i < t; i++) ls.hist.insert(ls.hist.end(), proj.begin() + (size_t)i * pout, proj.begin() + (size_t)i * pout + width);
@@ -3295,6 +3305,24 @@ int orc_post_row(int d, const float* post_norm, const float* pre_hada, float att
     L.cond_u.assign(cond_u, cond_u + 8 * 1024);
     const float ga = 1.0f / (lexpf(-L.attn_gate) + 1.0f);
     post_row(m, L, lane, ga, o, x1, pr, u, x, mlp_out);
+    return 0;
+}
+
+// infer.rs:1437-1486 on one row with given weights (the Needle 3 heads: 12
+// q and 2 kv heads of 48, values 64): rows cur, prev1, prev2 [800] (prev
+// NULL before position 0), taps q_taps [3][576], k_taps [3][96], v_taps
+// [3][128], q_norm, k_norm [48], cos / sin [24]. out [800].
+int orc_conv_rope(const float* cur, const float* prev1, const float* prev2, const float* q_taps, const float* k_taps,
+                  const float* v_taps, const float* q_norm, const float* k_norm, const float* cs, const float* sn, float* out) {
+    if (!cur || (!prev1 && prev2)) return -1;
+    Layer L;
+    L.q_taps.assign(q_taps, q_taps + 3 * 576);
+    L.k_taps.assign(k_taps, k_taps + 3 * 96);
+    L.v_taps.assign(v_taps, v_taps + 3 * 128);
+    L.q_norm.assign(q_norm, q_norm + 48);
+    L.k_norm.assign(k_norm, k_norm + 48);
+    const float* rows[3] = {cur, prev1, prev2};
+    conv_rope_row(L, rows, 12, 2, 48, 64, cs, sn, out);
     return 0;
 }
 

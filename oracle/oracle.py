@@ -51,6 +51,7 @@ def lib():
             "orc_mlp": (I, [P, I, P, P, P, P, P, P, P, P, P, P, P]),
             "orc_mhc_read": (I, [P, I, P, P, F, P, I, P, P, P, P, P, P, P]),
             "orc_post_row": (I, [I, P, P, F, F, P, F, P, P, P, P, P, P, P, P, P, P, P, I, P, P, P, P, P, P]),
+            "orc_conv_rope": (I, [P, P, P, P, P, P, P, P, P, P, P]),
             "orc_attend_head": (None, [P, P, P, P, I, I, I, P, I, P, I, I, P]),
             "orc_model_load": (P, [P, C.c_uint64]),
             "orc_model_free": (None, [P]),
@@ -192,6 +193,19 @@ def post_row(x, o, x1, pr, u, lane, post_norm, pre_hada, attn_gate, a_post, b_po
     if rc != 0:
         raise ValueError("bad post block arguments")
     return xs, mlp_out
+
+
+def conv_rope(cur, prev1, prev2, q_taps, k_taps, v_taps, q_norm, k_norm, cs, sn):
+    """The conv taps, head norms and RoPE of one row (infer.rs:1437-1486);
+    prev1 / prev2 None before position 0. Returns the q | k | v row [800]."""
+    f = lambda a: np.ascontiguousarray(a, np.float32)
+    out = np.zeros(800, np.float32)
+    opt = lambda a: _p(f(a)) if a is not None else None
+    rc = lib().orc_conv_rope(_p(f(cur)), opt(prev1), opt(prev2), _p(f(q_taps)), _p(f(k_taps)), _p(f(v_taps)),
+                             _p(f(q_norm)), _p(f(k_norm)), _p(f(cs)), _p(f(sn)), _p(out))
+    if rc != 0:
+        raise ValueError("bad conv arguments")
+    return out
 
 
 def set_team(threads: int) -> None:

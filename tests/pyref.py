@@ -603,3 +603,30 @@ def post_row(x, o, x1, pr, u, lane, post_norm, pre_hada, attn_gate, a_post, b_po
                 v = fma32(x[b * d + ch], f32(hres[a * 4 + b]), v)
             new[a * d + ch] = v
     return np.array(new, np.float32), mlp
+
+
+def conv_rope_row(rows, q_taps, k_taps, v_taps, q_norm, k_norm, cs, sn, nh=12, nkv=2, qk=48, vd=64):
+    """infer.rs:1437-1486 for one row: each of q | k | v through its three
+    conv taps (o = w0 * x0, then fma over the taps; a missing row before
+    position 0 multiplies zero), then each q and k head's zcn_inplace and
+    RoPE: x[f] = fma(-sin, x[f + half], cos * x[f]), x[f + half] =
+    fma(sin, x[f], cos * x[f + half])."""
+    qd, kd, vdim, half = nh * qk, nkv * qk, nkv * vd, qk // 2
+    out = [f32(0)] * (qd + kd + vdim)
+    for start, cw, w in ((0, qd, q_taps), (qd, kd, k_taps), (qd + kd, vdim, v_taps)):
+        w = np.asarray(w, np.float32).reshape(3, cw)
+        o = [f32(w[0][k] * f32(rows[0][start + k])) for k in range(cw)]
+        for j in (1, 2):
+            r = rows[j]
+            o = [fma32(w[j][k], f32(r[start + k]) if r is not None else f32(0), o[k]) for k in range(cw)]
+        out[start:start + cw] = o
+    for hh in range(nh + nkv):
+        off = hh * qk if hh < nh else qd + (hh - nh) * qk
+        scale = q_norm if hh < nh else k_norm
+        x = zcn(out[off:off + qk], scale)
+        for f in range(half):
+            a, b = x[f], x[f + half]
+            x[f] = fma32(f32(-f32(sn[f])), b, f32(f32(cs[f]) * a))
+            x[f + half] = fma32(f32(sn[f]), a, f32(f32(cs[f]) * b))
+        out[off:off + qk] = x
+    return np.array(out, np.float32)

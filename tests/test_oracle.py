@@ -248,6 +248,25 @@ def test_post_block_matches_python():
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
+@pytest.mark.timeout(300)
+@pytest.mark.parametrize("history", [0, 1, 2])
+def test_conv_rope_matches_python(history):
+    """The conv taps, q / k head norms and RoPE of one row (infer.rs:
+    1437-1486) at position 0 (no earlier rows), 1 and later, seeded weights:
+    the oracle against the pure-Python restatement, bit for bit."""
+    rng = np.random.default_rng(5 + history)
+    h16 = lambda a: np.asarray(a, np.float32).astype(np.float16).astype(np.float32)
+    rows = [(rng.standard_normal(800) * 0.6).astype(np.float32) for _ in range(3)]
+    rows = rows[:1 + history] + [None] * (2 - history)
+    taps = [h16(0.5 * rng.standard_normal(3 * n)) for n in (576, 96, 128)]
+    q_norm, k_norm = h16(0.1 * rng.standard_normal(48)), h16(0.1 * rng.standard_normal(48))
+    ang = rng.uniform(-3, 3, 24)
+    cs, sn = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    got = orc.conv_rope(rows[0], rows[1], rows[2], *taps, q_norm, k_norm, cs, sn)
+    want = pyref.conv_rope_row(rows, *taps, q_norm, k_norm, cs, sn)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
 def test_row_matches_unpack():
     rng = np.random.default_rng(1)
     w = (rng.standard_normal((4, 384)) * 0.02).astype(np.float32)
