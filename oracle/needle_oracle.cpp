@@ -1385,6 +1385,23 @@ static std::vector<float> dense_tensor(const Archive& a, size_t i, std::vector<i
 // crates/needle-core/src/cact.rs:173-202 (Header::to_config) and
 // crates/needle-engine/src/weights.rs:314-497 (record walk, fast mode),
 // infer.rs:938-962 (Tables::new).
+// infer.rs:938-946 (Tables::new): freq = powf(theta, i * (-2 / qk)) and
+// its sine and cosine, the single-token recurrence's step.
+static void rope_tables(Model& m, float theta, int qk) {
+    float coef = -2.0f / (float)qk;
+    m.freq.clear();
+    m.sd.clear();
+    m.cd.clear();
+    for (int k = 0; k < qk / 2; k++) {
+        float f = lpowf(theta, (float)k * coef);
+        float s, co;
+        lsincosf(f, &s, &co);
+        m.freq.push_back(f);
+        m.sd.push_back(s);
+        m.cd.push_back(co);
+    }
+}
+
 static void load_model(Model& m) {
     Archive a;
     parse_archive(m.bytes.data(), m.bytes.size(), a);
@@ -1509,15 +1526,7 @@ static void load_model(Model& m) {
         throw std::runtime_error("Hadamard permutations do not match hada_n");
     m.site_of_layer.assign(c.L, -1);
     for (size_t s = 0; s < c.sites.size(); s++) m.site_of_layer[c.sites[s]] = (int)s;
-    float coef = -2.0f / (float)c.qk;
-    for (int k = 0; k < c.qk / 2; k++) {
-        float f = lpowf(c.theta, (float)k * coef);
-        float s, co;
-        lsincosf(f, &s, &co);
-        m.freq.push_back(f);
-        m.sd.push_back(s);
-        m.cd.push_back(co);
-    }
+    rope_tables(m, c.theta, c.qk);
 }
 
 // ------------------------------------------------------------- session
@@ -3323,6 +3332,25 @@ int orc_conv_rope(const float* cur, const float* prev1, const float* prev2, cons
     L.k_norm.assign(k_norm, k_norm + 48);
     const float* rows[3] = {cur, prev1, prev2};
     conv_rope_row(L, rows, 12, 2, 48, 64, cs, sn, out);
+    return 0;
+}
+
+// infer.rs:1716-1744 (rope_rows) for a session that fed positions
+// p0 - n_prev .. p0 - 1 one row at a time before, then asks for t rows
+// from p0: each of those calls and this one as the oracle's sessions make
+// them (the direct angles for a chunk, the recurrence for a single token
+// after the newest row). Writes this call's cos / sin [t][qk / 2].
+int orc_rope_rows(float theta, int qk, int64_t p0, int n_prev, int t, float* cos_out, float* sin_out) {
+    if (qk < 2 || qk % 2 || t < 1 || n_prev < 0 || n_prev > p0) return -1;
+    Model m;
+    rope_tables(m, theta, qk);
+    Session st;
+    std::vector<float> cs, sn;
+    if (n_prev > 0) rope_rows(m, st, p0 - n_prev, 1, cs, sn);  // the first as a direct row
+    for (int64_t p = p0 - n_prev + 1; p < p0; p++) rope_rows(m, st, p, 1, cs, sn);
+    rope_rows(m, st, p0, t, cs, sn);
+    std::memcpy(cos_out, cs.data(), sizeof(float) * cs.size());
+    std::memcpy(sin_out, sn.data(), sizeof(float) * sn.size());
     return 0;
 }
 

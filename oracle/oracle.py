@@ -52,6 +52,7 @@ def lib():
             "orc_mhc_read": (I, [P, I, P, P, F, P, I, P, P, P, P, P, P, P]),
             "orc_post_row": (I, [I, P, P, F, F, P, F, P, P, P, P, P, P, P, P, P, P, P, I, P, P, P, P, P, P]),
             "orc_conv_rope": (I, [P, P, P, P, P, P, P, P, P, P, P]),
+            "orc_rope_rows": (I, [F, I, I64, I, I, P, P]),
             "orc_attend_head": (None, [P, P, P, P, I, I, I, P, I, P, I, I, P]),
             "orc_model_load": (P, [P, C.c_uint64]),
             "orc_model_free": (None, [P]),
@@ -206,6 +207,15 @@ def conv_rope(cur, prev1, prev2, q_taps, k_taps, v_taps, q_norm, k_norm, cs, sn)
     if rc != 0:
         raise ValueError("bad conv arguments")
     return out
+
+
+def rope_rows(theta, qk, p0, n_prev, t):
+    """The session RoPE rows of infer.rs:1716-1744 after n_prev single-token
+    rows up to p0 - 1: (cos, sin) [t][qk / 2] of rows p0 .. p0 + t - 1."""
+    cs, sn = np.zeros((t, qk // 2), np.float32), np.zeros((t, qk // 2), np.float32)
+    if lib().orc_rope_rows(float(theta), qk, int(p0), int(n_prev), int(t), _p(cs), _p(sn)) != 0:
+        raise ValueError("bad RoPE arguments")
+    return cs, sn
 
 
 def set_team(threads: int) -> None:

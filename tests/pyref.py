@@ -630,3 +630,43 @@ def conv_rope_row(rows, q_taps, k_taps, v_taps, q_norm, k_norm, cs, sn, nh=12, n
             x[f + half] = fma32(f32(sn[f]), a, f32(f32(cs[f]) * b))
         out[off:off + qk] = x
     return np.array(out, np.float32)
+
+
+def rope_tables(theta, qk):
+    """infer.rs:938-946: freq = powf(theta, i * (-2 / qk)) (libm on f64,
+    rounded once), and its sine and cosine."""
+    import math
+
+    coef = f32(f32(-2.0) / f32(qk))
+    freq = [f32(math.pow(float(f32(theta)), float(f32(f32(k) * coef)))) for k in range(qk // 2)]
+    return freq, [f32(math.sin(float(f))) for f in freq], [f32(math.cos(float(f))) for f in freq]
+
+
+def rope_rows(theta, qk, p0, n_prev, t):
+    """infer.rs:1716-1744 for a session that fed n_prev single-token rows up
+    to p0 - 1, then t rows from p0: a chunk (or a token with no newest row
+    before it) takes sincosf(freq * pos); a single token right after the
+    newest row takes the recurrence cos = fma(-sd, s0, cd * c0), sin =
+    fma(sd, c0, cd * s0)."""
+    import math
+
+    freq, sd, cd = rope_tables(theta, qk)
+
+    def direct(p):
+        a = [float(f32(f * f32(p))) for f in freq]
+        return [f32(math.cos(v)) for v in a], [f32(math.sin(v)) for v in a]
+
+    def recur(c0, s0):
+        return ([fma32(f32(-sd[f]), s0[f], f32(cd[f] * c0[f])) for f in range(len(freq))],
+                [fma32(sd[f], c0[f], f32(cd[f] * s0[f])) for f in range(len(freq))])
+
+    c = s = None
+    if n_prev > 0:
+        c, s = direct(p0 - n_prev)
+        for _ in range(p0 - n_prev + 1, p0):
+            c, s = recur(c, s)
+    if t == 1 and n_prev > 0:
+        c, s = recur(c, s)
+        return np.array([c], np.float32), np.array([s], np.float32)
+    rows = [direct(p0 + i) for i in range(t)]
+    return np.array([r[0] for r in rows], np.float32), np.array([r[1] for r in rows], np.float32)

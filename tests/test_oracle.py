@@ -267,6 +267,20 @@ def test_conv_rope_matches_python(history):
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
+@pytest.mark.parametrize("p0,n_prev,t", [(0, 0, 5), (37, 3, 1), (200, 120, 1), (50, 2, 4), (9, 0, 1)])
+def test_rope_rows_match_python(p0, n_prev, t):
+    """The RoPE tables and a session's rows (infer.rs:938-946, 1716-1744): a
+    chunk's direct angles, the single-token recurrence after 3 and after 120
+    single tokens, a chunk after single tokens, a lone first token: the
+    oracle against the pure-Python restatement, bit for bit (both on the
+    platform's f64 pow / sin / cos)."""
+    theta = np.float32(100000.0)
+    got_c, got_s = orc.rope_rows(theta, 48, p0, n_prev, t)
+    want_c, want_s = pyref.rope_rows(theta, 48, p0, n_prev, t)
+    assert np.array_equal(got_c.view(np.uint32), want_c.view(np.uint32))
+    assert np.array_equal(got_s.view(np.uint32), want_s.view(np.uint32))
+
+
 def test_row_matches_unpack():
     rng = np.random.default_rng(1)
     w = (rng.standard_normal((4, 384)) * 0.02).astype(np.float32)
