@@ -2020,12 +2020,44 @@ struct Trace {
 static thread_local Trace g_trace;
 
 // infer.rs:1244-1328
+// infer.rs:1262-1272: the slot (in its table) of the n-gram of `order`
+// tokens ending at position pos (tokens before position 0 read 0) for
+// order index oi and head h: the seeded multiply-xor hash, folded, modulo
+// the table's slots.
+static uint32_t engram_slot(const uint32_t* tokens, int64_t pos, int oi, int order, int h, int stride, int slots) {
+    const uint32_t SEED = 0x9E3779B9u, PRIME = 0x01000193u;  // config.rs:11-12
+    uint32_t acc = SEED * (uint32_t)(oi * stride + h + 1);
+    for (int j = 0; j < order; j++) {
+        uint32_t tok = pos >= j ? tokens[pos - j] : 0;
+        acc = (acc ^ tok) * PRIME;
+    }
+    acc ^= acc >> 15;
+    return acc % (uint32_t)slots;
+}
+
+// infer.rs:1307-1320 with engram_tap (667-687): the dilated conv of the
+// int8 value history (v8 [pos][d], vs [pos][d / 32]) at position pos, taps
+// [etaps][d], into dst [d] (zeroed by the caller): tap j reads position
+// pos - j * dil, stopping before position 0.
+static void engram_conv_row(const float* taps, const int8_t* v8, const float* vs, int64_t pos, int etaps, int dil, int d,
+                            float* dst) {
+    for (int j = 0; j < etaps; j++) {
+        int64_t p = pos - (int64_t)j * dil;
+        if (p < 0) break;
+        const int8_t* q8 = v8 + p * d;
+        const float* qs = vs + p * d / 32;
+        for (int ch = 0; ch < d; ch++) {
+            float deq = qs[ch / 32] * (float)q8[ch];
+            dst[ch] = std::fmaf(taps[(size_t)j * d + ch], deq, dst[ch]);
+        }
+    }
+}
+
 static void engram_native(const Model& m, Session& st, int64_t p0, int t, std::vector<std::vector<float>>& keys,
                           std::vector<std::vector<float>>& vals) {
     const Config& c = m.c;
     const int d = c.d, heads = c.eheads(), sub = c.esub;
     const int stride = c.eseed > 0 ? c.eseed : heads;
-    const uint32_t SEED = 0x9E3779B9u, PRIME = 0x01000193u;  // config.rs:11-12
     keys.assign(c.sites.size(), {});
     vals.assign(c.sites.size(), {});
     for (size_t site = 0; site < c.sites.size(); site++) {
@@ -2036,14 +2068,8 @@ static void engram_native(const Model& m, Session& st, int64_t p0, int t, std::v
                 int order = c.orders[oi];
                 for (int h = 0; h < heads; h++) {
                     if (pos + 1 < order) continue;
-                    uint32_t acc = SEED * (uint32_t)(oi * stride + h + 1);
-                    for (int j = 0; j < order; j++) {
-                        uint32_t tok = pos >= j ? st.tokens[pos - j] : 0;
-                        acc = (acc ^ tok) * PRIME;
-                    }
-                    acc ^= acc >> 15;
                     int tbl = (int)oi * heads + h;
-                    int row = tbl * c.eslots + (int)(acc % (uint32_t)c.eslots);
+                    int row = tbl * c.eslots + (int)engram_slot(st.tokens.data(), pos, (int)oi, order, h, stride, c.eslots);
                     qmat_row(m.engrams[site].tables, row, e.data() + (size_t)i * d + tbl * sub);
                 }
             }
@@ -2064,20 +2090,8 @@ static void engram_native(const Model& m, Session& st, int64_t p0, int t, std::v
         const std::vector<float>& taps = m.engrams[site].taps;
         std::vector<float> v((size_t)t * d, 0.f), k((size_t)t * d);
         for (int i = 0; i < t; i++) std::memcpy(&k[(size_t)i * d], &kv[(size_t)i * 2 * d], sizeof(float) * d);
-        for (int i = 0; i < t; i++) {
-            int64_t pos = p0 + i;
-            float* dst = v.data() + (size_t)i * d;
-            for (int j = 0; j < c.etaps; j++) {
-                int64_t p = pos - (int64_t)j * c.edil;
-                if (p < 0) break;
-                const int8_t* q8 = v8.data() + p * d;
-                const float* qs = vs.data() + p * d / 32;
-                for (int ch = 0; ch < d; ch++) {
-                    float deq = qs[ch / 32] * (float)q8[ch];
-                    dst[ch] = std::fmaf(taps[(size_t)j * d + ch], deq, dst[ch]);
-                }
-            }
-        }
+        for (int i = 0; i < t; i++)
+            engram_conv_row(taps.data(), v8.data(), vs.data(), p0 + i, c.etaps, c.edil, d, v.data() + (size_t)i * d);
         keys[site] = std::move(k);
         vals[site] = std::move(v);
         if (g_trace.on) {
@@ -3352,6 +3366,25 @@ int orc_rope_rows(float theta, int qk, int64_t p0, int n_prev, int t, float* cos
     std::memcpy(cos_out, cs.data(), sizeof(float) * cs.size());
     std::memcpy(sin_out, sn.data(), sizeof(float) * sn.size());
     return 0;
+}
+
+// The engram slot of each (position, order index, head) for tokens [n]
+// (orders [n_orders], heads, seed stride, slots): out [n][n_orders][heads],
+// -1 where the position is shorter than the order.
+void orc_engram_slots(const uint32_t* tokens, int n, const int* orders, int n_orders, int heads, int stride, int slots,
+                      int64_t* out) {
+    for (int pos = 0; pos < n; pos++)
+        for (int oi = 0; oi < n_orders; oi++)
+            for (int h = 0; h < heads; h++)
+                out[((size_t)pos * n_orders + oi) * heads + h] =
+                    pos + 1 < orders[oi] ? -1 : (int64_t)engram_slot(tokens, pos, oi, orders[oi], h, stride, slots);
+}
+
+// engram_conv_row at position pos over the history v8 [pos + 1][d], vs
+// [pos + 1][d / 32] with taps [etaps][d]: out [d].
+void orc_engram_conv(const float* taps, const int8_t* v8, const float* vs, int64_t pos, int etaps, int dil, int d, float* out) {
+    std::fill(out, out + d, 0.f);
+    engram_conv_row(taps, v8, vs, pos, etaps, dil, d, out);
 }
 
 // 1 when the 4-bit matmuls run their lane sums on AVX-512 VNNI.

@@ -53,6 +53,8 @@ def lib():
             "orc_post_row": (I, [I, P, P, F, F, P, F, P, P, P, P, P, P, P, P, P, P, P, I, P, P, P, P, P, P]),
             "orc_conv_rope": (I, [P, P, P, P, P, P, P, P, P, P, P]),
             "orc_rope_rows": (I, [F, I, I64, I, I, P, P]),
+            "orc_engram_slots": (None, [P, I, P, I, I, I, I, P]),
+            "orc_engram_conv": (None, [P, P, P, I64, I, I, I, P]),
             "orc_attend_head": (None, [P, P, P, P, I, I, I, P, I, P, I, I, P]),
             "orc_model_load": (P, [P, C.c_uint64]),
             "orc_model_free": (None, [P]),
@@ -216,6 +218,28 @@ def rope_rows(theta, qk, p0, n_prev, t):
     if lib().orc_rope_rows(float(theta), qk, int(p0), int(n_prev), int(t), _p(cs), _p(sn)) != 0:
         raise ValueError("bad RoPE arguments")
     return cs, sn
+
+
+def engram_slots(tokens, orders, heads, stride, slots):
+    """The engram hash's table slot per (position, order index, head), -1
+    before a full n-gram (infer.rs:1262-1272)."""
+    tokens = np.ascontiguousarray(tokens, np.uint32)
+    orders = np.ascontiguousarray(orders, np.int32)
+    out = np.zeros((len(tokens), len(orders), heads), np.int64)
+    lib().orc_engram_slots(_p(tokens), len(tokens), _p(orders), len(orders), heads, stride, slots, _p(out))
+    return out
+
+
+def engram_conv(taps, v8, vs, pos, dil):
+    """The engram's dilated conv over the int8 value history at position
+    pos (infer.rs:1307-1320): v [d]."""
+    taps = np.ascontiguousarray(taps, np.float32)
+    v8 = np.ascontiguousarray(v8, np.int8)
+    vs = np.ascontiguousarray(vs, np.float32)
+    d = taps.shape[1]
+    out = np.zeros(d, np.float32)
+    lib().orc_engram_conv(_p(taps), _p(v8), _p(vs), int(pos), taps.shape[0], int(dil), d, _p(out))
+    return out
 
 
 def set_team(threads: int) -> None:

@@ -670,3 +670,33 @@ def rope_rows(theta, qk, p0, n_prev, t):
         return np.array([c], np.float32), np.array([s], np.float32)
     rows = [direct(p0 + i) for i in range(t)]
     return np.array([r[0] for r in rows], np.float32), np.array([r[1] for r in rows], np.float32)
+
+
+def engram_slot(tokens, pos, oi, order, h, stride, slots):
+    """infer.rs:1262-1272: acc = SEED * (oi * stride + h + 1), then for each
+    of the n-gram's tokens (newest first, 0 before position 0) acc = (acc ^
+    tok) * PRIME, all mod 2^32; acc ^= acc >> 15; the slot is acc % slots
+    (config.rs:11-12 for the constants)."""
+    mask = 0xFFFFFFFF
+    acc = (0x9E3779B9 * (oi * stride + h + 1)) & mask
+    for j in range(order):
+        tok = int(tokens[pos - j]) if pos >= j else 0
+        acc = ((acc ^ tok) * 0x01000193) & mask
+    acc ^= acc >> 15
+    return acc % slots
+
+
+def engram_conv(taps, v8, vs, pos, dil):
+    """infer.rs:1307-1320 with engram_tap (667-687): tap j reads the int8
+    history at pos - j * dil (stopping before position 0), dequantized per
+    32-wide group, into an fma chain over the taps."""
+    etaps, d = np.asarray(taps).shape
+    dst = [f32(0)] * d
+    for j in range(etaps):
+        p = pos - j * dil
+        if p < 0:
+            break
+        for ch in range(d):
+            deq = f32(f32(vs[p][ch // 32]) * f32(int(v8[p][ch])))
+            dst[ch] = fma32(f32(taps[j][ch]), deq, dst[ch])
+    return np.array(dst, np.float32)

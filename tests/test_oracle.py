@@ -281,6 +281,38 @@ def test_rope_rows_match_python(p0, n_prev, t):
     assert np.array_equal(got_s.view(np.uint32), want_s.view(np.uint32))
 
 
+def test_engram_slots_match_python():
+    """The engram hash (infer.rs:1262-1272) at the Needle 3 geometry (orders
+    2 and 3, three heads, 18432 slots) over seeded token streams with the
+    vocabulary's extremes: the oracle's slots against the pure-Python
+    restatement, including the positions too short for an n-gram."""
+    rng = np.random.default_rng(12)
+    toks = rng.integers(0, 16384, 300).astype(np.uint32)
+    toks[:3] = (0, 16383, 0)
+    got = orc.engram_slots(toks, (2, 3), 3, 3, 18432)
+    for pos in range(len(toks)):
+        for oi, order in enumerate((2, 3)):
+            for h in range(3):
+                want = -1 if pos + 1 < order else pyref.engram_slot(toks, pos, oi, order, h, 3, 18432)
+                assert got[pos, oi, h] == want, (pos, oi, h)
+
+
+@pytest.mark.parametrize("pos", [0, 2, 5, 9, 40])
+def test_engram_conv_matches_python(pos):
+    """The engram's dilated conv over its int8 value history (infer.rs:
+    1307-1320, engram_tap 667-687; four taps, dilation 3) at the first
+    positions, where taps fall before position 0, and later: the oracle
+    against the pure-Python restatement, bit for bit."""
+    rng = np.random.default_rng(100 + pos)
+    d = 768
+    v8 = rng.integers(-128, 128, (pos + 1, d), dtype=np.int8)
+    vs = (np.abs(rng.standard_normal((pos + 1, d // 32))) * 0.02 + 1e-4).astype(np.float32)
+    taps = np.asarray(0.5 * rng.standard_normal((4, d)), np.float32).astype(np.float16).astype(np.float32)
+    got = orc.engram_conv(taps, v8, vs, pos, 3)
+    want = pyref.engram_conv(taps, v8, vs, pos, 3)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
 def test_row_matches_unpack():
     rng = np.random.default_rng(1)
     w = (rng.standard_normal((4, 384)) * 0.02).astype(np.float32)
