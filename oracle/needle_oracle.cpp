@@ -3846,12 +3846,16 @@ void orc_op_zcn(const float* x, const float* s, int T, int n, float* out) {
 // positions 0 .. T-1; freq per infer.rs:938-946.
 void orc_op_rope(const float* x, int T, float theta, float* out) {
     const int qk = 48, half = 24, heads = 14;
-    const float coef = -2.0f / (float)qk;
-    float freq[24];
-    for (int i = 0; i < half; i++) freq[i] = lpowf(theta, (float)i * coef);
+    if (T < 1) return;
+    // the tables and a fresh session's chunk rows (direct angles)
+    Model m;
+    rope_tables(m, theta, qk);
+    Session st;
+    std::vector<float> cosv, sinv;
+    rope_rows(m, st, 0, T, cosv, sinv);
     for (int t = 0; t < T; t++) {
-        float cs[24], sn[24];
-        for (int f = 0; f < half; f++) lsincosf(freq[f] * (float)t, &sn[f], &cs[f]);
+        const float* cs = cosv.data() + (size_t)t * half;
+        const float* sn = sinv.data() + (size_t)t * half;
         for (int h = 0; h < heads; h++) {
             const float* xi = x + (size_t)t * heads * qk + h * qk;
             float* o = out + (size_t)t * heads * qk + h * qk;
